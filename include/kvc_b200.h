@@ -1,0 +1,193 @@
+/*
+ * kvc_b200.h -- C ABI of the B200-native (sm_100a) kvcompress hot path.
+ *
+ * The reference (sachncs/kvcompress) is a Python package; its hot path is
+ * JoLTCompressor.compress / decompress (kvcompress/compressor/jolt.py:147-253)
+ * and FlashJoLTCompressor.compress_cell (kvcompress/compressor/flashjolt.py:
+ * 102-169).  This library replaces the torch ops those methods issue; the
+ * Python package kvcompress_b200 binds it with ctypes and keeps the
+ * reference's Python API on top.  Each entry point names the reference code
+ * it replaces.
+ *
+ * Conventions
+ *  - Plain device pointers and sizes; no allocation, no host synchronisation.
+ *    `stream` is a cudaStream_t passed as void* (NULL = legacy stream).
+ *  - "cells": one cell is one layer's K or V, shape (m, T, d) row-major with
+ *    m = batch * n_kv_heads (kvcompress/cache/compress.py:308-333).  Batched
+ *    entry points take a host array of `n_cells` device pointers, all cells
+ *    of one call sharing shape, dtype and allocation.
+ *  - Element types: KVC_F32 / KVC_F16 / KVC_BF16 for tensors of the cache's
+ *    dtype; KVC_F64 for solver buffers.
+ *  - Return 0 on success, a negative KVC_ERR_* on failure; the message is in
+ *    kvc_last_error() (thread-local).
+ *  - Scratch memory: callers pass `workspace` / `ws_bytes`; the matching
+ *    *_workspace_bytes() function gives the size needed.  Calls on different
+ *    streams with distinct workspaces are independent.
+ */
+#ifndef KVC_B200_H
+#define KVC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  KVC_OK = 0,
+  KVC_ERR_ARG = -1,
+  KVC_ERR_SHAPE = -2,
+  KVC_ERR_DTYPE = -3,
+  KVC_ERR_ALIGN = -4,
+  KVC_ERR_WORKSPACE = -5,
+  KVC_ERR_LAUNCH = -6,
+  KVC_ERR_TIMEOUT = -7,
+  KVC_ERR_UNSUPPORTED = -8
+};
+
+enum { KVC_F32 = 0, KVC_F16 = 1, KVC_BF16 = 2, KVC_F64 = 3, KVC_FP8E4M3 = 4 };
+
+/* Sketch-solver modes. */
+enum { KVC_SVD_EXACT = 0, KVC_SVD_RANDOMISED = 1 };
+/* Which side of A the Gram lives on (see kvc_sketch_solve). */
+enum { KVC_SIDE_LEFT = 0, KVC_SIDE_RIGHT = 1 };
+/* Quantiser scale layouts (kvcompress/compressor/quantization.py:410-452). */
+enum { KVC_SCALE_CHANNEL = 0, KVC_SCALE_GROUP = 1, KVC_SCALE_TENSOR = 2 };
+
+#define KVC_MAX_CELLS 64
+
+const char* kvc_last_error(void);
+int kvc_abi_version(void);
+
+/*
+ * Column Gram and sketch of a row-major (rows x p) matrix A per cell:
+ *   out = [ A^T A  (p x p) | A^T Omega (p x k) | sum(A*A) ]      (float64)
+ * laid out per cell at stride p*p + p*k + 1.
+ *
+ * Feature mode: A = x viewed as (m*T, d), so A^T A = A_f A_f^T with
+ * A_f = mode_n_unfold(x, 2), and A^T Omega = A_f Omega: the sketch product
+ * and the two power iterations of SVD.randomise (kvcompress/compressor/
+ * svd.py:259-265) and the Frobenius norm (svd.py:289) reduce to this one
+ * pass over x.  Token mode: A = x_proj in (T, m*rd) layout, k = 0.
+ * `omega` is one (rows x k) float32 matrix shared by every cell (NULL iff
+ * k == 0).  Summation order is fixed: results are bit-reproducible.
+ */
+size_t kvc_gram_workspace_bytes(int n_cells, int64_t rows, int p, int k);
+int kvc_gram(int n_cells, const void* const* a, int64_t rows, int p, int dtype,
+             const float* omega, int k, double* out, void* workspace, size_t ws_bytes,
+             void* stream);
+
+/*
+ * Randomised or exact truncated SVD of an A that is only seen through its
+ * Gram (replaces SVD.randomise, svd.py:221-316, and SVD.exact, svd.py:181-219).
+ *
+ * KVC_SIDE_LEFT (feature mode, A is p x n with n large):
+ *   gram per cell = kvc_gram output [G = A A^T | Y0 = A Omega | |A|^2].
+ *   Randomised: Q = orth(G^2 Y0) by subspace iteration, Ritz pairs of
+ *   Q^T G Q; exact: eigenpairs of G.  basis_out = U (p x rank) rounded to
+ *   `basis_dtype` (the input dtype, svd.py:507-510).
+ * KVC_SIDE_RIGHT (token mode, A is n x p with n = T large):
+ *   gram per cell = H = A^T A (p x p, kvc_gram output with k = 0).
+ *   `omega` (p x k, float32, shared).  basis_out = M (p x rank, float64)
+ *   with U = A M; apply it with kvc_apply_basis.
+ * sv2_out: the leading `rank` squared singular values per cell (may be
+ * NULL); tail_out: the discarded Frobenius mass per cell, as the reference
+ * reports it (svd.py:98-110 exact, svd.py:289-294 randomised).
+ * n_other: the long dimension of A (n), so that min(p, n_other) is the
+ * SVD's max_rank; n_power: power iterations (SVD.n_power, svd.py:131-142).
+ * Supports p, k <= 2046.
+ */
+size_t kvc_sketch_solve_workspace_bytes(int n_cells, int mode, int p, int k);
+int kvc_sketch_solve(int n_cells, int mode, int side, int p, int64_t n_other, int k, int rank,
+                     int n_power, const double* gram, int64_t gram_stride, const float* omega,
+                     void* basis_out, int basis_dtype, double* sv2_out, double* tail_out,
+                     void* workspace, size_t ws_bytes, void* stream);
+
+/*
+ * x_proj = x  x_3 U_d rounded to the cell dtype (tucker.py:251), written in
+ * token-unfolding layout (T, m*rd): x_proj_t[t, h*rd + r]
+ * (mode_n_unfold(x_proj, 1), tucker.py:254).
+ */
+int kvc_project_feature(int n_cells, const void* const* x, int64_t m, int64_t t, int d,
+                        int dtype, const void* const* u_feature, int rd, void* const* x_proj_t,
+                        void* stream);
+
+/* U = A M rounded to dtype: A (rows x p, dtype), M (p x r, float64 per cell
+ * at stride p*r), U (rows x r, dtype).  The lift u = q @ u_b of svd.py:285
+ * with the rounding of svd.py:507-510. */
+int kvc_apply_basis(int n_cells, const void* const* a, int64_t rows, int p, int dtype,
+                    const double* mat, int r, void* const* out, void* stream);
+
+/* core[h, a, r] = sum_t x_proj[h, t, r] * u_token[t, a], rounded to dtype
+ * (tucker.py:261).  x_proj_t in (T, m*rd) layout, u_token (T, rt). */
+size_t kvc_core_workspace_bytes(int n_cells, int64_t t, int m, int rd, int rt);
+int kvc_core(int n_cells, const void* const* x_proj_t, const void* const* u_token, int64_t t,
+             int m, int rd, int rt, int dtype, void* const* core, void* workspace,
+             size_t ws_bytes, void* stream);
+
+/*
+ * JL-rotated residual statistics (pass 1 of encode_residual,
+ * residual.py:201-216 + IntQuantizer.compute_params, quantization.py:410-452):
+ *   R   = x - reconstruct_partial_tucker(core, u_token, u_feature) in the cell
+ *         dtype (einsum order of tucker.py:184-189, jolt.py:311)
+ *   Rt  = float32(R) @ proj^T                       (residual.py:204-216)
+ * and from the per-column (or whole-tensor) min/max of Rt the quantiser's
+ * scale (float32) and zero point (int32).  rt = rd = 0 means "no Tucker
+ * term" and proj = NULL means "no rotation": then Rt = x, which is the
+ * quantize-only baseline (quantization_only.py:125-175) -- its statistics run
+ * in the cell dtype (`stat_dtype`), as the reference's do.
+ * scale_mode KVC_SCALE_CHANNEL (d values) or KVC_SCALE_TENSOR (1 value).
+ */
+size_t kvc_residual_stats_workspace_bytes(int n_cells, int64_t rows, int d);
+int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, int64_t t, int d, int dtype,
+                       const void* const* core, const void* const* u_token,
+                       const void* const* u_feature, int rt, int rd, const float* proj,
+                       int bits, int symmetric, int scale_mode, int stat_dtype,
+                       float* const* scale_out, int32_t* const* zp_out, void* workspace,
+                       size_t ws_bytes, void* stream);
+
+/*
+ * Pass 2 of encode_residual: recompute Rt, quantise
+ * q = clamp(rint(Rt / scale + zp)) (quantization.py:311-363) and bit-pack
+ * (bit_packing_signed, quantization.py:181-238) into codes
+ * (rows x ceil(d*bits/8)) uint8.  With scale_mode KVC_SCALE_GROUP the
+ * per-row group scales (rows x d/group) are computed here and written to
+ * scale/zp.  arith_dtype: dtype of the divide/add in the per-tensor branch
+ * (0-dim promotion, quantization.py:335-336); KVC_F32 elsewhere.
+ */
+int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, int64_t t, int d, int dtype,
+                       const void* const* core, const void* const* u_token,
+                       const void* const* u_feature, int rt, int rd, const float* proj,
+                       int bits, int symmetric, int scale_mode, int group_size, int stat_dtype,
+                       int arith_dtype, float* const* scale, int32_t* const* zp,
+                       uint8_t* const* codes, void* stream);
+
+/*
+ * Fused decompress of JoLT payloads (reconstruct_payload, jolt.py:401-463 with
+ * decode_residual, residual.py:242-288):
+ *   out = cast( Tucker(core, u_token, u_feature) in float32
+ *              + dequant(codes) @ proj , out_dtype )
+ * for the token range [t0, t1) of every cell (t0 = 0, t1 = T: the whole
+ * cell).  out is (m, t1 - t0, d).  Factors are float16 (factor_dtype).
+ * bits == 0: no residual term.  rt = rd = 0 / proj = NULL: the
+ * quantize-only decoder (quantization_only.py:177-198).
+ */
+int kvc_decompress(int n_cells, const uint8_t* const* codes, const float* const* scale,
+                   const int32_t* const* zp, int bits, int symmetric, int scale_mode,
+                   int group_size, const void* const* core, const void* const* u_token,
+                   const void* const* u_feature, int factor_dtype, int64_t m, int64_t t, int d,
+                   int rt, int rd, const float* proj, int64_t t0, int64_t t1, int out_dtype,
+                   void* const* out, void* stream);
+
+/* Elementwise cast between KVC_F32/F16/BF16/FP8E4M3 (torch .to semantics:
+ * round to nearest even; float8_e4m3fn does not saturate -- magnitudes that
+ * round above 448 become NaN).  Used by the fp8/fp16/bf16 identity
+ * compressors (identity.py:68-117, dispatch.py:106-125). */
+int kvc_cast(int64_t n, const void* in, int in_dtype, void* out, int out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KVC_B200_H */

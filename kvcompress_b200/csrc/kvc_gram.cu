@@ -1,0 +1,246 @@
+// Column Gram / cross products A^T B over a long row axis (SIMT, fp32 FMA).
+//
+// Used for
+//  * the feature-mode Gram + sketch  [x^T x | x^T Omega]  (kvc_gram),
+//  * the token-mode Gram  x_proj_t^T x_proj_t             (kvc_gram, k = 0),
+//  * the Tucker core       u_token^T x_proj_t              (kvc_core).
+// The row axis is split into chunks; each block accumulates one 64x64
+// output tile of one chunk in fp32 and writes it to the workspace; a second
+// kernel sums the chunks in a fixed order in fp64, so results are
+// bit-reproducible run to run.
+#include <algorithm>
+
+#include "kvc_common.cuh"
+
+namespace kvc {
+
+namespace {
+
+constexpr int TB = 64;   // output tile edge
+constexpr int RB = 32;   // rows staged per iteration
+constexpr int NT = 256;  // threads per block (16 x 16, 4x4 outputs each)
+
+template <typename TA, typename TB1>
+__global__ void __launch_bounds__(NT)
+atb_partial_kernel(CellPtrs A, CellPtrs B1, const float* __restrict__ B2, int64_t rows, int p,
+                   int q1, int q2, int chunks, int64_t chunk_rows, float* __restrict__ partial) {
+  const int cell = blockIdx.z;
+  const int chunk = blockIdx.x;
+  const int q = q1 + q2;
+  const int tiles_j = (q + TB - 1) / TB;
+  const int ti = blockIdx.y / tiles_j, tj = blockIdx.y % tiles_j;
+  const int i0 = ti * TB, j0 = tj * TB;
+  const TA* __restrict__ a = static_cast<const TA*>(A.p[cell]);
+  const TB1* __restrict__ b1 = static_cast<const TB1*>(B1.p[cell]);
+  __shared__ float sA[RB][TB];
+  __shared__ __align__(16) float sB[RB][TB];
+  const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
+  float acc[4][4];
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) acc[u][v] = 0.f;
+
+  const int64_t r_begin = (int64_t)chunk * chunk_rows;
+  const int64_t r_end = r_begin + chunk_rows < rows ? r_begin + chunk_rows : rows;
+  for (int64_t r0 = r_begin; r0 < r_end; r0 += RB) {
+    for (int e = threadIdx.x; e < RB * TB; e += NT) {
+      const int rr = e / TB, cc = e % TB;
+      const int64_t r = r0 + rr;
+      float va = 0.f, vb = 0.f;
+      if (r < r_end) {
+        const int ia = i0 + cc;
+        if (ia < p) va = Elt<TA>::to_f32(a[r * p + ia]);
+        const int jb = j0 + cc;
+        if (jb < q1) vb = Elt<TB1>::to_f32(b1[r * q1 + jb]);
+        else if (jb < q) vb = B2[r * q2 + (jb - q1)];
+      }
+      sA[rr][cc] = va;
+      sB[rr][cc] = vb;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int rr = 0; rr < RB; ++rr) {
+      float av[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) av[u] = sA[rr][ty * 4 + u];
+      const float4 bv = *reinterpret_cast<const float4*>(&sB[rr][tx * 4]);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        acc[u][0] = fmaf(av[u], bv.x, acc[u][0]);
+        acc[u][1] = fmaf(av[u], bv.y, acc[u][1]);
+        acc[u][2] = fmaf(av[u], bv.z, acc[u][2]);
+        acc[u][3] = fmaf(av[u], bv.w, acc[u][3]);
+      }
+    }
+    __syncthreads();
+  }
+  float* out = partial + ((int64_t)cell * chunks + chunk) * (int64_t)p * q;
+#pragma unroll
+  for (int u = 0; u < 4; ++u)
+#pragma unroll
+    for (int v = 0; v < 4; ++v) {
+      const int i = i0 + ty * 4 + u, j = j0 + tx * 4 + v;
+      if (i < p && j < q) out[(int64_t)i * q + j] = acc[u][v];
+    }
+}
+
+// Sum partials over chunks (fixed order, fp64) into the Gram layout
+// [A^T B1 (p x q1) | A^T B2 (p x q2) | trace] at `stride` doubles per cell.
+__global__ void gram_reduce_kernel(const float* __restrict__ partial, int n_cells, int chunks, int p,
+                                   int q1, int q2, double* __restrict__ out, int64_t stride) {
+  const int q = q1 + q2;
+  const int64_t total = (int64_t)n_cells * p * q;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int cell = (int)(idx / ((int64_t)p * q));
+    const int64_t e = idx % ((int64_t)p * q);
+    const int i = (int)(e / q), j = (int)(e % q);
+    const float* src = partial + (int64_t)cell * chunks * p * q + e;
+    double s = 0.0;
+    for (int c = 0; c < chunks; ++c) s += (double)src[(int64_t)c * p * q];
+    double* o = out + cell * stride;
+    if (j < q1) o[(int64_t)i * q1 + j] = s;
+    else o[(int64_t)p * q1 + (int64_t)i * q2 + (j - q1)] = s;
+  }
+}
+
+__global__ void gram_trace_kernel(double* out, int n_cells, int p, int q2, int64_t stride) {
+  const int cell = blockIdx.x * blockDim.x + threadIdx.x;
+  if (cell >= n_cells) return;
+  double* o = out + cell * stride;
+  double s = 0.0;
+  for (int i = 0; i < p; ++i) s += o[(int64_t)i * p + i];
+  o[(int64_t)p * p + (int64_t)p * q2] = s;
+}
+
+// core[h, a, r] = C[a, h*rd + r] with C = u_token^T x_proj_t (rt x m*rd).
+template <typename T>
+__global__ void core_reduce_kernel(const float* __restrict__ partial, int n_cells, int chunks,
+                                   int rt, int m, int rd, CellPtrsMut core) {
+  const int q = m * rd;
+  const int64_t total = (int64_t)n_cells * rt * q;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int cell = (int)(idx / ((int64_t)rt * q));
+    const int64_t e = idx % ((int64_t)rt * q);
+    const int a = (int)(e / q), c = (int)(e % q);
+    const int h = c / rd, r = c % rd;
+    const float* src = partial + (int64_t)cell * chunks * rt * q + e;
+    double s = 0.0;
+    for (int ch = 0; ch < chunks; ++ch) s += (double)src[(int64_t)ch * rt * q];
+    T* dst = static_cast<T*>(core.p[cell]);
+    dst[((int64_t)h * rt + a) * rd + r] = Elt<T>::from((float)s);
+  }
+}
+
+struct ChunkPlan {
+  int chunks;
+  int64_t chunk_rows;
+  int tiles;
+};
+
+ChunkPlan plan_chunks(int n_cells, int64_t rows, int p, int q) {
+  ChunkPlan pl;
+  pl.tiles = (int)(ceil_div(p, TB) * ceil_div(q, TB));
+  const int64_t target = 4LL * num_sms();
+  int64_t chunks = ceil_div(target, (int64_t)pl.tiles * std::max(1, n_cells));
+  const int64_t max_chunks = std::max<int64_t>(1, ceil_div(rows, RB));
+  chunks = std::max<int64_t>(1, std::min(chunks, max_chunks));
+  chunks = std::min<int64_t>(chunks, 65535);
+  int64_t cr = ceil_div(rows, chunks);
+  cr = ceil_div(cr, RB) * RB;
+  pl.chunk_rows = std::max<int64_t>(cr, RB);
+  pl.chunks = (int)ceil_div(rows, pl.chunk_rows);
+  if (pl.chunks < 1) pl.chunks = 1;
+  return pl;
+}
+
+template <typename TA, typename TB1>
+int launch_partial(int n_cells, const CellPtrs& a, const CellPtrs& b1, const float* b2, int64_t rows,
+                   int p, int q1, int q2, const ChunkPlan& pl, float* partial, cudaStream_t st) {
+  dim3 grid(pl.chunks, pl.tiles, n_cells);
+  atb_partial_kernel<TA, TB1><<<grid, NT, 0, st>>>(a, b1, b2, rows, p, q1, q2, pl.chunks,
+                                                   pl.chunk_rows, partial);
+  return check_launch("atb_partial_kernel");
+}
+
+}  // namespace
+}  // namespace kvc
+
+using namespace kvc;
+
+extern "C" size_t kvc_gram_workspace_bytes(int n_cells, int64_t rows, int p, int k) {
+  if (n_cells <= 0 || rows <= 0 || p <= 0 || k < 0) return 0;
+  ChunkPlan pl = plan_chunks(n_cells, rows, p, p + k);
+  return (size_t)n_cells * pl.chunks * (size_t)p * (p + k) * sizeof(float);
+}
+
+extern "C" int kvc_gram(int n_cells, const void* const* a, int64_t rows, int p, int dtype,
+                        const float* omega, int k, double* out, void* workspace, size_t ws_bytes,
+                        void* stream) {
+  if (n_cells <= 0 || n_cells > KVC_MAX_CELLS) return fail(KVC_ERR_ARG, "kvc_gram: bad n_cells");
+  if (rows <= 0 || p <= 0 || k < 0) return fail(KVC_ERR_SHAPE, "kvc_gram: bad shape");
+  if (!dtype_ok(dtype)) return fail(KVC_ERR_DTYPE, "kvc_gram: bad dtype");
+  if (k > 0 && omega == nullptr) return fail(KVC_ERR_ARG, "kvc_gram: omega is NULL");
+  if (!out) return fail(KVC_ERR_ARG, "kvc_gram: out is NULL");
+  ChunkPlan pl = plan_chunks(n_cells, rows, p, p + k);
+  const size_t need = (size_t)n_cells * pl.chunks * (size_t)p * (p + k) * sizeof(float);
+  if (!workspace || ws_bytes < need) return fail(KVC_ERR_WORKSPACE, "kvc_gram: workspace too small");
+  CellPtrs ap;
+  for (int c = 0; c < n_cells; ++c) {
+    if (!a[c]) return fail(KVC_ERR_ARG, "kvc_gram: NULL cell pointer");
+    ap.p[c] = a[c];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* partial = static_cast<float*>(workspace);
+  int rc;
+  KVC_DISPATCH_DTYPE(dtype, T, rc = launch_partial<T, T>(n_cells, ap, ap, omega, rows, p, p, k, pl,
+                                                         partial, st));
+  if (rc) return rc;
+  const int64_t stride = (int64_t)p * p + (int64_t)p * k + 1;
+  const int64_t total = (int64_t)n_cells * p * (p + k);
+  const int blocks = (int)std::min<int64_t>(ceil_div(total, 256), 8 * num_sms());
+  gram_reduce_kernel<<<blocks, 256, 0, st>>>(partial, n_cells, pl.chunks, p, p, k, out, stride);
+  if ((rc = check_launch("gram_reduce_kernel"))) return rc;
+  gram_trace_kernel<<<(n_cells + 63) / 64, 64, 0, st>>>(out, n_cells, p, k, stride);
+  return check_launch("gram_trace_kernel");
+}
+
+extern "C" size_t kvc_core_workspace_bytes(int n_cells, int64_t t, int m, int rd, int rt) {
+  if (n_cells <= 0 || t <= 0 || m <= 0 || rd <= 0 || rt <= 0) return 0;
+  ChunkPlan pl = plan_chunks(n_cells, t, rt, m * rd);
+  return (size_t)n_cells * pl.chunks * (size_t)rt * m * rd * sizeof(float);
+}
+
+extern "C" int kvc_core(int n_cells, const void* const* x_proj_t, const void* const* u_token,
+                        int64_t t, int m, int rd, int rt, int dtype, void* const* core,
+                        void* workspace, size_t ws_bytes, void* stream) {
+  if (n_cells <= 0 || n_cells > KVC_MAX_CELLS) return fail(KVC_ERR_ARG, "kvc_core: bad n_cells");
+  if (t <= 0 || m <= 0 || rd <= 0 || rt <= 0) return fail(KVC_ERR_SHAPE, "kvc_core: bad shape");
+  if (!dtype_ok(dtype)) return fail(KVC_ERR_DTYPE, "kvc_core: bad dtype");
+  const int q = m * rd;
+  ChunkPlan pl = plan_chunks(n_cells, t, rt, q);
+  const size_t need = (size_t)n_cells * pl.chunks * (size_t)rt * q * sizeof(float);
+  if (!workspace || ws_bytes < need) return fail(KVC_ERR_WORKSPACE, "kvc_core: workspace too small");
+  CellPtrs ut, xp;
+  CellPtrsMut cp;
+  for (int c = 0; c < n_cells; ++c) {
+    if (!x_proj_t[c] || !u_token[c] || !core[c]) return fail(KVC_ERR_ARG, "kvc_core: NULL pointer");
+    ut.p[c] = u_token[c];
+    xp.p[c] = x_proj_t[c];
+    cp.p[c] = core[c];
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  float* partial = static_cast<float*>(workspace);
+  int rc;
+  KVC_DISPATCH_DTYPE(dtype, T, rc = launch_partial<T, T>(n_cells, ut, xp, nullptr, t, rt, q, 0, pl,
+                                                         partial, st));
+  if (rc) return rc;
+  const int64_t total = (int64_t)n_cells * rt * q;
+  const int blocks = (int)std::min<int64_t>(ceil_div(total, 256), 8 * num_sms());
+  KVC_DISPATCH_DTYPE(dtype, T,
+                     core_reduce_kernel<T><<<blocks, 256, 0, st>>>(partial, n_cells, pl.chunks, rt,
+                                                                   m, rd, cp));
+  return check_launch("core_reduce_kernel");
+}

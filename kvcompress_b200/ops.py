@@ -1,0 +1,268 @@
+"""torch-facing wrappers of the sm_100a kernels (one function per C ABI stage).
+
+Every function takes CUDA tensors, launches on the current torch stream and
+returns new tensors; nothing synchronises with the host.  A batch of
+"cells" is a list of same-shape, same-dtype contiguous tensors (one layer's
+K and V, or many layers): one launch covers the whole batch.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Sequence
+
+import torch
+
+from kvcompress_b200._native import KVC, check, lib, ptr_array
+
+__all__ = [
+    "DTYPE_CODE",
+    "apply_basis",
+    "cast",
+    "core",
+    "decompress",
+    "gram",
+    "project_feature",
+    "residual_quant",
+    "residual_stats",
+    "sketch_solve",
+    "workspace",
+]
+
+DTYPE_CODE = {torch.float32: KVC.F32, torch.float16: KVC.F16, torch.bfloat16: KVC.BF16,
+              torch.float64: KVC.F64}
+if hasattr(torch, "float8_e4m3fn"):
+    DTYPE_CODE[torch.float8_e4m3fn] = KVC.FP8E4M3
+
+_WS: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _stream() -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
+    """Scratch buffer for one launch, reused per (device, stream).
+
+    Launches on one stream are ordered, so reuse is safe there; another
+    stream gets its own buffer.
+    """
+    dev = torch.device(device)
+    key = (dev.index if dev.index is not None else torch.cuda.current_device(),
+           torch.cuda.current_stream(dev).cuda_stream)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
+        _WS[key] = buf
+    return buf
+
+
+def _cells(xs: Sequence[torch.Tensor], what: str) -> tuple[torch.Tensor, ...]:
+    xs = tuple(xs)
+    if not xs:
+        raise ValueError(f"{what}: empty cell batch")
+    if len(xs) > KVC.MAX_CELLS:
+        raise ValueError(f"{what}: at most {KVC.MAX_CELLS} cells per launch")
+    x0 = xs[0]
+    if not x0.is_cuda:
+        raise RuntimeError(f"{what}: kvcompress_b200 runs on CUDA tensors only (got {x0.device})")
+    for x in xs:
+        if x.shape != x0.shape or x.dtype != x0.dtype or x.device != x0.device:
+            raise ValueError(f"{what}: cells must share shape, dtype and device")
+        if not x.is_contiguous():
+            raise ValueError(f"{what}: cells must be contiguous")
+    return xs
+
+
+def _code(dtype: torch.dtype) -> int:
+    try:
+        return DTYPE_CODE[dtype]
+    except KeyError:
+        raise TypeError(f"unsupported dtype {dtype}") from None
+
+
+def gram(cells: Sequence[torch.Tensor], omega: torch.Tensor | None) -> torch.Tensor:
+    """``[A^T A | A^T Omega | sum(A*A)]`` per cell, A = cell viewed (rows, p)."""
+    cells = _cells(cells, "gram")
+    p = cells[0].shape[-1]
+    rows = cells[0].numel() // p
+    k = 0 if omega is None else int(omega.shape[1])
+    if omega is not None:
+        if omega.dtype != torch.float32 or not omega.is_contiguous() or omega.shape[0] != rows:
+            raise ValueError("gram: omega must be a contiguous float32 (rows, k) tensor")
+    dev = cells[0].device
+    out = torch.empty(len(cells), p * p + p * k + 1, dtype=torch.float64, device=dev)
+    L = lib()
+    ws_n = L.kvc_gram_workspace_bytes(len(cells), rows, p, k)
+    ws = workspace(ws_n, dev)
+    check(L.kvc_gram(len(cells), ptr_array(c.data_ptr() for c in cells), rows, p,
+                     _code(cells[0].dtype), omega.data_ptr() if omega is not None else None, k,
+                     out.data_ptr(), ws.data_ptr(), ws.numel(), _stream()), "kvc_gram")
+    return out
+
+
+def sketch_solve(g: torch.Tensor, *, mode: int, side: int, p: int, n_other: int, k: int, rank: int,
+                 n_power: int, omega: torch.Tensor | None, basis_dtype: torch.dtype,
+                 gram_stride: int | None = None):
+    """Run the per-cell small solver; returns ``(basis, tail, sv2)``."""
+    n = int(g.shape[0])
+    dev = g.device
+    L = lib()
+    if side == KVC.SIDE_LEFT:
+        basis = torch.empty(n, p, rank, dtype=basis_dtype, device=dev)
+    else:
+        basis = torch.empty(n, p, rank, dtype=torch.float64, device=dev)
+    tail = torch.empty(n, dtype=torch.float64, device=dev)
+    sv2 = torch.empty(n, rank, dtype=torch.float64, device=dev)
+    kk = k if mode == KVC.SVD_RANDOMISED else 0
+    ws_n = L.kvc_sketch_solve_workspace_bytes(n, mode, p, kk)
+    ws = workspace(ws_n, dev)
+    stride = gram_stride if gram_stride is not None else int(g.shape[1])
+    check(L.kvc_sketch_solve(n, mode, side, p, n_other, kk, rank, n_power, g.data_ptr(), stride,
+                             omega.data_ptr() if omega is not None else None, basis.data_ptr(),
+                             _code(basis.dtype), sv2.data_ptr(), tail.data_ptr(), ws.data_ptr(),
+                             ws.numel(), _stream()), "kvc_sketch_solve")
+    return basis, tail, sv2
+
+
+def project_feature(xs: Sequence[torch.Tensor], u_feature: Sequence[torch.Tensor]) -> list[torch.Tensor]:
+    """``x_proj`` of each cell in token-unfolding layout ``(T, m * rd)``."""
+    xs = _cells(xs, "project_feature")
+    m, t, d = xs[0].shape
+    rd = int(u_feature[0].shape[1])
+    outs = [torch.empty(t, m * rd, dtype=xs[0].dtype, device=xs[0].device) for _ in xs]
+    check(lib().kvc_project_feature(len(xs), ptr_array(x.data_ptr() for x in xs), m, t, d,
+                                    _code(xs[0].dtype), ptr_array(u.data_ptr() for u in u_feature),
+                                    rd, ptr_array(o.data_ptr() for o in outs), _stream()),
+          "kvc_project_feature")
+    return outs
+
+
+def apply_basis(a: Sequence[torch.Tensor], mat: torch.Tensor) -> list[torch.Tensor]:
+    """``U = A M`` per cell; ``mat`` is (n_cells, p, r) float64."""
+    a = _cells(a, "apply_basis")
+    rows, p = a[0].shape
+    r = int(mat.shape[2])
+    outs = [torch.empty(rows, r, dtype=a[0].dtype, device=a[0].device) for _ in a]
+    check(lib().kvc_apply_basis(len(a), ptr_array(x.data_ptr() for x in a), rows, p,
+                                _code(a[0].dtype), mat.data_ptr(), r,
+                                ptr_array(o.data_ptr() for o in outs), _stream()), "kvc_apply_basis")
+    return outs
+
+
+def core(x_proj_t: Sequence[torch.Tensor], u_token: Sequence[torch.Tensor], m: int, rd: int) -> list[torch.Tensor]:
+    """Tucker core ``(m, rt, rd)`` per cell (tucker.py:261)."""
+    x_proj_t = _cells(x_proj_t, "core")
+    t = int(x_proj_t[0].shape[0])
+    rt = int(u_token[0].shape[1])
+    dev = x_proj_t[0].device
+    outs = [torch.empty(m, rt, rd, dtype=x_proj_t[0].dtype, device=dev) for _ in x_proj_t]
+    L = lib()
+    ws_n = L.kvc_core_workspace_bytes(len(outs), t, m, rd, rt)
+    ws = workspace(ws_n, dev)
+    check(L.kvc_core(len(outs), ptr_array(x.data_ptr() for x in x_proj_t),
+                     ptr_array(u.data_ptr() for u in u_token), t, m, rd, rt,
+                     _code(x_proj_t[0].dtype), ptr_array(o.data_ptr() for o in outs), ws.data_ptr(),
+                     ws.numel(), _stream()), "kvc_core")
+    return outs
+
+
+def _factor_ptrs(factors, n):
+    if factors is None:
+        z = ptr_array([0] * n)
+        return z, z, z, 0, 0
+    core_, ut, ud = factors
+    return (ptr_array(c.data_ptr() for c in core_), ptr_array(u.data_ptr() for u in ut),
+            ptr_array(u.data_ptr() for u in ud), int(ut[0].shape[1]), int(ud[0].shape[1]))
+
+
+def residual_stats(xs, factors, proj, *, bits: int, symmetric: bool, scale_mode: int,
+                   stat_dtype: torch.dtype):
+    """Scale / zero point of the (rotated) residual of each cell."""
+    xs = _cells(xs, "residual_stats")
+    m, t, d = xs[0].shape
+    dev = xs[0].device
+    n = len(xs)
+    ns = d if scale_mode == KVC.SCALE_CHANNEL else 1
+    shape = (d,) if scale_mode == KVC.SCALE_CHANNEL else ()
+    scales = [torch.empty(shape, dtype=torch.float32, device=dev) for _ in xs]
+    zps = [torch.empty(shape, dtype=torch.int32, device=dev) for _ in xs]
+    del ns
+    cp, up, dp, rt, rd = _factor_ptrs(factors, n)
+    L = lib()
+    ws_n = L.kvc_residual_stats_workspace_bytes(n, m * t, d)
+    ws = workspace(ws_n, dev)
+    check(L.kvc_residual_stats(n, ptr_array(x.data_ptr() for x in xs), m, t, d, _code(xs[0].dtype),
+                               cp, up, dp, rt, rd, proj.data_ptr() if proj is not None else None,
+                               bits, int(symmetric), scale_mode, _code(stat_dtype),
+                               ptr_array(s.data_ptr() for s in scales),
+                               ptr_array(z.data_ptr() for z in zps), ws.data_ptr(), ws.numel(),
+                               _stream()), "kvc_residual_stats")
+    return scales, zps
+
+
+def residual_quant(xs, factors, proj, scales, zps, *, bits: int, symmetric: bool, scale_mode: int,
+                   group_size: int | None, stat_dtype: torch.dtype, arith_dtype: torch.dtype):
+    """Quantised, bit-packed residual codes ``(m*T, ceil(d*bits/8))`` per cell.
+
+    With ``scale_mode == SCALE_GROUP`` the per-row group scales are computed
+    here: pass ``scales = zps = None`` and receive them back.
+    """
+    xs = _cells(xs, "residual_quant")
+    m, t, d = xs[0].shape
+    dev = xs[0].device
+    n = len(xs)
+    if scale_mode == KVC.SCALE_GROUP:
+        ng = d // int(group_size)
+        scales = [torch.empty(m * t, ng, dtype=torch.float32, device=dev) for _ in xs]
+        zps = [torch.empty(m * t, ng, dtype=torch.int32, device=dev) for _ in xs]
+    cb = (d * bits + 7) // 8
+    codes = [torch.empty(m * t, cb, dtype=torch.uint8, device=dev) for _ in xs]
+    cp, up, dp, rt, rd = _factor_ptrs(factors, n)
+    check(lib().kvc_residual_quant(n, ptr_array(x.data_ptr() for x in xs), m, t, d,
+                                   _code(xs[0].dtype), cp, up, dp, rt, rd,
+                                   proj.data_ptr() if proj is not None else None, bits,
+                                   int(symmetric), scale_mode, int(group_size or 0),
+                                   _code(stat_dtype), _code(arith_dtype),
+                                   ptr_array(s.data_ptr() for s in scales),
+                                   ptr_array(z.data_ptr() for z in zps),
+                                   ptr_array(c.data_ptr() for c in codes), _stream()),
+          "kvc_residual_quant")
+    return codes, scales, zps
+
+
+def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=None, bits: int = 0,
+               symmetric: bool = True, scale_mode: int = KVC.SCALE_CHANNEL, group_size=None,
+               factors=None, proj=None, t0: int = 0, t1: int | None = None, n_cells: int = 1,
+               device=None, out=None):
+    """Fused decode of ``n_cells`` cells; returns a list of ``(m, t1-t0, d)``."""
+    m, t, d = (int(s) for s in shape)
+    t1 = t if t1 is None else int(t1)
+    if out is None:
+        out = [torch.empty(m, t1 - t0, d, dtype=out_dtype, device=device) for _ in range(n_cells)]
+    n = len(out)
+    cp, up, dp, rt, rd = _factor_ptrs(factors, n)
+    fdt = _code(factors[0][0].dtype) if factors is not None else KVC.F16
+    if bits > 0:
+        c_arr = ptr_array(c.data_ptr() for c in codes)
+        s_arr = ptr_array(s.data_ptr() for s in scales)
+        z_arr = ptr_array(z.data_ptr() for z in zps)
+    else:
+        c_arr = s_arr = z_arr = ptr_array([0] * n)
+    check(lib().kvc_decompress(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
+                               int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
+                               proj.data_ptr() if proj is not None else None, t0, t1,
+                               _code(out_dtype), ptr_array(o.data_ptr() for o in out), _stream()),
+          "kvc_decompress")
+    return out
+
+
+def cast(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
+    """``x.to(dtype)`` through the extension (fp32/fp16/bf16/float8_e4m3fn)."""
+    if not x.is_cuda:
+        raise RuntimeError("cast: CUDA tensors only")
+    x = x.contiguous()
+    out = torch.empty(x.shape, dtype=dtype, device=x.device)
+    check(lib().kvc_cast(x.numel(), x.data_ptr(), _code(x.dtype), out.data_ptr(), _code(dtype),
+                         _stream()), "kvc_cast")
+    return out
