@@ -45,6 +45,7 @@ class CellResult:
     packed: torch.Tensor | None
     scale: torch.Tensor | None
     zero_point: torch.Tensor | None
+    factors_stored: tuple | None = None  # (core, u_token, u_feature) in the payload's factor dtype
 
 
 def scale_mode_of(per_channel: bool, group_size: int | None, d: int) -> int:
@@ -120,8 +121,13 @@ def compress_cells(
     symmetric: bool = True,
     per_channel: bool = True,
     group_size: int | None = None,
+    factor_dtype: torch.dtype | None = None,
 ) -> list[CellResult]:
-    """Compress same-shape cells ``(m, T, d)`` sharing one allocation."""
+    """Compress same-shape cells ``(m, T, d)`` sharing one allocation.
+
+    With ``factor_dtype`` the factors are also returned cast to it (one
+    launch per factor kind for the whole batch), as the payload stores them.
+    """
     if bits not in (0, 2, 4, 8):
         raise ValueError(f"bits must be 0, 2, 4, or 8, got {bits}")
     x0 = xs[0]
@@ -135,7 +141,8 @@ def compress_cells(
             out += compress_cells(xs[i:i + KVC.MAX_CELLS], r_token=r_token, r_feature=r_feature,
                                   bits=bits, svd=svd, cap=cap, forced_randomised=forced_randomised,
                                   seed=seed, jl_distribution=jl_distribution, sparsity=sparsity,
-                                  symmetric=symmetric, per_channel=per_channel, group_size=group_size)
+                                  symmetric=symmetric, per_channel=per_channel, group_size=group_size,
+                                  factor_dtype=factor_dtype)
         return out
     mode_scale = scale_mode_of(per_channel, group_size, d) if bits > 0 else KVC.SCALE_CHANNEL
     core, u_token, u_feature, tail_t, tail_f = tucker_cells(
@@ -158,9 +165,22 @@ def compress_cells(
             packed, _, _ = ops.residual_quant(
                 xs, factors, proj, scale, zps, bits=bits, symmetric=symmetric, scale_mode=mode_scale,
                 group_size=None, stat_dtype=torch.float32, arith_dtype=torch.float32)
+    stored = [None] * n
+    if factor_dtype is not None:
+        batches = [_batch_of(core), _batch_of(u_token), _batch_of(u_feature)]
+        cast = [b if b.dtype == factor_dtype else ops.cast(b, factor_dtype) for b in batches]
+        stored = [(cast[0][i], cast[1][i], cast[2][i]) for i in range(n)]
     return [CellResult(core=core[i], u_token=u_token[i], u_feature=u_feature[i],
                        tail_token=tail_t[i], tail_feature=tail_f[i], bits=bits, packed=packed[i],
-                       scale=scale[i], zero_point=zps[i]) for i in range(n)]
+                       scale=scale[i], zero_point=zps[i], factors_stored=stored[i]) for i in range(n)]
+
+
+def _batch_of(views: list[torch.Tensor]) -> torch.Tensor:
+    """The (n, ...) tensor a list of per-cell views was cut from."""
+    base = views[0]._base
+    if base is not None and base.shape[0] == len(views) and base[0].data_ptr() == views[0].data_ptr():
+        return base
+    return torch.stack(views)
 
 
 def decompress_cells(payloads, out_dtype: torch.dtype | None = None, t0: int = 0,

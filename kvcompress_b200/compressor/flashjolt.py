@@ -46,4 +46,5 @@ class FlashJoLTCompressor(JoLTCompressor):
         return compress_cells(xs, r_token=rt, r_feature=rd, bits=bits, svd=self.svd, cap=cap,
                               forced_randomised=True, seed=self.seed,
                               jl_distribution=self.jl_distribution, symmetric=self.symmetric_quant,
-                              per_channel=self.per_channel_quant, group_size=self.group_size)
+                              per_channel=self.per_channel_quant, group_size=self.group_size,
+                              factor_dtype=self.factor_dtype)

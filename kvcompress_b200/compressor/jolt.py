@@ -182,7 +182,7 @@ class JoLTCompressor(KVCompressor):
         return compress_cells(xs, r_token=rt, r_feature=rd, bits=bits, svd=self.svd, seed=self.seed,
                               jl_distribution=self.jl_distribution,
                               symmetric=self.symmetric_quant, per_channel=self.per_channel_quant,
-                              group_size=self.group_size)
+                              group_size=self.group_size, factor_dtype=self.factor_dtype)
 
     def compress_cell(self, x: torch.Tensor, allocation: Any) -> JoLTFactors:
         """One cell at a given allocation (jolt.py:273-329)."""
@@ -197,9 +197,12 @@ class JoLTCompressor(KVCompressor):
         if tails is None:
             tails = torch.stack([r.tail_token, r.tail_feature]).cpu().tolist()
         fdt = self.factor_dtype
-        core = ops.cast(r.core, fdt) if r.core.dtype != fdt else r.core.contiguous()
-        u_token = ops.cast(r.u_token, fdt) if r.u_token.dtype != fdt else r.u_token.contiguous()
-        u_feature = ops.cast(r.u_feature, fdt) if r.u_feature.dtype != fdt else r.u_feature.contiguous()
+        if r.factors_stored is not None and r.factors_stored[0].dtype == fdt:
+            core, u_token, u_feature = r.factors_stored
+        else:
+            core = ops.cast(r.core, fdt) if r.core.dtype != fdt else r.core.contiguous()
+            u_token = ops.cast(r.u_token, fdt) if r.u_token.dtype != fdt else r.u_token.contiguous()
+            u_feature = ops.cast(r.u_feature, fdt) if r.u_feature.dtype != fdt else r.u_feature.contiguous()
         data: dict[str, Any] = {"core": core, "u_token": u_token, "u_feature": u_feature}
         meta: dict[str, Any] = {
             "method": "jolt",

@@ -140,19 +140,17 @@ struct ChunkPlan {
   int tiles;
 };
 
+// The chunking depends on the row count only (never on the batch size or
+// the GPU), so a cell gets bit-identical sums whether it is compressed alone
+// or batched with other layers.
 ChunkPlan plan_chunks(int n_cells, int64_t rows, int p, int q) {
+  (void)n_cells;
   ChunkPlan pl;
   pl.tiles = (int)(ceil_div(p, TB) * ceil_div(q, TB));
-  const int64_t target = 4LL * num_sms();
-  int64_t chunks = ceil_div(target, (int64_t)pl.tiles * std::max(1, n_cells));
-  const int64_t max_chunks = std::max<int64_t>(1, ceil_div(rows, RB));
-  chunks = std::max<int64_t>(1, std::min(chunks, max_chunks));
-  chunks = std::min<int64_t>(chunks, 65535);
-  int64_t cr = ceil_div(rows, chunks);
+  int64_t cr = std::max<int64_t>(2048, ceil_div(rows, 128));
   cr = ceil_div(cr, RB) * RB;
-  pl.chunk_rows = std::max<int64_t>(cr, RB);
-  pl.chunks = (int)ceil_div(rows, pl.chunk_rows);
-  if (pl.chunks < 1) pl.chunks = 1;
+  pl.chunk_rows = cr;
+  pl.chunks = (int)std::max<int64_t>(1, ceil_div(rows, cr));
   return pl;
 }
 

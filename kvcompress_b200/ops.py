@@ -36,6 +36,44 @@ if hasattr(torch, "float8_e4m3fn"):
 
 _WS: dict[tuple[int, int], torch.Tensor] = {}
 
+# Optional launch log for the benchmark: (stage, start event, end event,
+# kernel launches, algorithmic bytes) per C ABI call on the current stream.
+_TRACE: list | None = None
+
+
+def trace_start() -> None:
+    """Record CUDA events around every stage launched from now on."""
+    global _TRACE
+    _TRACE = []
+
+
+def trace_stop() -> list:
+    """Stop recording and return the log."""
+    global _TRACE
+    log, _TRACE = _TRACE or [], None
+    return log
+
+
+class _Stage:
+    __slots__ = ("name", "launches", "nbytes", "ev0")
+
+    def __init__(self, name: str, launches: int, nbytes: int):
+        self.name, self.launches, self.nbytes = name, launches, nbytes
+        self.ev0 = None
+
+    def __enter__(self):
+        if _TRACE is not None:
+            self.ev0 = torch.cuda.Event(enable_timing=True)
+            self.ev0.record()
+        return self
+
+    def __exit__(self, *exc):
+        if _TRACE is not None and self.ev0 is not None and exc[0] is None:
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev1.record()
+            _TRACE.append((self.name, self.ev0, ev1, self.launches, self.nbytes))
+        return False
+
 
 def _stream() -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
@@ -95,9 +133,11 @@ def gram(cells: Sequence[torch.Tensor], omega: torch.Tensor | None) -> torch.Ten
     L = lib()
     ws_n = L.kvc_gram_workspace_bytes(len(cells), rows, p, k)
     ws = workspace(ws_n, dev)
-    check(L.kvc_gram(len(cells), ptr_array(c.data_ptr() for c in cells), rows, p,
-                     _code(cells[0].dtype), omega.data_ptr() if omega is not None else None, k,
-                     out.data_ptr(), ws.data_ptr(), ws.numel(), _stream()), "kvc_gram")
+    nbytes = len(cells) * cells[0].numel() * cells[0].element_size() + (0 if omega is None else omega.numel() * 4)
+    with _Stage("gram", 3, nbytes):
+        check(L.kvc_gram(len(cells), ptr_array(c.data_ptr() for c in cells), rows, p,
+                         _code(cells[0].dtype), omega.data_ptr() if omega is not None else None, k,
+                         out.data_ptr(), ws.data_ptr(), ws.numel(), _stream()), "kvc_gram")
     return out
 
 
@@ -118,10 +158,11 @@ def sketch_solve(g: torch.Tensor, *, mode: int, side: int, p: int, n_other: int,
     ws_n = L.kvc_sketch_solve_workspace_bytes(n, mode, p, kk)
     ws = workspace(ws_n, dev)
     stride = gram_stride if gram_stride is not None else int(g.shape[1])
-    check(L.kvc_sketch_solve(n, mode, side, p, n_other, kk, rank, n_power, g.data_ptr(), stride,
-                             omega.data_ptr() if omega is not None else None, basis.data_ptr(),
-                             _code(basis.dtype), sv2.data_ptr(), tail.data_ptr(), ws.data_ptr(),
-                             ws.numel(), _stream()), "kvc_sketch_solve")
+    with _Stage("sketch_solve", 1, g.numel() * 8):
+        check(L.kvc_sketch_solve(n, mode, side, p, n_other, kk, rank, n_power, g.data_ptr(), stride,
+                                 omega.data_ptr() if omega is not None else None, basis.data_ptr(),
+                                 _code(basis.dtype), sv2.data_ptr(), tail.data_ptr(), ws.data_ptr(),
+                                 ws.numel(), _stream()), "kvc_sketch_solve")
     return basis, tail, sv2
 
 
@@ -131,10 +172,12 @@ def project_feature(xs: Sequence[torch.Tensor], u_feature: Sequence[torch.Tensor
     m, t, d = xs[0].shape
     rd = int(u_feature[0].shape[1])
     outs = [torch.empty(t, m * rd, dtype=xs[0].dtype, device=xs[0].device) for _ in xs]
-    check(lib().kvc_project_feature(len(xs), ptr_array(x.data_ptr() for x in xs), m, t, d,
-                                    _code(xs[0].dtype), ptr_array(u.data_ptr() for u in u_feature),
-                                    rd, ptr_array(o.data_ptr() for o in outs), _stream()),
-          "kvc_project_feature")
+    nbytes = len(xs) * (xs[0].numel() + outs[0].numel()) * xs[0].element_size()
+    with _Stage("project_feature", 1, nbytes):
+        check(lib().kvc_project_feature(len(xs), ptr_array(x.data_ptr() for x in xs), m, t, d,
+                                        _code(xs[0].dtype), ptr_array(u.data_ptr() for u in u_feature),
+                                        rd, ptr_array(o.data_ptr() for o in outs), _stream()),
+              "kvc_project_feature")
     return outs
 
 
@@ -143,10 +186,13 @@ def apply_basis(a: Sequence[torch.Tensor], mat: torch.Tensor) -> list[torch.Tens
     a = _cells(a, "apply_basis")
     rows, p = a[0].shape
     r = int(mat.shape[2])
-    outs = [torch.empty(rows, r, dtype=a[0].dtype, device=a[0].device) for _ in a]
-    check(lib().kvc_apply_basis(len(a), ptr_array(x.data_ptr() for x in a), rows, p,
-                                _code(a[0].dtype), mat.data_ptr(), r,
-                                ptr_array(o.data_ptr() for o in outs), _stream()), "kvc_apply_basis")
+    batch = torch.empty(len(a), rows, r, dtype=a[0].dtype, device=a[0].device)
+    outs = [batch[i] for i in range(len(a))]
+    nbytes = len(a) * (a[0].numel() + outs[0].numel()) * a[0].element_size()
+    with _Stage("apply_basis", 1, nbytes):
+        check(lib().kvc_apply_basis(len(a), ptr_array(x.data_ptr() for x in a), rows, p,
+                                    _code(a[0].dtype), mat.data_ptr(), r,
+                                    ptr_array(o.data_ptr() for o in outs), _stream()), "kvc_apply_basis")
     return outs
 
 
@@ -156,14 +202,17 @@ def core(x_proj_t: Sequence[torch.Tensor], u_token: Sequence[torch.Tensor], m: i
     t = int(x_proj_t[0].shape[0])
     rt = int(u_token[0].shape[1])
     dev = x_proj_t[0].device
-    outs = [torch.empty(m, rt, rd, dtype=x_proj_t[0].dtype, device=dev) for _ in x_proj_t]
+    batch = torch.empty(len(x_proj_t), m, rt, rd, dtype=x_proj_t[0].dtype, device=dev)
+    outs = [batch[i] for i in range(len(x_proj_t))]
     L = lib()
     ws_n = L.kvc_core_workspace_bytes(len(outs), t, m, rd, rt)
     ws = workspace(ws_n, dev)
-    check(L.kvc_core(len(outs), ptr_array(x.data_ptr() for x in x_proj_t),
-                     ptr_array(u.data_ptr() for u in u_token), t, m, rd, rt,
-                     _code(x_proj_t[0].dtype), ptr_array(o.data_ptr() for o in outs), ws.data_ptr(),
-                     ws.numel(), _stream()), "kvc_core")
+    nbytes = len(outs) * (x_proj_t[0].numel() + u_token[0].numel()) * x_proj_t[0].element_size()
+    with _Stage("core", 2, nbytes):
+        check(L.kvc_core(len(outs), ptr_array(x.data_ptr() for x in x_proj_t),
+                         ptr_array(u.data_ptr() for u in u_token), t, m, rd, rt,
+                         _code(x_proj_t[0].dtype), ptr_array(o.data_ptr() for o in outs), ws.data_ptr(),
+                         ws.numel(), _stream()), "kvc_core")
     return outs
 
 
@@ -192,12 +241,13 @@ def residual_stats(xs, factors, proj, *, bits: int, symmetric: bool, scale_mode:
     L = lib()
     ws_n = L.kvc_residual_stats_workspace_bytes(n, m * t, d)
     ws = workspace(ws_n, dev)
-    check(L.kvc_residual_stats(n, ptr_array(x.data_ptr() for x in xs), m, t, d, _code(xs[0].dtype),
-                               cp, up, dp, rt, rd, proj.data_ptr() if proj is not None else None,
-                               bits, int(symmetric), scale_mode, _code(stat_dtype),
-                               ptr_array(s.data_ptr() for s in scales),
-                               ptr_array(z.data_ptr() for z in zps), ws.data_ptr(), ws.numel(),
-                               _stream()), "kvc_residual_stats")
+    with _Stage("residual_stats", 2, n * xs[0].numel() * xs[0].element_size()):
+        check(L.kvc_residual_stats(n, ptr_array(x.data_ptr() for x in xs), m, t, d, _code(xs[0].dtype),
+                                   cp, up, dp, rt, rd, proj.data_ptr() if proj is not None else None,
+                                   bits, int(symmetric), scale_mode, _code(stat_dtype),
+                                   ptr_array(s.data_ptr() for s in scales),
+                                   ptr_array(z.data_ptr() for z in zps), ws.data_ptr(), ws.numel(),
+                                   _stream()), "kvc_residual_stats")
     return scales, zps
 
 
@@ -219,15 +269,17 @@ def residual_quant(xs, factors, proj, scales, zps, *, bits: int, symmetric: bool
     cb = (d * bits + 7) // 8
     codes = [torch.empty(m * t, cb, dtype=torch.uint8, device=dev) for _ in xs]
     cp, up, dp, rt, rd = _factor_ptrs(factors, n)
-    check(lib().kvc_residual_quant(n, ptr_array(x.data_ptr() for x in xs), m, t, d,
-                                   _code(xs[0].dtype), cp, up, dp, rt, rd,
-                                   proj.data_ptr() if proj is not None else None, bits,
-                                   int(symmetric), scale_mode, int(group_size or 0),
-                                   _code(stat_dtype), _code(arith_dtype),
-                                   ptr_array(s.data_ptr() for s in scales),
-                                   ptr_array(z.data_ptr() for z in zps),
-                                   ptr_array(c.data_ptr() for c in codes), _stream()),
-          "kvc_residual_quant")
+    nbytes = n * (xs[0].numel() * xs[0].element_size() + codes[0].numel())
+    with _Stage("residual_quant", 1, nbytes):
+        check(lib().kvc_residual_quant(n, ptr_array(x.data_ptr() for x in xs), m, t, d,
+                                       _code(xs[0].dtype), cp, up, dp, rt, rd,
+                                       proj.data_ptr() if proj is not None else None, bits,
+                                       int(symmetric), scale_mode, int(group_size or 0),
+                                       _code(stat_dtype), _code(arith_dtype),
+                                       ptr_array(s.data_ptr() for s in scales),
+                                       ptr_array(z.data_ptr() for z in zps),
+                                       ptr_array(c.data_ptr() for c in codes), _stream()),
+              "kvc_residual_quant")
     return codes, scales, zps
 
 
@@ -249,11 +301,15 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
         z_arr = ptr_array(z.data_ptr() for z in zps)
     else:
         c_arr = s_arr = z_arr = ptr_array([0] * n)
-    check(lib().kvc_decompress(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
-                               int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
-                               proj.data_ptr() if proj is not None else None, t0, t1,
-                               _code(out_dtype), ptr_array(o.data_ptr() for o in out), _stream()),
-          "kvc_decompress")
+    nbytes = n * out[0].numel() * out[0].element_size()
+    if bits > 0:
+        nbytes += sum(c.numel() for c in codes) * (t1 - t0) // t
+    with _Stage("decompress", 1, nbytes):
+        check(lib().kvc_decompress(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
+                                   int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
+                                   proj.data_ptr() if proj is not None else None, t0, t1,
+                                   _code(out_dtype), ptr_array(o.data_ptr() for o in out), _stream()),
+              "kvc_decompress")
     return out
 
 
@@ -263,6 +319,7 @@ def cast(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
         raise RuntimeError("cast: CUDA tensors only")
     x = x.contiguous()
     out = torch.empty(x.shape, dtype=dtype, device=x.device)
-    check(lib().kvc_cast(x.numel(), x.data_ptr(), _code(x.dtype), out.data_ptr(), _code(dtype),
-                         _stream()), "kvc_cast")
+    with _Stage("cast", 1, x.numel() * (x.element_size() + out.element_size())):
+        check(lib().kvc_cast(x.numel(), x.data_ptr(), _code(x.dtype), out.data_ptr(), _code(dtype),
+                             _stream()), "kvc_cast")
     return out

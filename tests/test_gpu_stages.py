@@ -1,0 +1,211 @@
+"""Stage-level parity of the sm_100a kernels against the oracle / golden vectors.
+
+Integer outputs (scales from the same values, codes, packed bytes, fp8
+bytes) are compared bit for bit; floating-point stages with tolerances
+written next to each assert.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from kvcompress_b200 import ops
+from kvcompress_b200._native import KVC
+from kvcompress_b200.compressor.quantization import dequantize_tensor, quantize_tensor
+
+from _parity import f32, rel, to_cuda
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("case,bits", [("f32_flash_r1_b8", 8), ("bf16_flash_r1_b8", 8),
+                                       ("f32_flash_r4_b4", 4), ("f16_flash_r2_b2", 2)])
+def test_codes_bit_exact_given_reference_rotated(golden, case, bits):
+    """Same fp32 rotated residual -> same scales and same packed codes, bit for bit."""
+    rot = golden[case + "/rotated"]
+    cell = torch.from_numpy(rot).cuda().view(1, *rot.shape)
+    scales, zps = ops.residual_stats([cell], None, None, bits=bits, symmetric=True,
+                                     scale_mode=KVC.SCALE_CHANNEL, stat_dtype=torch.float32)
+    np.testing.assert_array_equal(scales[0].cpu().numpy(), golden[case + "/payload_residual_scale"])
+    np.testing.assert_array_equal(zps[0].cpu().numpy(), golden[case + "/payload_residual_zero_point"])
+    codes, _, _ = ops.residual_quant([cell], None, None, scales, zps, bits=bits, symmetric=True,
+                                     scale_mode=KVC.SCALE_CHANNEL, group_size=None,
+                                     stat_dtype=torch.float32, arith_dtype=torch.float32)
+    np.testing.assert_array_equal(codes[0].cpu().numpy(), golden.raw(case + "/payload_residual_packed"))
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+@pytest.mark.parametrize("symmetric", [True, False])
+@pytest.mark.parametrize("mode", ["channel", "group", "tensor"])
+def test_quantize_tensor_bit_exact(golden, bits, symmetric, mode):
+    x = torch.from_numpy(golden["quant/x"]).cuda()
+    tag = f"quant/b{bits}_{'sym' if symmetric else 'asym'}_{mode}/"
+    kw = dict(symmetric=symmetric, per_channel=(mode == "channel"), group_size=(32 if mode == "group" else None))
+    pay = quantize_tensor(x, dtype=f"int{bits}", **kw)
+    np.testing.assert_array_equal(pay["q"].cpu().numpy(), golden[tag + "q"])
+    np.testing.assert_array_equal(pay["scale"].cpu().numpy(), golden[tag + "scale"])
+    np.testing.assert_array_equal(pay["zero_point"].cpu().numpy(), golden[tag + "zero_point"])
+    deq = dequantize_tensor(pay, dtype=f"int{bits}", **kw)
+    np.testing.assert_array_equal(deq.cpu().numpy(), golden[tag + "deq"])
+
+
+@pytest.mark.parametrize("bits", [2, 4, 8])
+def test_quant_only_compressor_bit_exact(golden, bits):
+    from kvcompress_b200 import build_compressor
+
+    x = to_cuda(golden["intonly/x"], "bf16")
+    comp = build_compressor(f"int{bits}")
+    kp, vp = comp.compress(x, x)
+    p = f"intonly{bits}/"
+    np.testing.assert_array_equal(kp.data["q"].cpu().numpy(), golden[p + "q"])
+    np.testing.assert_array_equal(kp.data["scale"].cpu().numpy(), golden[p + "scale"])
+    np.testing.assert_array_equal(vp.data["q"].cpu().numpy(), golden[p + "q"])
+    kd, _ = comp.decompress(kp, vp)
+    assert kd.dtype == torch.bfloat16 and kd.shape == x.shape
+    np.testing.assert_array_equal(f32(kd), golden[p + "decompressed"])
+    assert kp.bytes_compressed == golden.meta[f"intonly{bits}"]["bytes"]
+
+
+def test_fp8_cast_all_bf16_patterns(golden):
+    allv = torch.arange(65536, dtype=torch.int32).to(torch.int16).view(torch.bfloat16).cuda()
+    got = ops.cast(allv, torch.float8_e4m3fn).view(torch.uint8).cpu().numpy()
+    np.testing.assert_array_equal(got, golden["fp8/all_bf16_bytes"])
+    # every fp8 byte back to bf16 / fp32 as torch decodes it
+    b = torch.arange(256, dtype=torch.int32).to(torch.uint8).view(torch.float8_e4m3fn)
+    for dt in (torch.bfloat16, torch.float32, torch.float16):
+        ours = ops.cast(b.cuda(), dt).cpu()
+        ref = b.to(dt)
+        assert torch.equal(ours.isnan(), ref.isnan())
+        ok = ~ref.isnan()
+        assert torch.equal(ours[ok], ref[ok])
+
+
+def test_fp8_compressor(golden):
+    from kvcompress_b200 import build_compressor
+
+    y = to_cuda(golden["fp8/x"], "bf16")
+    comp = build_compressor("fp8")
+    kp, vp = comp.compress(y, y)
+    np.testing.assert_array_equal(kp.data["value"].view(torch.uint8).cpu().numpy(), golden["fp8/bytes"])
+    kd, _ = comp.decompress(kp, vp)
+    np.testing.assert_array_equal(np.isnan(f32(kd)), np.isnan(golden["fp8/decompressed"]))
+    ok = ~np.isnan(golden["fp8/decompressed"])
+    np.testing.assert_array_equal(f32(kd)[ok], golden["fp8/decompressed"][ok])
+
+
+@pytest.mark.parametrize("dt", ["f32", "bf16"])
+def test_gram_matches_fp64(dt):
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(3, 1000, 64, generator=g)
+    om = torch.randn(3000, 7, generator=g)
+    cells = [to_cuda(x.numpy(), dt).view(3000, 64), to_cuda((x * 2).numpy(), dt).view(3000, 64)]
+    out = ops.gram(cells, om.cuda()).cpu().numpy()
+    for i, c in enumerate(cells):
+        a = c.float().cpu().numpy().astype(np.float64)
+        G = a.T @ a
+        Y = a.T @ om.numpy().astype(np.float64)
+        o = out[i]
+        assert rel(o[:64 * 64].reshape(64, 64), G) < 1e-6
+        assert rel(o[64 * 64:64 * 64 + 64 * 7].reshape(64, 7), Y) < 1e-6
+        assert abs(o[-1] / np.sum(a * a) - 1) < 1e-6
+    # bit-reproducible
+    out2 = ops.gram(cells, om.cuda()).cpu().numpy()
+    np.testing.assert_array_equal(out, out2)
+
+
+@pytest.mark.parametrize("p,side", [(64, KVC.SIDE_LEFT), (128, KVC.SIDE_LEFT), (40, KVC.SIDE_RIGHT)])
+def test_exact_solver_matches_numpy(p, side):
+    g = torch.Generator().manual_seed(p)
+    a = torch.randn(3 * p, p, generator=g, dtype=torch.float64) @ torch.diag(
+        torch.linspace(3, 0.1, p, dtype=torch.float64))
+    G = (a.T @ a).numpy()
+    gram = torch.from_numpy(np.concatenate([G.ravel(), [np.trace(G)]])[None]).cuda()
+    rank = 5
+    basis, tail, sv2 = ops.sketch_solve(gram, mode=KVC.SVD_EXACT, side=side, p=p, n_other=3 * p, k=0,
+                                        rank=rank, n_power=2, omega=None,
+                                        basis_dtype=torch.float32 if side == KVC.SIDE_LEFT else torch.float64)
+    w, v = np.linalg.eigh(G)
+    w, v = w[::-1], v[:, ::-1]
+    assert rel(sv2[0].cpu().numpy(), w[:rank]) < 1e-10
+    assert abs(tail[0].item() - w[rank:].sum() / w.sum()) < 1e-10
+    b = basis[0].double().cpu().numpy()
+    if side == KVC.SIDE_LEFT:
+        assert rel(b @ b.T, v[:, :rank] @ v[:, :rank].T) < 1e-5
+    else:
+        u = a.numpy() @ b  # U = A M has orthonormal columns
+        assert rel(u.T @ u, np.eye(rank)) < 1e-8
+
+
+def test_randomised_solver_full_sketch_is_exact():
+    """With k = p the sketch spans everything: randomised == exact."""
+    p = 24
+    g = torch.Generator().manual_seed(1)
+    a = torch.randn(200, p, generator=g, dtype=torch.float64)
+    G = (a.T @ a).numpy()
+    om = torch.randn(p, p, generator=g, dtype=torch.float32)
+    gram = torch.from_numpy(np.concatenate([G.ravel(), [np.trace(G)]])[None]).cuda()
+    m_r, t_r, s_r = ops.sketch_solve(gram, mode=KVC.SVD_RANDOMISED, side=KVC.SIDE_RIGHT, p=p, n_other=200,
+                                     k=p, rank=3, n_power=2, omega=om.cuda(), basis_dtype=torch.float64)
+    m_e, t_e, s_e = ops.sketch_solve(gram, mode=KVC.SVD_EXACT, side=KVC.SIDE_RIGHT, p=p, n_other=200,
+                                     k=0, rank=3, n_power=2, omega=None, basis_dtype=torch.float64)
+    assert rel(s_r.cpu().numpy(), s_e.cpu().numpy()) < 1e-10
+    ur = a.numpy() @ m_r[0].cpu().numpy()
+    ue = a.numpy() @ m_e[0].cpu().numpy()
+    assert rel(ur @ ur.T, ue @ ue.T) < 1e-8
+
+
+def test_decompress_reference_payloads(golden):
+    """Fused decode of the reference's own payloads vs the oracle decode."""
+    for case in ["f32_flash_r1_b8", "f32_flash_r4_b4", "bf16_flash_r1_b8", "bf16_flash_r128_b4",
+                 "bf16_jolt_r8_b2", "f16_flash_r2_b2", "bf16_flash_r3_b0"]:
+        meta = golden.meta[case]
+        m, t, d = meta["shape"]
+        bits = meta["alloc"][2]
+        p = case + "/"
+        proj = golden[f"jl/pi_d{d}_seed0"]
+        ref = oracle.jolt_decompress_cell(
+            golden.raw(p + "payload_core"), golden.raw(p + "payload_u_token"),
+            golden.raw(p + "payload_u_feature"), golden.raw(p + "payload_residual_packed"),
+            golden[p + "payload_residual_scale"], golden[p + "payload_residual_zero_point"], bits,
+            proj, meta["dtype"], (m, t, d))
+        dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[meta["dtype"]]
+        fac = ([torch.from_numpy(golden.raw(p + "payload_core")).cuda()],
+               [torch.from_numpy(golden.raw(p + "payload_u_token")).cuda()],
+               [torch.from_numpy(golden.raw(p + "payload_u_feature")).cuda()])
+        kw = {}
+        if bits:
+            kw = dict(codes=[torch.from_numpy(golden.raw(p + "payload_residual_packed")).cuda()],
+                      scales=[torch.from_numpy(golden[p + "payload_residual_scale"]).cuda()],
+                      zps=[torch.from_numpy(golden[p + "payload_residual_zero_point"]).cuda()],
+                      bits=bits, proj=torch.from_numpy(proj).cuda())
+        out = ops.decompress((m, t, d), dt, factors=fac, device="cuda", **kw)[0]
+        got = f32(out)
+        # fp32: summation order only; 16-bit: a few last-bit flips of the final cast
+        assert rel(got, ref) < (1e-6 if dt == torch.float32 else 2e-3), case
+        assert rel(got, golden[p + "decompressed"]) < (1e-5 if dt == torch.float32 else 4e-3), case
+
+
+def test_residual_kernel_on_reference_factors(golden):
+    """Scales and codes from the reference's own factors agree up to ties."""
+    for case in ["bf16_flash_r1_b8", "f32_flash_r4_b4", "bf16_flash_r128_b4"]:
+        meta = golden.meta[case]
+        m, t, d = meta["shape"]
+        bits = meta["alloc"][2]
+        p = case + "/"
+        dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[meta["dtype"]]
+        x = to_cuda(golden.case_input(case), meta["dtype"])
+        fac = ([to_cuda(golden[p + "core"], meta["dtype"])], [to_cuda(golden[p + "u_token"], meta["dtype"])],
+               [to_cuda(golden[p + "u_feature"], meta["dtype"])])
+        proj = torch.from_numpy(golden[f"jl/pi_d{d}_seed0"]).cuda()
+        scales, zps = ops.residual_stats([x], fac, proj, bits=bits, symmetric=True,
+                                         scale_mode=KVC.SCALE_CHANNEL, stat_dtype=torch.float32)
+        assert rel(scales[0].cpu().numpy(), golden[p + "payload_residual_scale"]) < 1e-5
+        codes, _, _ = ops.residual_quant([x], fac, proj, scales, zps, bits=bits, symmetric=True,
+                                         scale_mode=KVC.SCALE_CHANNEL, group_size=None,
+                                         stat_dtype=torch.float32, arith_dtype=torch.float32)
+        mism = np.mean(codes[0].cpu().numpy() != golden.raw(p + "payload_residual_packed"))
+        assert mism < 2e-3, (case, mism)
+        del dt
