@@ -138,6 +138,9 @@ int kvc_core(int n_cells, const void* const* x_proj_t, const void* const* u_toke
  * quantize-only baseline (quantization_only.py:125-175) -- its statistics run
  * in the cell dtype (`stat_dtype`), as the reference's do.
  * scale_mode KVC_SCALE_CHANNEL (d values) or KVC_SCALE_TENSOR (1 value).
+ * Min and max are exact and order independent, so the tensor-core path
+ * reduces them with integer atomics on order-preserving bit patterns and the
+ * result is still bit-reproducible.
  */
 size_t kvc_residual_stats_workspace_bytes(int n_cells, int64_t rows, int d);
 int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, int64_t t, int d, int dtype,
@@ -156,12 +159,13 @@ int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, int64_t t, 
  * scale/zp.  arith_dtype: dtype of the divide/add in the per-tensor branch
  * (0-dim promotion, quantization.py:335-336); KVC_F32 elsewhere.
  */
+size_t kvc_residual_quant_workspace_bytes(int n_cells, int d);
 int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, int64_t t, int d, int dtype,
                        const void* const* core, const void* const* u_token,
                        const void* const* u_feature, int rt, int rd, const float* proj,
                        int bits, int symmetric, int scale_mode, int group_size, int stat_dtype,
                        int arith_dtype, float* const* scale, int32_t* const* zp,
-                       uint8_t* const* codes, void* stream);
+                       uint8_t* const* codes, void* workspace, size_t ws_bytes, void* stream);
 
 /*
  * Fused decompress of JoLT payloads (reconstruct_payload, jolt.py:401-463 with
@@ -173,12 +177,28 @@ int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, int64_t t, 
  * bits == 0: no residual term.  rt = rd = 0 / proj = NULL: the
  * quantize-only decoder (quantization_only.py:177-198).
  */
+size_t kvc_decompress_workspace_bytes(int n_cells, int d);
 int kvc_decompress(int n_cells, const uint8_t* const* codes, const float* const* scale,
                    const int32_t* const* zp, int bits, int symmetric, int scale_mode,
                    int group_size, const void* const* core, const void* const* u_token,
                    const void* const* u_feature, int factor_dtype, int64_t m, int64_t t, int d,
                    int rt, int rd, const float* proj, int64_t t0, int64_t t1, int out_dtype,
-                   void* const* out, void* stream);
+                   void* const* out, void* workspace, size_t ws_bytes, void* stream);
+
+/*
+ * Kernel selection.  Policy 0 (default): bf16 cells with d in {64, 128},
+ * rd <= 16, a JL rotation and channel / tensor scales run on the tcgen05
+ * tensor-core kernels (residual encode) and symmetric per-channel 8/4/2-bit
+ * bf16 decodes run on the tcgen05 decoder; everything else on the SIMT
+ * kernels.  Policy 1: SIMT kernels only (used to cross-check the two).
+ * Process-wide; set it while no call is in flight.
+ */
+int kvc_set_kernel_policy(int policy);
+
+/* Reads and clears the device-side error word (an mbarrier wait in a
+ * tensor-core kernel that gave up records a nonzero code).  Synchronises
+ * the device: a diagnostic, not for the hot path. */
+int kvc_device_error(int* code);
 
 /* Elementwise cast between KVC_F32/F16/BF16/FP8E4M3 (torch .to semantics:
  * round to nearest even; float8_e4m3fn does not saturate -- magnitudes that

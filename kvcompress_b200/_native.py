@@ -51,10 +51,14 @@ _SIGNATURES = {
     "kvc_residual_stats_workspace_bytes": (SZ, [I, I64, I]),
     "kvc_residual_stats": (I, [I, PP, I64, I64, I, I, PP, PP, PP, I, I, P, I, I, I, I, PP, PP, P,
                                SZ, P]),
+    "kvc_residual_quant_workspace_bytes": (SZ, [I, I]),
     "kvc_residual_quant": (I, [I, PP, I64, I64, I, I, PP, PP, PP, I, I, P, I, I, I, I, I, I, PP, PP,
-                               PP, P]),
+                               PP, P, SZ, P]),
+    "kvc_decompress_workspace_bytes": (SZ, [I, I]),
     "kvc_decompress": (I, [I, PP, PP, PP, I, I, I, I, PP, PP, PP, I, I64, I64, I, I, I, P, I64, I64, I,
-                           PP, P]),
+                           PP, P, SZ, P]),
+    "kvc_set_kernel_policy": (I, [I]),
+    "kvc_device_error": (I, [ctypes.POINTER(I)]),
     "kvc_cast": (I, [I64, P, I, P, I, P]),
 }
 

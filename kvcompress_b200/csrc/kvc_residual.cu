@@ -16,8 +16,38 @@
 #include <algorithm>
 
 #include "kvc_common.cuh"
+#include "kvc_quant.cuh"
 
 namespace kvc {
+
+bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale_mode);
+size_t tc_residual_workspace(int n_cells, int d);
+int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
+                       const void* const* core, const void* const* u_token, const void* const* u_feature,
+                       int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
+                       int stat_dtype, int arith_dtype, float* const* scale, int32_t* const* zp,
+                       uint8_t* const* codes, void* workspace, size_t ws_bytes, cudaStream_t st);
+bool tc_decompress_eligible(int out_dtype, int d, int rd, int bits, int symmetric, int scale_mode,
+                            const float* proj);
+size_t tc_decompress_workspace(int n_cells, int d);
+int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* const* scale, int bits,
+                         const void* const* core, const void* const* u_token, const void* const* u_feature,
+                         int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd, const float* proj,
+                         int64_t t0, int64_t t1, void* const* out, void* workspace, size_t ws_bytes,
+                         cudaStream_t st);
+int tc_read_device_error(int* out);
+
+static int g_policy = 0;  // 0: tensor cores when eligible, 1: SIMT kernels only
+
+static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+template <typename P>
+static bool all_aligned(int n, P const* ptrs) {
+  for (int c = 0; c < n; ++c)
+    if (ptrs[c] && !aligned16(ptrs[c])) return false;
+  return true;
+}
+
 namespace {
 
 constexpr int ROWS = 32;
@@ -38,51 +68,6 @@ struct ResArgs {
   int code_bytes;
   int pi_in_smem;
 };
-
-__device__ __forceinline__ void qrange(int bits, int symmetric, int& qmin, int& qmax) {
-  if (symmetric) {
-    qmin = -(1 << (bits - 1));
-    qmax = (1 << (bits - 1)) - 1;
-  } else {
-    qmin = 0;
-    qmax = (1 << bits) - 1;
-  }
-}
-
-// scale / zero point from min/max, in the arithmetic of `dt`
-// (IntQuantizer.compute_params, quantization.py:437-452).
-__device__ void params_from_minmax(float mn, float mx, int bits, int symmetric, int dt, float& scale,
-                                   int32_t& zp) {
-  int qmin, qmax;
-  qrange(bits, symmetric, qmin, qmax);
-  const float eps = round_dt(1e-12f, dt);
-  if (symmetric) {
-    float am = fmaxf(fabsf(mn), fabsf(mx));
-    am = fmaxf(am, eps);
-    scale = round_dt(__fdiv_rn(am, (float)qmax), dt);
-    zp = 0;
-  } else {
-    float rng = fmaxf(round_dt(mx - mn, dt), eps);
-    scale = round_dt(__fdiv_rn(rng, (float)(qmax - qmin)), dt);
-    const float ratio = round_dt(__fdiv_rn(mn, scale), dt);
-    const float z = round_dt((float)qmin - ratio, dt);
-    zp = (int32_t)rintf(z);
-  }
-}
-
-__device__ __forceinline__ int quantize_one(float v, float s, int32_t zp, int qmin, int qmax,
-                                            int dt_arith) {
-  float sc;
-  if (dt_arith != KVC_F32) {
-    sc = round_dt(__fdiv_rn(v, s), dt_arith);
-    sc = round_dt(sc + (float)zp, dt_arith);
-  } else {
-    sc = __fadd_rn(__fdiv_rn(v, s), (float)zp);
-  }
-  float r = rintf(sc);
-  r = fminf(fmaxf(r, (float)qmin), (float)qmax);
-  return (int)r;
-}
 
 // Load a tile of rows into xs (fp32), subtract the Tucker reconstruction in
 // the cell dtype, rotate into rot.  Returns the number of valid rows.
@@ -487,7 +472,29 @@ using namespace kvc;
 
 extern "C" size_t kvc_residual_stats_workspace_bytes(int n_cells, int64_t rows, int d) {
   if (n_cells <= 0 || rows <= 0 || d <= 0) return 0;
-  return (size_t)n_cells * blocks_per_cell(rows, n_cells) * 2 * d * sizeof(float);
+  return std::max((size_t)n_cells * blocks_per_cell(rows, n_cells) * 2 * d * sizeof(float),
+                  tc_residual_workspace(n_cells, d));
+}
+
+extern "C" size_t kvc_residual_quant_workspace_bytes(int n_cells, int d) {
+  if (n_cells <= 0 || d <= 0) return 0;
+  return tc_residual_workspace(n_cells, d);
+}
+
+extern "C" size_t kvc_decompress_workspace_bytes(int n_cells, int d) {
+  if (n_cells <= 0 || d <= 0) return 0;
+  return tc_decompress_workspace(n_cells, d);
+}
+
+extern "C" int kvc_set_kernel_policy(int policy) {
+  if (policy != 0 && policy != 1) return fail(KVC_ERR_ARG, "kvc_set_kernel_policy: 0 (auto) or 1 (SIMT)");
+  g_policy = policy;
+  return KVC_OK;
+}
+
+extern "C" int kvc_device_error(int* code) {
+  if (!code) return fail(KVC_ERR_ARG, "kvc_device_error: NULL");
+  return tc_read_device_error(code);
 }
 
 extern "C" int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, int64_t t, int d,
@@ -501,6 +508,12 @@ extern "C" int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, 
                          symmetric, scale_mode, stat_dtype);
   if (rc) return rc;
   if (scale_mode == KVC_SCALE_GROUP) return fail(KVC_ERR_ARG, "kvc_residual_stats: group scales need no stats pass");
+  cudaStream_t st0 = static_cast<cudaStream_t>(stream);
+  if (g_policy == 0 && tc_residual_eligible(dtype, d, rd, proj, scale_mode) && all_aligned(n_cells, x)) {
+    return tc_residual_launch(0, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
+                              scale_mode, stat_dtype, KVC_F32, scale_out, zp_out, nullptr, workspace, ws_bytes,
+                              st0);
+  }
   const int bpc = blocks_per_cell(a.rows, n_cells);
   const size_t need = (size_t)n_cells * bpc * 2 * d * sizeof(float);
   if (!workspace || ws_bytes < need) return fail(KVC_ERR_WORKSPACE, "kvc_residual_stats: workspace too small");
@@ -530,7 +543,8 @@ extern "C" int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, 
                                   const void* const* u_feature, int rt, int rd, const float* proj,
                                   int bits, int symmetric, int scale_mode, int group_size,
                                   int stat_dtype, int arith_dtype, float* const* scale,
-                                  int32_t* const* zp, uint8_t* const* codes, void* stream) {
+                                  int32_t* const* zp, uint8_t* const* codes, void* workspace,
+                                  size_t ws_bytes, void* stream) {
   ResArgs a;
   int rc = fill_res_args(a, n_cells, x, m, t, d, dtype, core, u_token, u_feature, rt, rd, proj, bits,
                          symmetric, scale_mode, stat_dtype);
@@ -538,6 +552,13 @@ extern "C" int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, 
   if (scale_mode == KVC_SCALE_GROUP && (group_size <= 0 || d % group_size != 0))
     return fail(KVC_ERR_SHAPE, "kvc_residual_quant: d must be divisible by group_size");
   if (!dtype_ok(arith_dtype)) return fail(KVC_ERR_DTYPE, "kvc_residual_quant: bad arith dtype");
+  if (g_policy == 0 && scale_mode != KVC_SCALE_GROUP && tc_residual_eligible(dtype, d, rd, proj, scale_mode) &&
+      all_aligned(n_cells, x) && all_aligned(n_cells, codes) && workspace &&
+      ws_bytes >= tc_residual_workspace(n_cells, d)) {
+    return tc_residual_launch(1, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
+                              scale_mode, stat_dtype, arith_dtype, scale, zp, codes, workspace, ws_bytes,
+                              static_cast<cudaStream_t>(stream));
+  }
   a.group_size = group_size;
   a.arith_dtype = arith_dtype;
   a.code_bytes = (d * bits + 7) / 8;
@@ -562,7 +583,8 @@ extern "C" int kvc_decompress(int n_cells, const uint8_t* const* codes, const fl
                               int group_size, const void* const* core, const void* const* u_token,
                               const void* const* u_feature, int factor_dtype, int64_t m, int64_t t,
                               int d, int rt, int rd, const float* proj, int64_t t0, int64_t t1,
-                              int out_dtype, void* const* out, void* stream) {
+                              int out_dtype, void* const* out, void* workspace, size_t ws_bytes,
+                              void* stream) {
   if (n_cells <= 0 || n_cells > KVC_MAX_CELLS) return fail(KVC_ERR_ARG, "kvc_decompress: bad n_cells");
   if (m <= 0 || t <= 0 || d <= 0 || d > MAXD) return fail(KVC_ERR_SHAPE, "kvc_decompress: bad shape");
   if (t0 < 0 || t1 > t || t0 >= t1) return fail(KVC_ERR_SHAPE, "kvc_decompress: bad token range");
@@ -572,6 +594,18 @@ extern "C" int kvc_decompress(int n_cells, const uint8_t* const* codes, const fl
     return fail(KVC_ERR_DTYPE, "kvc_decompress: bad dtype");
   if (bits > 0 && scale_mode == KVC_SCALE_GROUP && (group_size <= 0 || d % group_size != 0))
     return fail(KVC_ERR_SHAPE, "kvc_decompress: d must be divisible by group_size");
+  for (int c = 0; c < n_cells; ++c) {
+    if (!out[c]) return fail(KVC_ERR_ARG, "kvc_decompress: NULL out");
+    if (bits > 0 && (!codes[c] || !scale[c] || !zp[c])) return fail(KVC_ERR_ARG, "kvc_decompress: NULL codes");
+    if (rt > 0 && (!core[c] || !u_token[c] || !u_feature[c]))
+      return fail(KVC_ERR_ARG, "kvc_decompress: NULL factor");
+  }
+  if (g_policy == 0 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj) &&
+      all_aligned(n_cells, codes) && all_aligned(n_cells, out) && workspace &&
+      ws_bytes >= tc_decompress_workspace(n_cells, d)) {
+    return tc_decompress_launch(n_cells, codes, scale, bits, core, u_token, u_feature, factor_dtype, m, t, d, rt,
+                                rd, proj, t0, t1, out, workspace, ws_bytes, static_cast<cudaStream_t>(stream));
+  }
   DecArgs a;
   memset(&a, 0, sizeof(a));
   for (int c = 0; c < n_cells; ++c) {

@@ -1,0 +1,163 @@
+// tcgen05 / TMEM / mbarrier building blocks for sm_100a (inline PTX).
+//
+// Operand tiles live in shared memory in the canonical K-major
+// SWIZZLE_128B layout: for a tile of R rows x K bf16/fp16 columns (K a
+// multiple of 64), element (r, k) sits at byte
+//   (k / 64) * R * 128 + (r / 8) * 1024 + (r % 8) * 128
+//   + (((k / 8) % 8) ^ (r % 8)) * 16 + (k % 8) * 2
+// i.e. 128-byte rows, 8-row / 1024-byte swizzle atoms, one atom column per
+// 64 elements of K.  Tile bases are 1024-byte aligned.  The shared-memory
+// matrix descriptor of such a tile has SBO = 1024 B, layout type
+// SWIZZLE_128B (2) and version 1; a K-slice of 16 elements (32 bytes) is
+// addressed by advancing the start address inside the 128-byte row.
+//
+// Every wait on an mbarrier is bounded: after kWaitLimit failed polls the
+// waiter records an error in g_kvc_device_error and gives up.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace kvc {
+namespace tc {
+
+constexpr uint32_t kWaitLimit = 1u << 22;
+
+// Error word of the kernels in the including translation unit (internal
+// linkage: the .cu that includes this header also reads it back).
+static __device__ int g_kvc_device_error = 0;
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ uint32_t sw128_off(int r, int k, int R) {
+  return (uint32_t)((k >> 6) * (R * 128) + (r >> 3) * 1024 + (r & 7) * 128 +
+                    ((((k >> 3) & 7) ^ (r & 7)) << 4) + ((k & 7) << 1));
+}
+
+// K-major SWIZZLE_128B shared-memory matrix descriptor.
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)1 << 16;            // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024 >> 4) << 32;  // stride byte offset: 8 rows x 128 B
+  d |= (uint64_t)1 << 46;            // descriptor version for sm_100
+  d |= (uint64_t)2 << 61;            // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: fp32 accumulate, A/B bf16 (is_bf16) or
+// fp16, both K-major, M x N tile.
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N, bool is_bf16) {
+  return (1u << 4) | ((is_bf16 ? 1u : 0u) << 7) | ((is_bf16 ? 1u : 0u) << 10) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                         uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(mbar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_alloc(uint32_t* dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(dst)),
+               "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns: thread (lane) gets its row.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P1;\n\tmbarrier.try_wait.parity.shared::cta.b64 P1, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, P1;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait for the phase with `parity` to complete; false on timeout
+// (the error is recorded for the host).
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, int code) {
+  for (uint32_t i = 0; i < kWaitLimit; ++i)
+    if (mbar_try_wait(b, parity)) return true;
+  atomicCAS(&g_kvc_device_error, 0, code);
+  return false;
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// After this, lane l holds op-reduction over the 32 lanes of column l of
+// the 32 x 32 block v (row = lane).  31 shuffles.
+template <bool MAX>
+__device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool upper = (lane & s) != 0;
+#pragma unroll
+    for (int j = 0; j < s; ++j) {
+      const float send = upper ? v[j] : v[j + s];
+      const float keep = upper ? v[j + s] : v[j];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, s);
+      v[j] = MAX ? fmaxf(keep, recv) : fminf(keep, recv);
+    }
+  }
+  return v[0];
+}
+
+}  // namespace tc
+}  // namespace kvc

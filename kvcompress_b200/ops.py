@@ -269,6 +269,7 @@ def residual_quant(xs, factors, proj, scales, zps, *, bits: int, symmetric: bool
     cb = (d * bits + 7) // 8
     codes = [torch.empty(m * t, cb, dtype=torch.uint8, device=dev) for _ in xs]
     cp, up, dp, rt, rd = _factor_ptrs(factors, n)
+    ws = workspace(lib().kvc_residual_quant_workspace_bytes(n, d), dev)
     nbytes = n * (xs[0].numel() * xs[0].element_size() + codes[0].numel())
     with _Stage("residual_quant", 1, nbytes):
         check(lib().kvc_residual_quant(n, ptr_array(x.data_ptr() for x in xs), m, t, d,
@@ -278,7 +279,8 @@ def residual_quant(xs, factors, proj, scales, zps, *, bits: int, symmetric: bool
                                        _code(stat_dtype), _code(arith_dtype),
                                        ptr_array(s.data_ptr() for s in scales),
                                        ptr_array(z.data_ptr() for z in zps),
-                                       ptr_array(c.data_ptr() for c in codes), _stream()),
+                                       ptr_array(c.data_ptr() for c in codes), ws.data_ptr(), ws.numel(),
+                                       _stream()),
               "kvc_residual_quant")
     return codes, scales, zps
 
@@ -301,6 +303,8 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
         z_arr = ptr_array(z.data_ptr() for z in zps)
     else:
         c_arr = s_arr = z_arr = ptr_array([0] * n)
+    dev0 = out[0].device
+    ws = workspace(lib().kvc_decompress_workspace_bytes(n, d), dev0)
     nbytes = n * out[0].numel() * out[0].element_size()
     if bits > 0:
         nbytes += sum(c.numel() for c in codes) * (t1 - t0) // t
@@ -308,9 +312,22 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
         check(lib().kvc_decompress(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
                                    int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
                                    proj.data_ptr() if proj is not None else None, t0, t1,
-                                   _code(out_dtype), ptr_array(o.data_ptr() for o in out), _stream()),
+                                   _code(out_dtype), ptr_array(o.data_ptr() for o in out),
+                                   ws.data_ptr(), ws.numel(), _stream()),
               "kvc_decompress")
     return out
+
+
+def set_kernel_policy(policy: int) -> None:
+    """0: tensor-core kernels where eligible (default); 1: SIMT kernels only."""
+    check(lib().kvc_set_kernel_policy(int(policy)), "kvc_set_kernel_policy")
+
+
+def device_error() -> int:
+    """Read and clear the device error word (synchronises the device)."""
+    code = ctypes.c_int(0)
+    check(lib().kvc_device_error(ctypes.byref(code)), "kvc_device_error")
+    return int(code.value)
 
 
 def cast(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:

@@ -209,3 +209,77 @@ def test_residual_kernel_on_reference_factors(golden):
         mism = np.mean(codes[0].cpu().numpy() != golden.raw(p + "payload_residual_packed"))
         assert mism < 2e-3, (case, mism)
         del dt
+
+
+def _policy(p):
+    ops.set_kernel_policy(p)
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("bits", [8, 4, 2])
+@pytest.mark.parametrize("rank", [(1, 1), (5, 3)])
+def test_tensor_core_residual_matches_simt(d, bits, rank):
+    """tcgen05 encode vs the SIMT encode of the same bf16 cells (two cells, ragged rows)."""
+    from kvcompress_b200.compressor.jl import cached_projection
+
+    g = torch.Generator(device="cuda").manual_seed(d + bits)
+    m, t = 3, 333
+    xs = [torch.randn(m, t, d, generator=g, device="cuda").bfloat16() for _ in range(2)]
+    rt, rd = rank
+    fac = ([torch.randn(m, rt, rd, generator=g, device="cuda").bfloat16() for _ in xs],
+           [(torch.randn(t, rt, generator=g, device="cuda") / 10).bfloat16() for _ in xs],
+           [(torch.randn(d, rd, generator=g, device="cuda") / 5).bfloat16() for _ in xs])
+    proj = cached_projection(d, d, seed=0, device="cuda").matrix
+    out = {}
+    try:
+        for pol in (0, 1):
+            _policy(pol)
+            sc, zp = ops.residual_stats(xs, fac, proj, bits=bits, symmetric=True, scale_mode=KVC.SCALE_CHANNEL,
+                                        stat_dtype=torch.float32)
+            codes, _, _ = ops.residual_quant(xs, fac, proj, sc, zp, bits=bits, symmetric=True,
+                                             scale_mode=KVC.SCALE_CHANNEL, group_size=None,
+                                             stat_dtype=torch.float32, arith_dtype=torch.float32)
+            out[pol] = ([s.cpu().numpy() for s in sc], [c.cpu().numpy() for c in codes])
+    finally:
+        _policy(0)
+    assert ops.device_error() == 0
+    for a, b in zip(out[0][0], out[1][0]):
+        assert rel(a, b) < 1e-6
+    for a, b in zip(out[0][1], out[1][1]):
+        assert np.mean(a != b) < 1e-3
+
+
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("bits", [8, 4, 2])
+@pytest.mark.parametrize("rank", [(1, 1), (7, 4)])
+def test_tensor_core_decompress_matches_simt(d, bits, rank):
+    from kvcompress_b200.compressor.jl import cached_projection
+
+    g = torch.Generator(device="cuda").manual_seed(7 * d + bits)
+    m, t = 2, 300
+    rt, rd = rank
+    cb = d * bits // 8
+    codes = [torch.randint(0, 256, (m * t, cb), generator=g, device="cuda", dtype=torch.int32).to(torch.uint8)
+             for _ in range(3)]
+    scales = [torch.rand(d, generator=g, device="cuda") * 0.1 + 0.01 for _ in range(3)]
+    zps = [torch.zeros(d, dtype=torch.int32, device="cuda") for _ in range(3)]
+    fac = ([torch.randn(m, rt, rd, generator=g, device="cuda").half() for _ in range(3)],
+           [(torch.randn(t, rt, generator=g, device="cuda") / 10).half() for _ in range(3)],
+           [(torch.randn(d, rd, generator=g, device="cuda") / 5).half() for _ in range(3)])
+    proj = cached_projection(d, d, seed=0, device="cuda").matrix
+    res = {}
+    try:
+        for pol in (0, 1):
+            _policy(pol)
+            outs = ops.decompress((m, t, d), torch.bfloat16, codes=codes, scales=scales, zps=zps, bits=bits,
+                                  factors=fac, proj=proj, n_cells=3, device="cuda")
+            part = ops.decompress((m, t, d), torch.bfloat16, codes=codes, scales=scales, zps=zps, bits=bits,
+                                  factors=fac, proj=proj, n_cells=3, device="cuda", t0=37, t1=299)
+            res[pol] = ([f32(o) for o in outs], [f32(o) for o in part])
+    finally:
+        _policy(0)
+    assert ops.device_error() == 0
+    for a, b in zip(res[0][0], res[1][0]):
+        assert rel(a, b) < 2e-3
+    for full, part in zip(res[0][0], res[0][1]):
+        np.testing.assert_array_equal(full[:, 37:299], part)
