@@ -14,6 +14,12 @@
 
 namespace kvc {
 
+bool tc_gram_eligible(int dtype, int p, int k);
+size_t tc_gram_workspace(int n_cells, int64_t rows);
+int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float* omega, int k, double* out,
+                   void* workspace, size_t ws_bytes, cudaStream_t st);
+int kernel_policy();
+
 namespace {
 
 constexpr int TB = 64;   // output tile edge
@@ -171,7 +177,8 @@ using namespace kvc;
 extern "C" size_t kvc_gram_workspace_bytes(int n_cells, int64_t rows, int p, int k) {
   if (n_cells <= 0 || rows <= 0 || p <= 0 || k < 0) return 0;
   ChunkPlan pl = plan_chunks(n_cells, rows, p, p + k);
-  return (size_t)n_cells * pl.chunks * (size_t)p * (p + k) * sizeof(float);
+  size_t simt = (size_t)n_cells * pl.chunks * (size_t)p * (p + k) * sizeof(float);
+  return std::max(simt, tc_gram_eligible(KVC_BF16, p, k) ? tc_gram_workspace(n_cells, rows) : (size_t)0);
 }
 
 extern "C" int kvc_gram(int n_cells, const void* const* a, int64_t rows, int p, int dtype,
@@ -186,17 +193,25 @@ extern "C" int kvc_gram(int n_cells, const void* const* a, int64_t rows, int p, 
   const size_t need = (size_t)n_cells * pl.chunks * (size_t)p * (p + k) * sizeof(float);
   if (!workspace || ws_bytes < need) return fail(KVC_ERR_WORKSPACE, "kvc_gram: workspace too small");
   CellPtrs ap;
+  bool aligned = true;
   for (int c = 0; c < n_cells; ++c) {
     if (!a[c]) return fail(KVC_ERR_ARG, "kvc_gram: NULL cell pointer");
     ap.p[c] = a[c];
+    aligned = aligned && (reinterpret_cast<uintptr_t>(a[c]) & 15u) == 0;
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  float* partial = static_cast<float*>(workspace);
+  const int64_t stride = (int64_t)p * p + (int64_t)p * k + 1;
   int rc;
+  if (kernel_policy() == 0 && k > 0 && aligned && tc_gram_eligible(dtype, p, k) &&
+      ws_bytes >= tc_gram_workspace(n_cells, rows)) {
+    if ((rc = tc_gram_launch(n_cells, a, rows, omega, k, out, workspace, ws_bytes, st))) return rc;
+    gram_trace_kernel<<<(n_cells + 63) / 64, 64, 0, st>>>(out, n_cells, p, k, stride);
+    return check_launch("gram_trace_kernel");
+  }
+  float* partial = static_cast<float*>(workspace);
   KVC_DISPATCH_DTYPE(dtype, T, rc = launch_partial<T, T>(n_cells, ap, ap, omega, rows, p, p, k, pl,
                                                          partial, st));
   if (rc) return rc;
-  const int64_t stride = (int64_t)p * p + (int64_t)p * k + 1;
   const int64_t total = (int64_t)n_cells * p * (p + k);
   const int blocks = (int)std::min<int64_t>(ceil_div(total, 256), 8 * num_sms());
   gram_reduce_kernel<<<blocks, 256, 0, st>>>(partial, n_cells, pl.chunks, p, p, k, out, stride);

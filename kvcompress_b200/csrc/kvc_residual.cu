@@ -38,6 +38,7 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
 int tc_read_device_error(int* out);
 
 static int g_policy = 0;  // 0: tensor cores when eligible, 1: SIMT kernels only
+int kernel_policy() { return g_policy; }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 

@@ -36,28 +36,32 @@ namespace {
 using namespace tc;
 
 constexpr int TILE_M = 128;
-constexpr int NTHREADS = 288;
+constexpr int NTHREADS = 416;  // 4 producer warps, 1 MMA warp, 8 epilogue warps
 constexpr int MMA_WARP = 4;
+constexpr int NEPI = 256;      // epilogue threads: 2 warps per TMEM lane group
 constexpr int RD_MAX = 16;
-constexpr int NSTAGE = 2;
+constexpr int NSTAGE = 3;
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   const uint32_t a = smem_u32(p);
   return p + ((1024u - (a & 1023u)) & 1023u);
 }
 
-template <int D, int NTERM>
+// STAGE_EXTRA: per-stage staging bytes beside the A tile (decode: the codes).
+template <int D, int NTERM, int STAGE_EXTRA = 0>
 struct Layout {
   static constexpr uint32_t B_TERM = D * D * 2;
   static constexpr uint32_t B_BYTES = NTERM * B_TERM;
   static constexpr uint32_t A_BYTES = TILE_M * D * 2;
   static constexpr uint32_t OFF_B = 0;
   static constexpr uint32_t OFF_A = B_BYTES;
-  static constexpr uint32_t OFF_UD = OFF_A + NSTAGE * A_BYTES;
-  static constexpr uint32_t OFF_SC = OFF_UD + D * RD_MAX * 4;      // 4 epilogue warps x (d scales, d zps)
-  static constexpr uint32_t OFF_BAR = OFF_SC + 4 * D * 8;
-  static constexpr uint32_t OFF_TM = OFF_BAR + 8 * 8;
-  static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;  // + alignment slack
+  static constexpr uint32_t OFF_X = OFF_A + NSTAGE * A_BYTES;          // staging
+  static constexpr uint32_t OFF_UD = OFF_X + NSTAGE * STAGE_EXTRA;
+  static constexpr uint32_t OFF_SC = OFF_UD + D * RD_MAX * 4;          // 8 epilogue warps x (scales, zps)
+  static constexpr uint32_t OFF_BAR = OFF_SC + 8 * D * 8;
+  static constexpr uint32_t NBAR = 2 * NSTAGE + 4;                     // full, empty, acc full, acc empty
+  static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
+  static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;                // + alignment slack
 };
 
 enum { MODE_STATS = 0, MODE_QUANT = 1 };
@@ -101,17 +105,17 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);  // full[2] empty[2] accf[2] acce[2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = full + NSTAGE;
+  uint64_t* accf = empty + NSTAGE;
+  uint64_t* acce = accf + 2;
   uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_TM);
-  float* ud_s = reinterpret_cast<float*>(smem + L::OFF_UD);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // per-epilogue-warp copy of the current cell's scales (refreshed with __syncwarp only)
-  float* sc_s = reinterpret_cast<float*>(smem + L::OFF_SC) + (warp & 3) * 2 * D;
-  int32_t* zp_s = reinterpret_cast<int32_t*>(sc_s + D);
 
   const int64_t tile_begin = (int64_t)blockIdx.x * A.tiles_per_cta;
   const int64_t tile_end = tile_begin + A.tiles_per_cta < A.total_tiles ? tile_begin + A.tiles_per_cta
                                                                        : A.total_tiles;
+  const int n_my = (int)(tile_end > tile_begin ? tile_end - tile_begin : 0);
 
   // ---- set-up: B operand, barriers, TMEM ----
   {
@@ -120,11 +124,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
     for (int i = threadIdx.x; i < (int)(L::B_BYTES / 16); i += NTHREADS) dst[i] = src[i];
   }
   if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 128);  // producer threads
+      mbar_init(&empty[i], 1);   // tcgen05.commit
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[0 + i], 128);  // full: producer threads
-      mbar_init(&bars[2 + i], 1);    // empty: tcgen05.commit
-      mbar_init(&bars[4 + i], 1);    // accumulator full: tcgen05.commit
-      mbar_init(&bars[6 + i], 128);  // accumulator empty: epilogue threads
+      mbar_init(&accf[i], 1);     // tcgen05.commit
+      mbar_init(&acce[i], NEPI);  // epilogue threads
     }
     mbar_fence_init();
   }
@@ -139,25 +145,51 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
   const uint32_t tmem = *tm_holder;
 
   if (warp < 4) {
-    // ---------------- producers ----------------
+    // ---------------- producers: cp.async x into the A stage, R in place ----------------
     constexpr int CH = D / 8;     // 16-byte chunks per row
     constexpr int RPI = 32 / CH;  // rows per warp iteration
+    constexpr int NIT = 32 / RPI;
     const int chunk = lane % CH, sub = lane / CH;
-    int cur_cell = -1;
-    const T* x = nullptr;
-    const T* core = nullptr;
-    const T* ut = nullptr;
     float udv[8][RDM];
-    int it = 0;
-    for (int64_t g = tile_begin; g < tile_end; ++g, ++it) {
+    int ud_cell = -1;
+    bool ok = true;
+    auto issue = [&](int j) {  // copies of the j-th local tile into its stage
+      const int64_t g = tile_begin + j;
       const int cell = (int)(g / A.tiles_per_cell);
-      const int64_t tile = g % A.tiles_per_cell;
-      if (cell != cur_cell) {
-        cur_cell = cell;
-        x = static_cast<const T*>(A.x.p[cell]);
-        if (A.rt > 0) {
-          core = static_cast<const T*>(A.core.p[cell]);
-          ut = static_cast<const T*>(A.ut.p[cell]);
+      const int64_t r0 = (g % A.tiles_per_cell) * TILE_M;
+      const int st = j % NSTAGE;
+      if (!mbar_wait(&empty[st], (uint32_t)((j / NSTAGE) & 1) ^ 1u, 0x101)) return false;
+      const T* x = static_cast<const T*>(A.x.p[cell]);
+      const uint32_t a_s = sbase + L::OFF_A + st * L::A_BYTES;
+#pragma unroll
+      for (int i = 0; i < NIT; ++i) {
+        const int rloc = warp * 32 + i * RPI + sub;
+        const int64_t row = r0 + rloc;
+        if (row < A.rows) cp_async16(a_s + sw128_off(rloc, chunk * 8, TILE_M), x + row * D + chunk * 8);
+      }
+      return true;
+    };
+    for (int j = 0; j < NSTAGE - 1; ++j) {
+      if (ok && j < n_my) ok = issue(j);
+      cp_async_commit();
+    }
+    for (int it = 0; it < n_my && ok; ++it) {
+      const int jn = it + NSTAGE - 1;
+      if (jn < n_my) ok = issue(jn);
+      cp_async_commit();
+      if (!ok) break;
+      cp_async_wait<NSTAGE - 1>();
+      const int64_t g = tile_begin + it;
+      const int cell = (int)(g / A.tiles_per_cell);
+      const int64_t r0 = (g % A.tiles_per_cell) * TILE_M;
+      uint8_t* As = smem + L::OFF_A + (it % NSTAGE) * L::A_BYTES;
+      const T* core = nullptr;
+      const T* ut = nullptr;
+      if (A.rt > 0) {
+        core = static_cast<const T*>(A.core.p[cell]);
+        ut = static_cast<const T*>(A.ut.p[cell]);
+        if (cell != ud_cell) {
+          ud_cell = cell;
           const T* ud = static_cast<const T*>(A.ud.p[cell]);
 #pragma unroll
           for (int e = 0; e < 8; ++e)
@@ -166,64 +198,58 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
               udv[e][r] = r < A.rd ? Elt<T>::to_f32(ud[(int64_t)(chunk * 8 + e) * A.rd + r]) : 0.f;
         }
       }
-      const int s = it & 1;
-      const uint32_t ph = (uint32_t)(it >> 1) & 1u;
-      if (!mbar_wait(&bars[2 + s], ph ^ 1u, 0x101)) break;
-      uint8_t* As = smem + L::OFF_A + s * L::A_BYTES;
-      const int64_t r0 = tile * TILE_M;
 #pragma unroll 2
-      for (int i = 0; i < 32 / RPI; ++i) {
+      for (int i = 0; i < NIT; ++i) {
         const int rloc = warp * 32 + i * RPI + sub;
         const int64_t row = r0 + rloc;
+        uint4* slot = reinterpret_cast<uint4*>(As + sw128_off(rloc, chunk * 8, TILE_M));
         float xv[8];
         if (row < A.rows) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(x + row * D + chunk * 8);
-          unpack8<T>(raw, xv);
-          if (A.rt > 0) {
-            const int64_t h = row / A.t, t = row % A.t;
-            float tmp[RDM];
+          if (A.rt == 0) continue;  // R = x, already in place
+          unpack8<T>(*slot, xv);
+          const int64_t h = row / A.t, t = row % A.t;
+          float tmp[RDM];
 #pragma unroll
-            for (int r = 0; r < RDM; ++r) {
-              float acc = 0.f;
-              if (r < A.rd) {
-                const T* cr = core + h * A.rt * A.rd + r;
-                const T* ur = ut + t * A.rt;
-                for (int a = 0; a < A.rt; ++a)
-                  acc = fmaf(Elt<T>::to_f32(cr[(int64_t)a * A.rd]), Elt<T>::to_f32(ur[a]), acc);
-              }
-              tmp[r] = Elt<T>::round(acc);
+          for (int r = 0; r < RDM; ++r) {
+            float acc = 0.f;
+            if (r < A.rd) {
+              const T* cr = core + h * A.rt * A.rd + r;
+              const T* ur = ut + t * A.rt;
+              for (int a = 0; a < A.rt; ++a)
+                acc = fmaf(Elt<T>::to_f32(cr[(int64_t)a * A.rd]), Elt<T>::to_f32(ur[a]), acc);
             }
+            tmp[r] = Elt<T>::round(acc);
+          }
 #pragma unroll
-            for (int e = 0; e < 8; ++e) {
-              float rec = 0.f;
+          for (int e = 0; e < 8; ++e) {
+            float rec = 0.f;
 #pragma unroll
-              for (int r = 0; r < RDM; ++r)
-                if (r < A.rd) rec = fmaf(tmp[r], udv[e][r], rec);
-              xv[e] = Elt<T>::round(xv[e] - Elt<T>::round(rec));
-            }
+            for (int r = 0; r < RDM; ++r)
+              if (r < A.rd) rec = fmaf(tmp[r], udv[e][r], rec);
+            xv[e] = Elt<T>::round(xv[e] - Elt<T>::round(rec));
           }
         } else {
 #pragma unroll
           for (int e = 0; e < 8; ++e) xv[e] = 0.f;
         }
-        *reinterpret_cast<uint4*>(As + sw128_off(rloc, chunk * 8, TILE_M)) = pack8<T>(xv);
+        *slot = pack8<T>(xv);
       }
       fence_async_smem();
-      mbar_arrive(&bars[0 + s]);
+      mbar_arrive(&full[it % NSTAGE]);
     }
+    cp_async_wait<0>();
   } else if (warp == MMA_WARP) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(TILE_M, D, std::is_same<T, __nv_bfloat16>::value);
       int it = 0;
-      for (int64_t g = tile_begin; g < tile_end; ++g, ++it) {
-        const int s = it & 1;
-        const uint32_t ph = (uint32_t)(it >> 1) & 1u;
-        if (!mbar_wait(&bars[0 + s], ph, 0x201)) break;
-        if (!mbar_wait(&bars[6 + s], ph ^ 1u, 0x202)) break;
+      for (; it < n_my; ++it) {
+        const int st = it % NSTAGE, ac = it & 1;
+        if (!mbar_wait(&full[st], (uint32_t)((it / NSTAGE) & 1), 0x201)) break;
+        if (!mbar_wait(&acce[ac], (uint32_t)((it >> 1) & 1) ^ 1u, 0x202)) break;
         tc_fence_after();
-        const uint32_t a_base = sbase + L::OFF_A + s * L::A_BYTES;
-        const uint32_t d_tmem = tmem + (uint32_t)(s * D);
+        const uint32_t a_base = sbase + L::OFF_A + st * L::A_BYTES;
+        const uint32_t d_tmem = tmem + (uint32_t)(ac * D);
 #pragma unroll
         for (int term = 0; term < NTERM; ++term) {
 #pragma unroll
@@ -234,21 +260,25 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
                      idesc, (term | ks) ? 1u : 0u);
           }
         }
-        umma_commit(&bars[2 + s]);
-        umma_commit(&bars[4 + s]);
+        umma_commit(&empty[st]);
+        umma_commit(&accf[ac]);
       }
       // do not leave while MMAs that write TMEM are still in flight
-      if (it > 0) mbar_wait(&bars[4 + ((it - 1) & 1)], (uint32_t)((it - 1) >> 1) & 1u, 0x203);
+      if (it > 0) mbar_wait(&accf[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, 0x203);
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue ----------------
+    // ---------------- epilogue: 2 warps per lane group, one column half each ----------------
+    const int e = warp - 5;
     const int lg = warp & 3;
+    const int half = e >> 2;
     const int rloc = lg * 32 + lane;
-    constexpr int NC = D / 32;
-    float rmax[NC], rmin[NC];
+    constexpr int NCH = D / 64;  // 32-column chunks per warp
+    float* sc_s = reinterpret_cast<float*>(smem + L::OFF_SC) + e * 2 * D;
+    int32_t* zp_s = reinterpret_cast<int32_t*>(sc_s + D);
+    float rmax[NCH], rmin[NCH];
 #pragma unroll
-    for (int c = 0; c < NC; ++c) {
+    for (int c = 0; c < NCH; ++c) {
       rmax[c] = -__int_as_float(0x7f800000);
       rmin[c] = __int_as_float(0x7f800000);
     }
@@ -256,17 +286,18 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
     qrange(A.bits > 0 ? A.bits : 8, A.symmetric, qmin, qmax);
     const int offset = A.symmetric ? (1 << (A.bits - 1)) : 0;
     int cur_cell = -1;
-    int it = 0;
-    for (int64_t g = tile_begin; g < tile_end; ++g, ++it) {
+    for (int it = 0; it < n_my; ++it) {
+      const int64_t g = tile_begin + it;
       const int cell = (int)(g / A.tiles_per_cell);
       const int64_t tile = g % A.tiles_per_cell;
       if (cell != cur_cell) {
         if (MODE == MODE_STATS && cur_cell >= 0) {
           int32_t* mm = A.minmax + (int64_t)cur_cell * 2 * D;
 #pragma unroll
-          for (int c = 0; c < NC; ++c) {
-            atomicMin(&mm[c * 32 + lane], ordered_bits(rmin[c]));
-            atomicMax(&mm[D + c * 32 + lane], ordered_bits(rmax[c]));
+          for (int c = 0; c < NCH; ++c) {
+            const int col = (half * NCH + c) * 32 + lane;
+            atomicMin(&mm[col], ordered_bits(rmin[c]));
+            atomicMax(&mm[D + col], ordered_bits(rmax[c]));
             rmax[c] = -__int_as_float(0x7f800000);
             rmin[c] = __int_as_float(0x7f800000);
           }
@@ -284,16 +315,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
         }
         cur_cell = cell;
       }
-      const int s = it & 1;
-      const uint32_t ph = (uint32_t)(it >> 1) & 1u;
-      if (!mbar_wait(&bars[4 + s], ph, 0x301)) break;
+      const int ac = it & 1;
+      if (!mbar_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x301)) break;
       tc_fence_after();
       const int64_t row = tile * TILE_M + rloc;
       const bool valid = row < A.rows;
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
+      for (int cc = 0; cc < NCH; ++cc) {
+        const int c = half * NCH + cc;
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(s * D + c * 32), v);
+        tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * D + c * 32), v);
         if (MODE == MODE_STATS) {
           float w[32];
 #pragma unroll
@@ -301,8 +332,8 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
             w[j] = valid ? v[j] : __int_as_float(0x7f800000);
             v[j] = valid ? v[j] : -__int_as_float(0x7f800000);
           }
-          rmax[c] = fmaxf(rmax[c], transpose_reduce32<true>(v));
-          rmin[c] = fminf(rmin[c], transpose_reduce32<false>(w));
+          rmax[cc] = fmaxf(rmax[cc], transpose_reduce32<true>(v));
+          rmin[cc] = fminf(rmin[cc], transpose_reduce32<false>(w));
         } else if (valid) {
           const int ad = A.scale_mode == KVC_SCALE_TENSOR ? A.arith_dtype : KVC_F32;
           uint32_t u[32];
@@ -356,14 +387,15 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
         }
       }
       tc_fence_before();
-      mbar_arrive(&bars[6 + s]);
+      mbar_arrive(&acce[ac]);
     }
     if (MODE == MODE_STATS && cur_cell >= 0) {
       int32_t* mm = A.minmax + (int64_t)cur_cell * 2 * D;
 #pragma unroll
-      for (int c = 0; c < NC; ++c) {
-        atomicMin(&mm[c * 32 + lane], ordered_bits(rmin[c]));
-        atomicMax(&mm[D + c * 32 + lane], ordered_bits(rmax[c]));
+      for (int c = 0; c < NCH; ++c) {
+        const int col = (half * NCH + c) * 32 + lane;
+        atomicMin(&mm[col], ordered_bits(rmin[c]));
+        atomicMax(&mm[D + col], ordered_bits(rmax[c]));
       }
     }
   }
@@ -438,13 +470,17 @@ struct TcDecArgs {
   const uint8_t* bops;  // per cell: 2 swizzled B tiles of diag(scale) Pi
 };
 
-template <typename TOut, int D, int RDM>
+template <typename TOut, int D, int RDM, int BITS>
 __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A) {
-  using L = Layout<D, 2>;
+  constexpr int CB = D * BITS / 8;  // code bytes per row
+  using L = Layout<D, 2, TILE_M * CB>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = full + NSTAGE;
+  uint64_t* accf = empty + NSTAGE;
+  uint64_t* acce = accf + 2;
   uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_TM);
   float* ud_s = reinterpret_cast<float*>(smem + L::OFF_UD);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -453,6 +489,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A)
   const int64_t tile_begin = (int64_t)blockIdx.x * A.tiles_per_cta;
   const int64_t tile_end = tile_begin + A.tiles_per_cta < A.tiles_per_cell ? tile_begin + A.tiles_per_cta
                                                                          : A.tiles_per_cell;
+  const int n_my = (int)(tile_end > tile_begin ? tile_end - tile_begin : 0);
   {
     const uint4* src = reinterpret_cast<const uint4*>(A.bops + (size_t)cell * L::B_BYTES);
     uint4* dst = reinterpret_cast<uint4*>(smem + L::OFF_B);
@@ -461,11 +498,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A)
   if (A.rt > 0)
     for (int i = threadIdx.x; i < D * A.rd; i += NTHREADS) ud_s[i] = load_dt(A.ud.p[cell], i, A.factor_dtype);
   if (threadIdx.x == 0) {
+    for (int i = 0; i < NSTAGE; ++i) {
+      mbar_init(&full[i], 128);
+      mbar_init(&empty[i], 1);
+    }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&bars[0 + i], 128);
-      mbar_init(&bars[2 + i], 1);
-      mbar_init(&bars[4 + i], 1);
-      mbar_init(&bars[6 + i], 128);
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], NEPI);
     }
     mbar_fence_init();
   }
@@ -480,58 +519,83 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A)
   const uint32_t tmem = *tm_holder;
 
   if (warp < 4) {
-    // codes -> exact integers in bf16 -> swizzled A tile
+    // codes -> (cp.async) staging -> exact integers in bf16 -> swizzled A tile
     const uint8_t* codes = static_cast<const uint8_t*>(A.codes.p[cell]);
-    const int lpr = A.code_bytes / 16;  // lanes per row (16 code bytes each)
-    const int rpi = 32 / lpr;
-    const int pos = lane % lpr, sub = lane / lpr;
-    const int per = 8 / A.bits;
-    const int vals = 16 * per;          // values per lane
-    const int offset = 1 << (A.bits - 1);
-    const int mask = (1 << A.bits) - 1;
-    int it = 0;
-    for (int64_t tile = tile_begin; tile < tile_end; ++tile, ++it) {
-      const int s = it & 1;
-      const uint32_t ph = (uint32_t)(it >> 1) & 1u;
-      if (!mbar_wait(&bars[2 + s], ph ^ 1u, 0x111)) break;
-      uint8_t* As = smem + L::OFF_A + s * L::A_BYTES;
-      for (int i = 0; i < 32 / rpi; ++i) {
-        const int rloc = warp * 32 + i * rpi + sub;
+    constexpr int LPR = CB / 16;      // lanes per row, 16 code bytes each
+    constexpr int RPI = 32 / LPR;
+    constexpr int NIT = 32 / RPI;
+    constexpr int PER = 8 / BITS;
+    constexpr int VALS = 16 * PER;    // values per lane
+    constexpr int OFFSET = 1 << (BITS - 1);
+    constexpr int MASK = (1 << BITS) - 1;
+    const int pos = lane % LPR, sub = lane / LPR;
+    bool ok = true;
+    auto issue = [&](int j) {
+      const int64_t tile = tile_begin + j;
+      const int st = j % NSTAGE;
+      if (!mbar_wait(&empty[st], (uint32_t)((j / NSTAGE) & 1) ^ 1u, 0x111)) return false;
+      const uint32_t c_s = sbase + L::OFF_X + st * (TILE_M * CB);
+#pragma unroll
+      for (int i = 0; i < NIT; ++i) {
+        const int rloc = warp * 32 + i * RPI + sub;
         const int64_t orow = tile * TILE_M + rloc;
-        uint4 raw = make_uint4(0, 0, 0, 0);
         if (orow < A.rows) {
           const int64_t h = orow / tl, t = A.t0 + orow % tl;
-          raw = *reinterpret_cast<const uint4*>(codes + (h * A.t + t) * A.code_bytes + pos * 16);
+          cp_async16(c_s + rloc * CB + pos * 16, codes + (h * A.t + t) * CB + pos * 16);
         }
-        const uint8_t* bytes = reinterpret_cast<const uint8_t*>(&raw);
-        const bool valid = orow < A.rows;
-        for (int cb = 0; cb < vals / 8; ++cb) {
+      }
+      return true;
+    };
+    for (int j = 0; j < NSTAGE - 1; ++j) {
+      if (ok && j < n_my) ok = issue(j);
+      cp_async_commit();
+    }
+    for (int it = 0; it < n_my && ok; ++it) {
+      const int jn = it + NSTAGE - 1;
+      if (jn < n_my) ok = issue(jn);
+      cp_async_commit();
+      if (!ok) break;
+      cp_async_wait<NSTAGE - 1>();
+      const int st = it % NSTAGE;
+      const uint8_t* Cs = smem + L::OFF_X + st * (TILE_M * CB);
+      uint8_t* As = smem + L::OFF_A + st * L::A_BYTES;
+      const int64_t tile = tile_begin + it;
+#pragma unroll
+      for (int i = 0; i < NIT; ++i) {
+        const int rloc = warp * 32 + i * RPI + sub;
+        const bool valid = tile * TILE_M + rloc < A.rows;
+        uint4 raw = make_uint4(0, 0, 0, 0);
+        if (valid) raw = *reinterpret_cast<const uint4*>(Cs + rloc * CB + pos * 16);
+        const uint32_t* words = reinterpret_cast<const uint32_t*>(&raw);
+#pragma unroll
+        for (int cb = 0; cb < VALS / 8; ++cb) {
           float v[8];
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             const int idx = cb * 8 + e;
-            const int byte = idx / per, sl = idx % per;
-            const int q = (int)((bytes[byte] >> (A.bits * (per - 1 - sl))) & mask) - offset;
+            const int byte = idx / PER, sl = idx % PER;
+            const uint32_t b = (words[byte >> 2] >> (8 * (byte & 3))) & 0xFFu;
+            const int q = (int)((b >> (BITS * (PER - 1 - sl))) & MASK) - OFFSET;
             v[e] = valid ? (float)q : 0.f;
           }
-          *reinterpret_cast<uint4*>(As + sw128_off(rloc, pos * vals + cb * 8, TILE_M)) = pack8<__nv_bfloat16>(v);
+          *reinterpret_cast<uint4*>(As + sw128_off(rloc, pos * VALS + cb * 8, TILE_M)) = pack8<__nv_bfloat16>(v);
         }
       }
       fence_async_smem();
-      mbar_arrive(&bars[0 + s]);
+      mbar_arrive(&full[st]);
     }
+    cp_async_wait<0>();
   } else if (warp == MMA_WARP) {
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(TILE_M, D, true);
       int it = 0;
-      for (int64_t tile = tile_begin; tile < tile_end; ++tile, ++it) {
-        const int s = it & 1;
-        const uint32_t ph = (uint32_t)(it >> 1) & 1u;
-        if (!mbar_wait(&bars[0 + s], ph, 0x211)) break;
-        if (!mbar_wait(&bars[6 + s], ph ^ 1u, 0x212)) break;
+      for (; it < n_my; ++it) {
+        const int st = it % NSTAGE, ac = it & 1;
+        if (!mbar_wait(&full[st], (uint32_t)((it / NSTAGE) & 1), 0x211)) break;
+        if (!mbar_wait(&acce[ac], (uint32_t)((it >> 1) & 1) ^ 1u, 0x212)) break;
         tc_fence_after();
-        const uint32_t a_base = sbase + L::OFF_A + s * L::A_BYTES;
-        const uint32_t d_tmem = tmem + (uint32_t)(s * D);
+        const uint32_t a_base = sbase + L::OFF_A + st * L::A_BYTES;
+        const uint32_t d_tmem = tmem + (uint32_t)(ac * D);
 #pragma unroll
         for (int term = 0; term < 2; ++term) {
 #pragma unroll
@@ -542,23 +606,24 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A)
                      idesc, (term | ks) ? 1u : 0u);
           }
         }
-        umma_commit(&bars[2 + s]);
-        umma_commit(&bars[4 + s]);
+        umma_commit(&empty[st]);
+        umma_commit(&accf[ac]);
       }
-      if (it > 0) mbar_wait(&bars[4 + ((it - 1) & 1)], (uint32_t)((it - 1) >> 1) & 1u, 0x213);
+      if (it > 0) mbar_wait(&accf[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, 0x213);
     }
     __syncwarp();
   } else {
+    const int e = warp - 5;
     const int lg = warp & 3;
+    const int half = e >> 2;
     const int rloc = lg * 32 + lane;
+    constexpr int NCH = D / 64;
     TOut* out = static_cast<TOut*>(A.out.p[cell]);
-    int it = 0;
-    for (int64_t tile = tile_begin; tile < tile_end; ++tile, ++it) {
-      const int s = it & 1;
-      const uint32_t ph = (uint32_t)(it >> 1) & 1u;
-      if (!mbar_wait(&bars[4 + s], ph, 0x311)) break;
+    for (int it = 0; it < n_my; ++it) {
+      const int ac = it & 1;
+      if (!mbar_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x311)) break;
       tc_fence_after();
-      const int64_t orow = tile * TILE_M + rloc;
+      const int64_t orow = (tile_begin + it) * TILE_M + rloc;
       const bool valid = orow < A.rows;
       float tmp[RDM];
 #pragma unroll
@@ -577,15 +642,16 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A)
         }
       }
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int cc = 0; cc < NCH; ++cc) {
+        const int c = half * NCH + cc;
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(s * D + c * 32), v);
+        tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * D + c * 32), v);
         if (valid) {
           float o[32];
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            float rec = 0.f;
             if (A.rt > 0) {
+              float rec = 0.f;
 #pragma unroll
               for (int r = 0; r < RDM; ++r)
                 if (r < A.rd) rec = fmaf(tmp[r], ud_s[(c * 32 + j) * A.rd + r], rec);
@@ -599,13 +665,13 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A)
           for (int q = 0; q < 4; ++q) {
             float w[8];
 #pragma unroll
-            for (int e = 0; e < 8; ++e) w[e] = o[q * 8 + e];
+            for (int k = 0; k < 8; ++k) w[k] = o[q * 8 + k];
             reinterpret_cast<uint4*>(dst)[q] = pack8<TOut>(w);
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(&bars[6 + s]);
+      mbar_arrive(&acce[ac]);
     }
   }
   tc_fence_before();
@@ -791,11 +857,18 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
   int rc = check_launch("prep_decode_kernel");
   if (rc) return rc;
   const dim3 grid((unsigned)ceil_div(a.tiles_per_cell, a.tiles_per_cta), n_cells);
-#define KVC_TC_DEC(DD, RR)                                                  \
+#define KVC_TC_DEC3(DD, RR, BB)                                             \
   do {                                                                      \
-    auto kern = tc_decompress_kernel<__nv_bfloat16, DD, RR>;                \
-    if ((rc = set_smem(kern, Layout<DD, 2>::BYTES))) return rc;             \
-    kern<<<grid, NTHREADS, Layout<DD, 2>::BYTES, st>>>(a);                  \
+    auto kern = tc_decompress_kernel<__nv_bfloat16, DD, RR, BB>;            \
+    using LL = Layout<DD, 2, TILE_M * DD * BB / 8>;                         \
+    if ((rc = set_smem(kern, LL::BYTES))) return rc;                        \
+    kern<<<grid, NTHREADS, LL::BYTES, st>>>(a);                             \
+  } while (0)
+#define KVC_TC_DEC(DD, RR)                            \
+  do {                                                \
+    if (bits == 8) KVC_TC_DEC3(DD, RR, 8);            \
+    else if (bits == 4) KVC_TC_DEC3(DD, RR, 4);       \
+    else KVC_TC_DEC3(DD, RR, 2);                      \
   } while (0)
   if (d == 128) {
     if (rd <= 1) KVC_TC_DEC(128, 1);
@@ -806,6 +879,7 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
     else if (rd <= 4) KVC_TC_DEC(64, 4);
     else KVC_TC_DEC(64, 16);
   }
+#undef KVC_TC_DEC3
 #undef KVC_TC_DEC
   return check_launch("tc_decompress_kernel");
 }

@@ -111,6 +111,62 @@ rowmat_kernel(CellPtrs A, CellPtrs B, int64_t rows, int K, int N, int64_t T, int
   }
 }
 
+// x_proj for small feature ranks (rd <= RDM): LPR lanes share a row, each
+// loads 16 bytes with one vector load, multiplies by its slice of U_d held in
+// registers, and the partial sums meet with a butterfly of shuffles.  Each
+// thread keeps UNROLL rows in flight.  Bandwidth-bound.
+template <typename T, int RDM, int LPR>
+__global__ void __launch_bounds__(256) project_small_kernel(CellPtrs X, CellPtrs U, int64_t rows, int d, int rd,
+                                                           int64_t T_, int m, CellPtrsMut out) {
+  constexpr int EPL = 16 / sizeof(T);  // elements per lane
+  constexpr int UNROLL = 4;
+  const int cell = blockIdx.y;
+  const T* x = static_cast<const T*>(X.p[cell]);
+  const T* u = static_cast<const T*>(U.p[cell]);
+  T* o = static_cast<T*>(out.p[cell]);
+  const int lane = threadIdx.x & 31;
+  const int pos = lane % LPR;
+  float uv[EPL][RDM];
+#pragma unroll
+  for (int e = 0; e < EPL; ++e)
+#pragma unroll
+    for (int r = 0; r < RDM; ++r) uv[e][r] = r < rd ? Elt<T>::to_f32(u[(int64_t)(pos * EPL + e) * rd + r]) : 0.f;
+  const int64_t groups = (int64_t)gridDim.x * (blockDim.x / LPR);
+  // the loop bound is warp-uniform (every lane reaches the shuffles)
+  const int64_t warp_gid = (int64_t)blockIdx.x * (blockDim.x / LPR) + (threadIdx.x & ~31) / LPR;
+  for (int64_t wbase = warp_gid; wbase < rows; wbase += groups * UNROLL) {
+    const int64_t base = wbase + lane / LPR;
+    uint4 raw[UNROLL];
+#pragma unroll
+    for (int q = 0; q < UNROLL; ++q) {
+      const int64_t row = base + q * groups;
+      raw[q] = row < rows ? *reinterpret_cast<const uint4*>(x + row * d + pos * EPL) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int q = 0; q < UNROLL; ++q) {
+      const int64_t row = base + q * groups;
+      const T* e = reinterpret_cast<const T*>(&raw[q]);
+      float acc[RDM];
+#pragma unroll
+      for (int r = 0; r < RDM; ++r) {
+        acc[r] = 0.f;
+#pragma unroll
+        for (int k = 0; k < EPL; ++k) acc[r] = fmaf(Elt<T>::to_f32(e[k]), uv[k][r], acc[r]);
+#pragma unroll
+        for (int off = LPR / 2; off > 0; off >>= 1) acc[r] += __shfl_xor_sync(0xffffffffu, acc[r], off);
+      }
+      if (pos < rd && row < rows) {
+        const int64_t h = row / T_, t = row % T_;
+        float v = 0.f;
+#pragma unroll
+        for (int r = 0; r < RDM; ++r)
+          if (r == pos) v = acc[r];
+        o[t * ((int64_t)m * rd) + h * rd + pos] = Elt<T>::from(v);
+      }
+    }
+  }
+}
+
 }  // namespace
 }  // namespace kvc
 
@@ -131,8 +187,25 @@ extern "C" int kvc_project_feature(int n_cells, const void* const* x, int64_t m,
     o.p[c] = x_proj_t[c];
   }
   const int64_t rows = m * t;
-  dim3 grid((unsigned)ceil_div(rows, TM), (unsigned)ceil_div(rd, TN), n_cells);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int lpr = (int)(d * dtype_size(dtype) / 16);
+  bool aligned = (d * dtype_size(dtype)) % 16 == 0;
+  for (int c = 0; c < n_cells; ++c) aligned = aligned && (reinterpret_cast<uintptr_t>(x[c]) & 15u) == 0;
+  if (rd <= 4 && aligned && (lpr == 8 || lpr == 16 || lpr == 32)) {
+    const int64_t per_block = 256 / lpr * 4;
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, per_block),
+                                                                    ceil_div(8LL * num_sms(), n_cells)));
+    dim3 grid(blocks, n_cells);
+#define KVC_PROJ(L)                                                                                   \
+  KVC_DISPATCH_DTYPE(dtype, T, project_small_kernel<T, 4, L><<<grid, 256, 0, st>>>(xa, ub, rows, d, rd, t, \
+                                                                                   (int)m, o))
+    if (lpr == 8) KVC_PROJ(8);
+    else if (lpr == 16) KVC_PROJ(16);
+    else KVC_PROJ(32);
+#undef KVC_PROJ
+    return check_launch("project_small_kernel");
+  }
+  dim3 grid((unsigned)ceil_div(rows, TM), (unsigned)ceil_div(rd, TN), n_cells);
   KVC_DISPATCH_DTYPE(dtype, T,
                      rowmat_kernel<T, T, true><<<grid, NT, 0, st>>>(xa, ub, rows, d, rd, t, (int)m, o));
   return check_launch("rowmat_kernel(project)");
