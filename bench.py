@@ -20,6 +20,7 @@ parallel replicas, weak scaling); the allocation is agreed once over NCCL
 from __future__ import annotations
 
 import argparse
+import dataclasses
 import json
 import os
 import statistics
@@ -40,13 +41,15 @@ FALLBACK_HBM_GBS = 6650.0
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=30)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="llama3-8b-kv-b1-t8192-bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--cpu-sample-layers", type=int, default=1)
+    ap.add_argument("--layers", type=int, default=0,
+                    help="override the workload's layer count (profiling a smaller case)")
     return ap.parse_args()
 
 
@@ -268,14 +271,16 @@ def run_ours(args, w):
         ev[2].record()
         return ev, payloads, outs
 
+    # nvidia-smi starts before the warm-up: its start-up stalls the GPU
+    # driver for up to a second and must not land in the timed region
+    clocks = ClockSampler(physical_gpu(local))
+    clocks.start()
+    time.sleep(1.5)
     for _ in range(args.warmup):
         step()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clocks = ClockSampler(physical_gpu(local))
-    clocks.start()
-    time.sleep(0.3)
     ops.trace_start()
     t_all0 = torch.cuda.Event(enable_timing=True)
     t_all1 = torch.cuda.Event(enable_timing=True)
@@ -292,6 +297,10 @@ def run_ours(args, w):
     log = ops.trace_stop()
     clk = clocks.stop()
 
+    if os.environ.get("KVC_BENCH_VERBOSE"):
+        for i, e in enumerate(evs):
+            print(f"step {i}: compress {e[0].elapsed_time(e[1]):.3f} ms, decompress {e[1].elapsed_time(e[2]):.3f} ms",
+                  file=sys.stderr)
     total_ms = t_all0.elapsed_time(t_all1) / args.steps
     comp_ms = sum(e[0].elapsed_time(e[1]) for e in evs) / args.steps
     dec_ms = sum(e[1].elapsed_time(e[2]) for e in evs) / args.steps
@@ -363,20 +372,23 @@ def e2e(comp, pairs, w, dev, world, steps: int = 2):
 
     host = [(k.cpu().pin_memory(), v.cpu().pin_memory()) for k, v in pairs]
     h2d = sum(k.numel() * k.element_size() * 2 for k, _ in host)
+    dev_in = [(torch.empty_like(k), torch.empty_like(v)) for k, v in pairs]
+    pinned_out: list[torch.Tensor] = []
 
     def once():
-        outs = []
-        for kh, vh in host:
-            kd = kh.to(dev, non_blocking=True)
-            vd = vh.to(dev, non_blocking=True)
+        slot = 0
+        for (kh, vh), (kd, vd) in zip(host, dev_in):
+            kd.copy_(kh, non_blocking=True)
+            vd.copy_(vh, non_blocking=True)
             kp, vp = comp.compress(kd, vd)
             for p in (kp, vp):
                 for t_ in p.data.values():
                     if t_.is_cuda:
-                        dst = torch.empty(t_.shape, dtype=t_.dtype, pin_memory=True)
-                        dst.copy_(t_, non_blocking=True)
-                        outs.append(dst)
-        return outs
+                        if slot == len(pinned_out):
+                            pinned_out.append(torch.empty(t_.shape, dtype=t_.dtype, pin_memory=True))
+                        pinned_out[slot].copy_(t_, non_blocking=True)
+                        slot += 1
+        return pinned_out[:slot]
 
     once()
     torch.cuda.synchronize()
@@ -404,6 +416,8 @@ def main():
     from kvcompress_b200.synthetic import WORKLOADS
 
     w = WORKLOADS[args.workload]
+    if args.layers:
+        w = dataclasses.replace(w, layers=args.layers)
     if args.impl == "reference":
         run_reference(args, w)
     else:

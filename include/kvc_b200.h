@@ -142,7 +142,7 @@ int kvc_core(int n_cells, const void* const* x_proj_t, const void* const* u_toke
  * reduces them with integer atomics on order-preserving bit patterns and the
  * result is still bit-reproducible.
  */
-size_t kvc_residual_stats_workspace_bytes(int n_cells, int64_t rows, int d);
+size_t kvc_residual_stats_workspace_bytes(int n_cells, int64_t rows, int d, int rd);
 int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, int64_t t, int d, int dtype,
                        const void* const* core, const void* const* u_token,
                        const void* const* u_feature, int rt, int rd, const float* proj,
@@ -159,7 +159,7 @@ int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, int64_t t, 
  * scale/zp.  arith_dtype: dtype of the divide/add in the per-tensor branch
  * (0-dim promotion, quantization.py:335-336); KVC_F32 elsewhere.
  */
-size_t kvc_residual_quant_workspace_bytes(int n_cells, int d);
+size_t kvc_residual_quant_workspace_bytes(int n_cells, int64_t rows, int d, int rd);
 int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, int64_t t, int d, int dtype,
                        const void* const* core, const void* const* u_token,
                        const void* const* u_feature, int rt, int rd, const float* proj,
@@ -177,7 +177,7 @@ int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, int64_t t, 
  * bits == 0: no residual term.  rt = rd = 0 / proj = NULL: the
  * quantize-only decoder (quantization_only.py:177-198).
  */
-size_t kvc_decompress_workspace_bytes(int n_cells, int d);
+size_t kvc_decompress_workspace_bytes(int n_cells, int64_t rows, int d, int rd);
 int kvc_decompress(int n_cells, const uint8_t* const* codes, const float* const* scale,
                    const int32_t* const* zp, int bits, int symmetric, int scale_mode,
                    int group_size, const void* const* core, const void* const* u_token,

@@ -48,13 +48,13 @@ _SIGNATURES = {
     "kvc_apply_basis": (I, [I, PP, I64, I, I, P, I, PP, P]),
     "kvc_core_workspace_bytes": (SZ, [I, I64, I, I, I]),
     "kvc_core": (I, [I, PP, PP, I64, I, I, I, I, PP, P, SZ, P]),
-    "kvc_residual_stats_workspace_bytes": (SZ, [I, I64, I]),
+    "kvc_residual_stats_workspace_bytes": (SZ, [I, I64, I, I]),
     "kvc_residual_stats": (I, [I, PP, I64, I64, I, I, PP, PP, PP, I, I, P, I, I, I, I, PP, PP, P,
                                SZ, P]),
-    "kvc_residual_quant_workspace_bytes": (SZ, [I, I]),
+    "kvc_residual_quant_workspace_bytes": (SZ, [I, I64, I, I]),
     "kvc_residual_quant": (I, [I, PP, I64, I64, I, I, PP, PP, PP, I, I, P, I, I, I, I, I, I, PP, PP,
                                PP, P, SZ, P]),
-    "kvc_decompress_workspace_bytes": (SZ, [I, I]),
+    "kvc_decompress_workspace_bytes": (SZ, [I, I64, I, I]),
     "kvc_decompress": (I, [I, PP, PP, PP, I, I, I, I, PP, PP, PP, I, I64, I64, I, I, I, P, I64, I64, I,
                            PP, P, SZ, P]),
     "kvc_set_kernel_policy": (I, [I]),

@@ -21,7 +21,7 @@
 namespace kvc {
 
 bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale_mode);
-size_t tc_residual_workspace(int n_cells, int d);
+size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd);
 int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
                        const void* const* core, const void* const* u_token, const void* const* u_feature,
                        int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
@@ -29,7 +29,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
                        uint8_t* const* codes, void* workspace, size_t ws_bytes, cudaStream_t st);
 bool tc_decompress_eligible(int out_dtype, int d, int rd, int bits, int symmetric, int scale_mode,
                             const float* proj);
-size_t tc_decompress_workspace(int n_cells, int d);
+size_t tc_decompress_workspace(int n_cells, int64_t rows, int d, int rd);
 int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* const* scale, int bits,
                          const void* const* core, const void* const* u_token, const void* const* u_feature,
                          int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd, const float* proj,
@@ -471,20 +471,20 @@ int blocks_per_cell(int64_t rows, int n_cells) {
 
 using namespace kvc;
 
-extern "C" size_t kvc_residual_stats_workspace_bytes(int n_cells, int64_t rows, int d) {
-  if (n_cells <= 0 || rows <= 0 || d <= 0) return 0;
+extern "C" size_t kvc_residual_stats_workspace_bytes(int n_cells, int64_t rows, int d, int rd) {
+  if (n_cells <= 0 || rows <= 0 || d <= 0 || rd < 0) return 0;
   return std::max((size_t)n_cells * blocks_per_cell(rows, n_cells) * 2 * d * sizeof(float),
-                  tc_residual_workspace(n_cells, d));
+                  tc_residual_workspace(n_cells, rows, d, rd));
 }
 
-extern "C" size_t kvc_residual_quant_workspace_bytes(int n_cells, int d) {
-  if (n_cells <= 0 || d <= 0) return 0;
-  return tc_residual_workspace(n_cells, d);
+extern "C" size_t kvc_residual_quant_workspace_bytes(int n_cells, int64_t rows, int d, int rd) {
+  if (n_cells <= 0 || rows <= 0 || d <= 0 || rd < 0) return 0;
+  return tc_residual_workspace(n_cells, rows, d, rd);
 }
 
-extern "C" size_t kvc_decompress_workspace_bytes(int n_cells, int d) {
-  if (n_cells <= 0 || d <= 0) return 0;
-  return tc_decompress_workspace(n_cells, d);
+extern "C" size_t kvc_decompress_workspace_bytes(int n_cells, int64_t rows, int d, int rd) {
+  if (n_cells <= 0 || rows <= 0 || d <= 0 || rd < 0) return 0;
+  return tc_decompress_workspace(n_cells, rows, d, rd);
 }
 
 extern "C" int kvc_set_kernel_policy(int policy) {
@@ -510,7 +510,8 @@ extern "C" int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, 
   if (rc) return rc;
   if (scale_mode == KVC_SCALE_GROUP) return fail(KVC_ERR_ARG, "kvc_residual_stats: group scales need no stats pass");
   cudaStream_t st0 = static_cast<cudaStream_t>(stream);
-  if (g_policy == 0 && tc_residual_eligible(dtype, d, rd, proj, scale_mode) && all_aligned(n_cells, x)) {
+  if (g_policy == 0 && tc_residual_eligible(dtype, d, rd, proj, scale_mode) && all_aligned(n_cells, x) &&
+      workspace && ws_bytes >= tc_residual_workspace(n_cells, m * t, d, rd)) {
     return tc_residual_launch(0, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
                               scale_mode, stat_dtype, KVC_F32, scale_out, zp_out, nullptr, workspace, ws_bytes,
                               st0);
@@ -555,7 +556,7 @@ extern "C" int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, 
   if (!dtype_ok(arith_dtype)) return fail(KVC_ERR_DTYPE, "kvc_residual_quant: bad arith dtype");
   if (g_policy == 0 && scale_mode != KVC_SCALE_GROUP && tc_residual_eligible(dtype, d, rd, proj, scale_mode) &&
       all_aligned(n_cells, x) && all_aligned(n_cells, codes) && workspace &&
-      ws_bytes >= tc_residual_workspace(n_cells, d)) {
+      ws_bytes >= tc_residual_workspace(n_cells, m * t, d, rd)) {
     return tc_residual_launch(1, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
                               scale_mode, stat_dtype, arith_dtype, scale, zp, codes, workspace, ws_bytes,
                               static_cast<cudaStream_t>(stream));
@@ -603,7 +604,7 @@ extern "C" int kvc_decompress(int n_cells, const uint8_t* const* codes, const fl
   }
   if (g_policy == 0 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj) &&
       all_aligned(n_cells, codes) && all_aligned(n_cells, out) && workspace &&
-      ws_bytes >= tc_decompress_workspace(n_cells, d)) {
+      ws_bytes >= tc_decompress_workspace(n_cells, m * t, d, rd)) {
     return tc_decompress_launch(n_cells, codes, scale, bits, core, u_token, u_feature, factor_dtype, m, t, d, rt,
                                 rd, proj, t0, t1, out, workspace, ws_bytes, static_cast<cudaStream_t>(stream));
   }

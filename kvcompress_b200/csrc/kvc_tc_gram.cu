@@ -7,15 +7,16 @@
 // Operands: an x tile of 128 rows staged by cp.async in the SWIZZLE_128B
 // layout is at the same time the MN-major A operand (x^T: M = feature,
 // K = row) and the MN-major B operand (x: N = feature); products of bf16
-// values are exact and accumulate in fp32 in TMEM.  Omega (fp32) is staged
-// per row, split in place into bf16 hi / lo (columns 0..31 / 32..63 of a
+// values are exact and accumulate in fp32 in TMEM.  Omega (fp32) is split
+// once by a small kernel into bf16 hi / lo (columns 0..31 / 32..63 of a
 // 64-column MN-major B tile), so Y carries ~16 mantissa bits of Omega.
 //
-// Work: the global (cell, tile) list is cut into one contiguous segment per
-// CTA; a CTA flushes its TMEM accumulator (two buffers) to a per-(cell,
-// segment) fp32 partial whenever the cell changes or its range ends, and a
-// second kernel sums the segments of each cell in order in fp64.  Results
-// are bit-reproducible for a given batch of cells.
+// Work: every cell is cut into segments of a fixed number of tiles that
+// depends on the row count only; CTAs take contiguous runs of segments, keep
+// one segment's sum in a TMEM accumulator (two buffers, so the flush of one
+// overlaps the next), flush it to a per-segment fp32 partial, and a second
+// kernel sums the segments of each cell in order in fp64.  The result of a
+// cell is therefore bit-identical however many cells share the launch.
 //
 // Warps 0-3 produce (cp.async, 4 stages), warp 4 issues tcgen05.mma,
 // warps 5-8 drain accumulators.  Every mbarrier wait is bounded.
@@ -47,12 +48,38 @@ struct GLayout {
 
 struct GramArgs {
   CellPtrs x;
-  const float* omega;  // rows x k, shared by every cell
+  const uint8_t* omega_pad;  // rows x 64 bf16: Omega hi in columns 0..31, lo in 32..63
   int k;
-  int64_t rows, tiles_per_cell, total_tiles, tpc;
-  int max_slots;
-  float* partial;      // [cell][slot][D][NACC]
+  int64_t rows, tiles_per_cell;
+  int64_t seg_tiles, segs_per_cell, total_segs;
+  float* partial;  // [segment][D][NACC]
 };
+
+// Walks the tiles of a run of segments in order.
+struct SegCursor {
+  int64_t s, t;  // segment, tile within the segment
+  __device__ __forceinline__ int64_t len(const GramArgs& A) const {
+    const int64_t first = (s % A.segs_per_cell) * A.seg_tiles;
+    return A.tiles_per_cell - first < A.seg_tiles ? A.tiles_per_cell - first : A.seg_tiles;
+  }
+  __device__ __forceinline__ int cell(const GramArgs& A) const { return (int)(s / A.segs_per_cell); }
+  __device__ __forceinline__ int64_t tile(const GramArgs& A) const {
+    return (s % A.segs_per_cell) * A.seg_tiles + t;
+  }
+  __device__ __forceinline__ void next(const GramArgs& A) {
+    if (++t == len(A)) {
+      ++s;
+      t = 0;
+    }
+  }
+};
+
+// Tiles before segment s in the global order.
+__host__ __device__ inline int64_t tiles_before(int64_t s, int64_t segs_per_cell, int64_t seg_tiles,
+                                                int64_t tiles_per_cell) {
+  const int64_t c = s / segs_per_cell, r = (s % segs_per_cell) * seg_tiles;
+  return c * tiles_per_cell + (r < tiles_per_cell ? r : tiles_per_cell);
+}
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   const uint32_t a = smem_u32(p);
@@ -71,13 +98,6 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) 
   return d;
 }
 
-__host__ __device__ inline int64_t seg_lo(int64_t cell, int64_t tiles_per_cell, int64_t tpc) {
-  return cell * tiles_per_cell / tpc;
-}
-__host__ __device__ inline int64_t seg_hi(int64_t cell, int64_t tiles_per_cell, int64_t tpc) {
-  return ((cell + 1) * tiles_per_cell - 1) / tpc;
-}
-
 __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -88,9 +108,10 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
   uint64_t* acce = accf + 2;
   uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + GLayout::OFF_TM);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t t_begin = (int64_t)blockIdx.x * A.tpc;
-  const int64_t t_end = t_begin + A.tpc < A.total_tiles ? t_begin + A.tpc : A.total_tiles;
-  const int n_my = (int)(t_end > t_begin ? t_end - t_begin : 0);
+  const int64_t s_begin = (int64_t)blockIdx.x * A.total_segs / gridDim.x;
+  const int64_t s_end = (int64_t)(blockIdx.x + 1) * A.total_segs / gridDim.x;
+  const int n_my = (int)(tiles_before(s_end, A.segs_per_cell, A.seg_tiles, A.tiles_per_cell) -
+                         tiles_before(s_begin, A.segs_per_cell, A.seg_tiles, A.tiles_per_cell));
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
@@ -113,83 +134,50 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
   const uint32_t tmem = *tm_holder;
 
   if (warp < 4) {
-    // ---------------- producers ----------------
-    const int ptid = threadIdx.x;        // 0..127: x chunk owner, and Omega row owner
-    const int chunk = ptid & 15;         // x: 16 chunks of 8 features per row
-    const int rsub = ptid >> 4;          // x: rows rsub, rsub + 8, ...
+    // ---------------- producers: one row of x and of Omega per thread ----------------
+    const int ptid = threadIdx.x;
     bool ok = true;
+    SegCursor ic{s_begin, 0}, pc{s_begin, 0};  // issue / processing positions
     auto issue = [&](int j) {
-      const int64_t g = t_begin + j;
-      const int cell = (int)(g / A.tiles_per_cell);
-      const int64_t r0 = (g % A.tiles_per_cell) * TILE;
+      const int cell = ic.cell(A);
+      const int64_t row = ic.tile(A) * TILE + ptid;
+      ic.next(A);
       const int st = j % NS;
       if (!mbar_wait(&empty[st], (uint32_t)((j / NS) & 1) ^ 1u, 0x401)) return false;
-      const uint32_t xs = sbase + st * GLayout::STAGE;
-      const uint32_t os = xs + GLayout::X_BYTES;
-      const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(A.x.p[cell]);
+      if (row < A.rows) {
+        const uint32_t xs = sbase + st * GLayout::STAGE;
+        const uint32_t os = xs + GLayout::X_BYTES;
+        const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(A.x.p[cell]) + row * D;
+        const uint8_t* om = A.omega_pad + row * (NY * 2);
 #pragma unroll
-      for (int i = 0; i < TILE / 8; ++i) {
-        const int r = rsub + 8 * i;
-        const int64_t row = r0 + r;
-        if (row < A.rows) cp_async16(xs + sw128_off(r, chunk * 8, TILE), x + row * D + chunk * 8);
+        for (int c = 0; c < D / 8; ++c) cp_async16(xs + sw128_off(ptid, c * 8, TILE), x + c * 8);
+#pragma unroll
+        for (int c = 0; c < NY / 8; ++c) cp_async16(os + sw128_off(ptid, c * 8, TILE), om + c * 16);
       }
-      const int64_t orow = r0 + ptid;
-      if (orow < A.rows)
-        for (int c = 0; c < A.k; ++c)
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(os + ptid * 128 + c * 4),
-                       "l"(A.omega + orow * A.k + c)
-                       : "memory");
       return true;
     };
     for (int j = 0; j < NS - 1; ++j) {
       if (ok && j < n_my) ok = issue(j);
       cp_async_commit();
     }
-    for (int it = 0; it < n_my && ok; ++it) {
+    for (int it = 0; it < n_my; ++it) {
       const int jn = it + NS - 1;
-      if (jn < n_my) ok = issue(jn);
+      if (ok && jn < n_my) ok = issue(jn);
       cp_async_commit();
-      if (!ok) break;
       cp_async_wait<NS - 1>();
+      if (!ok) continue;
       const int st = it % NS;
-      uint8_t* xs = smem + st * GLayout::STAGE;
-      uint8_t* os = xs + GLayout::X_BYTES;
-      const int64_t g = t_begin + it;
-      const int64_t r0 = (g % A.tiles_per_cell) * TILE;
-      // zero the x rows past the end of the cell
-      if (r0 + TILE > A.rows) {
+      const int64_t row = pc.tile(A) * TILE + ptid;
+      pc.next(A);
+      if (row >= A.rows) {  // rows past the end of the cell contribute zeros
+        uint8_t* xs = smem + st * GLayout::STAGE;
+        uint8_t* os = xs + GLayout::X_BYTES;
 #pragma unroll
-        for (int i = 0; i < TILE / 8; ++i) {
-          const int r = rsub + 8 * i;
-          if (r0 + r >= A.rows)
-            *reinterpret_cast<uint4*>(xs + sw128_off(r, chunk * 8, TILE)) = make_uint4(0, 0, 0, 0);
-        }
-      }
-      // Omega row ptid: fp32 (staged linearly in this row's 128 bytes) -> bf16 hi / lo, swizzled in place
-      {
-        float v[32];
-        const bool valid = r0 + ptid < A.rows;
-        const float* src = reinterpret_cast<const float*>(os + ptid * 128);
+        for (int c = 0; c < D / 8; ++c)
+          *reinterpret_cast<uint4*>(xs + sw128_off(ptid, c * 8, TILE)) = make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int c = 0; c < 32; ++c) v[c] = (valid && c < A.k) ? src[c] : 0.f;
-        uint16_t hi[32], lo[32];
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const __nv_bfloat16 h = __float2bfloat16_rn(v[c]);
-          const __nv_bfloat16 l = __float2bfloat16_rn(v[c] - __bfloat162float(h));
-          hi[c] = *reinterpret_cast<const uint16_t*>(&h);
-          lo[c] = *reinterpret_cast<const uint16_t*>(&l);
-        }
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          const uint16_t* s16 = q < 4 ? hi + 8 * q : lo + 8 * (q - 4);
-          uint4 w;
-          w.x = s16[0] | (uint32_t)s16[1] << 16;
-          w.y = s16[2] | (uint32_t)s16[3] << 16;
-          w.z = s16[4] | (uint32_t)s16[5] << 16;
-          w.w = s16[6] | (uint32_t)s16[7] << 16;
-          *reinterpret_cast<uint4*>(os + sw128_off(ptid, q * 8, TILE)) = w;
-        }
+        for (int c = 0; c < NY / 8; ++c)
+          *reinterpret_cast<uint4*>(os + sw128_off(ptid, c * 8, TILE)) = make_uint4(0, 0, 0, 0);
       }
       fence_async_smem();
       mbar_arrive(&full[st]);
@@ -201,14 +189,12 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
       // A = x^T and B = x, both MN-major; D[feature][feature / omega column]
       const uint32_t id_g = idesc_f16(D, D, true) | (1u << 15) | (1u << 16);
       const uint32_t id_y = idesc_f16(D, NY, true) | (1u << 15) | (1u << 16);
-      int cur_cell = -1, seg = -1, it = 0;
+      int seg = -1, it = 0;
       bool first = true;
-      for (; it < n_my; ++it) {
-        const int64_t g = t_begin + it;
-        const int cell = (int)(g / A.tiles_per_cell);
-        if (cell != cur_cell) {
-          if (cur_cell >= 0) umma_commit(&accf[seg & 1]);  // close the previous segment
-          cur_cell = cell;
+      SegCursor mc{s_begin, 0};
+      for (; it < n_my; ++it, mc.next(A)) {
+        if (mc.t == 0) {
+          if (seg >= 0) umma_commit(&accf[seg & 1]);  // close the previous segment
           ++seg;
           if (!mbar_wait(&acce[seg & 1], (uint32_t)((seg >> 1) & 1) ^ 1u, 0x402)) break;
           tc_fence_after();
@@ -231,7 +217,7 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
         first = false;
         umma_commit(&empty[st]);
       }
-      if (cur_cell >= 0 && it == n_my) umma_commit(&accf[seg & 1]);
+      if (seg >= 0 && it == n_my) umma_commit(&accf[seg & 1]);
       if (seg >= 0) mbar_wait(&accf[seg & 1], (uint32_t)((seg >> 1) & 1), 0x404);
     }
     __syncwarp();
@@ -239,15 +225,11 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
     // ---------------- epilogue: flush one segment's accumulator ----------------
     const int lg = warp & 3;
     const int feat = lg * 32 + lane;
-    int cur_cell = -1, seg = -1;
-    for (int it = 0; it <= n_my; ++it) {
-      const int cell = it < n_my ? (int)((t_begin + it) / A.tiles_per_cell) : -2;
-      if (cell == cur_cell) continue;
-      if (cur_cell >= 0) {
+    for (int seg = 0; seg < (int)(s_end - s_begin); ++seg) {
+      {
         if (!mbar_wait(&accf[seg & 1], (uint32_t)((seg >> 1) & 1), 0x405)) break;
         tc_fence_after();
-        const int slot = (int)(blockIdx.x - seg_lo(cur_cell, A.tiles_per_cell, A.tpc));
-        float* dst = A.partial + (((int64_t)cur_cell * A.max_slots + slot) * D + feat) * NACC;
+        float* dst = A.partial + ((s_begin + seg) * D + feat) * NACC;
 #pragma unroll
         for (int c = 0; c < NACC / 32; ++c) {
           float v[32];
@@ -259,9 +241,6 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
         tc_fence_before();
         mbar_arrive(&acce[seg & 1]);
       }
-      if (cell < 0) break;
-      cur_cell = cell;
-      ++seg;
     }
   }
   tc_fence_before();
@@ -272,18 +251,32 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
   }
 }
 
+// Omega (rows x k fp32) -> rows x 64 bf16: hi = bf16(w), lo = bf16(w - hi).
+__global__ void omega_pad_kernel(const float* __restrict__ omega, int64_t rows, int k, uint8_t* out) {
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < rows * 32;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = idx / 32;
+    const int c = (int)(idx % 32);
+    const float w = c < k ? omega[r * k + c] : 0.f;
+    const __nv_bfloat16 h = __float2bfloat16_rn(w);
+    const __nv_bfloat16 l = __float2bfloat16_rn(w - __bfloat162float(h));
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out + r * (NY * 2));
+    o[c] = h;
+    o[32 + c] = l;
+  }
+}
+
 // Sum the segments of each cell in order (fp64) into [G | Y | trace].
-__global__ void tc_gram_reduce_kernel(const float* __restrict__ partial, int n_cells, int64_t tiles_per_cell,
-                                      int64_t tpc, int max_slots, int k, double* __restrict__ out,
-                                      int64_t stride) {
+__global__ void tc_gram_reduce_kernel(const float* __restrict__ partial, int n_cells, int64_t segs_per_cell,
+                                      int k, double* __restrict__ out, int64_t stride) {
   const int64_t total = (int64_t)n_cells * D * (D + k);
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
     const int cell = (int)(idx / ((int64_t)D * (D + k)));
     const int64_t e = idx % ((int64_t)D * (D + k));
     const int i = (int)(e / (D + k)), j = (int)(e % (D + k));
-    const int nseg = (int)(seg_hi(cell, tiles_per_cell, tpc) - seg_lo(cell, tiles_per_cell, tpc) + 1);
-    const float* base = partial + ((int64_t)cell * max_slots * D + i) * NACC;
+    const int nseg = (int)segs_per_cell;
+    const float* base = partial + ((int64_t)cell * segs_per_cell * D + i) * NACC;
     double s = 0.0;
     if (j < D) {
       for (int sl = 0; sl < nseg; ++sl) s += (double)base[(int64_t)sl * D * NACC + j];
@@ -298,20 +291,19 @@ __global__ void tc_gram_reduce_kernel(const float* __restrict__ partial, int n_c
 }
 
 struct GPlan {
-  int64_t tiles_per_cell, total, tpc;
-  int ctas, max_slots;
+  int64_t tiles_per_cell, seg_tiles, segs_per_cell, total_segs;
+  int ctas;
 };
 
+// The segment length depends on the row count only (about 16 segments per
+// cell, 4..32 tiles each), never on how many cells share the launch.
 GPlan gplan(int n_cells, int64_t rows) {
   GPlan p;
   p.tiles_per_cell = ceil_div(rows, TILE);
-  p.total = p.tiles_per_cell * n_cells;
-  p.tpc = std::max<int64_t>(1, ceil_div(p.total, num_sms()));
-  p.ctas = (int)ceil_div(p.total, p.tpc);
-  int ms = 1;
-  for (int c = 0; c < n_cells; ++c)
-    ms = std::max<int>(ms, (int)(seg_hi(c, p.tiles_per_cell, p.tpc) - seg_lo(c, p.tiles_per_cell, p.tpc) + 1));
-  p.max_slots = ms;
+  p.seg_tiles = std::min<int64_t>(p.tiles_per_cell, std::min<int64_t>(32, std::max<int64_t>(4, ceil_div(p.tiles_per_cell, 16))));
+  p.segs_per_cell = ceil_div(p.tiles_per_cell, p.seg_tiles);
+  p.total_segs = p.segs_per_cell * n_cells;
+  p.ctas = (int)std::min<int64_t>(p.total_segs, num_sms());
   return p;
 }
 
@@ -319,26 +311,38 @@ GPlan gplan(int n_cells, int64_t rows) {
 
 bool tc_gram_eligible(int dtype, int p, int k) { return dtype == KVC_BF16 && p == D && k <= 32; }
 
+static size_t partial_bytes(int n_cells, const GPlan& p) {
+  (void)n_cells;
+  return ((size_t)p.total_segs * D * NACC * sizeof(float) + 255) & ~(size_t)255;
+}
+
 size_t tc_gram_workspace(int n_cells, int64_t rows) {
   GPlan p = gplan(n_cells, rows);
-  return (size_t)n_cells * p.max_slots * D * NACC * sizeof(float);
+  return partial_bytes(n_cells, p) + (size_t)rows * NY * 2;
 }
 
 int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float* omega, int k, double* out,
                    void* workspace, size_t ws_bytes, cudaStream_t st) {
   GPlan p = gplan(n_cells, rows);
-  if (!workspace || ws_bytes < (size_t)n_cells * p.max_slots * D * NACC * sizeof(float))
+  if (!workspace || ws_bytes < partial_bytes(n_cells, p) + (size_t)rows * NY * 2)
     return fail(KVC_ERR_WORKSPACE, "tensor-core gram: workspace too small");
   GramArgs g;
   memset(&g, 0, sizeof(g));
   for (int c = 0; c < n_cells; ++c) g.x.p[c] = a[c];
-  g.omega = omega;
+  uint8_t* opad = static_cast<uint8_t*>(workspace) + partial_bytes(n_cells, p);
+  g.omega_pad = opad;
   g.k = k;
+  {
+    const int blocks = (int)std::min<int64_t>(ceil_div(rows * 32, 256), 16LL * num_sms());
+    omega_pad_kernel<<<blocks, 256, 0, st>>>(omega, rows, k, opad);
+    int rc0 = check_launch("omega_pad_kernel");
+    if (rc0) return rc0;
+  }
   g.rows = rows;
   g.tiles_per_cell = p.tiles_per_cell;
-  g.total_tiles = p.total;
-  g.tpc = p.tpc;
-  g.max_slots = p.max_slots;
+  g.seg_tiles = p.seg_tiles;
+  g.segs_per_cell = p.segs_per_cell;
+  g.total_segs = p.total_segs;
   g.partial = static_cast<float*>(workspace);
   cudaError_t e = cudaFuncSetAttribute(tc_gram_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)GLayout::BYTES);
@@ -349,8 +353,7 @@ int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float*
   const int64_t stride = (int64_t)D * D + (int64_t)D * k + 1;
   const int64_t total = (int64_t)n_cells * D * (D + k);
   const int blocks = (int)std::min<int64_t>(ceil_div(total, 256), 8 * num_sms());
-  tc_gram_reduce_kernel<<<blocks, 256, 0, st>>>(g.partial, n_cells, p.tiles_per_cell, p.tpc, p.max_slots, k, out,
-                                                stride);
+  tc_gram_reduce_kernel<<<blocks, 256, 0, st>>>(g.partial, n_cells, p.segs_per_cell, k, out, stride);
   return check_launch("tc_gram_reduce_kernel");
 }
 

@@ -74,6 +74,8 @@ struct TcResArgs {
   int rt, rd;
   const void* bops;    // NTERM swizzled B tiles (global)
   int32_t* minmax;     // STATS: [cell][2][d] ordered ints (min, max)
+  const float* tmp;    // [cell][row][rd]: sum_a core[h][a][r] u_token[t][a], rounded to the cell dtype
+  const float* ud32;   // [cell][d][rd]: u_feature as float
   int bits, symmetric, scale_mode, arith_dtype, code_bytes;
 };
 
@@ -101,7 +103,7 @@ __device__ __forceinline__ void unpack8(const uint4& raw, float (&v)[8]) {
 // ------------------------------------------------------------------------
 template <typename T, int D, int NTERM, int MODE, int RDM>
 __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
-  using L = Layout<D, NTERM>;
+  using L = Layout<D, NTERM, TILE_M * RDM * 4>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -145,27 +147,30 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
   const uint32_t tmem = *tm_holder;
 
   if (warp < 4) {
-    // ---------------- producers: cp.async x into the A stage, R in place ----------------
-    constexpr int CH = D / 8;     // 16-byte chunks per row
-    constexpr int RPI = 32 / CH;  // rows per warp iteration
-    constexpr int NIT = 32 / RPI;
-    const int chunk = lane % CH, sub = lane / CH;
-    float udv[8][RDM];
-    int ud_cell = -1;
+    // ---------------- producers: one row per thread ----------------
+    // cp.async the row of x into the swizzled A stage (and its Tucker row
+    // term into a private slot), then R = x - Tucker in place.
+    constexpr int CH = D / 8;
+    const int ptid = threadIdx.x;  // row within the tile
+    float* tslot = reinterpret_cast<float*>(smem + L::OFF_X);  // [stage][128][RDM]
     bool ok = true;
-    auto issue = [&](int j) {  // copies of the j-th local tile into its stage
+    auto issue = [&](int j) {
       const int64_t g = tile_begin + j;
       const int cell = (int)(g / A.tiles_per_cell);
-      const int64_t r0 = (g % A.tiles_per_cell) * TILE_M;
+      const int64_t row = (g % A.tiles_per_cell) * TILE_M + ptid;
       const int st = j % NSTAGE;
       if (!mbar_wait(&empty[st], (uint32_t)((j / NSTAGE) & 1) ^ 1u, 0x101)) return false;
-      const T* x = static_cast<const T*>(A.x.p[cell]);
-      const uint32_t a_s = sbase + L::OFF_A + st * L::A_BYTES;
+      if (row < A.rows) {
+        const T* x = static_cast<const T*>(A.x.p[cell]) + row * D;
+        const uint32_t a_s = sbase + L::OFF_A + st * L::A_BYTES;
 #pragma unroll
-      for (int i = 0; i < NIT; ++i) {
-        const int rloc = warp * 32 + i * RPI + sub;
-        const int64_t row = r0 + rloc;
-        if (row < A.rows) cp_async16(a_s + sw128_off(rloc, chunk * 8, TILE_M), x + row * D + chunk * 8);
+        for (int c = 0; c < CH; ++c) cp_async16(a_s + sw128_off(ptid, c * 8, TILE_M), x + c * 8);
+        if (A.rt > 0) {
+          const float* tp = A.tmp + ((int64_t)cell * A.rows + row) * A.rd;
+          const uint32_t ts = smem_u32(tslot + (st * TILE_M + ptid) * RDM);
+          for (int r = 0; r < A.rd; ++r)
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ts + r * 4), "l"(tp + r) : "memory");
+        }
       }
       return true;
     };
@@ -173,69 +178,52 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
       if (ok && j < n_my) ok = issue(j);
       cp_async_commit();
     }
-    for (int it = 0; it < n_my && ok; ++it) {
+    for (int it = 0; it < n_my; ++it) {
       const int jn = it + NSTAGE - 1;
-      if (jn < n_my) ok = issue(jn);
+      if (ok && jn < n_my) ok = issue(jn);
       cp_async_commit();
-      if (!ok) break;
       cp_async_wait<NSTAGE - 1>();
+      if (!ok) continue;  // keep the loop shape; the MMA side times out too
+      const int st = it % NSTAGE;
       const int64_t g = tile_begin + it;
       const int cell = (int)(g / A.tiles_per_cell);
-      const int64_t r0 = (g % A.tiles_per_cell) * TILE_M;
-      uint8_t* As = smem + L::OFF_A + (it % NSTAGE) * L::A_BYTES;
-      const T* core = nullptr;
-      const T* ut = nullptr;
-      if (A.rt > 0) {
-        core = static_cast<const T*>(A.core.p[cell]);
-        ut = static_cast<const T*>(A.ut.p[cell]);
-        if (cell != ud_cell) {
-          ud_cell = cell;
-          const T* ud = static_cast<const T*>(A.ud.p[cell]);
+      const int64_t row = (g % A.tiles_per_cell) * TILE_M + ptid;
+      uint8_t* As = smem + L::OFF_A + st * L::A_BYTES;
+      if (row >= A.rows) {
 #pragma unroll
-          for (int e = 0; e < 8; ++e)
+        for (int c = 0; c < CH; ++c)
+          *reinterpret_cast<uint4*>(As + sw128_off(ptid, c * 8, TILE_M)) = make_uint4(0, 0, 0, 0);
+      } else if (A.rt > 0) {
+        float tv[RDM];
 #pragma unroll
-            for (int r = 0; r < RDM; ++r)
-              udv[e][r] = r < A.rd ? Elt<T>::to_f32(ud[(int64_t)(chunk * 8 + e) * A.rd + r]) : 0.f;
-        }
-      }
-#pragma unroll 2
-      for (int i = 0; i < NIT; ++i) {
-        const int rloc = warp * 32 + i * RPI + sub;
-        const int64_t row = r0 + rloc;
-        uint4* slot = reinterpret_cast<uint4*>(As + sw128_off(rloc, chunk * 8, TILE_M));
-        float xv[8];
-        if (row < A.rows) {
-          if (A.rt == 0) continue;  // R = x, already in place
+        for (int r = 0; r < RDM; ++r) tv[r] = r < A.rd ? tslot[(st * TILE_M + ptid) * RDM + r] : 0.f;
+        const float4* ud = reinterpret_cast<const float4*>(A.ud32 + (int64_t)cell * D * RDM);
+#pragma unroll 4
+        for (int c = 0; c < CH; ++c) {
+          uint4* slot = reinterpret_cast<uint4*>(As + sw128_off(ptid, c * 8, TILE_M));
+          float xv[8];
           unpack8<T>(*slot, xv);
-          const int64_t h = row / A.t, t = row % A.t;
-          float tmp[RDM];
+          float u[8 * RDM];
 #pragma unroll
-          for (int r = 0; r < RDM; ++r) {
-            float acc = 0.f;
-            if (r < A.rd) {
-              const T* cr = core + h * A.rt * A.rd + r;
-              const T* ur = ut + t * A.rt;
-              for (int a = 0; a < A.rt; ++a)
-                acc = fmaf(Elt<T>::to_f32(cr[(int64_t)a * A.rd]), Elt<T>::to_f32(ur[a]), acc);
-            }
-            tmp[r] = Elt<T>::round(acc);
+          for (int q = 0; q < 2 * RDM; ++q) {
+            const float4 f = __ldg(ud + c * 2 * RDM + q);
+            u[4 * q] = f.x;
+            u[4 * q + 1] = f.y;
+            u[4 * q + 2] = f.z;
+            u[4 * q + 3] = f.w;
           }
 #pragma unroll
           for (int e = 0; e < 8; ++e) {
             float rec = 0.f;
 #pragma unroll
-            for (int r = 0; r < RDM; ++r)
-              if (r < A.rd) rec = fmaf(tmp[r], udv[e][r], rec);
+            for (int r = 0; r < RDM; ++r) rec = fmaf(tv[r], u[e * RDM + r], rec);
             xv[e] = Elt<T>::round(xv[e] - Elt<T>::round(rec));
           }
-        } else {
-#pragma unroll
-          for (int e = 0; e < 8; ++e) xv[e] = 0.f;
+          *slot = pack8<T>(xv);
         }
-        *slot = pack8<T>(xv);
       }
       fence_async_smem();
-      mbar_arrive(&full[it % NSTAGE]);
+      mbar_arrive(&full[st]);
     }
     cp_async_wait<0>();
   } else if (warp == MMA_WARP) {
@@ -408,6 +396,37 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
   }
 }
 
+// Per-row Tucker term for the tensor-core kernels:
+//   tmp[cell][row][r] = sum_a core[h][a][r] * u_token[t][a]   (rows of [t0, t1))
+// rounded to `round_dt` (the compress side rounds it to the cell dtype like
+// the reference's einsum intermediate; the decode side keeps fp32), and
+// u_feature as float padded to rdm columns.
+__global__ void tucker_rows_kernel(CellPtrs core, CellPtrs ut, CellPtrs ud, int fdt, int round_dt_, int64_t m,
+                                   int64_t t0, int64_t tl, int rt, int rd, int d, int rdm, float* tmp,
+                                   float* ud32) {
+  const int cell = blockIdx.y;
+  const int64_t rows = m * tl;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < rows * rd;
+       idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = idx / rd;
+    const int r = (int)(idx % rd);
+    const int64_t h = row / tl, t = t0 + row % tl;
+    float acc = 0.f;
+    for (int a = 0; a < rt; ++a)
+      acc = fmaf(load_dt(core.p[cell], (h * rt + a) * rd + r, fdt), load_dt(ut.p[cell], t * rt + a, fdt), acc);
+    tmp[(int64_t)cell * rows * rd + idx] = round_dt(acc, round_dt_);
+  }
+  if (blockIdx.x == 0)
+    for (int i = threadIdx.x; i < d * rdm; i += blockDim.x) {
+      const int j = i / rdm, r = i % rdm;
+      ud32[(int64_t)cell * d * rdm + i] = r < rd ? load_dt(ud.p[cell], (int64_t)j * rd + r, fdt) : 0.f;
+    }
+}
+
+static int rdm_of(int rd) { return rd <= 1 ? 1 : (rd <= 4 ? 4 : 16); }
+
+static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
 // min / max arrays to their identities (ordered ints of +inf / -inf).
 __global__ void minmax_init_kernel(int32_t* mm, int n_cells, int d) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -468,6 +487,8 @@ struct TcDecArgs {
   int tiles_per_cta;
   int rt, rd, bits, code_bytes, factor_dtype;
   const uint8_t* bops;  // per cell: 2 swizzled B tiles of diag(scale) Pi
+  const float* tmp;     // [cell][out row][rd] fp32 Tucker row term
+  const float* ud32;    // [cell][d][rdm]
 };
 
 template <typename TOut, int D, int RDM, int BITS>
@@ -496,7 +517,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A)
     for (int i = threadIdx.x; i < (int)(L::B_BYTES / 16); i += NTHREADS) dst[i] = src[i];
   }
   if (A.rt > 0)
-    for (int i = threadIdx.x; i < D * A.rd; i += NTHREADS) ud_s[i] = load_dt(A.ud.p[cell], i, A.factor_dtype);
+    for (int i = threadIdx.x; i < D * RDM; i += NTHREADS) ud_s[i] = A.ud32[(int64_t)cell * D * RDM + i];
   if (threadIdx.x == 0) {
     for (int i = 0; i < NSTAGE; ++i) {
       mbar_init(&full[i], 128);
@@ -621,26 +642,14 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A)
     TOut* out = static_cast<TOut*>(A.out.p[cell]);
     for (int it = 0; it < n_my; ++it) {
       const int ac = it & 1;
-      if (!mbar_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x311)) break;
-      tc_fence_after();
       const int64_t orow = (tile_begin + it) * TILE_M + rloc;
       const bool valid = orow < A.rows;
-      float tmp[RDM];
+      float tmp[RDM];  // loaded before the wait so the latency overlaps it
 #pragma unroll
-      for (int r = 0; r < RDM; ++r) tmp[r] = 0.f;
-      if (valid && A.rt > 0) {
-        const int64_t h = orow / tl, t = A.t0 + orow % tl;
-#pragma unroll
-        for (int r = 0; r < RDM; ++r) {
-          if (r < A.rd) {
-            float acc = 0.f;
-            for (int a = 0; a < A.rt; ++a)
-              acc = fmaf(load_dt(A.core.p[cell], (h * A.rt + a) * A.rd + r, A.factor_dtype),
-                         load_dt(A.ut.p[cell], t * A.rt + a, A.factor_dtype), acc);
-            tmp[r] = acc;
-          }
-        }
-      }
+      for (int r = 0; r < RDM; ++r)
+        tmp[r] = (valid && A.rt > 0 && r < A.rd) ? __ldg(A.tmp + ((int64_t)cell * A.rows + orow) * A.rd + r) : 0.f;
+      if (!mbar_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x311)) break;
+      tc_fence_after();
 #pragma unroll
       for (int cc = 0; cc < NCH; ++cc) {
         const int c = half * NCH + cc;
@@ -654,7 +663,7 @@ __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A)
               float rec = 0.f;
 #pragma unroll
               for (int r = 0; r < RDM; ++r)
-                if (r < A.rd) rec = fmaf(tmp[r], ud_s[(c * 32 + j) * A.rd + r], rec);
+                rec = fmaf(tmp[r], ud_s[(c * 32 + j) * RDM + r], rec);
               o[j] = __fadd_rn(rec, v[j]);
             } else {
               o[j] = v[j];
@@ -714,8 +723,9 @@ bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale
          (scale_mode == KVC_SCALE_CHANNEL || scale_mode == KVC_SCALE_TENSOR);
 }
 
-size_t tc_residual_workspace(int n_cells, int d) {
-  return (size_t)3 * d * d * 2 + (size_t)n_cells * 2 * d * sizeof(int32_t) + 256;
+size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd) {
+  return align256((size_t)3 * d * d * 2) + align256((size_t)n_cells * 2 * d * sizeof(int32_t)) +
+         align256((size_t)n_cells * d * rdm_of(rd) * 4) + align256((size_t)n_cells * rows * rd * 4);
 }
 
 static int prep_rotation(const float* proj, int d, uint8_t* bops, cudaStream_t st) {
@@ -736,7 +746,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
                        int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
                        int stat_dtype, int arith_dtype, float* const* scale, int32_t* const* zp,
                        uint8_t* const* codes, void* workspace, size_t ws_bytes, cudaStream_t st) {
-  if (!workspace || ws_bytes < tc_residual_workspace(n_cells, d))
+  if (!workspace || ws_bytes < tc_residual_workspace(n_cells, m * t, d, rd))
     return fail(KVC_ERR_WORKSPACE, "tensor-core residual: workspace too small");
   TcResArgs a;
   memset(&a, 0, sizeof(a));
@@ -764,11 +774,31 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   plan_global(a, n_cells, a.rows);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint8_t* bops = ws;
-  int32_t* mm = reinterpret_cast<int32_t*>(ws + (size_t)3 * d * d * 2);
+  size_t off = align256((size_t)3 * d * d * 2);
+  int32_t* mm = reinterpret_cast<int32_t*>(ws + off);
+  off += align256((size_t)n_cells * 2 * d * sizeof(int32_t));
+  float* ud32 = reinterpret_cast<float*>(ws + off);
+  off += align256((size_t)n_cells * d * rdm_of(rd) * 4);
+  float* tmp = reinterpret_cast<float*>(ws + off);
   a.bops = bops;
   a.minmax = mm;
+  a.tmp = tmp;
+  a.ud32 = ud32;
   int rc = prep_rotation(proj, d, bops, st);
   if (rc) return rc;
+  if (rt > 0) {
+    CellPtrs cp, up, dp;
+    for (int c = 0; c < n_cells; ++c) {
+      cp.p[c] = core[c];
+      up.p[c] = u_token[c];
+      dp.p[c] = u_feature[c];
+    }
+    const int64_t rows = m * t;
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows * rd, 256), 1024));
+    tucker_rows_kernel<<<dim3(blocks, n_cells), 256, 0, st>>>(cp, up, dp, KVC_BF16, KVC_BF16, m, 0, t, rt, rd, d,
+                                                              rdm_of(rd), tmp, ud32);
+    if ((rc = check_launch("tucker_rows_kernel"))) return rc;
+  }
   const dim3 grid((unsigned)ceil_div(a.total_tiles, a.tiles_per_cta));
   if (mode == MODE_STATS) {
     minmax_init_kernel<<<(n_cells * 2 * d + 255) / 256, 256, 0, st>>>(mm, n_cells, d);
@@ -777,7 +807,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
 #define KVC_TC_RES(DD, MODEV, RR)                                                              \
   do {                                                                                         \
     auto kern = tc_residual_kernel<__nv_bfloat16, DD, 3, MODEV, RR>;                           \
-    const size_t sm = Layout<DD, 3>::BYTES;                                                    \
+    const size_t sm = Layout<DD, 3, TILE_M * RR * 4>::BYTES;                                   \
     if ((rc = set_smem(kern, sm))) return rc;                                                  \
     kern<<<grid, NTHREADS, sm, st>>>(a);                                                       \
   } while (0)
@@ -815,14 +845,17 @@ bool tc_decompress_eligible(int out_dtype, int d, int rd, int bits, int symmetri
          scale_mode == KVC_SCALE_CHANNEL && proj != nullptr;
 }
 
-size_t tc_decompress_workspace(int n_cells, int d) { return (size_t)n_cells * 2 * d * d * 2 + 256; }
+size_t tc_decompress_workspace(int n_cells, int64_t rows, int d, int rd) {
+  return align256((size_t)n_cells * 2 * d * d * 2) + align256((size_t)n_cells * d * rdm_of(rd) * 4) +
+         align256((size_t)n_cells * rows * rd * 4);
+}
 
 int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* const* scale, int bits,
                          const void* const* core, const void* const* u_token, const void* const* u_feature,
                          int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd, const float* proj,
                          int64_t t0, int64_t t1, void* const* out, void* workspace, size_t ws_bytes,
                          cudaStream_t st) {
-  if (!workspace || ws_bytes < tc_decompress_workspace(n_cells, d))
+  if (!workspace || ws_bytes < tc_decompress_workspace(n_cells, m * t, d, rd))
     return fail(KVC_ERR_WORKSPACE, "tensor-core decompress: workspace too small");
   TcDecArgs a;
   memset(&a, 0, sizeof(a));
@@ -852,10 +885,22 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
   a.code_bytes = (d * bits + 7) / 8;
   a.factor_dtype = factor_dtype;
   uint8_t* bops = static_cast<uint8_t*>(workspace);
+  size_t off = align256((size_t)n_cells * 2 * d * d * 2);
+  float* ud32 = reinterpret_cast<float*>(bops + off);
+  off += align256((size_t)n_cells * d * rdm_of(rd) * 4);
+  float* tmp = reinterpret_cast<float*>(bops + off);
   a.bops = bops;
+  a.tmp = tmp;
+  a.ud32 = ud32;
   prep_decode_kernel<<<dim3((d * d + 255) / 256, n_cells), 256, 0, st>>>(proj, sc, d, bops);
   int rc = check_launch("prep_decode_kernel");
   if (rc) return rc;
+  if (rt > 0) {
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(a.rows * rd, 256), 1024));
+    tucker_rows_kernel<<<dim3(blocks, n_cells), 256, 0, st>>>(a.core, a.ut, a.ud, factor_dtype, KVC_F32, m, t0,
+                                                              t1 - t0, rt, rd, d, rdm_of(rd), tmp, ud32);
+    if ((rc = check_launch("tucker_rows_kernel"))) return rc;
+  }
   const dim3 grid((unsigned)ceil_div(a.tiles_per_cell, a.tiles_per_cta), n_cells);
 #define KVC_TC_DEC3(DD, RR, BB)                                             \
   do {                                                                      \

@@ -239,7 +239,7 @@ def residual_stats(xs, factors, proj, *, bits: int, symmetric: bool, scale_mode:
     del ns
     cp, up, dp, rt, rd = _factor_ptrs(factors, n)
     L = lib()
-    ws_n = L.kvc_residual_stats_workspace_bytes(n, m * t, d)
+    ws_n = L.kvc_residual_stats_workspace_bytes(n, m * t, d, rd)
     ws = workspace(ws_n, dev)
     with _Stage("residual_stats", 2, n * xs[0].numel() * xs[0].element_size()):
         check(L.kvc_residual_stats(n, ptr_array(x.data_ptr() for x in xs), m, t, d, _code(xs[0].dtype),
@@ -269,7 +269,7 @@ def residual_quant(xs, factors, proj, scales, zps, *, bits: int, symmetric: bool
     cb = (d * bits + 7) // 8
     codes = [torch.empty(m * t, cb, dtype=torch.uint8, device=dev) for _ in xs]
     cp, up, dp, rt, rd = _factor_ptrs(factors, n)
-    ws = workspace(lib().kvc_residual_quant_workspace_bytes(n, d), dev)
+    ws = workspace(lib().kvc_residual_quant_workspace_bytes(n, m * t, d, rd), dev)
     nbytes = n * (xs[0].numel() * xs[0].element_size() + codes[0].numel())
     with _Stage("residual_quant", 1, nbytes):
         check(lib().kvc_residual_quant(n, ptr_array(x.data_ptr() for x in xs), m, t, d,
@@ -304,7 +304,7 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
     else:
         c_arr = s_arr = z_arr = ptr_array([0] * n)
     dev0 = out[0].device
-    ws = workspace(lib().kvc_decompress_workspace_bytes(n, d), dev0)
+    ws = workspace(lib().kvc_decompress_workspace_bytes(n, m * t, d, rd), dev0)
     nbytes = n * out[0].numel() * out[0].element_size()
     if bits > 0:
         nbytes += sum(c.numel() for c in codes) * (t1 - t0) // t

@@ -303,9 +303,11 @@ def test_tensor_core_gram_matches_simt(n_cells, rows, k):
     G = slice(0, 128 * 128)
     Y = slice(128 * 128, 128 * 128 + 128 * k)
     for i in range(n_cells):
-        assert rel(a[i, G], b[i, G]) < 2e-6
+        assert rel(a[i, G], b[i, G]) < 1e-5  # fp32 accumulation order (segment vs 2048-row chunk)
         assert rel(a[i, Y], b[i, Y]) < 5e-5  # Omega carried as bf16 hi + lo
-        assert abs(a[i, -1] / b[i, -1] - 1) < 2e-6
+        # the trace sums the fp32 diagonal; the tensor core accumulates a
+        # segment of up to 4096 rows in fp32 before the fp64 reduction
+        assert abs(a[i, -1] / b[i, -1] - 1) < 2e-5
     # deterministic for a given batch
     np.testing.assert_array_equal(a, ops.gram(cells, om).cpu().numpy())
 
@@ -317,7 +319,7 @@ def test_projection_kernel_matches_oracle(dt, d, rd):
     x_np = oracle.round_to(torch.randn(m, t, d, generator=g).numpy(), dt)
     u_np = oracle.round_to((torch.randn(d, rd, generator=g) / 8).numpy(), dt)
     xp = ops.project_feature([to_cuda(x_np, dt)], [to_cuda(u_np, dt)])[0]
-    ref = oracle.matmul_round(x_np.reshape(-1, d), u_np, dt).reshape(m, t, rd)
+    ref = oracle.jolt.matmul_round(x_np.reshape(-1, d), u_np, dt).reshape(m, t, rd)
     ref_t = np.moveaxis(ref, 1, 0).reshape(t, m * rd)
     got = f32(xp)
     mism = np.mean(got != ref_t)
