@@ -104,6 +104,7 @@ __device__ __forceinline__ void unpack8(const uint4& raw, float (&v)[8]) {
 template <typename T, int D, int NTERM, int MODE, int RDM>
 __global__ void __launch_bounds__(NTHREADS, 1) tc_residual_kernel(TcResArgs A) {
   using L = Layout<D, NTERM, TILE_M * RDM * 4>;
+  static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -495,6 +496,7 @@ template <typename TOut, int D, int RDM, int BITS>
 __global__ void __launch_bounds__(NTHREADS, 1) tc_decompress_kernel(TcDecArgs A) {
   constexpr int CB = D * BITS / 8;  // code bytes per row
   using L = Layout<D, 2, TILE_M * CB>;
+  static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -719,7 +721,7 @@ int set_smem(K kernel, size_t bytes) {
 // ------------------------------- launchers --------------------------------
 
 bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale_mode) {
-  return dtype == KVC_BF16 && (d == 64 || d == 128) && rd <= RD_MAX && proj != nullptr &&
+  return dtype == KVC_BF16 && (d == 64 || d == 128) && rd <= 4 && proj != nullptr &&
          (scale_mode == KVC_SCALE_CHANNEL || scale_mode == KVC_SCALE_TENSOR);
 }
 
@@ -814,8 +816,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
 #define KVC_TC_RES_R(DD, MODEV)                       \
   do {                                                \
     if (rd <= 1) KVC_TC_RES(DD, MODEV, 1);            \
-    else if (rd <= 4) KVC_TC_RES(DD, MODEV, 4);       \
-    else KVC_TC_RES(DD, MODEV, 16);                   \
+    else KVC_TC_RES(DD, MODEV, 4);                    \
   } while (0)
   if (mode == MODE_STATS) {
     if (d == 128) KVC_TC_RES_R(128, MODE_STATS);

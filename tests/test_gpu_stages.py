@@ -252,7 +252,7 @@ def test_tensor_core_residual_matches_simt(d, bits, rank):
 
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("bits", [8, 4, 2])
-@pytest.mark.parametrize("rank", [(1, 1), (7, 4)])
+@pytest.mark.parametrize("rank", [(1, 1), (7, 4), (6, 12)])
 def test_tensor_core_decompress_matches_simt(d, bits, rank):
     from kvcompress_b200.compressor.jl import cached_projection
 
@@ -322,6 +322,9 @@ def test_projection_kernel_matches_oracle(dt, d, rd):
     ref = oracle.jolt.matmul_round(x_np.reshape(-1, d), u_np, dt).reshape(m, t, rd)
     ref_t = np.moveaxis(ref, 1, 0).reshape(t, m * rd)
     got = f32(xp)
-    mism = np.mean(got != ref_t)
-    assert mism < 5e-3, mism  # 1-ulp flips where fp32 summation order meets a rounding tie
+    if dt != "f32":
+        # 16-bit outputs: equal except 1-ulp flips where the fp32 summation
+        # order meets a rounding tie
+        mism = np.mean(got != ref_t)
+        assert mism < 5e-3, mism
     assert rel(got, ref_t) < (1e-6 if dt == "f32" else 1e-2)
