@@ -186,6 +186,33 @@ int kvc_decompress(int n_cells, const uint8_t* const* codes, const float* const*
                    void* const* out, void* workspace, size_t ws_bytes, void* stream);
 
 /*
+ * kvc_decompress without a workspace argument: no counterpart in the
+ * reference.  It is for callers that cannot provide device scratch: a host
+ * runtime binding this ABI directly with no device allocator of its own, or
+ * an engine that forbids device allocation on its decode path.  It runs the
+ * same kernels as kvc_decompress, with scratch in a fixed array of
+ * KVC_NOALLOC_SCRATCH_BYTES per device inside this library, and allocates
+ * nothing.
+ *  - Limit: calls whose kvc_decompress_workspace_bytes(n_cells, m*t, d, rd)
+ *    exceeds KVC_NOALLOC_SCRATCH_BYTES fail with KVC_ERR_WORKSPACE (K and
+ *    V of one Llama-3-8B layer at 8k tokens need about 0.7 MB).
+ *  - The first call on each device looks up the array's address
+ *    (cudaGetSymbolAddress, which may load the module): make it before any
+ *    stream capture.
+ *  - Nothing in the array has to start at zero; each call writes every byte
+ *    it reads.
+ *  - One array per device: calls that overlap on the device (different
+ *    streams or host threads) race on it.  Calls on one stream are safe.
+ */
+#define KVC_NOALLOC_SCRATCH_BYTES (8u << 20)
+int kvc_decompress_noalloc(int n_cells, const uint8_t* const* codes, const float* const* scale,
+                           const int32_t* const* zp, int bits, int symmetric, int scale_mode,
+                           int group_size, const void* const* core, const void* const* u_token,
+                           const void* const* u_feature, int factor_dtype, int64_t m, int64_t t,
+                           int d, int rt, int rd, const float* proj, int64_t t0, int64_t t1,
+                           int out_dtype, void* const* out, void* stream);
+
+/*
  * Kernel selection.  Policy 0 (default): bf16 cells with d in {64, 128},
  * rd <= 16, a JL rotation and channel / tensor scales run on the tcgen05
  * tensor-core kernels (residual encode) and symmetric per-channel 8/4/2-bit

@@ -35,6 +35,8 @@ class KVC:
     SIDE_LEFT, SIDE_RIGHT = 0, 1
     SCALE_CHANNEL, SCALE_GROUP, SCALE_TENSOR = 0, 1, 2
     MAX_CELLS = 64
+    NOALLOC_SCRATCH_BYTES = 8 << 20
+    ERR_WORKSPACE = -5
 
 
 _SIGNATURES = {
@@ -57,6 +59,8 @@ _SIGNATURES = {
     "kvc_decompress_workspace_bytes": (SZ, [I, I64, I, I]),
     "kvc_decompress": (I, [I, PP, PP, PP, I, I, I, I, PP, PP, PP, I, I64, I64, I, I, I, P, I64, I64, I,
                            PP, P, SZ, P]),
+    "kvc_decompress_noalloc": (I, [I, PP, PP, PP, I, I, I, I, PP, PP, PP, I, I64, I64, I, I, I, P, I64,
+                                   I64, I, PP, P]),
     "kvc_set_kernel_policy": (I, [I]),
     "kvc_device_error": (I, [ctypes.POINTER(I)]),
     "kvc_cast": (I, [I64, P, I, P, I, P]),

@@ -21,6 +21,7 @@ __all__ = [
     "cast",
     "core",
     "decompress",
+    "decompress_noalloc",
     "gram",
     "project_feature",
     "residual_quant",
@@ -315,6 +316,38 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
                                    _code(out_dtype), ptr_array(o.data_ptr() for o in out),
                                    ws.data_ptr(), ws.numel(), _stream()),
               "kvc_decompress")
+    return out
+
+
+def decompress_noalloc(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=None, bits: int = 0,
+                       symmetric: bool = True, scale_mode: int = KVC.SCALE_CHANNEL, group_size=None,
+                       factors=None, proj=None, t0: int = 0, t1: int | None = None, out=None):
+    """``decompress`` through ``kvc_decompress_noalloc``: no workspace.
+
+    For callers that must not allocate device scratch: the library decodes
+    in its own fixed per-device array (``KVC.NOALLOC_SCRATCH_BYTES``) and
+    rejects larger decodes.  ``out`` must be given (this function allocates
+    nothing on the device).  Calls that overlap on the device race on that
+    array; calls on one stream are ordered.
+    """
+    if out is None:
+        raise ValueError("decompress_noalloc: pass preallocated `out` tensors")
+    m, t, d = (int(s) for s in shape)
+    t1 = t if t1 is None else int(t1)
+    n = len(out)
+    cp, up, dp, rt, rd = _factor_ptrs(factors, n)
+    fdt = _code(factors[0][0].dtype) if factors is not None else KVC.F16
+    if bits > 0:
+        c_arr = ptr_array(c.data_ptr() for c in codes)
+        s_arr = ptr_array(s.data_ptr() for s in scales)
+        z_arr = ptr_array(z.data_ptr() for z in zps)
+    else:
+        c_arr = s_arr = z_arr = ptr_array([0] * n)
+    check(lib().kvc_decompress_noalloc(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
+                                       int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
+                                       proj.data_ptr() if proj is not None else None, t0, t1,
+                                       _code(out_dtype), ptr_array(o.data_ptr() for o in out), _stream()),
+          "kvc_decompress_noalloc")
     return out
 
 
