@@ -24,7 +24,7 @@ import torch
 from kvcompress_b200 import ops
 from kvcompress_b200.compressor.allocator import AllocationResult, Cell, JointAllocator
 from kvcompress_b200.compressor.base import CompressedPayload, CompressorStats, KVCompressor
-from kvcompress_b200.compressor.cells import CellResult, compress_cells, decompress_cells
+from kvcompress_b200.compressor.cells import CellResult, _batch_of, compress_cells, decompress_cells
 from kvcompress_b200.compressor.svd import SVD
 
 __all__ = ["JoLTCompressor", "JoLTFactors"]
@@ -119,15 +119,17 @@ class JoLTCompressor(KVCompressor):
                 gk = (tuple(x.shape), x.dtype, x.device, a.tuple)
                 groups.setdefault(gk, []).append((li, side))
         results: dict[tuple[int, int], CellResult] = {}
+        order, tails_t, tails_f = [], [], []
         for (shape, _, _, (rt, rd, b)), members in groups.items():
             xs = [pairs[li][side].contiguous() for li, side in members]
             cell_res = self._compress_cells(xs, rt, rd, b, shape[1])
             for (li, side), r in zip(members, cell_res):
                 results[(li, side)] = r
-        # one host sync for every tail mass
-        order = sorted(results)
-        tails = torch.stack([torch.stack([results[k].tail_token, results[k].tail_feature])
-                             for k in order]).cpu().tolist()
+            order += members
+            tails_t.append(_batch_of([r.tail_token for r in cell_res]))
+            tails_f.append(_batch_of([r.tail_feature for r in cell_res]))
+        # one host sync for every tail mass (one small copy per batch)
+        tails = torch.stack([torch.cat(tails_t), torch.cat(tails_f)], dim=1).cpu().tolist()
         tail_of = {k: tv for k, tv in zip(order, tails)}
         out = []
         for li, ((key, value), res) in enumerate(zip(pairs, plans)):

@@ -91,6 +91,60 @@ atb_partial_kernel(CellPtrs A, CellPtrs B1, const float* __restrict__ B2, int64_
     }
 }
 
+// Skinny variant (p + q <= SK_MAXPQ): one block loads a chunk of SK_ROWS
+// rows of A and [B1 | B2] into shared memory with independent loads, then
+// each thread sums one or more outputs over the chunk.  Used for the token
+// Gram (p = m * rd) and the Tucker core (p = rt), whose operands are a few
+// columns wide: the tiled kernel above would serialise its loads there.
+constexpr int SK_ROWS = 256;
+constexpr int SK_MAXPQ = 48;
+
+template <typename TA, typename TB1>
+__global__ void __launch_bounds__(NT)
+atb_skinny_kernel(CellPtrs A, CellPtrs B1, const float* __restrict__ B2, int64_t rows, int p, int q1, int q2,
+                  int chunks, float* __restrict__ partial) {
+  extern __shared__ float sk[];
+  const int cell = blockIdx.y;
+  const int chunk = blockIdx.x;
+  const int q = q1 + q2;
+  float* sA = sk;                  // [SK_ROWS][p]
+  float* sB = sk + SK_ROWS * p;    // [SK_ROWS][q]
+  const int64_t r0 = (int64_t)chunk * SK_ROWS;
+  const int nr = (int)(rows - r0 < SK_ROWS ? rows - r0 : SK_ROWS);
+  const TA* __restrict__ a = static_cast<const TA*>(A.p[cell]) + r0 * p;
+  const TB1* __restrict__ b1 = static_cast<const TB1*>(B1.p[cell]) + r0 * q1;
+  const float* __restrict__ b2 = B2 ? B2 + r0 * q2 : nullptr;
+  const int na = nr * p;
+#pragma unroll 4
+  for (int e = threadIdx.x; e < SK_ROWS * p; e += NT) sA[e] = e < na ? Elt<TA>::to_f32(a[e]) : 0.f;
+  const int nb1 = nr * q1;
+#pragma unroll 4
+  for (int e = threadIdx.x; e < SK_ROWS * q1; e += NT) {
+    const int r = e / q1, j = e % q1;
+    sB[r * q + j] = e < nb1 ? Elt<TB1>::to_f32(b1[e]) : 0.f;
+  }
+  if (q2 > 0) {
+    const int nb2 = nr * q2;
+#pragma unroll 4
+    for (int e = threadIdx.x; e < SK_ROWS * q2; e += NT) {
+      const int r = e / q2, j = e % q2;
+      sB[r * q + q1 + j] = e < nb2 ? b2[e] : 0.f;
+    }
+  }
+  __syncthreads();
+  float* out = partial + ((int64_t)cell * chunks + chunk) * (int64_t)p * q;
+  for (int o = threadIdx.x; o < p * q; o += NT) {
+    const int i = o / q, j = o % q;
+    float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll 4
+    for (int r = 0; r < SK_ROWS; r += 2) {
+      acc0 = fmaf(sA[r * p + i], sB[r * q + j], acc0);
+      acc1 = fmaf(sA[(r + 1) * p + i], sB[(r + 1) * q + j], acc1);
+    }
+    out[o] = acc0 + acc1;
+  }
+}
+
 // Sum partials over chunks (fixed order, fp64) into the Gram layout
 // [A^T B1 (p x q1) | A^T B2 (p x q2) | trace] at `stride` doubles per cell.
 __global__ void gram_reduce_kernel(const float* __restrict__ partial, int n_cells, int chunks, int p,
@@ -144,6 +198,7 @@ struct ChunkPlan {
   int chunks;
   int64_t chunk_rows;
   int tiles;
+  bool skinny;
 };
 
 // The chunking depends on the row count only (never on the batch size or
@@ -152,6 +207,13 @@ struct ChunkPlan {
 ChunkPlan plan_chunks(int n_cells, int64_t rows, int p, int q) {
   (void)n_cells;
   ChunkPlan pl;
+  pl.skinny = p + q <= SK_MAXPQ;
+  if (pl.skinny) {
+    pl.tiles = 1;
+    pl.chunk_rows = SK_ROWS;
+    pl.chunks = (int)std::max<int64_t>(1, ceil_div(rows, SK_ROWS));
+    return pl;
+  }
   pl.tiles = (int)(ceil_div(p, TB) * ceil_div(q, TB));
   int64_t cr = std::max<int64_t>(2048, ceil_div(rows, 128));
   cr = ceil_div(cr, RB) * RB;
@@ -163,6 +225,12 @@ ChunkPlan plan_chunks(int n_cells, int64_t rows, int p, int q) {
 template <typename TA, typename TB1>
 int launch_partial(int n_cells, const CellPtrs& a, const CellPtrs& b1, const float* b2, int64_t rows,
                    int p, int q1, int q2, const ChunkPlan& pl, float* partial, cudaStream_t st) {
+  if (pl.skinny) {
+    const size_t smem = (size_t)SK_ROWS * (p + q1 + q2) * sizeof(float);
+    atb_skinny_kernel<TA, TB1><<<dim3(pl.chunks, n_cells), NT, smem, st>>>(a, b1, b2, rows, p, q1, q2, pl.chunks,
+                                                                           partial);
+    return check_launch("atb_skinny_kernel");
+  }
   dim3 grid(pl.chunks, pl.tiles, n_cells);
   atb_partial_kernel<TA, TB1><<<grid, NT, 0, st>>>(a, b1, b2, rows, p, q1, q2, pl.chunks,
                                                    pl.chunk_rows, partial);

@@ -36,6 +36,7 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
                          int64_t t0, int64_t t1, void* const* out, void* workspace, size_t ws_bytes,
                          cudaStream_t st);
 int tc_read_device_error(int* out);
+int tc_gram_read_device_error(int* out);
 
 static int g_policy = 0;  // 0: tensor cores when eligible, 1: SIMT kernels only
 int kernel_policy() { return g_policy; }
@@ -495,7 +496,12 @@ extern "C" int kvc_set_kernel_policy(int policy) {
 
 extern "C" int kvc_device_error(int* code) {
   if (!code) return fail(KVC_ERR_ARG, "kvc_device_error: NULL");
-  return tc_read_device_error(code);
+  int a = 0, b = 0;
+  int rc = tc_read_device_error(&a);
+  if (rc) return rc;
+  if ((rc = tc_gram_read_device_error(&b))) return rc;
+  *code = a ? a : b;
+  return KVC_OK;
 }
 
 extern "C" int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, int64_t t, int d,

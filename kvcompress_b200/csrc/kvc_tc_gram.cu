@@ -4,8 +4,8 @@
 // the quantities the reference's randomised SVD extracts with five passes
 // over the unfolding (kvcompress/compressor/svd.py:259-265, 289).
 //
-// Operands: an x tile of 128 rows staged by cp.async in the SWIZZLE_128B
-// layout is at the same time the MN-major A operand (x^T: M = feature,
+// Operands: an x tile of 128 rows loaded by TMA in the SWIZZLE_128B layout
+// (two 64-column boxes) is at the same time the MN-major A operand (x^T: M = feature,
 // K = row) and the MN-major B operand (x: N = feature); products of bf16
 // values are exact and accumulate in fp32 in TMEM.  Omega (fp32) is split
 // once by a small kernel into bf16 hi / lo (columns 0..31 / 32..63 of a
@@ -18,12 +18,14 @@
 // kernel sums the segments of each cell in order in fp64.  The result of a
 // cell is therefore bit-identical however many cells share the launch.
 //
-// Warps 0-3 produce (cp.async, 4 stages), warp 4 issues tcgen05.mma,
-// warps 5-8 drain accumulators.  Every mbarrier wait is bounded.
+// Warp 0 loads tiles by TMA (4 stages, rows past the end of a cell read as
+// zeros), warp 1 issues tcgen05.mma, warps 2-5 drain accumulators.  Every
+// mbarrier wait is bounded.
 #include <algorithm>
 
 #include "kvc_common.cuh"
 #include "kvc_tc.cuh"
+#include "kvc_tma.cuh"
 
 namespace kvc {
 namespace {
@@ -35,7 +37,10 @@ constexpr int TILE = 128;     // rows per tile (the MMA K extent of 8 K-steps)
 constexpr int NY = 64;        // Omega columns (hi 0..31, lo 32..63)
 constexpr int NACC = D + NY;  // accumulator columns: [G | Y]
 constexpr int NS = 4;         // pipeline stages
-constexpr int NTH = 288;
+constexpr int NTH = 192;      // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
+constexpr int TMA_WARP = 0;
+constexpr int MMA_WARP = 1;
+constexpr int EPI_WARP0 = 2;
 
 struct GLayout {
   static constexpr uint32_t X_BYTES = TILE * D * 2;   // 32 KB
@@ -47,8 +52,6 @@ struct GLayout {
 };
 
 struct GramArgs {
-  CellPtrs x;
-  const uint8_t* omega_pad;  // rows x 64 bf16: Omega hi in columns 0..31, lo in 32..63
   int k;
   int64_t rows, tiles_per_cell;
   int64_t seg_tiles, segs_per_cell, total_segs;
@@ -98,7 +101,9 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) 
   return d;
 }
 
-__global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
+__global__ void __launch_bounds__(NTH, 1)
+    tc_gram_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ CUtensorMap omap,
+                   const __grid_constant__ GramArgs A) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -115,8 +120,8 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&full[i], 128);
-      mbar_init(&empty[i], 1);
+      mbar_init(&full[i], 1);   // TMA issue + transaction bytes
+      mbar_init(&empty[i], 1);  // tcgen05.commit
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);
@@ -124,7 +129,7 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
     }
     mbar_fence_init();
   }
-  if (warp == 4) {
+  if (warp == MMA_WARP) {
     tmem_alloc(tm_holder, 512);
     tmem_relinquish();
   }
@@ -133,57 +138,24 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
   tc_fence_after();
   const uint32_t tmem = *tm_holder;
 
-  if (warp < 4) {
-    // ---------------- producers: one row of x and of Omega per thread ----------------
-    const int ptid = threadIdx.x;
-    bool ok = true;
-    SegCursor ic{s_begin, 0}, pc{s_begin, 0};  // issue / processing positions
-    auto issue = [&](int j) {
-      const int cell = ic.cell(A);
-      const int64_t row = ic.tile(A) * TILE + ptid;
-      ic.next(A);
-      const int st = j % NS;
-      if (!mbar_wait(&empty[st], (uint32_t)((j / NS) & 1) ^ 1u, 0x401)) return false;
-      if (row < A.rows) {
+  if (warp == TMA_WARP) {
+    // ---------------- TMA producer: x tile (two 64-column boxes) + Omega tile ----------------
+    if (lane == 0) {
+      SegCursor ic{s_begin, 0};
+      for (int j = 0; j < n_my; ++j, ic.next(A)) {
+        const int cell = ic.cell(A);
+        const int y = (int)(ic.tile(A) * TILE);
+        const int st = j % NS;
+        if (!mbar_wait(&empty[st], (uint32_t)((j / NS) & 1) ^ 1u, 0x401)) break;
+        mbar_expect_tx(&full[st], GLayout::STAGE);
         const uint32_t xs = sbase + st * GLayout::STAGE;
-        const uint32_t os = xs + GLayout::X_BYTES;
-        const __nv_bfloat16* x = static_cast<const __nv_bfloat16*>(A.x.p[cell]) + row * D;
-        const uint8_t* om = A.omega_pad + row * (NY * 2);
-#pragma unroll
-        for (int c = 0; c < D / 8; ++c) cp_async16(xs + sw128_off(ptid, c * 8, TILE), x + c * 8);
-#pragma unroll
-        for (int c = 0; c < NY / 8; ++c) cp_async16(os + sw128_off(ptid, c * 8, TILE), om + c * 16);
+        tma_load_2d(xs, &xmaps.m[cell], 0, y, &full[st]);
+        tma_load_2d(xs + TILE * 128, &xmaps.m[cell], 64, y, &full[st]);
+        tma_load_2d(xs + GLayout::X_BYTES, &omap, 0, y, &full[st]);
       }
-      return true;
-    };
-    for (int j = 0; j < NS - 1; ++j) {
-      if (ok && j < n_my) ok = issue(j);
-      cp_async_commit();
     }
-    for (int it = 0; it < n_my; ++it) {
-      const int jn = it + NS - 1;
-      if (ok && jn < n_my) ok = issue(jn);
-      cp_async_commit();
-      cp_async_wait<NS - 1>();
-      if (!ok) continue;
-      const int st = it % NS;
-      const int64_t row = pc.tile(A) * TILE + ptid;
-      pc.next(A);
-      if (row >= A.rows) {  // rows past the end of the cell contribute zeros
-        uint8_t* xs = smem + st * GLayout::STAGE;
-        uint8_t* os = xs + GLayout::X_BYTES;
-#pragma unroll
-        for (int c = 0; c < D / 8; ++c)
-          *reinterpret_cast<uint4*>(xs + sw128_off(ptid, c * 8, TILE)) = make_uint4(0, 0, 0, 0);
-#pragma unroll
-        for (int c = 0; c < NY / 8; ++c)
-          *reinterpret_cast<uint4*>(os + sw128_off(ptid, c * 8, TILE)) = make_uint4(0, 0, 0, 0);
-      }
-      fence_async_smem();
-      mbar_arrive(&full[st]);
-    }
-    cp_async_wait<0>();
-  } else if (warp == 4) {
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
       // A = x^T and B = x, both MN-major; D[feature][feature / omega column]
@@ -221,31 +193,29 @@ __global__ void __launch_bounds__(NTH, 1) tc_gram_kernel(GramArgs A) {
       if (seg >= 0) mbar_wait(&accf[seg & 1], (uint32_t)((seg >> 1) & 1), 0x404);
     }
     __syncwarp();
-  } else {
+  } else if (warp >= EPI_WARP0) {
     // ---------------- epilogue: flush one segment's accumulator ----------------
     const int lg = warp & 3;
     const int feat = lg * 32 + lane;
     for (int seg = 0; seg < (int)(s_end - s_begin); ++seg) {
-      {
-        if (!mbar_wait(&accf[seg & 1], (uint32_t)((seg >> 1) & 1), 0x405)) break;
-        tc_fence_after();
-        float* dst = A.partial + ((s_begin + seg) * D + feat) * NACC;
+      if (!__all_sync(0xffffffffu, mbar_wait(&accf[seg & 1], (uint32_t)((seg >> 1) & 1), 0x405))) break;
+      tc_fence_after();
+      float* dst = A.partial + ((s_begin + seg) * D + feat) * NACC;
 #pragma unroll
-        for (int c = 0; c < NACC / 32; ++c) {
-          float v[32];
-          tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)((seg & 1) * 256 + c * 32), v);
+      for (int c = 0; c < NACC / 32; ++c) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)((seg & 1) * 256 + c * 32), v);
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            reinterpret_cast<float4*>(dst + c * 32)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
-        }
-        tc_fence_before();
-        mbar_arrive(&acce[seg & 1]);
+        for (int q = 0; q < 8; ++q)
+          reinterpret_cast<float4*>(dst + c * 32)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
       }
+      tc_fence_before();
+      mbar_arrive(&acce[seg & 1]);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == MMA_WARP) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
@@ -326,11 +296,29 @@ int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float*
   GPlan p = gplan(n_cells, rows);
   if (!workspace || ws_bytes < partial_bytes(n_cells, p) + (size_t)rows * NY * 2)
     return fail(KVC_ERR_WORKSPACE, "tensor-core gram: workspace too small");
+  if (rows >= (1LL << 31)) return fail(KVC_ERR_SHAPE, "tensor-core gram: more than 2^31 rows per cell");
   GramArgs g;
   memset(&g, 0, sizeof(g));
-  for (int c = 0; c < n_cells; ++c) g.x.p[c] = a[c];
+  TmaMaps xmaps;
+  CUtensorMap omap;
+  int rc1;
+  for (int c = 0; c < n_cells; ++c) {
+    const uint64_t dims[2] = {(uint64_t)D, (uint64_t)rows};
+    const uint64_t strides[1] = {(uint64_t)D * 2};
+    const uint32_t box[2] = {64u, (uint32_t)TILE};
+    if ((rc1 = encode_tma(&xmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, a[c], dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc1;
+  }
   uint8_t* opad = static_cast<uint8_t*>(workspace) + partial_bytes(n_cells, p);
-  g.omega_pad = opad;
+  {
+    const uint64_t dims[2] = {(uint64_t)NY, (uint64_t)rows};
+    const uint64_t strides[1] = {(uint64_t)NY * 2};
+    const uint32_t box[2] = {(uint32_t)NY, (uint32_t)TILE};
+    if ((rc1 = encode_tma(&omap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, opad, dims, strides, box,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc1;
+  }
   g.k = k;
   {
     const int blocks = (int)std::min<int64_t>(ceil_div(rows * 32, 256), 16LL * num_sms());
@@ -347,7 +335,7 @@ int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float*
   cudaError_t e = cudaFuncSetAttribute(tc_gram_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        (int)GLayout::BYTES);
   if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-  tc_gram_kernel<<<p.ctas, NTH, GLayout::BYTES, st>>>(g);
+  tc_gram_kernel<<<p.ctas, NTH, GLayout::BYTES, st>>>(xmaps, omap, g);
   int rc = check_launch("tc_gram_kernel");
   if (rc) return rc;
   const int64_t stride = (int64_t)D * D + (int64_t)D * k + 1;
@@ -355,6 +343,16 @@ int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float*
   const int blocks = (int)std::min<int64_t>(ceil_div(total, 256), 8 * num_sms());
   tc_gram_reduce_kernel<<<blocks, 256, 0, st>>>(g.partial, n_cells, p.segs_per_cell, k, out, stride);
   return check_launch("tc_gram_reduce_kernel");
+}
+
+int tc_gram_read_device_error(int* out) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, tc::g_kvc_device_error, sizeof(int));
+  if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("device error read: ") + cudaGetErrorString(e));
+  *out = v;
+  int zero = 0;
+  cudaMemcpyToSymbol(tc::g_kvc_device_error, &zero, sizeof(int));
+  return KVC_OK;
 }
 
 }  // namespace kvc

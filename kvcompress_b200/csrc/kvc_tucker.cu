@@ -196,12 +196,18 @@ extern "C" int kvc_project_feature(int n_cells, const void* const* x, int64_t m,
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, per_block),
                                                                     ceil_div(8LL * num_sms(), n_cells)));
     dim3 grid(blocks, n_cells);
-#define KVC_PROJ(L)                                                                                   \
-  KVC_DISPATCH_DTYPE(dtype, T, project_small_kernel<T, 4, L><<<grid, 256, 0, st>>>(xa, ub, rows, d, rd, t, \
+#define KVC_PROJ(R, L)                                                                                \
+  KVC_DISPATCH_DTYPE(dtype, T, project_small_kernel<T, R, L><<<grid, 256, 0, st>>>(xa, ub, rows, d, rd, t, \
                                                                                    (int)m, o))
-    if (lpr == 8) KVC_PROJ(8);
-    else if (lpr == 16) KVC_PROJ(16);
-    else KVC_PROJ(32);
+    if (rd == 1) {
+      if (lpr == 8) KVC_PROJ(1, 8);
+      else if (lpr == 16) KVC_PROJ(1, 16);
+      else KVC_PROJ(1, 32);
+    } else {
+      if (lpr == 8) KVC_PROJ(4, 8);
+      else if (lpr == 16) KVC_PROJ(4, 16);
+      else KVC_PROJ(4, 32);
+    }
 #undef KVC_PROJ
     return check_launch("project_small_kernel");
   }
