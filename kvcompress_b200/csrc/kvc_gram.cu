@@ -165,13 +165,18 @@ __global__ void gram_reduce_kernel(const float* __restrict__ partial, int n_cell
   }
 }
 
+// trace of each cell's Gram, one warp per cell (fixed order: lane partial
+// sums over i = lane + 32 j, then a butterfly)
 __global__ void gram_trace_kernel(double* out, int n_cells, int p, int q2, int64_t stride) {
-  const int cell = blockIdx.x * blockDim.x + threadIdx.x;
+  const int cell = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
   if (cell >= n_cells) return;
   double* o = out + cell * stride;
   double s = 0.0;
-  for (int i = 0; i < p; ++i) s += o[(int64_t)i * p + i];
-  o[(int64_t)p * p + (int64_t)p * q2] = s;
+  for (int i = lane; i < p; i += 32) s += o[(int64_t)i * p + i];
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) o[(int64_t)p * p + (int64_t)p * q2] = s;
 }
 
 // core[h, a, r] = C[a, h*rd + r] with C = u_token^T x_proj_t (rt x m*rd).
@@ -273,7 +278,7 @@ extern "C" int kvc_gram(int n_cells, const void* const* a, int64_t rows, int p, 
   if (kernel_policy() == 0 && k > 0 && aligned && tc_gram_eligible(dtype, p, k) &&
       ws_bytes >= tc_gram_workspace(n_cells, rows)) {
     if ((rc = tc_gram_launch(n_cells, a, rows, omega, k, out, workspace, ws_bytes, st))) return rc;
-    gram_trace_kernel<<<(n_cells + 63) / 64, 64, 0, st>>>(out, n_cells, p, k, stride);
+    gram_trace_kernel<<<(n_cells + 3) / 4, 128, 0, st>>>(out, n_cells, p, k, stride);
     return check_launch("gram_trace_kernel");
   }
   float* partial = static_cast<float*>(workspace);
@@ -284,7 +289,7 @@ extern "C" int kvc_gram(int n_cells, const void* const* a, int64_t rows, int p, 
   const int blocks = (int)std::min<int64_t>(ceil_div(total, 256), 8 * num_sms());
   gram_reduce_kernel<<<blocks, 256, 0, st>>>(partial, n_cells, pl.chunks, p, p, k, out, stride);
   if ((rc = check_launch("gram_reduce_kernel"))) return rc;
-  gram_trace_kernel<<<(n_cells + 63) / 64, 64, 0, st>>>(out, n_cells, p, k, stride);
+  gram_trace_kernel<<<(n_cells + 3) / 4, 128, 0, st>>>(out, n_cells, p, k, stride);
   return check_launch("gram_trace_kernel");
 }
 

@@ -131,6 +131,10 @@ __device__ void blk_jacobi(double* A, double* V, int n, double* evals) {
     off = blk_sum(off);
     tot = blk_sum(tot);
     if (!(off > 1e-30 * tot)) break;
+    const double thr = 1e-15 * sqrt(tot);  // couplings at the rounding level of ||A||_F are done
+    __shared__ int any_rot;
+    if (threadIdx.x == 0) any_rot = 0;
+    __syncthreads();
     for (int round = 0; round < N - 1; ++round) {
       for (int pr = threadIdx.x; pr < H; pr += blockDim.x) {
         int p = pos[pr], q = pos[N - 1 - pr];
@@ -142,7 +146,8 @@ __device__ void blk_jacobi(double* A, double* V, int n, double* evals) {
         double c = 1.0, s = 0.0;
         if (q < n) {
           const double apq = A[(int64_t)p * n + q];
-          if (apq != 0.0) {
+          if (fabs(apq) > thr) {
+            any_rot = 1;
             const double app = A[(int64_t)p * n + p], aqq = A[(int64_t)q * n + q];
             const double tau = (aqq - app) / (2.0 * apq);
             const double t = (tau >= 0.0 ? 1.0 : -1.0) / (fabs(tau) + sqrt(1.0 + tau * tau));
@@ -191,6 +196,8 @@ __device__ void blk_jacobi(double* A, double* V, int n, double* evals) {
       }
       __syncthreads();
     }
+    if (!any_rot) break;  // a sweep without a rotation: converged
+    __syncthreads();
   }
   for (int i = threadIdx.x; i < n; i += blockDim.x) evals[i] = A[(int64_t)i * n + i];
   __syncthreads();
@@ -325,6 +332,349 @@ __global__ void __launch_bounds__(SNT) sketch_solve_kernel(SolveArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Shared-memory solver for the common randomised case (p <= 128, k <= 32).
+// Same algorithm and outputs as sketch_solve_kernel above, laid out for
+// latency: every operand lives in shared memory and every step is a short
+// block-wide phase (the Cholesky's trailing updates, the inverse of R by
+// parallel back-substitution, Q = Y R^{-1} as a product, one phase of 2 x 2
+// block updates per Jacobi round), so no single warp runs a long chain of
+// dependent fp64 operations.  Square roots and reciprocals take an fp32
+// hardware estimate refined by two Newton-Raphson steps in fp64.
+// ---------------------------------------------------------------------------
+constexpr int SM_P = 128;
+constexpr int SM_K = 32;
+constexpr int SM_QS = SM_K + 1;  // row stride (doubles) of Q and Z
+constexpr int SM_NT = 256;
+
+size_t small_smem_bytes(int p) {
+  return sizeof(double) * ((size_t)p * p + 2 * (size_t)p * SM_QS + 3 * SM_K * SM_K + 4 * SM_K + 64) +
+         sizeof(int) * (4 * SM_K + 64);
+}
+
+// 1/sqrt(x) and 1/x for normal positive / nonzero x: fp32 estimate, then two
+// Newton-Raphson steps y <- y (3 - x y^2) / 2 and y <- y (2 - x y) (each step
+// doubles the correct bits: ~22 -> 44 -> 88).
+__device__ __forceinline__ double rsqrt_nr(double x) {
+  double y = (double)rsqrtf((float)x);
+  y = y * fma(-0.5 * x, y * y, 1.5);
+  y = y * fma(-0.5 * x, y * y, 1.5);
+  return y;
+}
+__device__ __forceinline__ double rcp_nr(double x) {
+  double y = (double)(1.0f / (float)x);
+  y = y * fma(-x, y, 2.0);
+  y = y * fma(-x, y, 2.0);
+  return y;
+}
+// the fp32 estimate needs x inside the fp32 normal range
+__device__ __forceinline__ bool f32_range(double x) { return fabs(x) > 1e-36 && fabs(x) < 1e36; }
+__device__ __forceinline__ double rsqrt_any(double x) { return f32_range(x) ? rsqrt_nr(x) : 1.0 / sqrt(x); }
+__device__ __forceinline__ double rcp_any(double x) { return f32_range(x) ? rcp_nr(x) : 1.0 / x; }
+
+// Z (p x k) = G Q, G symmetric p x p.  Thread: one row, 8 columns.
+__device__ void sm_gemm(double* Z, const double* G, const double* Q, int p, int k) {
+  const int groups = (k + 7) / 8;
+  for (int task = threadIdx.x; task < p * groups; task += blockDim.x) {
+    const int i = task % p, jg = task / p;
+    double acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = 0.0;
+    for (int kk = 0; kk < p; ++kk) {
+      const double g = G[kk * p + i];
+      const double* q = Q + kk * SM_QS + jg * 8;
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[c] = fma(g, q[c], acc[c]);
+    }
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      if (jg * 8 + c < k) Z[i * SM_QS + jg * 8 + c] = acc[c];
+  }
+  __syncthreads();
+}
+
+// S (k x k, stride SM_K) = A^T B over p rows; one output per thread, rows in
+// a fixed order (two partial sums).
+__device__ void sm_colgram(double* S, const double* A, const double* B, int p, int k) {
+  for (int o = threadIdx.x; o < k * k; o += blockDim.x) {
+    const int i = o / k, j = o % k;
+    double s0 = 0.0, s1 = 0.0;
+    int r = 0;
+    for (; r + 1 < p; r += 2) {
+      s0 = fma(A[r * SM_QS + i], B[r * SM_QS + j], s0);
+      s1 = fma(A[(r + 1) * SM_QS + i], B[(r + 1) * SM_QS + j], s1);
+    }
+    if (r < p) s0 = fma(A[r * SM_QS + i], B[r * SM_QS + j], s0);
+    S[i * SM_K + j] = s0 + s1;
+  }
+  __syncthreads();
+}
+
+// Cholesky with rank dropping of S (k x k, upper triangle -> R): a column
+// whose pivot falls below 1e-10 of its original diagonal is zero.  Then
+// X = R^{-1} (upper triangular, zero rows and columns where R was dropped).
+__device__ void sm_chol_inv(double* S, double* X, double* diag0, int k) {
+  for (int i = threadIdx.x; i < k; i += blockDim.x) diag0[i] = S[i * SM_K + i];
+  __syncthreads();
+  for (int j = 0; j < k; ++j) {
+    const double d = S[j * SM_K + j], oj = diag0[j];
+    const bool keep = oj > 0.0 && d > 1e-10 * oj;
+    const double rs = keep ? rsqrt_any(d) : 0.0;  // 1 / R[j][j]
+    __syncthreads();  // everyone has read S[j][j]
+    for (int l = j + threadIdx.x; l < k; l += blockDim.x) S[j * SM_K + l] = l == j ? (keep ? d * rs : 0.0) : S[j * SM_K + l] * rs;
+    __syncthreads();
+    // trailing update S[i][l] -= R[j][i] R[j][l], j < i <= l < k
+    const int m = k - 1 - j;
+    for (int t = threadIdx.x; t < m * m; t += blockDim.x) {
+      const int i = j + 1 + t / m, l = j + 1 + t % m;
+      if (l >= i) S[i * SM_K + l] = fma(-S[j * SM_K + i], S[j * SM_K + l], S[i * SM_K + l]);
+    }
+    __syncthreads();
+  }
+  // X = R^{-1}: column c by back-substitution (columns in parallel)
+  for (int c = threadIdx.x; c < k; c += blockDim.x) {
+    for (int i = k - 1; i >= 0; --i) {
+      double v = 0.0;
+      if (i <= c) {
+        v = i == c ? 1.0 : 0.0;
+        for (int jj = i + 1; jj <= c; ++jj) v = fma(-S[i * SM_K + jj], X[jj * SM_K + c], v);
+        const double rii = S[i * SM_K + i];
+        v = rii > 0.0 ? v * rcp_any(rii) : 0.0;
+      }
+      X[i * SM_K + c] = v;
+    }
+  }
+  __syncthreads();
+}
+
+// Q (p x k) = Y X, X upper triangular; Y is left untouched
+__device__ void sm_apply_rinv(double* Q, const double* Y, const double* X, int p, int k) {
+  for (int o = threadIdx.x; o < p * k; o += blockDim.x) {
+    const int r = o / k, c = o % k;
+    double v = 0.0;
+    for (int j = 0; j <= c; ++j) v = fma(Y[r * SM_QS + j], X[j * SM_K + c], v);
+    Q[r * SM_QS + c] = v;
+  }
+  __syncthreads();
+}
+
+// One CholeskyQR pass in the inner product of Mtx (identity when NULL):
+// Q <- orth(Y); Y's storage becomes scratch.  Returns the new Q.
+__device__ double* sm_cholqr(double* Y, double* Z, double* S, double* X, double* diag0, const double* Mtx, int p,
+                             int k) {
+  if (Mtx) {
+    sm_gemm(Z, Mtx, Y, p, k);
+    sm_colgram(S, Y, Z, p, k);
+  } else {
+    sm_colgram(S, Y, Y, p, k);
+  }
+  sm_chol_inv(S, X, diag0, k);
+  sm_apply_rinv(Z, Y, X, p, k);
+  return Z;
+}
+
+// Cyclic two-sided Jacobi on A (n x n, stride SM_K); V gets the eigenvectors
+// in columns, ev the eigenvalues (unsorted).  Round-robin pairs: position 0
+// fixed, positions 1..N-1 rotated by the round index.  One phase per round
+// updates every 2 x 2 block A[{p1,q1}][{p2,q2}] <- J1^T A J2 and the pairs of
+// columns of V.
+__device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, int* pq, double* red) {
+  const int N = n + (n & 1), H = N / 2;
+  for (int idx = threadIdx.x; idx < n * SM_K; idx += blockDim.x) V[idx] = (idx / SM_K == idx % SM_K) ? 1.0 : 0.0;
+  __shared__ int any_rot;
+  for (int sweep = 0; sweep < MAX_SWEEPS && n > 1; ++sweep) {
+    // ||A||_F^2 and the off-diagonal part (one warp)
+    if (threadIdx.x < 32) {
+      double off = 0.0, tot = 0.0;
+      for (int idx = threadIdx.x; idx < n * n; idx += 32) {
+        const double a = A[(idx / n) * SM_K + idx % n];
+        tot += a * a;
+        if (idx / n != idx % n) off += a * a;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+        off += __shfl_xor_sync(0xffffffffu, off, o);
+        tot += __shfl_xor_sync(0xffffffffu, tot, o);
+      }
+      if (threadIdx.x == 0) {
+        red[0] = off;
+        red[1] = tot;
+        any_rot = 0;
+      }
+    }
+    __syncthreads();
+    const double off = red[0], tot = red[1];
+    if (!(off > 1e-30 * tot)) break;
+    // off-diagonal entries at the rounding level of ||A||_F can never be
+    // removed (a rotation leaves eps ||A|| behind), so they end the sweeps
+    const double thr = 1e-15 * sqrt(tot);
+    for (int round = 0; round < N - 1; ++round) {
+      if (threadIdx.x < H) {
+        const int lane = threadIdx.x;
+        const int i1 = lane, i2 = N - 1 - lane;
+        int pp = i1 == 0 ? 0 : 1 + (i1 - 1 - round + 2 * (N - 1)) % (N - 1);
+        int qq = 1 + (i2 - 1 - round + 2 * (N - 1)) % (N - 1);
+        if (pp > qq) {
+          const int tmp = pp;
+          pp = qq;
+          qq = tmp;
+        }
+        double c = 1.0, sn = 0.0;
+        if (qq < n) {
+          const double apq = A[pp * SM_K + qq];
+          const double app = A[pp * SM_K + pp], aqq = A[qq * SM_K + qq];
+          if (fabs(apq) > thr && fabs(apq) > 1e-16 * sqrt(fabs(app * aqq))) {
+            // t = sgn(tau) / (|tau| + sqrt(1 + tau^2)), tau = (aqq - app) / (2 apq)
+            const double h = aqq - app, g = 2.0 * apq;
+            const double z = fma(h, h, g * g);
+            const double t = (h >= 0.0 ? g : -g) * rcp_any(fabs(h) + z * rsqrt_any(z));
+            c = rsqrt_any(fma(t, t, 1.0));
+            sn = t * c;
+            any_rot = 1;
+          }
+        }
+        pq[2 * lane] = pp;
+        pq[2 * lane + 1] = qq < n ? qq : -1;
+        rot[2 * lane] = c;
+        rot[2 * lane + 1] = sn;
+      }
+      __syncthreads();
+      // A: 2 x 2 blocks (pair b1 rows, pair b2 columns); V: row i, pair b
+      const int nb = H * H;
+      for (int t = threadIdx.x; t < nb + n * H; t += blockDim.x) {
+        if (t < nb) {
+          const int b1 = t / H, b2 = t % H;
+          const int p1 = pq[2 * b1], q1 = pq[2 * b1 + 1], p2 = pq[2 * b2], q2 = pq[2 * b2 + 1];
+          const double c1 = rot[2 * b1], s1 = q1 < 0 ? 0.0 : rot[2 * b1 + 1];
+          const double c2 = rot[2 * b2], s2 = q2 < 0 ? 0.0 : rot[2 * b2 + 1];
+          if (s1 == 0.0 && s2 == 0.0) continue;
+          // rows {p1, q1} x columns {p2, q2}; a missing q is a dummy index
+          const double a = A[p1 * SM_K + p2];
+          const double b = q2 >= 0 ? A[p1 * SM_K + q2] : 0.0;
+          const double cq = q1 >= 0 ? A[q1 * SM_K + p2] : 0.0;
+          const double dq = (q1 >= 0 && q2 >= 0) ? A[q1 * SM_K + q2] : 0.0;
+          // rows: [a b; cq dq] <- J1^T [...] with (row p) c a - s cq, (row q) s a + c cq
+          const double r0 = c1 * a - s1 * cq, r1 = c1 * b - s1 * dq;
+          const double r2 = s1 * a + c1 * cq, r3 = s1 * b + c1 * dq;
+          // columns: (col p) c x - s y, (col q) s x + c y
+          A[p1 * SM_K + p2] = c2 * r0 - s2 * r1;
+          if (q2 >= 0) A[p1 * SM_K + q2] = s2 * r0 + c2 * r1;
+          if (q1 >= 0) {
+            A[q1 * SM_K + p2] = c2 * r2 - s2 * r3;
+            if (q2 >= 0) A[q1 * SM_K + q2] = s2 * r2 + c2 * r3;
+          }
+        } else {
+          const int u = t - nb, i = u / H, b = u % H;
+          const int p_ = pq[2 * b], q = pq[2 * b + 1];
+          if (q < 0) continue;
+          const double cc = rot[2 * b], ss = rot[2 * b + 1];
+          if (ss == 0.0) continue;
+          const double x = V[i * SM_K + p_], y = V[i * SM_K + q];
+          V[i * SM_K + p_] = cc * x - ss * y;
+          V[i * SM_K + q] = ss * x + cc * y;
+        }
+      }
+      __syncthreads();
+    }
+    const int rotated = any_rot;
+    __syncthreads();  // every thread has read the flag before the next sweep resets it
+    if (!rotated) break;  // a sweep without a rotation: converged
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) ev[i] = A[i * SM_K + i];
+  __syncthreads();
+}
+
+__global__ void __launch_bounds__(SM_NT) sketch_solve_small_kernel(SolveArgs a) {
+  extern __shared__ double sm[];
+  const int cell = blockIdx.x;
+  const int p = a.p, k = a.k, rank = a.rank;
+  const double* gram = a.gram + cell * a.gram_stride;
+  double* G = sm;                       // p x p
+  double* Q = G + p * p;                // p x SM_QS
+  double* Z = Q + p * SM_QS;            // p x SM_QS
+  double* S = Z + p * SM_QS;            // SM_K x SM_K
+  double* C = S + SM_K * SM_K;
+  double* V = C + SM_K * SM_K;
+  double* X = C;                        // R^{-1} of the CholeskyQR passes (C is set after them)
+  double* ev = V + SM_K * SM_K;         // SM_K
+  double* rot = ev + SM_K;              // 2 SM_K
+  double* diag0 = rot + 2 * SM_K;       // SM_K
+  double* red = diag0 + SM_K;           // 64 (reduction scratch)
+  int* order = reinterpret_cast<int*>(red + 64);
+  int* pq = order + SM_K;               // 2 SM_K
+  __shared__ double nrm_s;
+  for (int i = threadIdx.x; i < p * p; i += blockDim.x) G[i] = gram[i];
+  if (a.side == KVC_SIDE_LEFT) {
+    const double* y0 = gram + (int64_t)p * p;
+    for (int i = threadIdx.x; i < p * k; i += blockDim.x) Q[(i / k) * SM_QS + i % k] = y0[i];
+    if (threadIdx.x == 0) nrm_s = gram[(int64_t)p * p + (int64_t)p * k];
+  } else {
+    for (int i = threadIdx.x; i < p * k; i += blockDim.x) Q[(i / k) * SM_QS + i % k] = (double)a.omega[i];
+  }
+  __syncthreads();
+  if (a.side == KVC_SIDE_RIGHT && threadIdx.x == 0) {
+    double t = 0.0;
+    for (int i = 0; i < p; ++i) t += G[i * p + i];
+    nrm_s = t;
+  }
+  const double* Mtx = a.side == KVC_SIDE_RIGHT ? G : nullptr;
+  // one CholeskyQR pass keeps each power step well conditioned; the final
+  // basis gets a second pass for orthogonality to working precision
+  double* W = sm_cholqr(Q, Z, S, X, diag0, Mtx, p, k);  // result in Z
+  Z = Q;
+  Q = W;
+  if (a.n_power == 0) {
+    W = sm_cholqr(Q, Z, S, X, diag0, Mtx, p, k);
+    Z = Q;
+    Q = W;
+  }
+  for (int it = 0; it < a.n_power; ++it) {
+    sm_gemm(Z, G, Q, p, k);  // Z = G Q becomes the sketch
+    W = Q;
+    Q = Z;
+    Z = W;
+    W = sm_cholqr(Q, Z, S, X, diag0, Mtx, p, k);
+    Z = Q;
+    Q = W;
+    if (it + 1 == a.n_power) {
+      W = sm_cholqr(Q, Z, S, X, diag0, Mtx, p, k);
+      Z = Q;
+      Q = W;
+    }
+  }
+  sm_gemm(Z, G, Q, p, k);  // Z = G Q (or H W)
+  if (a.side == KVC_SIDE_LEFT) sm_colgram(C, Q, Z, p, k);  // Q^T G Q
+  else sm_colgram(C, Z, Z, p, k);                         // (H W)^T (H W)
+  sm_jacobi(C, V, k, ev, rot, pq, red);
+  for (int i = threadIdx.x; i < k; i += blockDim.x) ev[i] = ev[i] > 0.0 ? ev[i] : 0.0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    int r = 0;
+    const double v = ev[i];
+    for (int j = 0; j < k; ++j) r += (ev[j] > v) || (ev[j] == v && j < i);
+    order[r] = i;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double retained = 0.0;
+    for (int i = 0; i < rank; ++i) retained += ev[order[i]];
+    const double nrm = nrm_s;
+    const double t = nrm > 0.0 ? 1.0 - retained / nrm : 0.0;
+    a.tail[cell] = t > 0.0 ? t : 0.0;
+    if (a.sv2)
+      for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = ev[order[i]];
+  }
+  // basis = Q V[:, order[:rank]]
+  for (int idx = threadIdx.x; idx < p * rank; idx += blockDim.x) {
+    const int i = idx / rank, r = idx % rank;
+    const int col = order[r];
+    double s = 0.0;
+    for (int j = 0; j < k; ++j) s = fma(Q[i * SM_QS + j], V[j * SM_K + col], s);
+    if (a.side == KVC_SIDE_LEFT) store_dt(a.basis, (int64_t)cell * p * rank + idx, (float)s, a.basis_dtype);
+    else static_cast<double*>(a.basis)[(int64_t)cell * p * rank + idx] = s;
+  }
+}
+
 int64_t ws_per_cell(int mode, int p, int k) {
   const int64_t nmax = std::max(p, k);
   if (mode == KVC_SVD_EXACT) return 2 * nmax + 2LL * p * p;
@@ -385,6 +735,14 @@ extern "C" int kvc_sketch_solve(int n_cells, int mode, int side, int p, int64_t 
   a.tail = tail_out;
   a.ws = static_cast<double*>(workspace);
   a.ws_cell = per;
+  if (mode == KVC_SVD_RANDOMISED && p <= SM_P && kk <= SM_K) {
+    const size_t smem = small_smem_bytes(p);
+    cudaError_t e = cudaFuncSetAttribute(sketch_solve_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    sketch_solve_small_kernel<<<n_cells, SM_NT, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    return check_launch("sketch_solve_small_kernel");
+  }
   sketch_solve_kernel<<<n_cells, SNT, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return check_launch("sketch_solve_kernel");
 }

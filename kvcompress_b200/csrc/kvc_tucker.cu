@@ -167,6 +167,36 @@ __global__ void __launch_bounds__(256) project_small_kernel(CellPtrs X, CellPtrs
   }
 }
 
+// out (rows x N) = round_T(A (rows x K) * M (K x N)) for K <= 64, N <= 16:
+// one thread per row, M in shared memory as float, fp32 accumulation in k
+// order (the same arithmetic as rowmat_kernel).
+constexpr int SKK = 64, SKN = 16;
+template <typename T>
+__global__ void __launch_bounds__(256) rowmat_skinny_kernel(CellPtrs A, const double* __restrict__ mat, int64_t rows,
+                                                            int K, int N, CellPtrsMut out) {
+  __shared__ float sM[SKK * SKN];
+  const int cell = blockIdx.y;
+  const double* m = mat + (int64_t)cell * K * N;
+  for (int i = threadIdx.x; i < K * N; i += blockDim.x) sM[i] = (float)m[i];
+  __syncthreads();
+  const T* a = static_cast<const T*>(A.p[cell]);
+  T* o = static_cast<T*>(out.p[cell]);
+  for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows; r += (int64_t)gridDim.x * blockDim.x) {
+    float acc[SKN];
+#pragma unroll
+    for (int j = 0; j < SKN; ++j) acc[j] = 0.f;
+    for (int k = 0; k < K; ++k) {
+      const float av = Elt<T>::to_f32(a[r * K + k]);
+#pragma unroll
+      for (int j = 0; j < SKN; ++j)
+        if (j < N) acc[j] = fmaf(av, sM[k * N + j], acc[j]);
+    }
+#pragma unroll
+    for (int j = 0; j < SKN; ++j)
+      if (j < N) o[r * N + j] = Elt<T>::from(acc[j]);
+  }
+}
+
 }  // namespace
 }  // namespace kvc
 
@@ -231,8 +261,14 @@ extern "C" int kvc_apply_basis(int n_cells, const void* const* a, int64_t rows, 
     mm.p[c] = mat + (int64_t)c * p * r;
     o.p[c] = out[c];
   }
-  dim3 grid((unsigned)ceil_div(rows, TM), (unsigned)ceil_div(r, TN), n_cells);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p <= SKK && r <= SKN) {
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 256), ceil_div(4LL * num_sms(), n_cells)));
+    KVC_DISPATCH_DTYPE(dtype, T,
+                       rowmat_skinny_kernel<T><<<dim3(blocks, n_cells), 256, 0, st>>>(aa, mat, rows, p, r, o));
+    return check_launch("rowmat_skinny_kernel");
+  }
+  dim3 grid((unsigned)ceil_div(rows, TM), (unsigned)ceil_div(r, TN), n_cells);
   KVC_DISPATCH_DTYPE(dtype, T,
                      rowmat_kernel<T, double, false><<<grid, NT, 0, st>>>(aa, mm, rows, p, r, 1, 1, o));
   return check_launch("rowmat_kernel(apply)");
