@@ -1,32 +1,33 @@
 // Tensor-core (tcgen05 / TMEM, TMA-fed) kernels for the residual encode and
 // the fused decode, bf16 caches with head_dim 64 or 128.
 //
-// Both are persistent, warp-specialised kernels (448 threads, one CTA per
-// SM) over 128-row tiles of a cell:
+// All three are persistent, warp-specialised kernels (448 threads, one CTA
+// per SM) over 128-row tiles of a cell:
 //   warp 5     TMA: one thread loads each tile into a ring of NS stages
-//   warps 0-3  transform, one row per thread: the encode subtracts the
-//              Tucker term in place (R = x - recon), the decode turns codes
-//              into exact bf16 integers in the swizzled operand tile
+//   warps 0-3  transform, one row per thread
 //   warp 4     one thread issues tcgen05.mma into one of two accumulators
-//   warps 6-13 epilogue: two warps per TMEM lane group, one column half each
+//   warps 6-13 epilogue: two warps per TMEM lane group, one half each
 //
-// The constant operand sits in tensor memory as the MMA's A operand and the
-// tile of rows is the shared-memory B operand, so the accumulator is
-// feature-major: TMEM lane = output feature, column = row of the tile.
-//   encode:  A = Pi (rows = output features) in three bf16 terms (hi + mid +
-//            lo = Pi to fp32 precision), B = R; D = (R Pi^T)^T
-//            (kvcompress/compressor/residual.py:201-239).  A thread owns one
-//            feature, so the stats pass keeps its |max| (or min / max) in a
-//            register; the quantise pass writes the codes of 64 rows x 32
-//            features through shared memory with a TMA store.
-//   decode:  A = (diag(scale) Pi)^T in two bf16 terms (one buffer per cell,
-//            double-buffered in TMEM), B = the codes as exact bf16 integers;
-//            the epilogue adds the fp32 Tucker term and stores bf16 tiles by
-//            TMA (kvcompress/compressor/jolt.py:424-463, residual.py:242-288).
-// Keeping the constant operand out of shared memory buys a deeper TMA ring.
+// Stats pass (tc_stats_kernel), feature-major: A = Pi (rows = output
+// features) in three bf16 terms (hi + mid + lo = Pi to fp32 precision) sits
+// in TMEM, B = R = x - recon is the shared-memory tile, so TMEM lane = output
+// feature and a thread keeps its feature's |max| (or min / max) in a register
+// (kvcompress/compressor/residual.py:201-239).
 //
-// TMEM holds A as one row per lane with two 16-bit elements per 32-bit
-// column (element 2w in the low half), written by tcgen05.st.
+// Quantise pass (tc_quant_kernel) and decode (tc_decode_kernel), row-major:
+// the transform writes the tile's rows into a TMEM A buffer (double-buffered)
+// with tcgen05.st and frees its TMA stage at once; the constant operand is
+// the shared-memory B image.  TMEM lane = row, so an epilogue thread owns the
+// contiguous outputs of one row and stores them with 16-byte stores, with no
+// staging through shared memory.
+//   quantise: B = Pi in three bf16 terms; codes packed in registers.
+//   decode:   A = the codes as exact bf16 integers, B = diag(scale) Pi of the
+//             cell in two bf16 terms (bulk-loaded at each cell change); the
+//             epilogue adds the fp32 Tucker term and rounds to bf16
+//             (kvcompress/compressor/jolt.py:424-463, residual.py:242-288).
+//
+// TMEM holds an A tile as one row per lane with two 16-bit elements per
+// 32-bit column (element 2w in the low half).
 //
 // Every mbarrier wait is bounded (kvc_tc.cuh) and warp-uniform: a warp
 // whose wait times out leaves its loop as a whole, so the others time out
@@ -36,6 +37,7 @@
 
 #include "kvc_common.cuh"
 #include "kvc_quant.cuh"
+#include "kvc_sched.cuh"
 #include "kvc_tc.cuh"
 #include "kvc_tma.cuh"
 
@@ -117,30 +119,17 @@ __device__ __forceinline__ void load_a_rows(uint32_t tmem_lane_base, uint32_t co
 }
 
 // ------------------------------------------------------------------------
-// residual encode: STATS / QUANT
+// residual encode, stats pass: feature-major, one thread per output feature
 // ------------------------------------------------------------------------
-enum { MODE_STATS = 0, MODE_QUANT = 1 };
 
-// Quantiser of the fused encode.  The reference computes
-// q = rint(fl32(fl32(v / s) + zp)) (round half to even, then clamp).  Here
-// fl32(v / s) is rebuilt from inv = fl(1/s) and eta = fl(s inv - 1):
-// v inv = hi + e exactly (hi = fl(v inv), e by fma), and
-// v / s = v inv / (1 + eta) = hi + (e - hi eta) + O(2^-47 |v/s|), so
-// RN(hi + RN(e - hi eta)) equals fl32(v / s) unless v / s lies within
-// 5 * 2^-48 |v/s| of an fp32 rounding boundary (then they differ by one ulp,
-// which changes the code only when that ulp straddles a half-integer: of the
-// order of 1e-11 of the values).  No branch and no division per value.
-
-template <int D, int RDM, int NS, int MODE>
-struct EncLayout {
+template <int D, int RDM, int NS>
+struct StatsLayout {
   static constexpr uint32_t B_BYTES = TILE_M * D * 2;             // R tile (MMA B operand)
   static constexpr uint32_t T_BYTES = TILE_M * RDM * 4;           // Tucker row term of a tile
   static constexpr uint32_t U_BYTES = RDM == 1 ? D * 2 : D * 16;  // u_feature: bf16 [j] or fp32 [j][4]
-  static constexpr uint32_t Q_BUF = 64 * 32;                      // codes of 64 rows x 32 features (<= 8-bit)
   static constexpr uint32_t OFF_T = NS * B_BYTES;
   static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
-  static constexpr uint32_t OFF_Q = OFF_U + 4 * U_BYTES;          // 8 epilogue warps x 2 buffers
-  static constexpr uint32_t OFF_BAR = OFF_Q + (MODE == MODE_QUANT ? 8 * 2 * Q_BUF : 0);
+  static constexpr uint32_t OFF_BAR = OFF_U + 4 * U_BYTES;
   static constexpr uint32_t NBAR = 3 * NS + 4;                    // loaded, full, empty, acc full x2, acc empty x2
   static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
   static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;           // + alignment slack
@@ -154,13 +143,13 @@ struct EncArgs {
   const uint32_t* arows;  // A = Pi in three bf16 terms: [term][128 rows][D/2 pairs]
   int32_t* minmax;        // STATS: [cell][2][d] ordered ints (min, max)
   const float* tmp;       // [cell][tiles_per_cell * 128][rdm]: sum_a core[h][a][r] u_token[t][a], bf16-rounded
+  unsigned long long* sched;  // quantise: per-CTA tile ranges (kvc_sched.cuh)
 };
 
-template <int D, int MODE, bool SYM, int RDM, int NS>
+template <int D, bool SYM, int RDM, int NS>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    tc_encode_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ TmaMaps cmaps,
-                     const __grid_constant__ EncArgs A) {
-  using L = EncLayout<D, RDM, NS, MODE>;
+    tc_stats_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ EncArgs A) {
+  using L = StatsLayout<D, RDM, NS>;
   static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -328,16 +317,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int half = e >> 2;
     const int feat = lg * 32 + lane;
     const bool active = lg * 32 < D;  // warp-uniform (d = 64 uses lane groups 0-1)
-    uint8_t* qst = smem + L::OFF_Q + e * 2 * L::Q_BUF;
-    int qmin, qmax;
-    qrange(A.bits > 0 ? A.bits : 8, A.symmetric, qmin, qmax);
-    const int offset = A.symmetric ? (1 << (A.bits - 1)) : 0;
-    const int ad = A.scale_mode == KVC_SCALE_TENSOR ? A.arith_dtype : KVC_F32;
-    const float magic = 12582912.0f + (float)offset;  // 1.5 * 2^23 + offset
-    const int lo_bits = 0x4B400000 + offset + qmin, hi_bits = 0x4B400000 + offset + qmax;
     float run_max = 0.f, rmin = __int_as_float(0x7f800000), rmax = -__int_as_float(0x7f800000);
-    float s_j = 1.f, inv_j = 1.f, eta_j = 0.f, zp_j = 0.f;
-    bool fast = true;
     auto flush_stats = [&](int cell) {
       if (!active) return;
       int32_t* mm = A.minmax + (int64_t)cell * 2 * D;
@@ -358,124 +338,36 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int cell = (int)(g / A.tiles_per_cell);
       const int64_t tile = g % A.tiles_per_cell;
       if (cell != cur_cell) {
-        if (MODE == MODE_STATS && cur_cell >= 0) flush_stats(cur_cell);
-        if (MODE == MODE_QUANT && active) {
-          const int jj = A.scale_mode == KVC_SCALE_CHANNEL ? feat : 0;
-          s_j = static_cast<const float*>(A.scale.p[cell])[jj];
-          inv_j = __fdiv_rn(1.0f, s_j);
-          eta_j = fmaf(s_j, inv_j, -1.0f);
-          zp_j = (float)static_cast<const int32_t*>(A.zp.p[cell])[jj];
-          fast = A.scale_mode != KVC_SCALE_TENSOR || A.arith_dtype == KVC_F32;
-        }
+        if (cur_cell >= 0) flush_stats(cur_cell);
         cur_cell = cell;
       }
       const int ac = it & 1;
       if (!warp_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x301)) break;
       tc_fence_after();
       const int64_t row0 = tile * TILE_M + half * 64;  // first row of this warp's half
-      uint8_t* buf = qst + (it & 1) * L::Q_BUF;
-      if (MODE == MODE_QUANT && active && A.bits > 2) {
-        // the TMA store issued from this buffer two tiles ago has read it
-        if (lane == 0) bulk_wait_read<1>();
-        __syncwarp();
-      }
 #pragma unroll
       for (int cc = 0; cc < 2; ++cc) {
         float v[32];
         tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * TILE_M + half * 64 + cc * 32), v);
         if (!active) continue;
-        if (MODE == MODE_STATS) {
-          if (SYM) {
-            // rows past the end hold R = 0 and cannot raise |max|
+        if (SYM) {
+          // rows past the end hold R = 0 and cannot raise |max|
 #pragma unroll
-            for (int j = 0; j < 32; ++j) run_max = fmaxf(run_max, fabsf(v[j]));
-          } else {
-            const int64_t nvalid = A.rows - (row0 + cc * 32);
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < nvalid) {
-                rmax = fmaxf(rmax, v[j]);
-                rmin = fminf(rmin, v[j]);
-              }
-          }
+          for (int j = 0; j < 32; ++j) run_max = fmaxf(run_max, fabsf(v[j]));
         } else {
-          int code[32];
-          if (fast) {
-            // fl32(v / s) from the error-free product v * fl(1/s) = hi + e and
-            // the reciprocal's residual eta = s fl(1/s) - 1:  RN(hi + (e - hi eta)).
-            // Branch-free; the float bits of y = t + 1.5 * 2^23 + offset are
-            // 0x4B400000 + offset + rint(t) (ties to even), clamped to the codes
-            const uint64_t M2 = f2_pack(magic, magic), NEG1 = f2_pack(-1.f, -1.f);
-            const uint64_t I2 = f2_pack(inv_j, inv_j), NI2 = f2_pack(-inv_j, -inv_j);
-            const uint64_t E2 = f2_pack(eta_j, eta_j), Z2 = f2_pack(zp_j, zp_j);
+          const int64_t nvalid = A.rows - (row0 + cc * 32);
 #pragma unroll
-            for (int j = 0; j < 32; j += 2) {
-              const uint64_t v2 = f2_pack(v[j], v[j + 1]);
-              const uint64_t nhi = f2_mul(v2, NI2);        // -hi
-              const uint64_t e = f2_fma(v2, I2, nhi);       // v * inv - hi, exact
-              const uint64_t lo = f2_fma(nhi, E2, e);       // e - hi * eta
-              uint64_t t2 = f2_fma(nhi, NEG1, lo);          // RN(hi + lo) = fl32(v / s)
-              if (!SYM) t2 = f2_add(t2, Z2);                // fl32(v / s) + zp, as the reference
-              const uint64_t y2 = f2_add(t2, M2);
-              float y0, y1;
-              f2_unpack(y2, y0, y1);
-              code[j] = min(max(__float_as_int(y0), lo_bits), hi_bits) - 0x4B400000;
-              code[j + 1] = min(max(__float_as_int(y1), lo_bits), hi_bits) - 0x4B400000;
+          for (int j = 0; j < 32; ++j)
+            if (j < nvalid) {
+              rmax = fmaxf(rmax, v[j]);
+              rmin = fminf(rmin, v[j]);
             }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) code[j] = quantize_one(v[j], s_j, (int32_t)zp_j, qmin, qmax, ad) + offset;
-          }
-          // stage: buf[row][feature byte] for the 64 rows x 32 features of this warp
-          if (A.bits == 8) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) buf[(cc * 32 + j) * 32 + lane] = (uint8_t)code[j];
-          } else if (A.bits == 4) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int other = __shfl_xor_sync(0xffffffffu, code[j], 1);
-              if (!(lane & 1)) buf[(cc * 32 + j) * 16 + (lane >> 1)] = (uint8_t)((code[j] << 4) | (other & 0xF));
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              const int c1 = __shfl_down_sync(0xffffffffu, code[j], 1);
-              const int c2 = __shfl_down_sync(0xffffffffu, code[j], 2);
-              const int c3 = __shfl_down_sync(0xffffffffu, code[j], 3);
-              if (!(lane & 3))
-                buf[(cc * 32 + j) * 8 + (lane >> 2)] =
-                    (uint8_t)((code[j] << 6) | ((c1 & 3) << 4) | ((c2 & 3) << 2) | (c3 & 3));
-            }
-          }
-        }
-      }
-      if (MODE == MODE_QUANT && active) {
-        if (A.bits > 2) {
-          fence_async_smem();
-          __syncwarp();
-          if (lane == 0) {
-            if (row0 < A.rows) tma_store_2d(&cmaps.m[cell], lg * 4 * A.bits, (int)row0, smem_u32(buf));
-            bulk_commit();
-          }
-        } else {
-          // 2-bit: 8 bytes per row, below the 16-byte TMA box; lanes store rows
-          __syncwarp();
-          uint8_t* dst = static_cast<uint8_t*>(A.codes.p[cell]);
-#pragma unroll
-          for (int h2 = 0; h2 < 2; ++h2) {
-            const int r = lane + 32 * h2;
-            if (row0 + r < A.rows)
-              *reinterpret_cast<uint2*>(dst + (row0 + r) * A.code_bytes + lg * 8) =
-                  *reinterpret_cast<const uint2*>(buf + r * 8);
-          }
-          __syncwarp();
         }
       }
       tc_fence_before();
       mbar_arrive(&acce[ac]);
     }
-    if (MODE == MODE_STATS && cur_cell >= 0) flush_stats(cur_cell);
-    if (MODE == MODE_QUANT && lane == 0) bulk_wait<0>();
+    if (cur_cell >= 0) flush_stats(cur_cell);
     __syncwarp();
   }
 
@@ -518,6 +410,9 @@ int rdm_enc(int rd) { return rd <= 1 ? 1 : 4; }
 int rdm_dec(int rd) { return rd <= 1 ? 1 : (rd <= 4 ? 4 : 16); }
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+constexpr int kMaxCtas = 1024;                     // grid cap of the persistent kernels
+constexpr size_t kSchedBytes = kMaxCtas * 8;       // one tile-range word per CTA
 
 // min / max arrays to their identities (ordered ints of +inf / -inf).
 __global__ void minmax_init_kernel(int32_t* mm, int n_cells, int d) {
@@ -570,65 +465,96 @@ __global__ void prep_rotation_kernel(const float* __restrict__ proj, int d, uint
   }
 }
 
+// B images of the quantise pass, per cell: B[n][k] = Pi[n][k] / s_n in three
+// bf16 terms (hi + mid + lo, fp32 precision), swizzled K-major
+// [cell][term][n][k], so that the MMA yields R~ / s directly (fold = 0 keeps
+// Pi itself, for the per-tensor scales quantised in a 16-bit dtype).
+__global__ void prep_quant_b_kernel(const float* __restrict__ proj, CellPtrs scale, int per_feature, int fold,
+                                    int d, uint8_t* out, unsigned long long* sched_w, int nctas, int64_t per_cta,
+                                    int64_t total) {
+  const int cell = blockIdx.y;
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (cell == 0) sched::init_ranges(sched_w, e, nctas, per_cta, total);
+  if (e >= d * d) return;
+  const int n = e / d, k = e % d;
+  float rest = proj[e];
+  if (fold) rest = __fdiv_rn(rest, static_cast<const float*>(scale.p[cell])[per_feature ? n : 0]);
+  uint8_t* base = out + (size_t)cell * 3 * d * d * 2;
+  for (int term = 0; term < 3; ++term) {
+    const __nv_bfloat16 v = __float2bfloat16_rn(rest);
+    rest -= __bfloat162float(v);
+    *reinterpret_cast<__nv_bfloat16*>(base + (size_t)term * d * d * 2 + sw128_off(n, k, d)) = v;
+  }
+}
+
+// Quantiser of the fused encode.  The reference computes
+// q = rint(fl32(fl32(v / s) + zp)) (round half to even, then clamp), v the
+// fp32 rotated residual.  Here 1/s is folded into the B image (Pi / s in
+// three bf16 terms), so the accumulator already holds v / s to fp32
+// precision; the epilogue adds zp and rounds with the magic constant: the
+// float bits of y = t + 1.5 * 2^23 + offset are 0x4B400000 + offset + rint(t)
+// (ties to even), clamped to the code range.  The per-tensor scale with a
+// 16-bit arithmetic dtype keeps Pi unscaled and quantises each value with
+// the reference's own steps (quantize_one).
 // ------------------------------------------------------------------------
-// decode
+// quantise pass, row-major: A = R in TMEM (one row per lane), B = Pi in
+// shared memory; thread = row in the epilogue, codes stored directly
 // ------------------------------------------------------------------------
-template <int D, int CB, int NS>
-struct DecLayout {
-  static constexpr uint32_t B_BYTES = TILE_M * D * 2;  // codes as bf16 (MMA B operand)
-  static constexpr uint32_t C_BYTES = TILE_M * CB;     // codes as loaded
-  static constexpr uint32_t O_BUF = 64 * 32 * 2;       // 64 rows x 32 features bf16
-  static constexpr uint32_t OFF_C = NS * B_BYTES;
-  static constexpr uint32_t OFF_O = OFF_C + NS * C_BYTES;  // 8 epilogue warps x 2 buffers
-  static constexpr uint32_t OFF_R = OFF_O + 8 * 2 * O_BUF;  // 8 epilogue warps x 64 Tucker row terms (rd = 1)
-  static constexpr uint32_t OFF_BAR = OFF_R + 8 * 64 * 4;
-  static constexpr uint32_t NBAR = 3 * NS + 6;  // loaded, full, empty, acc full x2, acc empty x2, A free x2
+template <int D, int RDM, int NS>
+struct QuantLayout {
+  static constexpr uint32_t B_TERM = D * D * 2;
+  static constexpr uint32_t B_BYTES = 3 * B_TERM;                 // Pi / s of the cell in three terms
+  static constexpr uint32_t X_BYTES = TILE_M * D * 2;             // x tile (TMA, SWIZZLE_128B)
+  static constexpr uint32_t T_BYTES = TILE_M * RDM * 4;           // Tucker row term of a tile
+  static constexpr uint32_t U_BYTES = RDM == 1 ? D * 2 : D * 16;  // u_feature: bf16 [j] or fp32 [j][4]
+  static constexpr uint32_t S_BYTES = (D / 2) * 4;                // per epilogue warp: zp of its D/2 features
+  static constexpr uint32_t Q_BYTES = 32 * (D / 2);                // per epilogue warp: codes of 32 rows x D/2
+  static constexpr uint32_t OFF_X = B_BYTES;
+  static constexpr uint32_t OFF_Q = OFF_X + NS * X_BYTES;         // 1024-aligned (swizzled staging)
+  static constexpr uint32_t OFF_T = OFF_Q + 8 * Q_BYTES;
+  static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
+  static constexpr uint32_t OFF_S = OFF_U + 4 * U_BYTES;
+  static constexpr uint32_t OFF_RING = OFF_S + 8 * S_BYTES;      // tile ids drawn by the producer
+  static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
+  static constexpr uint32_t NBAR = 2 * NS + 2 * 2 + 4 + 2;  // loaded, empty, A full/free x2, acc full/empty x2, B free/ready
   static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
   static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;
 };
 
-struct DecArgsTc {
-  CellPtrs ud;
-  int64_t m, t0, tl, tiles_per_cell, total_tiles, tiles_per_cta;
-  int tb_per_head;
-  int rt, rd, factor_dtype;
-  const uint32_t* arows;  // per cell: A = (diag(scale) Pi)^T in two bf16 terms [cell][term][128][d/2]
-  const float* tmp;       // [cell][m * tl][rdm] fp32 Tucker row term
-};
-
-template <int D, int RDM, int BITS, int NS>
+template <int D, bool SYM, int RDM, int NS>
 __global__ void __launch_bounds__(NTHREADS, 1)
-    tc_decode_kernel(const __grid_constant__ TmaMaps cmaps, const __grid_constant__ TmaMaps omaps,
-                     const __grid_constant__ DecArgsTc A) {
-  constexpr int CB = D * BITS / 8;  // code bytes per row
-  using L = DecLayout<D, CB, NS>;
+    tc_quant_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ TmaMaps cmaps,
+                    const __grid_constant__ EncArgs A, const uint8_t* bimg) {
+  using L = QuantLayout<D, RDM, NS>;
   static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
+  constexpr uint32_t ACOLS = D / 2;  // TMEM columns of one A buffer (bf16 pairs)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
   uint64_t* loaded = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
-  uint64_t* full = loaded + NS;
-  uint64_t* empty = full + NS;
-  uint64_t* accf = empty + NS;
+  uint64_t* empty = loaded + NS;
+  uint64_t* afull = empty + NS;
+  uint64_t* afree = afull + 2;
+  uint64_t* accf = afree + 2;
   uint64_t* acce = accf + 2;
-  uint64_t* afree = acce + 2;
+  uint64_t* bfree = acce + 2;    // MMA: the last MMA of a cell has read B
+  uint64_t* bready = bfree + 1;  // TMA: the next cell's B has arrived
   uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_TM);
+  int32_t* ring = reinterpret_cast<int32_t*>(smem + L::OFF_RING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t tile_begin = (int64_t)blockIdx.x * A.tiles_per_cta;
-  const int64_t tile_end = tile_begin + A.tiles_per_cta < A.total_tiles ? tile_begin + A.tiles_per_cta
-                                                                       : A.total_tiles;
-  const int n_my = (int)(tile_end > tile_begin ? tile_end - tile_begin : 0);
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
-      mbar_init(&loaded[i], 1);
-      mbar_init(&full[i], 128);
-      mbar_init(&empty[i], 1);
+      mbar_init(&loaded[i], 1);  // TMA issue + transaction bytes
+      mbar_init(&empty[i], 128);  // transform threads, once the tile is in registers
     }
     for (int i = 0; i < 2; ++i) {
+      mbar_init(&afull[i], 128);  // transform threads, after their TMEM stores
+      mbar_init(&afree[i], 1);    // tcgen05.commit
       mbar_init(&accf[i], 1);
       mbar_init(&acce[i], NEPI);
-      mbar_init(&afree[i], 1);  // tcgen05.commit after the last MMA reading an A buffer
     }
+    mbar_init(bfree, 1);
+    mbar_init(bready, 1);
     mbar_fence_init();
   }
   if (warp == MMA_WARP) {
@@ -641,43 +567,455 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const uint32_t tmem = *tm_holder;
 
   if (warp < 4) {
-    // codes (dense rows of CB bytes) -> exact integers in bf16 -> swizzled B tile;
-    // at a cell change, the cell's A rows into the free TMEM buffer
-    constexpr int LPR = CB / 16 > 0 ? CB / 16 : 1;  // lanes per row, 16 code bytes each
-    constexpr int RPI = 32 / LPR;                   // rows per warp iteration
-    constexpr int NIT = 32 / RPI;
+    // ---------------- transform: R = x - recon of one row into a TMEM A buffer ----------------
+    const int ptid = threadIdx.x;
+    float* u32 = reinterpret_cast<float*>(smem + L::OFF_U + warp * L::U_BYTES);       // [j][4]
+    uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + warp * L::U_BYTES);  // [j]
+    int cur_cell = -1;
+    for (int it = 0;; ++it) {
+      const int st = it % NS, b = it & 1;
+      if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x171)) break;
+      const int32_t tile = sched::ring_get(ring, it);
+      // the MMAs of tile it - 2 read this A buffer last (long done in steady state)
+      if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x172)) break;
+      if (tile < 0) {  // no more tiles: pass the end on to the MMA thread
+        mbar_arrive(&afull[b]);
+        break;
+      }
+      const int cell = (int)(tile / A.tiles_per_cell);
+      const int64_t row = (tile % A.tiles_per_cell) * TILE_M + ptid;
+      if (A.rt > 0 && cell != cur_cell) {
+        __syncwarp();
+        const __nv_bfloat16* ud = static_cast<const __nv_bfloat16*>(A.ud.p[cell]);
+        if (RDM == 1) {
+          for (int j = lane; j < D; j += 32) ub[j] = reinterpret_cast<const uint16_t*>(ud)[j];
+        } else {
+          for (int i = lane; i < D * 4; i += 32) {
+            const int j = i >> 2, r = i & 3;
+            u32[i] = r < A.rd ? __bfloat162float(ud[j * A.rd + r]) : 0.f;
+          }
+        }
+        __syncwarp();
+        cur_cell = cell;
+      }
+      tc_fence_after();
+      const uint8_t* Xs = smem + L::OFF_X + st * L::X_BYTES;
+      const bool sub = A.rt > 0 && row < A.rows;
+      const uint32_t tm_row = tmem + ((uint32_t)(warp * 32) << 16) + b * ACOLS;
+      if (RDM == 1) {
+        const float* ts = reinterpret_cast<const float*>(smem + L::OFF_T + st * L::T_BYTES) + ptid;
+        const uint32_t th = sub ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(ts[0])) : 0u;
+        const uint32_t t2 = th | (th << 16);
+        const uint4* u4 = reinterpret_cast<const uint4*>(ub);
+#pragma unroll
+        for (int q = 0; q < (int)ACOLS / 32; ++q) {
+          uint32_t part[32];  // 64 features as bf16 pairs
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const int c = q * 8 + c8;
+            uint4 x = *reinterpret_cast<const uint4*>(Xs + sw128_off(ptid, c * 8, TILE_M));
+            if (sub) {
+              // rd == 1: recon = bf16(t * u_j) and R = bf16(x - recon), each a
+              // single rounding of the exact bf16 product / difference
+              const uint4 u = u4[c];
+              x.x = bf16x2_sub(x.x, bf16x2_mul(t2, u.x));
+              x.y = bf16x2_sub(x.y, bf16x2_mul(t2, u.y));
+              x.z = bf16x2_sub(x.z, bf16x2_mul(t2, u.z));
+              x.w = bf16x2_sub(x.w, bf16x2_mul(t2, u.w));
+            }
+            part[4 * c8] = x.x;
+            part[4 * c8 + 1] = x.y;
+            part[4 * c8 + 2] = x.z;
+            part[4 * c8 + 3] = x.w;
+          }
+          tmem_st32(tm_row + q * 32, part);
+        }
+      } else {
+        const float4 tv = sub ? *reinterpret_cast<const float4*>(smem + L::OFF_T + st * L::T_BYTES + ptid * 16)
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+        const float4* u4 = reinterpret_cast<const float4*>(u32);
+#pragma unroll
+        for (int q = 0; q < (int)ACOLS / 32; ++q) {
+          uint32_t part[32];
+#pragma unroll
+          for (int c8 = 0; c8 < 8; ++c8) {
+            const int c = q * 8 + c8;
+            const uint4 raw = *reinterpret_cast<const uint4*>(Xs + sw128_off(ptid, c * 8, TILE_M));
+            float xv[8];
+            unpack8_bf16(raw, xv);
+            if (sub) {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) {
+                const float4 u = u4[c * 8 + e];
+                float rec = tv.x * u.x;
+                rec = fmaf(tv.y, u.y, rec);
+                rec = fmaf(tv.z, u.z, rec);
+                rec = fmaf(tv.w, u.w, rec);
+                xv[e] = Elt<__nv_bfloat16>::round(xv[e] - Elt<__nv_bfloat16>::round(rec));
+              }
+            }
+            const uint4 w = pack8_bf16(xv);
+            part[4 * c8] = w.x;
+            part[4 * c8 + 1] = w.y;
+            part[4 * c8 + 2] = w.z;
+            part[4 * c8 + 3] = w.w;
+          }
+          tmem_st32(tm_row + q * 32, part);
+        }
+      }
+      mbar_arrive(&empty[st]);  // the x stage is no longer needed
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&afull[b]);
+    }
+  } else if (warp == TMA_WARP) {
+    if (lane == 0) {
+      int victim = (int)blockIdx.x;
+      for (int it = 0;; ++it) {
+        const int64_t tile = sched::next_tile(A.sched, (int)blockIdx.x, (int)gridDim.x, victim);
+        sched::ring_put(ring, it, (int32_t)tile);
+        const int st = it % NS;
+        if (!mbar_wait(&empty[st], (uint32_t)((it / NS) & 1) ^ 1u, 0x173)) break;
+        if (tile < 0) {  // the end: a plain arrive completes the stage with no bytes
+          mbar_arrive(&loaded[st]);
+          break;
+        }
+        const int cell = (int)(tile / A.tiles_per_cell);
+        const int y = (int)((tile % A.tiles_per_cell) * TILE_M);
+        mbar_expect_tx(&loaded[st], L::X_BYTES + (A.rt > 0 ? L::T_BYTES : 0u));
+        const uint32_t dst = sbase + L::OFF_X + st * L::X_BYTES;
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h) tma_load_2d(dst + h * TILE_M * 128, &xmaps.m[cell], h * 64, y, &loaded[st]);
+        if (A.rt > 0)
+          bulk_load(sbase + L::OFF_T + st * L::T_BYTES,
+                    A.tmp + ((int64_t)cell * A.tiles_per_cell * TILE_M + y) * RDM, L::T_BYTES, &loaded[st]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    // D[row][feature] = sum_k R[row][k] (Pi / s)[feature][k]
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(TILE_M, D, true);
+      int it = 0, cur_cell = -1, nb = 0;
+      bool ended = false;
+      for (;; ++it) {
+        const int b = it & 1, ac = it & 1;
+        if (!mbar_wait(&afull[b], (uint32_t)((it >> 1) & 1), 0x271)) break;
+        const int32_t tile = sched::ring_get(ring, it);
+        if (!mbar_wait(&acce[ac], (uint32_t)((it >> 1) & 1) ^ 1u, 0x272)) break;
+        if (tile < 0) {  // the end: the epilogue learns it from the same accumulator barrier
+          umma_commit(&accf[ac]);
+          ended = true;
+          break;
+        }
+        const int cell = (int)(tile / A.tiles_per_cell);
+        if (cell != cur_cell) {
+          // Pi / s of the new cell: after this thread's MMAs on the old one
+          if (cur_cell >= 0) {
+            umma_commit(bfree);
+            if (!mbar_wait(bfree, (uint32_t)((nb - 1) & 1), 0x274)) break;
+          }
+          mbar_expect_tx(bready, L::B_BYTES);
+#pragma unroll
+          for (int term = 0; term < 3; ++term)
+            bulk_load(sbase + term * L::B_TERM, bimg + (size_t)cell * L::B_BYTES + term * L::B_TERM, L::B_TERM,
+                      bready);
+          if (!mbar_wait(bready, (uint32_t)(nb & 1), 0x275)) break;
+          ++nb;
+          cur_cell = cell;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * D);
+#pragma unroll
+        for (int term = 0; term < 3; ++term) {
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint32_t kb = (uint32_t)((ks >> 2) * (D * 128) + (ks & 3) * 32);
+            umma_f16_ts(d_tmem, tmem + b * ACOLS + (uint32_t)(ks * 8), desc_sw128(sbase + term * L::B_TERM + kb),
+                        idesc, (term | ks) ? 1u : 0u);
+          }
+        }
+        umma_commit(&afree[b]);
+        umma_commit(&accf[ac]);
+      }
+      // do not leave while MMAs that write TMEM are still in flight
+      if (ended) mbar_wait(&accf[it & 1], (uint32_t)(it >> 1) & 1u, 0x273);
+      else if (it > 0) mbar_wait(&accf[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, 0x273);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: thread = row, D/2 features per warp ----------------
+    const int e = warp - EPI_WARP0;
+    const int lg = warp & 3;
+    const int half = e >> 2;
+    const int rloc = lg * 32 + lane;
+    constexpr int NCH = D / 64;  // 32-feature chunks per warp
+    float* zpf = reinterpret_cast<float*>(smem + L::OFF_S + e * L::S_BYTES);  // [feature]: zp
+    // codes of this warp's half row: cbw bytes.  From 16 bytes up they are
+    // staged as [32 rows][cbw] in shared memory with the swizzle of that
+    // width (16-byte chunk j of row r at j ^ ((r * cbw / 128) mod (cbw / 16)),
+    // conflict-free) and leave by one TMA store of whole rows; 8-byte half
+    // rows (d = 64, 2 bits) are stored directly.
+    uint8_t* stg = smem + L::OFF_Q + e * L::Q_BYTES;
+    const int cbw = (D / 2) * A.bits / 8;
+    const bool tma_out = cbw >= 16;
+    const int swz = tma_out ? ((lane * cbw) >> 7) & (cbw / 16 - 1) : 0;
+    uint8_t* srow = stg + lane * cbw;
+    int qmin, qmax;
+    qrange(A.bits, A.symmetric, qmin, qmax);
+    const int offset = A.symmetric ? (1 << (A.bits - 1)) : 0;
+    const int ad = A.scale_mode == KVC_SCALE_TENSOR ? A.arith_dtype : KVC_F32;
+    const bool fast = A.scale_mode != KVC_SCALE_TENSOR || A.arith_dtype == KVC_F32;
+    const float magic = 12582912.0f + (float)offset;  // 1.5 * 2^23 + offset
+    const int lo_bits = 0x4B400000 + offset + qmin, hi_bits = 0x4B400000 + offset + qmax;
+    float s_t = 1.f;  // per-tensor scale and zero point (the unfolded path)
+    int32_t zp_t = 0;
+    int cur_cell = -1;
+    for (int it = 0;; ++it) {
+      const int ac = it & 1;
+      if (!warp_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x371)) break;
+      const int32_t tile = sched::ring_get(ring, it);
+      if (tile < 0) break;
+      const int cell = (int)(tile / A.tiles_per_cell);
+      const int64_t row = (tile % A.tiles_per_cell) * TILE_M + rloc;
+      if (cell != cur_cell) {
+        const int32_t* zz = static_cast<const int32_t*>(A.zp.p[cell]);
+        if (!SYM) {
+          __syncwarp();
+          for (int jl = lane; jl < D / 2; jl += 32)
+            zpf[jl] = (float)zz[A.scale_mode == KVC_SCALE_CHANNEL ? half * (D / 2) + jl : 0];
+          __syncwarp();
+        }
+        s_t = static_cast<const float*>(A.scale.p[cell])[0];
+        zp_t = zz[0];
+        cur_cell = cell;
+      }
+      tc_fence_after();
+      if (tma_out) {
+        // the previous tile's store has read the staging rows
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+      }
+#pragma unroll
+      for (int cc = 0; cc < NCH; ++cc) {
+        const int c = half * NCH + cc;  // global 32-feature chunk
+        float v[32];
+        tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * D + c * 32), v);
+        int code[32];
+        if (fast) {
+          // v holds R~ / s: add zp, round half to even with the magic
+          // constant and clamp on the float bits
+          const uint64_t M2 = f2_pack(magic, magic);
+          const uint64_t* z2 = reinterpret_cast<const uint64_t*>(zpf + cc * 32);
+#pragma unroll
+          for (int j = 0; j < 32; j += 2) {
+            uint64_t t2 = f2_pack(v[j], v[j + 1]);
+            if (!SYM) t2 = f2_add(t2, z2[j / 2]);
+            float y0, y1;
+            f2_unpack(f2_add(t2, M2), y0, y1);
+            code[j] = min(max(__float_as_int(y0), lo_bits), hi_bits);
+            code[j + 1] = min(max(__float_as_int(y1), lo_bits), hi_bits);
+          }
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) code[j] = quantize_one(v[j], s_t, zp_t, qmin, qmax, ad) + offset;
+        }
+        // low byte of each code is (q + offset) & 0xFF
+        if (A.bits == 8) {
+          uint32_t w[8];
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            w[q] = __byte_perm(__byte_perm(code[4 * q], code[4 * q + 1], 0x0040),
+                               __byte_perm(code[4 * q + 2], code[4 * q + 3], 0x0040), 0x5410);
+          const int j = cc * 2;  // 16-byte chunks of the staged half row
+          *reinterpret_cast<uint4*>(srow + ((j ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          *reinterpret_cast<uint4*>(srow + (((j + 1) ^ swz) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+        } else if (A.bits == 4) {
+          uint32_t w[4];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint32_t pb[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              pb[i] = ((uint32_t)code[8 * q + 2 * i] << 4) | ((uint32_t)code[8 * q + 2 * i + 1] & 0xFu);
+            w[q] = __byte_perm(__byte_perm(pb[0], pb[1], 0x0040), __byte_perm(pb[2], pb[3], 0x0040), 0x5410);
+          }
+          *reinterpret_cast<uint4*>(srow + ((cc ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        } else {
+          uint32_t w[2];
+#pragma unroll
+          for (int q = 0; q < 2; ++q) {
+            uint32_t pb[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int k = 16 * q + 4 * i;
+              pb[i] = ((uint32_t)code[k] << 6) | (((uint32_t)code[k + 1] & 3u) << 4) |
+                      (((uint32_t)code[k + 2] & 3u) << 2) | ((uint32_t)code[k + 3] & 3u);
+            }
+            w[q] = __byte_perm(__byte_perm(pb[0], pb[1], 0x0040), __byte_perm(pb[2], pb[3], 0x0040), 0x5410);
+          }
+          if (tma_out) {
+            // 8 bytes per 32 features: chunk cc / 2, half cc % 2
+            *reinterpret_cast<uint2*>(srow + (((cc >> 1) ^ swz) << 4) + (cc & 1) * 8) = make_uint2(w[0], w[1]);
+          } else if (row < A.rows) {
+            uint8_t* dst = static_cast<uint8_t*>(A.codes.p[cell]) + row * A.code_bytes + c * 8;
+            *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+          }
+        }
+      }
+      if (tma_out) {
+        fence_async_smem();
+        __syncwarp();
+        const int64_t row0 = (tile % A.tiles_per_cell) * TILE_M + lg * 32;
+        if (lane == 0) {
+          if (row0 < A.rows) tma_store_2d(&cmaps.m[cell], half * cbw, (int)row0, smem_u32(stg));
+          bulk_commit();
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acce[ac]);
+    }
+    if (lane == 0) bulk_wait<0>();  // shared memory outlives the stores
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------
+// decode, row-major: A = the codes as exact bf16 integers in TMEM (one row
+// per lane), B = diag(scale) Pi of the cell in shared memory (reloaded at a
+// cell change), thread = row in the epilogue, bf16 rows stored directly
+// ------------------------------------------------------------------------
+// rd = 1: the Tucker term t_row * u_feature is one more K-step of the MMA
+// (A: t split hi + mid + lo, B: u split hi + lo, every pairing once), so the
+// epilogue only rounds; rd > 1 adds it in the epilogue.
+template <int D, int CB, int RDM, int NS>
+struct DecLayout {
+  static constexpr bool FOLD = RDM == 1;
+  static constexpr uint32_t B_TERM = D * D * 2;
+  static constexpr uint32_t B_TUCKER = FOLD ? D * 128 : 0;  // the extra K block (SW128, 16 of 64 used)
+  static constexpr uint32_t B_BYTES = 2 * B_TERM + B_TUCKER;  // diag(scale) Pi in two terms (+ u_feature)
+  static constexpr uint32_t C_BYTES = TILE_M * CB;    // codes as loaded (dense rows)
+  static constexpr uint32_t U_BYTES = FOLD ? 0 : (D / 2) * RDM * 4;  // per epilogue warp: u_feature of its features
+  static constexpr uint32_t O_BYTES = 32 * D;              // per epilogue warp: 32 rows x D/2 bf16
+  // rd = 1: the tile's Tucker terms, bulk-copied from the 16-byte boundary at
+  // or below the first row (up to 3 floats early), 132 floats
+  static constexpr uint32_t T_BYTES = FOLD ? (TILE_M + 4) * 4 : 0;
+  static constexpr uint32_t OFF_C = B_BYTES;
+  static constexpr uint32_t OFF_O = OFF_C + NS * C_BYTES;  // 1024-aligned (swizzled staging)
+  static constexpr uint32_t OFF_U = OFF_O + 8 * O_BYTES;
+  static constexpr uint32_t OFF_T = OFF_U + 8 * U_BYTES;
+  static constexpr uint32_t OFF_RING = OFF_T + NS * T_BYTES;  // tile ids drawn by the producer
+  static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
+  static constexpr uint32_t NBAR = 2 * NS + 2 * 2 + 4 + 2;  // loaded, empty, A full/free x2, acc x2 x2, B free/ready
+  static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
+  static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;
+};
+
+struct DecArgsTc {
+  CellPtrs ud;
+  CellPtrsMut out;
+  int64_t m, t0, tl, tiles_per_cell, total_tiles, tiles_per_cta;
+  int tb_per_head;
+  int rt, rd, factor_dtype;
+  const uint8_t* bimg;  // per cell: two swizzled B images of diag(scale) Pi (+ the u_feature block)
+  const float* tmp;     // [cell][m * tl][rdm] fp32 Tucker row term (+ 132 floats of slack at the end)
+  unsigned long long* sched;  // per-CTA tile ranges (kvc_sched.cuh)
+};
+
+template <int D, int RDM, int BITS, int NS>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    tc_decode_kernel(const __grid_constant__ TmaMaps cmaps, const __grid_constant__ TmaMaps omaps,
+                     const __grid_constant__ DecArgsTc A) {
+  constexpr int CB = D * BITS / 8;  // code bytes per row
+  using L = DecLayout<D, CB, RDM, NS>;
+  static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
+  static_assert(CB % 16 == 0, "code rows must be whole 16-byte chunks");
+  constexpr bool FOLD = L::FOLD;
+  // TMEM columns of one A buffer: D / 2 (+ 8 for the Tucker K-step, padded
+  // so both buffers start on a 32-column boundary)
+  constexpr uint32_t ACOLS = D / 2 + (FOLD ? 32 : 0);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* loaded = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = loaded + NS;
+  uint64_t* afull = empty + NS;
+  uint64_t* afree = afull + 2;
+  uint64_t* accf = afree + 2;
+  uint64_t* acce = accf + 2;
+  uint64_t* bfree = acce + 2;    // the MMAs on the old cell's B are done
+  uint64_t* bready = bfree + 1;  // the new cell's B has arrived
+  uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_TM);
+  int32_t* ring = reinterpret_cast<int32_t*>(smem + L::OFF_RING);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&loaded[i], 1);
+      mbar_init(&empty[i], 128);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&afull[i], 128);
+      mbar_init(&afree[i], 1);
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], NEPI);
+    }
+    mbar_init(bfree, 1);
+    mbar_init(bready, 1);
+    mbar_fence_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tm_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tm_holder;
+
+  if (warp < 4) {
+    // ---------------- transform: codes of one row -> exact bf16 integers in a TMEM A buffer ----------------
+    const int ptid = threadIdx.x;
+    constexpr int NCH16 = CB / 16;  // 16-byte chunks per row
     constexpr int PER = 8 / BITS;   // codes per byte
-    constexpr int VALS = 16 * PER;  // values per lane
-    static_assert(CB % 16 == 0, "code rows must be whole 16-byte chunks");
-    const int pos = lane % LPR, sub = lane / LPR;
     // a code byte b placed in the mantissa of 2^23 reads 2^23 + b; subtracting
     // 2^23 + offset leaves the signed code exactly
     const float bias = 8388608.0f + (float)(1 << (BITS - 1));
     const uint64_t NB2 = f2_pack(-bias, -bias);
-    int cur_cell = -1, seq = -1;
-    for (int it = 0; it < n_my; ++it) {
-      const int64_t g = tile_begin + it;
-      const int cell = (int)(g / A.tiles_per_cell);
-      const int st = it % NS;
-      if (cell != cur_cell) {
-        ++seq;
-        const int b = seq & 1;
-        // the MMAs of the cell two changes back read this buffer last
-        if (seq >= 2 && !warp_wait(&afree[b], (uint32_t)(((seq - b) / 2 - 1) & 1), 0x161)) break;
-        tc_fence_after();
-        load_a_rows<D / 2>(tmem + ((uint32_t)(warp * 32) << 16), (uint32_t)(b * D),
-                           A.arows + (size_t)cell * 2 * 128 * (D / 2), 2, warp * 32 + lane, 128);
-        cur_cell = cell;
+    for (int it = 0;; ++it) {
+      const int st = it % NS, b = it & 1;
+      if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x181)) break;
+      const int32_t tile = sched::ring_get(ring, it);
+      if (tile < 0) {  // no more tiles: pass the end on to the MMA thread
+        if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x182)) break;
+        mbar_arrive(&afull[b]);
+        break;
       }
-      if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x141)) break;
-      const uint8_t* Cs = smem + L::OFF_C + st * L::C_BYTES;
-      uint8_t* Bs = smem + st * L::B_BYTES;
+      float tv = 0.f;  // this row's Tucker term (rd = 1)
+      if (FOLD && A.rt > 0) {
+        const int64_t tc = tile % A.tiles_per_cell;
+        const int64_t i_tok = (tc % A.tb_per_head) * TILE_M + ptid;
+        const int64_t base = (int64_t)(tile / A.tiles_per_cell) * A.m * A.tl + (tc / A.tb_per_head) * A.tl +
+                             (tc % A.tb_per_head) * TILE_M;
+        if (i_tok < A.tl)
+          tv = reinterpret_cast<const float*>(smem + L::OFF_T + st * L::T_BYTES)[(base & 3) + ptid];
+      }
+      const uint8_t* Cs = smem + L::OFF_C + st * L::C_BYTES + ptid * CB;
+      // the stage is written by TMA with the swizzle of its row width (32,
+      // 64 or 128 B): 16-byte chunk c of row r sits at c ^ ((r * CB / 128) mod
+      // (CB / 16)), which spreads the 8 rows of a quarter-warp over the banks
+      const int swz = (ptid * CB >> 7) & (NCH16 - 1);
+      uint32_t r[D / 2];
 #pragma unroll
-      for (int i = 0; i < NIT; ++i) {
-        const int rloc = warp * 32 + i * RPI + sub;
-        const uint4 raw = *reinterpret_cast<const uint4*>(Cs + rloc * CB + pos * 16);
+      for (int c = 0; c < NCH16; ++c) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(Cs + ((c ^ swz) << 4));
         const uint32_t words[4] = {raw.x, raw.y, raw.z, raw.w};
-        uint32_t o[VALS / 2];  // bf16 pairs in value order
+        // chunk c holds values [c * 16 * PER, (c + 1) * 16 * PER): 8 * PER bf16 pairs
 #pragma unroll
         for (int wi = 0; wi < 4; ++wi) {
           uint32_t pl[PER];  // plane p: the code at bit offset BITS*(PER-1-p) of every byte
@@ -692,160 +1030,218 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             float q0, q1;
             f2_unpack(f2_add(f2_pack(f0, f1), NB2), q0, q1);
             const __nv_bfloat162 h = __floats2bfloat162_rn(q0, q1);
-            o[(wi * 4 * PER + k) / 2] = *reinterpret_cast<const uint32_t*>(&h);
+            r[(c * 16 * PER + wi * 4 * PER + k) / 2] = *reinterpret_cast<const uint32_t*>(&h);
           }
         }
-#pragma unroll
-        for (int cb = 0; cb < VALS / 8; ++cb)
-          *reinterpret_cast<uint4*>(Bs + sw128_off(rloc, pos * VALS + cb * 8, TILE_M)) =
-              make_uint4(o[4 * cb], o[4 * cb + 1], o[4 * cb + 2], o[4 * cb + 3]);
       }
-      fence_async_smem();
+      mbar_arrive(&empty[st]);  // the codes stage is no longer needed
+      if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x182)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int q = 0; q < D / 64; ++q) {
+        uint32_t part[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) part[i] = r[q * 32 + i];
+        tmem_st32(tmem + ((uint32_t)(warp * 32) << 16) + b * ACOLS + q * 32, part);
+      }
+      if (FOLD) {
+        // K positions 0-5 of the extra step: (hi, mid, lo, hi, mid, lo) of t
+        const __nv_bfloat16 th = __float2bfloat16_rn(tv);
+        const float r1 = tv - __bfloat162float(th);
+        const __nv_bfloat16 tm = __float2bfloat16_rn(r1);
+        const __nv_bfloat16 tlo = __float2bfloat16_rn(r1 - __bfloat162float(tm));
+        const uint32_t h = __bfloat16_as_ushort(th), mi = __bfloat16_as_ushort(tm), lo = __bfloat16_as_ushort(tlo);
+        const uint32_t ext[8] = {h | (mi << 16), lo | (h << 16), mi | (lo << 16), 0u, 0u, 0u, 0u, 0u};
+        tmem_st8(tmem + ((uint32_t)(warp * 32) << 16) + b * ACOLS + D / 2, ext);
+      }
+      tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&full[st]);
+      mbar_arrive(&afull[b]);
     }
   } else if (warp == TMA_WARP) {
     if (lane == 0) {
-      for (int it = 0; it < n_my; ++it) {
-        const int64_t g = tile_begin + it;
+      int victim = (int)blockIdx.x;
+      for (int it = 0;; ++it) {
+        const int64_t g = sched::next_tile(A.sched, (int)blockIdx.x, (int)gridDim.x, victim);
+        sched::ring_put(ring, it, (int32_t)g);
+        const int st = it % NS;
+        if (!mbar_wait(&empty[st], (uint32_t)((it / NS) & 1) ^ 1u, 0x192)) break;
+        if (g < 0) {  // the end: a plain arrive completes the stage with no bytes
+          mbar_arrive(&loaded[st]);
+          break;
+        }
         const int cell = (int)(g / A.tiles_per_cell);
         const int64_t tile = g % A.tiles_per_cell;
         const int h = (int)(tile / A.tb_per_head);
-        const int tok = (int)(A.t0 + (tile % A.tb_per_head) * TILE_M);
-        const int st = it % NS;
-        if (!mbar_wait(&empty[st], (uint32_t)((it / NS) & 1) ^ 1u, 0x151)) break;
-        mbar_expect_tx(&loaded[st], L::C_BYTES);
-        tma_load_3d(sbase + L::OFF_C + st * L::C_BYTES, &cmaps.m[cell], 0, tok, h, &loaded[st]);
+        const int64_t i0 = (tile % A.tb_per_head) * TILE_M;
+        const bool tload = FOLD && A.rt > 0;
+        mbar_expect_tx(&loaded[st], L::C_BYTES + (tload ? L::T_BYTES : 0u));
+        tma_load_3d(sbase + L::OFF_C + st * L::C_BYTES, &cmaps.m[cell], 0, (int)(A.t0 + i0), h, &loaded[st]);
+        if (tload) {
+          const int64_t base = (int64_t)cell * A.m * A.tl + (int64_t)h * A.tl + i0;
+          bulk_load(sbase + L::OFF_T + st * L::T_BYTES, A.tmp + (base & ~(int64_t)3), L::T_BYTES, &loaded[st]);
+        }
       }
     }
     __syncwarp();
   } else if (warp == MMA_WARP) {
+    // D[row][n] = sum_k q[row][k] scale[k] Pi[k][n]
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(128, TILE_M, true);
-      int it = 0, cur_cell = -1, seq = -1;
-      for (; it < n_my; ++it) {
-        const int cell = (int)((tile_begin + it) / A.tiles_per_cell);
+      const uint32_t idesc = idesc_f16(TILE_M, D, true);
+      int it = 0, cur_cell = -1, nb = 0;
+      bool ended = false;
+      for (;; ++it) {
+        const int b = it & 1, ac = it & 1;
+        if (!mbar_wait(&afull[b], (uint32_t)((it >> 1) & 1), 0x292)) break;
+        const int32_t g = sched::ring_get(ring, it);
+        if (!mbar_wait(&acce[ac], (uint32_t)((it >> 1) & 1) ^ 1u, 0x293)) break;
+        if (g < 0) {  // the end: the epilogue learns it from the same accumulator barrier
+          umma_commit(&accf[ac]);
+          ended = true;
+          break;
+        }
+        const int cell = (int)(g / A.tiles_per_cell);
         if (cell != cur_cell) {
-          if (seq >= 0) umma_commit(&afree[seq & 1]);  // releases the old buffer when its MMAs finish
-          ++seq;
+          // diag(scale) Pi of the new cell: after this thread's MMAs on the old one
+          if (cur_cell >= 0) {
+            umma_commit(bfree);
+            if (!mbar_wait(bfree, (uint32_t)((nb - 1) & 1), 0x291)) break;
+          }
+          mbar_expect_tx(bready, L::B_BYTES);
+          const uint8_t* src = A.bimg + (size_t)cell * L::B_BYTES;
+          bulk_load(sbase, src, L::B_TERM, bready);
+          bulk_load(sbase + L::B_TERM, src + L::B_TERM, L::B_TERM, bready);
+          if (FOLD) bulk_load(sbase + 2 * L::B_TERM, src + 2 * L::B_TERM, L::B_TUCKER, bready);
+          if (!mbar_wait(bready, (uint32_t)(nb & 1), 0x295)) break;
+          ++nb;
           cur_cell = cell;
         }
-        const int st = it % NS, ac = it & 1;
-        if (!mbar_wait(&full[st], (uint32_t)((it / NS) & 1), 0x211)) break;
-        if (!mbar_wait(&acce[ac], (uint32_t)((it >> 1) & 1) ^ 1u, 0x212)) break;
         tc_fence_after();
-        const uint32_t b_base = sbase + st * L::B_BYTES;
-        const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * TILE_M);
-        const uint32_t a_base = tmem + (uint32_t)((seq & 1) * D);
+        const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * D);
 #pragma unroll
         for (int term = 0; term < 2; ++term) {
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
-            const uint32_t kb = (uint32_t)((ks >> 2) * (TILE_M * 128) + (ks & 3) * 32);
-            umma_f16_ts(d_tmem, a_base + (uint32_t)(term * (D / 2) + ks * 8), desc_sw128(b_base + kb), idesc,
-                        (term | ks) ? 1u : 0u);
+            const uint32_t kb = (uint32_t)((ks >> 2) * (D * 128) + (ks & 3) * 32);
+            umma_f16_ts(d_tmem, tmem + b * ACOLS + (uint32_t)(ks * 8), desc_sw128(sbase + term * L::B_TERM + kb),
+                        idesc, (term | ks) ? 1u : 0u);
           }
         }
-        umma_commit(&empty[st]);
+        if (FOLD)  // + t_row * u_feature: K positions 0-5 of the extra block
+          umma_f16_ts(d_tmem, tmem + b * ACOLS + (uint32_t)(D / 2), desc_sw128(sbase + 2 * L::B_TERM), idesc, 1u);
+        umma_commit(&afree[b]);
         umma_commit(&accf[ac]);
       }
-      if (it > 0) mbar_wait(&accf[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, 0x213);
+      if (ended) mbar_wait(&accf[it & 1], (uint32_t)(it >> 1) & 1u, 0x294);
+      else if (it > 0) mbar_wait(&accf[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, 0x294);
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue: thread = output feature, 64 rows per tile ----------------
+    // ---------------- epilogue: thread = row, D/2 features per warp ----------------
     const int e = warp - EPI_WARP0;
     const int lg = warp & 3;
     const int half = e >> 2;
-    const int feat = lg * 32 + lane;
-    const bool active = lg * 32 < D;
-    uint8_t* ost = smem + L::OFF_O + e * 2 * L::O_BUF;
-    float* rst = reinterpret_cast<float*>(smem + L::OFF_R) + e * 64;  // this warp's 64 Tucker row terms
-    float u[RDM];
-#pragma unroll
-    for (int r = 0; r < RDM; ++r) u[r] = 0.f;
+    const int rloc = lg * 32 + lane;
+    constexpr int NCH = D / 64;
+    float* us = reinterpret_cast<float*>(smem + L::OFF_U + e * L::U_BYTES);  // [feature][RDM]
+    // the warp's 32 rows x D/2 outputs (D bytes a row) are staged with the
+    // swizzle of that width (16-byte chunk j of row r at j ^ ((r * D / 128)
+    // mod (D / 16)), conflict-free) and leave by one TMA store
+    uint8_t* stg = smem + L::OFF_O + e * L::O_BYTES;
+    const int swz = ((lane * D) >> 7) & (D / 16 - 1);
+    uint8_t* srow = stg + lane * D;
     int cur_cell = -1;
-    for (int it = 0; it < n_my; ++it) {
+    for (int it = 0;; ++it) {
       const int ac = it & 1;
-      const int64_t g = tile_begin + it;
+      if (!warp_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x391)) break;
+      const int32_t g = sched::ring_get(ring, it);
+      if (g < 0) break;
       const int cell = (int)(g / A.tiles_per_cell);
       const int64_t tile = g % A.tiles_per_cell;
-      const int h = (int)(tile / A.tb_per_head);
-      const int64_t i0 = (tile % A.tb_per_head) * TILE_M + half * 64;  // first token (within [t0, t1)) of this half
-      if (cell != cur_cell) {
-        if (A.rt > 0 && active)
-#pragma unroll
-          for (int r = 0; r < RDM; ++r)
-            u[r] = r < A.rd ? load_dt(A.ud.p[cell], (int64_t)feat * A.rd + r, A.factor_dtype) : 0.f;
+      const int64_t h = tile / A.tb_per_head;
+      const int64_t i_tok = (tile % A.tb_per_head) * TILE_M + rloc;  // token within [t0, t1)
+      const bool valid = i_tok < A.tl;
+      const int64_t orow = h * A.tl + i_tok;  // row of the Tucker term
+      if (!FOLD && cell != cur_cell) {
+        __syncwarp();
+        if (A.rt > 0)
+          for (int i = lane; i < (D / 2) * RDM; i += 32) {
+            const int jl = i / RDM, r = i % RDM;
+            us[i] = r < A.rd ? load_dt(A.ud.p[cell], (int64_t)(half * (D / 2) + jl) * A.rd + r, A.factor_dtype)
+                             : 0.f;
+          }
+        __syncwarp();
         cur_cell = cell;
       }
-      // Tucker row terms of the 64 rows (rd = 1): one row per lane, loaded
-      // before the accumulator wait, shared through this warp's slots
-      const float* tp = A.tmp + ((int64_t)cell * A.m * A.tl + (int64_t)h * A.tl) * RDM;
-      float tl0 = 0.f, tl1 = 0.f;
-      if (A.rt > 0 && RDM == 1) {
-        if (i0 + lane < A.tl) tl0 = __ldg(tp + i0 + lane);
-        if (i0 + 32 + lane < A.tl) tl1 = __ldg(tp + i0 + 32 + lane);
-      }
-      if (!warp_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x311)) break;
+      float tv[RDM];  // this row's Tucker term (rd > 1), loaded before the wait
+#pragma unroll
+      for (int r = 0; r < RDM; ++r)
+        tv[r] = (!FOLD && valid && A.rt > 0) ? __ldg(A.tmp + ((int64_t)cell * A.m * A.tl + orow) * RDM + r) : 0.f;
       tc_fence_after();
-      uint8_t* buf = ost + (it & 1) * L::O_BUF;
-      if (active) {
-        if (lane == 0) bulk_wait_read<1>();
-        rst[lane] = tl0;
-        rst[32 + lane] = tl1;
-        __syncwarp();
-      }
+      // the previous tile's store has read the staging rows
+      if (lane == 0) bulk_wait_read<0>();
+      __syncwarp();
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
+      for (int cc = 0; cc < NCH; ++cc) {
+        const int c = half * NCH + cc;
         float v[32];
-        tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * TILE_M + half * 64 + cc * 32), v);
-        if (!active) continue;
-        uint16_t* ob = reinterpret_cast<uint16_t*>(buf) + cc * 32 * 32 + lane;
-        if (A.rt > 0 && RDM == 1) {
-          // out = bf16(fl(t * u) + v): the reference adds the fp32 Tucker
-          // reconstruction to the fp32 decoded residual
-          const float4* t4 = reinterpret_cast<const float4*>(rst + cc * 32);
-          const uint64_t U2 = f2_pack(u[0], u[0]);
+        tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * D + c * 32), v);
+        uint32_t o[16];
+        if (FOLD) {
+          // the accumulator already holds residual + Tucker term
 #pragma unroll
-          for (int q = 0; q < 8; ++q) {
-            const float4 t = t4[q];
-            float o0, o1, o2, o3;
-            f2_unpack(f2_add(f2_mul(f2_pack(t.x, t.y), U2), f2_pack(v[4 * q], v[4 * q + 1])), o0, o1);
-            f2_unpack(f2_add(f2_mul(f2_pack(t.z, t.w), U2), f2_pack(v[4 * q + 2], v[4 * q + 3])), o2, o3);
-            ob[(4 * q) * 32] = __bfloat16_as_ushort(__float2bfloat16_rn(o0));
-            ob[(4 * q + 1) * 32] = __bfloat16_as_ushort(__float2bfloat16_rn(o1));
-            ob[(4 * q + 2) * 32] = __bfloat16_as_ushort(__float2bfloat16_rn(o2));
-            ob[(4 * q + 3) * 32] = __bfloat16_as_ushort(__float2bfloat16_rn(o3));
+          for (int j = 0; j < 32; j += 2) {
+            const __nv_bfloat162 hh = __floats2bfloat162_rn(v[j], v[j + 1]);
+            o[j / 2] = *reinterpret_cast<const uint32_t*>(&hh);
           }
         } else {
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float o = v[j];
-            if (A.rt > 0) {
-              const int64_t i = i0 + cc * 32 + j;
-              float rec = 0.f;
-              if (i < A.tl)
+          for (int j = 0; j < 32; j += 2) {
+            float oo[2];
 #pragma unroll
-                for (int r = 0; r < RDM; ++r) rec = fmaf(__ldg(tp + i * RDM + r), u[r], rec);
-              o = __fadd_rn(rec, v[j]);
+            for (int x = 0; x < 2; ++x) {
+              if (A.rt > 0) {
+                const int f = cc * 32 + j + x;
+                float rec = 0.f;
+                if (RDM == 1) {
+                  rec = tv[0] * us[f];
+                } else {
+                  const float4* u4 = reinterpret_cast<const float4*>(us + f * RDM);
+#pragma unroll
+                  for (int r4 = 0; r4 < RDM / 4; ++r4) {
+                    const float4 u = u4[r4];
+                    rec = fmaf(tv[4 * r4], u.x, rec);
+                    rec = fmaf(tv[4 * r4 + 1], u.y, rec);
+                    rec = fmaf(tv[4 * r4 + 2], u.z, rec);
+                    rec = fmaf(tv[4 * r4 + 3], u.w, rec);
+                  }
+                }
+                oo[x] = __fadd_rn(rec, v[j + x]);
+              } else {
+                oo[x] = v[j + x];
+              }
             }
-            ob[j * 32] = __bfloat16_as_ushort(__float2bfloat16_rn(o));
+            const __nv_bfloat162 hh = __floats2bfloat162_rn(oo[0], oo[1]);
+            o[j / 2] = *reinterpret_cast<const uint32_t*>(&hh);
           }
         }
-      }
-      if (active) {
-        fence_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          if (i0 < A.tl) tma_store_3d(&omaps.m[cell], lg * 32, (int)i0, h, smem_u32(buf));
-          bulk_commit();
-        }
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          *reinterpret_cast<uint4*>(srow + (((cc * 4 + q) ^ swz) << 4)) =
+              make_uint4(o[4 * q], o[4 * q + 1], o[4 * q + 2], o[4 * q + 3]);
       }
       tc_fence_before();
       mbar_arrive(&acce[ac]);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        // rows at or past tl are clipped by the store
+        const int i0 = (int)((tile % A.tb_per_head) * TILE_M + lg * 32);
+        tma_store_3d(&omaps.m[cell], half * (D / 2), i0, (int)h, smem_u32(stg));
+        bulk_commit();
+      }
     }
-    if (lane == 0) bulk_wait<0>();
+    if (lane == 0) bulk_wait<0>();  // shared memory outlives the stores
     __syncwarp();
   }
   tc_fence_before();
@@ -856,26 +1252,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
 }
 
-// A rows of the decode, per cell: A[n][k] = scale[k] * Pi[k][n] in two bf16
-// terms as 32-bit pairs [cell][term][n < 128][d / 2]; rows n >= d are zero.
-__global__ void prep_decode_kernel(const float* __restrict__ proj, CellPtrs scale, int d, uint32_t* out) {
+// B images of the decode, per cell: B[n][k] = scale[k] * Pi[k][n] in two
+// bf16 terms, swizzled K-major [cell][term] (D[row][n] = sum_k q[row][k] B[n][k]),
+// then (rd = 1) the Tucker block B[n][k] for k < 64: u_feature[n] split
+// hi + lo at k = 0-2 and 3-5 (the A side holds t_row split hi + mid + lo
+// twice), zero elsewhere; zero throughout when there is no Tucker term.
+__global__ void prep_decode_kernel(const float* __restrict__ proj, CellPtrs scale, CellPtrs ufeat, int fdt,
+                                   int tucker_block, int d, uint8_t* out, unsigned long long* sched_w, int nctas,
+                                   int64_t per_cta, int64_t total) {
   const int cell = blockIdx.y;
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;  // (n, w) over 128 x d/2
-  const int wpr = d / 2;
-  if (e >= 128 * wpr) return;
-  const int n = e / wpr, w = e % wpr;
-  const float* sc = static_cast<const float*>(scale.p[cell]);
-  float r0 = 0.f, r1 = 0.f;
-  if (n < d) {
-    r0 = __fmul_rn(sc[2 * w], proj[(int64_t)(2 * w) * d + n]);
-    r1 = __fmul_rn(sc[2 * w + 1], proj[(int64_t)(2 * w + 1) * d + n]);
-  }
-  uint32_t* base = out + (size_t)cell * 2 * 128 * wpr;
-  for (int term = 0; term < 2; ++term) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(r0, r1);
-    r0 -= __low2float(h);
-    r1 -= __high2float(h);
-    base[((size_t)term * 128 + n) * wpr + w] = *reinterpret_cast<const uint32_t*>(&h);
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;
+  if (cell == 0) sched::init_ranges(sched_w, e, nctas, per_cta, total);
+  const size_t per_cell = (size_t)2 * d * d * 2 + (tucker_block ? (size_t)d * 128 : 0);
+  uint8_t* base = out + (size_t)cell * per_cell;
+  if (e < d * d) {
+    const int n = e / d, k = e % d;
+    const float sk = static_cast<const float*>(scale.p[cell])[k];
+    float rest = __fmul_rn(sk, proj[(int64_t)k * d + n]);
+    for (int term = 0; term < 2; ++term) {
+      const __nv_bfloat16 v = __float2bfloat16_rn(rest);
+      rest -= __bfloat162float(v);
+      *reinterpret_cast<__nv_bfloat16*>(base + (size_t)term * d * d * 2 + sw128_off(n, k, d)) = v;
+    }
+  } else if (tucker_block && e < d * d + d * 64) {
+    const int n = (e - d * d) / 64, k = (e - d * d) % 64;
+    float v = 0.f;
+    if (k < 6 && ufeat.p[cell]) {
+      const float u = load_dt(ufeat.p[cell], n, fdt);
+      const float hi = __bfloat162float(__float2bfloat16_rn(u));
+      v = k < 3 ? hi : u - hi;
+    }
+    *reinterpret_cast<__nv_bfloat16*>(base + (size_t)2 * d * d * 2 + sw128_off(n, k, d)) = __float2bfloat16_rn(v);
   }
 }
 
@@ -898,7 +1305,8 @@ bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale
 size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd) {
   const int64_t rows_pad = ceil_div(rows, TILE_M) * TILE_M;
   return align256((size_t)3 * 128 * (d / 2) * 4) + align256((size_t)n_cells * 2 * d * sizeof(int32_t)) +
-         align256((size_t)n_cells * rows_pad * rdm_enc(rd) * 4);
+         align256((size_t)n_cells * rows_pad * rdm_enc(rd) * 4) + align256((size_t)n_cells * 3 * d * d * 2) +
+         kSchedBytes;
 }
 
 int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
@@ -916,6 +1324,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   EncArgs a;
   memset(&a, 0, sizeof(a));
   memset(&cmaps, 0, sizeof(cmaps));
+  const int cbw = (d / 2) * bits / 8;  // code bytes of half a row (one epilogue warp)
   const int cb = (d * bits + 7) / 8;
   int rc;
   for (int c = 0; c < n_cells; ++c) {
@@ -925,14 +1334,15 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
     if ((rc = encode_tma(&xmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x[c], dims, strides, box,
                          CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc;
-    if (mode == 1 && bits > 2) {
-      // codes of 64 rows x 32 features: 4 * bits bytes per row
+    if (mode == 1 && cbw >= 16) {
+      // codes of 32 rows x half a row, swizzled by the half-row width
       const uint64_t cd[2] = {(uint64_t)cb, (uint64_t)rows};
       const uint64_t cs[1] = {(uint64_t)cb};
-      const uint32_t cbx[2] = {(uint32_t)(4 * bits), 64u};
-      if ((rc = encode_tma(&cmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, codes[c], cd, cs, cbx,
-                           CU_TENSOR_MAP_SWIZZLE_NONE)))
-        return rc;
+      const uint32_t cbx[2] = {(uint32_t)cbw, 32u};
+      const CUtensorMapSwizzle sw = cbw == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                    : cbw == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                                : CU_TENSOR_MAP_SWIZZLE_NONE;
+      if ((rc = encode_tma(&cmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, codes[c], cd, cs, cbx, sw))) return rc;
     }
     if (rt > 0) a.ud.p[c] = u_feature[c];
     if (scale) a.scale.p[c] = scale[c];
@@ -949,7 +1359,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   a.code_bytes = cb;
   a.tiles_per_cell = ceil_div(rows, TILE_M);
   a.total_tiles = a.tiles_per_cell * n_cells;
-  const int64_t ctas = std::min<int64_t>(a.total_tiles, num_sms());
+  const int64_t ctas = std::min<int64_t>(std::min<int64_t>(a.total_tiles, num_sms()), kMaxCtas);
   a.tiles_per_cta = ceil_div(a.total_tiles, ctas);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
   uint32_t* arows = reinterpret_cast<uint32_t*>(ws);
@@ -957,11 +1367,27 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   int32_t* mm = reinterpret_cast<int32_t*>(ws + off);
   off += align256((size_t)n_cells * 2 * d * sizeof(int32_t));
   float* tmp = reinterpret_cast<float*>(ws + off);
+  off += align256((size_t)n_cells * a.tiles_per_cell * TILE_M * rdm * 4);
+  uint8_t* bimg = ws + off;  // quantise: n_cells x 3 x d x d bf16
+  off += align256((size_t)n_cells * 3 * d * d * 2);
+  a.sched = reinterpret_cast<unsigned long long*>(ws + off);
   a.arows = arows;
   a.minmax = mm;
   a.tmp = tmp;
-  prep_rotation_kernel<<<(128 * (d / 2) + 255) / 256, 256, 0, st>>>(proj, d, arows);
-  if ((rc = check_launch("prep_rotation_kernel"))) return rc;
+  // the stats pass takes Pi as TMEM rows, the quantise pass Pi / s of each
+  // cell as shared-memory B images
+  if (mode == 0) {
+    prep_rotation_kernel<<<(128 * (d / 2) + 255) / 256, 256, 0, st>>>(proj, d, arows);
+    if ((rc = check_launch("prep_rotation_kernel"))) return rc;
+  } else {
+    CellPtrs sp;
+    for (int c = 0; c < n_cells; ++c) sp.p[c] = scale[c];
+    const int fold = scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32;
+    prep_quant_b_kernel<<<dim3((std::max(d * d, kMaxCtas) + 255) / 256, n_cells), 256, 0, st>>>(
+        proj, sp, scale_mode == KVC_SCALE_CHANNEL, fold, d, bimg, a.sched,
+        (int)ceil_div(a.total_tiles, a.tiles_per_cta), a.tiles_per_cta, a.total_tiles);
+    if ((rc = check_launch("prep_quant_b_kernel"))) return rc;
+  }
   if (rt > 0) {
     CellPtrs cp, up;
     for (int c = 0; c < n_cells; ++c) {
@@ -978,39 +1404,47 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
     minmax_init_kernel<<<(n_cells * 2 * d + 255) / 256, 256, 0, st>>>(mm, n_cells, d);
     if ((rc = check_launch("minmax_init_kernel"))) return rc;
   }
-#define KVC_TC_ENC(DD, MODEV, SYMV, RR, NSV)                     \
-  do {                                                           \
-    auto kern = tc_encode_kernel<DD, MODEV, SYMV, RR, NSV>;      \
-    constexpr size_t sm = EncLayout<DD, RR, NSV, MODEV>::BYTES;  \
-    if ((rc = set_smem(kern, sm))) return rc;                    \
-    kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a);           \
-  } while (0)
-#define KVC_TC_ENC_R(DD, MODEV, SYMV, NSV)              \
+#define KVC_TC_STATS(DD, SYMV, RR, NSV)                 \
   do {                                                  \
-    if (rdm == 1) KVC_TC_ENC(DD, MODEV, SYMV, 1, NSV);  \
-    else KVC_TC_ENC(DD, MODEV, SYMV, 4, NSV);           \
+    auto kern = tc_stats_kernel<DD, SYMV, RR, NSV>;     \
+    constexpr size_t sm = StatsLayout<DD, RR, NSV>::BYTES; \
+    if ((rc = set_smem(kern, sm))) return rc;           \
+    kern<<<grid, NTHREADS, sm, st>>>(xmaps, a);         \
+  } while (0)
+#define KVC_TC_QUANT(DD, SYMV, RR, NSV)                                          \
+  do {                                                                           \
+    auto kern = tc_quant_kernel<DD, SYMV, RR, NSV>;                              \
+    constexpr size_t sm = QuantLayout<DD, RR, NSV>::BYTES;                       \
+    if ((rc = set_smem(kern, sm))) return rc;                                    \
+    kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, bimg);                     \
+  } while (0)
+#define KVC_TC_ENC_R(WHICH, DD, SYMV, NSV)     \
+  do {                                         \
+    if (rdm == 1) WHICH(DD, SYMV, 1, NSV);     \
+    else WHICH(DD, SYMV, 4, NSV);              \
   } while (0)
   const bool sym = symmetric != 0;
   if (mode == 0) {
     if (d == 128) {
-      if (sym) KVC_TC_ENC_R(128, MODE_STATS, true, 6);
-      else KVC_TC_ENC_R(128, MODE_STATS, false, 6);
+      if (sym) KVC_TC_ENC_R(KVC_TC_STATS, 128, true, 6);
+      else KVC_TC_ENC_R(KVC_TC_STATS, 128, false, 6);
     } else {
-      if (sym) KVC_TC_ENC_R(64, MODE_STATS, true, 8);
-      else KVC_TC_ENC_R(64, MODE_STATS, false, 8);
+      if (sym) KVC_TC_ENC_R(KVC_TC_STATS, 64, true, 8);
+      else KVC_TC_ENC_R(KVC_TC_STATS, 64, false, 8);
     }
   } else {
     if (d == 128) {
-      if (sym) KVC_TC_ENC_R(128, MODE_QUANT, true, 5);
-      else KVC_TC_ENC_R(128, MODE_QUANT, false, 5);
+      if (sym) KVC_TC_ENC_R(KVC_TC_QUANT, 128, true, 3);
+      else KVC_TC_ENC_R(KVC_TC_QUANT, 128, false, 3);
     } else {
-      if (sym) KVC_TC_ENC_R(64, MODE_QUANT, true, 8);
-      else KVC_TC_ENC_R(64, MODE_QUANT, false, 8);
+      if (sym) KVC_TC_ENC_R(KVC_TC_QUANT, 64, true, 6);
+      else KVC_TC_ENC_R(KVC_TC_QUANT, 64, false, 6);
     }
   }
 #undef KVC_TC_ENC_R
-#undef KVC_TC_ENC
-  if ((rc = check_launch("tc_encode_kernel"))) return rc;
+#undef KVC_TC_QUANT
+#undef KVC_TC_STATS
+  if ((rc = check_launch(mode == 0 ? "tc_stats_kernel" : "tc_quant_kernel"))) return rc;
   if (mode == 0) {
     CellPtrsMut sc, zz;
     for (int c = 0; c < n_cells; ++c) {
@@ -1030,7 +1464,8 @@ bool tc_decompress_eligible(int out_dtype, int d, int rd, int bits, int symmetri
 }
 
 size_t tc_decompress_workspace(int n_cells, int64_t rows, int d, int rd) {
-  return align256((size_t)n_cells * 2 * 128 * (d / 2) * 4) + align256((size_t)n_cells * rows * rdm_dec(rd) * 4);
+  const size_t bimg = (size_t)n_cells * ((size_t)4 * d * d + (rdm_dec(rd) == 1 ? (size_t)128 * d : 0));
+  return align256(bimg) + align256((size_t)n_cells * rows * rdm_dec(rd) * 4 + 132 * 4) + kSchedBytes;
 }
 
 int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* const* scale, int bits,
@@ -1054,17 +1489,24 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
     const uint64_t dims[3] = {(uint64_t)cb, (uint64_t)t, (uint64_t)m};
     const uint64_t strides[2] = {(uint64_t)cb, (uint64_t)cb * t};
     const uint32_t box[3] = {(uint32_t)cb, (uint32_t)TILE_M, 1u};
-    if ((rc = encode_tma(&cmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, codes[c], dims, strides, box,
-                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+    // rows of 32 / 64 / 128 B take the swizzle of their width (the kernel
+    // reads chunk c of row r at c ^ ((r * cb / 128) mod (cb / 16)))
+    const CUtensorMapSwizzle swz = cb == 128  ? CU_TENSOR_MAP_SWIZZLE_128B
+                                   : cb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
+                                   : cb == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                              : CU_TENSOR_MAP_SWIZZLE_NONE;
+    if ((rc = encode_tma(&cmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, codes[c], dims, strides, box, swz)))
       return rc;
-    // output (m, tl, d) bf16: boxes of 32 features x 64 tokens
+    // output (m, tl, d) bf16: boxes of d/2 features x 32 tokens, swizzled by
+    // their d-byte rows
     const uint64_t od[3] = {(uint64_t)d, (uint64_t)tl, (uint64_t)m};
     const uint64_t os[2] = {(uint64_t)d * 2, (uint64_t)d * 2 * tl};
-    const uint32_t ob[3] = {32u, 64u, 1u};
+    const uint32_t ob[3] = {(uint32_t)(d / 2), 32u, 1u};
     if ((rc = encode_tma(&omaps.m[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out[c], od, os, ob,
-                         CU_TENSOR_MAP_SWIZZLE_NONE)))
+                         d == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
       return rc;
     sc.p[c] = scale[c];
+    a.out.p[c] = out[c];
     if (rt > 0) a.ud.p[c] = u_feature[c];
   }
   a.m = m;
@@ -1073,17 +1515,24 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
   a.tb_per_head = (int)ceil_div(tl, TILE_M);
   a.tiles_per_cell = m * a.tb_per_head;
   a.total_tiles = a.tiles_per_cell * n_cells;
-  const int64_t ctas = std::min<int64_t>(a.total_tiles, num_sms());
+  const int64_t ctas = std::min<int64_t>(std::min<int64_t>(a.total_tiles, num_sms()), kMaxCtas);
   a.tiles_per_cta = ceil_div(a.total_tiles, ctas);
   a.rt = rt;
   a.rd = rd;
   a.factor_dtype = factor_dtype;
-  uint32_t* arows = static_cast<uint32_t*>(workspace);
-  float* tmp = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) +
-                                        align256((size_t)n_cells * 2 * 128 * (d / 2) * 4));
-  a.arows = arows;
+  const int tucker_block = rdm == 1;
+  uint8_t* bimg = static_cast<uint8_t*>(workspace);
+  float* tmp = reinterpret_cast<float*>(
+      bimg + align256((size_t)n_cells * ((size_t)4 * d * d + (tucker_block ? (size_t)128 * d : 0))));
+  a.bimg = bimg;
   a.tmp = tmp;
-  prep_decode_kernel<<<dim3((128 * (d / 2) + 255) / 256, n_cells), 256, 0, st>>>(proj, sc, d, arows);
+  a.sched = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(tmp) +
+                                                  align256((size_t)n_cells * m * t * rdm * 4 + 132 * 4));
+  CellPtrs uf;
+  for (int c = 0; c < n_cells; ++c) uf.p[c] = rt > 0 ? u_feature[c] : nullptr;
+  prep_decode_kernel<<<dim3((std::max(d * d + d * 64, kMaxCtas) + 255) / 256, n_cells), 256, 0, st>>>(
+      proj, sc, uf, factor_dtype, tucker_block, d, bimg, a.sched, (int)ceil_div(a.total_tiles, a.tiles_per_cta),
+      a.tiles_per_cta, a.total_tiles);
   if ((rc = check_launch("prep_decode_kernel"))) return rc;
   if (rt > 0) {
     CellPtrs cp, up;
@@ -1099,8 +1548,8 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
   const dim3 grid((unsigned)ceil_div(a.total_tiles, a.tiles_per_cta));
 #define KVC_TC_DEC3(DD, RR, BB)                                      \
   do {                                                               \
-    auto kern = tc_decode_kernel<DD, RR, BB, 3>;                     \
-    using LL = DecLayout<DD, DD * BB / 8, 3>;                        \
+    auto kern = tc_decode_kernel<DD, RR, BB, 4>;                     \
+    using LL = DecLayout<DD, DD * BB / 8, RR, 4>;                    \
     if ((rc = set_smem(kern, LL::BYTES))) return rc;                 \
     kern<<<grid, NTHREADS, LL::BYTES, st>>>(cmaps, omaps, a);        \
   } while (0)

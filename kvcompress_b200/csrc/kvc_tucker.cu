@@ -9,6 +9,7 @@
 #include <algorithm>
 
 #include "kvc_common.cuh"
+#include "kvc_tc.cuh"
 
 namespace kvc {
 namespace {
@@ -167,6 +168,60 @@ __global__ void __launch_bounds__(256) project_small_kernel(CellPtrs X, CellPtrs
   }
 }
 
+// x_proj for bf16 cells with rd == 1 and d = 8 * LPR: LPR lanes per row,
+// each holding 8 values as 4 packed pairs; fp32 accumulation in packed
+// pairs (even / odd elements), then a butterfly over the row's lanes.
+// Four rows per thread in flight.
+template <int LPR>
+__global__ void __launch_bounds__(256) project_rd1_bf16_kernel(CellPtrs X, CellPtrs U, int64_t rows, int d,
+                                                              int64_t T_, int m, CellPtrsMut out) {
+  constexpr int UNROLL = 4;
+  const int cell = blockIdx.y;
+  const uint4* x = static_cast<const uint4*>(X.p[cell]);
+  const uint16_t* u = static_cast<const uint16_t*>(U.p[cell]);
+  __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out.p[cell]);
+  const int lane = threadIdx.x & 31;
+  const int pos = lane % LPR;
+  // this lane's 8 entries of u_feature (a column of d), as packed fp32 pairs
+  uint64_t u2[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const float lo = __uint_as_float((uint32_t)u[pos * 8 + 2 * q] << 16);
+    const float hi = __uint_as_float((uint32_t)u[pos * 8 + 2 * q + 1] << 16);
+    u2[q] = tc::f2_pack(lo, hi);
+  }
+  const int64_t groups = (int64_t)gridDim.x * (blockDim.x / LPR);
+  const int64_t warp_gid = (int64_t)blockIdx.x * (blockDim.x / LPR) + (threadIdx.x & ~31) / LPR;
+  const int rows_per_chunk = d / 8;  // uint4 per row
+  for (int64_t wbase = warp_gid; wbase < rows; wbase += groups * UNROLL) {  // warp-uniform bound
+    const int64_t base = wbase + lane / LPR;
+    uint4 raw[UNROLL];
+#pragma unroll
+    for (int q = 0; q < UNROLL; ++q) {
+      const int64_t row = base + q * groups;
+      raw[q] = row < rows ? __ldg(x + row * rows_per_chunk + pos) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int q = 0; q < UNROLL; ++q) {
+      const uint32_t w[4] = {raw[q].x, raw[q].y, raw[q].z, raw[q].w};
+      uint64_t acc = tc::f2_pack(0.f, 0.f);
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        acc = tc::f2_fma(tc::f2_pack(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u)), u2[i], acc);
+      float a0, a1;
+      tc::f2_unpack(acc, a0, a1);
+      float sum = a0 + a1;
+#pragma unroll
+      for (int off = LPR / 2; off > 0; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+      const int64_t row = base + q * groups;
+      if (pos == 0 && row < rows) {
+        const int64_t h = row / T_, t = row % T_;
+        o[t * m + h] = __float2bfloat16_rn(sum);
+      }
+    }
+  }
+}
+
 // out (rows x N) = round_T(A (rows x K) * M (K x N)) for K <= 64, N <= 16:
 // one thread per row, M in shared memory as float, fp32 accumulation in k
 // order (the same arithmetic as rowmat_kernel).
@@ -221,6 +276,15 @@ extern "C" int kvc_project_feature(int n_cells, const void* const* x, int64_t m,
   const int lpr = (int)(d * dtype_size(dtype) / 16);
   bool aligned = (d * dtype_size(dtype)) % 16 == 0;
   for (int c = 0; c < n_cells; ++c) aligned = aligned && (reinterpret_cast<uintptr_t>(x[c]) & 15u) == 0;
+  if (rd == 1 && dtype == KVC_BF16 && aligned && (lpr == 8 || lpr == 16)) {
+    const int64_t per_block = 256 / lpr * 4;
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, per_block),
+                                                                    ceil_div(8LL * num_sms(), n_cells)));
+    dim3 grid(blocks, n_cells);
+    if (lpr == 8) project_rd1_bf16_kernel<8><<<grid, 256, 0, st>>>(xa, ub, rows, d, t, (int)m, o);
+    else project_rd1_bf16_kernel<16><<<grid, 256, 0, st>>>(xa, ub, rows, d, t, (int)m, o);
+    return check_launch("project_rd1_bf16_kernel");
+  }
   if (rd <= 4 && aligned && (lpr == 8 || lpr == 16 || lpr == 32)) {
     const int64_t per_block = 256 / lpr * 4;
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, per_block),
