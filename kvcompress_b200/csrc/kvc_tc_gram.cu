@@ -24,6 +24,7 @@
 #include <algorithm>
 
 #include "kvc_common.cuh"
+#include "kvc_sched.cuh"
 #include "kvc_tc.cuh"
 #include "kvc_tma.cuh"
 
@@ -46,7 +47,8 @@ struct GLayout {
   static constexpr uint32_t X_BYTES = TILE * D * 2;   // 32 KB
   static constexpr uint32_t O_BYTES = TILE * NY * 2;  // 16 KB
   static constexpr uint32_t STAGE = X_BYTES + O_BYTES;
-  static constexpr uint32_t OFF_BAR = NS * STAGE;
+  static constexpr uint32_t OFF_RING = NS * STAGE;  // segment ids drawn by the producer
+  static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
   static constexpr uint32_t OFF_TM = OFF_BAR + (2 * NS + 4) * 8;
   static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;
 };
@@ -58,30 +60,10 @@ struct GramArgs {
   float* partial;  // [segment][D][NACC]
 };
 
-// Walks the tiles of a run of segments in order.
-struct SegCursor {
-  int64_t s, t;  // segment, tile within the segment
-  __device__ __forceinline__ int64_t len(const GramArgs& A) const {
-    const int64_t first = (s % A.segs_per_cell) * A.seg_tiles;
-    return A.tiles_per_cell - first < A.seg_tiles ? A.tiles_per_cell - first : A.seg_tiles;
-  }
-  __device__ __forceinline__ int cell(const GramArgs& A) const { return (int)(s / A.segs_per_cell); }
-  __device__ __forceinline__ int64_t tile(const GramArgs& A) const {
-    return (s % A.segs_per_cell) * A.seg_tiles + t;
-  }
-  __device__ __forceinline__ void next(const GramArgs& A) {
-    if (++t == len(A)) {
-      ++s;
-      t = 0;
-    }
-  }
-};
-
-// Tiles before segment s in the global order.
-__host__ __device__ inline int64_t tiles_before(int64_t s, int64_t segs_per_cell, int64_t seg_tiles,
-                                                int64_t tiles_per_cell) {
-  const int64_t c = s / segs_per_cell, r = (s % segs_per_cell) * seg_tiles;
-  return c * tiles_per_cell + (r < tiles_per_cell ? r : tiles_per_cell);
+// Tiles in segment s (the last segment of a cell may be short).
+__device__ __forceinline__ int seg_len(const GramArgs& A, int64_t s) {
+  const int64_t first = (s % A.segs_per_cell) * A.seg_tiles;
+  return (int)(A.tiles_per_cell - first < A.seg_tiles ? A.tiles_per_cell - first : A.seg_tiles);
 }
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
@@ -101,6 +83,9 @@ __device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) 
   return d;
 }
 
+// Work unit: one segment (seg_tiles consecutive tiles of a cell), summed
+// into its own fp32 partial, so the sums do not depend on which CTA made
+// them; each CTA takes a contiguous range of segments (kvc_sched.cuh).
 __global__ void __launch_bounds__(NTH, 1)
     tc_gram_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ CUtensorMap omap,
                    const __grid_constant__ GramArgs A) {
@@ -112,11 +97,8 @@ __global__ void __launch_bounds__(NTH, 1)
   uint64_t* accf = empty + NS;
   uint64_t* acce = accf + 2;
   uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + GLayout::OFF_TM);
+  int32_t* ring = reinterpret_cast<int32_t*>(smem + GLayout::OFF_RING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int64_t s_begin = (int64_t)blockIdx.x * A.total_segs / gridDim.x;
-  const int64_t s_end = (int64_t)(blockIdx.x + 1) * A.total_segs / gridDim.x;
-  const int n_my = (int)(tiles_before(s_end, A.segs_per_cell, A.seg_tiles, A.tiles_per_cell) -
-                         tiles_before(s_begin, A.segs_per_cell, A.seg_tiles, A.tiles_per_cell));
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
@@ -141,17 +123,34 @@ __global__ void __launch_bounds__(NTH, 1)
   if (warp == TMA_WARP) {
     // ---------------- TMA producer: x tile (two 64-column boxes) + Omega tile ----------------
     if (lane == 0) {
-      SegCursor ic{s_begin, 0};
-      for (int j = 0; j < n_my; ++j, ic.next(A)) {
-        const int cell = ic.cell(A);
-        const int y = (int)(ic.tile(A) * TILE);
-        const int st = j % NS;
-        if (!mbar_wait(&empty[st], (uint32_t)((j / NS) & 1) ^ 1u, 0x401)) break;
-        mbar_expect_tx(&full[st], GLayout::STAGE);
-        const uint32_t xs = sbase + st * GLayout::STAGE;
-        tma_load_2d(xs, &xmaps.m[cell], 0, y, &full[st]);
-        tma_load_2d(xs + TILE * 128, &xmaps.m[cell], 64, y, &full[st]);
-        tma_load_2d(xs + GLayout::X_BYTES, &omap, 0, y, &full[st]);
+      sched::Cursor cur((A.total_segs + gridDim.x - 1) / gridDim.x, A.total_segs);
+      int j = 0;  // stage uses so far
+      for (int si = 0;; ++si) {
+        const int64_t sg = sched::next_tile(cur);
+        sched::ring_put(ring, si, (int32_t)sg);
+        if (sg < 0) {  // the end, through the next stage with no bytes
+          const int st = j % NS;
+          if (mbar_wait(&empty[st], (uint32_t)((j / NS) & 1) ^ 1u, 0x401)) mbar_arrive(&full[st]);
+          break;
+        }
+        const int cell = (int)(sg / A.segs_per_cell);
+        const int64_t t0 = (sg % A.segs_per_cell) * A.seg_tiles;
+        const int n = seg_len(A, sg);
+        bool ok = true;
+        for (int t = 0; t < n; ++t, ++j) {
+          const int st = j % NS;
+          if (!mbar_wait(&empty[st], (uint32_t)((j / NS) & 1) ^ 1u, 0x401)) {
+            ok = false;
+            break;
+          }
+          const int y = (int)((t0 + t) * TILE);
+          mbar_expect_tx(&full[st], GLayout::STAGE);
+          const uint32_t xs = sbase + st * GLayout::STAGE;
+          tma_load_2d(xs, &xmaps.m[cell], 0, y, &full[st]);
+          tma_load_2d(xs + TILE * 128, &xmaps.m[cell], 64, y, &full[st]);
+          tma_load_2d(xs + GLayout::X_BYTES, &omap, 0, y, &full[st]);
+        }
+        if (!ok) break;
       }
     }
     __syncwarp();
@@ -161,56 +160,72 @@ __global__ void __launch_bounds__(NTH, 1)
       // A = x^T and B = x, both MN-major; D[feature][feature / omega column]
       const uint32_t id_g = idesc_f16(D, D, true) | (1u << 15) | (1u << 16);
       const uint32_t id_y = idesc_f16(D, NY, true) | (1u << 15) | (1u << 16);
-      int seg = -1, it = 0;
-      bool first = true;
-      SegCursor mc{s_begin, 0};
-      for (; it < n_my; ++it, mc.next(A)) {
-        if (mc.t == 0) {
-          if (seg >= 0) umma_commit(&accf[seg & 1]);  // close the previous segment
-          ++seg;
-          if (!mbar_wait(&acce[seg & 1], (uint32_t)((seg >> 1) & 1) ^ 1u, 0x402)) break;
-          tc_fence_after();
-          first = true;
+      int j = 0, si = 0;
+      bool ok = true;
+      for (;; ++si) {
+        // the segment's first stage (or the end marker) orders the ring read
+        if (!mbar_wait(&full[j % NS], (uint32_t)((j / NS) & 1), 0x403)) {
+          ok = false;
+          break;
         }
-        const int st = it % NS;
-        if (!mbar_wait(&full[st], (uint32_t)((it / NS) & 1), 0x403)) break;
+        const int32_t sg = sched::ring_get(ring, si);
+        if (!mbar_wait(&acce[si & 1], (uint32_t)((si >> 1) & 1) ^ 1u, 0x402)) {
+          ok = false;
+          break;
+        }
+        if (sg < 0) {  // the end: the epilogue learns it from the same accumulator barrier
+          umma_commit(&accf[si & 1]);
+          break;
+        }
         tc_fence_after();
-        const uint32_t xs = sbase + st * GLayout::STAGE;
-        const uint32_t os = xs + GLayout::X_BYTES;
-        const uint32_t acc = tmem + (uint32_t)((seg & 1) * 256);
+        const int n = seg_len(A, sg);
+        const uint32_t acc = tmem + (uint32_t)((si & 1) * 256);
+        for (int t = 0; t < n && ok; ++t, ++j) {
+          const int st = j % NS;
+          if (t > 0 && !mbar_wait(&full[st], (uint32_t)((j / NS) & 1), 0x403)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xs = sbase + st * GLayout::STAGE;
+          const uint32_t os = xs + GLayout::X_BYTES;
 #pragma unroll
-        for (int ks = 0; ks < TILE / 16; ++ks) {
-          const uint64_t da = desc_mn_sw128(xs + ks * 2048, TILE * 128);
-          const uint64_t dy = desc_mn_sw128(os + ks * 2048, TILE * 128);
-          const uint32_t accumulate = (first && ks == 0) ? 0u : 1u;
-          umma_f16(acc, da, da, id_g, accumulate);
-          umma_f16(acc + D, da, dy, id_y, accumulate);
+          for (int ks = 0; ks < TILE / 16; ++ks) {
+            const uint64_t da = desc_mn_sw128(xs + ks * 2048, TILE * 128);
+            const uint64_t dy = desc_mn_sw128(os + ks * 2048, TILE * 128);
+            const uint32_t accumulate = (t == 0 && ks == 0) ? 0u : 1u;
+            umma_f16(acc, da, da, id_g, accumulate);
+            umma_f16(acc + D, da, dy, id_y, accumulate);
+          }
+          umma_commit(&empty[st]);
         }
-        first = false;
-        umma_commit(&empty[st]);
+        if (!ok) break;
+        umma_commit(&accf[si & 1]);
       }
-      if (seg >= 0 && it == n_my) umma_commit(&accf[seg & 1]);
-      if (seg >= 0) mbar_wait(&accf[seg & 1], (uint32_t)((seg >> 1) & 1), 0x404);
+      // do not leave while MMAs that write TMEM are still in flight
+      if (ok) mbar_wait(&accf[si & 1], (uint32_t)((si >> 1) & 1), 0x404);
     }
     __syncwarp();
   } else if (warp >= EPI_WARP0) {
     // ---------------- epilogue: flush one segment's accumulator ----------------
     const int lg = warp & 3;
     const int feat = lg * 32 + lane;
-    for (int seg = 0; seg < (int)(s_end - s_begin); ++seg) {
-      if (!__all_sync(0xffffffffu, mbar_wait(&accf[seg & 1], (uint32_t)((seg >> 1) & 1), 0x405))) break;
+    for (int si = 0;; ++si) {
+      if (!__all_sync(0xffffffffu, mbar_wait(&accf[si & 1], (uint32_t)((si >> 1) & 1), 0x405))) break;
+      const int32_t sg = sched::ring_get(ring, si);
+      if (sg < 0) break;
       tc_fence_after();
-      float* dst = A.partial + ((s_begin + seg) * D + feat) * NACC;
+      float* dst = A.partial + ((int64_t)sg * D + feat) * NACC;
 #pragma unroll
       for (int c = 0; c < NACC / 32; ++c) {
         float v[32];
-        tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)((seg & 1) * 256 + c * 32), v);
+        tmem_ld32(tmem + ((uint32_t)(lg * 32) << 16) + (uint32_t)((si & 1) * 256 + c * 32), v);
 #pragma unroll
         for (int q = 0; q < 8; ++q)
           reinterpret_cast<float4*>(dst + c * 32)[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
       }
       tc_fence_before();
-      mbar_arrive(&acce[seg & 1]);
+      mbar_arrive(&acce[si & 1]);
     }
   }
   tc_fence_before();
@@ -273,7 +288,7 @@ GPlan gplan(int n_cells, int64_t rows) {
   p.seg_tiles = std::min<int64_t>(p.tiles_per_cell, std::min<int64_t>(32, std::max<int64_t>(4, ceil_div(p.tiles_per_cell, 16))));
   p.segs_per_cell = ceil_div(p.tiles_per_cell, p.seg_tiles);
   p.total_segs = p.segs_per_cell * n_cells;
-  p.ctas = (int)std::min<int64_t>(p.total_segs, num_sms());
+  p.ctas = (int)std::min<int64_t>(std::min<int64_t>(p.total_segs, num_sms()), 1024);
   return p;
 }
 
@@ -286,15 +301,17 @@ static size_t partial_bytes(int n_cells, const GPlan& p) {
   return ((size_t)p.total_segs * D * NACC * sizeof(float) + 255) & ~(size_t)255;
 }
 
+static size_t opad_bytes(int64_t rows) { return ((size_t)rows * NY * 2 + 255) & ~(size_t)255; }
+
 size_t tc_gram_workspace(int n_cells, int64_t rows) {
   GPlan p = gplan(n_cells, rows);
-  return partial_bytes(n_cells, p) + (size_t)rows * NY * 2;
+  return partial_bytes(n_cells, p) + opad_bytes(rows);
 }
 
 int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float* omega, int k, double* out,
                    void* workspace, size_t ws_bytes, cudaStream_t st) {
   GPlan p = gplan(n_cells, rows);
-  if (!workspace || ws_bytes < partial_bytes(n_cells, p) + (size_t)rows * NY * 2)
+  if (!workspace || ws_bytes < tc_gram_workspace(n_cells, rows))
     return fail(KVC_ERR_WORKSPACE, "tensor-core gram: workspace too small");
   if (rows >= (1LL << 31)) return fail(KVC_ERR_SHAPE, "tensor-core gram: more than 2^31 rows per cell");
   GramArgs g;

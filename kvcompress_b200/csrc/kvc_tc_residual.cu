@@ -129,7 +129,8 @@ struct StatsLayout {
   static constexpr uint32_t U_BYTES = RDM == 1 ? D * 2 : D * 16;  // u_feature: bf16 [j] or fp32 [j][4]
   static constexpr uint32_t OFF_T = NS * B_BYTES;
   static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
-  static constexpr uint32_t OFF_BAR = OFF_U + 4 * U_BYTES;
+  static constexpr uint32_t OFF_RING = OFF_U + 4 * U_BYTES;  // tile ids drawn by the producer
+  static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
   static constexpr uint32_t NBAR = 3 * NS + 4;                    // loaded, full, empty, acc full x2, acc empty x2
   static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
   static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;           // + alignment slack
@@ -143,7 +144,6 @@ struct EncArgs {
   const uint32_t* arows;  // A = Pi in three bf16 terms: [term][128 rows][D/2 pairs]
   int32_t* minmax;        // STATS: [cell][2][d] ordered ints (min, max)
   const float* tmp;       // [cell][tiles_per_cell * 128][rdm]: sum_a core[h][a][r] u_token[t][a], bf16-rounded
-  unsigned long long* sched;  // quantise: per-CTA tile ranges (kvc_sched.cuh)
 };
 
 template <int D, bool SYM, int RDM, int NS>
@@ -160,12 +160,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* accf = empty + NS;
   uint64_t* acce = accf + 2;
   uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_TM);
+  int32_t* ring = reinterpret_cast<int32_t*>(smem + L::OFF_RING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  const int64_t tile_begin = (int64_t)blockIdx.x * A.tiles_per_cta;
-  const int64_t tile_end = tile_begin + A.tiles_per_cta < A.total_tiles ? tile_begin + A.tiles_per_cta
-                                                                       : A.total_tiles;
-  const int n_my = (int)(tile_end > tile_begin ? tile_end - tile_begin : 0);
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
@@ -199,11 +195,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     float* u32 = reinterpret_cast<float*>(smem + L::OFF_U + warp * L::U_BYTES);       // [j][4]
     uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + warp * L::U_BYTES);  // [j]
     int cur_cell = -1;
-    for (int it = 0; it < n_my; ++it) {
-      const int64_t g = tile_begin + it;
+    for (int it = 0;; ++it) {
+      const int st = it % NS;
+      if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x131)) break;
+      const int32_t g = sched::ring_get(ring, it);
+      if (g < 0) {  // no more tiles: pass the end on to the MMA thread
+        mbar_arrive(&full[st]);
+        break;
+      }
       const int cell = (int)(g / A.tiles_per_cell);
       const int64_t row = (g % A.tiles_per_cell) * TILE_M + ptid;
-      const int st = it % NS;
       if (A.rt > 0 && cell != cur_cell) {
         __syncwarp();
         const __nv_bfloat16* ud = static_cast<const __nv_bfloat16*>(A.ud.p[cell]);
@@ -218,7 +219,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __syncwarp();
         cur_cell = cell;
       }
-      if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x131)) break;
       if (A.rt > 0 && row < A.rows) {
         uint8_t* Bs = smem + st * L::B_BYTES;
         const float* ts = reinterpret_cast<const float*>(smem + L::OFF_T + st * L::T_BYTES) + ptid * RDM;
@@ -266,12 +266,18 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   } else if (warp == TMA_WARP) {
     // ---------------- TMA producer: x tile (+ Tucker row term) ----------------
     if (lane == 0) {
-      for (int it = 0; it < n_my; ++it) {
-        const int64_t g = tile_begin + it;
-        const int cell = (int)(g / A.tiles_per_cell);
-        const int y = (int)((g % A.tiles_per_cell) * TILE_M);
+      sched::Cursor cur(A.tiles_per_cta, A.total_tiles);
+      for (int it = 0;; ++it) {
+        const int64_t g = sched::next_tile(cur);
+        sched::ring_put(ring, it, (int32_t)g);
         const int st = it % NS;
         if (!mbar_wait(&empty[st], (uint32_t)((it / NS) & 1) ^ 1u, 0x121)) break;
+        if (g < 0) {  // the end: a plain arrive completes the stage with no bytes
+          mbar_arrive(&loaded[st]);
+          break;
+        }
+        const int cell = (int)(g / A.tiles_per_cell);
+        const int y = (int)((g % A.tiles_per_cell) * TILE_M);
         mbar_expect_tx(&loaded[st], L::B_BYTES + (A.rt > 0 ? L::T_BYTES : 0u));
         const uint32_t dst = sbase + st * L::B_BYTES;
 #pragma unroll
@@ -287,10 +293,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (lane == 0) {
       const uint32_t idesc = idesc_f16(128, TILE_M, true);
       int it = 0;
-      for (; it < n_my; ++it) {
+      bool ended = false;
+      for (;; ++it) {
         const int st = it % NS, ac = it & 1;
         if (!mbar_wait(&full[st], (uint32_t)((it / NS) & 1), 0x201)) break;
+        const int32_t g = sched::ring_get(ring, it);
         if (!mbar_wait(&acce[ac], (uint32_t)((it >> 1) & 1) ^ 1u, 0x202)) break;
+        if (g < 0) {  // the end: the epilogue learns it from the same accumulator barrier
+          umma_commit(&accf[ac]);
+          ended = true;
+          break;
+        }
         tc_fence_after();
         const uint32_t b_base = sbase + st * L::B_BYTES;
         const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * TILE_M);
@@ -307,7 +320,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         umma_commit(&accf[ac]);
       }
       // do not leave while MMAs that write TMEM are still in flight
-      if (it > 0) mbar_wait(&accf[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, 0x203);
+      if (ended) mbar_wait(&accf[it & 1], (uint32_t)(it >> 1) & 1u, 0x203);
+      else if (it > 0) mbar_wait(&accf[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, 0x203);
     }
     __syncwarp();
   } else {
@@ -333,16 +347,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     };
     int cur_cell = -1;
-    for (int it = 0; it < n_my; ++it) {
-      const int64_t g = tile_begin + it;
+    for (int it = 0;; ++it) {
+      const int ac = it & 1;
+      if (!warp_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x301)) break;
+      const int32_t g = sched::ring_get(ring, it);
+      if (g < 0) break;
       const int cell = (int)(g / A.tiles_per_cell);
       const int64_t tile = g % A.tiles_per_cell;
       if (cell != cur_cell) {
         if (cur_cell >= 0) flush_stats(cur_cell);
         cur_cell = cell;
       }
-      const int ac = it & 1;
-      if (!warp_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x301)) break;
       tc_fence_after();
       const int64_t row0 = tile * TILE_M + half * 64;  // first row of this warp's half
 #pragma unroll
@@ -411,8 +426,7 @@ int rdm_dec(int rd) { return rd <= 1 ? 1 : (rd <= 4 ? 4 : 16); }
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
-constexpr int kMaxCtas = 1024;                     // grid cap of the persistent kernels
-constexpr size_t kSchedBytes = kMaxCtas * 8;       // one tile-range word per CTA
+constexpr int kMaxCtas = 1024;  // grid cap of the persistent kernels
 
 // min / max arrays to their identities (ordered ints of +inf / -inf).
 __global__ void minmax_init_kernel(int32_t* mm, int n_cells, int d) {
@@ -470,11 +484,9 @@ __global__ void prep_rotation_kernel(const float* __restrict__ proj, int d, uint
 // [cell][term][n][k], so that the MMA yields R~ / s directly (fold = 0 keeps
 // Pi itself, for the per-tensor scales quantised in a 16-bit dtype).
 __global__ void prep_quant_b_kernel(const float* __restrict__ proj, CellPtrs scale, int per_feature, int fold,
-                                    int d, uint8_t* out, unsigned long long* sched_w, int nctas, int64_t per_cta,
-                                    int64_t total) {
+                                    int d, uint8_t* out) {
   const int cell = blockIdx.y;
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (cell == 0) sched::init_ranges(sched_w, e, nctas, per_cta, total);
   if (e >= d * d) return;
   const int n = e / d, k = e % d;
   float rest = proj[e];
@@ -576,9 +588,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const int st = it % NS, b = it & 1;
       if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x171)) break;
       const int32_t tile = sched::ring_get(ring, it);
-      // the MMAs of tile it - 2 read this A buffer last (long done in steady state)
-      if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x172)) break;
       if (tile < 0) {  // no more tiles: pass the end on to the MMA thread
+        if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x172)) break;
         mbar_arrive(&afull[b]);
         break;
       }
@@ -598,39 +609,50 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __syncwarp();
         cur_cell = cell;
       }
-      tc_fence_after();
       const uint8_t* Xs = smem + L::OFF_X + st * L::X_BYTES;
       const bool sub = A.rt > 0 && row < A.rows;
       const uint32_t tm_row = tmem + ((uint32_t)(warp * 32) << 16) + b * ACOLS;
       if (RDM == 1) {
+        // the whole row in registers first, so the x stage goes back to the
+        // producer before this warp waits for its A buffer
         const float* ts = reinterpret_cast<const float*>(smem + L::OFF_T + st * L::T_BYTES) + ptid;
         const uint32_t th = sub ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(ts[0])) : 0u;
         const uint32_t t2 = th | (th << 16);
         const uint4* u4 = reinterpret_cast<const uint4*>(ub);
+        uint32_t r[D / 2];
+#pragma unroll
+        for (int c = 0; c < D / 8; ++c) {
+          uint4 x = *reinterpret_cast<const uint4*>(Xs + sw128_off(ptid, c * 8, TILE_M));
+          if (sub) {
+            // rd == 1: recon = bf16(t * u_j) and R = bf16(x - recon), each a
+            // single rounding of the exact bf16 product / difference
+            const uint4 u = u4[c];
+            x.x = bf16x2_sub(x.x, bf16x2_mul(t2, u.x));
+            x.y = bf16x2_sub(x.y, bf16x2_mul(t2, u.y));
+            x.z = bf16x2_sub(x.z, bf16x2_mul(t2, u.z));
+            x.w = bf16x2_sub(x.w, bf16x2_mul(t2, u.w));
+          }
+          r[4 * c] = x.x;
+          r[4 * c + 1] = x.y;
+          r[4 * c + 2] = x.z;
+          r[4 * c + 3] = x.w;
+        }
+        mbar_arrive(&empty[st]);  // the x stage is no longer needed
+        // the MMAs of tile it - 2 read this A buffer last
+        if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x172)) break;
+        tc_fence_after();
 #pragma unroll
         for (int q = 0; q < (int)ACOLS / 32; ++q) {
-          uint32_t part[32];  // 64 features as bf16 pairs
+          uint32_t part[32];
 #pragma unroll
-          for (int c8 = 0; c8 < 8; ++c8) {
-            const int c = q * 8 + c8;
-            uint4 x = *reinterpret_cast<const uint4*>(Xs + sw128_off(ptid, c * 8, TILE_M));
-            if (sub) {
-              // rd == 1: recon = bf16(t * u_j) and R = bf16(x - recon), each a
-              // single rounding of the exact bf16 product / difference
-              const uint4 u = u4[c];
-              x.x = bf16x2_sub(x.x, bf16x2_mul(t2, u.x));
-              x.y = bf16x2_sub(x.y, bf16x2_mul(t2, u.y));
-              x.z = bf16x2_sub(x.z, bf16x2_mul(t2, u.z));
-              x.w = bf16x2_sub(x.w, bf16x2_mul(t2, u.w));
-            }
-            part[4 * c8] = x.x;
-            part[4 * c8 + 1] = x.y;
-            part[4 * c8 + 2] = x.z;
-            part[4 * c8 + 3] = x.w;
-          }
+          for (int i = 0; i < 32; ++i) part[i] = r[q * 32 + i];
           tmem_st32(tm_row + q * 32, part);
         }
       } else {
+        // rd > 1: 64 features at a time (register pressure); the A buffer
+        // must be free before the first store
+        if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x172)) break;
+        tc_fence_after();
         const float4 tv = sub ? *reinterpret_cast<const float4*>(smem + L::OFF_T + st * L::T_BYTES + ptid * 16)
                               : make_float4(0.f, 0.f, 0.f, 0.f);
         const float4* u4 = reinterpret_cast<const float4*>(u32);
@@ -662,17 +684,17 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           tmem_st32(tm_row + q * 32, part);
         }
+        mbar_arrive(&empty[st]);  // the x stage is no longer needed
       }
-      mbar_arrive(&empty[st]);  // the x stage is no longer needed
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&afull[b]);
     }
   } else if (warp == TMA_WARP) {
     if (lane == 0) {
-      int victim = (int)blockIdx.x;
+      sched::Cursor cur(A.tiles_per_cta, A.total_tiles);
       for (int it = 0;; ++it) {
-        const int64_t tile = sched::next_tile(A.sched, (int)blockIdx.x, (int)gridDim.x, victim);
+        const int64_t tile = sched::next_tile(cur);
         sched::ring_put(ring, it, (int32_t)tile);
         const int st = it % NS;
         if (!mbar_wait(&empty[st], (uint32_t)((it / NS) & 1) ^ 1u, 0x173)) break;
@@ -917,6 +939,17 @@ struct DecLayout {
   static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;
 };
 
+// Deepest codes ring (at most 8 stages) whose layout fits the 227 KB.
+template <int D, int CB, int RDM, int NS = 8>
+struct DecStages {
+  static constexpr int value =
+      DecLayout<D, CB, RDM, NS>::BYTES <= 227 * 1024 ? NS : DecStages<D, CB, RDM, NS - 1>::value;
+};
+template <int D, int CB, int RDM>
+struct DecStages<D, CB, RDM, 2> {
+  static constexpr int value = 2;
+};
+
 struct DecArgsTc {
   CellPtrs ud;
   CellPtrsMut out;
@@ -925,7 +958,6 @@ struct DecArgsTc {
   int rt, rd, factor_dtype;
   const uint8_t* bimg;  // per cell: two swizzled B images of diag(scale) Pi (+ the u_feature block)
   const float* tmp;     // [cell][m * tl][rdm] fp32 Tucker row term (+ 132 floats of slack at the end)
-  unsigned long long* sched;  // per-CTA tile ranges (kvc_sched.cuh)
 };
 
 template <int D, int RDM, int BITS, int NS>
@@ -1060,9 +1092,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
   } else if (warp == TMA_WARP) {
     if (lane == 0) {
-      int victim = (int)blockIdx.x;
+      sched::Cursor cur(A.tiles_per_cta, A.total_tiles);
       for (int it = 0;; ++it) {
-        const int64_t g = sched::next_tile(A.sched, (int)blockIdx.x, (int)gridDim.x, victim);
+        const int64_t g = sched::next_tile(cur);
         sched::ring_put(ring, it, (int32_t)g);
         const int st = it % NS;
         if (!mbar_wait(&empty[st], (uint32_t)((it / NS) & 1) ^ 1u, 0x192)) break;
@@ -1258,11 +1290,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 // hi + lo at k = 0-2 and 3-5 (the A side holds t_row split hi + mid + lo
 // twice), zero elsewhere; zero throughout when there is no Tucker term.
 __global__ void prep_decode_kernel(const float* __restrict__ proj, CellPtrs scale, CellPtrs ufeat, int fdt,
-                                   int tucker_block, int d, uint8_t* out, unsigned long long* sched_w, int nctas,
-                                   int64_t per_cta, int64_t total) {
+                                   int tucker_block, int d, uint8_t* out) {
   const int cell = blockIdx.y;
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  if (cell == 0) sched::init_ranges(sched_w, e, nctas, per_cta, total);
   const size_t per_cell = (size_t)2 * d * d * 2 + (tucker_block ? (size_t)d * 128 : 0);
   uint8_t* base = out + (size_t)cell * per_cell;
   if (e < d * d) {
@@ -1305,8 +1335,7 @@ bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale
 size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd) {
   const int64_t rows_pad = ceil_div(rows, TILE_M) * TILE_M;
   return align256((size_t)3 * 128 * (d / 2) * 4) + align256((size_t)n_cells * 2 * d * sizeof(int32_t)) +
-         align256((size_t)n_cells * rows_pad * rdm_enc(rd) * 4) + align256((size_t)n_cells * 3 * d * d * 2) +
-         kSchedBytes;
+         align256((size_t)n_cells * rows_pad * rdm_enc(rd) * 4) + align256((size_t)n_cells * 3 * d * d * 2);
 }
 
 int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
@@ -1369,8 +1398,6 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   float* tmp = reinterpret_cast<float*>(ws + off);
   off += align256((size_t)n_cells * a.tiles_per_cell * TILE_M * rdm * 4);
   uint8_t* bimg = ws + off;  // quantise: n_cells x 3 x d x d bf16
-  off += align256((size_t)n_cells * 3 * d * d * 2);
-  a.sched = reinterpret_cast<unsigned long long*>(ws + off);
   a.arows = arows;
   a.minmax = mm;
   a.tmp = tmp;
@@ -1383,9 +1410,8 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
     CellPtrs sp;
     for (int c = 0; c < n_cells; ++c) sp.p[c] = scale[c];
     const int fold = scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32;
-    prep_quant_b_kernel<<<dim3((std::max(d * d, kMaxCtas) + 255) / 256, n_cells), 256, 0, st>>>(
-        proj, sp, scale_mode == KVC_SCALE_CHANNEL, fold, d, bimg, a.sched,
-        (int)ceil_div(a.total_tiles, a.tiles_per_cta), a.tiles_per_cta, a.total_tiles);
+    prep_quant_b_kernel<<<dim3((d * d + 255) / 256, n_cells), 256, 0, st>>>(
+        proj, sp, scale_mode == KVC_SCALE_CHANNEL, fold, d, bimg);
     if ((rc = check_launch("prep_quant_b_kernel"))) return rc;
   }
   if (rt > 0) {
@@ -1465,7 +1491,7 @@ bool tc_decompress_eligible(int out_dtype, int d, int rd, int bits, int symmetri
 
 size_t tc_decompress_workspace(int n_cells, int64_t rows, int d, int rd) {
   const size_t bimg = (size_t)n_cells * ((size_t)4 * d * d + (rdm_dec(rd) == 1 ? (size_t)128 * d : 0));
-  return align256(bimg) + align256((size_t)n_cells * rows * rdm_dec(rd) * 4 + 132 * 4) + kSchedBytes;
+  return align256(bimg) + align256((size_t)n_cells * rows * rdm_dec(rd) * 4 + 132 * 4);
 }
 
 int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* const* scale, int bits,
@@ -1526,13 +1552,10 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
       bimg + align256((size_t)n_cells * ((size_t)4 * d * d + (tucker_block ? (size_t)128 * d : 0))));
   a.bimg = bimg;
   a.tmp = tmp;
-  a.sched = reinterpret_cast<unsigned long long*>(reinterpret_cast<uint8_t*>(tmp) +
-                                                  align256((size_t)n_cells * m * t * rdm * 4 + 132 * 4));
   CellPtrs uf;
   for (int c = 0; c < n_cells; ++c) uf.p[c] = rt > 0 ? u_feature[c] : nullptr;
-  prep_decode_kernel<<<dim3((std::max(d * d + d * 64, kMaxCtas) + 255) / 256, n_cells), 256, 0, st>>>(
-      proj, sc, uf, factor_dtype, tucker_block, d, bimg, a.sched, (int)ceil_div(a.total_tiles, a.tiles_per_cta),
-      a.tiles_per_cta, a.total_tiles);
+  prep_decode_kernel<<<dim3((d * d + d * 64 + 255) / 256, n_cells), 256, 0, st>>>(proj, sc, uf, factor_dtype,
+                                                                                tucker_block, d, bimg);
   if ((rc = check_launch("prep_decode_kernel"))) return rc;
   if (rt > 0) {
     CellPtrs cp, up;
@@ -1548,8 +1571,9 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
   const dim3 grid((unsigned)ceil_div(a.total_tiles, a.tiles_per_cta));
 #define KVC_TC_DEC3(DD, RR, BB)                                      \
   do {                                                               \
-    auto kern = tc_decode_kernel<DD, RR, BB, 4>;                     \
-    using LL = DecLayout<DD, DD * BB / 8, RR, 4>;                    \
+    constexpr int NSD = DecStages<DD, DD * BB / 8, RR>::value;       \
+    auto kern = tc_decode_kernel<DD, RR, BB, NSD>;                   \
+    using LL = DecLayout<DD, DD * BB / 8, RR, NSD>;                  \
     if ((rc = set_smem(kern, LL::BYTES))) return rc;                 \
     kern<<<grid, NTHREADS, LL::BYTES, st>>>(cmaps, omaps, a);        \
   } while (0)
