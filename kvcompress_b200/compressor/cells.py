@@ -71,11 +71,11 @@ def tucker_cells(xs: list[torch.Tensor], *, r_token: int, r_feature: int, svd: S
     Returns lists ``(core, u_token, u_feature)`` in the cell dtype and the
     per-cell token / feature tail masses as float64 device tensors.
     """
+    xs = ops.cells(xs, "tucker")
     x0 = xs[0]
     m, t, d = (int(s) for s in x0.shape)
     dt = x0.dtype
     dev = x0.device
-    n = len(xs)
     # ranks clipped by the axis lengths (tucker.py:230-238)
     rt_req = max(1, min(int(r_token), t))
     rd_req = max(1, min(int(r_feature), d))
@@ -84,11 +84,11 @@ def tucker_cells(xs: list[torch.Tensor], *, r_token: int, r_feature: int, svd: S
     n_f = m * t
     mode_f, rd, k_f = svd.resolve(d, n_f, rd_req, cap, forced_randomised)
     om_f = sketch_omega(n_f, k_f, svd.seed, dev) if mode_f == KVC.SVD_RANDOMISED else None
-    flat = [x.view(n_f, d) for x in xs]
+    flat = xs.reshape(n_f, d)
     g_f = ops.gram(flat, om_f)
     u_d, tail_f, _ = ops.sketch_solve(g_f, mode=mode_f, side=KVC.SIDE_LEFT, p=d, n_other=n_f, k=k_f,
                                       rank=rd, n_power=svd.n_power, omega=None, basis_dtype=dt)
-    u_feature = [u_d[i] for i in range(n)]
+    u_feature = ops.split(u_d)
 
     # --- projection to (T, m*rd) ------------------------------------------
     x_proj_t = ops.project_feature(xs, u_feature)
@@ -144,6 +144,7 @@ def compress_cells(
                                   symmetric=symmetric, per_channel=per_channel, group_size=group_size,
                                   factor_dtype=factor_dtype)
         return out
+    xs = ops.cells(xs, "compress")
     mode_scale = scale_mode_of(per_channel, group_size, d) if bits > 0 else KVC.SCALE_CHANNEL
     core, u_token, u_feature, tail_t, tail_f = tucker_cells(
         xs, r_token=r_token, r_feature=r_feature, svd=svd, cap=cap,

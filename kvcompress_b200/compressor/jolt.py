@@ -27,6 +27,12 @@ from kvcompress_b200.compressor.base import CompressedPayload, CompressorStats, 
 from kvcompress_b200.compressor.cells import CellResult, _batch_of, compress_cells, decompress_cells
 from kvcompress_b200.compressor.svd import SVD
 
+# metadata that must agree for payloads to share one decode launch
+_GROUP_META = ("bits", "residual_seed", "residual_distribution", "residual_sparsity", "residual_symmetric",
+               "residual_per_channel", "residual_group_size")
+
+_DESC: dict[tuple[int, int, int, int], tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
+
 __all__ = ["JoLTCompressor", "JoLTFactors"]
 
 _DTYPES = (torch.float32, torch.float16, torch.bfloat16)
@@ -128,15 +134,19 @@ class JoLTCompressor(KVCompressor):
             order += members
             tails_t.append(_batch_of([r.tail_token for r in cell_res]))
             tails_f.append(_batch_of([r.tail_feature for r in cell_res]))
-        # one host sync for every tail mass (one small copy per batch)
-        tails = torch.stack([torch.cat(tails_t), torch.cat(tails_f)], dim=1).cpu().tolist()
-        tail_of = {k: tv for k, tv in zip(order, tails)}
+        # payloads first (host work that overlaps the kernels still running),
+        # then one host sync for every tail mass (one small copy per batch)
         out = []
         for li, ((key, value), res) in enumerate(zip(pairs, plans)):
             k_alloc, v_alloc = res.allocations
-            kp = self.build_payload(key, JoLTFactors(results[(li, 0)], None, k_alloc), tail_of[(li, 0)])
-            vp = self.build_payload(value, JoLTFactors(results[(li, 1)], None, v_alloc), tail_of[(li, 1)])
+            kp = self.build_payload(key, JoLTFactors(results[(li, 0)], None, k_alloc), (0.0, 0.0))
+            vp = self.build_payload(value, JoLTFactors(results[(li, 1)], None, v_alloc), (0.0, 0.0))
             out.append((kp, vp))
+        tails = torch.stack([torch.cat(tails_t), torch.cat(tails_f)], dim=1).cpu().tolist()
+        for (li, side), (tt, tf) in zip(order, tails):
+            md = out[li][side].metadata
+            md["tail_token_mass"] = float(tt)
+            md["tail_feature_mass"] = float(tf)
         elapsed = (time.perf_counter() - t_start) * 1000
         key, value = pairs[-1]
         kp, vp = out[-1]
@@ -164,12 +174,10 @@ class JoLTCompressor(KVCompressor):
         groups: dict[tuple, list[int]] = {}
         for i, p in enumerate(flat):
             md = p.metadata
-            gk = (tuple(p.shape), p.dtype, tuple(p.data["core"].shape), p.data["core"].dtype,
-                  p.data["core"].device, "residual_packed" in p.data and
-                  p.data["residual_packed"].numel() > 0, md.get("bits"),
-                  md.get("residual_seed"), md.get("residual_distribution"),
-                  md.get("residual_sparsity"), md.get("residual_symmetric"),
-                  md.get("residual_per_channel"), md.get("residual_group_size"))
+            core = p.data["core"]
+            packed = p.data.get("residual_packed")
+            gk = (tuple(p.shape), p.dtype, core.shape, core.dtype, core.get_device(),
+                  packed is not None and packed.numel() > 0, *(md.get(k) for k in _GROUP_META))
             groups.setdefault(gk, []).append(i)
         outs: list[torch.Tensor | None] = [None] * len(flat)
         for members in groups.values():
@@ -232,9 +240,15 @@ class JoLTCompressor(KVCompressor):
             data["residual_scale"] = r.scale
             data["residual_zero_point"] = r.zero_point
         # small int32 descriptors live on the host, as in the reference
-        data["residual_original_shape"] = torch.tensor([m, t, d], dtype=torch.int32)
-        data["residual_original_last"] = torch.tensor(d, dtype=torch.int32)
-        data["residual_dtype"] = torch.tensor(r.bits, dtype=torch.int32)
+        # (copies of cached templates: cheaper than building each from lists)
+        tmpl = _DESC.get((m, t, d, r.bits))
+        if tmpl is None:
+            tmpl = (torch.tensor([m, t, d], dtype=torch.int32), torch.tensor(d, dtype=torch.int32),
+                    torch.tensor(r.bits, dtype=torch.int32))
+            _DESC[(m, t, d, r.bits)] = tmpl
+        data["residual_original_shape"] = tmpl[0].clone()
+        data["residual_original_last"] = tmpl[1].clone()
+        data["residual_dtype"] = tmpl[2].clone()
         return CompressedPayload(
             method="jolt", shape=tuple(original.shape), dtype=original.dtype, metadata=meta, data=data,
             stats=CompressorStats(

@@ -46,11 +46,25 @@ _SKETCH_LOCK = threading.Lock()
 _SKETCH_MAX = 8
 
 
+def _seed_generators(seed: int) -> None:
+    """``torch.manual_seed(seed)`` for the CPU and CUDA generators.
+
+    Seeds the same generators as ``torch.manual_seed`` on a CUDA host without
+    its deferred-initialisation bookkeeping for other device types (a stack
+    capture per call, the largest host cost of a compress call)."""
+    torch.random.default_generator.manual_seed(seed)
+    if torch.cuda.is_initialized():
+        for g in torch.cuda.default_generators:
+            g.manual_seed(seed)
+    else:
+        torch.cuda.manual_seed_all(seed)
+
+
 def sketch_omega(n: int, k: int, seed: int, device: torch.device) -> torch.Tensor:
     """The reference's sketch ``torch.manual_seed(seed); torch.randn(n, k)`` on ``device``."""
     device = torch.device(device)
     key = (int(n), int(k), int(seed), str(device))
-    torch.manual_seed(int(seed))
+    _seed_generators(int(seed))
     with _SKETCH_LOCK:
         hit = _SKETCH.get(key)
         if hit is not None:

@@ -17,7 +17,9 @@ from kvcompress_b200._native import KVC, check, lib, ptr_array
 
 __all__ = [
     "DTYPE_CODE",
+    "Cells",
     "apply_basis",
+    "cells",
     "cast",
     "core",
     "decompress",
@@ -27,6 +29,7 @@ __all__ = [
     "residual_quant",
     "residual_stats",
     "sketch_solve",
+    "split",
     "workspace",
 ]
 
@@ -96,7 +99,49 @@ def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return buf
 
 
-def _cells(xs: Sequence[torch.Tensor], what: str) -> tuple[torch.Tensor, ...]:
+class Cells(list):
+    """A checked batch of same-shape, same-dtype contiguous CUDA tensors with
+    its host array of device pointers, built once and reused by every launch
+    that takes the batch (the per-tensor Python work, not the launches, is
+    what a 64-cell call spends its host time on)."""
+
+    __slots__ = ("_ptrs",)
+
+    def __init__(self, xs=(), ptrs=None):
+        super().__init__(xs)
+        self._ptrs = ptrs
+
+    def ptrs(self) -> ctypes.Array:
+        if self._ptrs is None:
+            self._ptrs = ptr_array(x.data_ptr() for x in self)
+        return self._ptrs
+
+    def reshape(self, *shape) -> "Cells":
+        """The same cells under another shape (same storage, same pointers)."""
+        return Cells([x.view(*shape) for x in self], self._ptrs)
+
+
+def cells(xs: Sequence[torch.Tensor], what: str = "cells") -> Cells:
+    """Check a batch once; later launches on it skip the checks."""
+    return _cells(xs, what)
+
+
+def split(batch: torch.Tensor) -> Cells:
+    """``batch[i]`` for every i, as a batch whose pointers are computed from
+    the base address (one allocation, one ``data_ptr`` call)."""
+    views = batch.unbind(0)
+    base = batch.data_ptr()
+    step = batch.stride(0) * batch.element_size() if batch.dim() > 0 else 0
+    return Cells(views, ptr_array(base + i * step for i in range(len(views))))
+
+
+def _ptrs(seq) -> ctypes.Array:
+    return seq.ptrs() if isinstance(seq, Cells) else ptr_array(t.data_ptr() for t in seq)
+
+
+def _cells(xs: Sequence[torch.Tensor], what: str) -> Cells:
+    if isinstance(xs, Cells) and 0 < len(xs) <= KVC.MAX_CELLS:
+        return xs
     xs = tuple(xs)
     if not xs:
         raise ValueError(f"{what}: empty cell batch")
@@ -110,7 +155,13 @@ def _cells(xs: Sequence[torch.Tensor], what: str) -> tuple[torch.Tensor, ...]:
             raise ValueError(f"{what}: cells must share shape, dtype and device")
         if not x.is_contiguous():
             raise ValueError(f"{what}: cells must be contiguous")
-    return xs
+    return Cells(xs)
+
+
+def _views(batch: torch.Tensor) -> Cells:
+    """Per-cell outputs as views of one allocation (one allocator call per
+    launch instead of one per cell; each view is contiguous)."""
+    return split(batch)
 
 
 def _code(dtype: torch.dtype) -> int:
@@ -136,7 +187,7 @@ def gram(cells: Sequence[torch.Tensor], omega: torch.Tensor | None) -> torch.Ten
     ws = workspace(ws_n, dev)
     nbytes = len(cells) * cells[0].numel() * cells[0].element_size() + (0 if omega is None else omega.numel() * 4)
     with _Stage("gram", 3, nbytes):
-        check(L.kvc_gram(len(cells), ptr_array(c.data_ptr() for c in cells), rows, p,
+        check(L.kvc_gram(len(cells), _ptrs(cells), rows, p,
                          _code(cells[0].dtype), omega.data_ptr() if omega is not None else None, k,
                          out.data_ptr(), ws.data_ptr(), ws.numel(), _stream()), "kvc_gram")
     return out
@@ -172,12 +223,12 @@ def project_feature(xs: Sequence[torch.Tensor], u_feature: Sequence[torch.Tensor
     xs = _cells(xs, "project_feature")
     m, t, d = xs[0].shape
     rd = int(u_feature[0].shape[1])
-    outs = [torch.empty(t, m * rd, dtype=xs[0].dtype, device=xs[0].device) for _ in xs]
+    outs = _views(torch.empty(len(xs), t, m * rd, dtype=xs[0].dtype, device=xs[0].device))
     nbytes = len(xs) * (xs[0].numel() + outs[0].numel()) * xs[0].element_size()
     with _Stage("project_feature", 1, nbytes):
-        check(lib().kvc_project_feature(len(xs), ptr_array(x.data_ptr() for x in xs), m, t, d,
-                                        _code(xs[0].dtype), ptr_array(u.data_ptr() for u in u_feature),
-                                        rd, ptr_array(o.data_ptr() for o in outs), _stream()),
+        check(lib().kvc_project_feature(len(xs), _ptrs(xs), m, t, d,
+                                        _code(xs[0].dtype), _ptrs(u_feature),
+                                        rd, _ptrs(outs), _stream()),
               "kvc_project_feature")
     return outs
 
@@ -187,13 +238,12 @@ def apply_basis(a: Sequence[torch.Tensor], mat: torch.Tensor) -> list[torch.Tens
     a = _cells(a, "apply_basis")
     rows, p = a[0].shape
     r = int(mat.shape[2])
-    batch = torch.empty(len(a), rows, r, dtype=a[0].dtype, device=a[0].device)
-    outs = [batch[i] for i in range(len(a))]
+    outs = _views(torch.empty(len(a), rows, r, dtype=a[0].dtype, device=a[0].device))
     nbytes = len(a) * (a[0].numel() + outs[0].numel()) * a[0].element_size()
     with _Stage("apply_basis", 1, nbytes):
-        check(lib().kvc_apply_basis(len(a), ptr_array(x.data_ptr() for x in a), rows, p,
+        check(lib().kvc_apply_basis(len(a), _ptrs(a), rows, p,
                                     _code(a[0].dtype), mat.data_ptr(), r,
-                                    ptr_array(o.data_ptr() for o in outs), _stream()), "kvc_apply_basis")
+                                    _ptrs(outs), _stream()), "kvc_apply_basis")
     return outs
 
 
@@ -203,16 +253,15 @@ def core(x_proj_t: Sequence[torch.Tensor], u_token: Sequence[torch.Tensor], m: i
     t = int(x_proj_t[0].shape[0])
     rt = int(u_token[0].shape[1])
     dev = x_proj_t[0].device
-    batch = torch.empty(len(x_proj_t), m, rt, rd, dtype=x_proj_t[0].dtype, device=dev)
-    outs = [batch[i] for i in range(len(x_proj_t))]
+    outs = _views(torch.empty(len(x_proj_t), m, rt, rd, dtype=x_proj_t[0].dtype, device=dev))
     L = lib()
     ws_n = L.kvc_core_workspace_bytes(len(outs), t, m, rd, rt)
     ws = workspace(ws_n, dev)
     nbytes = len(outs) * (x_proj_t[0].numel() + u_token[0].numel()) * x_proj_t[0].element_size()
     with _Stage("core", 2, nbytes):
-        check(L.kvc_core(len(outs), ptr_array(x.data_ptr() for x in x_proj_t),
-                         ptr_array(u.data_ptr() for u in u_token), t, m, rd, rt,
-                         _code(x_proj_t[0].dtype), ptr_array(o.data_ptr() for o in outs), ws.data_ptr(),
+        check(L.kvc_core(len(outs), _ptrs(x_proj_t),
+                         _ptrs(u_token), t, m, rd, rt,
+                         _code(x_proj_t[0].dtype), _ptrs(outs), ws.data_ptr(),
                          ws.numel(), _stream()), "kvc_core")
     return outs
 
@@ -222,8 +271,8 @@ def _factor_ptrs(factors, n):
         z = ptr_array([0] * n)
         return z, z, z, 0, 0
     core_, ut, ud = factors
-    return (ptr_array(c.data_ptr() for c in core_), ptr_array(u.data_ptr() for u in ut),
-            ptr_array(u.data_ptr() for u in ud), int(ut[0].shape[1]), int(ud[0].shape[1]))
+    return (_ptrs(core_), _ptrs(ut),
+            _ptrs(ud), int(ut[0].shape[1]), int(ud[0].shape[1]))
 
 
 def residual_stats(xs, factors, proj, *, bits: int, symmetric: bool, scale_mode: int,
@@ -235,19 +284,19 @@ def residual_stats(xs, factors, proj, *, bits: int, symmetric: bool, scale_mode:
     n = len(xs)
     ns = d if scale_mode == KVC.SCALE_CHANNEL else 1
     shape = (d,) if scale_mode == KVC.SCALE_CHANNEL else ()
-    scales = [torch.empty(shape, dtype=torch.float32, device=dev) for _ in xs]
-    zps = [torch.empty(shape, dtype=torch.int32, device=dev) for _ in xs]
+    scales = _views(torch.empty((n,) + shape, dtype=torch.float32, device=dev))
+    zps = _views(torch.empty((n,) + shape, dtype=torch.int32, device=dev))
     del ns
     cp, up, dp, rt, rd = _factor_ptrs(factors, n)
     L = lib()
     ws_n = L.kvc_residual_stats_workspace_bytes(n, m * t, d, rd)
     ws = workspace(ws_n, dev)
     with _Stage("residual_stats", 2, n * xs[0].numel() * xs[0].element_size()):
-        check(L.kvc_residual_stats(n, ptr_array(x.data_ptr() for x in xs), m, t, d, _code(xs[0].dtype),
+        check(L.kvc_residual_stats(n, _ptrs(xs), m, t, d, _code(xs[0].dtype),
                                    cp, up, dp, rt, rd, proj.data_ptr() if proj is not None else None,
                                    bits, int(symmetric), scale_mode, _code(stat_dtype),
-                                   ptr_array(s.data_ptr() for s in scales),
-                                   ptr_array(z.data_ptr() for z in zps), ws.data_ptr(), ws.numel(),
+                                   _ptrs(scales),
+                                   _ptrs(zps), ws.data_ptr(), ws.numel(),
                                    _stream()), "kvc_residual_stats")
     return scales, zps
 
@@ -265,22 +314,22 @@ def residual_quant(xs, factors, proj, scales, zps, *, bits: int, symmetric: bool
     n = len(xs)
     if scale_mode == KVC.SCALE_GROUP:
         ng = d // int(group_size)
-        scales = [torch.empty(m * t, ng, dtype=torch.float32, device=dev) for _ in xs]
-        zps = [torch.empty(m * t, ng, dtype=torch.int32, device=dev) for _ in xs]
+        scales = _views(torch.empty(n, m * t, ng, dtype=torch.float32, device=dev))
+        zps = _views(torch.empty(n, m * t, ng, dtype=torch.int32, device=dev))
     cb = (d * bits + 7) // 8
-    codes = [torch.empty(m * t, cb, dtype=torch.uint8, device=dev) for _ in xs]
+    codes = _views(torch.empty(n, m * t, cb, dtype=torch.uint8, device=dev))
     cp, up, dp, rt, rd = _factor_ptrs(factors, n)
     ws = workspace(lib().kvc_residual_quant_workspace_bytes(n, m * t, d, rd), dev)
     nbytes = n * (xs[0].numel() * xs[0].element_size() + codes[0].numel())
     with _Stage("residual_quant", 1, nbytes):
-        check(lib().kvc_residual_quant(n, ptr_array(x.data_ptr() for x in xs), m, t, d,
+        check(lib().kvc_residual_quant(n, _ptrs(xs), m, t, d,
                                        _code(xs[0].dtype), cp, up, dp, rt, rd,
                                        proj.data_ptr() if proj is not None else None, bits,
                                        int(symmetric), scale_mode, int(group_size or 0),
                                        _code(stat_dtype), _code(arith_dtype),
-                                       ptr_array(s.data_ptr() for s in scales),
-                                       ptr_array(z.data_ptr() for z in zps),
-                                       ptr_array(c.data_ptr() for c in codes), ws.data_ptr(), ws.numel(),
+                                       _ptrs(scales),
+                                       _ptrs(zps),
+                                       _ptrs(codes), ws.data_ptr(), ws.numel(),
                                        _stream()),
               "kvc_residual_quant")
     return codes, scales, zps
@@ -294,14 +343,14 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
     m, t, d = (int(s) for s in shape)
     t1 = t if t1 is None else int(t1)
     if out is None:
-        out = [torch.empty(m, t1 - t0, d, dtype=out_dtype, device=device) for _ in range(n_cells)]
+        out = _views(torch.empty(n_cells, m, t1 - t0, d, dtype=out_dtype, device=device))
     n = len(out)
     cp, up, dp, rt, rd = _factor_ptrs(factors, n)
     fdt = _code(factors[0][0].dtype) if factors is not None else KVC.F16
     if bits > 0:
-        c_arr = ptr_array(c.data_ptr() for c in codes)
-        s_arr = ptr_array(s.data_ptr() for s in scales)
-        z_arr = ptr_array(z.data_ptr() for z in zps)
+        c_arr = _ptrs(codes)
+        s_arr = _ptrs(scales)
+        z_arr = _ptrs(zps)
     else:
         c_arr = s_arr = z_arr = ptr_array([0] * n)
     dev0 = out[0].device
@@ -313,7 +362,7 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
         check(lib().kvc_decompress(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
                                    int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
                                    proj.data_ptr() if proj is not None else None, t0, t1,
-                                   _code(out_dtype), ptr_array(o.data_ptr() for o in out),
+                                   _code(out_dtype), _ptrs(out),
                                    ws.data_ptr(), ws.numel(), _stream()),
               "kvc_decompress")
     return out
@@ -338,15 +387,15 @@ def decompress_noalloc(shape, out_dtype: torch.dtype, *, codes=None, scales=None
     cp, up, dp, rt, rd = _factor_ptrs(factors, n)
     fdt = _code(factors[0][0].dtype) if factors is not None else KVC.F16
     if bits > 0:
-        c_arr = ptr_array(c.data_ptr() for c in codes)
-        s_arr = ptr_array(s.data_ptr() for s in scales)
-        z_arr = ptr_array(z.data_ptr() for z in zps)
+        c_arr = _ptrs(codes)
+        s_arr = _ptrs(scales)
+        z_arr = _ptrs(zps)
     else:
         c_arr = s_arr = z_arr = ptr_array([0] * n)
     check(lib().kvc_decompress_noalloc(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
                                        int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
                                        proj.data_ptr() if proj is not None else None, t0, t1,
-                                       _code(out_dtype), ptr_array(o.data_ptr() for o in out), _stream()),
+                                       _code(out_dtype), _ptrs(out), _stream()),
           "kvc_decompress_noalloc")
     return out
 
