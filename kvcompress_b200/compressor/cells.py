@@ -178,6 +178,8 @@ def compress_cells(
 
 def _batch_of(views: list[torch.Tensor]) -> torch.Tensor:
     """The (n, ...) tensor a list of per-cell views was cut from."""
+    if isinstance(views, ops.Cells) and views.batch is not None:
+        return views.batch
     base = views[0]._base
     if base is not None and base.shape[0] == len(views) and base[0].data_ptr() == views[0].data_ptr():
         return base

@@ -239,16 +239,14 @@ class JoLTCompressor(KVCompressor):
             data["residual_packed"] = r.packed
             data["residual_scale"] = r.scale
             data["residual_zero_point"] = r.zero_point
-        # small int32 descriptors live on the host, as in the reference
-        # (copies of cached templates: cheaper than building each from lists)
+        # small int32 descriptors live on the host, as in the reference; they
+        # are read-only, so payloads of one shape share them
         tmpl = _DESC.get((m, t, d, r.bits))
         if tmpl is None:
             tmpl = (torch.tensor([m, t, d], dtype=torch.int32), torch.tensor(d, dtype=torch.int32),
                     torch.tensor(r.bits, dtype=torch.int32))
             _DESC[(m, t, d, r.bits)] = tmpl
-        data["residual_original_shape"] = tmpl[0].clone()
-        data["residual_original_last"] = tmpl[1].clone()
-        data["residual_dtype"] = tmpl[2].clone()
+        data["residual_original_shape"], data["residual_original_last"], data["residual_dtype"] = tmpl
         return CompressedPayload(
             method="jolt", shape=tuple(original.shape), dtype=original.dtype, metadata=meta, data=data,
             stats=CompressorStats(

@@ -9,7 +9,9 @@
 #include <algorithm>
 
 #include "kvc_common.cuh"
+#include "kvc_sched.cuh"
 #include "kvc_tc.cuh"
+#include "kvc_tma.cuh"
 
 namespace kvc {
 namespace {
@@ -222,6 +224,123 @@ __global__ void __launch_bounds__(256) project_rd1_bf16_kernel(CellPtrs X, CellP
   }
 }
 
+// x_proj for bf16 cells with rd == 1 and d = 64 or 128, streamed by TMA:
+// tiles of 128 rows (one head, 128 tokens) in (cell, token block, head)
+// order, heads fastest, so the scattered 2-byte outputs of one token block
+// meet in L2 before they are written back.  Each CTA owns a contiguous run
+// of tiles; one producer thread keeps NS tiles in flight (SWIZZLE_128B boxes
+// of 64 columns), and two consumer threads share a row: thread (r, half)
+// sums the 64 (or 32) products of its half in packed fp32 pairs, and the
+// halves meet by a shuffle.  A quarter-warp holds 8 rows of one half, so
+// the swizzle puts its 16-byte reads in 8 different bank groups.
+constexpr int PJ_ROWS = 128, PJ_THREADS = 288;  // 8 consumer warps + 1 producer warp
+
+template <int D, int NS>
+struct PjLayout {
+  static constexpr uint32_t STAGE = PJ_ROWS * D * 2;
+  static constexpr uint32_t OFF_RING = NS * STAGE;
+  static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
+  static constexpr uint32_t BYTES = OFF_BAR + 2 * NS * 8 + 1024;
+};
+
+struct PjArgs {
+  CellPtrs u;
+  CellPtrsMut out;
+  int64_t t, tb, units, per_cta;  // tokens, token blocks per head, tiles, tiles per CTA
+  int m;
+};
+
+template <int D, int NS>
+__global__ void __launch_bounds__(PJ_THREADS, 1)
+    project_rd1_tma_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ PjArgs A) {
+  using L = PjLayout<D, NS>;
+  static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
+  constexpr int HALF = D / 2;     // elements per thread
+  constexpr int NCH = HALF / 8;   // 16-byte chunks per thread
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (tc::smem_u32(smem_raw) & 1023u)) & 1023u);
+  const uint32_t sbase = tc::smem_u32(smem);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = full + NS;
+  int32_t* ring = reinterpret_cast<int32_t*>(smem + L::OFF_RING);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      tc::mbar_init(&full[i], 1);
+      tc::mbar_init(&empty[i], 8);  // one arrive per consumer warp
+    }
+    tc::mbar_fence_init();
+  }
+  __syncthreads();
+  if (warp == 8) {
+    if (lane == 0) {
+      sched::Cursor cur(A.per_cta, A.units);
+      for (int it = 0;; ++it) {
+        const int64_t u = sched::next_tile(cur);
+        sched::ring_put(ring, it, (int32_t)u);
+        const int st = it % NS;
+        if (!tc::mbar_wait(&empty[st], (uint32_t)((it / NS) & 1) ^ 1u, 0x501)) break;
+        if (u < 0) {
+          tc::mbar_arrive(&full[st]);
+          break;
+        }
+        const int cell = (int)(u / (A.tb * A.m));
+        const int64_t r = u % (A.tb * A.m);
+        const int y = (int)((r % A.m) * A.t + (r / A.m) * PJ_ROWS);  // row of the cell's (m * T) x D view
+        tc::mbar_expect_tx(&full[st], L::STAGE);
+#pragma unroll
+        for (int hcol = 0; hcol < D / 64; ++hcol)
+          tc::tma_load_2d(sbase + st * L::STAGE + hcol * PJ_ROWS * 128, &xmaps.m[cell], hcol * 64, y, &full[st]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // thread -> (row, half): lanes 0-7 and 16-23 hold half 0, 8-15 and 24-31 half 1
+    const int half = (threadIdx.x >> 3) & 1;
+    const int row = (threadIdx.x & 7) | ((threadIdx.x >> 4) << 3);
+    uint64_t u2[HALF / 2];  // this half of u_feature as packed fp32 pairs
+    int cur_cell = -1;
+    for (int it = 0;; ++it) {
+      const int st = it % NS;
+      if (!__all_sync(0xffffffffu, tc::mbar_wait(&full[st], (uint32_t)((it / NS) & 1), 0x502))) break;
+      const int32_t u = sched::ring_get(ring, it);
+      if (u < 0) break;
+      const int cell = (int)(u / (A.tb * A.m));
+      if (cell != cur_cell) {
+        const uint16_t* uf = static_cast<const uint16_t*>(A.u.p[cell]) + half * HALF;
+#pragma unroll
+        for (int q = 0; q < HALF / 2; ++q)
+          u2[q] = tc::f2_pack(__uint_as_float((uint32_t)uf[2 * q] << 16), __uint_as_float((uint32_t)uf[2 * q + 1] << 16));
+        cur_cell = cell;
+      }
+      // half 0 = columns 0-63 (first box), half 1 = 64-127 (D = 128); for
+      // D = 64 both halves share the one box, 32 columns each
+      const uint8_t* rs = smem + st * L::STAGE + (D == 128 ? half * PJ_ROWS * 128 : 0) + row * 128;
+      uint64_t acc = tc::f2_pack(0.f, 0.f);
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        const int chunk = (D == 128 ? c : half * NCH + c) ^ (row & 7);  // SWIZZLE_128B
+        const uint4 raw = *reinterpret_cast<const uint4*>(rs + chunk * 16);
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          acc = tc::f2_fma(tc::f2_pack(__uint_as_float(w[i] << 16), __uint_as_float(w[i] & 0xFFFF0000u)),
+                           u2[c * 4 + i], acc);
+      }
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(&empty[st]);  // the stage has been read
+      float a0, a1;
+      tc::f2_unpack(acc, a0, a1);
+      float sum = a0 + a1;
+      sum += __shfl_xor_sync(0xffffffffu, sum, 8);
+      const int64_t r = u % (A.tb * A.m);
+      const int64_t h = r % A.m, tok = (r / A.m) * PJ_ROWS + row;
+      if (half == 0 && tok < A.t)
+        static_cast<__nv_bfloat16*>(A.out.p[cell])[tok * A.m + h] = __float2bfloat16_rn(sum);
+    }
+  }
+}
+
 // out (rows x N) = round_T(A (rows x K) * M (K x N)) for K <= 64, N <= 16:
 // one thread per row, M in shared memory as float, fp32 accumulation in k
 // order (the same arithmetic as rowmat_kernel).
@@ -276,6 +395,42 @@ extern "C" int kvc_project_feature(int n_cells, const void* const* x, int64_t m,
   const int lpr = (int)(d * dtype_size(dtype) / 16);
   bool aligned = (d * dtype_size(dtype)) % 16 == 0;
   for (int c = 0; c < n_cells; ++c) aligned = aligned && (reinterpret_cast<uintptr_t>(x[c]) & 15u) == 0;
+  if (rd == 1 && dtype == KVC_BF16 && aligned && (d == 64 || d == 128) && rows < (1LL << 31)) {
+    TmaMaps xm;
+    int rc;
+    for (int c = 0; c < n_cells; ++c) {
+      const uint64_t dims[2] = {(uint64_t)d, (uint64_t)rows};
+      const uint64_t strides[1] = {(uint64_t)d * 2};
+      const uint32_t box[2] = {64u, (uint32_t)PJ_ROWS};
+      if ((rc = encode_tma(&xm.m[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, x[c], dims, strides, box,
+                           CU_TENSOR_MAP_SWIZZLE_128B)))
+        return rc;
+    }
+    PjArgs a;
+    a.u = ub;
+    a.out = o;
+    a.t = t;
+    a.m = (int)m;
+    a.tb = ceil_div(t, PJ_ROWS);
+    a.units = (int64_t)n_cells * m * a.tb;
+    const int64_t ctas = std::min<int64_t>(a.units, num_sms());
+    a.per_cta = ceil_div(a.units, ctas);
+    const dim3 grid((unsigned)ceil_div(a.units, a.per_cta));
+    if (d == 128) {
+      auto kern = project_rd1_tma_kernel<128, 6>;
+      constexpr size_t sm = PjLayout<128, 6>::BYTES;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+        return fail(KVC_ERR_LAUNCH, "kvc_project_feature: cudaFuncSetAttribute");
+      kern<<<grid, PJ_THREADS, sm, st>>>(xm, a);
+    } else {
+      auto kern = project_rd1_tma_kernel<64, 8>;
+      constexpr size_t sm = PjLayout<64, 8>::BYTES;
+      if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) != cudaSuccess)
+        return fail(KVC_ERR_LAUNCH, "kvc_project_feature: cudaFuncSetAttribute");
+      kern<<<grid, PJ_THREADS, sm, st>>>(xm, a);
+    }
+    return check_launch("project_rd1_tma_kernel");
+  }
   if (rd == 1 && dtype == KVC_BF16 && aligned && (lpr == 8 || lpr == 16)) {
     const int64_t per_block = 256 / lpr * 4;
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, per_block),

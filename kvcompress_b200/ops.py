@@ -79,8 +79,16 @@ class _Stage:
         return False
 
 
+def _raw_stream(dev_index: int | None = None) -> int:
+    """The current stream of a device as a raw pointer (torch's private fast
+    accessor when it exists: the public one builds a Stream object)."""
+    idx = torch.cuda.current_device() if dev_index is None else dev_index
+    fast = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    return fast(idx) if fast is not None else torch.cuda.current_stream(idx).cuda_stream
+
+
 def _stream() -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    return ctypes.c_void_p(_raw_stream())
 
 
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
@@ -90,8 +98,8 @@ def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     stream gets its own buffer.
     """
     dev = torch.device(device)
-    key = (dev.index if dev.index is not None else torch.cuda.current_device(),
-           torch.cuda.current_stream(dev).cuda_stream)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    key = (idx, _raw_stream(idx))
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
@@ -99,26 +107,58 @@ def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     return buf
 
 
-class Cells(list):
+class Cells(Sequence):
     """A checked batch of same-shape, same-dtype contiguous CUDA tensors with
     its host array of device pointers, built once and reused by every launch
     that takes the batch (the per-tensor Python work, not the launches, is
-    what a 64-cell call spends its host time on)."""
+    what a 64-cell call spends its host time on).
 
-    __slots__ = ("_ptrs",)
+    Either a list of tensors, or one tensor whose first dimension indexes the
+    cells; then the per-cell views are made only when asked for, and the
+    pointers are computed from the base address."""
 
-    def __init__(self, xs=(), ptrs=None):
-        super().__init__(xs)
+    __slots__ = ("_items", "_batch", "_ptrs")
+
+    def __init__(self, items=None, ptrs=None, batch: torch.Tensor | None = None):
+        self._items = None if items is None else list(items)
+        self._batch = batch
         self._ptrs = ptrs
+
+    def __len__(self) -> int:
+        return int(self._batch.shape[0]) if self._batch is not None else len(self._items)
+
+    def __getitem__(self, i):
+        if self._items is None:
+            if isinstance(i, int) and i == 0:
+                return self._batch[0]  # shape / dtype probes: no need for every view
+            self._items = list(self._batch.unbind(0))  # one call for all the views
+        return self._items[i]
+
+    def __iter__(self):
+        if self._items is None:
+            self._items = list(self._batch.unbind(0))
+        return iter(self._items)
+
+    @property
+    def batch(self) -> torch.Tensor | None:
+        """The tensor the cells are slices of, when they are."""
+        return self._batch
 
     def ptrs(self) -> ctypes.Array:
         if self._ptrs is None:
-            self._ptrs = ptr_array(x.data_ptr() for x in self)
+            if self._batch is not None:
+                b = self._batch
+                base, step = b.data_ptr(), b.stride(0) * b.element_size()
+                self._ptrs = ptr_array(base + i * step for i in range(len(self)))
+            else:
+                self._ptrs = ptr_array(x.data_ptr() for x in self._items)
         return self._ptrs
 
     def reshape(self, *shape) -> "Cells":
         """The same cells under another shape (same storage, same pointers)."""
-        return Cells([x.view(*shape) for x in self], self._ptrs)
+        if self._batch is not None and self._items is None:
+            return Cells(batch=self._batch.view(len(self), *shape), ptrs=self._ptrs)
+        return Cells([x.view(*shape) for x in self._items], self._ptrs)
 
 
 def cells(xs: Sequence[torch.Tensor], what: str = "cells") -> Cells:
@@ -127,12 +167,9 @@ def cells(xs: Sequence[torch.Tensor], what: str = "cells") -> Cells:
 
 
 def split(batch: torch.Tensor) -> Cells:
-    """``batch[i]`` for every i, as a batch whose pointers are computed from
-    the base address (one allocation, one ``data_ptr`` call)."""
-    views = batch.unbind(0)
-    base = batch.data_ptr()
-    step = batch.stride(0) * batch.element_size() if batch.dim() > 0 else 0
-    return Cells(views, ptr_array(base + i * step for i in range(len(views))))
+    """``batch[i]`` for every i, as a batch of cells (one allocation; views and
+    pointers are derived from it)."""
+    return Cells(batch=batch)
 
 
 def _ptrs(seq) -> ctypes.Array:
@@ -142,6 +179,8 @@ def _ptrs(seq) -> ctypes.Array:
 def _cells(xs: Sequence[torch.Tensor], what: str) -> Cells:
     if isinstance(xs, Cells) and 0 < len(xs) <= KVC.MAX_CELLS:
         return xs
+    if isinstance(xs, Cells):
+        xs = list(xs)
     xs = tuple(xs)
     if not xs:
         raise ValueError(f"{what}: empty cell batch")
