@@ -232,6 +232,25 @@ def workload_config(w, n, alloc):
     }
 
 
+PROFILE_SUMMARY = os.path.join(os.path.dirname(os.path.abspath(__file__)), "profiles",
+                               "tc_kernels_llama3-8b-8layers.md")
+
+
+def ncu_traffic(stage: str, cells: int):
+    """DRAM bytes (read + write) of one launch of ``stage`` from the committed
+    ncu summary (a 16-cell capture), scaled by the cells processed; None when
+    the summary has no figure for the stage."""
+    try:
+        with open(PROFILE_SUMMARY) as f:
+            for line in f:
+                parts = line.split()
+                if len(parts) == 3 and parts[0] == "traffic_per_cell_bytes" and parts[1] == stage:
+                    return float(parts[2]) * cells
+    except OSError:
+        pass
+    return None
+
+
 def run_ours(args, w):
     import torch.distributed as dist
 
@@ -352,8 +371,9 @@ def run_ours(args, w):
         "gpu_launches": launches,
         "clocks": clk,
         "roofline": {"bound": "hbm", "kernel": dname, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                     "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
-                     "launch_ms": dms / dcalls},
+                     "frac": achieved / peak, "peak_source": peak_kind,
+                     "traffic": ncu_traffic(dname, 2 * w.layers), "traffic_unit": "bytes per launch",
+                     "algorithmic_bytes": dbytes / dcalls, "launch_ms": dms / dcalls},
         "stages_ms_per_step": {k: v[0] / args.steps for k, v in sorted(stage.items())},
     }
     if not args.no_e2e:
