@@ -47,6 +47,7 @@ def parse_args():
     ap.add_argument("--workload", default="llama3-8b-kv-b1-t8192-bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--stream-block", type=int, default=256, help="tokens per block of the decode-stream line")
     ap.add_argument("--cpu-sample-layers", type=int, default=1)
     ap.add_argument("--layers", type=int, default=0,
                     help="override the workload's layer count (profiling a smaller case)")
@@ -376,6 +377,7 @@ def run_ours(args, w):
                      "algorithmic_bytes": dbytes / dcalls, "launch_ms": dms / dcalls},
         "stages_ms_per_step": {k: v[0] / args.steps for k, v in sorted(stage.items())},
     }
+    line["decode_stream"] = decode_stream(payloads, world, dev, block=args.stream_block)
     if not args.no_e2e:
         line["e2e"] = e2e(comp, pairs, w, dev, world, steps=min(args.steps, 3))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -386,6 +388,56 @@ def run_ours(args, w):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def decode_stream(payloads, world, dev, block: int = 256, passes: int = 3):
+    """Every layer's K and V decoded in consecutive blocks of ``block``
+    tokens through ``DecodeStream`` (plan made once, two launches per block):
+    the per-block cost a blockwise consumer pays, device-timed."""
+    import torch.distributed as dist
+
+    from kvcompress_b200 import DecodeStream
+
+    stream = DecodeStream(payloads)
+    tokens = stream.tokens
+    n_blocks = (tokens + block - 1) // block
+    for t0, t1, _ in stream.blocks(block):  # warm-up pass
+        pass
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(passes):
+        for t0, t1, _ in stream.blocks(block):
+            pass
+    e1.record()
+    torch.cuda.synchronize()
+    # the same blocks recorded once as a CUDA graph and replayed
+    cap = stream.capture(block)
+    cap.replay()
+    torch.cuda.synchronize()
+    g0, g1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    g0.record()
+    for _ in range(passes):
+        cap.replay()
+    g1.record()
+    torch.cuda.synchronize()
+    ms = torch.tensor([e0.elapsed_time(e1) / passes, g0.elapsed_time(g1) / passes], dtype=torch.float64,
+                      device=dev)
+    if world > 1:
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+    ms, gms = (float(v) for v in ms.tolist())
+    del cap
+    out_bytes = sum(p.shape[0] * p.shape[1] * p.shape[2] * 2 for pair in payloads for p in pair)
+    code_bytes = sum(p.data["residual_packed"].numel() for pair in payloads for p in pair)
+    return {"block_tokens": block, "blocks_per_pass": n_blocks, "planned": stream.planned,
+            "ms_per_pass": ms, "us_per_block": 1000.0 * ms / n_blocks,
+            "value": world * (out_bytes + code_bytes) / (ms / 1000.0) / 1e9, "unit": "GB/s",
+            "graph": {"ms_per_pass": gms, "us_per_block": 1000.0 * gms / n_blocks,
+                      "value": world * (out_bytes + code_bytes) / (gms / 1000.0) / 1e9, "unit": "GB/s"},
+            "what": "all layers' K and V, tokens [t0, t0 + block) per launch pair, through DecodeStream; "
+                    "graph: the same blocks as one CUDA graph (DecodeStream.capture)"}
 
 
 def e2e(comp, pairs, w, dev, world, steps: int = 2):

@@ -213,6 +213,34 @@ int kvc_decompress_noalloc(int n_cells, const uint8_t* const* codes, const float
                            int out_dtype, void* const* out, void* stream);
 
 /*
+ * Token-range decode streams (a consumer that reads the cache in blocks of
+ * tokens, e.g. 256-token blocks per layer).  The reference decodes a whole
+ * payload per call (reconstruct_payload, jolt.py:401-463); these split that
+ * decode into a plan made once per set of payloads and runs over [t0, t1).
+ *  - kvc_decode_plan_bytes: size of the caller-owned host buffer of a plan.
+ *  - kvc_decode_plan_init: same arguments as kvc_decompress without the
+ *    range and outputs.  Builds the codes tensor maps into the plan and each
+ *    cell's B image into the workspace (kvc_decompress_workspace_bytes of
+ *    the full payloads); the workspace and the payload tensors must stay
+ *    alive and unchanged while the plan is used.  Only layouts that take the
+ *    tensor-core decode have plans; others return KVC_ERR_UNSUPPORTED
+ *    (decode them with kvc_decompress).
+ *  - kvc_decode_plan_run: decodes tokens [t0, t1) of every cell into out[c]
+ *    ((m, t1 - t0, d) bf16, 16-byte aligned): two kernel launches, bit for
+ *    bit the same rows as kvc_decompress over that range.  Runs of one plan
+ *    share its workspace: issue them on one stream.
+ */
+size_t kvc_decode_plan_bytes(void);
+int kvc_decode_plan_init(void* plan, size_t plan_bytes, int n_cells, const uint8_t* const* codes,
+                         const float* const* scale, const int32_t* const* zp, int bits, int symmetric,
+                         int scale_mode, int group_size, const void* const* core,
+                         const void* const* u_token, const void* const* u_feature, int factor_dtype,
+                         int64_t m, int64_t t, int d, int rt, int rd, const float* proj, int out_dtype,
+                         void* workspace, size_t ws_bytes, void* stream);
+int kvc_decode_plan_run(const void* plan, size_t plan_bytes, int64_t t0, int64_t t1, void* const* out,
+                        void* stream);
+
+/*
  * Kernel selection.  Policy 0 (default): bf16 cells with d in {64, 128},
  * rd <= 16, a JL rotation and channel / tensor scales run on the tcgen05
  * tensor-core kernels (residual encode) and symmetric per-channel 8/4/2-bit

@@ -6,12 +6,12 @@ schema, cache); the arithmetic runs in the hand-written CUDA kernels of
 """
 
 from kvcompress_b200.cache import CacheManager, CompressedKVCache, CompressionMetadata
-from kvcompress_b200.compressor import (CompressedPayload, CompressorStats, FlashJoLTCompressor,
+from kvcompress_b200.compressor import (CompressedPayload, CompressorStats, DecodeStream, FlashJoLTCompressor,
                                         IdentityCompressor, IntQuantOnlyCompressor, JoLTCompressor,
                                         JointAllocator, KVCompressor, build_compressor, flashjolt_cap,
                                         supported_methods)
 
 __all__ = ["CacheManager", "CompressedKVCache", "CompressedPayload", "CompressionMetadata",
-           "CompressorStats", "FlashJoLTCompressor", "IdentityCompressor", "IntQuantOnlyCompressor",
+           "CompressorStats", "DecodeStream", "FlashJoLTCompressor", "IdentityCompressor", "IntQuantOnlyCompressor",
            "JoLTCompressor", "JointAllocator", "KVCompressor", "build_compressor", "flashjolt_cap",
            "supported_methods"]

@@ -36,7 +36,9 @@ class KVC:
     SCALE_CHANNEL, SCALE_GROUP, SCALE_TENSOR = 0, 1, 2
     MAX_CELLS = 64
     NOALLOC_SCRATCH_BYTES = 8 << 20
+    ERR_ARG = -1
     ERR_WORKSPACE = -5
+    ERR_UNSUPPORTED = -8
 
 
 _SIGNATURES = {
@@ -61,6 +63,10 @@ _SIGNATURES = {
                            PP, P, SZ, P]),
     "kvc_decompress_noalloc": (I, [I, PP, PP, PP, I, I, I, I, PP, PP, PP, I, I64, I64, I, I, I, P, I64,
                                    I64, I, PP, P]),
+    "kvc_decode_plan_bytes": (SZ, []),
+    "kvc_decode_plan_init": (I, [P, SZ, I, PP, PP, PP, I, I, I, I, PP, PP, PP, I, I64, I64, I, I, I, P, I,
+                                 P, SZ, P]),
+    "kvc_decode_plan_run": (I, [P, SZ, I64, I64, PP, P]),
     "kvc_set_kernel_policy": (I, [I]),
     "kvc_device_error": (I, [ctypes.POINTER(I)]),
     "kvc_cast": (I, [I64, P, I, P, I, P]),

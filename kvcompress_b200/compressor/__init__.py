@@ -8,8 +8,9 @@ from kvcompress_b200.compressor.flashjolt import FlashJoLTCompressor, flashjolt_
 from kvcompress_b200.compressor.identity import IdentityCompressor
 from kvcompress_b200.compressor.jolt import JoLTCompressor
 from kvcompress_b200.compressor.quantization_only import IntQuantOnlyCompressor
+from kvcompress_b200.compressor.stream import DecodeStream
 
 __all__ = ["Allocation", "AllocationResult", "Cell", "CompressedPayload", "CompressorStats",
-           "FlashJoLTCompressor", "IdentityCompressor", "IntQuantOnlyCompressor", "JoLTCompressor",
+           "DecodeStream", "FlashJoLTCompressor", "IdentityCompressor", "IntQuantOnlyCompressor", "JoLTCompressor",
            "JointAllocator", "KVCompressor", "METHODS", "build_compressor", "flashjolt_cap",
            "supported_methods"]

@@ -186,6 +186,32 @@ def _batch_of(views: list[torch.Tensor]) -> torch.Tensor:
     return torch.stack(views)
 
 
+def decode_args(payloads, out_dtype: torch.dtype | None = None):
+    """``(shape, out dtype, device, keyword arguments of ops.decompress)`` of
+    same-layout JoLT payloads (at most ``KVC.MAX_CELLS``)."""
+    p0 = payloads[0]
+    m, t, d = (int(s) for s in p0.shape)
+    dev = p0.data["core"].device
+    odt = out_dtype or p0.dtype
+    kw: dict = {"factors": ([p.data["core"] for p in payloads], [p.data["u_token"] for p in payloads],
+                            [p.data["u_feature"] for p in payloads])}
+    bits = int(p0.metadata.get("bits", 0)) if "residual_packed" in p0.data else 0
+    if bits and p0.data["residual_packed"].numel() == 0:
+        bits = 0
+    if bits > 0:
+        meta = p0.metadata
+        mode = scale_mode_of(bool(meta["residual_per_channel"]), meta.get("residual_group_size"), d)
+        proj = cached_projection(d, d, distribution=meta["residual_distribution"],
+                                 seed=int(meta["residual_seed"]), device=dev, dtype=torch.float32,
+                                 sparsity=float(meta["residual_sparsity"])).matrix
+        kw.update(codes=[p.data["residual_packed"] for p in payloads],
+                  scales=[p.data["residual_scale"] for p in payloads],
+                  zps=[p.data["residual_zero_point"] for p in payloads], bits=bits,
+                  symmetric=bool(meta["residual_symmetric"]), scale_mode=mode,
+                  group_size=meta.get("residual_group_size"), proj=proj)
+    return (m, t, d), odt, dev, kw
+
+
 def decompress_cells(payloads, out_dtype: torch.dtype | None = None, t0: int = 0,
                      t1: int | None = None) -> list[torch.Tensor]:
     """Reconstruct same-layout JoLT payloads in one fused launch per batch.
@@ -193,31 +219,10 @@ def decompress_cells(payloads, out_dtype: torch.dtype | None = None, t0: int = 0
     ``payloads`` share shape, ranks, bits and quantiser settings; returns
     ``(m, t1 - t0, d)`` tensors in each payload's original dtype.
     """
-    p0 = payloads[0]
     if len(payloads) > KVC.MAX_CELLS:
         out = []
         for i in range(0, len(payloads), KVC.MAX_CELLS):
             out += decompress_cells(payloads[i:i + KVC.MAX_CELLS], out_dtype, t0, t1)
         return out
-    m, t, d = (int(s) for s in p0.shape)
-    dev = p0.data["core"].device
-    odt = out_dtype or p0.dtype
-    factors = ([p.data["core"] for p in payloads], [p.data["u_token"] for p in payloads],
-               [p.data["u_feature"] for p in payloads])
-    bits = int(p0.metadata.get("bits", 0)) if "residual_packed" in p0.data else 0
-    if bits and p0.data["residual_packed"].numel() == 0:
-        bits = 0
-    kw = {}
-    if bits > 0:
-        meta = p0.metadata
-        mode = scale_mode_of(bool(meta["residual_per_channel"]), meta.get("residual_group_size"), d)
-        proj = cached_projection(d, d, distribution=meta["residual_distribution"],
-                                 seed=int(meta["residual_seed"]), device=dev, dtype=torch.float32,
-                                 sparsity=float(meta["residual_sparsity"])).matrix
-        kw = dict(codes=[p.data["residual_packed"] for p in payloads],
-                  scales=[p.data["residual_scale"] for p in payloads],
-                  zps=[p.data["residual_zero_point"] for p in payloads], bits=bits,
-                  symmetric=bool(meta["residual_symmetric"]), scale_mode=mode,
-                  group_size=meta.get("residual_group_size"), proj=proj)
-    return ops.decompress((m, t, d), odt, factors=factors, t0=t0, t1=t1, n_cells=len(payloads),
-                          device=dev, **kw)
+    shape, odt, dev, kw = decode_args(payloads, out_dtype)
+    return ops.decompress(shape, odt, t0=t0, t1=t1, n_cells=len(payloads), device=dev, **kw)

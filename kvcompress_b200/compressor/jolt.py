@@ -31,6 +31,20 @@ from kvcompress_b200.compressor.svd import SVD
 _GROUP_META = ("bits", "residual_seed", "residual_distribution", "residual_sparsity", "residual_symmetric",
                "residual_per_channel", "residual_group_size")
 
+def group_payloads(flat) -> list[list[int]]:
+    """Indices of payloads that can share one decode launch (same shape,
+    dtype, ranks, factor dtype, device, bits and quantiser settings)."""
+    groups: dict[tuple, list[int]] = {}
+    for i, p in enumerate(flat):
+        md = p.metadata
+        core = p.data["core"]
+        packed = p.data.get("residual_packed")
+        gk = (tuple(p.shape), p.dtype, core.shape, core.dtype, core.get_device(),
+              packed is not None and packed.numel() > 0, *(md.get(k) for k in _GROUP_META))
+        groups.setdefault(gk, []).append(i)
+    return list(groups.values())
+
+
 _DESC: dict[tuple[int, int, int, int], tuple[torch.Tensor, torch.Tensor, torch.Tensor]] = {}
 
 __all__ = ["JoLTCompressor", "JoLTFactors"]
@@ -171,16 +185,8 @@ class JoLTCompressor(KVCompressor):
         for p in flat:
             if p.method != "jolt":
                 raise ValueError(f"JoLT cannot decode payload with method={p.method!r}")
-        groups: dict[tuple, list[int]] = {}
-        for i, p in enumerate(flat):
-            md = p.metadata
-            core = p.data["core"]
-            packed = p.data.get("residual_packed")
-            gk = (tuple(p.shape), p.dtype, core.shape, core.dtype, core.get_device(),
-                  packed is not None and packed.numel() > 0, *(md.get(k) for k in _GROUP_META))
-            groups.setdefault(gk, []).append(i)
         outs: list[torch.Tensor | None] = [None] * len(flat)
-        for members in groups.values():
+        for members in group_payloads(flat):
             rec = decompress_cells([flat[i] for i in members])
             for i, r in zip(members, rec):
                 outs[i] = r

@@ -16,6 +16,7 @@
 #include <algorithm>
 
 #include "kvc_common.cuh"
+#include "kvc_plan.cuh"
 #include "kvc_quant.cuh"
 
 namespace kvc {
@@ -658,4 +659,61 @@ extern "C" int kvc_decompress(int n_cells, const uint8_t* const* codes, const fl
     decompress_kernel<T><<<grid, NT, smem, st>>>(a);
   });
   return check_launch("decompress_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// Decode plans (token-range streams).  A plan is host bytes owned by the
+// caller: a magic word, then the TcDecodePlan (copied through an aligned
+// local, since the caller's buffer need not be 64-byte aligned).
+
+namespace {
+constexpr uint64_t kPlanMagic = 0x6b76635f706c616eull;  // "kvc_plan"
+constexpr size_t kPlanHeader = 64;                      // keeps the plan body 64-byte aligned in place
+}  // namespace
+
+extern "C" size_t kvc_decode_plan_bytes(void) { return kPlanHeader + sizeof(TcDecodePlan); }
+
+extern "C" int kvc_decode_plan_init(void* plan, size_t plan_bytes, int n_cells, const uint8_t* const* codes,
+                                    const float* const* scale, const int32_t* const* zp, int bits, int symmetric,
+                                    int scale_mode, int group_size, const void* const* core,
+                                    const void* const* u_token, const void* const* u_feature, int factor_dtype,
+                                    int64_t m, int64_t t, int d, int rt, int rd, const float* proj, int out_dtype,
+                                    void* workspace, size_t ws_bytes, void* stream) {
+  if (!plan || plan_bytes < kvc_decode_plan_bytes()) return fail(KVC_ERR_ARG, "kvc_decode_plan_init: plan buffer too small");
+  memset(plan, 0, kvc_decode_plan_bytes());
+  if (n_cells <= 0 || n_cells > KVC_MAX_CELLS) return fail(KVC_ERR_ARG, "kvc_decode_plan_init: bad n_cells");
+  if (m <= 0 || t <= 0 || d <= 0 || d > MAXD) return fail(KVC_ERR_SHAPE, "kvc_decode_plan_init: bad shape");
+  if (bits != 0 && bits != 2 && bits != 4 && bits != 8) return fail(KVC_ERR_ARG, "kvc_decode_plan_init: bad bits");
+  if (rt < 0 || rd < 0 || (rt == 0) != (rd == 0) || rd > d)
+    return fail(KVC_ERR_SHAPE, "kvc_decode_plan_init: bad ranks");
+  if (!dtype_ok(out_dtype) || (rt > 0 && !dtype_ok(factor_dtype)))
+    return fail(KVC_ERR_DTYPE, "kvc_decode_plan_init: bad dtype");
+  for (int c = 0; c < n_cells; ++c) {
+    if (bits > 0 && (!codes[c] || !scale[c] || !zp[c])) return fail(KVC_ERR_ARG, "kvc_decode_plan_init: NULL codes");
+    if (rt > 0 && (!core[c] || !u_token[c] || !u_feature[c]))
+      return fail(KVC_ERR_ARG, "kvc_decode_plan_init: NULL factor");
+  }
+  (void)group_size;
+  if (!(g_policy == 0 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj) &&
+        all_aligned(n_cells, codes)))
+    return fail(KVC_ERR_UNSUPPORTED,
+                "kvc_decode_plan_init: no tensor-core plan for this layout (decode with kvc_decompress)");
+  TcDecodePlan local;
+  const int rc = tc_decode_plan_init(&local, n_cells, codes, scale, bits, core, u_token, u_feature, factor_dtype, m,
+                                     t, d, rt, rd, proj, workspace, ws_bytes, static_cast<cudaStream_t>(stream));
+  if (rc) return rc;
+  memcpy(static_cast<uint8_t*>(plan) + kPlanHeader, &local, sizeof(local));
+  memcpy(plan, &kPlanMagic, sizeof(kPlanMagic));
+  return KVC_OK;
+}
+
+extern "C" int kvc_decode_plan_run(const void* plan, size_t plan_bytes, int64_t t0, int64_t t1, void* const* out,
+                                   void* stream) {
+  uint64_t magic = 0;
+  if (!plan || plan_bytes < kvc_decode_plan_bytes()) return fail(KVC_ERR_ARG, "kvc_decode_plan_run: plan buffer too small");
+  memcpy(&magic, plan, sizeof(magic));
+  if (magic != kPlanMagic) return fail(KVC_ERR_ARG, "kvc_decode_plan_run: not an initialised plan");
+  TcDecodePlan local;
+  memcpy(&local, static_cast<const uint8_t*>(plan) + kPlanHeader, sizeof(local));
+  return tc_decode_plan_run(&local, t0, t1, out, static_cast<cudaStream_t>(stream));
 }

@@ -36,6 +36,7 @@
 #include <type_traits>
 
 #include "kvc_common.cuh"
+#include "kvc_plan.cuh"
 #include "kvc_quant.cuh"
 #include "kvc_sched.cuh"
 #include "kvc_tc.cuh"
@@ -1494,22 +1495,29 @@ size_t tc_decompress_workspace(int n_cells, int64_t rows, int d, int rd) {
   return align256(bimg) + align256((size_t)n_cells * rows * rdm_dec(rd) * 4 + 132 * 4);
 }
 
-int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* const* scale, int bits,
-                         const void* const* core, const void* const* u_token, const void* const* u_feature,
-                         int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd, const float* proj,
-                         int64_t t0, int64_t t1, void* const* out, void* workspace, size_t ws_bytes,
-                         cudaStream_t st) {
+// A decode plan holds what does not depend on the token range: the codes'
+// tensor maps, the factor pointers and, in its workspace, each cell's B image
+// (built once by prep_decode_kernel).  Runs then decode any [t0, t1) with the
+// Tucker-term kernel and the decode kernel only.
+int tc_decode_plan_init(TcDecodePlan* p, int n_cells, const uint8_t* const* codes, const float* const* scale,
+                        int bits, const void* const* core, const void* const* u_token,
+                        const void* const* u_feature, int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd,
+                        const float* proj, void* workspace, size_t ws_bytes, cudaStream_t st) {
   if (!workspace || ws_bytes < tc_decompress_workspace(n_cells, m * t, d, rd))
     return fail(KVC_ERR_WORKSPACE, "tensor-core decompress: workspace too small");
-  const int64_t tl = t1 - t0;
-  const int rdm = rdm_dec(rd);
-  if (t >= (1LL << 31) || m * tl * rdm >= (1LL << 31) || ceil_div(tl, TILE_M) * m >= (1LL << 31))
+  if (t >= (1LL << 31) || m * t * rdm_dec(rd) >= (1LL << 31) || ceil_div(t, TILE_M) * m >= (1LL << 31))
     return fail(KVC_ERR_SHAPE, "tensor-core decompress: shape too large");
-  TmaMaps cmaps, omaps;
-  DecArgsTc a;
-  memset(&a, 0, sizeof(a));
-  CellPtrs sc;
+  memset(p, 0, sizeof(*p));
+  p->n_cells = n_cells;
+  p->d = d;
+  p->bits = bits;
+  p->rt = rt;
+  p->rd = rd;
+  p->factor_dtype = factor_dtype;
+  p->m = m;
+  p->t = t;
   const int cb = d * bits / 8;
+  CellPtrs sc, uf;
   int rc;
   for (int c = 0; c < n_cells; ++c) {
     const uint64_t dims[3] = {(uint64_t)cb, (uint64_t)t, (uint64_t)m};
@@ -1521,8 +1529,38 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
                                    : cb == 64 ? CU_TENSOR_MAP_SWIZZLE_64B
                                    : cb == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
                                               : CU_TENSOR_MAP_SWIZZLE_NONE;
-    if ((rc = encode_tma(&cmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, codes[c], dims, strides, box, swz)))
+    if ((rc = encode_tma(&p->cmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, codes[c], dims, strides, box, swz)))
       return rc;
+    sc.p[c] = scale[c];
+    uf.p[c] = rt > 0 ? u_feature[c] : nullptr;
+    if (rt > 0) {
+      p->core.p[c] = core[c];
+      p->ut.p[c] = u_token[c];
+      p->ud.p[c] = u_feature[c];
+    }
+  }
+  const int tucker_block = rdm_dec(rd) == 1;
+  p->bimg = static_cast<uint8_t*>(workspace);
+  p->tmp = reinterpret_cast<float*>(
+      p->bimg + align256((size_t)n_cells * ((size_t)4 * d * d + (tucker_block ? (size_t)128 * d : 0))));
+  prep_decode_kernel<<<dim3((d * d + d * 64 + 255) / 256, n_cells), 256, 0, st>>>(proj, sc, uf, factor_dtype,
+                                                                                tucker_block, d, p->bimg);
+  return check_launch("prep_decode_kernel");
+}
+
+int tc_decode_plan_run(const TcDecodePlan* p, int64_t t0, int64_t t1, void* const* out, cudaStream_t st) {
+  const int n_cells = p->n_cells, d = p->d, bits = p->bits, rt = p->rt, rd = p->rd;
+  const int64_t m = p->m, t = p->t;
+  if (t0 < 0 || t1 > t || t0 >= t1) return fail(KVC_ERR_SHAPE, "tensor-core decompress: bad token range");
+  const int64_t tl = t1 - t0;
+  const int rdm = rdm_dec(rd);
+  TmaMaps omaps;
+  DecArgsTc a;
+  memset(&a, 0, sizeof(a));
+  int rc;
+  for (int c = 0; c < n_cells; ++c) {
+    if (!out[c] || (reinterpret_cast<uintptr_t>(out[c]) & 15u))
+      return fail(KVC_ERR_ALIGN, "tensor-core decompress: output not 16-byte aligned");
     // output (m, tl, d) bf16: boxes of d/2 features x 32 tokens, swizzled by
     // their d-byte rows
     const uint64_t od[3] = {(uint64_t)d, (uint64_t)tl, (uint64_t)m};
@@ -1531,9 +1569,8 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
     if ((rc = encode_tma(&omaps.m[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out[c], od, os, ob,
                          d == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
       return rc;
-    sc.p[c] = scale[c];
     a.out.p[c] = out[c];
-    if (rt > 0) a.ud.p[c] = u_feature[c];
+    if (rt > 0) a.ud.p[c] = p->ud.p[c];
   }
   a.m = m;
   a.t0 = t0;
@@ -1545,30 +1582,17 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
   a.tiles_per_cta = ceil_div(a.total_tiles, ctas);
   a.rt = rt;
   a.rd = rd;
-  a.factor_dtype = factor_dtype;
-  const int tucker_block = rdm == 1;
-  uint8_t* bimg = static_cast<uint8_t*>(workspace);
-  float* tmp = reinterpret_cast<float*>(
-      bimg + align256((size_t)n_cells * ((size_t)4 * d * d + (tucker_block ? (size_t)128 * d : 0))));
-  a.bimg = bimg;
-  a.tmp = tmp;
-  CellPtrs uf;
-  for (int c = 0; c < n_cells; ++c) uf.p[c] = rt > 0 ? u_feature[c] : nullptr;
-  prep_decode_kernel<<<dim3((d * d + d * 64 + 255) / 256, n_cells), 256, 0, st>>>(proj, sc, uf, factor_dtype,
-                                                                                tucker_block, d, bimg);
-  if ((rc = check_launch("prep_decode_kernel"))) return rc;
+  a.factor_dtype = p->factor_dtype;
+  a.bimg = p->bimg;
+  a.tmp = p->tmp;
   if (rt > 0) {
-    CellPtrs cp, up;
-    for (int c = 0; c < n_cells; ++c) {
-      cp.p[c] = core[c];
-      up.p[c] = u_token[c];
-    }
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(m * tl * rdm, 256), 1024));
-    tucker_rows_kernel<<<dim3(blocks, n_cells), 256, 0, st>>>(cp, up, factor_dtype, KVC_F32, m, t0, tl, rt, rd, rdm,
-                                                              m * tl, tmp);
+    tucker_rows_kernel<<<dim3(blocks, n_cells), 256, 0, st>>>(p->core, p->ut, p->factor_dtype, KVC_F32, m, t0, tl, rt,
+                                                              rd, rdm, m * tl, p->tmp);
     if ((rc = check_launch("tucker_rows_kernel"))) return rc;
   }
   const dim3 grid((unsigned)ceil_div(a.total_tiles, a.tiles_per_cta));
+  const TmaMaps& cmaps = p->cmaps;
 #define KVC_TC_DEC3(DD, RR, BB)                                      \
   do {                                                               \
     constexpr int NSD = DecStages<DD, DD * BB / 8, RR>::value;       \
@@ -1596,6 +1620,18 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
 #undef KVC_TC_DEC3
 #undef KVC_TC_DEC
   return check_launch("tc_decode_kernel");
+}
+
+int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* const* scale, int bits,
+                         const void* const* core, const void* const* u_token, const void* const* u_feature,
+                         int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd, const float* proj,
+                         int64_t t0, int64_t t1, void* const* out, void* workspace, size_t ws_bytes,
+                         cudaStream_t st) {
+  TcDecodePlan plan;
+  int rc = tc_decode_plan_init(&plan, n_cells, codes, scale, bits, core, u_token, u_feature, factor_dtype, m, t, d,
+                               rt, rd, proj, workspace, ws_bytes, st);
+  if (rc) return rc;
+  return tc_decode_plan_run(&plan, t0, t1, out, st);
 }
 
 int tc_read_device_error(int* out) {

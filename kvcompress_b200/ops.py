@@ -18,6 +18,7 @@ from kvcompress_b200._native import KVC, check, lib, ptr_array
 __all__ = [
     "DTYPE_CODE",
     "Cells",
+    "DecodePlan",
     "apply_basis",
     "cells",
     "cast",
@@ -405,6 +406,59 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
                                    ws.data_ptr(), ws.numel(), _stream()),
               "kvc_decompress")
     return out
+
+
+class DecodePlan:
+    """A tensor-core decode prepared once for token-range runs
+    (``kvc_decode_plan_init`` / ``kvc_decode_plan_run``).
+
+    Holds the plan's host bytes, its own device workspace (the cells' B
+    images and the Tucker row terms) and references to the payload tensors,
+    which must not change while the plan lives.  ``run(t0, t1)`` decodes
+    tokens ``[t0, t1)`` of every cell with two kernel launches, bit for bit
+    the rows ``decompress`` gives for that range.  Use one plan from one
+    stream at a time.  ``DecodePlan.make`` returns None for layouts without a
+    tensor-core plan (decode those with ``decompress``).
+    """
+
+    def __init__(self, L, buf, ws, keep, shape, out_dtype, n, device, m, t, d, bits):
+        self._L, self._buf, self._ws, self._keep = L, buf, ws, keep
+        self.shape, self.out_dtype, self.n_cells, self.device = shape, out_dtype, n, device
+        self._m, self._t, self._d, self._bits = m, t, d, bits
+        self._codes_bytes = [c.numel() for c in keep[0]] if bits > 0 else [0] * n
+
+    @classmethod
+    def make(cls, shape, out_dtype: torch.dtype, *, codes, scales, zps, bits: int, symmetric: bool = True,
+             scale_mode: int = KVC.SCALE_CHANNEL, group_size=None, factors=None, proj=None):
+        m, t, d = (int(s) for s in shape)
+        n = len(codes)
+        L = lib()
+        cp, up, dp, rt, rd = _factor_ptrs(factors, n)
+        fdt = _code(factors[0][0].dtype) if factors is not None else KVC.F16
+        dev = codes[0].device
+        ws = torch.empty(max(int(L.kvc_decompress_workspace_bytes(n, m * t, d, rd)), 256), dtype=torch.uint8,
+                         device=dev)
+        nb = int(L.kvc_decode_plan_bytes())
+        buf = ctypes.create_string_buffer(nb)
+        rc = L.kvc_decode_plan_init(buf, nb, n, _ptrs(codes), _ptrs(scales), _ptrs(zps), bits, int(symmetric),
+                                    scale_mode, int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
+                                    proj.data_ptr() if proj is not None else None, _code(out_dtype),
+                                    ws.data_ptr(), ws.numel(), _stream())
+        if rc == KVC.ERR_UNSUPPORTED:
+            return None
+        check(rc, "kvc_decode_plan_init")
+        keep = (list(codes), list(scales), list(zps), factors, proj)
+        return cls(L, buf, ws, keep, (m, t, d), out_dtype, n, dev, m, t, d, bits)
+
+    def run(self, t0: int, t1: int, out=None) -> Cells:
+        m, t, d = self._m, self._t, self._d
+        if out is None:
+            out = _views(torch.empty(self.n_cells, m, t1 - t0, d, dtype=self.out_dtype, device=self.device))
+        nbytes = self.n_cells * out[0].numel() * out[0].element_size() + sum(self._codes_bytes) * (t1 - t0) // t
+        with _Stage("decode_range", 2, nbytes):
+            check(self._L.kvc_decode_plan_run(self._buf, len(self._buf), int(t0), int(t1), _ptrs(out), _stream()),
+                  "kvc_decode_plan_run")
+        return out
 
 
 def decompress_noalloc(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=None, bits: int = 0,
