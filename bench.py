@@ -47,7 +47,7 @@ def parse_args():
     ap.add_argument("--workload", default="llama3-8b-kv-b1-t8192-bf16")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--stream-block", type=int, default=256, help="tokens per block of the decode-stream line")
+    ap.add_argument("--stream-block", type=int, default=256, help="tokens per block of the decode-stream line (0: no such line)")
     ap.add_argument("--cpu-sample-layers", type=int, default=1)
     ap.add_argument("--layers", type=int, default=0,
                     help="override the workload's layer count (profiling a smaller case)")
@@ -377,7 +377,8 @@ def run_ours(args, w):
                      "algorithmic_bytes": dbytes / dcalls, "launch_ms": dms / dcalls},
         "stages_ms_per_step": {k: v[0] / args.steps for k, v in sorted(stage.items())},
     }
-    line["decode_stream"] = decode_stream(payloads, world, dev, block=args.stream_block)
+    if args.stream_block > 0:
+        line["decode_stream"] = decode_stream(payloads, world, dev, block=args.stream_block)
     if not args.no_e2e:
         line["e2e"] = e2e(comp, pairs, w, dev, world, steps=min(args.steps, 3))
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -213,6 +213,37 @@ int kvc_decompress_noalloc(int n_cells, const uint8_t* const* codes, const float
                            int out_dtype, void* const* out, void* stream);
 
 /*
+ * The whole compress of a batch of same-shape cells in one call:
+ * partial_tucker_st_hosvd + encode_residual (tucker.py:192-279,
+ * residual.py:155-239, as orchestrated by jolt.py:273-329).  Runs kvc_gram,
+ * kvc_sketch_solve, kvc_project_feature, kvc_gram, kvc_sketch_solve,
+ * kvc_apply_basis, kvc_core, kvc_residual_stats (not for group scales),
+ * kvc_residual_quant and the factor casts on one stream.  rt / rd are the
+ * clipped ranks, mode_* / k_* the SVD mode and sketch width of each side
+ * (omega_f: (m*T, k_f) and omega_t: (m*rd, k_t) float32, NULL for exact).
+ * Outputs are contiguous batches, cell-major: core (n, m, rt, rd),
+ * u_token (n, T, rt), u_feature (n, d, rd) in the cell dtype; core_f /
+ * u_token_f / u_feature_f in factor_dtype (NULL: no cast); tails (n,) fp64;
+ * with bits > 0 scales / zero points ((n, d), (n, m*T, d/g) or (n,)) and
+ * codes (n, m*T, ceil(d*bits/8)).  Intermediates live in the workspace.
+ */
+size_t kvc_compress_workspace_bytes(int n_cells, int64_t m, int64_t t, int d, int dtype, int rt, int rd,
+                                    int mode_f, int k_f, int mode_t, int k_t, int bits, int scale_mode);
+int kvc_compress(int n_cells, const void* const* x, int64_t m, int64_t t, int d, int dtype, int rt, int rd,
+                 int mode_f, int k_f, const float* omega_f, int mode_t, int k_t, const float* omega_t,
+                 int n_power, const float* proj, int bits, int symmetric, int scale_mode, int group_size,
+                 int stat_dtype, int arith_dtype, int factor_dtype, void* core_out, void* u_token_out,
+                 void* u_feature_out, void* core_f, void* u_token_f, void* u_feature_f,
+                 double* tail_token, double* tail_feature, float* scale_out, int32_t* zp_out,
+                 uint8_t* codes_out, void* workspace, size_t ws_bytes, void* stream);
+
+/* Stage timing of kvc_compress on the calling thread: events[2 i] and
+ * events[2 i + 1] (cudaEvent_t) are recorded on the call's stream around
+ * stage i = feature Gram, feature solve, projection, token Gram, token
+ * solve, U_T, core, residual stats, quantise, casts.  n_events = 0 stops. */
+int kvc_trace_stages(void* const* events, int n_events);
+
+/*
  * Token-range decode streams (a consumer that reads the cache in blocks of
  * tokens, e.g. 256-token blocks per layer).  The reference decodes a whole
  * payload per call (reconstruct_payload, jolt.py:401-463); these split that

@@ -146,31 +146,32 @@ def compress_cells(
         return out
     xs = ops.cells(xs, "compress")
     mode_scale = scale_mode_of(per_channel, group_size, d) if bits > 0 else KVC.SCALE_CHANNEL
-    core, u_token, u_feature, tail_t, tail_f = tucker_cells(
-        xs, r_token=r_token, r_feature=r_feature, svd=svd, cap=cap,
-        forced_randomised=forced_randomised)
-
-    # --- residual -----------------------------------------------------------
-    packed = scale = zps = [None] * n
+    # ranks clipped by the axis lengths and each side's SVD mode and sketch
+    # (tucker.py:230-262, svd.py:221-316): the same decisions as tucker_cells
+    rt_req = max(1, min(int(r_token), t))
+    rd_req = max(1, min(int(r_feature), d))
+    mode_f, rd, k_f = svd.resolve(d, m * t, rd_req, cap, forced_randomised)
+    om_f = sketch_omega(m * t, k_f, svd.seed, dev) if mode_f == KVC.SVD_RANDOMISED else None
+    c = m * rd
+    mode_t, rt, k_t = svd.resolve(t, c, rt_req, cap, forced_randomised)
+    om_t = sketch_omega(c, k_t, svd.seed, dev) if mode_t == KVC.SVD_RANDOMISED else None
+    proj = cached_projection(d, d, distribution=jl_distribution, seed=seed, device=dev, dtype=torch.float32,
+                             sparsity=sparsity).matrix if bits > 0 else None
+    r = ops.compress(xs, rt=rt, rd=rd, mode_f=mode_f, k_f=k_f, omega_f=om_f, mode_t=mode_t, k_t=k_t,
+                     omega_t=om_t, n_power=svd.n_power, proj=proj, bits=bits, symmetric=symmetric,
+                     scale_mode=mode_scale, group_size=group_size, factor_dtype=factor_dtype)
+    core, u_token, u_feature = ops.split(r["core"]), ops.split(r["u_token"]), ops.split(r["u_feature"])
+    tail_t, tail_f = ops.split(r["tail_token"]), ops.split(r["tail_feature"])
     if bits > 0:
-        proj = cached_projection(d, d, distribution=jl_distribution, seed=seed, device=dev,
-                                 dtype=torch.float32, sparsity=sparsity).matrix
-        factors = (core, u_token, u_feature)
-        if mode_scale == KVC.SCALE_GROUP:
-            packed, scale, zps = ops.residual_quant(
-                xs, factors, proj, None, None, bits=bits, symmetric=symmetric, scale_mode=mode_scale,
-                group_size=group_size, stat_dtype=torch.float32, arith_dtype=torch.float32)
-        else:
-            scale, zps = ops.residual_stats(xs, factors, proj, bits=bits, symmetric=symmetric,
-                                            scale_mode=mode_scale, stat_dtype=torch.float32)
-            packed, _, _ = ops.residual_quant(
-                xs, factors, proj, scale, zps, bits=bits, symmetric=symmetric, scale_mode=mode_scale,
-                group_size=None, stat_dtype=torch.float32, arith_dtype=torch.float32)
+        packed, scale, zps = ops.split(r["codes"]), ops.split(r["scale"]), ops.split(r["zero_point"])
+    else:
+        packed = scale = zps = [None] * n
     stored = [None] * n
     if factor_dtype is not None:
-        batches = [_batch_of(core), _batch_of(u_token), _batch_of(u_feature)]
-        cast = [b if b.dtype == factor_dtype else ops.cast(b, factor_dtype) for b in batches]
-        stored = [(cast[0][i], cast[1][i], cast[2][i]) for i in range(n)]
+        sc, su, sf = (r[k + "_stored"] if r[k + "_stored"] is not None else r[k]
+                      for k in ("core", "u_token", "u_feature"))
+        sc, su, sf = ops.split(sc), ops.split(su), ops.split(sf)
+        stored = [(sc[i], su[i], sf[i]) for i in range(n)]
     return [CellResult(core=core[i], u_token=u_token[i], u_feature=u_feature[i],
                        tail_token=tail_t[i], tail_feature=tail_f[i], bits=bits, packed=packed[i],
                        scale=scale[i], zero_point=zps[i], factors_stored=stored[i]) for i in range(n)]
@@ -181,7 +182,9 @@ def _batch_of(views: list[torch.Tensor]) -> torch.Tensor:
     if isinstance(views, ops.Cells) and views.batch is not None:
         return views.batch
     base = views[0]._base
-    if base is not None and base.shape[0] == len(views) and base[0].data_ptr() == views[0].data_ptr():
+    if (base is not None and base.dim() == views[0].dim() + 1 and base.shape[0] == len(views)
+            and base.shape[1:] == views[0].shape and base[0].data_ptr() == views[0].data_ptr()
+            and all(v._base is base for v in views)):
         return base
     return torch.stack(views)
 

@@ -116,6 +116,7 @@ class JoLTCompressor(KVCompressor):
         """Compress several layers; cells of equal shape and allocation share launches."""
         t_start = time.perf_counter()
         plans = []
+        alloc_of: dict[tuple[int, int, int], AllocationResult] = {}  # layers of one shape share the allocation
         for key, value in pairs:
             if key.shape != value.shape:
                 raise ValueError(f"K/V shape mismatch: {key.shape} vs {value.shape}")
@@ -128,9 +129,12 @@ class JoLTCompressor(KVCompressor):
                 if x.dtype not in _DTYPES:
                     raise TypeError(f"unsupported K/V dtype {x.dtype}")
             m, t, d = key.shape
-            res = self.allocator.optimize([
-                Cell(shape=(m, t, d), kind="key", layer_group=0, candidate_bits=self.bits),
-                Cell(shape=(m, t, d), kind="value", layer_group=0, candidate_bits=self.bits)])
+            res = alloc_of.get((m, t, d))
+            if res is None:
+                res = self.allocator.optimize([
+                    Cell(shape=(m, t, d), kind="key", layer_group=0, candidate_bits=self.bits),
+                    Cell(shape=(m, t, d), kind="value", layer_group=0, candidate_bits=self.bits)])
+                alloc_of[(m, t, d)] = res
             plans.append(res)
         # group cells by (shape, dtype, allocation) so each group is one batch
         groups: dict[tuple, list[tuple[int, int]]] = {}
@@ -141,7 +145,9 @@ class JoLTCompressor(KVCompressor):
         results: dict[tuple[int, int], CellResult] = {}
         order, tails_t, tails_f = [], [], []
         for (shape, _, _, (rt, rd, b)), members in groups.items():
-            xs = [pairs[li][side].contiguous() for li, side in members]
+            # same shape, dtype and device by the grouping, CUDA and a K/V dtype by
+            # the checks above: the batch goes to the kernels without re-checks
+            xs = ops.Cells([pairs[li][side].contiguous() for li, side in members])
             cell_res = self._compress_cells(xs, rt, rd, b, shape[1])
             for (li, side), r in zip(members, cell_res):
                 results[(li, side)] = r
@@ -156,8 +162,8 @@ class JoLTCompressor(KVCompressor):
             kp = self.build_payload(key, JoLTFactors(results[(li, 0)], None, k_alloc), (0.0, 0.0))
             vp = self.build_payload(value, JoLTFactors(results[(li, 1)], None, v_alloc), (0.0, 0.0))
             out.append((kp, vp))
-        tails = torch.stack([torch.cat(tails_t), torch.cat(tails_f)], dim=1).cpu().tolist()
-        for (li, side), (tt, tf) in zip(order, tails):
+        flat = torch.cat(tails_t + tails_f).cpu().tolist()
+        for (li, side), tt, tf in zip(order, flat[:len(order)], flat[len(order):]):
             md = out[li][side].metadata
             md["tail_token_mass"] = float(tt)
             md["tail_feature_mass"] = float(tf)

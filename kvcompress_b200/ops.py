@@ -21,6 +21,7 @@ __all__ = [
     "DecodePlan",
     "apply_basis",
     "cells",
+    "compress",
     "cast",
     "core",
     "decompress",
@@ -406,6 +407,85 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
                                    ws.data_ptr(), ws.numel(), _stream()),
               "kvc_decompress")
     return out
+
+
+def compress(xs, *, rt: int, rd: int, mode_f: int, k_f: int, omega_f: torch.Tensor | None, mode_t: int, k_t: int,
+             omega_t: torch.Tensor | None, n_power: int, proj: torch.Tensor | None, bits: int, symmetric: bool,
+             scale_mode: int, group_size: int | None, factor_dtype: torch.dtype | None,
+             stat_dtype: torch.dtype = torch.float32, arith_dtype: torch.dtype = torch.float32) -> dict:
+    """The whole compress of same-shape cells in one C call (``kvc_compress``).
+
+    Returns batches (first dimension = cell): ``core`` (n, m, rt, rd),
+    ``u_token`` (n, T, rt), ``u_feature`` (n, d, rd) in the cell dtype, the
+    same in ``factor_dtype`` under ``*_stored`` (None when the dtypes agree),
+    ``tail_token`` / ``tail_feature`` (n,) float64 and, with ``bits > 0``,
+    ``scale`` / ``zero_point`` / ``codes``."""
+    xs = _cells(xs, "compress")
+    m, t, d = (int(v) for v in xs[0].shape)
+    dev, dt = xs[0].device, xs[0].dtype
+    n = len(xs)
+    L = lib()
+    core_ = torch.empty(n, m, rt, rd, dtype=dt, device=dev)
+    ut = torch.empty(n, t, rt, dtype=dt, device=dev)
+    ud = torch.empty(n, d, rd, dtype=dt, device=dev)
+    cast = factor_dtype is not None and factor_dtype != dt
+    core_f = torch.empty(n, m, rt, rd, dtype=factor_dtype, device=dev) if cast else None
+    ut_f = torch.empty(n, t, rt, dtype=factor_dtype, device=dev) if cast else None
+    ud_f = torch.empty(n, d, rd, dtype=factor_dtype, device=dev) if cast else None
+    tails = (torch.empty(n, dtype=torch.float64, device=dev), torch.empty(n, dtype=torch.float64, device=dev))
+    out = {"core": core_, "u_token": ut, "u_feature": ud, "core_stored": core_f, "u_token_stored": ut_f,
+           "u_feature_stored": ud_f, "tail_token": tails[0], "tail_feature": tails[1],
+           "scale": None, "zero_point": None, "codes": None}
+    sc = zp = codes = None
+    if bits > 0:
+        if scale_mode == KVC.SCALE_CHANNEL:
+            sshape = (n, d)
+        elif scale_mode == KVC.SCALE_GROUP:
+            sshape = (n, m * t, d // int(group_size))
+        else:
+            sshape = (n,)
+        sc = torch.empty(sshape, dtype=torch.float32, device=dev)
+        zp = torch.empty(sshape, dtype=torch.int32, device=dev)
+        codes = torch.empty(n, m * t, (d * bits + 7) // 8, dtype=torch.uint8, device=dev)
+        out.update(scale=sc, zero_point=zp, codes=codes)
+    ws = workspace(L.kvc_compress_workspace_bytes(n, m, t, d, _code(dt), rt, rd, mode_f, k_f, mode_t, k_t, bits,
+                                                  scale_mode), dev)
+    ptr = lambda x: x.data_ptr() if x is not None else None  # noqa: E731
+    evs = None
+    if _TRACE is not None:
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * len(_COMPRESS_STAGES))]
+        for e in evs:
+            e.record()  # creates the CUDA event the library records again
+        ev_arr = ptr_array(e.cuda_event for e in evs)  # the library keeps this pointer until reset
+        check(L.kvc_trace_stages(ev_arr, len(evs)), "kvc_trace_stages")
+    try:
+        check(L.kvc_compress(n, _ptrs(xs), m, t, d, _code(dt), rt, rd, mode_f, k_f, ptr(omega_f), mode_t, k_t,
+                             ptr(omega_t), n_power, ptr(proj), bits, int(symmetric), scale_mode, int(group_size or 0),
+                             _code(stat_dtype), _code(arith_dtype), _code(factor_dtype or dt), ptr(core_), ptr(ut),
+                             ptr(ud), ptr(core_f), ptr(ut_f), ptr(ud_f), ptr(tails[0]), ptr(tails[1]), ptr(sc),
+                             ptr(zp), ptr(codes), ws.data_ptr(), ws.numel(), _stream()), "kvc_compress")
+    finally:
+        if evs is not None:
+            L.kvc_trace_stages(None, 0)
+            del ev_arr
+    if evs is not None:
+        x_bytes = n * xs[0].numel() * xs[0].element_size()
+        xp_bytes = n * t * m * rd * xs[0].element_size()
+        sizes = {"gram": x_bytes, "sketch_solve": 0, "project_feature": x_bytes + xp_bytes, "apply_basis": xp_bytes,
+                 "core": xp_bytes, "residual_stats": x_bytes,
+                 "residual_quant": x_bytes + (codes.numel() if codes is not None else 0), "cast": 0}
+        for i, (name, launches) in enumerate(_COMPRESS_STAGES):
+            if name in ("residual_stats", "residual_quant") and bits == 0:
+                continue
+            nb = xp_bytes if (name == "gram" and i > 0) else sizes[name]
+            _TRACE.append((name, evs[2 * i], evs[2 * i + 1], launches, nb))
+    return out
+
+
+# kvc_compress's stages in order, with the kernels each launches on the
+# tensor-core path (the stage timing of the bench)
+_COMPRESS_STAGES = [("gram", 5), ("sketch_solve", 1), ("project_feature", 1), ("gram", 4), ("sketch_solve", 1),
+                    ("apply_basis", 1), ("core", 1), ("residual_stats", 5), ("residual_quant", 3), ("cast", 3)]
 
 
 class DecodePlan:
