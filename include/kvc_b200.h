@@ -223,7 +223,10 @@ int kvc_decompress_noalloc(int n_cells, const uint8_t* const* codes, const float
  * (omega_f: (m*T, k_f) and omega_t: (m*rd, k_t) float32, NULL for exact).
  * Outputs are contiguous batches, cell-major: core (n, m, rt, rd),
  * u_token (n, T, rt), u_feature (n, d, rd) in the cell dtype; core_f /
- * u_token_f / u_feature_f in factor_dtype (NULL: no cast); tails (n,) fp64;
+ * u_token_f / u_feature_f in factor_dtype (NULL: no cast); tails (n,) fp64,
+ * also copied to tails_host (2n doubles, token then feature; host memory,
+ * pinned for an asynchronous copy; NULL: no copy) as soon as the solves are
+ * done, after which tails_ready (a cudaEvent_t, optional) is recorded;
  * with bits > 0 scales / zero points ((n, d), (n, m*T, d/g) or (n,)) and
  * codes (n, m*T, ceil(d*bits/8)).  Intermediates live in the workspace.
  */
@@ -234,8 +237,9 @@ int kvc_compress(int n_cells, const void* const* x, int64_t m, int64_t t, int d,
                  int n_power, const float* proj, int bits, int symmetric, int scale_mode, int group_size,
                  int stat_dtype, int arith_dtype, int factor_dtype, void* core_out, void* u_token_out,
                  void* u_feature_out, void* core_f, void* u_token_f, void* u_feature_f,
-                 double* tail_token, double* tail_feature, float* scale_out, int32_t* zp_out,
-                 uint8_t* codes_out, void* workspace, size_t ws_bytes, void* stream);
+                 double* tail_token, double* tail_feature, double* tails_host, void* tails_ready,
+                 float* scale_out, int32_t* zp_out, uint8_t* codes_out, void* workspace, size_t ws_bytes,
+                 void* stream);
 
 /* Stage timing of kvc_compress on the calling thread: events[2 i] and
  * events[2 i + 1] (cudaEvent_t) are recorded on the call's stream around

@@ -69,7 +69,7 @@ _SIGNATURES = {
     "kvc_decode_plan_run": (I, [P, SZ, I64, I64, PP, P]),
     "kvc_compress_workspace_bytes": (SZ, [I, I64, I64, I, I, I, I, I, I, I, I, I, I]),
     "kvc_compress": (I, [I, PP, I64, I64, I, I, I, I, I, I, P, I, I, P, I, P, I, I, I, I, I, I, I, P, P, P, P, P,
-                         P, P, P, P, P, P, P, SZ, P]),
+                         P, P, P, P, P, P, P, P, P, SZ, P]),
     "kvc_trace_stages": (I, [PP, I]),
     "kvc_set_kernel_policy": (I, [I]),
     "kvc_device_error": (I, [ctypes.POINTER(I)]),

@@ -46,6 +46,9 @@ class CellResult:
     scale: torch.Tensor | None
     zero_point: torch.Tensor | None
     factors_stored: tuple | None = None  # (core, u_token, u_feature) in the payload's factor dtype
+    # (pinned host tensor [token tails | feature tails] of the cell's batch,
+    # index of the cell, CUDA event recorded once the host copy is done)
+    tails_host: tuple | None = None
 
 
 def scale_mode_of(per_channel: bool, group_size: int | None, d: int) -> int:
@@ -172,9 +175,11 @@ def compress_cells(
                       for k in ("core", "u_token", "u_feature"))
         sc, su, sf = ops.split(sc), ops.split(su), ops.split(sf)
         stored = [(sc[i], su[i], sf[i]) for i in range(n)]
+    th = r["tails_host"], r["tails_ready"]
     return [CellResult(core=core[i], u_token=u_token[i], u_feature=u_feature[i],
                        tail_token=tail_t[i], tail_feature=tail_f[i], bits=bits, packed=packed[i],
-                       scale=scale[i], zero_point=zps[i], factors_stored=stored[i]) for i in range(n)]
+                       scale=scale[i], zero_point=zps[i], factors_stored=stored[i],
+                       tails_host=(th[0], i, th[1])) for i in range(n)]
 
 
 def _batch_of(views: list[torch.Tensor]) -> torch.Tensor:

@@ -24,7 +24,7 @@ import torch
 from kvcompress_b200 import ops
 from kvcompress_b200.compressor.allocator import AllocationResult, Cell, JointAllocator
 from kvcompress_b200.compressor.base import CompressedPayload, CompressorStats, KVCompressor
-from kvcompress_b200.compressor.cells import CellResult, _batch_of, compress_cells, decompress_cells
+from kvcompress_b200.compressor.cells import CellResult, compress_cells, decompress_cells
 from kvcompress_b200.compressor.svd import SVD
 
 # metadata that must agree for payloads to share one decode launch
@@ -143,7 +143,7 @@ class JoLTCompressor(KVCompressor):
                 gk = (tuple(x.shape), x.dtype, x.device, a.tuple)
                 groups.setdefault(gk, []).append((li, side))
         results: dict[tuple[int, int], CellResult] = {}
-        order, tails_t, tails_f = [], [], []
+        order, tails_t = [], []
         for (shape, _, _, (rt, rd, b)), members in groups.items():
             # same shape, dtype and device by the grouping, CUDA and a K/V dtype by
             # the checks above: the batch goes to the kernels without re-checks
@@ -152,8 +152,7 @@ class JoLTCompressor(KVCompressor):
             for (li, side), r in zip(members, cell_res):
                 results[(li, side)] = r
             order += members
-            tails_t.append(_batch_of([r.tail_token for r in cell_res]))
-            tails_f.append(_batch_of([r.tail_feature for r in cell_res]))
+            tails_t.append(cell_res)
         # payloads first (host work that overlaps the kernels still running),
         # then one host sync for every tail mass (one small copy per batch)
         out = []
@@ -162,8 +161,18 @@ class JoLTCompressor(KVCompressor):
             kp = self.build_payload(key, JoLTFactors(results[(li, 0)], None, k_alloc), (0.0, 0.0))
             vp = self.build_payload(value, JoLTFactors(results[(li, 1)], None, v_alloc), (0.0, 0.0))
             out.append((kp, vp))
-        flat = torch.cat(tails_t + tails_f).cpu().tolist()
-        for (li, side), tt, tf in zip(order, flat[:len(order)], flat[len(order):]):
+        # the tail masses, copied to pinned host memory by kvc_compress as soon
+        # as the solves were done: usually ready by now, while the residual
+        # passes still run
+        tt_all, tf_all = [], []
+        for cell_res in tails_t:
+            host, _, ready = cell_res[0].tails_host
+            ready.synchronize()
+            vals = host.tolist()
+            k = len(cell_res)
+            tt_all += vals[:k]
+            tf_all += vals[k:2 * k]
+        for (li, side), tt, tf in zip(order, tt_all, tf_all):
             md = out[li][side].metadata
             md["tail_token_mass"] = float(tt)
             md["tail_feature_mass"] = float(tf)

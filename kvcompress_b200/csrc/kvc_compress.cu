@@ -100,8 +100,9 @@ extern "C" int kvc_compress(int n_cells, const void* const* x, int64_t m, int64_
                             int n_power, const float* proj, int bits, int symmetric, int scale_mode, int group_size,
                             int stat_dtype, int arith_dtype, int factor_dtype, void* core_out, void* u_token_out,
                             void* u_feature_out, void* core_f, void* u_token_f, void* u_feature_f,
-                            double* tail_token, double* tail_feature, float* scale_out, int32_t* zp_out,
-                            uint8_t* codes_out, void* workspace, size_t ws_bytes, void* stream) {
+                            double* tail_token, double* tail_feature, double* tails_host, void* tails_ready,
+                            float* scale_out, int32_t* zp_out, uint8_t* codes_out, void* workspace,
+                            size_t ws_bytes, void* stream) {
   if (n_cells <= 0 || n_cells > KVC_MAX_CELLS) return fail(KVC_ERR_ARG, "kvc_compress: bad n_cells");
   if (m <= 0 || t <= 0 || d <= 0 || rt <= 0 || rd <= 0 || rd > d || rt > t)
     return fail(KVC_ERR_SHAPE, "kvc_compress: bad shape or ranks");
@@ -165,6 +166,16 @@ extern "C" int kvc_compress(int n_cells, const void* const* x, int64_t m, int64_
                              mat, KVC_F64, sv2, tail_token, scratch, scr, stream)))
     return rc;
   if ((rc = mark(ST_SOLVE_T, 1, stream))) return rc;
+  if (tails_host) {
+    // the tail masses are final here: copy them out and signal, so the
+    // caller can read them while the remaining stages run
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(tails_host, tail_token, (size_t)n * 8, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(tails_host + n, tail_feature, (size_t)n * 8, cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess && tails_ready) e = cudaEventRecord(static_cast<cudaEvent_t>(tails_ready), st);
+    if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("kvc_compress tails copy: ") + cudaGetErrorString(e));
+  }
   if ((rc = mark(ST_APPLY, 0, stream))) return rc;
   if ((rc = kvc_apply_basis(n, xp, t, (int)c, dtype, mat, rt, ut, stream))) return rc;
   if ((rc = mark(ST_APPLY, 1, stream))) return rc;

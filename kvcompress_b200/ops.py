@@ -433,8 +433,15 @@ def compress(xs, *, rt: int, rd: int, mode_f: int, k_f: int, omega_f: torch.Tens
     ut_f = torch.empty(n, t, rt, dtype=factor_dtype, device=dev) if cast else None
     ud_f = torch.empty(n, d, rd, dtype=factor_dtype, device=dev) if cast else None
     tails = (torch.empty(n, dtype=torch.float64, device=dev), torch.empty(n, dtype=torch.float64, device=dev))
+    # the tails also land in pinned host memory as soon as the solves finish;
+    # ``tails_ready`` is recorded then (the caller can read them while the
+    # residual passes run)
+    tails_host = torch.empty(2 * n, dtype=torch.float64, pin_memory=True)
+    tails_ready = torch.cuda.Event()
+    tails_ready.record()  # creates the CUDA event the library records again
     out = {"core": core_, "u_token": ut, "u_feature": ud, "core_stored": core_f, "u_token_stored": ut_f,
            "u_feature_stored": ud_f, "tail_token": tails[0], "tail_feature": tails[1],
+           "tails_host": tails_host, "tails_ready": tails_ready,
            "scale": None, "zero_point": None, "codes": None}
     sc = zp = codes = None
     if bits > 0:
@@ -462,7 +469,8 @@ def compress(xs, *, rt: int, rd: int, mode_f: int, k_f: int, omega_f: torch.Tens
         check(L.kvc_compress(n, _ptrs(xs), m, t, d, _code(dt), rt, rd, mode_f, k_f, ptr(omega_f), mode_t, k_t,
                              ptr(omega_t), n_power, ptr(proj), bits, int(symmetric), scale_mode, int(group_size or 0),
                              _code(stat_dtype), _code(arith_dtype), _code(factor_dtype or dt), ptr(core_), ptr(ut),
-                             ptr(ud), ptr(core_f), ptr(ut_f), ptr(ud_f), ptr(tails[0]), ptr(tails[1]), ptr(sc),
+                             ptr(ud), ptr(core_f), ptr(ut_f), ptr(ud_f), ptr(tails[0]), ptr(tails[1]),
+                             tails_host.data_ptr(), tails_ready.cuda_event, ptr(sc),
                              ptr(zp), ptr(codes), ws.data_ptr(), ws.numel(), _stream()), "kvc_compress")
     finally:
         if evs is not None:
