@@ -512,8 +512,11 @@ __device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, 
       if (threadIdx.x < H) {
         const int lane = threadIdx.x;
         const int i1 = lane, i2 = N - 1 - lane;
-        int pp = i1 == 0 ? 0 : 1 + (i1 - 1 - round + 2 * (N - 1)) % (N - 1);
-        int qq = 1 + (i2 - 1 - round + 2 * (N - 1)) % (N - 1);
+        // positions 1..N-1 rotated by the round: (v mod (N - 1)) for v in
+        // (-(N - 1), N - 1) is one conditional add
+        const int v1 = i1 - 1 - round, v2 = i2 - 1 - round;
+        int pp = i1 == 0 ? 0 : 1 + (v1 < 0 ? v1 + N - 1 : v1);
+        int qq = 1 + (v2 < 0 ? v2 + N - 1 : v2);
         if (pp > qq) {
           const int tmp = pp;
           pp = qq;
@@ -523,13 +526,18 @@ __device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, 
         if (qq < n) {
           const double apq = A[pp * SM_K + qq];
           const double app = A[pp * SM_K + pp], aqq = A[qq * SM_K + qq];
-          if (fabs(apq) > thr && fabs(apq) > 1e-16 * sqrt(fabs(app * aqq))) {
-            // t = sgn(tau) / (|tau| + sqrt(1 + tau^2)), tau = (aqq - app) / (2 apq)
+          if (fabs(apq) > thr && apq * apq > 1e-32 * fabs(app * aqq)) {
+            // with h = aqq - app, g = 2 apq, r = sqrt(h^2 + g^2) the rotation
+            // t = sgn(h) g / (|h| + r) has c = 1 / sqrt(1 + t^2) =
+            // (|h| + r) / sqrt(2 r (r + |h|)) and s = t c = sgn(h) g / sqrt(2 r (r + |h|)):
+            // two reciprocal square roots
             const double h = aqq - app, g = 2.0 * apq;
             const double z = fma(h, h, g * g);
-            const double t = (h >= 0.0 ? g : -g) * rcp_any(fabs(h) + z * rsqrt_any(z));
-            c = rsqrt_any(fma(t, t, 1.0));
-            sn = t * c;
+            const double r = z * rsqrt_any(z);
+            const double ah = fabs(h) + r;
+            const double q = rsqrt_any(2.0 * r * ah);
+            c = ah * q;
+            sn = (h >= 0.0 ? g : -g) * q;
             any_rot = 1;
           }
         }
@@ -539,11 +547,14 @@ __device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, 
         rot[2 * lane + 1] = sn;
       }
       __syncthreads();
-      // A: 2 x 2 blocks (pair b1 rows, pair b2 columns); V: row i, pair b
-      const int nb = H * H;
-      for (int t = threadIdx.x; t < nb + n * H; t += blockDim.x) {
+      // A: 2 x 2 blocks (pair b1 rows, pair b2 columns); V: row i, pair b.
+      // Pairs are indexed in a power-of-two stride hs >= H (shifts, no division).
+      const int hs = H <= 1 ? 1 : 1 << (32 - __clz(H - 1)), sh = __ffs(hs) - 1;
+      const int nb = H * hs;
+      for (int t = threadIdx.x; t < nb + n * hs; t += blockDim.x) {
         if (t < nb) {
-          const int b1 = t / H, b2 = t % H;
+          const int b1 = t >> sh, b2 = t & (hs - 1);
+          if (b2 >= H) continue;
           const int p1 = pq[2 * b1], q1 = pq[2 * b1 + 1], p2 = pq[2 * b2], q2 = pq[2 * b2 + 1];
           const double c1 = rot[2 * b1], s1 = q1 < 0 ? 0.0 : rot[2 * b1 + 1];
           const double c2 = rot[2 * b2], s2 = q2 < 0 ? 0.0 : rot[2 * b2 + 1];
@@ -564,7 +575,8 @@ __device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, 
             if (q2 >= 0) A[q1 * SM_K + q2] = s2 * r2 + c2 * r3;
           }
         } else {
-          const int u = t - nb, i = u / H, b = u % H;
+          const int u = t - nb, i = u >> sh, b = u & (hs - 1);
+          if (b >= H) continue;
           const int p_ = pq[2 * b], q = pq[2 * b + 1];
           if (q < 0) continue;
           const double cc = rot[2 * b], ss = rot[2 * b + 1];

@@ -316,6 +316,15 @@ int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float*
   if (rows >= (1LL << 31)) return fail(KVC_ERR_SHAPE, "tensor-core gram: more than 2^31 rows per cell");
   GramArgs g;
   memset(&g, 0, sizeof(g));
+  uint8_t* opad = static_cast<uint8_t*>(workspace) + partial_bytes(n_cells, p);
+  g.k = k;
+  {
+    const int blocks = (int)std::min<int64_t>(ceil_div(rows * 32, 256), 16LL * num_sms());
+    omega_pad_kernel<<<blocks, 256, 0, st>>>(omega, rows, k, opad);
+    int rc0 = check_launch("omega_pad_kernel");
+    if (rc0) return rc0;
+  }
+  // the tensor maps are encoded while the padding kernel runs
   TmaMaps xmaps;
   CUtensorMap omap;
   int rc1;
@@ -327,7 +336,6 @@ int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float*
                           CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc1;
   }
-  uint8_t* opad = static_cast<uint8_t*>(workspace) + partial_bytes(n_cells, p);
   {
     const uint64_t dims[2] = {(uint64_t)NY, (uint64_t)rows};
     const uint64_t strides[1] = {(uint64_t)NY * 2};
@@ -336,13 +344,7 @@ int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float*
                           CU_TENSOR_MAP_SWIZZLE_128B)))
       return rc1;
   }
-  g.k = k;
-  {
-    const int blocks = (int)std::min<int64_t>(ceil_div(rows * 32, 256), 16LL * num_sms());
-    omega_pad_kernel<<<blocks, 256, 0, st>>>(omega, rows, k, opad);
-    int rc0 = check_launch("omega_pad_kernel");
-    if (rc0) return rc0;
-  }
+
   g.rows = rows;
   g.tiles_per_cell = p.tiles_per_cell;
   g.seg_tiles = p.seg_tiles;
