@@ -3,7 +3,7 @@
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import Any, Iterator
+from typing import Any, Iterator, Sequence
 
 import torch
 
@@ -30,6 +30,14 @@ class CacheManager:
         self.cache.store(layer, key, value, **kwargs)
         if layer not in self.live_layers:
             self.live_layers.append(layer)
+
+    def store_layers(self, layers: Sequence[int], keys: Sequence[torch.Tensor], values: Sequence[torch.Tensor],
+                     **kwargs: Any) -> None:
+        """``store`` of several layers as one batched compress."""
+        self.cache.store_layers(layers, keys, values, **kwargs)
+        for layer in layers:
+            if layer not in self.live_layers:
+                self.live_layers.append(layer)
 
     def retrieve(self, layer: int) -> tuple[torch.Tensor, torch.Tensor]:
         return self.cache.retrieve(layer)
