@@ -59,6 +59,9 @@ enum { KVC_SCALE_CHANNEL = 0, KVC_SCALE_GROUP = 1, KVC_SCALE_TENSOR = 2 };
 
 const char* kvc_last_error(void);
 int kvc_abi_version(void);
+/* Kernels the calling host thread has launched through the library so far
+ * (successful launches; a running count, no counterpart in the reference). */
+unsigned long long kvc_launch_count(void);
 
 /*
  * Column Gram and sketch of a row-major (rows x p) matrix A per cell:

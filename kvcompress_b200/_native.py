@@ -43,6 +43,7 @@ class KVC:
 
 _SIGNATURES = {
     "kvc_last_error": (ctypes.c_char_p, []),
+    "kvc_launch_count": (ctypes.c_ulonglong, []),
     "kvc_abi_version": (I, []),
     "kvc_gram_workspace_bytes": (SZ, [I, I64, I, I]),
     "kvc_gram": (I, [I, PP, I64, I, I, P, I, P, P, SZ, P]),

@@ -7,6 +7,9 @@
 namespace kvc {
 
 static thread_local std::string g_last_error;
+// kernels this host thread launched through the library (every launch is
+// followed by check_launch)
+static thread_local unsigned long long g_launches = 0;
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 
@@ -18,6 +21,7 @@ int fail(int code, const std::string& msg) {
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string(what) + ": " + cudaGetErrorString(e));
+  ++g_launches;
   return KVC_OK;
 }
 
@@ -38,3 +42,5 @@ int num_sms() {
 extern "C" const char* kvc_last_error(void) { return kvc::g_last_error.c_str(); }
 
 extern "C" int kvc_abi_version(void) { return 1; }
+
+extern "C" unsigned long long kvc_launch_count(void) { return kvc::g_launches; }

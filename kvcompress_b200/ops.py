@@ -492,8 +492,8 @@ def compress(xs, *, rt: int, rd: int, mode_f: int, k_f: int, omega_f: torch.Tens
 
 # kvc_compress's stages in order, with the kernels each launches on the
 # tensor-core path (the stage timing of the bench)
-_COMPRESS_STAGES = [("gram", 5), ("sketch_solve", 1), ("project_feature", 1), ("gram", 4), ("sketch_solve", 1),
-                    ("apply_basis", 1), ("core", 1), ("residual_stats", 5), ("residual_quant", 3), ("cast", 3)]
+_COMPRESS_STAGES = [("gram", 4), ("sketch_solve", 1), ("project_feature", 1), ("gram", 3), ("sketch_solve", 1),
+                    ("apply_basis", 1), ("core", 2), ("residual_stats", 5), ("residual_quant", 3), ("cast", 3)]
 
 
 class DecodePlan:
@@ -584,6 +584,11 @@ def decompress_noalloc(shape, out_dtype: torch.dtype, *, codes=None, scales=None
 def set_kernel_policy(policy: int) -> None:
     """0: tensor-core kernels where eligible (default); 1: SIMT kernels only."""
     check(lib().kvc_set_kernel_policy(int(policy)), "kvc_set_kernel_policy")
+
+
+def launch_count() -> int:
+    """Kernels this host thread has launched through the library so far."""
+    return int(lib().kvc_launch_count())
 
 
 def device_error() -> int:

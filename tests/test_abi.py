@@ -38,6 +38,7 @@ def test_binding_covers_header():
 def test_host_only_entry_points():
     L = lib()
     assert L.kvc_abi_version() == 1
+    assert isinstance(L.kvc_launch_count(), int) and L.kvc_launch_count() >= 0
     # workspace queries are pure host arithmetic
     assert L.kvc_sketch_solve_workspace_bytes(2, 1, 128, 11) > 0
     assert L.kvc_sketch_solve_workspace_bytes(0, 1, 128, 11) == 0

@@ -171,6 +171,24 @@ def test_many_layers_equal_single_layer_calls():
         assert torch.equal(kd, k1) and torch.equal(vd, v1)
 
 
+def test_launch_counts_of_a_batched_step():
+    """The library's own launch counter: a batched compress of same-shape
+    bf16 cells is 24 kernels on the tensor-core path (one kvc_compress
+    call), the batched decode 3, however many layers share the call."""
+    from kvcompress_b200 import ops
+
+    w = WORKLOADS["llama3-8b-kv-b1-t8192-bf16"]
+    pairs = [tuple(x.reshape(8, 512, 128).cuda() for x in make_kv_layer(w, i, tokens=512)) for i in range(4)]
+    comp = build_compressor("flashjolt", compression_ratio=4.0)
+    comp.compress_many(pairs)  # warm caches (sketch, projection)
+    c0 = ops.launch_count()
+    many = comp.compress_many(pairs)
+    c1 = ops.launch_count()
+    comp.decompress_many(many)
+    c2 = ops.launch_count()
+    assert (c1 - c0, c2 - c1) == (24, 3)
+
+
 def test_token_range_decompress_matches_full():
     w = WORKLOADS["qwen2-7b-kv-b4-t131072-bf16"]
     k, v = make_kv_layer(w, 0, tokens=1000, batch=1)
