@@ -116,32 +116,33 @@ class JoLTCompressor(KVCompressor):
         """Compress several layers; cells of equal shape and allocation share launches."""
         t_start = time.perf_counter()
         plans = []
-        alloc_of: dict[tuple[int, int, int], AllocationResult] = {}  # layers of one shape share the allocation
-        for key, value in pairs:
-            if key.shape != value.shape:
-                raise ValueError(f"K/V shape mismatch: {key.shape} vs {value.shape}")
-            if key.dim() != 3:
-                raise ValueError(f"JoLT expects 3-D (m, T, dh); got {tuple(key.shape)}")
-            for x in (key, value):
-                if not x.is_cuda:
-                    raise RuntimeError("kvcompress_b200 compresses CUDA tensors only "
-                                       f"(got a {x.device} tensor)")
-                if x.dtype not in _DTYPES:
-                    raise TypeError(f"unsupported K/V dtype {x.dtype}")
-            m, t, d = key.shape
-            res = alloc_of.get((m, t, d))
-            if res is None:
+        # layers of one shape share the allocation: (result, (K allocation, V allocation))
+        alloc_of: dict[torch.Size, tuple[AllocationResult, tuple]] = {}
+        # group cells by (shape, dtype, device, allocation) so each group is one batch; every tensor
+        # attribute is read once (a 64-cell call spends its host time on such reads)
+        groups: dict[tuple, list[tuple[int, int]]] = {}
+        for li, (key, value) in enumerate(pairs):
+            ks, kdt, kdev = key.shape, key.dtype, key.device
+            vs, vdt, vdev = value.shape, value.dtype, value.device
+            if ks != vs:
+                raise ValueError(f"K/V shape mismatch: {ks} vs {vs}")
+            if len(ks) != 3:
+                raise ValueError(f"JoLT expects 3-D (m, T, dh); got {tuple(ks)}")
+            for dev, dt in ((kdev, kdt), (vdev, vdt)):
+                if dev.type != "cuda":
+                    raise RuntimeError(f"kvcompress_b200 compresses CUDA tensors only (got a {dev} tensor)")
+                if dt not in _DTYPES:
+                    raise TypeError(f"unsupported K/V dtype {dt}")
+            hit = alloc_of.get(ks)
+            if hit is None:
+                m, t, d = ks
                 res = self.allocator.optimize([
                     Cell(shape=(m, t, d), kind="key", layer_group=0, candidate_bits=self.bits),
                     Cell(shape=(m, t, d), kind="value", layer_group=0, candidate_bits=self.bits)])
-                alloc_of[(m, t, d)] = res
-            plans.append(res)
-        # group cells by (shape, dtype, allocation) so each group is one batch
-        groups: dict[tuple, list[tuple[int, int]]] = {}
-        for li, ((key, value), res) in enumerate(zip(pairs, plans)):
-            for side, (x, a) in enumerate(zip((key, value), res.allocations)):
-                gk = (tuple(x.shape), x.dtype, x.device, a.tuple)
-                groups.setdefault(gk, []).append((li, side))
+                hit = alloc_of[ks] = (res, tuple(a.tuple for a in res.allocations))
+            plans.append(hit[0])
+            groups.setdefault((ks, kdt, kdev, hit[1][0]), []).append((li, 0))
+            groups.setdefault((ks, vdt, vdev, hit[1][1]), []).append((li, 1))
         results: dict[tuple[int, int], CellResult] = {}
         order, tails_t = [], []
         for (shape, _, _, (rt, rd, b)), members in groups.items():

@@ -8,8 +8,10 @@
 // (two 64-column boxes) is at the same time the MN-major A operand (x^T: M = feature,
 // K = row) and the MN-major B operand (x: N = feature); products of bf16
 // values are exact and accumulate in fp32 in TMEM.  Omega (fp32) is split
-// once by a small kernel into bf16 hi / lo (columns 0..31 / 32..63 of a
-// 64-column MN-major B tile), so Y carries ~16 mantissa bits of Omega.
+// once by a small kernel into bf16 hi / lo (columns 0..NY/2-1 / NY/2..NY-1 of
+// an NY-column MN-major B tile), so Y carries ~16 mantissa bits of Omega.
+// NY = 32 (SWIZZLE_64B rows) for k <= 16, which leaves room for five stages;
+// NY = 64 (SWIZZLE_128B) with four stages up to k = 32.
 //
 // Work: every cell is cut into segments of a fixed number of tiles that
 // depends on the row count only; CTAs take contiguous runs of segments, keep
@@ -18,8 +20,8 @@
 // kernel sums the segments of each cell in order in fp64.  The result of a
 // cell is therefore bit-identical however many cells share the launch.
 //
-// Warp 0 loads tiles by TMA (4 stages, rows past the end of a cell read as
-// zeros), warp 1 issues tcgen05.mma, warps 2-5 drain accumulators.  Every
+// Warp 0 loads tiles by TMA (4 or 5 stages, rows past the end of a cell read
+// as zeros), warp 1 issues tcgen05.mma, warps 2-5 drain accumulators.  Every
 // mbarrier wait is bounded.
 #include <algorithm>
 
@@ -35,17 +37,18 @@ using namespace tc;
 
 constexpr int D = 128;        // head_dim handled here
 constexpr int TILE = 128;     // rows per tile (the MMA K extent of 8 K-steps)
-constexpr int NY = 64;        // Omega columns (hi 0..31, lo 32..63)
-constexpr int NACC = D + NY;  // accumulator columns: [G | Y]
-constexpr int NS = 4;         // pipeline stages
 constexpr int NTH = 192;      // warp 0 TMA, warp 1 MMA, warps 2-5 epilogue
 constexpr int TMA_WARP = 0;
 constexpr int MMA_WARP = 1;
 constexpr int EPI_WARP0 = 2;
 
+// NY Omega columns (hi, then lo), NS pipeline stages
+template <int NY, int NS>
 struct GLayout {
+  static constexpr int NACC = D + NY;                 // accumulator columns: [G | Y]
   static constexpr uint32_t X_BYTES = TILE * D * 2;   // 32 KB
-  static constexpr uint32_t O_BYTES = TILE * NY * 2;  // 16 KB
+  static constexpr uint32_t O_BYTES = TILE * NY * 2;  // 8 or 16 KB
+  static constexpr uint32_t O_ROW = NY * 2;           // bytes per Omega row: the swizzle span
   static constexpr uint32_t STAGE = X_BYTES + O_BYTES;
   static constexpr uint32_t OFF_RING = NS * STAGE;  // segment ids drawn by the producer
   static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
@@ -71,24 +74,31 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   return p + ((1024u - (a & 1023u)) & 1023u);
 }
 
-// MN-major SWIZZLE_128B descriptor: LBO = stride between 64-element MN
-// groups, SBO = stride between 8-row K groups.
-__device__ __forceinline__ uint64_t desc_mn_sw128(uint32_t saddr, uint32_t lbo) {
+// MN-major swizzled descriptor: rows of SPAN bytes (128: SWIZZLE_128B, 64:
+// SWIZZLE_64B), LBO = stride between MN groups of one row's elements, SBO =
+// stride between 8-row K groups (8 rows x SPAN bytes).
+template <int SPAN>
+__device__ __forceinline__ uint64_t desc_mn_sw(uint32_t saddr, uint32_t lbo) {
+  static_assert(SPAN == 128 || SPAN == 64, "128- or 64-byte swizzle");
   uint64_t d = 0;
   d |= (uint64_t)((saddr & 0x3FFFFu) >> 4);
   d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)((8 * SPAN) >> 4) << 32;
   d |= (uint64_t)1 << 46;
-  d |= (uint64_t)2 << 61;
+  d |= (uint64_t)(SPAN == 128 ? 2 : 4) << 61;
   return d;
 }
 
 // Work unit: one segment (seg_tiles consecutive tiles of a cell), summed
 // into its own fp32 partial, so the sums do not depend on which CTA made
 // them; each CTA takes a contiguous range of segments (kvc_sched.cuh).
+template <int NY, int NS>
 __global__ void __launch_bounds__(NTH, 1)
     tc_gram_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ CUtensorMap omap,
                    const __grid_constant__ GramArgs A) {
+  using GLayout = kvc::GLayout<NY, NS>;
+  constexpr int NACC = GLayout::NACC;
+  static_assert(GLayout::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
   const uint32_t sbase = smem_u32(smem);
@@ -191,8 +201,8 @@ __global__ void __launch_bounds__(NTH, 1)
           const uint32_t os = xs + GLayout::X_BYTES;
 #pragma unroll
           for (int ks = 0; ks < TILE / 16; ++ks) {
-            const uint64_t da = desc_mn_sw128(xs + ks * 2048, TILE * 128);
-            const uint64_t dy = desc_mn_sw128(os + ks * 2048, TILE * 128);
+            const uint64_t da = desc_mn_sw<128>(xs + ks * 2048, TILE * 128);
+            const uint64_t dy = desc_mn_sw<GLayout::O_ROW>(os + ks * 16 * GLayout::O_ROW, TILE * GLayout::O_ROW);
             const uint32_t accumulate = (t == 0 && ks == 0) ? 0u : 1u;
             umma_f16(acc, da, da, id_g, accumulate);
             umma_f16(acc + D, da, dy, id_y, accumulate);
@@ -236,24 +246,28 @@ __global__ void __launch_bounds__(NTH, 1)
   }
 }
 
-// Omega (rows x k fp32) -> rows x 64 bf16: hi = bf16(w), lo = bf16(w - hi).
-__global__ void omega_pad_kernel(const float* __restrict__ omega, int64_t rows, int k, uint8_t* out) {
-  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < rows * 32;
+// Omega (rows x k fp32) -> rows x ny bf16: hi = bf16(w) in columns
+// [0, ny/2), lo = bf16(w - hi) in [ny/2, ny).
+__global__ void omega_pad_kernel(const float* __restrict__ omega, int64_t rows, int k, int ny, uint8_t* out) {
+  const int half = ny / 2;
+  for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < rows * half;
        idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t r = idx / 32;
-    const int c = (int)(idx % 32);
+    const int64_t r = idx / half;
+    const int c = (int)(idx % half);
     const float w = c < k ? omega[r * k + c] : 0.f;
     const __nv_bfloat16 h = __float2bfloat16_rn(w);
     const __nv_bfloat16 l = __float2bfloat16_rn(w - __bfloat162float(h));
-    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out + r * (NY * 2));
+    __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(out + r * (ny * 2));
     o[c] = h;
-    o[32 + c] = l;
+    o[half + c] = l;
   }
 }
 
 // Sum the segments of each cell in order (fp64) into [G | Y | trace].
+template <int NY>
 __global__ void tc_gram_reduce_kernel(const float* __restrict__ partial, int n_cells, int64_t segs_per_cell,
                                       int k, double* __restrict__ out, int64_t stride) {
+  constexpr int NACC = D + NY;
   const int64_t total = (int64_t)n_cells * D * (D + k);
   for (int64_t idx = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; idx < total;
        idx += (int64_t)gridDim.x * blockDim.x) {
@@ -269,7 +283,7 @@ __global__ void tc_gram_reduce_kernel(const float* __restrict__ partial, int n_c
     } else {
       const int jj = j - D;
       for (int sl = 0; sl < nseg; ++sl)
-        s += (double)base[(int64_t)sl * D * NACC + D + jj] + (double)base[(int64_t)sl * D * NACC + D + 32 + jj];
+        s += (double)base[(int64_t)sl * D * NACC + D + jj] + (double)base[(int64_t)sl * D * NACC + D + NY / 2 + jj];
       out[cell * stride + (int64_t)D * D + (int64_t)i * k + jj] = s;
     }
   }
@@ -296,31 +310,32 @@ GPlan gplan(int n_cells, int64_t rows) {
 
 bool tc_gram_eligible(int dtype, int p, int k) { return dtype == KVC_BF16 && p == D && k <= 32; }
 
+// workspace sized for the wider Omega tile (NY = 64), whichever the launch uses
+constexpr int NY_MAX = 64;
+
 static size_t partial_bytes(int n_cells, const GPlan& p) {
   (void)n_cells;
-  return ((size_t)p.total_segs * D * NACC * sizeof(float) + 255) & ~(size_t)255;
+  return ((size_t)p.total_segs * D * (D + NY_MAX) * sizeof(float) + 255) & ~(size_t)255;
 }
 
-static size_t opad_bytes(int64_t rows) { return ((size_t)rows * NY * 2 + 255) & ~(size_t)255; }
+static size_t opad_bytes(int64_t rows) { return ((size_t)rows * NY_MAX * 2 + 255) & ~(size_t)255; }
 
 size_t tc_gram_workspace(int n_cells, int64_t rows) {
   GPlan p = gplan(n_cells, rows);
   return partial_bytes(n_cells, p) + opad_bytes(rows);
 }
 
-int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float* omega, int k, double* out,
-                   void* workspace, size_t ws_bytes, cudaStream_t st) {
-  GPlan p = gplan(n_cells, rows);
-  if (!workspace || ws_bytes < tc_gram_workspace(n_cells, rows))
-    return fail(KVC_ERR_WORKSPACE, "tensor-core gram: workspace too small");
-  if (rows >= (1LL << 31)) return fail(KVC_ERR_SHAPE, "tensor-core gram: more than 2^31 rows per cell");
+template <int NY, int NS>
+static int tc_gram_run(int n_cells, const void* const* a, int64_t rows, const float* omega, int k, double* out,
+                       const GPlan& p, void* workspace, cudaStream_t st) {
+  using L = GLayout<NY, NS>;
   GramArgs g;
   memset(&g, 0, sizeof(g));
   uint8_t* opad = static_cast<uint8_t*>(workspace) + partial_bytes(n_cells, p);
   g.k = k;
   {
-    const int blocks = (int)std::min<int64_t>(ceil_div(rows * 32, 256), 16LL * num_sms());
-    omega_pad_kernel<<<blocks, 256, 0, st>>>(omega, rows, k, opad);
+    const int blocks = (int)std::min<int64_t>(ceil_div(rows * (NY / 2), 256), 16LL * num_sms());
+    omega_pad_kernel<<<blocks, 256, 0, st>>>(omega, rows, k, NY, opad);
     int rc0 = check_launch("omega_pad_kernel");
     if (rc0) return rc0;
   }
@@ -341,27 +356,37 @@ int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float*
     const uint64_t strides[1] = {(uint64_t)NY * 2};
     const uint32_t box[2] = {(uint32_t)NY, (uint32_t)TILE};
     if ((rc1 = encode_tma(&omap, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, opad, dims, strides, box,
-                          CU_TENSOR_MAP_SWIZZLE_128B)))
+                          NY == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
       return rc1;
   }
-
   g.rows = rows;
   g.tiles_per_cell = p.tiles_per_cell;
   g.seg_tiles = p.seg_tiles;
   g.segs_per_cell = p.segs_per_cell;
   g.total_segs = p.total_segs;
   g.partial = static_cast<float*>(workspace);
-  cudaError_t e = cudaFuncSetAttribute(tc_gram_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)GLayout::BYTES);
+  cudaError_t e = cudaFuncSetAttribute(tc_gram_kernel<NY, NS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)L::BYTES);
   if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-  tc_gram_kernel<<<p.ctas, NTH, GLayout::BYTES, st>>>(xmaps, omap, g);
+  tc_gram_kernel<NY, NS><<<p.ctas, NTH, L::BYTES, st>>>(xmaps, omap, g);
   int rc = check_launch("tc_gram_kernel");
   if (rc) return rc;
   const int64_t stride = (int64_t)D * D + (int64_t)D * k + 1;
   const int64_t total = (int64_t)n_cells * D * (D + k);
   const int blocks = (int)std::min<int64_t>(ceil_div(total, 256), 8 * num_sms());
-  tc_gram_reduce_kernel<<<blocks, 256, 0, st>>>(g.partial, n_cells, p.segs_per_cell, k, out, stride);
+  tc_gram_reduce_kernel<NY><<<blocks, 256, 0, st>>>(g.partial, n_cells, p.segs_per_cell, k, out, stride);
   return check_launch("tc_gram_reduce_kernel");
+}
+
+int tc_gram_launch(int n_cells, const void* const* a, int64_t rows, const float* omega, int k, double* out,
+                   void* workspace, size_t ws_bytes, cudaStream_t st) {
+  GPlan p = gplan(n_cells, rows);
+  if (!workspace || ws_bytes < tc_gram_workspace(n_cells, rows))
+    return fail(KVC_ERR_WORKSPACE, "tensor-core gram: workspace too small");
+  if (rows >= (1LL << 31)) return fail(KVC_ERR_SHAPE, "tensor-core gram: more than 2^31 rows per cell");
+  // Omega rows of 32 columns (hi / lo of k <= 16) leave room for a fifth stage
+  if (k <= 16) return tc_gram_run<32, 5>(n_cells, a, rows, omega, k, out, p, workspace, st);
+  return tc_gram_run<64, 4>(n_cells, a, rows, omega, k, out, p, workspace, st);
 }
 
 int tc_gram_read_device_error(int* out) {
