@@ -413,24 +413,38 @@ __device__ void sm_colgram(double* S, const double* A, const double* B, int p, i
 // Cholesky with rank dropping of S (k x k, upper triangle -> R): a column
 // whose pivot falls below 1e-10 of its original diagonal is zero.  Then
 // X = R^{-1} (upper triangular, zero rows and columns where R was dropped).
+// diag0 points to 2 SM_K doubles of scratch.
+//
+// One barrier per elimination step: step j updates the trailing rows with
+// the unscaled row j (S[i][l] -= S[j][i] S[j][l] / d) and scales row j - 1,
+// which nobody reads in that phase; 1 / R[j][j] is kept for the
+// back-substitution.
 __device__ void sm_chol_inv(double* S, double* X, double* diag0, int k) {
+  double* rinv = diag0 + SM_K;  // 1 / R[j][j], 0 where the column was dropped
   for (int i = threadIdx.x; i < k; i += blockDim.x) diag0[i] = S[i * SM_K + i];
   __syncthreads();
   for (int j = 0; j < k; ++j) {
     const double d = S[j * SM_K + j], oj = diag0[j];
     const bool keep = oj > 0.0 && d > 1e-10 * oj;
-    const double rs = keep ? rsqrt_any(d) : 0.0;  // 1 / R[j][j]
-    __syncthreads();  // everyone has read S[j][j]
-    for (int l = j + threadIdx.x; l < k; l += blockDim.x) S[j * SM_K + l] = l == j ? (keep ? d * rs : 0.0) : S[j * SM_K + l] * rs;
-    __syncthreads();
-    // trailing update S[i][l] -= R[j][i] R[j][l], j < i <= l < k
-    const int m = k - 1 - j;
-    for (int t = threadIdx.x; t < m * m; t += blockDim.x) {
-      const int i = j + 1 + t / m, l = j + 1 + t % m;
-      if (l >= i) S[i * SM_K + l] = fma(-S[j * SM_K + i], S[j * SM_K + l], S[i * SM_K + l]);
+    const double rs = keep ? rsqrt_any(d) : 0.0;
+    const double inv_d = rs * rs;
+    if (threadIdx.x == 0) rinv[j] = rs;
+    // scaling of row j - 1 (R[j-1][l] = S[j-1][l] / R[j-1][j-1], the diagonal
+    // included), then the trailing update of rows j + 1 .. k - 1
+    const int ns = j > 0 ? k - j + 1 : 0, m = k - 1 - j;
+    for (int t = threadIdx.x; t < ns + m * m; t += blockDim.x) {
+      if (t < ns) {
+        const int l = j - 1 + t;
+        S[(j - 1) * SM_K + l] *= rinv[j - 1];
+      } else {
+        const int u = t - ns, i = j + 1 + u / m, l = j + 1 + u % m;
+        if (l >= i) S[i * SM_K + l] = fma(-S[j * SM_K + i] * inv_d, S[j * SM_K + l], S[i * SM_K + l]);
+      }
     }
     __syncthreads();
   }
+  if (threadIdx.x == 0) S[(k - 1) * SM_K + k - 1] *= rinv[k - 1];
+  __syncthreads();
   // X = R^{-1}: column c by back-substitution (columns in parallel)
   for (int c = threadIdx.x; c < k; c += blockDim.x) {
     for (int i = k - 1; i >= 0; --i) {
@@ -438,8 +452,7 @@ __device__ void sm_chol_inv(double* S, double* X, double* diag0, int k) {
       if (i <= c) {
         v = i == c ? 1.0 : 0.0;
         for (int jj = i + 1; jj <= c; ++jj) v = fma(-S[i * SM_K + jj], X[jj * SM_K + c], v);
-        const double rii = S[i * SM_K + i];
-        v = rii > 0.0 ? v * rcp_any(rii) : 0.0;
+        v *= rinv[i];
       }
       X[i * SM_K + c] = v;
     }
@@ -528,16 +541,30 @@ __device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, 
           const double app = A[pp * SM_K + pp], aqq = A[qq * SM_K + qq];
           if (fabs(apq) > thr && apq * apq > 1e-32 * fabs(app * aqq)) {
             // with h = aqq - app, g = 2 apq, r = sqrt(h^2 + g^2) the rotation
-            // t = sgn(h) g / (|h| + r) has c = 1 / sqrt(1 + t^2) =
-            // (|h| + r) / sqrt(2 r (r + |h|)) and s = t c = sgn(h) g / sqrt(2 r (r + |h|)):
-            // two reciprocal square roots
+            // t = sgn(h) g / (|h| + r) has c = 1 / sqrt(1 + t^2), s = t c
             const double h = aqq - app, g = 2.0 * apq;
-            const double z = fma(h, h, g * g);
-            const double r = z * rsqrt_any(z);
-            const double ah = fabs(h) + r;
-            const double q = rsqrt_any(2.0 * r * ah);
-            c = ah * q;
-            sn = (h >= 0.0 ? g : -g) * q;
+            if (f32_range(g) && (h == 0.0 || f32_range(h))) {
+              // the angle in fp32, (c, s) normalised in fp64: a rotation off
+              // by ~1e-7 of its angle leaves ~1e-7 of apq, which later
+              // rotations remove, while c^2 + s^2 = 1 to fp64 keeps V
+              // orthogonal (fp64 operations are the long-latency ones here)
+              const float hf = (float)h, gf = (float)g;
+              const float tf = __fdividef(hf >= 0.f ? gf : -gf, fabsf(hf) + hypotf(hf, gf));
+              const float cf = rsqrtf(fmaf(tf, tf, 1.f));
+              const double cd = (double)cf, sd = (double)(tf * cf);
+              const double e = fma(cd, cd, fma(sd, sd, -1.0));    // c^2 + s^2 - 1
+              const double f = fma(fma(0.375, e, -0.5), e, 1.0);  // (1 + e)^(-1/2) up to O(e^3)
+              c = cd * f;
+              sn = sd * f;
+            } else {
+              // c = (|h| + r) / sqrt(2 r (r + |h|)), s = sgn(h) g / sqrt(2 r (r + |h|))
+              const double z = fma(h, h, g * g);
+              const double r = z * rsqrt_any(z);
+              const double ah = fabs(h) + r;
+              const double q = rsqrt_any(2.0 * r * ah);
+              c = ah * q;
+              sn = (h >= 0.0 ? g : -g) * q;
+            }
             any_rot = 1;
           }
         }
