@@ -578,14 +578,14 @@ __device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, 
       // Pairs are indexed in a power-of-two stride hs >= H (shifts, no division).
       const int hs = H <= 1 ? 1 : 1 << (32 - __clz(H - 1)), sh = __ffs(hs) - 1;
       const int nb = H * hs;
-      for (int t = threadIdx.x; t < nb + n * hs; t += blockDim.x) {
+      auto task = [&](int t) {
         if (t < nb) {
           const int b1 = t >> sh, b2 = t & (hs - 1);
-          if (b2 >= H) continue;
+          if (b2 >= H) return;
           const int p1 = pq[2 * b1], q1 = pq[2 * b1 + 1], p2 = pq[2 * b2], q2 = pq[2 * b2 + 1];
           const double c1 = rot[2 * b1], s1 = q1 < 0 ? 0.0 : rot[2 * b1 + 1];
           const double c2 = rot[2 * b2], s2 = q2 < 0 ? 0.0 : rot[2 * b2 + 1];
-          if (s1 == 0.0 && s2 == 0.0) continue;
+          if (s1 == 0.0 && s2 == 0.0) return;
           // rows {p1, q1} x columns {p2, q2}; a missing q is a dummy index
           const double a = A[p1 * SM_K + p2];
           const double b = q2 >= 0 ? A[p1 * SM_K + q2] : 0.0;
@@ -603,15 +603,27 @@ __device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, 
           }
         } else {
           const int u = t - nb, i = u >> sh, b = u & (hs - 1);
-          if (b >= H) continue;
+          if (b >= H) return;
           const int p_ = pq[2 * b], q = pq[2 * b + 1];
-          if (q < 0) continue;
+          if (q < 0) return;
           const double cc = rot[2 * b], ss = rot[2 * b + 1];
-          if (ss == 0.0) continue;
+          if (ss == 0.0) return;
           const double x = V[i * SM_K + p_], y = V[i * SM_K + q];
           V[i * SM_K + p_] = cc * x - ss * y;
           V[i * SM_K + q] = ss * x + cc * y;
         }
+      };
+      // the A blocks and the rows of V go to different warps where the block
+      // has room (no warp runs both kinds of task one after the other)
+      const int vb = (nb + 31) & ~31;
+      if (vb + 32 <= (int)blockDim.x) {
+        if ((int)threadIdx.x < vb) {
+          for (int t = threadIdx.x; t < nb; t += vb) task(t);
+        } else {
+          for (int u = threadIdx.x - vb; u < n * hs; u += blockDim.x - vb) task(nb + u);
+        }
+      } else {
+        for (int t = threadIdx.x; t < nb + n * hs; t += blockDim.x) task(t);
       }
       __syncthreads();
     }
