@@ -53,6 +53,9 @@ constexpr int MMA_WARP = 4;
 constexpr int TMA_WARP = 5;
 constexpr int EPI_WARP0 = 6;
 constexpr int NEPI = 256;  // epilogue threads
+// the stats pass: transform warps 0-3 and 10-13 (two per TMEM lane group,
+// one feature half each), epilogue warps 6-9
+constexpr int STATS_XF_WARP1 = 10;
 constexpr int RD_MAX = 16;
 constexpr uint32_t TM_ACC = 256;  // TMEM column of accumulator 0 (1 at +128)
 
@@ -127,10 +130,11 @@ template <int D, int RDM, int NS>
 struct StatsLayout {
   static constexpr uint32_t B_BYTES = TILE_M * D * 2;             // R tile (MMA B operand)
   static constexpr uint32_t T_BYTES = TILE_M * RDM * 4;           // Tucker row term of a tile
-  static constexpr uint32_t U_BYTES = RDM == 1 ? D * 2 : D * 16;  // u_feature: bf16 [j] or fp32 [j][4]
+  static constexpr uint32_t U_BYTES = RDM == 1 ? D : D * 8;  // per transform warp, its D/2 features of
+                                                              // u_feature: bf16 [j] or fp32 [j][4]
   static constexpr uint32_t OFF_T = NS * B_BYTES;
   static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
-  static constexpr uint32_t OFF_RING = OFF_U + 4 * U_BYTES;  // tile ids drawn by the producer
+  static constexpr uint32_t OFF_RING = OFF_U + 8 * U_BYTES;  // tile ids drawn by the producer
   static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
   static constexpr uint32_t NBAR = 3 * NS + 4;                    // loaded, full, empty, acc full x2, acc empty x2
   static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
@@ -167,12 +171,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (threadIdx.x == 0) {
     for (int i = 0; i < NS; ++i) {
       mbar_init(&loaded[i], 1);  // TMA issue + transaction bytes
-      mbar_init(&full[i], 128);  // transform threads
+      mbar_init(&full[i], 256);  // transform threads
       mbar_init(&empty[i], 1);   // tcgen05.commit
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);     // tcgen05.commit
-      mbar_init(&acce[i], NEPI);  // epilogue threads
+      mbar_init(&acce[i], 128);   // epilogue threads
     }
     mbar_fence_init();
   }
@@ -190,11 +194,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   __syncthreads();
   tc_fence_after();
 
-  if (warp < 4) {
-    // ---------------- transform: R = x - recon, one row per thread ----------------
-    const int ptid = threadIdx.x;
-    float* u32 = reinterpret_cast<float*>(smem + L::OFF_U + warp * L::U_BYTES);       // [j][4]
-    uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + warp * L::U_BYTES);  // [j]
+  if (warp < 4 || warp >= STATS_XF_WARP1) {
+    // ---------------- transform: R = x - recon, in place, one row per thread ----------------
+    // two warps per row block: warp w takes rows (w % 4) * 32.. and feature half `part`
+    constexpr int HF = D / 2, HC = HF / 8;  // features and 16-byte chunks per part
+    const int lgw = warp & 3, part = warp < 4 ? 0 : 1;
+    const int ptid = lgw * 32 + lane;
+    float* u32 = reinterpret_cast<float*>(smem + L::OFF_U + (part * 4 + lgw) * L::U_BYTES);       // [j][4]
+    uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + (part * 4 + lgw) * L::U_BYTES);  // [j]
     int cur_cell = -1;
     for (int it = 0;; ++it) {
       const int st = it % NS;
@@ -210,11 +217,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __syncwarp();
         const __nv_bfloat16* ud = static_cast<const __nv_bfloat16*>(A.ud.p[cell]);
         if (RDM == 1) {
-          for (int j = lane; j < D; j += 32) ub[j] = reinterpret_cast<const uint16_t*>(ud)[j];
+          for (int j = lane; j < HF; j += 32) ub[j] = reinterpret_cast<const uint16_t*>(ud)[part * HF + j];
         } else {
-          for (int i = lane; i < D * 4; i += 32) {
+          for (int i = lane; i < HF * 4; i += 32) {
             const int j = i >> 2, r = i & 3;
-            u32[i] = r < A.rd ? __bfloat162float(ud[j * A.rd + r]) : 0.f;
+            u32[i] = r < A.rd ? __bfloat162float(ud[(part * HF + j) * A.rd + r]) : 0.f;
           }
         }
         __syncwarp();
@@ -230,8 +237,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t t2 = th | (th << 16);
           const uint4* u4 = reinterpret_cast<const uint4*>(ub);
 #pragma unroll
-          for (int c = 0; c < D / 8; ++c) {
-            uint4* slot = reinterpret_cast<uint4*>(Bs + sw128_off(ptid, c * 8, TILE_M));
+          for (int c = 0; c < HC; ++c) {
+            uint4* slot = reinterpret_cast<uint4*>(Bs + sw128_off(ptid, (part * HC + c) * 8, TILE_M));
             uint4 x = *slot;
             const uint4 u = u4[c];
             x.x = bf16x2_sub(x.x, bf16x2_mul(t2, u.x));
@@ -244,8 +251,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const float4 tv = *reinterpret_cast<const float4*>(ts);
           const float4* u4 = reinterpret_cast<const float4*>(u32);
 #pragma unroll 2
-          for (int c = 0; c < D / 8; ++c) {
-            uint4* slot = reinterpret_cast<uint4*>(Bs + sw128_off(ptid, c * 8, TILE_M));
+          for (int c = 0; c < HC; ++c) {
+            uint4* slot = reinterpret_cast<uint4*>(Bs + sw128_off(ptid, (part * HC + c) * 8, TILE_M));
             float xv[8];
             unpack8_bf16(*slot, xv);
 #pragma unroll
@@ -326,10 +333,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     __syncwarp();
   } else {
-    // ---------------- epilogue: thread = output feature, 64 rows per tile ----------------
-    const int e = warp - EPI_WARP0;
+    // ---------------- epilogue: thread = output feature, the tile's 128 rows ----------------
+    // (warps 6-9, one per TMEM lane group)
     const int lg = warp & 3;
-    const int half = e >> 2;
     const int feat = lg * 32 + lane;
     const bool active = lg * 32 < D;  // warp-uniform (d = 64 uses lane groups 0-1)
     float run_max = 0.f, rmin = __int_as_float(0x7f800000), rmax = -__int_as_float(0x7f800000);
@@ -360,11 +366,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         cur_cell = cell;
       }
       tc_fence_after();
-      const int64_t row0 = tile * TILE_M + half * 64;  // first row of this warp's half
+      const int64_t row0 = tile * TILE_M;
 #pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
+      for (int cc = 0; cc < 4; ++cc) {
         float v[32];
-        tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * TILE_M + half * 64 + cc * 32), v);
+        tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * TILE_M + cc * 32), v);
         if (!active) continue;
         if (SYM) {
           // rows past the end hold R = 0 and cannot raise |max|
