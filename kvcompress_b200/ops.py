@@ -45,18 +45,26 @@ _WS: dict[tuple[int, int], torch.Tensor] = {}
 # Optional launch log for the benchmark: (stage, start event, end event,
 # kernel launches, algorithmic bytes) per C ABI call on the current stream.
 _TRACE: list | None = None
+_TRACE_STAGES: frozenset | None = None  # stages to record (None: every stage)
 
 
-def trace_start() -> None:
-    """Record CUDA events around every stage launched from now on."""
-    global _TRACE
+def trace_start(stages=None) -> None:
+    """Record CUDA events around every stage launched from now on, or only
+    around the named ``stages`` (each recorded event pair costs the stream a
+    little time, so a timed run records only the stages it reports)."""
+    global _TRACE, _TRACE_STAGES
     _TRACE = []
+    _TRACE_STAGES = None if stages is None else frozenset(stages)
+
+
+def _traced(name: str) -> bool:
+    return _TRACE is not None and (_TRACE_STAGES is None or name in _TRACE_STAGES)
 
 
 def trace_stop() -> list:
     """Stop recording and return the log."""
-    global _TRACE
-    log, _TRACE = _TRACE or [], None
+    global _TRACE, _TRACE_STAGES
+    log, _TRACE, _TRACE_STAGES = _TRACE or [], None, None
     return log
 
 
@@ -68,7 +76,7 @@ class _Stage:
         self.ev0 = None
 
     def __enter__(self):
-        if _TRACE is not None:
+        if _traced(self.name):
             self.ev0 = torch.cuda.Event(enable_timing=True)
             self.ev0.record()
         return self
@@ -460,10 +468,13 @@ def compress(xs, *, rt: int, rd: int, mode_f: int, k_f: int, omega_f: torch.Tens
     ptr = lambda x: x.data_ptr() if x is not None else None  # noqa: E731
     evs = None
     if _TRACE is not None:
-        evs = [torch.cuda.Event(enable_timing=True) for _ in range(2 * len(_COMPRESS_STAGES))]
+        evs = [torch.cuda.Event(enable_timing=True) if _traced(name) else None
+               for name, _ in _COMPRESS_STAGES for _ in range(2)]
         for e in evs:
-            e.record()  # creates the CUDA event the library records again
-        ev_arr = ptr_array(e.cuda_event for e in evs)  # the library keeps this pointer until reset
+            if e is not None:
+                e.record()  # creates the CUDA event the library records again
+        # stages without events get null pointers, which the library skips
+        ev_arr = ptr_array(e.cuda_event if e is not None else 0 for e in evs)  # kept by the library until reset
         check(L.kvc_trace_stages(ev_arr, len(evs)), "kvc_trace_stages")
     try:
         check(L.kvc_compress(n, _ptrs(xs), m, t, d, _code(dt), rt, rd, mode_f, k_f, ptr(omega_f), mode_t, k_t,
@@ -483,7 +494,7 @@ def compress(xs, *, rt: int, rd: int, mode_f: int, k_f: int, omega_f: torch.Tens
                  "core": xp_bytes, "residual_stats": x_bytes,
                  "residual_quant": x_bytes + (codes.numel() if codes is not None else 0), "cast": 0}
         for i, (name, launches) in enumerate(_COMPRESS_STAGES):
-            if name in ("residual_stats", "residual_quant") and bits == 0:
+            if (name in ("residual_stats", "residual_quant") and bits == 0) or evs[2 * i] is None:
                 continue
             nb = xp_bytes if (name == "gram" and i > 0) else sizes[name]
             _TRACE.append((name, evs[2 * i], evs[2 * i + 1], launches, nb))
