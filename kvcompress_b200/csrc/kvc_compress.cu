@@ -20,6 +20,11 @@
 #include "kvc_common.cuh"
 
 namespace kvc {
+
+// lets the next tensor-core quantise launch on this thread reuse the Tucker
+// row terms the stats launch before it left in the shared scratch
+void tc_reuse_tucker_rows(bool allow);
+
 namespace {
 
 size_t a256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -200,9 +205,12 @@ extern "C" int kvc_compress(int n_cells, const void* const* x, int64_t m, int64_
       return rc;
     if ((rc = mark(ST_STATS, 1, stream))) return rc;
     if ((rc = mark(ST_QUANT, 0, stream))) return rc;
-    if ((rc = kvc_residual_quant(n, xf, m, t, d, dtype, co, ut, ud, rt, rd, proj, bits, symmetric, scale_mode,
-                                 group_size, stat_dtype, arith_dtype, sc, zz, cd, scratch, scr, stream)))
-      return rc;
+    // the stats call just above left the Tucker row terms in the same scratch
+    tc_reuse_tucker_rows(true);
+    rc = kvc_residual_quant(n, xf, m, t, d, dtype, co, ut, ud, rt, rd, proj, bits, symmetric, scale_mode,
+                            group_size, stat_dtype, arith_dtype, sc, zz, cd, scratch, scr, stream);
+    tc_reuse_tucker_rows(false);
+    if (rc) return rc;
     if ((rc = mark(ST_QUANT, 1, stream))) return rc;
   }
   if ((rc = mark(ST_CAST, 0, stream))) return rc;

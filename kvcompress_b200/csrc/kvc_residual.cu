@@ -36,6 +36,7 @@ int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* 
                          int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd, const float* proj,
                          int64_t t0, int64_t t1, void* const* out, void* workspace, size_t ws_bytes,
                          cudaStream_t st);
+void tc_reuse_tucker_rows(bool allow);
 int tc_read_device_error(int* out);
 int tc_gram_read_device_error(int* out);
 

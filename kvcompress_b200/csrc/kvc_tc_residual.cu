@@ -1345,6 +1345,23 @@ size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd) {
          align256((size_t)n_cells * rows_pad * rdm_enc(rd) * 4) + align256((size_t)n_cells * 3 * d * d * 2);
 }
 
+// The Tucker row terms a stats launch left in its workspace, per host thread:
+// a quantise launch on the same workspace, cells and factors may use them
+// instead of recomputing them when its caller allows it
+// (tc_reuse_tucker_rows: kvc_compress, whose quantise call follows its stats
+// call on the same stream with nothing in between).
+struct RowsKey {
+  const void* ws;
+  int n_cells, rdm;
+  int64_t rows;
+  const void* core0;
+  const void* ut0;
+};
+static thread_local RowsKey tl_rows_key = {nullptr, 0, 0, 0, nullptr, nullptr};
+static thread_local bool tl_rows_reuse = false;
+
+void tc_reuse_tucker_rows(bool allow) { tl_rows_reuse = allow; }
+
 int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
                        const void* const* core, const void* const* u_token, const void* const* u_feature,
                        int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
@@ -1421,7 +1438,13 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
         proj, sp, scale_mode == KVC_SCALE_CHANNEL, fold, d, bimg);
     if ((rc = check_launch("prep_quant_b_kernel"))) return rc;
   }
-  if (rt > 0) {
+  const RowsKey key = {workspace, n_cells, rdm, rows, rt > 0 ? core[0] : nullptr, rt > 0 ? u_token[0] : nullptr};
+  const bool rows_ready = mode == 1 && tl_rows_reuse && tl_rows_key.ws == key.ws &&
+                          tl_rows_key.n_cells == key.n_cells && tl_rows_key.rdm == key.rdm &&
+                          tl_rows_key.rows == key.rows && tl_rows_key.core0 == key.core0 &&
+                          tl_rows_key.ut0 == key.ut0;
+  tl_rows_key = RowsKey{nullptr, 0, 0, 0, nullptr, nullptr};
+  if (rt > 0 && !rows_ready) {
     CellPtrs cp, up;
     for (int c = 0; c < n_cells; ++c) {
       cp.p[c] = core[c];
@@ -1485,7 +1508,8 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
       zz.p[c] = zp[c];
     }
     minmax_finalize_kernel<<<n_cells, 128, 0, st>>>(mm, n_cells, d, bits, symmetric, scale_mode, stat_dtype, sc, zz);
-    return check_launch("minmax_finalize_kernel");
+    if ((rc = check_launch("minmax_finalize_kernel"))) return rc;
+    tl_rows_key = key;  // the row terms stay in the workspace for a following quantise launch
   }
   return KVC_OK;
 }
