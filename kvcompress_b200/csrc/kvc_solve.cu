@@ -517,7 +517,11 @@ __device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, 
     }
     __syncthreads();
     const double off = red[0], tot = red[1];
-    if (!(off > 1e-30 * tot)) break;
+    // converged once the off-diagonal part is below 1e-12 of ||A||_F: the
+    // eigenvalues are then exact to ~1e-24 and the eigenvectors to ~1e-12
+    // over the gap, well past the fp32 / 16-bit outputs (one to two sweeps
+    // fewer than driving it to the fp64 rounding level)
+    if (!(off > 1e-24 * tot)) break;
     // off-diagonal entries at the rounding level of ||A||_F can never be
     // removed (a rotation leaves eps ||A|| behind), so they end the sweeps
     const double thr = 1e-15 * sqrt(tot);
