@@ -411,7 +411,7 @@ def run_ours(args, w):
 
 def decode_stream(payloads, world, dev, block: int = 256, passes: int = 3):
     """Every layer's K and V decoded in consecutive blocks of ``block``
-    tokens through ``DecodeStream`` (plan made once, two launches per block):
+    tokens through ``DecodeStream`` (plan made once, one launch per block and group):
     the per-block cost a blockwise consumer pays, device-timed."""
     import torch.distributed as dist
 

@@ -264,8 +264,10 @@ int kvc_trace_stages(void* const* events, int n_events);
  *    tensor-core decode have plans; others return KVC_ERR_UNSUPPORTED
  *    (decode them with kvc_decompress).
  *  - kvc_decode_plan_run: decodes tokens [t0, t1) of every cell into out[c]
- *    ((m, t1 - t0, d) bf16, 16-byte aligned): two kernel launches, bit for
- *    bit the same rows as kvc_decompress over that range.  Runs of one plan
+ *    ((m, t1 - t0, d) bf16, 16-byte aligned): one kernel launch for rank-1
+ *    factors in fp16 / bf16 over whole 128-token blocks starting at a
+ *    multiple of 8 (the row terms are formed inside the decode), two
+ *    otherwise; bit for bit the same rows as kvc_decompress over that range.  Runs of one plan
  *    share its workspace: issue them on one stream.
  */
 size_t kvc_decode_plan_bytes(void);

@@ -7,7 +7,7 @@ The reference decodes whole payloads (``reconstruct_payload``,
 kvcompress/compressor/jolt.py:401-463); here the part of the decode that does
 not depend on the range (the codes' tensor maps and each cell's rotation
 image) is built once per group of same-layout payloads, and each block is
-two kernel launches per group (``ops.DecodePlan``).  Layouts without a
+one or two kernel launches per group (``ops.DecodePlan``).  Layouts without a
 tensor-core plan fall back to ``decompress_tokens``'s path for every block.
 """
 
@@ -70,7 +70,7 @@ class DecodeStream:
         return all(plan is not None for _, plan in self._groups)
 
     def decode(self, t0: int, t1: int):
-        """Tokens ``[t0, t1)`` of every payload (two launches per group)."""
+        """Tokens ``[t0, t1)`` of every payload (one or two launches per group)."""
         t0, t1 = int(t0), int(t1)
         if not 0 <= t0 < t1 <= self.tokens:
             raise ValueError(f"DecodeStream.decode: bad token range [{t0}, {t1}) of {self.tokens}")

@@ -959,10 +959,15 @@ struct DecStages<D, CB, RDM, 2> {
 
 struct DecArgsTc {
   CellPtrs ud;
+  CellPtrs core, ut;  // rows_direct: the rank-1 factors the row terms come from
   CellPtrsMut out;
   int64_t m, t0, tl, tiles_per_cell, total_tiles, tiles_per_cta;
   int tb_per_head;
   int rt, rd, factor_dtype;
+  // rt = rd = 1, 2-byte factors, 128-token head blocks, 16-byte aligned
+  // u_token rows: each tile's row terms core[h] * u_token[t] are formed in
+  // the kernel from a 256-byte bulk copy of u_token (no row-term kernel)
+  int rows_direct;
   const uint8_t* bimg;  // per cell: two swizzled B images of diag(scale) Pi (+ the u_feature block)
   const float* tmp;     // [cell][m * tl][rdm] fp32 Tucker row term (+ 132 floats of slack at the end)
 };
@@ -1041,8 +1046,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int64_t i_tok = (tc % A.tb_per_head) * TILE_M + ptid;
         const int64_t base = (int64_t)(tile / A.tiles_per_cell) * A.m * A.tl + (tc / A.tb_per_head) * A.tl +
                              (tc % A.tb_per_head) * TILE_M;
-        if (i_tok < A.tl)
+        if (A.rows_direct) {
+          // core[h] * u_token[t]: the exact fp32 product of two 2-byte values,
+          // the row term the row-term kernel would have written
+          const int h = (int)(tc / A.tb_per_head);
+          tv = load_dt(A.core.p[tile / A.tiles_per_cell], h, A.factor_dtype) *
+               load_dt(smem + L::OFF_T + st * L::T_BYTES, ptid, A.factor_dtype);
+        } else if (i_tok < A.tl) {
           tv = reinterpret_cast<const float*>(smem + L::OFF_T + st * L::T_BYTES)[(base & 3) + ptid];
+        }
       }
       const uint8_t* Cs = smem + L::OFF_C + st * L::C_BYTES + ptid * CB;
       // the stage is written by TMA with the swizzle of its row width (32,
@@ -1114,9 +1126,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const int h = (int)(tile / A.tb_per_head);
         const int64_t i0 = (tile % A.tb_per_head) * TILE_M;
         const bool tload = FOLD && A.rt > 0;
-        mbar_expect_tx(&loaded[st], L::C_BYTES + (tload ? L::T_BYTES : 0u));
+        const uint32_t tbytes = !tload ? 0u : A.rows_direct ? TILE_M * 2u : L::T_BYTES;
+        mbar_expect_tx(&loaded[st], L::C_BYTES + tbytes);
         tma_load_3d(sbase + L::OFF_C + st * L::C_BYTES, &cmaps.m[cell], 0, (int)(A.t0 + i0), h, &loaded[st]);
-        if (tload) {
+        if (tload && A.rows_direct) {
+          // u_token of the tile's 128 tokens (t0 + i0 .. + 127), 256 bytes
+          bulk_load(sbase + L::OFF_T + st * L::T_BYTES,
+                    static_cast<const uint8_t*>(A.ut.p[cell]) + (A.t0 + i0) * 2, TILE_M * 2u, &loaded[st]);
+        } else if (tload) {
           const int64_t base = (int64_t)cell * A.m * A.tl + (int64_t)h * A.tl + i0;
           bulk_load(sbase + L::OFF_T + st * L::T_BYTES, A.tmp + (base & ~(int64_t)3), L::T_BYTES, &loaded[st]);
         }
@@ -1615,7 +1632,18 @@ int tc_decode_plan_run(const TcDecodePlan* p, int64_t t0, int64_t t1, void* cons
   a.factor_dtype = p->factor_dtype;
   a.bimg = p->bimg;
   a.tmp = p->tmp;
-  if (rt > 0) {
+  bool direct = rt == 1 && rd == 1 && (p->factor_dtype == KVC_F16 || p->factor_dtype == KVC_BF16) &&
+                tl % TILE_M == 0 && t0 % 8 == 0;
+  for (int c = 0; c < n_cells && direct; ++c)
+    direct = (reinterpret_cast<uintptr_t>(p->ut.p[c]) & 15u) == 0;
+  a.rows_direct = direct ? 1 : 0;
+  if (direct) {
+    for (int c = 0; c < n_cells; ++c) {
+      a.core.p[c] = p->core.p[c];
+      a.ut.p[c] = p->ut.p[c];
+    }
+  }
+  if (rt > 0 && !direct) {
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(m * tl * rdm, 256), 1024));
     tucker_rows_kernel<<<dim3(blocks, n_cells), 256, 0, st>>>(p->core, p->ut, p->factor_dtype, KVC_F32, m, t0, tl, rt,
                                                               rd, rdm, m * tl, p->tmp);

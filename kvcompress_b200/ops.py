@@ -514,7 +514,7 @@ class DecodePlan:
     Holds the plan's host bytes, its own device workspace (the cells' B
     images and the Tucker row terms) and references to the payload tensors,
     which must not change while the plan lives.  ``run(t0, t1)`` decodes
-    tokens ``[t0, t1)`` of every cell with two kernel launches, bit for bit
+    tokens ``[t0, t1)`` of every cell with one or two kernel launches, bit for bit
     the rows ``decompress`` gives for that range.  Use one plan from one
     stream at a time.  ``DecodePlan.make`` returns None for layouts without a
     tensor-core plan (decode those with ``decompress``).
