@@ -58,6 +58,7 @@ constexpr int NEPI = 256;  // epilogue threads
 constexpr int STATS_XF_WARP1 = 10;
 constexpr int RD_MAX = 16;
 constexpr uint32_t TM_ACC = 256;  // TMEM column of accumulator 0 (1 at +128)
+constexpr int CORE_MAX = 64;      // heads per cell whose row terms the encode forms in the kernel
 
 __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
   const uint32_t a = smem_u32(p);
@@ -134,7 +135,8 @@ struct StatsLayout {
                                                               // u_feature: bf16 [j] or fp32 [j][4]
   static constexpr uint32_t OFF_T = NS * B_BYTES;
   static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
-  static constexpr uint32_t OFF_RING = OFF_U + 8 * U_BYTES;  // tile ids drawn by the producer
+  static constexpr uint32_t OFF_CORE = OFF_U + 8 * U_BYTES;  // per transform warp: core[h] of the cell
+  static constexpr uint32_t OFF_RING = OFF_CORE + 8 * CORE_MAX * 4;  // tile ids drawn by the producer
   static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
   static constexpr uint32_t NBAR = 3 * NS + 4;                    // loaded, full, empty, acc full x2, acc empty x2
   static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
@@ -149,7 +151,27 @@ struct EncArgs {
   const uint32_t* arows;  // A = Pi in three bf16 terms: [term][128 rows][D/2 pairs]
   int32_t* minmax;        // STATS: [cell][2][d] ordered ints (min, max)
   const float* tmp;       // [cell][tiles_per_cell * 128][rdm]: sum_a core[h][a][r] u_token[t][a], bf16-rounded
+  // rows_direct (rt = rd = 1, T a multiple of 128, at most CORE_MAX heads,
+  // 16-byte aligned u_token): a tile's row terms bf16(core[h] * u_token[t])
+  // are formed in the kernel from a 256-byte bulk copy of u_token and the
+  // cell's core[] kept in shared memory, instead of from tmp
+  CellPtrs core, ut;
+  int64_t t_tok;  // tokens per head
+  int rows_direct;
 };
+
+// Bits of the bf16 Tucker term of a tile's row ptid (rd = 1): from the
+// stage's row-term window, or (rows_direct) bf16(core[h] * u_token[t]) from
+// the stage's u_token copy and the warp's core[] table, the exact bf16
+// product rounded once as the row-term kernel rounds it.  row0: the tile's
+// first row in the cell.
+__device__ __forceinline__ uint32_t enc_row_term(const EncArgs& A, const uint8_t* tslot, const float* cs, int ptid,
+                                                 int64_t row0) {
+  // rows of a cell stay below 2^31 (checked by the launcher): 32-bit division
+  const float v = A.rows_direct ? cs[(uint32_t)row0 / (uint32_t)A.t_tok] * load_dt(tslot, ptid, KVC_BF16)
+                                : reinterpret_cast<const float*>(tslot)[ptid];
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
+}
 
 template <int D, bool SYM, int RDM, int NS>
 __global__ void __launch_bounds__(NTHREADS, 1)
@@ -202,6 +224,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int ptid = lgw * 32 + lane;
     float* u32 = reinterpret_cast<float*>(smem + L::OFF_U + (part * 4 + lgw) * L::U_BYTES);       // [j][4]
     uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + (part * 4 + lgw) * L::U_BYTES);  // [j]
+    float* cs = reinterpret_cast<float*>(smem + L::OFF_CORE) + (part * 4 + lgw) * CORE_MAX;     // [h]
     int cur_cell = -1;
     for (int it = 0;; ++it) {
       const int st = it % NS;
@@ -224,6 +247,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             u32[i] = r < A.rd ? __bfloat162float(ud[(part * HF + j) * A.rd + r]) : 0.f;
           }
         }
+        if (A.rows_direct)
+          for (int j = lane; j < (int)(A.rows / A.t_tok); j += 32) cs[j] = load_dt(A.core.p[cell], j, KVC_BF16);
         __syncwarp();
         cur_cell = cell;
       }
@@ -233,7 +258,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (RDM == 1) {
           // rd == 1: recon = bf16(t * u_j) and R = bf16(x - recon), each a
           // single rounding of the exact bf16 product / difference
-          const uint32_t th = (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(ts[0]));
+          const uint32_t th = enc_row_term(A, smem + L::OFF_T + st * L::T_BYTES, cs, ptid, row - ptid);
           const uint32_t t2 = th | (th << 16);
           const uint4* u4 = reinterpret_cast<const uint4*>(ub);
 #pragma unroll
@@ -286,11 +311,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         const int cell = (int)(g / A.tiles_per_cell);
         const int y = (int)((g % A.tiles_per_cell) * TILE_M);
-        mbar_expect_tx(&loaded[st], L::B_BYTES + (A.rt > 0 ? L::T_BYTES : 0u));
+        mbar_expect_tx(&loaded[st], L::B_BYTES + (A.rt > 0 ? (A.rows_direct ? TILE_M * 2u : L::T_BYTES) : 0u));
         const uint32_t dst = sbase + st * L::B_BYTES;
 #pragma unroll
         for (int h = 0; h < D / 64; ++h) tma_load_2d(dst + h * TILE_M * 128, &xmaps.m[cell], h * 64, y, &loaded[st]);
-        if (A.rt > 0)
+        if (A.rt > 0 && A.rows_direct)
+          bulk_load(sbase + L::OFF_T + st * L::T_BYTES,
+                    static_cast<const uint8_t*>(A.ut.p[cell]) + ((uint32_t)y % (uint32_t)A.t_tok) * 2u, TILE_M * 2u,
+                    &loaded[st]);
+        else if (A.rt > 0)
           bulk_load(sbase + L::OFF_T + st * L::T_BYTES,
                     A.tmp + ((int64_t)cell * A.tiles_per_cell * TILE_M + y) * RDM, L::T_BYTES, &loaded[st]);
       }
@@ -533,7 +562,8 @@ struct QuantLayout {
   static constexpr uint32_t OFF_T = OFF_Q + 8 * Q_BYTES;
   static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
   static constexpr uint32_t OFF_S = OFF_U + 4 * U_BYTES;
-  static constexpr uint32_t OFF_RING = OFF_S + 8 * S_BYTES;      // tile ids drawn by the producer
+  static constexpr uint32_t OFF_CORE = OFF_S + 8 * S_BYTES;   // per transform warp: core[h] of the cell
+  static constexpr uint32_t OFF_RING = OFF_CORE + 4 * CORE_MAX * 4;  // tile ids drawn by the producer
   static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
   static constexpr uint32_t NBAR = 2 * NS + 2 * 2 + 4 + 2;  // loaded, empty, A full/free x2, acc full/empty x2, B free/ready
   static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
@@ -590,6 +620,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int ptid = threadIdx.x;
     float* u32 = reinterpret_cast<float*>(smem + L::OFF_U + warp * L::U_BYTES);       // [j][4]
     uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + warp * L::U_BYTES);  // [j]
+    float* cs = reinterpret_cast<float*>(smem + L::OFF_CORE) + warp * CORE_MAX;      // [h]
     int cur_cell = -1;
     for (int it = 0;; ++it) {
       const int st = it % NS, b = it & 1;
@@ -613,6 +644,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             u32[i] = r < A.rd ? __bfloat162float(ud[j * A.rd + r]) : 0.f;
           }
         }
+        if (A.rows_direct)
+          for (int j = lane; j < (int)(A.rows / A.t_tok); j += 32) cs[j] = load_dt(A.core.p[cell], j, KVC_BF16);
         __syncwarp();
         cur_cell = cell;
       }
@@ -622,8 +655,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (RDM == 1) {
         // the whole row in registers first, so the x stage goes back to the
         // producer before this warp waits for its A buffer
-        const float* ts = reinterpret_cast<const float*>(smem + L::OFF_T + st * L::T_BYTES) + ptid;
-        const uint32_t th = sub ? (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(ts[0])) : 0u;
+        const uint32_t th = sub ? enc_row_term(A, smem + L::OFF_T + st * L::T_BYTES, cs, ptid, row - ptid) : 0u;
         const uint32_t t2 = th | (th << 16);
         const uint4* u4 = reinterpret_cast<const uint4*>(ub);
         uint32_t r[D / 2];
@@ -711,11 +743,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         const int cell = (int)(tile / A.tiles_per_cell);
         const int y = (int)((tile % A.tiles_per_cell) * TILE_M);
-        mbar_expect_tx(&loaded[st], L::X_BYTES + (A.rt > 0 ? L::T_BYTES : 0u));
+        mbar_expect_tx(&loaded[st], L::X_BYTES + (A.rt > 0 ? (A.rows_direct ? TILE_M * 2u : L::T_BYTES) : 0u));
         const uint32_t dst = sbase + L::OFF_X + st * L::X_BYTES;
 #pragma unroll
         for (int h = 0; h < D / 64; ++h) tma_load_2d(dst + h * TILE_M * 128, &xmaps.m[cell], h * 64, y, &loaded[st]);
-        if (A.rt > 0)
+        if (A.rt > 0 && A.rows_direct)
+          bulk_load(sbase + L::OFF_T + st * L::T_BYTES,
+                    static_cast<const uint8_t*>(A.ut.p[cell]) + ((uint32_t)y % (uint32_t)A.t_tok) * 2u, TILE_M * 2u,
+                    &loaded[st]);
+        else if (A.rt > 0)
           bulk_load(sbase + L::OFF_T + st * L::T_BYTES,
                     A.tmp + ((int64_t)cell * A.tiles_per_cell * TILE_M + y) * RDM, L::T_BYTES, &loaded[st]);
       }
@@ -1456,10 +1492,20 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
     if ((rc = check_launch("prep_quant_b_kernel"))) return rc;
   }
   const RowsKey key = {workspace, n_cells, rdm, rows, rt > 0 ? core[0] : nullptr, rt > 0 ? u_token[0] : nullptr};
-  const bool rows_ready = mode == 1 && tl_rows_reuse && tl_rows_key.ws == key.ws &&
+  bool direct = rt == 1 && rd == 1 && t % TILE_M == 0 && m <= CORE_MAX;
+  for (int c = 0; c < n_cells && direct; ++c) direct = (reinterpret_cast<uintptr_t>(u_token[c]) & 15u) == 0;
+  a.rows_direct = direct ? 1 : 0;
+  a.t_tok = t;
+  if (direct) {
+    for (int c = 0; c < n_cells; ++c) {
+      a.core.p[c] = core[c];
+      a.ut.p[c] = u_token[c];
+    }
+  }
+  const bool rows_ready = direct || (mode == 1 && tl_rows_reuse && tl_rows_key.ws == key.ws &&
                           tl_rows_key.n_cells == key.n_cells && tl_rows_key.rdm == key.rdm &&
                           tl_rows_key.rows == key.rows && tl_rows_key.core0 == key.core0 &&
-                          tl_rows_key.ut0 == key.ut0;
+                          tl_rows_key.ut0 == key.ut0);
   tl_rows_key = RowsKey{nullptr, 0, 0, 0, nullptr, nullptr};
   if (rt > 0 && !rows_ready) {
     CellPtrs cp, up;

@@ -504,7 +504,7 @@ def compress(xs, *, rt: int, rd: int, mode_f: int, k_f: int, omega_f: torch.Tens
 # kvc_compress's stages in order, with the kernels each launches on the
 # tensor-core path (the stage timing of the bench)
 _COMPRESS_STAGES = [("gram", 4), ("sketch_solve", 1), ("project_feature", 1), ("gram", 3), ("sketch_solve", 1),
-                    ("apply_basis", 1), ("core", 2), ("residual_stats", 5), ("residual_quant", 2), ("cast", 3)]
+                    ("apply_basis", 1), ("core", 2), ("residual_stats", 4), ("residual_quant", 2), ("cast", 3)]
 
 
 class DecodePlan:
