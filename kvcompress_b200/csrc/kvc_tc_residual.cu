@@ -653,30 +653,34 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       const bool sub = A.rt > 0 && row < A.rows;
       const uint32_t tm_row = tmem + ((uint32_t)(warp * 32) << 16) + b * ACOLS;
       if (RDM == 1) {
-        // the whole row in registers first, so the x stage goes back to the
-        // producer before this warp waits for its A buffer
-        const uint32_t th = sub ? enc_row_term(A, smem + L::OFF_T + st * L::T_BYTES, cs, ptid, row - ptid) : 0u;
-        const uint32_t t2 = th | (th << 16);
-        const uint4* u4 = reinterpret_cast<const uint4*>(ub);
+        // the whole row and its Tucker term in registers first, so the x
+        // stage goes back to the producer before the arithmetic and before
+        // this warp waits for its A buffer
         uint32_t r[D / 2];
 #pragma unroll
         for (int c = 0; c < D / 8; ++c) {
-          uint4 x = *reinterpret_cast<const uint4*>(Xs + sw128_off(ptid, c * 8, TILE_M));
-          if (sub) {
-            // rd == 1: recon = bf16(t * u_j) and R = bf16(x - recon), each a
-            // single rounding of the exact bf16 product / difference
-            const uint4 u = u4[c];
-            x.x = bf16x2_sub(x.x, bf16x2_mul(t2, u.x));
-            x.y = bf16x2_sub(x.y, bf16x2_mul(t2, u.y));
-            x.z = bf16x2_sub(x.z, bf16x2_mul(t2, u.z));
-            x.w = bf16x2_sub(x.w, bf16x2_mul(t2, u.w));
-          }
+          const uint4 x = *reinterpret_cast<const uint4*>(Xs + sw128_off(ptid, c * 8, TILE_M));
           r[4 * c] = x.x;
           r[4 * c + 1] = x.y;
           r[4 * c + 2] = x.z;
           r[4 * c + 3] = x.w;
         }
+        const uint32_t th = sub ? enc_row_term(A, smem + L::OFF_T + st * L::T_BYTES, cs, ptid, row - ptid) : 0u;
         mbar_arrive(&empty[st]);  // the x stage is no longer needed
+        if (sub) {
+          // rd == 1: recon = bf16(t * u_j) and R = bf16(x - recon), each a
+          // single rounding of the exact bf16 product / difference
+          const uint32_t t2 = th | (th << 16);
+          const uint4* u4 = reinterpret_cast<const uint4*>(ub);
+#pragma unroll
+          for (int c = 0; c < D / 8; ++c) {
+            const uint4 u = u4[c];
+            r[4 * c] = bf16x2_sub(r[4 * c], bf16x2_mul(t2, u.x));
+            r[4 * c + 1] = bf16x2_sub(r[4 * c + 1], bf16x2_mul(t2, u.y));
+            r[4 * c + 2] = bf16x2_sub(r[4 * c + 2], bf16x2_mul(t2, u.z));
+            r[4 * c + 3] = bf16x2_sub(r[4 * c + 3], bf16x2_mul(t2, u.w));
+          }
+        }
         // the MMAs of tile it - 2 read this A buffer last
         if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x172)) break;
         tc_fence_after();
