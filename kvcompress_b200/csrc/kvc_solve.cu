@@ -344,11 +344,11 @@ __global__ void __launch_bounds__(SNT) sketch_solve_kernel(SolveArgs a) {
 // ---------------------------------------------------------------------------
 constexpr int SM_P = 128;
 constexpr int SM_K = 32;
-constexpr int SM_QS = SM_K + 1;  // row stride (doubles) of Q and Z
+constexpr int SM_QS = SM_K + 2;  // row stride (doubles) of Q and Z: even, so rows start on 16 bytes
 constexpr int SM_NT = 256;
 
 size_t small_smem_bytes(int p) {
-  return sizeof(double) * ((size_t)p * p + 2 * (size_t)p * SM_QS + 3 * SM_K * SM_K + 4 * SM_K + 64) +
+  return sizeof(double) * (((size_t)p * p + 1) / 2 * 2 + 2 * (size_t)p * SM_QS + 3 * SM_K * SM_K + 4 * SM_K + 64) +
          sizeof(int) * (4 * SM_K + 64);
 }
 
@@ -372,19 +372,36 @@ __device__ __forceinline__ bool f32_range(double x) { return fabs(x) > 1e-36 && 
 __device__ __forceinline__ double rsqrt_any(double x) { return f32_range(x) ? rsqrt_nr(x) : 1.0 / sqrt(x); }
 __device__ __forceinline__ double rcp_any(double x) { return f32_range(x) ? rcp_nr(x) : 1.0 / x; }
 
-// Z (p x k) = G Q, G symmetric p x p.  Thread: one row, 8 columns.
+// Z (p x k) = G Q, G symmetric p x p.  Thread: one row, 8 columns.  The
+// eight Q values of a step are read as four 16-byte pairs when Q is 16-byte
+// aligned (the shared-memory wavefronts of these broadcast reads are what
+// bound the product); the FMAs run in the same order either way.
 __device__ void sm_gemm(double* Z, const double* G, const double* Q, int p, int k) {
   const int groups = (k + 7) / 8;
+  const bool paired = (reinterpret_cast<uintptr_t>(Q) & 15) == 0;
   for (int task = threadIdx.x; task < p * groups; task += blockDim.x) {
     const int i = task % p, jg = task / p;
     double acc[8];
 #pragma unroll
     for (int c = 0; c < 8; ++c) acc[c] = 0.0;
-    for (int kk = 0; kk < p; ++kk) {
-      const double g = G[kk * p + i];
-      const double* q = Q + kk * SM_QS + jg * 8;
+    if (paired) {
+      for (int kk = 0; kk < p; ++kk) {
+        const double g = G[kk * p + i];
+        const double2* q = reinterpret_cast<const double2*>(Q + kk * SM_QS + jg * 8);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) acc[c] = fma(g, q[c], acc[c]);
+        for (int c = 0; c < 4; ++c) {
+          const double2 v = q[c];
+          acc[2 * c] = fma(g, v.x, acc[2 * c]);
+          acc[2 * c + 1] = fma(g, v.y, acc[2 * c + 1]);
+        }
+      }
+    } else {
+      for (int kk = 0; kk < p; ++kk) {
+        const double g = G[kk * p + i];
+        const double* q = Q + kk * SM_QS + jg * 8;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] = fma(g, q[c], acc[c]);
+      }
     }
 #pragma unroll
     for (int c = 0; c < 8; ++c)
@@ -640,12 +657,12 @@ __device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, 
 }
 
 __global__ void __launch_bounds__(SM_NT) sketch_solve_small_kernel(SolveArgs a) {
-  extern __shared__ double sm[];
+  extern __shared__ __align__(16) double sm[];
   const int cell = blockIdx.x;
   const int p = a.p, k = a.k, rank = a.rank;
   const double* gram = a.gram + cell * a.gram_stride;
   double* G = sm;                       // p x p
-  double* Q = G + p * p;                // p x SM_QS
+  double* Q = G + (p * p + 1) / 2 * 2;  // p x SM_QS, 16-byte aligned
   double* Z = Q + p * SM_QS;            // p x SM_QS
   double* S = Z + p * SM_QS;            // SM_K x SM_K
   double* C = S + SM_K * SM_K;
