@@ -675,7 +675,21 @@ __global__ void __launch_bounds__(SM_NT) sketch_solve_small_kernel(SolveArgs a) 
   int* order = reinterpret_cast<int*>(red + 64);
   int* pq = order + SM_K;               // 2 SM_K
   __shared__ double nrm_s;
-  for (int i = threadIdx.x; i < p * p; i += blockDim.x) G[i] = gram[i];
+  {
+    // sixteen loads in flight per thread before their stores (the Gram is
+    // 128 KB at p = 128, one L2 round trip per batch)
+    constexpr int U = 16;
+    const int nt = blockDim.x, pp = p * p;
+    int i = threadIdx.x;
+    for (; i + (U - 1) * nt < pp; i += U * nt) {
+      double v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = __ldcg(gram + i + u * nt);
+#pragma unroll
+      for (int u = 0; u < U; ++u) G[i + u * nt] = v[u];
+    }
+    for (; i < pp; i += nt) G[i] = __ldcg(gram + i);
+  }
   if (a.side == KVC_SIDE_LEFT) {
     const double* y0 = gram + (int64_t)p * p;
     for (int i = threadIdx.x; i < p * k; i += blockDim.x) Q[(i / k) * SM_QS + i % k] = y0[i];
