@@ -196,10 +196,14 @@ int kvc_decompress(int n_cells, const uint8_t* const* codes, const float* const*
  * same kernels as kvc_decompress, with scratch in a fixed array of
  * KVC_NOALLOC_SCRATCH_BYTES per device inside this library, and allocates
  * nothing.
- *  - Limit: calls whose kvc_decompress_workspace_bytes(n_cells, m*t, d, rd)
- *    exceeds KVC_NOALLOC_SCRATCH_BYTES fail with KVC_ERR_WORKSPACE (K and
- *    V of one Llama-3-8B layer at 8k tokens need about 0.7 MB).
- *  - The first call on each device looks up the array's address
+ *  - Limit: decodes that take the tensor-core decoder (bf16 output, d of 64
+ *    or 128, a JL rotation, symmetric per-channel scales) and whose
+ *    kvc_decompress_workspace_bytes(n_cells, m*t, d, rd) exceeds
+ *    KVC_NOALLOC_SCRATCH_BYTES fail with KVC_ERR_WORKSPACE (K and V of one
+ *    Llama-3-8B layer at 8k tokens need about 0.7 MB).  Other layouts are
+ *    decoded by the SIMT kernel, which uses no scratch, at any size.
+ *  - The first call on each device (and again after that device's context
+ *    was destroyed and re-created) looks up the array's address
  *    (cudaGetSymbolAddress, which may load the module): make it before any
  *    stream capture.
  *  - Nothing in the array has to start at zero; each call writes every byte

@@ -9,12 +9,16 @@
 //
 // Scratch: g_noalloc_scratch, KVC_NOALLOC_SCRATCH_BYTES (8 MiB) per device,
 // allocated with the module.  Its address is looked up with
-// cudaGetSymbolAddress once per device, on the first call on that device;
-// that lookup may load the module, so make the first call on each device
-// before any stream capture.  Sizes whose decode scratch
+// cudaGetSymbolAddress once per device and CUDA context, on the first call
+// on that device (again after the device's context was destroyed and made
+// anew, e.g. after cudaDeviceReset: the old address would point into a
+// context that no longer exists); that lookup may load the module, so make
+// the first call on each device before any stream capture.  Only decodes that
+// take the tensor-core kernel use scratch: those whose scratch
 // (kvc_decompress_workspace_bytes) exceeds the array are rejected with
-// KVC_ERR_WORKSPACE.  Nothing is allocated: no cudaMalloc / cudaFree and no
-// allocating library call.
+// KVC_ERR_WORKSPACE; layouts that kvc_decompress decodes with its SIMT kernel
+// use none and have no size limit.  Nothing is allocated: no cudaMalloc /
+// cudaFree and no allocating library call.
 //
 // Nothing in the scratch has to start at zero: every byte the decode reads is
 // written earlier in the same call, on the same stream (operand tiles,
@@ -22,6 +26,8 @@
 // device, so two calls whose work overlaps in time on the device (different
 // streams, or different host threads) race on it; calls on one stream are
 // ordered and safe.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "kvc_common.cuh"
@@ -36,6 +42,9 @@ extern "C" int kvc_decompress(int n_cells, const uint8_t* const* codes, const fl
                               void* stream);
 
 namespace kvc {
+int kernel_policy();
+bool tc_decompress_eligible(int out_dtype, int d, int rd, int bits, int symmetric, int scale_mode,
+                            const float* proj);
 namespace {
 
 constexpr size_t kScratchBytes = (size_t)KVC_NOALLOC_SCRATCH_BYTES;
@@ -44,7 +53,28 @@ constexpr int kMaxDevices = 64;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kScratchBytes];
 
 std::mutex g_mu;
-void* g_scratch_addr[kMaxDevices];  // per device, looked up once
+// per device: the context the address was looked up in, and the address
+CUcontext g_scratch_ctx[kMaxDevices];
+void* g_scratch_addr[kMaxDevices];
+
+// cuCtxGetCurrent through the runtime's driver entry point (the library does
+// not link the driver library itself, so it loads on machines without one)
+typedef CUresult (*CtxGetCurrentFn)(CUcontext*);
+CtxGetCurrentFn g_ctx_get_current = nullptr;
+
+CUcontext current_context() {
+  if (!g_ctx_get_current) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &fn, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return nullptr;
+    g_ctx_get_current = reinterpret_cast<CtxGetCurrentFn>(fn);
+  }
+  CUcontext ctx = nullptr;
+  if (g_ctx_get_current(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
 
 // Device address of the scratch array on the current device.
 int scratch_address(void** addr) {
@@ -52,13 +82,18 @@ int scratch_address(void** addr) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(KVC_ERR_ARG, "kvc_decompress_noalloc: device ordinal out of range");
+  // the thread's current context; NULL before the runtime made one current
+  // (then the lookup below makes the device's primary context current)
   std::lock_guard<std::mutex> lock(g_mu);
-  if (!g_scratch_addr[dev]) {
+  CUcontext ctx = current_context();
+  if (!g_scratch_addr[dev] || !ctx || ctx != g_scratch_ctx[dev]) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
     if (e != cudaSuccess || !p)
       return fail(KVC_ERR_LAUNCH, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+    ctx = current_context();
     g_scratch_addr[dev] = p;
+    g_scratch_ctx[dev] = ctx;
   }
   *addr = g_scratch_addr[dev];
   return KVC_OK;
@@ -77,10 +112,14 @@ extern "C" int kvc_decompress_noalloc(int n_cells, const uint8_t* const* codes, 
                                       int out_dtype, void* const* out, void* stream) {
   if (n_cells <= 0 || n_cells > KVC_MAX_CELLS) return fail(KVC_ERR_ARG, "kvc_decompress_noalloc: bad n_cells");
   if (m <= 0 || t <= 0 || d <= 0 || rd < 0) return fail(KVC_ERR_SHAPE, "kvc_decompress_noalloc: bad shape");
-  const size_t need = kvc_decompress_workspace_bytes(n_cells, m * t, d, rd);
-  if (need > kScratchBytes)
-    return fail(KVC_ERR_WORKSPACE, "kvc_decompress_noalloc: needs " + std::to_string(need) +
-                                       " bytes of scratch, above the fixed " + std::to_string(kScratchBytes));
+  // only the tensor-core decode reads the workspace; the SIMT decode of the
+  // other layouts ignores it, so its size is no limit there
+  if (kernel_policy() == 0 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj)) {
+    const size_t need = kvc_decompress_workspace_bytes(n_cells, m * t, d, rd);
+    if (need > kScratchBytes)
+      return fail(KVC_ERR_WORKSPACE, "kvc_decompress_noalloc: needs " + std::to_string(need) +
+                                         " bytes of scratch, above the fixed " + std::to_string(kScratchBytes));
+  }
   void* scratch = nullptr;
   int rc = scratch_address(&scratch);
   if (rc) return rc;

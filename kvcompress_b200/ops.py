@@ -101,6 +101,33 @@ def _stream() -> ctypes.c_void_p:
     return ctypes.c_void_p(_raw_stream())
 
 
+class _NoGuard:
+    __slots__ = ()
+
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NO_GUARD = _NoGuard()
+
+
+def _on(device) -> object:
+    """Make ``device`` current around a library call.
+
+    The C functions launch on the calling thread's current device and take the
+    current stream of that device; tensors placed on another GPU (a model moved
+    with ``.to("cuda:1")`` and no ``torch.cuda.set_device``) would otherwise be
+    handed to kernels running on the wrong device.  No-op (and no driver call)
+    when the device is already current."""
+    idx = torch.device(device).index
+    if idx is None or idx == torch.cuda.current_device():
+        return _NO_GUARD
+    return torch.cuda.device(idx)
+
+
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     """Scratch buffer for one launch, reused per (device, stream).
 
@@ -235,7 +262,7 @@ def gram(cells: Sequence[torch.Tensor], omega: torch.Tensor | None) -> torch.Ten
     ws_n = L.kvc_gram_workspace_bytes(len(cells), rows, p, k)
     ws = workspace(ws_n, dev)
     nbytes = len(cells) * cells[0].numel() * cells[0].element_size() + (0 if omega is None else omega.numel() * 4)
-    with _Stage("gram", 3, nbytes):
+    with _on(dev), _Stage("gram", 3, nbytes):
         check(L.kvc_gram(len(cells), _ptrs(cells), rows, p,
                          _code(cells[0].dtype), omega.data_ptr() if omega is not None else None, k,
                          out.data_ptr(), ws.data_ptr(), ws.numel(), _stream()), "kvc_gram")
@@ -259,7 +286,7 @@ def sketch_solve(g: torch.Tensor, *, mode: int, side: int, p: int, n_other: int,
     ws_n = L.kvc_sketch_solve_workspace_bytes(n, mode, p, kk)
     ws = workspace(ws_n, dev)
     stride = gram_stride if gram_stride is not None else int(g.shape[1])
-    with _Stage("sketch_solve", 1, g.numel() * 8):
+    with _on(dev), _Stage("sketch_solve", 1, g.numel() * 8):
         check(L.kvc_sketch_solve(n, mode, side, p, n_other, kk, rank, n_power, g.data_ptr(), stride,
                                  omega.data_ptr() if omega is not None else None, basis.data_ptr(),
                                  _code(basis.dtype), sv2.data_ptr(), tail.data_ptr(), ws.data_ptr(),
@@ -274,7 +301,7 @@ def project_feature(xs: Sequence[torch.Tensor], u_feature: Sequence[torch.Tensor
     rd = int(u_feature[0].shape[1])
     outs = _views(torch.empty(len(xs), t, m * rd, dtype=xs[0].dtype, device=xs[0].device))
     nbytes = len(xs) * (xs[0].numel() + outs[0].numel()) * xs[0].element_size()
-    with _Stage("project_feature", 1, nbytes):
+    with _on(xs[0].device), _Stage("project_feature", 1, nbytes):
         check(lib().kvc_project_feature(len(xs), _ptrs(xs), m, t, d,
                                         _code(xs[0].dtype), _ptrs(u_feature),
                                         rd, _ptrs(outs), _stream()),
@@ -289,7 +316,7 @@ def apply_basis(a: Sequence[torch.Tensor], mat: torch.Tensor) -> list[torch.Tens
     r = int(mat.shape[2])
     outs = _views(torch.empty(len(a), rows, r, dtype=a[0].dtype, device=a[0].device))
     nbytes = len(a) * (a[0].numel() + outs[0].numel()) * a[0].element_size()
-    with _Stage("apply_basis", 1, nbytes):
+    with _on(a[0].device), _Stage("apply_basis", 1, nbytes):
         check(lib().kvc_apply_basis(len(a), _ptrs(a), rows, p,
                                     _code(a[0].dtype), mat.data_ptr(), r,
                                     _ptrs(outs), _stream()), "kvc_apply_basis")
@@ -307,7 +334,7 @@ def core(x_proj_t: Sequence[torch.Tensor], u_token: Sequence[torch.Tensor], m: i
     ws_n = L.kvc_core_workspace_bytes(len(outs), t, m, rd, rt)
     ws = workspace(ws_n, dev)
     nbytes = len(outs) * (x_proj_t[0].numel() + u_token[0].numel()) * x_proj_t[0].element_size()
-    with _Stage("core", 2, nbytes):
+    with _on(dev), _Stage("core", 2, nbytes):
         check(L.kvc_core(len(outs), _ptrs(x_proj_t),
                          _ptrs(u_token), t, m, rd, rt,
                          _code(x_proj_t[0].dtype), _ptrs(outs), ws.data_ptr(),
@@ -340,7 +367,7 @@ def residual_stats(xs, factors, proj, *, bits: int, symmetric: bool, scale_mode:
     L = lib()
     ws_n = L.kvc_residual_stats_workspace_bytes(n, m * t, d, rd)
     ws = workspace(ws_n, dev)
-    with _Stage("residual_stats", 2, n * xs[0].numel() * xs[0].element_size()):
+    with _on(dev), _Stage("residual_stats", 2, n * xs[0].numel() * xs[0].element_size()):
         check(L.kvc_residual_stats(n, _ptrs(xs), m, t, d, _code(xs[0].dtype),
                                    cp, up, dp, rt, rd, proj.data_ptr() if proj is not None else None,
                                    bits, int(symmetric), scale_mode, _code(stat_dtype),
@@ -370,7 +397,7 @@ def residual_quant(xs, factors, proj, scales, zps, *, bits: int, symmetric: bool
     cp, up, dp, rt, rd = _factor_ptrs(factors, n)
     ws = workspace(lib().kvc_residual_quant_workspace_bytes(n, m * t, d, rd), dev)
     nbytes = n * (xs[0].numel() * xs[0].element_size() + codes[0].numel())
-    with _Stage("residual_quant", 1, nbytes):
+    with _on(dev), _Stage("residual_quant", 1, nbytes):
         check(lib().kvc_residual_quant(n, _ptrs(xs), m, t, d,
                                        _code(xs[0].dtype), cp, up, dp, rt, rd,
                                        proj.data_ptr() if proj is not None else None, bits,
@@ -407,7 +434,7 @@ def decompress(shape, out_dtype: torch.dtype, *, codes=None, scales=None, zps=No
     nbytes = n * out[0].numel() * out[0].element_size()
     if bits > 0:
         nbytes += sum(c.numel() for c in codes) * (t1 - t0) // t
-    with _Stage("decompress", 1, nbytes):
+    with _on(dev0), _Stage("decompress", 1, nbytes):
         check(lib().kvc_decompress(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
                                    int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
                                    proj.data_ptr() if proj is not None else None, t0, t1,
@@ -429,6 +456,15 @@ def compress(xs, *, rt: int, rd: int, mode_f: int, k_f: int, omega_f: torch.Tens
     ``tail_token`` / ``tail_feature`` (n,) float64 and, with ``bits > 0``,
     ``scale`` / ``zero_point`` / ``codes``."""
     xs = _cells(xs, "compress")
+    with _on(xs[0].device):
+        return _compress(xs, rt=rt, rd=rd, mode_f=mode_f, k_f=k_f, omega_f=omega_f, mode_t=mode_t, k_t=k_t,
+                         omega_t=omega_t, n_power=n_power, proj=proj, bits=bits, symmetric=symmetric,
+                         scale_mode=scale_mode, group_size=group_size, factor_dtype=factor_dtype,
+                         stat_dtype=stat_dtype, arith_dtype=arith_dtype)
+
+
+def _compress(xs, *, rt, rd, mode_f, k_f, omega_f, mode_t, k_t, omega_t, n_power, proj, bits, symmetric,
+              scale_mode, group_size, factor_dtype, stat_dtype, arith_dtype) -> dict:
     m, t, d = (int(v) for v in xs[0].shape)
     dev, dt = xs[0].device, xs[0].dtype
     n = len(xs)
@@ -539,10 +575,11 @@ class DecodePlan:
                          device=dev)
         nb = int(L.kvc_decode_plan_bytes())
         buf = ctypes.create_string_buffer(nb)
-        rc = L.kvc_decode_plan_init(buf, nb, n, _ptrs(codes), _ptrs(scales), _ptrs(zps), bits, int(symmetric),
-                                    scale_mode, int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
-                                    proj.data_ptr() if proj is not None else None, _code(out_dtype),
-                                    ws.data_ptr(), ws.numel(), _stream())
+        with _on(dev):
+            rc = L.kvc_decode_plan_init(buf, nb, n, _ptrs(codes), _ptrs(scales), _ptrs(zps), bits, int(symmetric),
+                                        scale_mode, int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
+                                        proj.data_ptr() if proj is not None else None, _code(out_dtype),
+                                        ws.data_ptr(), ws.numel(), _stream())
         if rc == KVC.ERR_UNSUPPORTED:
             return None
         check(rc, "kvc_decode_plan_init")
@@ -554,7 +591,7 @@ class DecodePlan:
         if out is None:
             out = _views(torch.empty(self.n_cells, m, t1 - t0, d, dtype=self.out_dtype, device=self.device))
         nbytes = self.n_cells * out[0].numel() * out[0].element_size() + sum(self._codes_bytes) * (t1 - t0) // t
-        with _Stage("decode_range", 2, nbytes):
+        with _on(self.device), _Stage("decode_range", 2, nbytes):
             check(self._L.kvc_decode_plan_run(self._buf, len(self._buf), int(t0), int(t1), _ptrs(out), _stream()),
                   "kvc_decode_plan_run")
         return out
@@ -584,11 +621,12 @@ def decompress_noalloc(shape, out_dtype: torch.dtype, *, codes=None, scales=None
         z_arr = _ptrs(zps)
     else:
         c_arr = s_arr = z_arr = ptr_array([0] * n)
-    check(lib().kvc_decompress_noalloc(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
-                                       int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
-                                       proj.data_ptr() if proj is not None else None, t0, t1,
-                                       _code(out_dtype), _ptrs(out), _stream()),
-          "kvc_decompress_noalloc")
+    with _on(out[0].device):  # the stream, the library's scratch and the tensors on one device
+        check(lib().kvc_decompress_noalloc(n, c_arr, s_arr, z_arr, bits, int(symmetric), scale_mode,
+                                           int(group_size or 0), cp, up, dp, fdt, m, t, d, rt, rd,
+                                           proj.data_ptr() if proj is not None else None, t0, t1,
+                                           _code(out_dtype), _ptrs(out), _stream()),
+              "kvc_decompress_noalloc")
     return out
 
 
@@ -615,7 +653,7 @@ def cast(x: torch.Tensor, dtype: torch.dtype) -> torch.Tensor:
         raise RuntimeError("cast: CUDA tensors only")
     x = x.contiguous()
     out = torch.empty(x.shape, dtype=dtype, device=x.device)
-    with _Stage("cast", 1, x.numel() * (x.element_size() + out.element_size())):
+    with _on(x.device), _Stage("cast", 1, x.numel() * (x.element_size() + out.element_size())):
         check(lib().kvc_cast(x.numel(), x.data_ptr(), _code(x.dtype), out.data_ptr(), _code(dtype),
                              _stream()), "kvc_cast")
     return out

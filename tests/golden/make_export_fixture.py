@@ -19,7 +19,8 @@ Runs the reference's ``export_kv`` on a small seeded two-layer cache (bf16,
 * ``ref_export_layout.json``: tensor names, dtypes and shapes of the file,
   which ``export_kv`` here must reproduce for the same cache.
 
-The reference is imported from ``/root/reference`` (never copied).
+The reference is imported (never copied) from the source tree named by
+``--reference PATH`` or ``$KVCOMPRESS_REFERENCE``.
 """
 
 from __future__ import annotations
@@ -32,10 +33,11 @@ import sys
 import numpy as np
 import torch
 
-REF = "/root/reference"
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, REF)
-sys.path.insert(0, os.path.abspath(os.path.join(HERE, "..", "..")))
+sys.path.insert(0, HERE)
+from _reference import import_reference  # noqa: E402
+
+REF = import_reference()
 
 from kvcompress.adapters.vllm import export_kv, import_kv  # noqa: E402
 

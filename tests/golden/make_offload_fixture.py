@@ -12,7 +12,8 @@ dh)`` layout, then its ``decompress_block`` on every layer, and saves:
 * ``ref_offload.json``: per cell the payload's method, shape, dtype,
   metadata and byte count.
 
-The reference is imported from ``/root/reference`` (never copied).
+The reference is imported (never copied) from the source tree named by
+``--reference PATH`` or ``$KVCOMPRESS_REFERENCE``.
 """
 
 from __future__ import annotations
@@ -24,10 +25,11 @@ import sys
 import numpy as np
 import torch
 
-REF = "/root/reference"
 HERE = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, REF)
-sys.path.insert(0, os.path.abspath(os.path.join(HERE, "..", "..")))
+sys.path.insert(0, HERE)
+from _reference import import_reference  # noqa: E402
+
+REF = import_reference()
 
 from kvcompress import build_compressor  # noqa: E402
 from kvcompress.adapters.vllm_kv_offload import JoLTOffloadHandler  # noqa: E402

@@ -63,3 +63,23 @@ def test_cpu_tensors_fail_loudly():
         build_compressor("flashjolt", compression_ratio=4.0).compress(k, k[:1])
     with pytest.raises(ValueError):
         build_compressor("flashjolt", compression_ratio=4.0).compress(k[0], k[0])
+
+
+def test_library_calls_run_on_the_tensors_device(monkeypatch):
+    """``ops._on``: the library launches on the calling thread's current
+    device, so every wrapper makes the tensors' device current first; no
+    switch (no driver call) when it already is."""
+    from kvcompress_b200 import ops
+
+    switched = []
+
+    class FakeDevice:
+        def __init__(self, idx):
+            switched.append(idx)
+
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 0)
+    monkeypatch.setattr(torch.cuda, "device", FakeDevice)
+    assert ops._on(torch.device("cuda", 0)) is ops._NO_GUARD
+    assert ops._on(torch.device("cuda")) is ops._NO_GUARD
+    assert isinstance(ops._on(torch.device("cuda", 1)), FakeDevice)
+    assert switched == [1]
