@@ -67,6 +67,12 @@ WORKLOADS = {
     "llama3-8b-kv-b1-t8192-bf16": KVWorkload(
         "llama3-8b-kv-b1-t8192-bf16", 32, 8, 128, 1, 8192, torch.bfloat16,
         32, 0.1, 8, 500000.0, "flashjolt", 4.0),
+    # Llama-3-8B-shaped, batch 8 x 32k, FlashJoLT 4x: the cache of the
+    # previous entry compressed the FlashJoLT way (randomised SVDs), the
+    # target workload for 1 / 2 / 4 / 8 GPUs.
+    "llama3-8b-kv-b8-t32768-bf16": KVWorkload(
+        "llama3-8b-kv-b8-t32768-bf16", 32, 8, 128, 8, 32768, torch.bfloat16,
+        16, 0.1, 4, 10000.0, "flashjolt", 4.0),
     # Llama-3-8B-shaped, batch 8 x 32k, exact JoLT 3x.
     "llama3-8b-kv-b8-t32768-bf16-jolt": KVWorkload(
         "llama3-8b-kv-b8-t32768-bf16-jolt", 32, 8, 128, 8, 32768, torch.bfloat16,
