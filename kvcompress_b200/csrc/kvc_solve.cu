@@ -16,20 +16,22 @@
 //   EXACT: eigenpairs of G (LEFT) or H (RIGHT, U = A V Lambda^{-1/2}).
 //
 // orth() is CholeskyQR2 with rank dropping (a column whose Cholesky pivot
-// falls below 1e-10 of its norm is set to zero); the eigensolver is cyclic
-// two-sided Jacobi with round-robin parallel ordering.  Every loop has a
-// fixed trip count bound (at most 60 sweeps).
+// falls below 1e-10 of its norm is set to zero).  Only the `rank` leading
+// eigenpairs are computed, by the selected-eigenpair method of LAPACK's
+// dsyevx (Householder tridiagonalisation, bisection on Sturm counts,
+// inverse iteration, back-transformation; kvc_eig.cuh).  Every loop has a
+// fixed trip count bound.
 #include <algorithm>
 #include <cmath>
 
 #include "kvc_common.cuh"
+#include "kvc_eig.cuh"
 
 namespace kvc {
 namespace {
 
 constexpr int SNT = 512;
-constexpr int MAX_SWEEPS = 60;
-constexpr int MAX_PAIRS = 1024;
+constexpr int MAX_DIM = 2046;  // largest p and k of the general solver
 
 // C (M x N) = op(A) * B.  A is M x K row-major, or K x M when transA.
 __device__ void blk_gemm(double* __restrict__ C, const double* __restrict__ A, bool transA,
@@ -91,129 +93,6 @@ __device__ void blk_orth2(double* Y, int p, int k, const double* Mtx, double* Z,
   blk_cholqr(Y, p, k, Mtx, Z, S);
 }
 
-__device__ double blk_sum(double v) {
-  __shared__ double red[SNT / 32];
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
-  __syncthreads();
-  if (l == 0) red[w] = v;
-  __syncthreads();
-  double t = 0.0;
-  if (threadIdx.x < 32) {
-    t = threadIdx.x < (int)(blockDim.x / 32) ? red[threadIdx.x] : 0.0;
-    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
-  }
-  __shared__ double res;
-  if (threadIdx.x == 0) res = t;
-  __syncthreads();
-  return res;
-}
-
-// Symmetric eigensolver: A (n x n) is destroyed, V receives eigenvectors in
-// columns, evals[i] = A[i][i] after convergence (unsorted).
-__device__ void blk_jacobi(double* A, double* V, int n, double* evals) {
-  __shared__ int pos[2 * MAX_PAIRS];
-  __shared__ double cs[MAX_PAIRS], sn[MAX_PAIRS];
-  __shared__ int pp[MAX_PAIRS], qq[MAX_PAIRS];
-  const int N = n + (n & 1);
-  const int H = N / 2;
-  for (int64_t idx = threadIdx.x; idx < (int64_t)n * n; idx += blockDim.x)
-    V[idx] = (idx / n == idx % n) ? 1.0 : 0.0;
-  for (int i = threadIdx.x; i < N; i += blockDim.x) pos[i] = i;
-  __syncthreads();
-  for (int sweep = 0; sweep < MAX_SWEEPS && n > 1; ++sweep) {
-    double off = 0.0, tot = 0.0;
-    for (int64_t idx = threadIdx.x; idx < (int64_t)n * n; idx += blockDim.x) {
-      const double a = A[idx];
-      tot += a * a;
-      if (idx / n != idx % n) off += a * a;
-    }
-    off = blk_sum(off);
-    tot = blk_sum(tot);
-    if (!(off > 1e-30 * tot)) break;
-    const double thr = 1e-15 * sqrt(tot);  // couplings at the rounding level of ||A||_F are done
-    __shared__ int any_rot;
-    if (threadIdx.x == 0) any_rot = 0;
-    __syncthreads();
-    for (int round = 0; round < N - 1; ++round) {
-      for (int pr = threadIdx.x; pr < H; pr += blockDim.x) {
-        int p = pos[pr], q = pos[N - 1 - pr];
-        if (p > q) {
-          const int t = p;
-          p = q;
-          q = t;
-        }
-        double c = 1.0, s = 0.0;
-        if (q < n) {
-          const double apq = A[(int64_t)p * n + q];
-          if (fabs(apq) > thr) {
-            any_rot = 1;
-            const double app = A[(int64_t)p * n + p], aqq = A[(int64_t)q * n + q];
-            const double tau = (aqq - app) / (2.0 * apq);
-            const double t = (tau >= 0.0 ? 1.0 : -1.0) / (fabs(tau) + sqrt(1.0 + tau * tau));
-            c = 1.0 / sqrt(1.0 + t * t);
-            s = t * c;
-          }
-        }
-        cs[pr] = c;
-        sn[pr] = s;
-        pp[pr] = p;
-        qq[pr] = q < n ? q : -1;
-      }
-      __syncthreads();
-      // rows: A <- J^T A
-      for (int64_t task = threadIdx.x; task < (int64_t)H * n; task += blockDim.x) {
-        const int pr = (int)(task / n), j = (int)(task % n);
-        const int q = qq[pr];
-        if (q < 0 || sn[pr] == 0.0) continue;
-        const int p = pp[pr];
-        const double c = cs[pr], s = sn[pr];
-        const double a = A[(int64_t)p * n + j], b = A[(int64_t)q * n + j];
-        A[(int64_t)p * n + j] = c * a - s * b;
-        A[(int64_t)q * n + j] = s * a + c * b;
-      }
-      __syncthreads();
-      // columns: A <- A J, V <- V J
-      for (int64_t task = threadIdx.x; task < (int64_t)H * n; task += blockDim.x) {
-        const int pr = (int)(task / n), i = (int)(task % n);
-        const int q = qq[pr];
-        if (q < 0 || sn[pr] == 0.0) continue;
-        const int p = pp[pr];
-        const double c = cs[pr], s = sn[pr];
-        double a = A[(int64_t)i * n + p], b = A[(int64_t)i * n + q];
-        A[(int64_t)i * n + p] = c * a - s * b;
-        A[(int64_t)i * n + q] = s * a + c * b;
-        a = V[(int64_t)i * n + p];
-        b = V[(int64_t)i * n + q];
-        V[(int64_t)i * n + p] = c * a - s * b;
-        V[(int64_t)i * n + q] = s * a + c * b;
-      }
-      __syncthreads();
-      if (threadIdx.x == 0) {
-        const int last = pos[N - 1];
-        for (int i = N - 1; i >= 2; --i) pos[i] = pos[i - 1];
-        pos[1] = last;
-      }
-      __syncthreads();
-    }
-    if (!any_rot) break;  // a sweep without a rotation: converged
-    __syncthreads();
-  }
-  for (int i = threadIdx.x; i < n; i += blockDim.x) evals[i] = A[(int64_t)i * n + i];
-  __syncthreads();
-}
-
-// order[r] = index of the r-th largest eigenvalue (ties by index).
-__device__ void blk_order_desc(const double* ev, int n, int* order) {
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    int r = 0;
-    const double v = ev[i];
-    for (int j = 0; j < n; ++j) r += (ev[j] > v) || (ev[j] == v && j < i);
-    order[r] = i;
-  }
-  __syncthreads();
-}
-
 struct SolveArgs {
   int mode, side, p, k, rank, n_power, basis_dtype;
   int64_t n_other;
@@ -227,60 +106,72 @@ struct SolveArgs {
   int64_t ws_cell;
 };
 
+// Workspace layout of the general solver per cell (doubles):
+//   exact:      A (p x p) | Zt (rank x p) | vec (8 p) | lam (p) | eig scratch
+//   randomised: Q (p x k) | Z (p x k) | S (k x k) | C (k x k) | Zt (k x k) |
+//               vec (8 k) | lam (k) | eig scratch
+// where the eigensolver's scratch is 3 n doubles for each of min(n, SNT)
+// threads (n = p exact, k randomised).
+__host__ __device__ inline int64_t eig_scratch_doubles(int n) { return 3LL * n * (n < SNT ? n : SNT); }
+
 __global__ void __launch_bounds__(SNT) sketch_solve_kernel(SolveArgs a) {
+  __shared__ double red[64];
+  __shared__ int cnt[SNT];
   const int cell = blockIdx.x;
   const int p = a.p, k = a.k, rank = a.rank;
   const double* gram = a.gram + cell * a.gram_stride;
   double* ws = a.ws + cell * a.ws_cell;
-  const int nmax = p > k ? p : k;
-  double* ev = ws;                      // nmax
-  int* order = reinterpret_cast<int*>(ws + nmax);  // nmax ints (<= nmax doubles)
-  double* base = ws + 2 * (int64_t)nmax;
   __shared__ double nrm_s;
 
   if (a.mode == KVC_SVD_EXACT) {
-    double* A = base;                          // p x p
-    double* V = base + (int64_t)p * p;         // p x p
-    for (int64_t i = threadIdx.x; i < (int64_t)p * p; i += blockDim.x) A[i] = gram[i];
-    __syncthreads();
-    blk_jacobi(A, V, p, ev);
-    for (int i = threadIdx.x; i < p; i += blockDim.x) ev[i] = ev[i] > 0.0 ? ev[i] : 0.0;
-    __syncthreads();
-    blk_order_desc(ev, p, order);
+    double* A = ws;                               // p x p
+    double* Zt = A + (int64_t)p * p;              // rank x p
+    double* vec = Zt + (int64_t)rank * p;         // 8 p
+    double* lam = vec + eig::vec_doubles(p);      // p
+    double* scr = lam + p;
+    double part = 0.0;
+    for (int64_t i = threadIdx.x; i < (int64_t)p * p; i += blockDim.x) {
+      const double g = gram[i];
+      A[i] = g;
+      if (i / p == i % p) part += g;
+    }
+    const double total = eig::block_sum(part, red);  // trace = |A|_F^2 (its barriers order the copy)
+    eig::eig_top(A, p, p, rank, lam, Zt, p, vec, cnt, red, scr);
     const int64_t max_rank = a.n_other < p ? a.n_other : p;
     if (threadIdx.x == 0) {
-      double total = 0.0, tail = 0.0;
-      for (int i = 0; i < p; ++i) total += ev[order[i]];
-      for (int i = rank; i < p; ++i) tail += ev[order[i]];
-      a.tail[cell] = (rank >= max_rank || !(total > 0.0)) ? 0.0 : tail / total;
+      double kept = 0.0;
+      for (int i = 0; i < rank; ++i) kept += fmax(lam[i], 0.0);
+      const double t = total > 0.0 ? (total - kept) / total : 0.0;
+      a.tail[cell] = (rank >= max_rank || !(total > 0.0)) ? 0.0 : fmax(t, 0.0);
       if (a.sv2)
-        for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = ev[order[i]];
+        for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = fmax(lam[i], 0.0);
     }
-    __syncthreads();
     if (a.side == KVC_SIDE_LEFT) {
       for (int64_t idx = threadIdx.x; idx < (int64_t)p * rank; idx += blockDim.x) {
         const int i = (int)(idx / rank), r = (int)(idx % rank);
-        store_dt(a.basis, (int64_t)cell * p * rank + idx, (float)V[(int64_t)i * p + order[r]],
-                 a.basis_dtype);
+        store_dt(a.basis, (int64_t)cell * p * rank + idx, (float)Zt[(int64_t)r * p + i], a.basis_dtype);
       }
     } else {
-      const double lmax = ev[order[0]];
+      const double lmax = fmax(lam[0], 0.0);
       double* M = static_cast<double*>(a.basis) + (int64_t)cell * p * rank;
       for (int64_t idx = threadIdx.x; idx < (int64_t)p * rank; idx += blockDim.x) {
         const int i = (int)(idx / rank), r = (int)(idx % rank);
-        const double lam = ev[order[r]];
-        M[idx] = (lam > 1e-14 * lmax && lam > 0.0) ? V[(int64_t)i * p + order[r]] / sqrt(lam) : 0.0;
+        const double l = lam[r];
+        M[idx] = (l > 1e-14 * lmax && l > 0.0) ? Zt[(int64_t)r * p + i] / sqrt(l) : 0.0;
       }
     }
     return;
   }
 
   // randomised
-  double* Q = base;                               // p x k
+  double* Q = ws;                                 // p x k
   double* Z = Q + (int64_t)p * k;                 // p x k
   double* S = Z + (int64_t)p * k;                 // k x k
   double* C = S + (int64_t)k * k;                 // k x k
-  double* V = C + (int64_t)k * k;                 // k x k
+  double* Zt = C + (int64_t)k * k;                // k x k (rank rows used)
+  double* vec = Zt + (int64_t)k * k;              // 8 k
+  double* lam = vec + eig::vec_doubles(k);        // k
+  double* scr = lam + k;
   const double* Mtx = nullptr;
   const double* G = gram;
   if (a.side == KVC_SIDE_LEFT) {
@@ -307,26 +198,21 @@ __global__ void __launch_bounds__(SNT) sketch_solve_kernel(SolveArgs a) {
   blk_gemm(Z, G, false, Q, p, k, p);              // Z = G Q (or H W)
   if (a.side == KVC_SIDE_LEFT) blk_gemm(C, Q, true, Z, k, k, p);   // Q^T G Q
   else blk_gemm(C, Z, true, Z, k, k, p);                           // (H W)^T (H W)
-  blk_jacobi(C, V, k, ev);
-  for (int i = threadIdx.x; i < k; i += blockDim.x) ev[i] = ev[i] > 0.0 ? ev[i] : 0.0;
-  __syncthreads();
-  blk_order_desc(ev, k, order);
+  eig::eig_top(C, k, k, rank, lam, Zt, k, vec, cnt, red, scr);
   if (threadIdx.x == 0) {
     double retained = 0.0;
-    for (int i = 0; i < rank; ++i) retained += ev[order[i]];
+    for (int i = 0; i < rank; ++i) retained += fmax(lam[i], 0.0);
     const double nrm = nrm_s;
     double t = nrm > 0.0 ? 1.0 - retained / nrm : 0.0;
     a.tail[cell] = t > 0.0 ? t : 0.0;
     if (a.sv2)
-      for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = ev[order[i]];
+      for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = fmax(lam[i], 0.0);
   }
-  __syncthreads();
-  // basis = Q V[:, order[:rank]]
+  // basis = Q V[:, :rank] (V's columns are Zt's rows)
   for (int64_t idx = threadIdx.x; idx < (int64_t)p * rank; idx += blockDim.x) {
     const int i = (int)(idx / rank), r = (int)(idx % rank);
-    const int col = order[r];
     double s = 0.0;
-    for (int j = 0; j < k; ++j) s = fma(Q[(int64_t)i * k + j], V[(int64_t)j * k + col], s);
+    for (int j = 0; j < k; ++j) s = fma(Q[(int64_t)i * k + j], Zt[(int64_t)r * k + j], s);
     if (a.side == KVC_SIDE_LEFT) store_dt(a.basis, (int64_t)cell * p * rank + idx, (float)s, a.basis_dtype);
     else static_cast<double*>(a.basis)[(int64_t)cell * p * rank + idx] = s;
   }
@@ -347,9 +233,11 @@ constexpr int SM_K = 32;
 constexpr int SM_QS = SM_K + 2;  // row stride (doubles) of Q and Z: even, so rows start on 16 bytes
 constexpr int SM_NT = 256;
 
+// G | Q | Z | S | C | Zt | vec (8 SM_K) | lam | diag0 (2 SM_K) | red (64) | cnt
 size_t small_smem_bytes(int p) {
-  return sizeof(double) * (((size_t)p * p + 1) / 2 * 2 + 2 * (size_t)p * SM_QS + 3 * SM_K * SM_K + 4 * SM_K + 64) +
-         sizeof(int) * (4 * SM_K + 64);
+  return sizeof(double) * (((size_t)p * p + 1) / 2 * 2 + 2 * (size_t)p * SM_QS + 3 * SM_K * SM_K +
+                           eig::vec_doubles(SM_K) + 3 * SM_K + 64) +
+         sizeof(int) * SM_NT;
 }
 
 // 1/sqrt(x) and 1/x for normal positive / nonzero x: fp32 estimate, then two
@@ -361,16 +249,9 @@ __device__ __forceinline__ double rsqrt_nr(double x) {
   y = y * fma(-0.5 * x, y * y, 1.5);
   return y;
 }
-__device__ __forceinline__ double rcp_nr(double x) {
-  double y = (double)(1.0f / (float)x);
-  y = y * fma(-x, y, 2.0);
-  y = y * fma(-x, y, 2.0);
-  return y;
-}
 // the fp32 estimate needs x inside the fp32 normal range
 __device__ __forceinline__ bool f32_range(double x) { return fabs(x) > 1e-36 && fabs(x) < 1e36; }
 __device__ __forceinline__ double rsqrt_any(double x) { return f32_range(x) ? rsqrt_nr(x) : 1.0 / sqrt(x); }
-__device__ __forceinline__ double rcp_any(double x) { return f32_range(x) ? rcp_nr(x) : 1.0 / x; }
 
 // Z (p x k) = G Q, G symmetric p x p.  Thread: one row, 8 columns.  The
 // eight Q values of a step are read as four 16-byte pairs when Q is 16-byte
@@ -503,159 +384,6 @@ __device__ double* sm_cholqr(double* Y, double* Z, double* S, double* X, double*
   return Z;
 }
 
-// Cyclic two-sided Jacobi on A (n x n, stride SM_K); V gets the eigenvectors
-// in columns, ev the eigenvalues (unsorted).  Round-robin pairs: position 0
-// fixed, positions 1..N-1 rotated by the round index.  One phase per round
-// updates every 2 x 2 block A[{p1,q1}][{p2,q2}] <- J1^T A J2 and the pairs of
-// columns of V.
-__device__ void sm_jacobi(double* A, double* V, int n, double* ev, double* rot, int* pq, double* red) {
-  const int N = n + (n & 1), H = N / 2;
-  for (int idx = threadIdx.x; idx < n * SM_K; idx += blockDim.x) V[idx] = (idx / SM_K == idx % SM_K) ? 1.0 : 0.0;
-  __shared__ int any_rot;
-  for (int sweep = 0; sweep < MAX_SWEEPS && n > 1; ++sweep) {
-    // ||A||_F^2 and the off-diagonal part (one warp)
-    if (threadIdx.x < 32) {
-      double off = 0.0, tot = 0.0;
-      for (int idx = threadIdx.x; idx < n * n; idx += 32) {
-        const double a = A[(idx / n) * SM_K + idx % n];
-        tot += a * a;
-        if (idx / n != idx % n) off += a * a;
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        off += __shfl_xor_sync(0xffffffffu, off, o);
-        tot += __shfl_xor_sync(0xffffffffu, tot, o);
-      }
-      if (threadIdx.x == 0) {
-        red[0] = off;
-        red[1] = tot;
-        any_rot = 0;
-      }
-    }
-    __syncthreads();
-    const double off = red[0], tot = red[1];
-    // converged once the off-diagonal part is below 1e-12 of ||A||_F: the
-    // eigenvalues are then exact to ~1e-24 and the eigenvectors to ~1e-12
-    // over the gap, well past the fp32 / 16-bit outputs (one to two sweeps
-    // fewer than driving it to the fp64 rounding level)
-    if (!(off > 1e-24 * tot)) break;
-    // off-diagonal entries at the rounding level of ||A||_F can never be
-    // removed (a rotation leaves eps ||A|| behind), so they end the sweeps
-    const double thr = 1e-15 * sqrt(tot);
-    for (int round = 0; round < N - 1; ++round) {
-      if (threadIdx.x < H) {
-        const int lane = threadIdx.x;
-        const int i1 = lane, i2 = N - 1 - lane;
-        // positions 1..N-1 rotated by the round: (v mod (N - 1)) for v in
-        // (-(N - 1), N - 1) is one conditional add
-        const int v1 = i1 - 1 - round, v2 = i2 - 1 - round;
-        int pp = i1 == 0 ? 0 : 1 + (v1 < 0 ? v1 + N - 1 : v1);
-        int qq = 1 + (v2 < 0 ? v2 + N - 1 : v2);
-        if (pp > qq) {
-          const int tmp = pp;
-          pp = qq;
-          qq = tmp;
-        }
-        double c = 1.0, sn = 0.0;
-        if (qq < n) {
-          const double apq = A[pp * SM_K + qq];
-          const double app = A[pp * SM_K + pp], aqq = A[qq * SM_K + qq];
-          if (fabs(apq) > thr && apq * apq > 1e-32 * fabs(app * aqq)) {
-            // with h = aqq - app, g = 2 apq, r = sqrt(h^2 + g^2) the rotation
-            // t = sgn(h) g / (|h| + r) has c = 1 / sqrt(1 + t^2), s = t c
-            const double h = aqq - app, g = 2.0 * apq;
-            if (f32_range(g) && (h == 0.0 || f32_range(h))) {
-              // the angle in fp32, (c, s) normalised in fp64: a rotation off
-              // by ~1e-7 of its angle leaves ~1e-7 of apq, which later
-              // rotations remove, while c^2 + s^2 = 1 to fp64 keeps V
-              // orthogonal (fp64 operations are the long-latency ones here)
-              const float hf = (float)h, gf = (float)g;
-              const float tf = __fdividef(hf >= 0.f ? gf : -gf, fabsf(hf) + hypotf(hf, gf));
-              const float cf = rsqrtf(fmaf(tf, tf, 1.f));
-              const double cd = (double)cf, sd = (double)(tf * cf);
-              const double e = fma(cd, cd, fma(sd, sd, -1.0));    // c^2 + s^2 - 1
-              const double f = fma(fma(0.375, e, -0.5), e, 1.0);  // (1 + e)^(-1/2) up to O(e^3)
-              c = cd * f;
-              sn = sd * f;
-            } else {
-              // c = (|h| + r) / sqrt(2 r (r + |h|)), s = sgn(h) g / sqrt(2 r (r + |h|))
-              const double z = fma(h, h, g * g);
-              const double r = z * rsqrt_any(z);
-              const double ah = fabs(h) + r;
-              const double q = rsqrt_any(2.0 * r * ah);
-              c = ah * q;
-              sn = (h >= 0.0 ? g : -g) * q;
-            }
-            any_rot = 1;
-          }
-        }
-        pq[2 * lane] = pp;
-        pq[2 * lane + 1] = qq < n ? qq : -1;
-        rot[2 * lane] = c;
-        rot[2 * lane + 1] = sn;
-      }
-      __syncthreads();
-      // A: 2 x 2 blocks (pair b1 rows, pair b2 columns); V: row i, pair b.
-      // Pairs are indexed in a power-of-two stride hs >= H (shifts, no division).
-      const int hs = H <= 1 ? 1 : 1 << (32 - __clz(H - 1)), sh = __ffs(hs) - 1;
-      const int nb = H * hs;
-      auto task = [&](int t) {
-        if (t < nb) {
-          const int b1 = t >> sh, b2 = t & (hs - 1);
-          if (b2 >= H) return;
-          const int p1 = pq[2 * b1], q1 = pq[2 * b1 + 1], p2 = pq[2 * b2], q2 = pq[2 * b2 + 1];
-          const double c1 = rot[2 * b1], s1 = q1 < 0 ? 0.0 : rot[2 * b1 + 1];
-          const double c2 = rot[2 * b2], s2 = q2 < 0 ? 0.0 : rot[2 * b2 + 1];
-          if (s1 == 0.0 && s2 == 0.0) return;
-          // rows {p1, q1} x columns {p2, q2}; a missing q is a dummy index
-          const double a = A[p1 * SM_K + p2];
-          const double b = q2 >= 0 ? A[p1 * SM_K + q2] : 0.0;
-          const double cq = q1 >= 0 ? A[q1 * SM_K + p2] : 0.0;
-          const double dq = (q1 >= 0 && q2 >= 0) ? A[q1 * SM_K + q2] : 0.0;
-          // rows: [a b; cq dq] <- J1^T [...] with (row p) c a - s cq, (row q) s a + c cq
-          const double r0 = c1 * a - s1 * cq, r1 = c1 * b - s1 * dq;
-          const double r2 = s1 * a + c1 * cq, r3 = s1 * b + c1 * dq;
-          // columns: (col p) c x - s y, (col q) s x + c y
-          A[p1 * SM_K + p2] = c2 * r0 - s2 * r1;
-          if (q2 >= 0) A[p1 * SM_K + q2] = s2 * r0 + c2 * r1;
-          if (q1 >= 0) {
-            A[q1 * SM_K + p2] = c2 * r2 - s2 * r3;
-            if (q2 >= 0) A[q1 * SM_K + q2] = s2 * r2 + c2 * r3;
-          }
-        } else {
-          const int u = t - nb, i = u >> sh, b = u & (hs - 1);
-          if (b >= H) return;
-          const int p_ = pq[2 * b], q = pq[2 * b + 1];
-          if (q < 0) return;
-          const double cc = rot[2 * b], ss = rot[2 * b + 1];
-          if (ss == 0.0) return;
-          const double x = V[i * SM_K + p_], y = V[i * SM_K + q];
-          V[i * SM_K + p_] = cc * x - ss * y;
-          V[i * SM_K + q] = ss * x + cc * y;
-        }
-      };
-      // the A blocks and the rows of V go to different warps where the block
-      // has room (no warp runs both kinds of task one after the other)
-      const int vb = (nb + 31) & ~31;
-      if (vb + 32 <= (int)blockDim.x) {
-        if ((int)threadIdx.x < vb) {
-          for (int t = threadIdx.x; t < nb; t += vb) task(t);
-        } else {
-          for (int u = threadIdx.x - vb; u < n * hs; u += blockDim.x - vb) task(nb + u);
-        }
-      } else {
-        for (int t = threadIdx.x; t < nb + n * hs; t += blockDim.x) task(t);
-      }
-      __syncthreads();
-    }
-    const int rotated = any_rot;
-    __syncthreads();  // every thread has read the flag before the next sweep resets it
-    if (!rotated) break;  // a sweep without a rotation: converged
-  }
-  for (int i = threadIdx.x; i < n; i += blockDim.x) ev[i] = A[i * SM_K + i];
-  __syncthreads();
-}
-
 __global__ void __launch_bounds__(SM_NT) sketch_solve_small_kernel(SolveArgs a) {
   extern __shared__ __align__(16) double sm[];
   const int cell = blockIdx.x;
@@ -666,14 +394,13 @@ __global__ void __launch_bounds__(SM_NT) sketch_solve_small_kernel(SolveArgs a) 
   double* Z = Q + p * SM_QS;            // p x SM_QS
   double* S = Z + p * SM_QS;            // SM_K x SM_K
   double* C = S + SM_K * SM_K;
-  double* V = C + SM_K * SM_K;
+  double* Zt = C + SM_K * SM_K;         // Ritz vectors as rows (rank x SM_K)
   double* X = C;                        // R^{-1} of the CholeskyQR passes (C is set after them)
-  double* ev = V + SM_K * SM_K;         // SM_K
-  double* rot = ev + SM_K;              // 2 SM_K
-  double* diag0 = rot + 2 * SM_K;       // SM_K
-  double* red = diag0 + SM_K;           // 64 (reduction scratch)
-  int* order = reinterpret_cast<int*>(red + 64);
-  int* pq = order + SM_K;               // 2 SM_K
+  double* vec = Zt + SM_K * SM_K;       // eigensolver vectors
+  double* lam = vec + eig::vec_doubles(SM_K);  // SM_K
+  double* diag0 = lam + SM_K;           // 2 SM_K
+  double* red = diag0 + 2 * SM_K;       // 64 (reduction scratch)
+  int* cnt = reinterpret_cast<int*>(red + 64);  // SM_NT
   __shared__ double nrm_s;
   {
     // sixteen loads in flight per thread before their stores (the Gram is
@@ -731,40 +458,99 @@ __global__ void __launch_bounds__(SM_NT) sketch_solve_small_kernel(SolveArgs a) 
   sm_gemm(Z, G, Q, p, k);  // Z = G Q (or H W)
   if (a.side == KVC_SIDE_LEFT) sm_colgram(C, Q, Z, p, k);  // Q^T G Q
   else sm_colgram(C, Z, Z, p, k);                         // (H W)^T (H W)
-  sm_jacobi(C, V, k, ev, rot, pq, red);
-  for (int i = threadIdx.x; i < k; i += blockDim.x) ev[i] = ev[i] > 0.0 ? ev[i] : 0.0;
-  __syncthreads();
-  for (int i = threadIdx.x; i < k; i += blockDim.x) {
-    int r = 0;
-    const double v = ev[i];
-    for (int j = 0; j < k; ++j) r += (ev[j] > v) || (ev[j] == v && j < i);
-    order[r] = i;
-  }
-  __syncthreads();
+  // the rank leading Ritz pairs (eigenpairs of C); the eigensolver's
+  // per-thread scratch is in the workspace
+  eig::eig_top(C, SM_K, k, rank, lam, Zt, SM_K, vec, cnt, red, a.ws + cell * a.ws_cell);
   if (threadIdx.x == 0) {
     double retained = 0.0;
-    for (int i = 0; i < rank; ++i) retained += ev[order[i]];
+    for (int i = 0; i < rank; ++i) retained += fmax(lam[i], 0.0);
     const double nrm = nrm_s;
     const double t = nrm > 0.0 ? 1.0 - retained / nrm : 0.0;
     a.tail[cell] = t > 0.0 ? t : 0.0;
     if (a.sv2)
-      for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = ev[order[i]];
+      for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = fmax(lam[i], 0.0);
   }
-  // basis = Q V[:, order[:rank]]
+  // basis = Q V[:, :rank] (V's columns are Zt's rows)
   for (int idx = threadIdx.x; idx < p * rank; idx += blockDim.x) {
     const int i = idx / rank, r = idx % rank;
-    const int col = order[r];
     double s = 0.0;
-    for (int j = 0; j < k; ++j) s = fma(Q[i * SM_QS + j], V[j * SM_K + col], s);
+    for (int j = 0; j < k; ++j) s = fma(Q[i * SM_QS + j], Zt[r * SM_K + j], s);
     if (a.side == KVC_SIDE_LEFT) store_dt(a.basis, (int64_t)cell * p * rank + idx, (float)s, a.basis_dtype);
     else static_cast<double*>(a.basis)[(int64_t)cell * p * rank + idx] = s;
   }
 }
 
+// ---------------------------------------------------------------------------
+// Exact mode for p <= 128 (SVD.exact through the Gram, svd.py:181-219): the
+// Gram in shared memory, its rank leading eigenpairs by eig::eig_top; the
+// eigenvectors and the eigensolver's per-thread scratch in the workspace.
+// ---------------------------------------------------------------------------
+constexpr int EX_P = 128;
+
+size_t exact_small_smem_bytes(int p) {
+  return sizeof(double) * ((size_t)p * p + eig::vec_doubles(p) + p + 64) + sizeof(int) * SM_NT;
+}
+
+__global__ void __launch_bounds__(SM_NT) exact_solve_small_kernel(SolveArgs a) {
+  extern __shared__ __align__(16) double sm[];
+  const int cell = blockIdx.x;
+  const int p = a.p, rank = a.rank;
+  const double* gram = a.gram + cell * a.gram_stride;
+  double* G = sm;                              // p x p
+  double* vec = G + p * p;                     // eigensolver vectors
+  double* lam = vec + eig::vec_doubles(p);     // p
+  double* red = lam + p;                       // 64
+  int* cnt = reinterpret_cast<int*>(red + 64); // SM_NT
+  double* Zt = a.ws + cell * a.ws_cell;        // rank x p
+  double* scr = Zt + (int64_t)rank * p;
+  {
+    constexpr int U = 16;  // loads in flight per thread before their stores
+    const int nt = blockDim.x, pp = p * p;
+    int i = threadIdx.x;
+    for (; i + (U - 1) * nt < pp; i += U * nt) {
+      double v[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) v[u] = __ldcg(gram + i + u * nt);
+#pragma unroll
+      for (int u = 0; u < U; ++u) G[i + u * nt] = v[u];
+    }
+    for (; i < pp; i += nt) G[i] = __ldcg(gram + i);
+  }
+  __syncthreads();
+  double part = 0.0;
+  for (int i = threadIdx.x; i < p; i += blockDim.x) part += G[i * (p + 1)];
+  const double total = eig::block_sum(part, red);  // trace = |A|_F^2
+  eig::eig_top(G, p, p, rank, lam, Zt, p, vec, cnt, red, scr);
+  const int64_t max_rank = a.n_other < p ? a.n_other : p;
+  if (threadIdx.x == 0) {
+    double kept = 0.0;
+    for (int i = 0; i < rank; ++i) kept += fmax(lam[i], 0.0);
+    const double t = total > 0.0 ? (total - kept) / total : 0.0;
+    a.tail[cell] = (rank >= max_rank || !(total > 0.0)) ? 0.0 : fmax(t, 0.0);
+    if (a.sv2)
+      for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = fmax(lam[i], 0.0);
+  }
+  if (a.side == KVC_SIDE_LEFT) {
+    for (int idx = threadIdx.x; idx < p * rank; idx += blockDim.x) {
+      const int i = idx / rank, r = idx % rank;
+      store_dt(a.basis, (int64_t)cell * p * rank + idx, (float)Zt[(int64_t)r * p + i], a.basis_dtype);
+    }
+  } else {
+    const double lmax = fmax(lam[0], 0.0);
+    double* M = static_cast<double*>(a.basis) + (int64_t)cell * p * rank;
+    for (int idx = threadIdx.x; idx < p * rank; idx += blockDim.x) {
+      const int i = idx / rank, r = idx % rank;
+      const double l = lam[r];
+      M[idx] = (l > 1e-14 * lmax && l > 0.0) ? Zt[(int64_t)r * p + i] / sqrt(l) : 0.0;
+    }
+  }
+}
+
+// Workspace doubles per cell: the general solver's layout (above), which
+// also covers the shared-memory kernels' eigenvectors and scratch.
 int64_t ws_per_cell(int mode, int p, int k) {
-  const int64_t nmax = std::max(p, k);
-  if (mode == KVC_SVD_EXACT) return 2 * nmax + 2LL * p * p;
-  return 2 * nmax + 2LL * p * k + 3LL * k * k;
+  if (mode == KVC_SVD_EXACT) return 2LL * p * p + eig::vec_doubles(p) + p + eig_scratch_doubles(p);
+  return 2LL * p * k + 3LL * k * k + eig::vec_doubles(k) + k + eig_scratch_doubles(k);
 }
 
 }  // namespace
@@ -787,9 +573,9 @@ extern "C" int kvc_sketch_solve(int n_cells, int mode, int side, int p, int64_t 
     return fail(KVC_ERR_ARG, "kvc_sketch_solve: bad mode");
   if (side != KVC_SIDE_LEFT && side != KVC_SIDE_RIGHT)
     return fail(KVC_ERR_ARG, "kvc_sketch_solve: bad side");
-  if (p <= 0 || p > 2 * MAX_PAIRS - 2 || rank <= 0 || rank > p || n_other <= 0)
+  if (p <= 0 || p > MAX_DIM || rank <= 0 || rank > p || n_other <= 0)
     return fail(KVC_ERR_SHAPE, "kvc_sketch_solve: bad p/rank");
-  if (mode == KVC_SVD_RANDOMISED && (k < rank || k > p || k > 2 * MAX_PAIRS - 2))
+  if (mode == KVC_SVD_RANDOMISED && (k < rank || k > p || k > MAX_DIM))
     return fail(KVC_ERR_SHAPE, "kvc_sketch_solve: sketch width must satisfy rank <= k <= p");
   if (mode == KVC_SVD_RANDOMISED && (n_power < 0 || n_power > 16))
     return fail(KVC_ERR_ARG, "kvc_sketch_solve: n_power out of range");
@@ -828,6 +614,14 @@ extern "C" int kvc_sketch_solve(int n_cells, int mode, int side, int p, int64_t 
     if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     sketch_solve_small_kernel<<<n_cells, SM_NT, smem, static_cast<cudaStream_t>(stream)>>>(a);
     return check_launch("sketch_solve_small_kernel");
+  }
+  if (mode == KVC_SVD_EXACT && p <= EX_P) {
+    const size_t smem = exact_small_smem_bytes(p);
+    cudaError_t e = cudaFuncSetAttribute(exact_solve_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+    if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    exact_solve_small_kernel<<<n_cells, SM_NT, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    return check_launch("exact_solve_small_kernel");
   }
   sketch_solve_kernel<<<n_cells, SNT, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return check_launch("sketch_solve_kernel");
