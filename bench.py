@@ -43,6 +43,7 @@ if ROOT not in sys.path:
 METRIC = "compress tokens/s + decompress GB/s (Llama-3-8B KV shape) at 1/2/4/8 B200, %roofline"
 DEFAULT_WORKLOAD = "llama3-8b-kv-b8-t32768-bf16"
 SINGLE_GPU_WORKLOAD = "llama3-8b-kv-b1-t8192-bf16"
+STREAM_WORKLOAD = "qwen2-7b-kv-b4-t131072-bf16"
 BREAKDOWN_STEPS = 3  # traced steps for the per-stage times, before the timed region
 FALLBACK_HBM_GBS = 6650.0
 REFERENCE_DIR = os.path.join(ROOT, "baseline", "_ref")
@@ -64,6 +65,8 @@ def parse_args():
     ap.add_argument("--e2e-host-layers", type=int, default=8,
                     help="distinct layers held in pinned host memory for the e2e line (reused cyclically)")
     ap.add_argument("--stream-block", type=int, default=256, help="tokens per block of the decode-stream line (0: no such line)")
+    ap.add_argument("--stream-workload", default=STREAM_WORKLOAD,
+                    help="the decode-stream config measured at N = 1, with the int4 / fp8 baselines ('' to skip)")
     ap.add_argument("--layers", type=int, default=0,
                     help="override the workload's layer count (profiling a smaller case)")
     return ap.parse_args()
@@ -512,6 +515,10 @@ def run_ours(args, w):
         torch.cuda.empty_cache()
         line["single_gpu_config"] = single_gpu(WORKLOADS[args.single_gpu_workload], args, dev, peak,
                                                cpu=not args.no_cpu_baseline)
+    if world == 1 and args.stream_workload and args.stream_block > 0:
+        pairs = None
+        torch.cuda.empty_cache()
+        line["decode_stream_config"] = stream_config(WORKLOADS[args.stream_workload], dev, peak, args.stream_block)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         # a bounded sample: one sequence's slice of a layer when the layer is large
         cb = reference_cpu(w, steps=1, batch=1 if w.batch > 1 else None)
@@ -561,6 +568,71 @@ def single_gpu(w, args, dev, peak, cpu: bool):
         if cb is not None:
             out["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         out["cpu_port"] = port_cpu(w, steps=1)
+    return out
+
+
+def _timed(fn, reps: int = 3):
+    """Device time (ms) of fn() on the current stream: one untimed call, then
+    the mean of ``reps``."""
+    out = fn()
+    torch.cuda.synchronize()
+    del out
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        out = fn()
+        del out
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def stream_config(w, dev, peak, block: int):
+    """The decode-time config: the cache compressed once with FlashJoLT, then
+    reconstructed in ``block``-token blocks through DecodeStream (eager and as
+    one CUDA graph), next to a whole-cache decode and the int4 per-channel and
+    fp8 quantise-only baselines (quantization_only.py:125-198, identity.py:
+    68-89) compressing and decoding the same tensors."""
+    from kvcompress_b200 import build_compressor
+    from kvcompress_b200.synthetic import make_kv_layer
+
+    m, t, d = w.cell_shape
+    comp = build_compressor(w.method, compression_ratio=w.compression_ratio, bits=w.bits)
+    pairs = []
+    for li in range(w.layers):
+        k, v = make_kv_layer(w, li, device=dev)
+        pairs.append((k.reshape(m, t, d), v.reshape(m, t, d)))
+    in_bytes = sum(x.numel() * x.element_size() for pair in pairs for x in pair)
+    comp_ms = _timed(lambda: comp.compress_many(pairs), reps=2)
+    payloads = comp.compress_many(pairs)
+    pay_bytes = sum(p.bytes_compressed for pair in payloads for p in pair)
+    out = {"workload": w.name, "config": workload_config(w, 1, [payloads[0][0].metadata[k]
+                                                               for k in ("r_token", "r_feature", "bits")]),
+           "cache_bytes": in_bytes, "compress_ms": comp_ms,
+           "compress_tokens_per_s": w.batch * w.tokens / (comp_ms / 1000.0)}
+    out["stream"] = decode_stream(payloads, 1, dev, block=block, passes=2)
+    out["stream"]["graph"]["frac_of_hbm"] = out["stream"]["graph"]["value"] / peak
+    dec_ms = _timed(lambda: comp.decompress_many(payloads), reps=2)
+    out["full_decode"] = {"ms": dec_ms, "value": (pay_bytes + in_bytes) / (dec_ms / 1000.0) / 1e9, "unit": "GB/s",
+                          "frac_of_hbm": (pay_bytes + in_bytes) / (dec_ms / 1000.0) / 1e9 / peak}
+    del payloads
+    base = {}
+    for name in ("int4", "fp8"):
+        bc = build_compressor(name)
+        c_ms = _timed(lambda: [bc.compress(k_, v_) for k_, v_ in pairs], reps=2)
+        pays = [bc.compress(k_, v_) for k_, v_ in pairs]
+        pb = sum(p.bytes_compressed for pair in pays for p in pair)
+        d_ms = _timed(lambda: [bc.decompress(kp, vp) for kp, vp in pays], reps=2)
+        base[name] = {"compress_ms": c_ms, "compress_gbs": (in_bytes + pb) / (c_ms / 1000.0) / 1e9,
+                      "decompress_ms": d_ms, "decompress_gbs": (in_bytes + pb) / (d_ms / 1000.0) / 1e9,
+                      "decompress_frac_of_hbm": (in_bytes + pb) / (d_ms / 1000.0) / 1e9 / peak,
+                      "ratio_vs_16bit": in_bytes / pb,
+                      "per_block_us": 1000.0 * d_ms / ((t + block - 1) // block)}
+        del pays
+    out["baselines"] = base
+    out["what"] = ("FlashJoLT payloads decoded block by block (DecodeStream; graph = one CUDA graph over every block) "
+                   "and whole; int4 per-channel / fp8 baselines compress and decode every layer's K and V "
+                   "(per_block_us: their whole decode divided by the blocks of the stream)")
     return out
 
 

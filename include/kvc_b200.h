@@ -99,7 +99,9 @@ int kvc_gram(int n_cells, const void* const* a, int64_t rows, int p, int dtype,
  * reports it (svd.py:98-110 exact, svd.py:289-294 randomised).
  * n_other: the long dimension of A (n), so that min(p, n_other) is the
  * SVD's max_rank; n_power: power iterations (SVD.n_power, svd.py:131-142).
- * Supports p, k <= 2046.
+ * Supports p <= 2046 and sketch widths k <= 1024 (q <= 512 gives k <= 513).
+ * Only the `rank` leading eigenpairs are computed (Householder
+ * tridiagonalisation, bisection, inverse iteration: the dsyevx method).
  */
 size_t kvc_sketch_solve_workspace_bytes(int n_cells, int mode, int p, int k);
 int kvc_sketch_solve(int n_cells, int mode, int side, int p, int64_t n_other, int k, int rank,

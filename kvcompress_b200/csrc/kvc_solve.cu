@@ -31,67 +31,8 @@ namespace kvc {
 namespace {
 
 constexpr int SNT = 512;
-constexpr int MAX_DIM = 2046;  // largest p and k of the general solver
-
-// C (M x N) = op(A) * B.  A is M x K row-major, or K x M when transA.
-__device__ void blk_gemm(double* __restrict__ C, const double* __restrict__ A, bool transA,
-                         const double* __restrict__ B, int M, int N, int K) {
-  for (int idx = threadIdx.x; idx < M * N; idx += blockDim.x) {
-    const int i = idx / N, j = idx % N;
-    double s = 0.0;
-    if (!transA)
-      for (int k = 0; k < K; ++k) s = fma(A[(int64_t)i * K + k], B[(int64_t)k * N + j], s);
-    else
-      for (int k = 0; k < K; ++k) s = fma(A[(int64_t)k * M + i], B[(int64_t)k * N + j], s);
-    C[idx] = s;
-  }
-  __syncthreads();
-}
-
-// One CholeskyQR pass: Y (p x k) <- Y R^{-1} with R^T R = Y^T Mtx Y
-// (Mtx = identity when NULL).  Z: p x k scratch, S: k x k scratch.
-__device__ void blk_cholqr(double* Y, int p, int k, const double* Mtx, double* Z, double* S) {
-  const double* MY = Y;
-  if (Mtx) {
-    blk_gemm(Z, Mtx, false, Y, p, k, p);
-    MY = Z;
-  }
-  blk_gemm(S, Y, true, MY, k, k, p);
-  __shared__ double rjj_s;
-  for (int j = 0; j < k; ++j) {
-    if (threadIdx.x == 0) {
-      const double orig = S[(int64_t)j * k + j];
-      double d = orig;
-      for (int i = 0; i < j; ++i) d -= S[(int64_t)i * k + j] * S[(int64_t)i * k + j];
-      const double r = (orig > 0.0 && d > 1e-10 * orig) ? sqrt(d) : 0.0;
-      S[(int64_t)j * k + j] = r;
-      rjj_s = r;
-    }
-    __syncthreads();
-    const double rjj = rjj_s;
-    for (int l = j + 1 + threadIdx.x; l < k; l += blockDim.x) {
-      double v = S[(int64_t)j * k + l];
-      for (int i = 0; i < j; ++i) v -= S[(int64_t)i * k + j] * S[(int64_t)i * k + l];
-      S[(int64_t)j * k + l] = rjj > 0.0 ? v / rjj : 0.0;
-    }
-    __syncthreads();
-  }
-  for (int r = threadIdx.x; r < p; r += blockDim.x) {
-    double* y = Y + (int64_t)r * k;
-    for (int j = 0; j < k; ++j) {
-      double v = y[j];
-      for (int i = 0; i < j; ++i) v -= y[i] * S[(int64_t)i * k + j];
-      const double rjj = S[(int64_t)j * k + j];
-      y[j] = rjj > 0.0 ? v / rjj : 0.0;
-    }
-  }
-  __syncthreads();
-}
-
-__device__ void blk_orth2(double* Y, int p, int k, const double* Mtx, double* Z, double* S) {
-  blk_cholqr(Y, p, k, Mtx, Z, S);
-  blk_cholqr(Y, p, k, Mtx, Z, S);
-}
+constexpr int MAX_DIM = 2046;     // largest p of the solver
+constexpr int MAX_SKETCH = 1024;  // largest sketch width k (the row blocks of W R^{-1} live in shared memory)
 
 struct SolveArgs {
   int mode, side, p, k, rank, n_power, basis_dtype;
@@ -106,127 +47,71 @@ struct SolveArgs {
   int64_t ws_cell;
 };
 
-// Workspace layout of the general solver per cell (doubles):
-//   exact:      A (p x p) | Zt (rank x p) | vec (8 p) | lam (p) | eig scratch
-//   randomised: Q (p x k) | Z (p x k) | S (k x k) | C (k x k) | Zt (k x k) |
-//               vec (8 k) | lam (k) | eig scratch
+// Workspace layout per cell (doubles):
+//   exact (exact_solve_kernel, p > 128):
+//               A (p x p) | Zt (rank x p) | vec (8 p) | lam (p) | eig scratch
+//   randomised (the multi-launch path below, p > 128 or k > 32):
+//               W (p x k) | Z (p x k) | S (k x k) | C (k x k) | Zt (k x k) |
+//               vec (8 k) | lam (k) | misc (2) | eig scratch
 // where the eigensolver's scratch is 3 n doubles for each of min(n, SNT)
 // threads (n = p exact, k randomised).
 __host__ __device__ inline int64_t eig_scratch_doubles(int n) { return 3LL * n * (n < SNT ? n : SNT); }
 
-__global__ void __launch_bounds__(SNT) sketch_solve_kernel(SolveArgs a) {
+// Exact mode for p > 128: the Gram copied to the workspace and its rank
+// leading eigenpairs found there (served from L2).
+__global__ void __launch_bounds__(SNT) exact_solve_kernel(SolveArgs a) {
   __shared__ double red[64];
   __shared__ int cnt[SNT];
   const int cell = blockIdx.x;
-  const int p = a.p, k = a.k, rank = a.rank;
+  const int p = a.p, rank = a.rank;
   const double* gram = a.gram + cell * a.gram_stride;
   double* ws = a.ws + cell * a.ws_cell;
-  __shared__ double nrm_s;
-
-  if (a.mode == KVC_SVD_EXACT) {
-    double* A = ws;                               // p x p
-    double* Zt = A + (int64_t)p * p;              // rank x p
-    double* vec = Zt + (int64_t)rank * p;         // 8 p
-    double* lam = vec + eig::vec_doubles(p);      // p
-    double* scr = lam + p;
-    double part = 0.0;
-    for (int64_t i = threadIdx.x; i < (int64_t)p * p; i += blockDim.x) {
-      const double g = gram[i];
-      A[i] = g;
-      if (i / p == i % p) part += g;
-    }
-    const double total = eig::block_sum(part, red);  // trace = |A|_F^2 (its barriers order the copy)
-    eig::eig_top(A, p, p, rank, lam, Zt, p, vec, cnt, red, scr);
-    const int64_t max_rank = a.n_other < p ? a.n_other : p;
-    if (threadIdx.x == 0) {
-      double kept = 0.0;
-      for (int i = 0; i < rank; ++i) kept += fmax(lam[i], 0.0);
-      const double t = total > 0.0 ? (total - kept) / total : 0.0;
-      a.tail[cell] = (rank >= max_rank || !(total > 0.0)) ? 0.0 : fmax(t, 0.0);
-      if (a.sv2)
-        for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = fmax(lam[i], 0.0);
-    }
-    if (a.side == KVC_SIDE_LEFT) {
-      for (int64_t idx = threadIdx.x; idx < (int64_t)p * rank; idx += blockDim.x) {
-        const int i = (int)(idx / rank), r = (int)(idx % rank);
-        store_dt(a.basis, (int64_t)cell * p * rank + idx, (float)Zt[(int64_t)r * p + i], a.basis_dtype);
-      }
-    } else {
-      const double lmax = fmax(lam[0], 0.0);
-      double* M = static_cast<double*>(a.basis) + (int64_t)cell * p * rank;
-      for (int64_t idx = threadIdx.x; idx < (int64_t)p * rank; idx += blockDim.x) {
-        const int i = (int)(idx / rank), r = (int)(idx % rank);
-        const double l = lam[r];
-        M[idx] = (l > 1e-14 * lmax && l > 0.0) ? Zt[(int64_t)r * p + i] / sqrt(l) : 0.0;
-      }
-    }
-    return;
+  double* A = ws;                               // p x p
+  double* Zt = A + (int64_t)p * p;              // rank x p
+  double* vec = Zt + (int64_t)rank * p;         // 8 p
+  double* lam = vec + eig::vec_doubles(p);      // p
+  double* scr = lam + p;
+  double part = 0.0;
+  for (int64_t i = threadIdx.x; i < (int64_t)p * p; i += blockDim.x) {
+    const double g = gram[i];
+    A[i] = g;
+    if (i / p == i % p) part += g;
   }
-
-  // randomised
-  double* Q = ws;                                 // p x k
-  double* Z = Q + (int64_t)p * k;                 // p x k
-  double* S = Z + (int64_t)p * k;                 // k x k
-  double* C = S + (int64_t)k * k;                 // k x k
-  double* Zt = C + (int64_t)k * k;                // k x k (rank rows used)
-  double* vec = Zt + (int64_t)k * k;              // 8 k
-  double* lam = vec + eig::vec_doubles(k);        // k
-  double* scr = lam + k;
-  const double* Mtx = nullptr;
-  const double* G = gram;
-  if (a.side == KVC_SIDE_LEFT) {
-    const double* y0 = gram + (int64_t)p * p;
-    for (int64_t i = threadIdx.x; i < (int64_t)p * k; i += blockDim.x) Q[i] = y0[i];
-    if (threadIdx.x == 0) nrm_s = gram[(int64_t)p * p + (int64_t)p * k];
-  } else {
-    Mtx = gram;
-    for (int64_t i = threadIdx.x; i < (int64_t)p * k; i += blockDim.x) Q[i] = (double)a.omega[i];
-    if (threadIdx.x == 0) {
-      double t = 0.0;
-      for (int i = 0; i < p; ++i) t += gram[(int64_t)i * p + i];
-      nrm_s = t;
-    }
-  }
-  __syncthreads();
-  blk_orth2(Q, p, k, Mtx, Z, S);
-  for (int it = 0; it < a.n_power; ++it) {
-    blk_gemm(Z, G, false, Q, p, k, p);
-    for (int64_t i = threadIdx.x; i < (int64_t)p * k; i += blockDim.x) Q[i] = Z[i];
-    __syncthreads();
-    blk_orth2(Q, p, k, Mtx, Z, S);
-  }
-  blk_gemm(Z, G, false, Q, p, k, p);              // Z = G Q (or H W)
-  if (a.side == KVC_SIDE_LEFT) blk_gemm(C, Q, true, Z, k, k, p);   // Q^T G Q
-  else blk_gemm(C, Z, true, Z, k, k, p);                           // (H W)^T (H W)
-  eig::eig_top(C, k, k, rank, lam, Zt, k, vec, cnt, red, scr);
+  const double total = eig::block_sum(part, red);  // trace = |A|_F^2 (its barriers order the copy)
+  eig::eig_top(A, p, p, rank, lam, Zt, p, vec, cnt, red, scr);
+  const int64_t max_rank = a.n_other < p ? a.n_other : p;
   if (threadIdx.x == 0) {
-    double retained = 0.0;
-    for (int i = 0; i < rank; ++i) retained += fmax(lam[i], 0.0);
-    const double nrm = nrm_s;
-    double t = nrm > 0.0 ? 1.0 - retained / nrm : 0.0;
-    a.tail[cell] = t > 0.0 ? t : 0.0;
+    double kept = 0.0;
+    for (int i = 0; i < rank; ++i) kept += fmax(lam[i], 0.0);
+    const double t = total > 0.0 ? (total - kept) / total : 0.0;
+    a.tail[cell] = (rank >= max_rank || !(total > 0.0)) ? 0.0 : fmax(t, 0.0);
     if (a.sv2)
       for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = fmax(lam[i], 0.0);
   }
-  // basis = Q V[:, :rank] (V's columns are Zt's rows)
-  for (int64_t idx = threadIdx.x; idx < (int64_t)p * rank; idx += blockDim.x) {
-    const int i = (int)(idx / rank), r = (int)(idx % rank);
-    double s = 0.0;
-    for (int j = 0; j < k; ++j) s = fma(Q[(int64_t)i * k + j], Zt[(int64_t)r * k + j], s);
-    if (a.side == KVC_SIDE_LEFT) store_dt(a.basis, (int64_t)cell * p * rank + idx, (float)s, a.basis_dtype);
-    else static_cast<double*>(a.basis)[(int64_t)cell * p * rank + idx] = s;
+  if (a.side == KVC_SIDE_LEFT) {
+    for (int64_t idx = threadIdx.x; idx < (int64_t)p * rank; idx += blockDim.x) {
+      const int i = (int)(idx / rank), r = (int)(idx % rank);
+      store_dt(a.basis, (int64_t)cell * p * rank + idx, (float)Zt[(int64_t)r * p + i], a.basis_dtype);
+    }
+  } else {
+    const double lmax = fmax(lam[0], 0.0);
+    double* M = static_cast<double*>(a.basis) + (int64_t)cell * p * rank;
+    for (int64_t idx = threadIdx.x; idx < (int64_t)p * rank; idx += blockDim.x) {
+      const int i = (int)(idx / rank), r = (int)(idx % rank);
+      const double l = lam[r];
+      M[idx] = (l > 1e-14 * lmax && l > 0.0) ? Zt[(int64_t)r * p + i] / sqrt(l) : 0.0;
+    }
   }
 }
 
 // ---------------------------------------------------------------------------
 // Shared-memory solver for the common randomised case (p <= 128, k <= 32).
-// Same algorithm and outputs as sketch_solve_kernel above, laid out for
-// latency: every operand lives in shared memory and every step is a short
-// block-wide phase (the Cholesky's trailing updates, the inverse of R by
-// parallel back-substitution, Q = Y R^{-1} as a product, one phase of 2 x 2
-// block updates per Jacobi round), so no single warp runs a long chain of
-// dependent fp64 operations.  Square roots and reciprocals take an fp32
-// hardware estimate refined by two Newton-Raphson steps in fp64.
+// Same algorithm and outputs as the multi-launch path for larger problems,
+// laid out for latency: every operand lives in shared memory and every step
+// is a short block-wide phase (the Cholesky's trailing updates, the inverse of
+// R by parallel back-substitution, Q = Y R^{-1} as a product), so no single
+// warp runs a long chain of dependent fp64 operations.  Square roots take an
+// fp32 hardware estimate refined by two Newton-Raphson steps in fp64.
 // ---------------------------------------------------------------------------
 constexpr int SM_P = 128;
 constexpr int SM_K = 32;
@@ -546,11 +431,377 @@ __global__ void __launch_bounds__(SM_NT) exact_solve_small_kernel(SolveArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Randomised problems beyond the shared-memory solver (p > 128 or k > 32; the
+// q-capped token sketch of FlashJoLT is 513 wide over p = m * rd up to 1024).
+// The algorithm of sketch_solve_small_kernel as a sequence of batched
+// launches: the products (G W, W^T Z, ...) are fp64 GEMMs over many CTAs; the
+// Cholesky of each CholeskyQR pass is one CTA per cell (blocked, the panel
+// rows in shared memory); W R^{-1} is a triangular solve over blocks of rows;
+// the Ritz pairs come from eig::eig_top on the k x k Ritz matrix.
+// ---------------------------------------------------------------------------
+struct Gemm {
+  const double* A;
+  const double* B;
+  double* C;
+  int M, N, K, lda, ldb, ldc, tA, tB;
+  int64_t sA, sB, sC;  // per-cell strides (doubles)
+};
+
+constexpr int GT = 64;    // output tile GT x GT
+constexpr int GKD = 16;   // depth per stage
+constexpr int GNT = 256;  // 16 x 16 threads, 4 x 4 outputs each (strided by 16: conflict-free reads)
+
+// C = op(A) op(B) per cell (row-major; op = transpose when tA / tB).
+__global__ void __launch_bounds__(GNT) f64_gemm_kernel(Gemm g) {
+  __shared__ double As[GKD][GT + 1];
+  __shared__ double Bs[GKD][GT + 1];
+  const int cell = blockIdx.z;
+  const double* A = g.A + cell * g.sA;
+  const double* B = g.B + cell * g.sB;
+  double* C = g.C + cell * g.sC;
+  const int i0 = blockIdx.y * GT, j0 = blockIdx.x * GT;
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  double acc[4][4];
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) acc[r][c] = 0.0;
+  for (int l0 = 0; l0 < g.K; l0 += GKD) {
+    for (int e = threadIdx.x; e < GT * GKD; e += GNT) {
+      // consecutive threads read consecutive addresses
+      const int ii = g.tA ? e % GT : e / GKD, ll = g.tA ? e / GT : e % GKD;
+      const int i = i0 + ii, l = l0 + ll;
+      double v = 0.0;
+      if (i < g.M && l < g.K) v = g.tA ? A[(int64_t)l * g.lda + i] : A[(int64_t)i * g.lda + l];
+      As[ll][ii] = v;
+    }
+    for (int e = threadIdx.x; e < GT * GKD; e += GNT) {
+      const int jj = g.tB ? e / GKD : e % GT, ll = g.tB ? e % GKD : e / GT;
+      const int j = j0 + jj, l = l0 + ll;
+      double v = 0.0;
+      if (j < g.N && l < g.K) v = g.tB ? B[(int64_t)j * g.ldb + l] : B[(int64_t)l * g.ldb + j];
+      Bs[ll][jj] = v;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int ll = 0; ll < GKD; ++ll) {
+      double a[4], b[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) a[r] = As[ll][ty + 16 * r];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) b[c] = Bs[ll][tx + 16 * c];
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) acc[r][c] = fma(a[r], b[c], acc[r][c]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int r = 0; r < 4; ++r)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const int i = i0 + ty + 16 * r, j = j0 + tx + 16 * c;
+      if (i < g.M && j < g.N) C[(int64_t)i * g.ldc + j] = acc[r][c];
+    }
+}
+
+int launch_gemm(const Gemm& g, int n_cells, cudaStream_t st) {
+  const dim3 grid((g.N + GT - 1) / GT, (g.M + GT - 1) / GT, n_cells);
+  f64_gemm_kernel<<<grid, GNT, 0, st>>>(g);
+  return check_launch("f64_gemm_kernel");
+}
+
+constexpr int CH_NT = 256;
+constexpr int CH_ROWS = 32;  // panel rows (fewer when k is large: the panel lives in shared memory)
+
+int chol_panel_rows(int k) { return std::max(1, std::min(CH_ROWS, (int)(28000 / std::max(k, 1)))); }
+
+// In place per cell: S (k x k, row-major) -> R in its upper triangle with
+// S = R^T R (CholeskyQR's Gram), rinv[j] = 1 / R[j][j].  Rank dropping as in
+// sm_chol_inv: a pivot at or below 1e-10 of the column's original diagonal
+// makes the row of R zero and rinv[j] = 0.  Right-looking, nb panel rows at
+// a time: the panel is factored in shared memory (one barrier per column,
+// the row scaled one step late), then the trailing upper triangle takes the
+// rank-nb update in 4 x 4 register tiles.
+__global__ void __launch_bounds__(CH_NT) chol_kernel(double* Sb, int k, int nbmax, int64_t sS, double* rinvb,
+                                                     int64_t sR) {
+  extern __shared__ double P[];  // nbmax x k
+  __shared__ double dg[CH_ROWS], ri[CH_ROWS];
+  double* S = Sb + blockIdx.x * sS;
+  double* rinv = rinvb + blockIdx.x * sR;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) rinv[i] = S[(int64_t)i * k + i];  // original diagonal
+  __syncthreads();
+  for (int j0 = 0; j0 < k; j0 += nbmax) {
+    const int nb = min(nbmax, k - j0), w = k - j0;
+    for (int e = threadIdx.x; e < nb * w; e += blockDim.x) {
+      const int r = e / w, c = e % w;
+      P[r * w + c] = S[(int64_t)(j0 + r) * k + j0 + c];
+    }
+    for (int r = threadIdx.x; r < nb; r += blockDim.x) dg[r] = rinv[j0 + r];
+    __syncthreads();
+    for (int j = 0; j < nb; ++j) {
+      const double d = P[j * w + j], o = dg[j];
+      const bool keep = o > 0.0 && d > 1e-10 * o;
+      const double rs = keep ? 1.0 / sqrt(d) : 0.0;
+      const double inv_d = rs * rs;
+      const int ns = j > 0 ? w - (j - 1) : 0;
+      const int nu = (nb - 1 - j) * w;
+      for (int t = threadIdx.x; t < ns + nu; t += blockDim.x) {
+        if (t < ns) {
+          P[(j - 1) * w + (j - 1) + t] *= ri[j - 1];
+        } else {
+          const int u = t - ns, i = j + 1 + u / w, c = u % w;
+          if (c >= i) P[i * w + c] = fma(-P[j * w + i] * inv_d, P[j * w + c], P[i * w + c]);
+        }
+      }
+      if (threadIdx.x == 0) ri[j] = rs;
+      __syncthreads();
+    }
+    for (int c = nb - 1 + threadIdx.x; c < w; c += blockDim.x) P[(nb - 1) * w + c] *= ri[nb - 1];
+    __syncthreads();
+    // the panel rows of R (upper part) and their inverse pivots
+    for (int e = threadIdx.x; e < nb * w; e += blockDim.x) {
+      const int r = e / w, c = e % w;
+      S[(int64_t)(j0 + r) * k + j0 + c] = c >= r ? P[r * w + c] : 0.0;
+    }
+    for (int r = threadIdx.x; r < nb; r += blockDim.x) rinv[j0 + r] = ri[r];
+    // trailing update of the upper triangle: S[i][c] -= sum_r R[r][i] R[r][c]
+    const int m = w - nb, T = (m + 3) / 4;
+    for (int t = threadIdx.x; t < T * T; t += blockDim.x) {
+      const int ta = t / T, tb = t % T;
+      if (tb < ta) continue;
+      double acc[4][4];
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) acc[a][b] = 0.0;
+      const int ib = nb + 4 * ta, cb = nb + 4 * tb;
+      for (int r = 0; r < nb; ++r) {
+        double x[4], y[4];
+#pragma unroll
+        for (int a = 0; a < 4; ++a) x[a] = ib + a < w ? P[r * w + ib + a] : 0.0;
+#pragma unroll
+        for (int b = 0; b < 4; ++b) y[b] = cb + b < w ? P[r * w + cb + b] : 0.0;
+#pragma unroll
+        for (int a = 0; a < 4; ++a)
+#pragma unroll
+          for (int b = 0; b < 4; ++b) acc[a][b] = fma(x[a], y[b], acc[a][b]);
+      }
+#pragma unroll
+      for (int a = 0; a < 4; ++a)
+#pragma unroll
+        for (int b = 0; b < 4; ++b) {
+          const int i = ib + a, c = cb + b;
+          if (i < w && c < w && c >= i) S[(int64_t)(j0 + i) * k + j0 + c] -= acc[a][b];
+        }
+    }
+    __syncthreads();
+  }
+}
+
+constexpr int TS_ROWS = 16;  // rows of W per CTA: 16 lanes of a warp per row
+constexpr int TS_NT = 256;
+
+// W <- W R^{-1} per cell (R upper triangular from chol_kernel, rinv its
+// inverse pivots; a dropped column of R gives a zero column of W).  Each CTA
+// holds TS_ROWS rows of W in shared memory and sweeps the columns in blocks
+// of 32: first the rank update by the finished columns (R read through L1,
+// shared by every row), then the block's own forward substitution, column by
+// column, with the 16 lanes of a row splitting each dot product.
+__global__ void __launch_bounds__(TS_NT) trsm_kernel(double* Wb, int p, int k, int64_t sW, const double* Rb,
+                                                     int64_t sR, const double* rinvb, int64_t sri) {
+  extern __shared__ double Wl[];  // TS_ROWS x k
+  const int cell = blockIdx.y;
+  double* W = Wb + cell * sW;
+  const double* R = Rb + cell * sR;
+  const double* rinv = rinvb + cell * sri;
+  const int row0 = blockIdx.x * TS_ROWS;
+  const int nr = min(TS_ROWS, p - row0);
+  for (int e = threadIdx.x; e < TS_ROWS * k; e += blockDim.x) {
+    const int r = e / k, c = e % k;
+    Wl[e] = r < nr ? W[(int64_t)(row0 + r) * k + c] : 0.0;
+  }
+  __syncthreads();
+  const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
+  double* wr = Wl + r * k;
+  for (int J0 = 0; J0 < k; J0 += 32) {
+    const int cb = min(32, k - J0);
+    // rank update by columns [0, J0)
+    if (J0 > 0) {
+      double a0 = 0.0, a1 = 0.0;
+      const int c0 = J0 + lane, c1 = J0 + lane + 16;
+      for (int i = 0; i < J0; ++i) {
+        const double wi = wr[i];
+        if (c0 < k) a0 = fma(wi, __ldg(R + (int64_t)i * k + c0), a0);
+        if (c1 < k) a1 = fma(wi, __ldg(R + (int64_t)i * k + c1), a1);
+      }
+      if (c0 < k) wr[c0] -= a0;
+      if (c1 < k) wr[c1] -= a1;
+    }
+    __syncwarp();
+    // forward substitution inside the block
+    for (int c = 0; c < cb; ++c) {
+      const int col = J0 + c;
+      double part = 0.0;
+      if (lane < c) part = wr[J0 + lane] * __ldg(R + (int64_t)(J0 + lane) * k + col);
+      if (lane + 16 < c) part = fma(wr[J0 + lane + 16], __ldg(R + (int64_t)(J0 + lane + 16) * k + col), part);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
+      if (lane == 0) wr[col] = (wr[col] - part) * rinv[col];
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < nr * k; e += blockDim.x) {
+    const int rr = e / k, c = e % k;
+    W[(int64_t)(row0 + rr) * k + c] = Wl[e];
+  }
+}
+
+// Offsets (doubles) of the randomised multi-launch path's per-cell workspace.
+struct LrLayout {
+  int64_t W, Z, S, C, Zt, vec, lam, rinv, misc, scr, total;
+};
+
+LrLayout lr_layout(int p, int k) {
+  LrLayout L;
+  L.W = 0;
+  L.Z = L.W + (int64_t)p * k;
+  L.S = L.Z + (int64_t)p * k;
+  L.C = L.S + (int64_t)k * k;
+  L.Zt = L.C + (int64_t)k * k;
+  L.vec = L.Zt + (int64_t)k * k;
+  L.lam = L.vec + eig::vec_doubles(k);
+  L.rinv = L.lam + k;
+  L.misc = L.rinv + k;
+  L.scr = L.misc + 2;
+  L.total = L.scr + eig_scratch_doubles(k);
+  return L;
+}
+
+// W = the starting sketch (LEFT: Y0 = A Omega from the Gram buffer; RIGHT:
+// Omega), misc[0] = |A|_F^2.
+__global__ void lr_init_kernel(SolveArgs a, LrLayout L) {
+  const int cell = blockIdx.x, p = a.p, k = a.k;
+  const double* gram = a.gram + cell * a.gram_stride;
+  double* ws = a.ws + cell * a.ws_cell;
+  if (a.side == KVC_SIDE_LEFT) {
+    const double* y0 = gram + (int64_t)p * p;
+    for (int64_t i = threadIdx.x; i < (int64_t)p * k; i += blockDim.x) ws[L.W + i] = y0[i];
+    if (threadIdx.x == 0) ws[L.misc] = gram[(int64_t)p * p + (int64_t)p * k];
+  } else {
+    for (int64_t i = threadIdx.x; i < (int64_t)p * k; i += blockDim.x) ws[L.W + i] = (double)a.omega[i];
+    __shared__ double red[64];
+    double part = 0.0;
+    for (int i = threadIdx.x; i < p; i += blockDim.x) part += gram[(int64_t)i * p + i];
+    const double t = eig::block_sum(part, red);
+    if (threadIdx.x == 0) ws[L.misc] = t;
+  }
+}
+
+// The Ritz pairs: the rank leading eigenpairs of C; tail and sv2.
+__global__ void __launch_bounds__(SNT) lr_eig_kernel(SolveArgs a, LrLayout L) {
+  __shared__ double red[64];
+  __shared__ int cnt[SNT];
+  const int cell = blockIdx.x, k = a.k, rank = a.rank;
+  double* ws = a.ws + cell * a.ws_cell;
+  double* lam = ws + L.lam;
+  eig::eig_top(ws + L.C, k, k, rank, lam, ws + L.Zt, k, ws + L.vec, cnt, red, ws + L.scr);
+  if (threadIdx.x == 0) {
+    double retained = 0.0;
+    for (int i = 0; i < rank; ++i) retained += fmax(lam[i], 0.0);
+    const double nrm = ws[L.misc];
+    const double t = nrm > 0.0 ? 1.0 - retained / nrm : 0.0;
+    a.tail[cell] = t > 0.0 ? t : 0.0;
+    if (a.sv2)
+      for (int i = 0; i < rank; ++i) a.sv2[(int64_t)cell * rank + i] = fmax(lam[i], 0.0);
+  }
+}
+
+// LEFT basis: the product in the Z slot rounded to the basis dtype.
+__global__ void lr_store_kernel(SolveArgs a, LrLayout L) {
+  const int cell = blockIdx.y;
+  const double* z = a.ws + cell * a.ws_cell + L.Z;
+  const int64_t n = (int64_t)a.p * a.rank;
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    store_dt(a.basis, (int64_t)cell * n + i, (float)z[i], a.basis_dtype);
+}
+
+int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
+  const int p = a.p, k = a.k;
+  const LrLayout L = lr_layout(p, k);
+  const int64_t cs = a.ws_cell;
+  double* ws = a.ws;
+  const int nbmax = chol_panel_rows(k);
+  const size_t chol_smem = sizeof(double) * (size_t)nbmax * k;
+  const size_t trsm_smem = sizeof(double) * (size_t)TS_ROWS * k;
+  cudaError_t e = cudaFuncSetAttribute(chol_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chol_smem);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(trsm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)trsm_smem);
+  if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+  int rc;
+  lr_init_kernel<<<n_cells, 256, 0, st>>>(a, L);
+  if ((rc = check_launch("lr_init_kernel"))) return rc;
+  int64_t cur = L.W, oth = L.Z;  // the current basis and the other p x k slot
+  auto gemm = [&](const double* A, int64_t sA, int lda, int tA, const double* B, int64_t sB, int ldb, int tB,
+                  double* C, int64_t sC, int ldc, int M, int N, int K) {
+    Gemm g{A, B, C, M, N, K, lda, ldb, ldc, tA, tB, sA, sB, sC};
+    return launch_gemm(g, n_cells, st);
+  };
+  // one CholeskyQR pass on the current basis, in the inner product of H (RIGHT) or I (LEFT)
+  auto orth = [&]() -> int {
+    int r2;
+    const double* rhs = ws + cur;
+    if (a.side == KVC_SIDE_RIGHT) {
+      if ((r2 = gemm(a.gram, a.gram_stride, p, 0, ws + cur, cs, k, 0, ws + oth, cs, k, p, k, p))) return r2;
+      rhs = ws + oth;
+    }
+    if ((r2 = gemm(ws + cur, cs, k, 1, rhs, cs, k, 0, ws + L.S, cs, k, k, k, p))) return r2;
+    chol_kernel<<<n_cells, CH_NT, chol_smem, st>>>(ws + L.S, k, nbmax, cs, ws + L.rinv, cs);
+    if ((r2 = check_launch("chol_kernel"))) return r2;
+    const dim3 grid((p + TS_ROWS - 1) / TS_ROWS, n_cells);
+    trsm_kernel<<<grid, TS_NT, trsm_smem, st>>>(ws + cur, p, k, cs, ws + L.S, cs, ws + L.rinv, cs);
+    return check_launch("trsm_kernel");
+  };
+  if ((rc = orth())) return rc;
+  if (a.n_power == 0 && (rc = orth())) return rc;
+  for (int it = 0; it < a.n_power; ++it) {
+    // the other slot = G W becomes the sketch
+    if ((rc = gemm(a.gram, a.gram_stride, p, 0, ws + cur, cs, k, 0, ws + oth, cs, k, p, k, p))) return rc;
+    std::swap(cur, oth);
+    if ((rc = orth())) return rc;
+    if (it + 1 == a.n_power && (rc = orth())) return rc;
+  }
+  // Ritz matrix: C = W^T G W (LEFT) or (H W)^T (H W) (RIGHT)
+  if ((rc = gemm(a.gram, a.gram_stride, p, 0, ws + cur, cs, k, 0, ws + oth, cs, k, p, k, p))) return rc;
+  if (a.side == KVC_SIDE_LEFT) rc = gemm(ws + cur, cs, k, 1, ws + oth, cs, k, 0, ws + L.C, cs, k, k, k, p);
+  else rc = gemm(ws + oth, cs, k, 1, ws + oth, cs, k, 0, ws + L.C, cs, k, k, k, p);
+  if (rc) return rc;
+  lr_eig_kernel<<<n_cells, SNT, 0, st>>>(a, L);
+  if ((rc = check_launch("lr_eig_kernel"))) return rc;
+  // basis = W Zt^T (p x rank)
+  if (a.side == KVC_SIDE_RIGHT) {
+    return gemm(ws + cur, cs, k, 0, ws + L.Zt, cs, k, 1, static_cast<double*>(a.basis), (int64_t)p * a.rank, a.rank,
+                p, a.rank, k);
+  }
+  if ((rc = gemm(ws + cur, cs, k, 0, ws + L.Zt, cs, k, 1, ws + oth, cs, a.rank, p, a.rank, k))) return rc;
+  SolveArgs b = a;
+  b.ws = ws;
+  // the product sits in the slot `oth`; point the store kernel's Z slot at it
+  LrLayout L2 = L;
+  L2.Z = oth;
+  const dim3 grid(std::max(1, std::min(64, (int)(((int64_t)p * a.rank + 255) / 256))), n_cells);
+  lr_store_kernel<<<grid, 256, 0, st>>>(b, L2);
+  return check_launch("lr_store_kernel");
+}
+
 // Workspace doubles per cell: the general solver's layout (above), which
 // also covers the shared-memory kernels' eigenvectors and scratch.
 int64_t ws_per_cell(int mode, int p, int k) {
   if (mode == KVC_SVD_EXACT) return 2LL * p * p + eig::vec_doubles(p) + p + eig_scratch_doubles(p);
-  return 2LL * p * k + 3LL * k * k + eig::vec_doubles(k) + k + eig_scratch_doubles(k);
+  return lr_layout(p, k).total;
 }
 
 }  // namespace
@@ -575,8 +826,8 @@ extern "C" int kvc_sketch_solve(int n_cells, int mode, int side, int p, int64_t 
     return fail(KVC_ERR_ARG, "kvc_sketch_solve: bad side");
   if (p <= 0 || p > MAX_DIM || rank <= 0 || rank > p || n_other <= 0)
     return fail(KVC_ERR_SHAPE, "kvc_sketch_solve: bad p/rank");
-  if (mode == KVC_SVD_RANDOMISED && (k < rank || k > p || k > MAX_DIM))
-    return fail(KVC_ERR_SHAPE, "kvc_sketch_solve: sketch width must satisfy rank <= k <= p");
+  if (mode == KVC_SVD_RANDOMISED && (k < rank || k > p || k > MAX_SKETCH))
+    return fail(KVC_ERR_SHAPE, "kvc_sketch_solve: sketch width must satisfy rank <= k <= min(p, 1024)");
   if (mode == KVC_SVD_RANDOMISED && (n_power < 0 || n_power > 16))
     return fail(KVC_ERR_ARG, "kvc_sketch_solve: n_power out of range");
   if (side == KVC_SIDE_RIGHT && mode == KVC_SVD_RANDOMISED && !omega)
@@ -623,6 +874,7 @@ extern "C" int kvc_sketch_solve(int n_cells, int mode, int side, int p, int64_t 
     exact_solve_small_kernel<<<n_cells, SM_NT, smem, static_cast<cudaStream_t>(stream)>>>(a);
     return check_launch("exact_solve_small_kernel");
   }
-  sketch_solve_kernel<<<n_cells, SNT, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  return check_launch("sketch_solve_kernel");
+  if (mode == KVC_SVD_RANDOMISED) return lr_solve(a, n_cells, static_cast<cudaStream_t>(stream));
+  exact_solve_kernel<<<n_cells, SNT, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("exact_solve_kernel");
 }

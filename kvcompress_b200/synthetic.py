@@ -124,25 +124,30 @@ def make_kv_layer(
     device: str | torch.device = "cpu",
     tokens: int | None = None,
     batch: int | None = None,
+    precise: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """K and V of one layer, shape ``(batch, n_kv, T, head_dim)`` in ``w.dtype``.
 
     ``tokens`` / ``batch`` override the workload's sizes (small parity cases
-    keep the value distribution of the full workload).
+    keep the value distribution of the full workload).  ``precise`` does the
+    arithmetic in float64 before the final cast, so the same bytes come out on
+    any CPU whatever its BLAS (the parity fixtures of large caches regenerate
+    their inputs this way instead of storing them).
     """
     t = int(tokens or w.tokens)
     b = int(batch or w.batch)
     d, r = w.head_dim, w.latent_rank
     sigma = layer_sigma(w, layer, seed)
+    fdt = torch.float64 if precise else torch.float32
     out = []
     for kind in (0, 1):
         g = torch.Generator(device=device).manual_seed(int(seed) * 1_000_003 + 2 * int(layer) + kind)
         s = b * w.n_kv
-        a = torch.randn(s, t, r, generator=g, device=device, dtype=torch.float32)
-        bm = torch.randn(s, r, d, generator=g, device=device, dtype=torch.float32) / math.sqrt(r)
+        a = torch.randn(s, t, r, generator=g, device=device, dtype=fdt)
+        bm = torch.randn(s, r, d, generator=g, device=device, dtype=fdt) / math.sqrt(r)
         x = torch.bmm(a, bm)
         del a, bm
-        x.add_(torch.randn(s, t, d, generator=g, device=device, dtype=torch.float32), alpha=sigma)
+        x.add_(torch.randn(s, t, d, generator=g, device=device, dtype=fdt), alpha=sigma)
         if kind == 0:
             ch = outlier_channels(d, w.n_outliers, seed).to(device)
             x[..., ch] *= 8.0

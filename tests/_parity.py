@@ -50,3 +50,37 @@ def oracle_jolt(x: np.ndarray, dt: str, alloc, *, method: str, cap, proj: np.nda
 def projector(u: np.ndarray) -> np.ndarray:
     u = np.asarray(u, np.float64)
     return u @ u.T
+
+
+def recon_rows(core, u_token, u_feature, dt: str, rows: np.ndarray, t: int) -> np.ndarray:
+    """Rows ``rows`` of the (m*T, d) view of ``reconstruct_partial_tucker``
+    (tucker.py:159-189), rounded as the reference rounds: the token-rank
+    contraction in float32 rounded to ``dt``, then the feature rank."""
+    core = np.asarray(core, np.float32)
+    u_token = np.asarray(u_token, np.float32)
+    u_feature = np.asarray(u_feature, np.float32)
+    h, tt = rows // t, rows % t
+    tmp = oracle.round_to(np.einsum("nar,na->nr", core[h], u_token[tt], dtype=np.float32), dt)
+    return oracle.matmul_round(tmp, u_feature.T, dt)
+
+
+def near_ties(x_rows, recon, dt: str, proj, scale, margin: float = 1e-3) -> np.ndarray:
+    """Codes whose quantiser input lies within ``margin`` quantisation steps of
+    a rounding boundary (symmetric scales, zero point 0): the fp32 rotation may
+    round either way there.  The rotated residual is evaluated in float64 from
+    the residual in the cell dtype (jolt.py:311, residual.py:201-216)."""
+    resid = oracle.dt_op(lambda a, b: a - b, dt, np.asarray(x_rows, np.float32), recon)
+    rot = np.asarray(resid, np.float64) @ np.asarray(proj, np.float64).T
+    v = rot / np.asarray(scale, np.float64)
+    return np.abs(v - np.floor(v) - 0.5) < margin
+
+
+def assert_codes_match(got_packed, ref_packed, bits: int, d: int, ties: np.ndarray) -> float:
+    """Every code away from a tie is identical; returns the fraction of the
+    near-tie codes that differ (the flip rate)."""
+    got = oracle.unpack_codes(np.asarray(got_packed), bits, d)
+    ref = oracle.unpack_codes(np.asarray(ref_packed), bits, d)
+    diff = got != ref
+    bad = diff & ~ties
+    assert not bad.any(), f"{int(bad.sum())} codes differ away from ties (first at {np.argwhere(bad)[0]})"
+    return float(diff.sum()) / max(1, int(ties.sum()))

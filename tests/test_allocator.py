@@ -83,3 +83,50 @@ def test_distributed_allocation_gloo():
         assert allocs == [a.tuple for a in ref.allocations]
         assert lam == ref.lambda_star
         assert idx == ([0, 1] if rank == 0 else [2, 3])
+
+
+def _shard_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        import bench
+
+        shape, n_layers = (64, 32768, 128), 32
+        layers = bench.my_layers(n_layers, world, rank)
+        mine = [Cell(shape=shape, kind=kind) for _ in layers for kind in ("key", "value")]
+        res, idx = JointAllocator(target_ratio=4.0).optimize_distributed(mine)
+        q.put((rank, layers, [a.tuple for a in res.allocations], [a.cost_bytes for a in res.allocations], idx,
+               res.total_bytes))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_cell_sharded_cache_allocation_gloo():
+    """The benchmark's sharding of one 8 x 32k Llama-3-8B cache over two ranks
+    (contiguous layer blocks, K and V cells): the allocation agreed over the
+    ranks equals the one-process allocation of all 64 cells and the per-layer
+    allocation every compress call uses, and the payload bytes add up to the
+    same total."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + ((os.getpid() + 1000) % 2000)
+    procs = [ctx.Process(target=_shard_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    outs = sorted(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    shape = (64, 32768, 128)
+    assert outs[0][1] == list(range(16)) and outs[1][1] == list(range(16, 32))
+    one = JointAllocator(target_ratio=4.0).optimize([Cell(shape=shape, kind=k) for _ in range(32)
+                                                     for k in ("key", "value")])
+    per_layer = JointAllocator(target_ratio=4.0).optimize([Cell(shape=shape, kind="key"),
+                                                           Cell(shape=shape, kind="value")])
+    for rank, _layers, allocs, costs, idx, total in outs:
+        assert allocs == [a.tuple for a in one.allocations]
+        assert allocs == [a.tuple for a in per_layer.allocations] * 32
+        assert costs == [a.cost_bytes for a in one.allocations]
+        assert total == one.total_bytes == 32 * per_layer.total_bytes
+        assert idx == list(range(32 * rank, 32 * rank + 32))

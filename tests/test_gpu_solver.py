@@ -94,7 +94,7 @@ def test_randomised_left(n, p, k, rank):
 
 
 @pytest.mark.parametrize("n,p,k,rank", [(8192, 8, 8, 1), (32768, 64, 11, 1), (4096, 256, 74, 64),
-                                        (2048, 200, 37, 27)])
+                                        (2048, 200, 37, 27), (4096, 1024, 513, 512)])
 def test_randomised_right(n, p, k, rank):
     a = _matrix(n, p, seed=7 * p + k, decay=2.0)
     rng = np.random.default_rng(p)
