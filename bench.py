@@ -44,6 +44,7 @@ METRIC = "compress tokens/s + decompress GB/s (Llama-3-8B KV shape) at 1/2/4/8 B
 DEFAULT_WORKLOAD = "llama3-8b-kv-b8-t32768-bf16"
 SINGLE_GPU_WORKLOAD = "llama3-8b-kv-b1-t8192-bf16"
 STREAM_WORKLOAD = "qwen2-7b-kv-b4-t131072-bf16"
+QCAP_WORKLOAD = "llama3-8b-kv-b8-t4096-bf16-qcap"
 BREAKDOWN_STEPS = 3  # traced steps for the per-stage times, before the timed region
 FALLBACK_HBM_GBS = 6650.0
 REFERENCE_DIR = os.path.join(ROOT, "baseline", "_ref")
@@ -65,6 +66,8 @@ def parse_args():
     ap.add_argument("--e2e-host-layers", type=int, default=8,
                     help="distinct layers held in pinned host memory for the e2e line (reused cyclically)")
     ap.add_argument("--stream-block", type=int, default=256, help="tokens per block of the decode-stream line (0: no such line)")
+    ap.add_argument("--qcap-workload", default=QCAP_WORKLOAD,
+                    help="the q-capped sketch config measured at N = 1 ('' to skip)")
     ap.add_argument("--stream-workload", default=STREAM_WORKLOAD,
                     help="the decode-stream config measured at N = 1, with the int4 / fp8 baselines ('' to skip)")
     ap.add_argument("--layers", type=int, default=0,
@@ -515,6 +518,10 @@ def run_ours(args, w):
         torch.cuda.empty_cache()
         line["single_gpu_config"] = single_gpu(WORKLOADS[args.single_gpu_workload], args, dev, peak,
                                                cpu=not args.no_cpu_baseline)
+    if world == 1 and args.qcap_workload:
+        pairs = None
+        torch.cuda.empty_cache()
+        line["qcap_config"] = single_gpu(WORKLOADS[args.qcap_workload], args, dev, peak, cpu=False)
     if world == 1 and args.stream_workload and args.stream_block > 0:
         pairs = None
         torch.cuda.empty_cache()

@@ -73,6 +73,12 @@ WORKLOADS = {
     "llama3-8b-kv-b8-t32768-bf16": KVWorkload(
         "llama3-8b-kv-b8-t32768-bf16", 32, 8, 128, 8, 32768, torch.bfloat16,
         16, 0.1, 4, 10000.0, "flashjolt", 4.0),
+    # One layer of the batch 8 cache at 4k tokens, FlashJoLT 4x with residual
+    # bits (0, 2, 4): the allocator picks (512, 16, 4), so the token sketch
+    # meets the q cap (513 wide).
+    "llama3-8b-kv-b8-t4096-bf16-qcap": KVWorkload(
+        "llama3-8b-kv-b8-t4096-bf16-qcap", 1, 8, 128, 8, 4096, torch.bfloat16,
+        16, 0.1, 4, 10000.0, "flashjolt", 4.0, bits=(0, 2, 4)),
     # Llama-3-8B-shaped, batch 8 x 32k, exact JoLT 3x.
     "llama3-8b-kv-b8-t32768-bf16-jolt": KVWorkload(
         "llama3-8b-kv-b8-t32768-bf16-jolt", 32, 8, 128, 8, 32768, torch.bfloat16,
