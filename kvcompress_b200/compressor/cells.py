@@ -90,7 +90,7 @@ def tucker_cells(xs: list[torch.Tensor], *, r_token: int, r_feature: int, svd: S
     flat = xs.reshape(n_f, d)
     g_f = ops.gram(flat, om_f)
     u_d, tail_f, _ = ops.sketch_solve(g_f, mode=mode_f, side=KVC.SIDE_LEFT, p=d, n_other=n_f, k=k_f,
-                                      rank=rd, n_power=svd.n_power, omega=None, basis_dtype=dt)
+                                      rank=rd, n_power=svd.n_power, omega=None, basis_dtype=dt, want_sv2=False)
     u_feature = ops.split(u_d)
 
     # --- projection to (T, m*rd) ------------------------------------------
@@ -103,7 +103,7 @@ def tucker_cells(xs: list[torch.Tensor], *, r_token: int, r_feature: int, svd: S
     g_t = ops.gram(x_proj_t, None)
     mat, tail_t, _ = ops.sketch_solve(g_t, mode=mode_t, side=KVC.SIDE_RIGHT, p=c, n_other=t, k=k_t,
                                       rank=rt, n_power=svd.n_power, omega=om_t,
-                                      basis_dtype=torch.float64)
+                                      basis_dtype=torch.float64, want_sv2=False)
     u_token = ops.apply_basis(x_proj_t, mat)
     core = ops.core(x_proj_t, u_token, m, rd)
     return core, u_token, u_feature, tail_t, tail_f

@@ -155,7 +155,7 @@ extern "C" int kvc_compress(int n_cells, const void* const* x, int64_t m, int64_
   if ((rc = mark(ST_GRAM_F, 1, stream))) return rc;
   if ((rc = mark(ST_SOLVE_F, 0, stream))) return rc;
   if ((rc = kvc_sketch_solve(n, mode_f, KVC_SIDE_LEFT, d, m * t, kf, rd, n_power, gram_f,
-                             (int64_t)d * d + (int64_t)d * kf + 1, nullptr, u_feature_out, dtype, sv2, tail_feature,
+                             (int64_t)d * d + (int64_t)d * kf + 1, nullptr, u_feature_out, dtype, nullptr, tail_feature,
                              scratch, scr, stream)))
     return rc;
   if ((rc = mark(ST_SOLVE_F, 1, stream))) return rc;
@@ -168,7 +168,7 @@ extern "C" int kvc_compress(int n_cells, const void* const* x, int64_t m, int64_
   if ((rc = mark(ST_GRAM_T, 1, stream))) return rc;
   if ((rc = mark(ST_SOLVE_T, 0, stream))) return rc;
   if ((rc = kvc_sketch_solve(n, mode_t, KVC_SIDE_RIGHT, (int)c, t, kt, rt, n_power, gram_t, c * c + 1, omega_t,
-                             mat, KVC_F64, sv2, tail_token, scratch, scr, stream)))
+                             mat, KVC_F64, nullptr, tail_token, scratch, scr, stream)))
     return rc;
   if ((rc = mark(ST_SOLVE_T, 1, stream))) return rc;
   if (tails_host) {

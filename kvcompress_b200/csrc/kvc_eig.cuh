@@ -123,16 +123,25 @@ __device__ inline void tridiagonalize(double* A, int lda, int n, double* d, doub
       col[0] = v0;  // v_j kept in column j (the rest of x is already v)
     }
     __syncthreads();
-    // p = t S v, S = A[j+1:, j+1:] (columns read: consecutive threads,
-    // consecutive addresses)
+    // p = t S v, S = A[j+1:, j+1:] (columns read: consecutive rows of a
+    // group, consecutive addresses); tpr threads split each row's sum when
+    // the trailing matrix is small, which shortens the dependent chain
     const double* S = A + (int64_t)(j + 1) * lda + (j + 1);
+    int tpr = 1;
+    while (tpr < 32 && tpr * 2 * m <= (int)blockDim.x) tpr *= 2;
+    const int sub = threadIdx.x & (tpr - 1), rpp = blockDim.x / tpr;
     double kp = 0.0;
-    for (int i = threadIdx.x; i < m; i += blockDim.x) {
+    for (int i0 = 0; i0 < m; i0 += rpp) {  // the same trip count for every thread (the shuffles)
+      const int i = i0 + (int)threadIdx.x / tpr;
       double acc = 0.0;
-      for (int k = 0; k < m; ++k) acc = fma(S[(int64_t)k * lda + i], vs[k], acc);
-      const double p = t * acc;
-      ps[i] = p;
-      kp = fma(vs[i], p, kp);
+      if (i < m)
+        for (int k = sub; k < m; k += tpr) acc = fma(S[(int64_t)k * lda + i], vs[k], acc);
+      for (int o = tpr >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (i < m && sub == 0) {
+        const double p = t * acc;
+        ps[i] = p;
+        kp = fma(vs[i], p, kp);
+      }
     }
     const double K = 0.5 * t * block_sum(kp, red);
     // w = p - K v (in ps)
@@ -308,19 +317,21 @@ __device__ inline void tri_solve(const double* d, const double* e, int n, double
 }
 
 // 3. Eigenvectors of T for lam[0..r) (descending) into rows of Zt (r x n,
-// row stride ldz): thread-parallel over clusters of eigenvalues closer than
-// 1e-7 * nrm, each cluster's vectors in order, re-orthogonalised against the
-// cluster's earlier ones.  scratch: per-thread 3 n doubles at
-// scratch + threadIdx.x * sstride (shared, local or global memory).
+// row stride ldz): parallel over clusters of eigenvalues closer than
+// 1e-7 * nrm (threads 0 .. workers - 1; a cluster's vectors in order, each
+// re-orthogonalised against the cluster's earlier ones).  scratch: 3 n
+// doubles per worker at scratch + threadIdx.x * sstride; shared memory keeps
+// the solves' read-after-write chains short.
 __device__ inline void tri_eigenvectors(const double* d, const double* e, int n, const double* lam, int r, double nrm,
-                                        double* Zt, int ldz, double* scratch, int64_t sstride) {
+                                        double* Zt, int ldz, double* scratch, int64_t sstride, int workers) {
   const double ctol = 1e-7 * nrm;
   const double inv_scale = nrm > 0.0 ? 1.0 / nrm : 1.0;
   const double tiny = 1e-15;
   double* dd = scratch + threadIdx.x * sstride;
   double* u1 = dd + n;
   double* u2 = u1 + n;
-  for (int a0 = threadIdx.x; a0 < r; a0 += blockDim.x) {
+  const int nw = workers < (int)blockDim.x ? workers : (int)blockDim.x;
+  for (int a0 = threadIdx.x; a0 < r && (int)threadIdx.x < nw; a0 += nw) {
     if (a0 > 0 && lam[a0 - 1] - lam[a0] <= ctol) continue;  // not a cluster start
     int a1 = a0 + 1;
     while (a1 < r && lam[a1 - 1] - lam[a1] <= ctol) ++a1;
@@ -381,11 +392,11 @@ __host__ __device__ constexpr int64_t vec_doubles(int n) { return 8LL * n; }
 // The r leading eigenpairs of the symmetric n x n matrix A (destroyed): lam
 // (r, descending) and the eigenvectors as rows of Zt (r x n, row stride ldz).
 // vec: vec_doubles(n) doubles; cnt: blockDim.x ints; red: 64 doubles (all
-// shared); scratch: 3 n doubles per thread of the first min(r, blockDim.x)
-// threads, thread t at scratch + t * 3 n.  Returns the spectral scale used
-// for the tolerances (a bound on max |lambda|).
+// shared); scratch: 3 n doubles for each of the first `workers` threads
+// (thread t at scratch + t * 3 n), which compute the eigenvectors.  Returns
+// the spectral scale used for the tolerances (a bound on max |lambda|).
 __device__ inline double eig_top(double* A, int lda, int n, int r, double* lam, double* Zt, int ldz, double* vec,
-                                 int* cnt, double* red, double* scratch) {
+                                 int* cnt, double* red, double* scratch, int workers) {
   double* d = vec;
   double* e = d + n;
   double* tau = e + n;
@@ -396,7 +407,7 @@ __device__ inline double eig_top(double* A, int lda, int n, int r, double* lam, 
   double* hi = lo + n;
   tridiagonalize(A, lda, n, d, e, tau, vs, ps, red);
   const double nrm = top_eigenvalues(d, e, n, r, lam, e2, lo, hi, cnt, red);
-  tri_eigenvectors(d, e, n, lam, r, nrm, Zt, ldz, scratch, 3LL * n);
+  tri_eigenvectors(d, e, n, lam, r, nrm, Zt, ldz, scratch, 3LL * n, workers);
   back_transform(A, lda, tau, n, Zt, ldz, r);
   return nrm;
 }

@@ -52,7 +52,7 @@ struct SolveArgs {
 //               A (p x p) | Zt (rank x p) | vec (8 p) | lam (p) | eig scratch
 //   randomised (the multi-launch path below, p > 128 or k > 32):
 //               W (p x k) | Z (p x k) | S (k x k) | C (k x k) | Zt (k x k) |
-//               vec (8 k) | lam (k) | misc (2) | eig scratch
+//               vec (8 k) | lam (k) | rinv (k) | misc (4) | eig scratch
 // where the eigensolver's scratch is 3 n doubles for each of min(n, SNT)
 // threads (n = p exact, k randomised).
 __host__ __device__ inline int64_t eig_scratch_doubles(int n) { return 3LL * n * (n < SNT ? n : SNT); }
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(SNT) exact_solve_kernel(SolveArgs a) {
     if (i / p == i % p) part += g;
   }
   const double total = eig::block_sum(part, red);  // trace = |A|_F^2 (its barriers order the copy)
-  eig::eig_top(A, p, p, rank, lam, Zt, p, vec, cnt, red, scr);
+  eig::eig_top(A, p, p, rank, lam, Zt, p, vec, cnt, red, scr, SNT);
   const int64_t max_rank = a.n_other < p ? a.n_other : p;
   if (threadIdx.x == 0) {
     double kept = 0.0;
@@ -344,8 +344,9 @@ __global__ void __launch_bounds__(SM_NT) sketch_solve_small_kernel(SolveArgs a) 
   if (a.side == KVC_SIDE_LEFT) sm_colgram(C, Q, Z, p, k);  // Q^T G Q
   else sm_colgram(C, Z, Z, p, k);                         // (H W)^T (H W)
   // the rank leading Ritz pairs (eigenpairs of C); the eigensolver's
-  // per-thread scratch is in the workspace
-  eig::eig_top(C, SM_K, k, rank, lam, Zt, SM_K, vec, cnt, red, a.ws + cell * a.ws_cell);
+  // per-thread scratch is the Z buffer, free once C is formed
+  const int workers = std::max(1, std::min(rank, (p * SM_QS) / (3 * k)));
+  eig::eig_top(C, SM_K, k, rank, lam, Zt, SM_K, vec, cnt, red, Z, workers);
   if (threadIdx.x == 0) {
     double retained = 0.0;
     for (int i = 0; i < rank; ++i) retained += fmax(lam[i], 0.0);
@@ -371,12 +372,19 @@ __global__ void __launch_bounds__(SM_NT) sketch_solve_small_kernel(SolveArgs a) 
 // eigenvectors and the eigensolver's per-thread scratch in the workspace.
 // ---------------------------------------------------------------------------
 constexpr int EX_P = 128;
+constexpr size_t SMEM_LIMIT = 227 * 1024;  // dynamic shared memory of one CTA (opt-in maximum)
+
+constexpr int EX_WORKERS = 8;  // threads computing eigenvectors when they fit in shared memory
 
 size_t exact_small_smem_bytes(int p) {
   return sizeof(double) * ((size_t)p * p + eig::vec_doubles(p) + p + 64) + sizeof(int) * SM_NT;
 }
+// the eigenvectors (rank x p) and EX_WORKERS solve scratches in shared memory too
+size_t exact_small_smem_bytes_vectors(int p, int rank) {
+  return exact_small_smem_bytes(p) + sizeof(double) * ((size_t)rank * p + 3 * (size_t)p * EX_WORKERS);
+}
 
-__global__ void __launch_bounds__(SM_NT) exact_solve_small_kernel(SolveArgs a) {
+__global__ void __launch_bounds__(SM_NT) exact_solve_small_kernel(SolveArgs a, int vectors_in_smem) {
   extern __shared__ __align__(16) double sm[];
   const int cell = blockIdx.x;
   const int p = a.p, rank = a.rank;
@@ -386,8 +394,9 @@ __global__ void __launch_bounds__(SM_NT) exact_solve_small_kernel(SolveArgs a) {
   double* lam = vec + eig::vec_doubles(p);     // p
   double* red = lam + p;                       // 64
   int* cnt = reinterpret_cast<int*>(red + 64); // SM_NT
-  double* Zt = a.ws + cell * a.ws_cell;        // rank x p
+  double* Zt = vectors_in_smem ? reinterpret_cast<double*>(cnt + SM_NT) : a.ws + cell * a.ws_cell;  // rank x p
   double* scr = Zt + (int64_t)rank * p;
+  const int workers = vectors_in_smem ? EX_WORKERS : SM_NT;
   {
     constexpr int U = 16;  // loads in flight per thread before their stores
     const int nt = blockDim.x, pp = p * p;
@@ -405,7 +414,7 @@ __global__ void __launch_bounds__(SM_NT) exact_solve_small_kernel(SolveArgs a) {
   double part = 0.0;
   for (int i = threadIdx.x; i < p; i += blockDim.x) part += G[i * (p + 1)];
   const double total = eig::block_sum(part, red);  // trace = |A|_F^2
-  eig::eig_top(G, p, p, rank, lam, Zt, p, vec, cnt, red, scr);
+  eig::eig_top(G, p, p, rank, lam, Zt, p, vec, cnt, red, scr, workers);
   const int64_t max_rank = a.n_other < p ? a.n_other : p;
   if (threadIdx.x == 0) {
     double kept = 0.0;
@@ -604,6 +613,77 @@ __global__ void __launch_bounds__(CH_NT) chol_kernel(double* Sb, int k, int nbma
 constexpr int TS_ROWS = 16;  // rows of W per CTA: 16 lanes of a warp per row
 constexpr int TS_NT = 256;
 
+// w <- w R^{-1} for the 16 rows w of Wl (row stride ldw, 256 threads: row
+// threadIdx / 16, lane threadIdx % 16): R upper triangular (k x k, row
+// stride k, read through L1), rinv its inverse pivots.  Columns in blocks of
+// 32: the rank update by the finished columns, then the block's forward
+// substitution column by column, the 16 lanes of a row splitting each dot.
+__device__ inline void rows_solve_upper(double* Wl, int ldw, int k, const double* __restrict__ R,
+                                        const double* __restrict__ rinv) {
+  const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
+  double* wr = Wl + r * ldw;
+  for (int J0 = 0; J0 < k; J0 += 32) {
+    const int cb = min(32, k - J0);
+    if (J0 > 0) {
+      double a0 = 0.0, a1 = 0.0;
+      const int c0 = J0 + lane, c1 = J0 + lane + 16;
+      for (int i = 0; i < J0; ++i) {
+        const double wi = wr[i];
+        if (c0 < k) a0 = fma(wi, __ldg(R + (int64_t)i * k + c0), a0);
+        if (c1 < k) a1 = fma(wi, __ldg(R + (int64_t)i * k + c1), a1);
+      }
+      if (c0 < k) wr[c0] -= a0;
+      if (c1 < k) wr[c1] -= a1;
+    }
+    __syncwarp();
+    for (int c = 0; c < cb; ++c) {
+      const int col = J0 + c;
+      double part = 0.0;
+      if (lane < c) part = wr[J0 + lane] * __ldg(R + (int64_t)(J0 + lane) * k + col);
+      if (lane + 16 < c) part = fma(wr[J0 + lane + 16], __ldg(R + (int64_t)(J0 + lane + 16) * k + col), part);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
+      if (lane == 0) wr[col] = (wr[col] - part) * rinv[col];
+      __syncwarp();
+    }
+  }
+}
+
+// w <- w R^{-T} for the 16 rows of Wl (the same thread layout): y R^T = w,
+// y_j = (w_j - sum_{i > j} y_i R[j][i]) / R[j][j], columns in blocks of 32
+// from the last.
+__device__ inline void rows_solve_upper_t(double* Wl, int ldw, int k, const double* __restrict__ R,
+                                          const double* __restrict__ rinv) {
+  const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
+  double* wr = Wl + r * ldw;
+  for (int J0 = ((k - 1) / 32) * 32; J0 >= 0; J0 -= 32) {
+    const int cb = min(32, k - J0), end = J0 + cb;
+    if (end < k) {
+      double a0 = 0.0, a1 = 0.0;
+      const int j0 = J0 + lane, j1 = J0 + lane + 16;
+      for (int i = end; i < k; ++i) {
+        const double yi = wr[i];
+        if (j0 < end) a0 = fma(yi, __ldg(R + (int64_t)j0 * k + i), a0);
+        if (j1 < end) a1 = fma(yi, __ldg(R + (int64_t)j1 * k + i), a1);
+      }
+      if (j0 < end) wr[j0] -= a0;
+      if (j1 < end) wr[j1] -= a1;
+    }
+    __syncwarp();
+    for (int c = cb - 1; c >= 0; --c) {
+      const int col = J0 + c;
+      double part = 0.0;
+      if (lane > c && lane < cb) part = wr[J0 + lane] * __ldg(R + (int64_t)col * k + J0 + lane);
+      if (lane + 16 > c && lane + 16 < cb)
+        part = fma(wr[J0 + lane + 16], __ldg(R + (int64_t)col * k + J0 + lane + 16), part);
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
+      if (lane == 0) wr[col] = (wr[col] - part) * rinv[col];
+      __syncwarp();
+    }
+  }
+}
+
 // W <- W R^{-1} per cell (R upper triangular from chol_kernel, rinv its
 // inverse pivots; a dropped column of R gives a zero column of W).  Each CTA
 // holds TS_ROWS rows of W in shared memory and sweeps the columns in blocks
@@ -624,35 +704,7 @@ __global__ void __launch_bounds__(TS_NT) trsm_kernel(double* Wb, int p, int k, i
     Wl[e] = r < nr ? W[(int64_t)(row0 + r) * k + c] : 0.0;
   }
   __syncthreads();
-  const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
-  double* wr = Wl + r * k;
-  for (int J0 = 0; J0 < k; J0 += 32) {
-    const int cb = min(32, k - J0);
-    // rank update by columns [0, J0)
-    if (J0 > 0) {
-      double a0 = 0.0, a1 = 0.0;
-      const int c0 = J0 + lane, c1 = J0 + lane + 16;
-      for (int i = 0; i < J0; ++i) {
-        const double wi = wr[i];
-        if (c0 < k) a0 = fma(wi, __ldg(R + (int64_t)i * k + c0), a0);
-        if (c1 < k) a1 = fma(wi, __ldg(R + (int64_t)i * k + c1), a1);
-      }
-      if (c0 < k) wr[c0] -= a0;
-      if (c1 < k) wr[c1] -= a1;
-    }
-    __syncwarp();
-    // forward substitution inside the block
-    for (int c = 0; c < cb; ++c) {
-      const int col = J0 + c;
-      double part = 0.0;
-      if (lane < c) part = wr[J0 + lane] * __ldg(R + (int64_t)(J0 + lane) * k + col);
-      if (lane + 16 < c) part = fma(wr[J0 + lane + 16], __ldg(R + (int64_t)(J0 + lane + 16) * k + col), part);
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
-      if (lane == 0) wr[col] = (wr[col] - part) * rinv[col];
-      __syncwarp();
-    }
-  }
+  rows_solve_upper(Wl, k, k, R, rinv);
   __syncthreads();
   for (int e = threadIdx.x; e < nr * k; e += blockDim.x) {
     const int rr = e / k, c = e % k;
@@ -676,7 +728,7 @@ LrLayout lr_layout(int p, int k) {
   L.lam = L.vec + eig::vec_doubles(k);
   L.rinv = L.lam + k;
   L.misc = L.rinv + k;
-  L.scr = L.misc + 2;
+  L.scr = L.misc + 4;
   L.total = L.scr + eig_scratch_doubles(k);
   return L;
 }
@@ -708,7 +760,7 @@ __global__ void __launch_bounds__(SNT) lr_eig_kernel(SolveArgs a, LrLayout L) {
   const int cell = blockIdx.x, k = a.k, rank = a.rank;
   double* ws = a.ws + cell * a.ws_cell;
   double* lam = ws + L.lam;
-  eig::eig_top(ws + L.C, k, k, rank, lam, ws + L.Zt, k, ws + L.vec, cnt, red, ws + L.scr);
+  eig::eig_top(ws + L.C, k, k, rank, lam, ws + L.Zt, k, ws + L.vec, cnt, red, ws + L.scr, SNT);
   if (threadIdx.x == 0) {
     double retained = 0.0;
     for (int i = 0; i < rank; ++i) retained += fmax(lam[i], 0.0);
@@ -727,6 +779,256 @@ __global__ void lr_store_kernel(SolveArgs a, LrLayout L) {
   const int64_t n = (int64_t)a.p * a.rank;
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
     store_dt(a.basis, (int64_t)cell * n + i, (float)z[i], a.basis_dtype);
+}
+
+// ---------------------------------------------------------------------------
+// The Ritz step of wide sketches when no singular values are asked for (every
+// compress call): the span of the `rank` leading Ritz vectors is the
+// complement, inside the sketch space, of the s = k - rank trailing ones, and
+// s is at most the oversampling.  So only the trailing ones are found: block
+// inverse iteration on C + delta I (its Cholesky factor from chol_kernel;
+// IV_ROWS vectors, each step W <- W R^{-1} R^{-T} and CholeskyQR2 of the
+// rows), a Rayleigh-Ritz on the IV_ROWS x IV_ROWS projection, then
+// Householder reflectors H_0 .. H_{s-1} of the s trailing vectors; the basis
+// is (W H_0 ... H_{s-1})[:, s:].  Its columns are an orthonormal basis of
+// the same Ritz subspace (not ordered by singular value); the tail mass is
+// exact: |A|^2 - trace(C) + the s trailing Ritz values.
+// ---------------------------------------------------------------------------
+constexpr int CP_MIN_K = 129;  // sketches at least this wide take the complement path
+constexpr int CP_MAX_S = 16;   // largest k - rank it handles
+constexpr int IV_ROWS = 16;    // vectors of the block inverse iteration (the 16 rows of rows_solve_*)
+constexpr int IV_ITERS = 10;
+
+// C += delta I (delta = 1e-13 of its largest diagonal entry, so the
+// Cholesky succeeds on a semi-definite C); misc[1] = trace(C), misc[2] = delta.
+__global__ void cp_shift_kernel(double* wsb, int64_t cs, LrLayout L, int k) {
+  __shared__ double red[64];
+  __shared__ double mm[2];
+  double* ws = wsb + blockIdx.x * cs;
+  double* C = ws + L.C;
+  double tr = 0.0, mx = 0.0;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) {
+    const double v = C[(int64_t)i * k + i];
+    tr += v;
+    mx = fmax(mx, v);
+  }
+  tr = eig::block_sum(tr, red);
+  eig::block_minmax(mx, mx, red, mm);
+  const double delta = 1e-13 * mm[1] + 1e-300;
+  for (int i = threadIdx.x; i < k; i += blockDim.x) C[(int64_t)i * k + i] += delta;
+  if (threadIdx.x == 0) {
+    ws[L.misc + 1] = tr;
+    ws[L.misc + 2] = delta;
+  }
+}
+
+// CholeskyQR of the nb rows of X (row stride ldx, length k): G = X X^T, its
+// Cholesky L (rank dropping as chol_kernel), X <- L^{-1} X column by column.
+__device__ inline void cp_orth_rows(double* X, int ldx, int k, int nb, double* G) {
+  const int a = threadIdx.x >> 4, b = threadIdx.x & 15;
+  if (a < nb && b < nb && b <= a) {
+    const double* xa = X + a * ldx;
+    const double* xb = X + b * ldx;
+    double s0 = 0.0, s1 = 0.0;
+    int i = 0;
+    for (; i + 1 < k; i += 2) {
+      s0 = fma(xa[i], xb[i], s0);
+      s1 = fma(xa[i + 1], xb[i + 1], s1);
+    }
+    if (i < k) s0 = fma(xa[i], xb[i], s0);
+    G[a * IV_ROWS + b] = s0 + s1;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    // G = L L^T in place (lower), rank dropping; L[j][j] stored inverted
+    for (int j = 0; j < nb; ++j) {
+      const double o = G[j * IV_ROWS + j];
+      double d = o;
+      for (int q = 0; q < j; ++q) d -= G[j * IV_ROWS + q] * G[j * IV_ROWS + q];
+      const double ri = (o > 0.0 && d > 1e-10 * o) ? 1.0 / sqrt(d) : 0.0;
+      G[j * IV_ROWS + j] = ri;
+      for (int i2 = j + 1; i2 < nb; ++i2) {
+        double v = G[i2 * IV_ROWS + j];
+        for (int q = 0; q < j; ++q) v -= G[i2 * IV_ROWS + q] * G[j * IV_ROWS + q];
+        G[i2 * IV_ROWS + j] = v * ri;
+      }
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < k; c += blockDim.x) {
+    double x[IV_ROWS];
+#pragma unroll
+    for (int q = 0; q < IV_ROWS; ++q) x[q] = q < nb ? X[q * ldx + c] : 0.0;
+#pragma unroll
+    for (int q = 0; q < IV_ROWS; ++q) {
+      if (q >= nb) break;
+      double v = x[q];
+      for (int j = 0; j < q; ++j) v -= G[q * IV_ROWS + j] * x[j];
+      x[q] = v * G[q * IV_ROWS + q];
+      X[q * ldx + c] = x[q];
+    }
+  }
+  __syncthreads();
+}
+
+// One CTA per cell: the s trailing Ritz vectors of C by block inverse
+// iteration and Rayleigh-Ritz, then their Householder reflectors (v_q in the
+// S slot, rows of length k; tau_q in the lam slot) and the tail mass.
+__global__ void __launch_bounds__(TS_NT) cp_bottom_kernel(SolveArgs a, LrLayout L, int s, int nb, int ldx) {
+  extern __shared__ double X[];  // nb (<= IV_ROWS) rows of stride ldx
+  __shared__ double G[IV_ROWS * IV_ROWS], T[IV_ROWS * IV_ROWS], Mb[IV_ROWS * 32];
+  __shared__ double Zs[IV_ROWS * IV_ROWS], vec[8 * IV_ROWS], lam[IV_ROWS], red[64];
+  __shared__ double scr[3 * IV_ROWS * IV_ROWS];
+  __shared__ int cnt[TS_NT];
+  const int cell = blockIdx.x, k = a.k;
+  double* ws = a.ws + cell * a.ws_cell;
+  const double* R = ws + L.C;
+  const double* rinv = ws + L.rinv;
+  for (int e = threadIdx.x; e < IV_ROWS * ldx; e += blockDim.x) {
+    const int r = e / ldx, c = e % ldx;
+    X[e] = (r < nb && c < k) ? eig::start_entry(r, c) : 0.0;
+  }
+  __syncthreads();
+  cp_orth_rows(X, ldx, k, nb, G);
+  cp_orth_rows(X, ldx, k, nb, G);
+  for (int it = 0; it < IV_ITERS; ++it) {
+    rows_solve_upper(X, ldx, k, R, rinv);
+    rows_solve_upper_t(X, ldx, k, R, rinv);
+    __syncthreads();
+    cp_orth_rows(X, ldx, k, nb, G);
+    cp_orth_rows(X, ldx, k, nb, G);
+  }
+  // T = (X R^T)(X R^T)^T - delta I = X C X^T, 32 columns of M = X R^T at a time
+  for (int e = threadIdx.x; e < IV_ROWS * IV_ROWS; e += blockDim.x) T[e] = 0.0;
+  __syncthreads();
+  for (int J0 = 0; J0 < k; J0 += 32) {
+    for (int e = threadIdx.x; e < IV_ROWS * 32; e += blockDim.x) {
+      const int r = e >> 5, jj = e & 31, j = J0 + jj;
+      double m = 0.0;
+      if (r < nb && j < k) {
+        const double* xr = X + r * ldx;
+        for (int i = j; i < k; ++i) m = fma(xr[i], __ldg(R + (int64_t)j * k + i), m);
+      }
+      Mb[e] = m;
+    }
+    __syncthreads();
+    {
+      const int r = threadIdx.x >> 4, q = threadIdx.x & 15;
+      double t = 0.0;
+#pragma unroll 8
+      for (int jj = 0; jj < 32; ++jj) t = fma(Mb[r * 32 + jj], Mb[q * 32 + jj], t);
+      T[r * IV_ROWS + q] += t;
+    }
+    __syncthreads();
+  }
+  // the s trailing eigenpairs of T = the s leading ones of -T
+  const double delta = ws[L.misc + 2];
+  for (int e = threadIdx.x; e < IV_ROWS * IV_ROWS; e += blockDim.x) {
+    const int r = e / IV_ROWS, q = e % IV_ROWS;
+    G[e] = (r < nb && q < nb) ? -(T[e] - (r == q ? delta : 0.0)) : 0.0;
+  }
+  __syncthreads();
+  eig::eig_top(G, IV_ROWS, nb, s, lam, Zs, IV_ROWS, vec, cnt, red, scr, s);
+  // tail = 1 - (trace C - sum of the trailing Ritz values) / |A|^2
+  if (threadIdx.x == 0) {
+    double trailing = 0.0;
+    for (int q = 0; q < s; ++q) trailing += fmax(-lam[q], 0.0);
+    const double retained = ws[L.misc + 1] - (double)k * delta - trailing;
+    const double nrm = ws[L.misc];
+    const double t = nrm > 0.0 ? 1.0 - retained / nrm : 0.0;
+    a.tail[cell] = t > 0.0 ? t : 0.0;
+  }
+  // the trailing Ritz vectors X_s = Zs X (s rows), column by column in place
+  for (int c = threadIdx.x; c < k; c += blockDim.x) {
+    double x[IV_ROWS];
+#pragma unroll
+    for (int q = 0; q < IV_ROWS; ++q) x[q] = q < nb ? X[q * ldx + c] : 0.0;
+    for (int q = 0; q < s; ++q) {
+      double v = 0.0;
+#pragma unroll
+      for (int j = 0; j < IV_ROWS; ++j) v = fma(Zs[q * IV_ROWS + j], x[j], v);
+      X[q * ldx + c] = v;
+    }
+  }
+  __syncthreads();
+  // Householder QR of X_s^T (k x s): reflector q on entries q .. k-1
+  double* V = ws + L.S;     // v_q as rows of length k
+  double* tau = ws + L.lam;
+  for (int q = 0; q < s; ++q) {
+    double* xq = X + q * ldx;
+    double part = 0.0;
+    for (int i = q + 1 + threadIdx.x; i < k; i += blockDim.x) part = fma(xq[i], xq[i], part);
+    const double sig = eig::block_sum(part, red);
+    const double x0 = xq[q];
+    double tq = 0.0, v0 = x0;
+    if (sig > 0.0 || x0 < 0.0) {
+      const double nx = sqrt(fma(x0, x0, sig));
+      const double alpha = x0 >= 0.0 ? -nx : nx;
+      v0 = x0 - alpha;
+      tq = 2.0 / fma(v0, v0, sig);
+    }
+    for (int i = threadIdx.x; i < k; i += blockDim.x) V[(int64_t)q * k + i] = i < q ? 0.0 : (i == q ? v0 : xq[i]);
+    if (threadIdx.x == 0) tau[q] = tq;
+    __syncthreads();
+    const double* vq = V + (int64_t)q * k;
+    for (int q2 = q + 1; q2 < s; ++q2) {
+      double* y = X + q2 * ldx;
+      double pd = 0.0;
+      for (int i = q + threadIdx.x; i < k; i += blockDim.x) pd = fma(vq[i], y[i], pd);
+      const double dot = eig::block_sum(pd, red) * tq;
+      for (int i = q + threadIdx.x; i < k; i += blockDim.x) y[i] = fma(-dot, vq[i], y[i]);
+      __syncthreads();
+    }
+  }
+}
+
+// s = 0: the basis is the sketch space, the tail 1 - trace(C) / |A|^2.
+__global__ void cp_tail_kernel(SolveArgs a, LrLayout L, int n_cells) {
+  for (int c = threadIdx.x; c < n_cells; c += blockDim.x) {
+    const double* ws = a.ws + c * a.ws_cell;
+    const double nrm = ws[L.misc];
+    const double retained = ws[L.misc + 1];
+    const double t = nrm > 0.0 ? 1.0 - retained / nrm : 0.0;
+    a.tail[c] = t > 0.0 ? t : 0.0;
+  }
+}
+
+// basis rows = (w H_0 ... H_{s-1})[s:] for every row w of W (16 rows per
+// CTA, 16 lanes per row); the reflectors from cp_bottom_kernel.
+__global__ void __launch_bounds__(TS_NT) cp_complement_kernel(SolveArgs a, LrLayout L, int64_t w_off, int s) {
+  extern __shared__ double Wl[];  // TS_ROWS x k
+  const int cell = blockIdx.y, p = a.p, k = a.k, rank = a.rank;
+  const double* ws = a.ws + cell * a.ws_cell;
+  const double* W = ws + w_off;
+  const double* V = ws + L.S;
+  const double* tau = ws + L.lam;
+  const int row0 = blockIdx.x * TS_ROWS;
+  const int nr = min(TS_ROWS, p - row0);
+  for (int e = threadIdx.x; e < TS_ROWS * k; e += blockDim.x) {
+    const int r = e / k, c = e % k;
+    Wl[e] = r < nr ? W[(int64_t)(row0 + r) * k + c] : 0.0;
+  }
+  __syncthreads();
+  const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
+  double* wr = Wl + r * k;
+  for (int q = 0; q < s; ++q) {
+    const double* vq = V + (int64_t)q * k;
+    double part = 0.0;
+    for (int i = q + lane; i < k; i += 16) part = fma(wr[i], __ldg(vq + i), part);
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
+    const double dot = part * tau[q];
+    for (int i = q + lane; i < k; i += 16) wr[i] = fma(-dot, __ldg(vq + i), wr[i]);
+    __syncwarp();
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < nr * rank; e += blockDim.x) {
+    const int rr = e / rank, c = e % rank;
+    const double v = Wl[rr * k + s + c];
+    const int64_t o = ((int64_t)cell * p + row0 + rr) * rank + c;
+    if (a.side == KVC_SIDE_RIGHT) static_cast<double*>(a.basis)[o] = v;
+    else store_dt(a.basis, o, (float)v, a.basis_dtype);
+  }
 }
 
 int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
@@ -779,6 +1081,34 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
   if (a.side == KVC_SIDE_LEFT) rc = gemm(ws + cur, cs, k, 1, ws + oth, cs, k, 0, ws + L.C, cs, k, k, k, p);
   else rc = gemm(ws + oth, cs, k, 1, ws + oth, cs, k, 0, ws + L.C, cs, k, k, k, p);
   if (rc) return rc;
+  const int s = k - a.rank;
+  if (k >= CP_MIN_K && s <= CP_MAX_S && !a.sv2) {
+    // the complement of the s trailing Ritz vectors
+    const int cp_smem = (int)(sizeof(double) * (size_t)TS_ROWS * k);
+    const int ldx = k | 1;  // odd row stride: the rows' Gram reads are conflict-free
+    const int iv_smem = (int)(sizeof(double) * (size_t)IV_ROWS * ldx);
+    if ((e = cudaFuncSetAttribute(cp_complement_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cp_smem)) ==
+        cudaSuccess)
+      e = cudaFuncSetAttribute(cp_bottom_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, iv_smem);
+    if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+    if (s > 0) {
+      cp_shift_kernel<<<n_cells, 256, 0, st>>>(ws, cs, L, k);
+      if ((rc = check_launch("cp_shift_kernel"))) return rc;
+      chol_kernel<<<n_cells, CH_NT, chol_smem, st>>>(ws + L.C, k, nbmax, cs, ws + L.rinv, cs);
+      if ((rc = check_launch("chol_kernel"))) return rc;
+      cp_bottom_kernel<<<n_cells, TS_NT, iv_smem, st>>>(a, L, s, std::min(IV_ROWS, std::max(s + 8, s)), ldx);
+      if ((rc = check_launch("cp_bottom_kernel"))) return rc;
+    } else {
+      // the sketch space itself: tail = 1 - trace(C) / |A|^2
+      cp_shift_kernel<<<n_cells, 256, 0, st>>>(ws, cs, L, k);
+      if ((rc = check_launch("cp_shift_kernel"))) return rc;
+      cp_tail_kernel<<<1, 64, 0, st>>>(a, L, n_cells);
+      if ((rc = check_launch("cp_tail_kernel"))) return rc;
+    }
+    const dim3 grid((p + TS_ROWS - 1) / TS_ROWS, n_cells);
+    cp_complement_kernel<<<grid, TS_NT, cp_smem, st>>>(a, L, cur, s);
+    return check_launch("cp_complement_kernel");
+  }
   lr_eig_kernel<<<n_cells, SNT, 0, st>>>(a, L);
   if ((rc = check_launch("lr_eig_kernel"))) return rc;
   // basis = W Zt^T (p x rank)
@@ -867,11 +1197,12 @@ extern "C" int kvc_sketch_solve(int n_cells, int mode, int side, int p, int64_t 
     return check_launch("sketch_solve_small_kernel");
   }
   if (mode == KVC_SVD_EXACT && p <= EX_P) {
-    const size_t smem = exact_small_smem_bytes(p);
+    const int in_smem = exact_small_smem_bytes_vectors(p, rank) <= SMEM_LIMIT;
+    const size_t smem = in_smem ? exact_small_smem_bytes_vectors(p, rank) : exact_small_smem_bytes(p);
     cudaError_t e = cudaFuncSetAttribute(exact_solve_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
     if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-    exact_solve_small_kernel<<<n_cells, SM_NT, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    exact_solve_small_kernel<<<n_cells, SM_NT, smem, static_cast<cudaStream_t>(stream)>>>(a, in_smem);
     return check_launch("exact_solve_small_kernel");
   }
   if (mode == KVC_SVD_RANDOMISED) return lr_solve(a, n_cells, static_cast<cudaStream_t>(stream));

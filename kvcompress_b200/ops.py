@@ -271,8 +271,12 @@ def gram(cells: Sequence[torch.Tensor], omega: torch.Tensor | None) -> torch.Ten
 
 def sketch_solve(g: torch.Tensor, *, mode: int, side: int, p: int, n_other: int, k: int, rank: int,
                  n_power: int, omega: torch.Tensor | None, basis_dtype: torch.dtype,
-                 gram_stride: int | None = None):
-    """Run the per-cell small solver; returns ``(basis, tail, sv2)``."""
+                 gram_stride: int | None = None, want_sv2: bool = True):
+    """Run the per-cell small solver; returns ``(basis, tail, sv2)``.
+
+    ``want_sv2=False`` asks for no squared singular values (``sv2`` is then
+    None): wide sketches then take the solver's complement path, whose basis
+    spans the same Ritz subspace without ordering its columns."""
     n = int(g.shape[0])
     dev = g.device
     L = lib()
@@ -281,7 +285,7 @@ def sketch_solve(g: torch.Tensor, *, mode: int, side: int, p: int, n_other: int,
     else:
         basis = torch.empty(n, p, rank, dtype=torch.float64, device=dev)
     tail = torch.empty(n, dtype=torch.float64, device=dev)
-    sv2 = torch.empty(n, rank, dtype=torch.float64, device=dev)
+    sv2 = torch.empty(n, rank, dtype=torch.float64, device=dev) if want_sv2 else None
     kk = k if mode == KVC.SVD_RANDOMISED else 0
     ws_n = L.kvc_sketch_solve_workspace_bytes(n, mode, p, kk)
     ws = workspace(ws_n, dev)
@@ -289,7 +293,8 @@ def sketch_solve(g: torch.Tensor, *, mode: int, side: int, p: int, n_other: int,
     with _on(dev), _Stage("sketch_solve", 1, g.numel() * 8):
         check(L.kvc_sketch_solve(n, mode, side, p, n_other, kk, rank, n_power, g.data_ptr(), stride,
                                  omega.data_ptr() if omega is not None else None, basis.data_ptr(),
-                                 _code(basis.dtype), sv2.data_ptr(), tail.data_ptr(), ws.data_ptr(),
+                                 _code(basis.dtype), sv2.data_ptr() if sv2 is not None else None, tail.data_ptr(),
+                                 ws.data_ptr(),
                                  ws.numel(), _stream()), "kvc_sketch_solve")
     return basis, tail, sv2
 

@@ -6,6 +6,7 @@ import numpy as np
 import torch
 
 import oracle
+import oracle.jolt as _oj
 
 TORCH_DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
 NP_DT = {torch.float32: "f32", torch.float16: "f16", torch.bfloat16: "bf16"}
@@ -60,8 +61,8 @@ def recon_rows(core, u_token, u_feature, dt: str, rows: np.ndarray, t: int) -> n
     u_token = np.asarray(u_token, np.float32)
     u_feature = np.asarray(u_feature, np.float32)
     h, tt = rows // t, rows % t
-    tmp = oracle.round_to(np.einsum("nar,na->nr", core[h], u_token[tt], dtype=np.float32), dt)
-    return oracle.matmul_round(tmp, u_feature.T, dt)
+    tmp = _oj.round_to(np.einsum("nar,na->nr", core[h], u_token[tt], dtype=np.float32), dt)
+    return _oj.matmul_round(tmp, u_feature.T, dt)
 
 
 def near_ties(x_rows, recon, dt: str, proj, scale, margin: float = 1e-3) -> np.ndarray:
@@ -69,7 +70,7 @@ def near_ties(x_rows, recon, dt: str, proj, scale, margin: float = 1e-3) -> np.n
     a rounding boundary (symmetric scales, zero point 0): the fp32 rotation may
     round either way there.  The rotated residual is evaluated in float64 from
     the residual in the cell dtype (jolt.py:311, residual.py:201-216)."""
-    resid = oracle.dt_op(lambda a, b: a - b, dt, np.asarray(x_rows, np.float32), recon)
+    resid = _oj.dt_op(lambda a, b: a - b, dt, np.asarray(x_rows, np.float32), recon)
     rot = np.asarray(resid, np.float64) @ np.asarray(proj, np.float64).T
     v = rot / np.asarray(scale, np.float64)
     return np.abs(v - np.floor(v) - 0.5) < margin

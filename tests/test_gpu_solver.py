@@ -111,6 +111,27 @@ def test_randomised_right(n, p, k, rank):
     assert np.abs(u.T @ u - np.eye(rank)).max() < 1e-8
 
 
+@pytest.mark.parametrize("n,p,k,rank", [(4096, 1024, 513, 512), (4096, 1024, 513, 503), (3000, 300, 150, 150),
+                                        (5000, 700, 300, 290)])
+def test_randomised_right_complement(n, p, k, rank):
+    """Wide sketches without singular values (every compress call): the basis
+    spans the top-rank Ritz subspace (columns not ordered) and the tail mass
+    is the exact one."""
+    a = _matrix(n, p, seed=3 * p + k, decay=2.0)
+    rng = np.random.default_rng(p + 1)
+    om = rng.standard_normal((p, k)).astype(np.float32)
+    H, u_ref, w_ref, tail_ref = _right_randomised(a, om.astype(np.float64), rank)
+    gram = torch.from_numpy(np.concatenate([H.ravel(), [np.trace(H)]])[None]).cuda()
+    m, tail, sv2 = ops.sketch_solve(gram, mode=KVC.SVD_RANDOMISED, side=KVC.SIDE_RIGHT, p=p, n_other=n, k=k,
+                                    rank=rank, n_power=2, omega=torch.from_numpy(om).cuda(),
+                                    basis_dtype=torch.float64, want_sv2=False)
+    assert sv2 is None
+    u = a @ m[0].cpu().numpy()
+    assert abs(tail[0].item() - tail_ref) < 1e-9
+    assert np.abs(u.T @ u - np.eye(rank)).max() < 1e-8
+    assert _rel(u @ u.T, u_ref @ u_ref.T) < 1e-7
+
+
 @pytest.mark.parametrize("p,rank,side", [(64, 1, KVC.SIDE_LEFT), (64, 32, KVC.SIDE_LEFT), (128, 1, KVC.SIDE_LEFT),
                                          (128, 64, KVC.SIDE_LEFT), (128, 128, KVC.SIDE_LEFT),
                                          (96, 48, KVC.SIDE_RIGHT), (200, 100, KVC.SIDE_LEFT),

@@ -225,9 +225,10 @@ def _policy(p):
 def _exact_codes(x, recon, proj, scale, bits, d):
     """Packed codes of the float64 rotated residual (the rounding away from ties)."""
     import oracle
+    import oracle.jolt
 
     m, t, _ = x.shape
-    resid = oracle.dt_op(lambda a, b: a - b, "bf16", f32(x).reshape(m * t, d), recon)
+    resid = oracle.jolt.dt_op(lambda a, b: a - b, "bf16", f32(x).reshape(m * t, d), recon)
     rot = (np.asarray(resid, np.float64) @ proj.cpu().numpy().astype(np.float64).T)
     qmax = (1 << (bits - 1)) - 1
     q = np.clip(np.rint(rot / np.asarray(scale, np.float64)), -qmax - 1, qmax).astype(np.int32)
