@@ -26,10 +26,65 @@ constexpr int TB = 64;   // output tile edge
 constexpr int RB = 32;   // rows staged per iteration
 constexpr int NT = 256;  // threads per block (16 x 16, 4x4 outputs each)
 
+// One operand's RB x TB stage (rows r0.., columns c0.. of a row-major matrix
+// with ld columns, the columns past ncols zero) held in registers until it
+// is stored to shared memory, so the next stage's loads are in flight while
+// the current one is multiplied.  16-bit operands whose row length is a
+// multiple of 8 on 16-byte boundaries take one 16-byte load per thread.
+template <typename T>
+struct StageRegs {
+  uint4 v;
+  float s[RB * TB / NT];
+
+  __device__ __forceinline__ void load(const T* __restrict__ base, int64_t r0, int64_t r_end, int c0, int ncols,
+                                       int ld, bool vec, const float* __restrict__ extra, int q1) {
+    if constexpr (sizeof(T) == 2) {
+      if (vec) {
+        const int rr = threadIdx.x >> 3, col = c0 + ((threadIdx.x & 7) << 3);
+        const int64_t r = r0 + rr;
+        v = (r < r_end && col < ncols) ? __ldg(reinterpret_cast<const uint4*>(base + r * ld + col))
+                                       : make_uint4(0u, 0u, 0u, 0u);
+        return;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < RB * TB / NT; ++u) {
+      const int e = threadIdx.x + u * NT;
+      const int rr = e / TB, cc = e % TB;
+      const int64_t r = r0 + rr;
+      const int c = c0 + cc;
+      float val = 0.f;
+      if (r < r_end) {
+        if (c < q1) val = Elt<T>::to_f32(base[r * ld + c]);
+        else if (c < ncols) val = extra[r * (ncols - q1) + (c - q1)];
+      }
+      s[u] = val;
+    }
+  }
+
+  __device__ __forceinline__ void store(float (*sm)[TB], bool vec) {
+    if constexpr (sizeof(T) == 2) {
+      if (vec) {
+        const int rr = threadIdx.x >> 3, cb = (threadIdx.x & 7) << 3;
+        const T* e = reinterpret_cast<const T*>(&v);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) sm[rr][cb + q] = Elt<T>::to_f32(e[q]);
+        return;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < RB * TB / NT; ++u) {
+      const int e = threadIdx.x + u * NT;
+      sm[e / TB][e % TB] = s[u];
+    }
+  }
+};
+
 template <typename TA, typename TB1>
 __global__ void __launch_bounds__(NT)
 atb_partial_kernel(CellPtrs A, CellPtrs B1, const float* __restrict__ B2, int64_t rows, int p,
-                   int q1, int q2, int chunks, int64_t chunk_rows, float* __restrict__ partial) {
+                   int q1, int q2, int chunks, int64_t chunk_rows, float* __restrict__ partial, int vec_a,
+                   int vec_b) {
   const int cell = blockIdx.z;
   const int chunk = blockIdx.x;
   const int q = q1 + q2;
@@ -49,22 +104,18 @@ atb_partial_kernel(CellPtrs A, CellPtrs B1, const float* __restrict__ B2, int64_
 
   const int64_t r_begin = (int64_t)chunk * chunk_rows;
   const int64_t r_end = r_begin + chunk_rows < rows ? r_begin + chunk_rows : rows;
+  StageRegs<TA> ra;
+  StageRegs<TB1> rb;
+  ra.load(a, r_begin, r_end, i0, p, p, vec_a, nullptr, p);
+  rb.load(b1, r_begin, r_end, j0, q, q1, vec_b, B2, q1);
   for (int64_t r0 = r_begin; r0 < r_end; r0 += RB) {
-    for (int e = threadIdx.x; e < RB * TB; e += NT) {
-      const int rr = e / TB, cc = e % TB;
-      const int64_t r = r0 + rr;
-      float va = 0.f, vb = 0.f;
-      if (r < r_end) {
-        const int ia = i0 + cc;
-        if (ia < p) va = Elt<TA>::to_f32(a[r * p + ia]);
-        const int jb = j0 + cc;
-        if (jb < q1) vb = Elt<TB1>::to_f32(b1[r * q1 + jb]);
-        else if (jb < q) vb = B2[r * q2 + (jb - q1)];
-      }
-      sA[rr][cc] = va;
-      sB[rr][cc] = vb;
-    }
+    ra.store(sA, vec_a);
+    rb.store(sB, vec_b);
     __syncthreads();
+    if (r0 + RB < r_end) {
+      ra.load(a, r0 + RB, r_end, i0, p, p, vec_a, nullptr, p);
+      rb.load(b1, r0 + RB, r_end, j0, q, q1, vec_b, B2, q1);
+    }
 #pragma unroll 4
     for (int rr = 0; rr < RB; ++rr) {
       float av[4];
@@ -227,6 +278,19 @@ ChunkPlan plan_chunks(int n_cells, int64_t rows, int p, int q) {
   return pl;
 }
 
+// 16-bit rows of a multiple of 8 elements, every cell's base on a 16-byte boundary
+template <typename T>
+bool rows_vectorizable(const CellPtrs& x, int n_cells, int width) {
+  if constexpr (sizeof(T) != 2) {
+    return false;
+  } else {
+    if (width % 8 != 0) return false;
+    for (int c = 0; c < n_cells; ++c)
+      if (reinterpret_cast<uintptr_t>(x.p[c]) & 15u) return false;
+    return true;
+  }
+}
+
 template <typename TA, typename TB1>
 int launch_partial(int n_cells, const CellPtrs& a, const CellPtrs& b1, const float* b2, int64_t rows,
                    int p, int q1, int q2, const ChunkPlan& pl, float* partial, cudaStream_t st) {
@@ -237,8 +301,10 @@ int launch_partial(int n_cells, const CellPtrs& a, const CellPtrs& b1, const flo
     return check_launch("atb_skinny_kernel");
   }
   dim3 grid(pl.chunks, pl.tiles, n_cells);
+  const int vec_a = rows_vectorizable<TA>(a, n_cells, p);
+  const int vec_b = q2 == 0 && rows_vectorizable<TB1>(b1, n_cells, q1);
   atb_partial_kernel<TA, TB1><<<grid, NT, 0, st>>>(a, b1, b2, rows, p, q1, q2, pl.chunks,
-                                                   pl.chunk_rows, partial);
+                                                   pl.chunk_rows, partial, vec_a, vec_b);
   return check_launch("atb_partial_kernel");
 }
 

@@ -797,7 +797,7 @@ __global__ void lr_store_kernel(SolveArgs a, LrLayout L) {
 constexpr int CP_MIN_K = 129;  // sketches at least this wide take the complement path
 constexpr int CP_MAX_S = 16;   // largest k - rank it handles
 constexpr int IV_ROWS = 16;    // vectors of the block inverse iteration (the 16 rows of rows_solve_*)
-constexpr int IV_ITERS = 10;
+constexpr int IV_ITERS = 12;
 
 // C += delta I (delta = 1e-13 of its largest diagonal entry, so the
 // Cholesky succeeds on a semi-definite C); misc[1] = trace(C), misc[2] = delta.
@@ -1096,7 +1096,8 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
       if ((rc = check_launch("cp_shift_kernel"))) return rc;
       chol_kernel<<<n_cells, CH_NT, chol_smem, st>>>(ws + L.C, k, nbmax, cs, ws + L.rinv, cs);
       if ((rc = check_launch("chol_kernel"))) return rc;
-      cp_bottom_kernel<<<n_cells, TS_NT, iv_smem, st>>>(a, L, s, std::min(IV_ROWS, std::max(s + 8, s)), ldx);
+      // all IV_ROWS vectors: the row solves process 16 rows whatever their number
+      cp_bottom_kernel<<<n_cells, TS_NT, iv_smem, st>>>(a, L, s, IV_ROWS, ldx);
       if ((rc = check_launch("cp_bottom_kernel"))) return rc;
     } else {
       // the sketch space itself: tail = 1 - trace(C) / |A|^2

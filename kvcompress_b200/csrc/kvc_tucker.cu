@@ -355,15 +355,44 @@ __global__ void __launch_bounds__(256) rowmat_skinny_kernel(CellPtrs A, const do
   __syncthreads();
   const T* a = static_cast<const T*>(A.p[cell]);
   T* o = static_cast<T*>(out.p[cell]);
+  // 16-bit rows of a multiple of 8 elements on 16-byte boundaries: the whole
+  // row in flight at once (up to eight 16-byte loads per thread)
+  const bool vec = sizeof(T) == 2 && K % 8 == 0 && (reinterpret_cast<uintptr_t>(a) & 15u) == 0;
   for (int64_t r = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; r < rows; r += (int64_t)gridDim.x * blockDim.x) {
     float acc[SKN];
 #pragma unroll
     for (int j = 0; j < SKN; ++j) acc[j] = 0.f;
-    for (int k = 0; k < K; ++k) {
-      const float av = Elt<T>::to_f32(a[r * K + k]);
+    bool done = false;
+    if constexpr (sizeof(T) == 2) {
+      if (vec) {
+        done = true;
+        uint4 raw[SKK / 8];
+        const uint4* src = reinterpret_cast<const uint4*>(a + r * K);
 #pragma unroll
-      for (int j = 0; j < SKN; ++j)
-        if (j < N) acc[j] = fmaf(av, sM[k * N + j], acc[j]);
+        for (int c = 0; c < SKK / 8; ++c)
+          if (c < K / 8) raw[c] = __ldg(src + c);
+#pragma unroll
+        for (int c = 0; c < SKK / 8; ++c) {
+          if (c >= K / 8) break;
+          const T* e = reinterpret_cast<const T*>(&raw[c]);
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const float av = Elt<T>::to_f32(e[q]);
+            const int k = c * 8 + q;
+#pragma unroll
+            for (int j = 0; j < SKN; ++j)
+              if (j < N) acc[j] = fmaf(av, sM[k * N + j], acc[j]);
+          }
+        }
+      }
+    }
+    if (!done) {
+      for (int k = 0; k < K; ++k) {
+        const float av = Elt<T>::to_f32(a[r * K + k]);
+#pragma unroll
+        for (int j = 0; j < SKN; ++j)
+          if (j < N) acc[j] = fmaf(av, sM[k * N + j], acc[j]);
+      }
     }
 #pragma unroll
     for (int j = 0; j < SKN; ++j)
@@ -482,7 +511,7 @@ extern "C" int kvc_apply_basis(int n_cells, const void* const* a, int64_t rows, 
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p <= SKK && r <= SKN) {
-    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 256), ceil_div(4LL * num_sms(), n_cells)));
+    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 256), ceil_div(16LL * num_sms(), n_cells)));
     KVC_DISPATCH_DTYPE(dtype, T,
                        rowmat_skinny_kernel<T><<<dim3(blocks, n_cells), 256, 0, st>>>(aa, mat, rows, p, r, o));
     return check_launch("rowmat_skinny_kernel");
