@@ -158,6 +158,11 @@ struct EncArgs {
   CellPtrs core, ut;
   int64_t t_tok;  // tokens per head
   int rows_direct;
+  // STATS: [cell] the float bits of max |R| (atomicMax; for the fp16
+  // quantise mode); QUANT (fp16 mode): [cell][1 + d] = 2^E (R's scale), then
+  // per output feature n the epilogue's factor 2^-(E + G_n)
+  uint32_t* rmax;
+  const float* fscale;
 };
 
 // Bits of the bf16 Tucker term of a tile's row ptid (rd = 1): from the
@@ -252,6 +257,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         __syncwarp();
         cur_cell = cell;
       }
+      uint32_t rm = 0u;  // float bits of this thread's max |R| (monotonic for non-negative floats)
       if (A.rt > 0 && row < A.rows) {
         uint8_t* Bs = smem + st * L::B_BYTES;
         const float* ts = reinterpret_cast<const float*>(smem + L::OFF_T + st * L::T_BYTES) + ptid * RDM;
@@ -261,6 +267,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const uint32_t th = enc_row_term(A, smem + L::OFF_T + st * L::T_BYTES, cs, ptid, row - ptid);
           const uint32_t t2 = th | (th << 16);
           const uint4* u4 = reinterpret_cast<const uint4*>(ub);
+          uint32_t mh = 0u;  // max of the bf16 magnitude bits (both halves)
 #pragma unroll
           for (int c = 0; c < HC; ++c) {
             uint4* slot = reinterpret_cast<uint4*>(Bs + sw128_off(ptid, (part * HC + c) * 8, TILE_M));
@@ -271,7 +278,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             x.z = bf16x2_sub(x.z, bf16x2_mul(t2, u.z));
             x.w = bf16x2_sub(x.w, bf16x2_mul(t2, u.w));
             *slot = x;
+            mh = __vmaxu2(mh, __vmaxu2(__vmaxu2(x.x & 0x7FFF7FFFu, x.y & 0x7FFF7FFFu),
+                                       __vmaxu2(x.z & 0x7FFF7FFFu, x.w & 0x7FFF7FFFu)));
           }
+          rm = max(mh & 0xFFFFu, mh >> 16) << 16;
         } else {
           const float4 tv = *reinterpret_cast<const float4*>(ts);
           const float4* u4 = reinterpret_cast<const float4*>(u32);
@@ -288,10 +298,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
               rec = fmaf(tv.z, u.z, rec);
               rec = fmaf(tv.w, u.w, rec);
               xv[e] = Elt<__nv_bfloat16>::round(xv[e] - Elt<__nv_bfloat16>::round(rec));
+              rm = max(rm, __float_as_uint(fabsf(xv[e])));
             }
             *slot = pack8_bf16(xv);
           }
         }
+      }
+      if (A.rmax) {
+        const uint32_t wm = __reduce_max_sync(0xffffffffu, rm);
+        if (lane == 0 && wm) atomicMax(A.rmax + cell, wm);
       }
       fence_async_smem();
       mbar_arrive(&full[st]);
@@ -465,8 +480,9 @@ size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 constexpr int kMaxCtas = 1024;  // grid cap of the persistent kernels
 
 // min / max arrays to their identities (ordered ints of +inf / -inf).
-__global__ void minmax_init_kernel(int32_t* mm, int n_cells, int d) {
+__global__ void minmax_init_kernel(int32_t* mm, int n_cells, int d, uint32_t* rmax) {
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (rmax && i < n_cells) rmax[i] = 0u;
   if (i >= n_cells * 2 * d) return;
   const bool is_max = (i / d) & 1;
   mm[i] = is_max ? (int32_t)0x807FFFFF : (int32_t)0x7F800000;
@@ -535,6 +551,43 @@ __global__ void prep_quant_b_kernel(const float* __restrict__ proj, CellPtrs sca
   }
 }
 
+// The fp16 form of those B images (the quantise pass's fp16 mode, d = 128,
+// per-channel scales, Tucker factors present).  Two fp16 terms hold a 22-bit
+// split of Pi[n][k] / s_n * 2^G_n, G_n putting the row's largest magnitude
+// in [2^13, 2^14); the rows R enter the MMA as fp16 scaled by 2^E, E from the
+// cell's max |R| (the stats pass) the same way.  Both scalings are exact
+// powers of two and fp16 x fp16 products are exact in fp32, so the
+// epilogue's factor 2^-(E + G_n) gives R~ / s with an error below 2^-21 of
+// the largest term.  One block per (row n, cell), one thread per k.
+__global__ void prep_quant_b16_kernel(const float* __restrict__ proj, CellPtrs scale,
+                                      const uint32_t* __restrict__ rmax, int d, uint8_t* out, float* fscale) {
+  __shared__ float red[32];
+  const int cell = blockIdx.y, n = blockIdx.x, k = threadIdx.x;
+  const float v = k < d ? __fdiv_rn(proj[n * d + k], static_cast<const float*>(scale.p[cell])[n]) : 0.f;
+  float m = fabsf(v);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+  if ((k & 31) == 0) red[k >> 5] = m;
+  __syncthreads();
+  m = 0.f;
+  for (int w = 0; w < (int)(blockDim.x + 31) / 32; ++w) m = fmaxf(m, red[w]);
+  const int G = (m > 0.f && isfinite(m)) ? 13 - ilogbf(m) : 0;
+  const float rm = __uint_as_float(rmax[cell]);
+  const int E = (rm > 0.f && isfinite(rm)) ? 13 - ilogbf(rm) : 0;
+  if (k < d) {
+    const float b = ldexpf(v, G);
+    const __half hi = __float2half_rn(b);
+    const __half lo = __float2half_rn(b - __half2float(hi));
+    uint8_t* base = out + (size_t)cell * 3 * d * d * 2;
+    *reinterpret_cast<__half*>(base + sw128_off(n, k, d)) = hi;
+    *reinterpret_cast<__half*>(base + (size_t)d * d * 2 + sw128_off(n, k, d)) = lo;
+  }
+  if (k == 0) {
+    fscale[(size_t)cell * (1 + d) + 1 + n] = ldexpf(1.f, -(E + G));
+    if (n == 0) fscale[(size_t)cell * (1 + d)] = ldexpf(1.f, E);
+  }
+}
+
 // Quantiser of the fused encode.  The reference computes
 // q = rint(fl32(fl32(v / s) + zp)) (round half to even, then clamp), v the
 // fp32 rotated residual.  Here 1/s is folded into the B image (Pi / s in
@@ -548,10 +601,11 @@ __global__ void prep_quant_b_kernel(const float* __restrict__ proj, CellPtrs sca
 // quantise pass, row-major: A = R in TMEM (one row per lane), B = Pi in
 // shared memory; thread = row in the epilogue, codes stored directly
 // ------------------------------------------------------------------------
-template <int D, int RDM, int NS>
+template <int D, int RDM, int NS, bool F16 = false>
 struct QuantLayout {
+  static constexpr int NTERM = F16 ? 2 : 3;
   static constexpr uint32_t B_TERM = D * D * 2;
-  static constexpr uint32_t B_BYTES = 3 * B_TERM;                 // Pi / s of the cell in three terms
+  static constexpr uint32_t B_BYTES = NTERM * B_TERM;             // Pi / s of the cell in NTERM terms
   static constexpr uint32_t X_BYTES = TILE_M * D * 2;             // x tile (TMA, SWIZZLE_128B)
   static constexpr uint32_t T_BYTES = TILE_M * RDM * 4;           // Tucker row term of a tile
   static constexpr uint32_t U_BYTES = RDM == 1 ? D * 2 : D * 16;  // u_feature: bf16 [j] or fp32 [j][4]
@@ -562,7 +616,8 @@ struct QuantLayout {
   static constexpr uint32_t OFF_T = OFF_Q + 8 * Q_BYTES;
   static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
   static constexpr uint32_t OFF_S = OFF_U + 4 * U_BYTES;
-  static constexpr uint32_t OFF_CORE = OFF_S + 8 * S_BYTES;   // per transform warp: core[h] of the cell
+  static constexpr uint32_t OFF_C = OFF_S + 8 * S_BYTES;       // fp16 mode, per epilogue warp: 2^-(E + G_n)
+  static constexpr uint32_t OFF_CORE = OFF_C + (F16 ? 8 * S_BYTES : 0);  // per transform warp: core[h] of the cell
   static constexpr uint32_t OFF_RING = OFF_CORE + 4 * CORE_MAX * 4;  // tile ids drawn by the producer
   static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
   static constexpr uint32_t NBAR = 2 * NS + 2 * 2 + 4 + 2;  // loaded, empty, A full/free x2, acc full/empty x2, B free/ready
@@ -570,11 +625,12 @@ struct QuantLayout {
   static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;
 };
 
-template <int D, bool SYM, int RDM, int NS>
+template <int D, bool SYM, int RDM, int NS, bool F16 = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_quant_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ TmaMaps cmaps,
                     const __grid_constant__ EncArgs A, const uint8_t* bimg) {
-  using L = QuantLayout<D, RDM, NS>;
+  static_assert(!F16 || RDM == 1, "the fp16 mode takes rank-1 row terms");
+  using L = QuantLayout<D, RDM, NS, F16>;
   static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   constexpr uint32_t ACOLS = D / 2;  // TMEM columns of one A buffer (bf16 pairs)
   extern __shared__ uint8_t smem_raw[];
@@ -622,6 +678,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + warp * L::U_BYTES);  // [j]
     float* cs = reinterpret_cast<float*>(smem + L::OFF_CORE) + warp * CORE_MAX;      // [h]
     int cur_cell = -1;
+    float es = 1.f;  // fp16 mode: 2^E of the cell
     for (int it = 0;; ++it) {
       const int st = it % NS, b = it & 1;
       if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x171)) break;
@@ -646,6 +703,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         if (A.rows_direct)
           for (int j = lane; j < (int)(A.rows / A.t_tok); j += 32) cs[j] = load_dt(A.core.p[cell], j, KVC_BF16);
+        if (F16) es = A.fscale[(size_t)cell * (1 + D)];
         __syncwarp();
         cur_cell = cell;
       }
@@ -679,6 +737,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             r[4 * c + 1] = bf16x2_sub(r[4 * c + 1], bf16x2_mul(t2, u.y));
             r[4 * c + 2] = bf16x2_sub(r[4 * c + 2], bf16x2_mul(t2, u.z));
             r[4 * c + 3] = bf16x2_sub(r[4 * c + 3], bf16x2_mul(t2, u.w));
+          }
+        }
+        if constexpr (F16) {
+          // R * 2^E in fp16: exact for every bf16 value down to 2^-14 of the
+          // scaled range (smaller ones are negligible against the step)
+#pragma unroll
+          for (int i = 0; i < D / 2; ++i) {
+            const float lo = __uint_as_float(r[i] << 16) * es, hi = __uint_as_float(r[i] & 0xFFFF0000u) * es;
+            const __half2 h2 = __floats2half2_rn(lo, hi);
+            r[i] = *reinterpret_cast<const uint32_t*>(&h2);
           }
         }
         // the MMAs of tile it - 2 read this A buffer last
@@ -764,7 +832,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   } else if (warp == MMA_WARP) {
     // D[row][feature] = sum_k R[row][k] (Pi / s)[feature][k]
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(TILE_M, D, true);
+      const uint32_t idesc = idesc_f16(TILE_M, D, !F16);
       int it = 0, cur_cell = -1, nb = 0;
       bool ended = false;
       for (;; ++it) {
@@ -786,8 +854,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           mbar_expect_tx(bready, L::B_BYTES);
 #pragma unroll
-          for (int term = 0; term < 3; ++term)
-            bulk_load(sbase + term * L::B_TERM, bimg + (size_t)cell * L::B_BYTES + term * L::B_TERM, L::B_TERM,
+          for (int term = 0; term < L::NTERM; ++term)
+            bulk_load(sbase + term * L::B_TERM, bimg + (size_t)cell * 3 * L::B_TERM + term * L::B_TERM, L::B_TERM,
                       bready);
           if (!mbar_wait(bready, (uint32_t)(nb & 1), 0x275)) break;
           ++nb;
@@ -796,7 +864,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         tc_fence_after();
         const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * D);
 #pragma unroll
-        for (int term = 0; term < 3; ++term) {
+        for (int term = 0; term < L::NTERM; ++term) {
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t kb = (uint32_t)((ks >> 2) * (D * 128) + (ks & 3) * 32);
@@ -820,6 +888,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int rloc = lg * 32 + lane;
     constexpr int NCH = D / 64;  // 32-feature chunks per warp
     float* zpf = reinterpret_cast<float*>(smem + L::OFF_S + e * L::S_BYTES);  // [feature]: zp
+    float* cf = reinterpret_cast<float*>(smem + L::OFF_C + e * L::S_BYTES);   // fp16 mode: 2^-(E + G_n)
     // codes of this warp's half row: cbw bytes.  From 16 bytes up they are
     // staged as [32 rows][cbw] in shared memory with the swizzle of that
     // width (16-byte chunk j of row r at j ^ ((r * cbw / 128) mod (cbw / 16)),
@@ -855,6 +924,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             zpf[jl] = (float)zz[A.scale_mode == KVC_SCALE_CHANNEL ? half * (D / 2) + jl : 0];
           __syncwarp();
         }
+        if (F16) {
+          __syncwarp();
+          for (int jl = lane; jl < D / 2; jl += 32) cf[jl] = A.fscale[(size_t)cell * (1 + D) + 1 + half * (D / 2) + jl];
+          __syncwarp();
+        }
         s_t = static_cast<const float*>(A.scale.p[cell])[0];
         zp_t = zz[0];
         cur_cell = cell;
@@ -876,9 +950,11 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // constant and clamp on the float bits
           const uint64_t M2 = f2_pack(magic, magic);
           const uint64_t* z2 = reinterpret_cast<const uint64_t*>(zpf + cc * 32);
+          const uint64_t* c2 = reinterpret_cast<const uint64_t*>(cf + cc * 32);
 #pragma unroll
           for (int j = 0; j < 32; j += 2) {
             uint64_t t2 = f2_pack(v[j], v[j + 1]);
+            if (F16) t2 = f2_mul(t2, c2[j / 2]);  // exact: powers of two
             if (!SYM) t2 = f2_add(t2, z2[j / 2]);
             float y0, y1;
             f2_unpack(f2_add(t2, M2), y0, y1);
@@ -1399,7 +1475,8 @@ bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale
 size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd) {
   const int64_t rows_pad = ceil_div(rows, TILE_M) * TILE_M;
   return align256((size_t)3 * 128 * (d / 2) * 4) + align256((size_t)n_cells * 2 * d * sizeof(int32_t)) +
-         align256((size_t)n_cells * rows_pad * rdm_enc(rd) * 4) + align256((size_t)n_cells * 3 * d * d * 2);
+         align256((size_t)n_cells * rows_pad * rdm_enc(rd) * 4) + align256((size_t)n_cells * 3 * d * d * 2) +
+         align256((size_t)n_cells * 4) + align256((size_t)n_cells * (1 + d) * 4);
 }
 
 // The Tucker row terms a stats launch left in its workspace, per host thread:
@@ -1478,24 +1555,29 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   off += align256((size_t)n_cells * 2 * d * sizeof(int32_t));
   float* tmp = reinterpret_cast<float*>(ws + off);
   off += align256((size_t)n_cells * a.tiles_per_cell * TILE_M * rdm * 4);
-  uint8_t* bimg = ws + off;  // quantise: n_cells x 3 x d x d bf16
+  uint8_t* bimg = ws + off;  // quantise: n_cells x 3 x d x d 16-bit
+  off += align256((size_t)n_cells * 3 * d * d * 2);
+  uint32_t* rmax = reinterpret_cast<uint32_t*>(ws + off);  // stats: max |R| per cell
+  off += align256((size_t)n_cells * 4);
+  float* fscale = reinterpret_cast<float*>(ws + off);  // fp16 quantise: 2^E, 2^-(E + G_n) per cell
   a.arows = arows;
   a.minmax = mm;
   a.tmp = tmp;
+  a.rmax = mode == 0 ? rmax : nullptr;
   // the stats pass takes Pi as TMEM rows, the quantise pass Pi / s of each
   // cell as shared-memory B images
   if (mode == 0) {
     prep_rotation_kernel<<<(128 * (d / 2) + 255) / 256, 256, 0, st>>>(proj, d, arows);
     if ((rc = check_launch("prep_rotation_kernel"))) return rc;
-  } else {
-    CellPtrs sp;
-    for (int c = 0; c < n_cells; ++c) sp.p[c] = scale[c];
-    const int fold = scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32;
-    prep_quant_b_kernel<<<dim3((d * d + 255) / 256, n_cells), 256, 0, st>>>(
-        proj, sp, scale_mode == KVC_SCALE_CHANNEL, fold, d, bimg);
-    if ((rc = check_launch("prep_quant_b_kernel"))) return rc;
   }
   const RowsKey key = {workspace, n_cells, rdm, rows, rt > 0 ? core[0] : nullptr, rt > 0 ? u_token[0] : nullptr};
+  // the stats launch just before on this workspace and these cells left
+  // max |R| per cell: the quantise pass may take its fp16 mode
+  const bool after_stats = mode == 1 && tl_rows_reuse && tl_rows_key.ws == key.ws &&
+                           tl_rows_key.n_cells == key.n_cells && tl_rows_key.rdm == key.rdm &&
+                           tl_rows_key.rows == key.rows && tl_rows_key.core0 == key.core0 &&
+                           tl_rows_key.ut0 == key.ut0;
+  const bool f16 = after_stats && d == 128 && rdm == 1 && rt > 0 && scale_mode == KVC_SCALE_CHANNEL;
   bool direct = rt == 1 && rd == 1 && t % TILE_M == 0 && m <= CORE_MAX;
   for (int c = 0; c < n_cells && direct; ++c) direct = (reinterpret_cast<uintptr_t>(u_token[c]) & 15u) == 0;
   a.rows_direct = direct ? 1 : 0;
@@ -1506,11 +1588,22 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
       a.ut.p[c] = u_token[c];
     }
   }
-  const bool rows_ready = direct || (mode == 1 && tl_rows_reuse && tl_rows_key.ws == key.ws &&
-                          tl_rows_key.n_cells == key.n_cells && tl_rows_key.rdm == key.rdm &&
-                          tl_rows_key.rows == key.rows && tl_rows_key.core0 == key.core0 &&
-                          tl_rows_key.ut0 == key.ut0);
+  const bool rows_ready = direct || after_stats;
   tl_rows_key = RowsKey{nullptr, 0, 0, 0, nullptr, nullptr};
+  if (mode == 1) {
+    CellPtrs sp;
+    for (int c = 0; c < n_cells; ++c) sp.p[c] = scale[c];
+    if (f16) {
+      prep_quant_b16_kernel<<<dim3(d, n_cells), d, 0, st>>>(proj, sp, rmax, d, bimg, fscale);
+      if ((rc = check_launch("prep_quant_b16_kernel"))) return rc;
+      a.fscale = fscale;
+    } else {
+      const int fold = scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32;
+      prep_quant_b_kernel<<<dim3((d * d + 255) / 256, n_cells), 256, 0, st>>>(
+          proj, sp, scale_mode == KVC_SCALE_CHANNEL, fold, d, bimg);
+      if ((rc = check_launch("prep_quant_b_kernel"))) return rc;
+    }
+  }
   if (rt > 0 && !rows_ready) {
     CellPtrs cp, up;
     for (int c = 0; c < n_cells; ++c) {
@@ -1524,7 +1617,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   }
   const dim3 grid((unsigned)ceil_div(a.total_tiles, a.tiles_per_cta));
   if (mode == 0) {
-    minmax_init_kernel<<<(n_cells * 2 * d + 255) / 256, 256, 0, st>>>(mm, n_cells, d);
+    minmax_init_kernel<<<(n_cells * 2 * d + 255) / 256, 256, 0, st>>>(mm, n_cells, d, rmax);
     if ((rc = check_launch("minmax_init_kernel"))) return rc;
   }
 #define KVC_TC_STATS(DD, SYMV, RR, NSV)                 \
@@ -1538,6 +1631,13 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   do {                                                                           \
     auto kern = tc_quant_kernel<DD, SYMV, RR, NSV>;                              \
     constexpr size_t sm = QuantLayout<DD, RR, NSV>::BYTES;                       \
+    if ((rc = set_smem(kern, sm))) return rc;                                    \
+    kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, bimg);                     \
+  } while (0)
+#define KVC_TC_QUANT16(SYMV)                                                     \
+  do {                                                                           \
+    auto kern = tc_quant_kernel<128, SYMV, 1, 4, true>;                          \
+    constexpr size_t sm = QuantLayout<128, 1, 4, true>::BYTES;                   \
     if ((rc = set_smem(kern, sm))) return rc;                                    \
     kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, bimg);                     \
   } while (0)
@@ -1556,7 +1656,11 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
       else KVC_TC_ENC_R(KVC_TC_STATS, 64, false, 8);
     }
   } else {
-    if (d == 128) {
+    if (f16) {
+      // two fp16 terms of Pi / s (64 KB) leave room for a fourth x stage
+      if (sym) KVC_TC_QUANT16(true);
+      else KVC_TC_QUANT16(false);
+    } else if (d == 128) {
       if (sym) KVC_TC_ENC_R(KVC_TC_QUANT, 128, true, 3);
       else KVC_TC_ENC_R(KVC_TC_QUANT, 128, false, 3);
     } else {
@@ -1565,6 +1669,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
     }
   }
 #undef KVC_TC_ENC_R
+#undef KVC_TC_QUANT16
 #undef KVC_TC_QUANT
 #undef KVC_TC_STATS
   if ((rc = check_launch(mode == 0 ? "tc_stats_kernel" : "tc_quant_kernel"))) return rc;
