@@ -239,3 +239,44 @@ def test_cache_roundtrip():
     assert k0.shape == (8, 256, 128)
     assert cache.stats()["n_layers"] == 3 and cache.compression_ratio() > 1.0
     assert len(cache.metadata().layers) == 6
+
+
+@pytest.mark.parametrize("layer,tokens", [(2, 2048), (9, 8192)])
+def test_compress_codes_exact_away_from_ties(layer, tokens):
+    """The codes of the whole compress (for bf16 rank-1 cells its quantise
+    pass runs in fp16 with power-of-two scalings) equal the rounding of the
+    exact rotated residual of the cell's own factors, except within 1e-3
+    quantisation steps of a rounding boundary."""
+    import oracle
+    import oracle.jolt
+
+    from _parity import near_ties, recon_rows
+
+    w = WORKLOADS["llama3-8b-kv-b1-t8192-bf16"]
+    k, v = make_kv_layer(w, layer, tokens=tokens)
+    comp = build_compressor("flashjolt", compression_ratio=4.0)
+    proj = cached_projection_np(128)
+    flips = []
+    for x in (k, v):
+        xc = x.reshape(8, tokens, 128).cuda()
+        fac = comp.compress_cell(xc, Allocation(1, 1, 8, 0, 0.0)).tucker
+        m, t, d = xc.shape
+        rows = np.arange(m * t)
+        recon = recon_rows(f32(fac.core), f32(fac.u_token), f32(fac.u_feature), "bf16", rows, t)
+        x_rows = f32(xc).reshape(m * t, d)
+        scale = fac.scale.cpu().numpy()
+        ties = near_ties(x_rows, recon, "bf16", proj, scale)
+        resid = oracle.jolt.dt_op(lambda a, b: a - b, "bf16", x_rows, recon)
+        rot = np.asarray(resid, np.float64) @ proj.astype(np.float64).T
+        q = np.clip(np.rint(rot / scale.astype(np.float64)), -128, 127).astype(np.int32)
+        got = oracle.unpack_codes(fac.packed.cpu().numpy(), 8, d)
+        diff = got != q
+        assert not (diff & ~ties).any(), int((diff & ~ties).sum())
+        flips.append(float(diff.sum()) / max(1, int(ties.sum())))
+    print(f"layer {layer}, {tokens} tokens: near-tie flip rate {max(flips):.3f}")
+
+
+def cached_projection_np(d):
+    from kvcompress_b200.compressor.jl import cached_projection
+
+    return cached_projection(d, d, seed=0).matrix.numpy()
