@@ -613,7 +613,7 @@ __global__ void __launch_bounds__(CH_NT) chol_kernel(double* Sb, int k, int nbma
 constexpr int TS_ROWS = 16;  // rows of W per CTA: 16 lanes of a warp per row
 constexpr int TS_NT = 256;
 
-// w <- w R^{-1} for the 16 rows w of Wl (row stride ldw, 256 threads: row
+// w <- w R^{-1} for the blockDim / 16 rows w of Wl (row stride ldw; row
 // threadIdx / 16, lane threadIdx % 16): R upper triangular (k x k, row
 // stride k, read through L1), rinv its inverse pivots.  Columns in blocks of
 // 32: the rank update by the finished columns, then the block's forward
@@ -649,7 +649,7 @@ __device__ inline void rows_solve_upper(double* Wl, int ldw, int k, const double
   }
 }
 
-// w <- w R^{-T} for the 16 rows of Wl (the same thread layout): y R^T = w,
+// w <- w R^{-T} for the blockDim / 16 rows of Wl (the same thread layout): y R^T = w,
 // y_j = (w_j - sum_{i > j} y_i R[j][i]) / R[j][j], columns in blocks of 32
 // from the last.
 __device__ inline void rows_solve_upper_t(double* Wl, int ldw, int k, const double* __restrict__ R,
@@ -787,8 +787,9 @@ __global__ void lr_store_kernel(SolveArgs a, LrLayout L) {
 // complement, inside the sketch space, of the s = k - rank trailing ones, and
 // s is at most the oversampling.  So only the trailing ones are found: block
 // inverse iteration on C + delta I (its Cholesky factor from chol_kernel;
-// IV_ROWS vectors, each step W <- W R^{-1} R^{-T} and CholeskyQR2 of the
-// rows), a Rayleigh-Ritz on the IV_ROWS x IV_ROWS projection, then
+// nb = 32 vectors where they fit in shared memory, else 16; each step
+// W <- W R^{-1} R^{-T} and CholeskyQR2 of the rows), a Rayleigh-Ritz on the
+// nb x nb projection, then
 // Householder reflectors H_0 .. H_{s-1} of the s trailing vectors; the basis
 // is (W H_0 ... H_{s-1})[:, s:].  Its columns are an orthonormal basis of
 // the same Ritz subspace (not ordered by singular value); the tail mass is
@@ -796,8 +797,9 @@ __global__ void lr_store_kernel(SolveArgs a, LrLayout L) {
 // ---------------------------------------------------------------------------
 constexpr int CP_MIN_K = 129;  // sketches at least this wide take the complement path
 constexpr int CP_MAX_S = 16;   // largest k - rank it handles
-constexpr int IV_ROWS = 16;    // vectors of the block inverse iteration (the 16 rows of rows_solve_*)
-constexpr int IV_ITERS = 12;
+constexpr int IV_GROUP = 16;   // vectors when 32 do not fit in shared memory
+constexpr int IV_MAX = 32;     // vectors of the block inverse iteration (16 threads each)
+constexpr int IV_ITERS = 20;   // steps: trailing Ritz values of flat spectra to ~1e-9 of |A|^2
 
 // C += delta I (delta = 1e-13 of its largest diagonal entry, so the
 // Cholesky succeeds on a semi-definite C); misc[1] = trace(C), misc[2] = delta.
@@ -822,11 +824,13 @@ __global__ void cp_shift_kernel(double* wsb, int64_t cs, LrLayout L, int k) {
   }
 }
 
-// CholeskyQR of the nb rows of X (row stride ldx, length k): G = X X^T, its
-// Cholesky L (rank dropping as chol_kernel), X <- L^{-1} X column by column.
+// CholeskyQR of the nb (<= IV_MAX) rows of X (row stride ldx, length k):
+// G = X X^T, its Cholesky L (rank dropping as chol_kernel), X <- L^{-1} X
+// column by column.
 __device__ inline void cp_orth_rows(double* X, int ldx, int k, int nb, double* G) {
-  const int a = threadIdx.x >> 4, b = threadIdx.x & 15;
-  if (a < nb && b < nb && b <= a) {
+  for (int e = threadIdx.x; e < nb * nb; e += blockDim.x) {
+    const int a = e / nb, b = e % nb;
+    if (b > a) continue;
     const double* xa = X + a * ldx;
     const double* xb = X + b * ldx;
     double s0 = 0.0, s1 = 0.0;
@@ -836,57 +840,59 @@ __device__ inline void cp_orth_rows(double* X, int ldx, int k, int nb, double* G
       s1 = fma(xa[i + 1], xb[i + 1], s1);
     }
     if (i < k) s0 = fma(xa[i], xb[i], s0);
-    G[a * IV_ROWS + b] = s0 + s1;
+    G[a * IV_MAX + b] = s0 + s1;
   }
   __syncthreads();
   if (threadIdx.x == 0) {
     // G = L L^T in place (lower), rank dropping; L[j][j] stored inverted
     for (int j = 0; j < nb; ++j) {
-      const double o = G[j * IV_ROWS + j];
+      const double o = G[j * IV_MAX + j];
       double d = o;
-      for (int q = 0; q < j; ++q) d -= G[j * IV_ROWS + q] * G[j * IV_ROWS + q];
+      for (int q = 0; q < j; ++q) d -= G[j * IV_MAX + q] * G[j * IV_MAX + q];
       const double ri = (o > 0.0 && d > 1e-10 * o) ? 1.0 / sqrt(d) : 0.0;
-      G[j * IV_ROWS + j] = ri;
+      G[j * IV_MAX + j] = ri;
       for (int i2 = j + 1; i2 < nb; ++i2) {
-        double v = G[i2 * IV_ROWS + j];
-        for (int q = 0; q < j; ++q) v -= G[i2 * IV_ROWS + q] * G[j * IV_ROWS + q];
-        G[i2 * IV_ROWS + j] = v * ri;
+        double v = G[i2 * IV_MAX + j];
+        for (int q = 0; q < j; ++q) v -= G[i2 * IV_MAX + q] * G[j * IV_MAX + q];
+        G[i2 * IV_MAX + j] = v * ri;
       }
     }
   }
   __syncthreads();
   for (int c = threadIdx.x; c < k; c += blockDim.x) {
-    double x[IV_ROWS];
+    double x[IV_MAX];
 #pragma unroll
-    for (int q = 0; q < IV_ROWS; ++q) x[q] = q < nb ? X[q * ldx + c] : 0.0;
+    for (int q = 0; q < IV_MAX; ++q) x[q] = q < nb ? X[q * ldx + c] : 0.0;
 #pragma unroll
-    for (int q = 0; q < IV_ROWS; ++q) {
+    for (int q = 0; q < IV_MAX; ++q) {
       if (q >= nb) break;
       double v = x[q];
-      for (int j = 0; j < q; ++j) v -= G[q * IV_ROWS + j] * x[j];
-      x[q] = v * G[q * IV_ROWS + q];
+      for (int j = 0; j < q; ++j) v -= G[q * IV_MAX + j] * x[j];
+      x[q] = v * G[q * IV_MAX + q];
       X[q * ldx + c] = x[q];
     }
   }
   __syncthreads();
 }
 
-// One CTA per cell: the s trailing Ritz vectors of C by block inverse
-// iteration and Rayleigh-Ritz, then their Householder reflectors (v_q in the
-// S slot, rows of length k; tau_q in the lam slot) and the tail mass.
-__global__ void __launch_bounds__(TS_NT) cp_bottom_kernel(SolveArgs a, LrLayout L, int s, int nb, int ldx) {
-  extern __shared__ double X[];  // nb (<= IV_ROWS) rows of stride ldx
-  __shared__ double G[IV_ROWS * IV_ROWS], T[IV_ROWS * IV_ROWS], Mb[IV_ROWS * 32];
-  __shared__ double Zs[IV_ROWS * IV_ROWS], vec[8 * IV_ROWS], lam[IV_ROWS], red[64];
-  __shared__ double scr[3 * IV_ROWS * IV_ROWS];
-  __shared__ int cnt[TS_NT];
+// One CTA of 16 nb threads per cell: the s trailing Ritz vectors of C by
+// block inverse iteration on nb vectors (16 or 32; the row solves give each
+// vector 16 threads) and Rayleigh-Ritz, then their Householder reflectors
+// (v_q in the S slot, rows of length k; tau_q in the lam slot) and the tail
+// mass.
+__global__ void __launch_bounds__(16 * IV_MAX) cp_bottom_kernel(SolveArgs a, LrLayout L, int s, int nb, int ldx) {
+  extern __shared__ double X[];  // nb rows of stride ldx
+  __shared__ double G[IV_MAX * IV_MAX], T[IV_MAX * IV_MAX], Mb[IV_MAX * 32];
+  __shared__ double Zs[CP_MAX_S * IV_MAX], vec[8 * IV_MAX], lam[IV_MAX], red[64];
+  __shared__ double scr[3 * IV_MAX * CP_MAX_S];
+  __shared__ int cnt[16 * IV_MAX];
   const int cell = blockIdx.x, k = a.k;
   double* ws = a.ws + cell * a.ws_cell;
   const double* R = ws + L.C;
   const double* rinv = ws + L.rinv;
-  for (int e = threadIdx.x; e < IV_ROWS * ldx; e += blockDim.x) {
+  for (int e = threadIdx.x; e < nb * ldx; e += blockDim.x) {
     const int r = e / ldx, c = e % ldx;
-    X[e] = (r < nb && c < k) ? eig::start_entry(r, c) : 0.0;
+    X[e] = c < k ? eig::start_entry(r, c) : 0.0;
   }
   __syncthreads();
   cp_orth_rows(X, ldx, k, nb, G);
@@ -899,36 +905,36 @@ __global__ void __launch_bounds__(TS_NT) cp_bottom_kernel(SolveArgs a, LrLayout 
     cp_orth_rows(X, ldx, k, nb, G);
   }
   // T = (X R^T)(X R^T)^T - delta I = X C X^T, 32 columns of M = X R^T at a time
-  for (int e = threadIdx.x; e < IV_ROWS * IV_ROWS; e += blockDim.x) T[e] = 0.0;
+  for (int e = threadIdx.x; e < IV_MAX * IV_MAX; e += blockDim.x) T[e] = 0.0;
   __syncthreads();
   for (int J0 = 0; J0 < k; J0 += 32) {
-    for (int e = threadIdx.x; e < IV_ROWS * 32; e += blockDim.x) {
+    for (int e = threadIdx.x; e < nb * 32; e += blockDim.x) {
       const int r = e >> 5, jj = e & 31, j = J0 + jj;
       double m = 0.0;
-      if (r < nb && j < k) {
+      if (j < k) {
         const double* xr = X + r * ldx;
         for (int i = j; i < k; ++i) m = fma(xr[i], __ldg(R + (int64_t)j * k + i), m);
       }
       Mb[e] = m;
     }
     __syncthreads();
-    {
-      const int r = threadIdx.x >> 4, q = threadIdx.x & 15;
+    for (int e = threadIdx.x; e < nb * nb; e += blockDim.x) {
+      const int r = e / nb, q = e % nb;
       double t = 0.0;
 #pragma unroll 8
       for (int jj = 0; jj < 32; ++jj) t = fma(Mb[r * 32 + jj], Mb[q * 32 + jj], t);
-      T[r * IV_ROWS + q] += t;
+      T[r * IV_MAX + q] += t;
     }
     __syncthreads();
   }
   // the s trailing eigenpairs of T = the s leading ones of -T
   const double delta = ws[L.misc + 2];
-  for (int e = threadIdx.x; e < IV_ROWS * IV_ROWS; e += blockDim.x) {
-    const int r = e / IV_ROWS, q = e % IV_ROWS;
+  for (int e = threadIdx.x; e < IV_MAX * IV_MAX; e += blockDim.x) {
+    const int r = e / IV_MAX, q = e % IV_MAX;
     G[e] = (r < nb && q < nb) ? -(T[e] - (r == q ? delta : 0.0)) : 0.0;
   }
   __syncthreads();
-  eig::eig_top(G, IV_ROWS, nb, s, lam, Zs, IV_ROWS, vec, cnt, red, scr, s);
+  eig::eig_top(G, IV_MAX, nb, s, lam, Zs, IV_MAX, vec, cnt, red, scr, s);
   // tail = 1 - (trace C - sum of the trailing Ritz values) / |A|^2
   if (threadIdx.x == 0) {
     double trailing = 0.0;
@@ -940,13 +946,13 @@ __global__ void __launch_bounds__(TS_NT) cp_bottom_kernel(SolveArgs a, LrLayout 
   }
   // the trailing Ritz vectors X_s = Zs X (s rows), column by column in place
   for (int c = threadIdx.x; c < k; c += blockDim.x) {
-    double x[IV_ROWS];
+    double x[IV_MAX];
 #pragma unroll
-    for (int q = 0; q < IV_ROWS; ++q) x[q] = q < nb ? X[q * ldx + c] : 0.0;
+    for (int q = 0; q < IV_MAX; ++q) x[q] = q < nb ? X[q * ldx + c] : 0.0;
     for (int q = 0; q < s; ++q) {
       double v = 0.0;
 #pragma unroll
-      for (int j = 0; j < IV_ROWS; ++j) v = fma(Zs[q * IV_ROWS + j], x[j], v);
+      for (int j = 0; j < IV_MAX; ++j) v = fma(Zs[q * IV_MAX + j], x[j], v);
       X[q * ldx + c] = v;
     }
   }
@@ -1082,11 +1088,16 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
   else rc = gemm(ws + oth, cs, k, 1, ws + oth, cs, k, 0, ws + L.C, cs, k, k, k, p);
   if (rc) return rc;
   const int s = k - a.rank;
-  if (k >= CP_MIN_K && s <= CP_MAX_S && !a.sv2) {
+  const int ldx = k | 1;  // odd row stride: the rows' Gram reads are conflict-free
+  // 32 vectors when their rows fit next to the static arrays (k <= 680),
+  // else 16; IV_ITERS steps resolve s <= 16 trailing vectors with 32 and
+  // s <= 4 with 16; other sketches take the full eigensolver
+  const int nb = sizeof(double) * (size_t)IV_MAX * ldx <= 170 * 1024 ? IV_MAX : IV_GROUP;
+  const int cp_max_s = nb == IV_MAX ? CP_MAX_S : 4;
+  if (k >= CP_MIN_K && s <= cp_max_s && !a.sv2) {
     // the complement of the s trailing Ritz vectors
     const int cp_smem = (int)(sizeof(double) * (size_t)TS_ROWS * k);
-    const int ldx = k | 1;  // odd row stride: the rows' Gram reads are conflict-free
-    const int iv_smem = (int)(sizeof(double) * (size_t)IV_ROWS * ldx);
+    const int iv_smem = (int)(sizeof(double) * (size_t)nb * ldx);
     if ((e = cudaFuncSetAttribute(cp_complement_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cp_smem)) ==
         cudaSuccess)
       e = cudaFuncSetAttribute(cp_bottom_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, iv_smem);
@@ -1096,8 +1107,7 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
       if ((rc = check_launch("cp_shift_kernel"))) return rc;
       chol_kernel<<<n_cells, CH_NT, chol_smem, st>>>(ws + L.C, k, nbmax, cs, ws + L.rinv, cs);
       if ((rc = check_launch("chol_kernel"))) return rc;
-      // all IV_ROWS vectors: the row solves process 16 rows whatever their number
-      cp_bottom_kernel<<<n_cells, TS_NT, iv_smem, st>>>(a, L, s, IV_ROWS, ldx);
+      cp_bottom_kernel<<<n_cells, 16 * nb, iv_smem, st>>>(a, L, s, nb, ldx);
       if ((rc = check_launch("cp_bottom_kernel"))) return rc;
     } else {
       // the sketch space itself: tail = 1 - trace(C) / |A|^2

@@ -11,7 +11,8 @@ tests/golden/make_large_golden.py) and against the oracle.
 
 Bars: allocations, payload schema, byte counts and the compressor's stats
 identical to the reference's; end-to-end relative error within 2 % of the
-reference's; where the rank-(1, 1) subspaces are well separated the decode
+reference's; tail masses within 1e-5 (absolute) of the oracle's run on this
+device's sketches; where the rank-(1, 1) subspaces are well separated the decode
 within 1e-3 (fp32) / 1e-2 (bf16) of the reference's or the oracle's; and
 codes made from the reference's own factors identical to its codes except
 within 1e-3 quantisation steps of a rounding boundary.  The large inputs are
@@ -30,6 +31,7 @@ import pytest
 import torch
 
 import oracle
+import oracle.jolt as _oj
 from kvcompress_b200 import build_compressor, ops
 from kvcompress_b200._native import KVC
 from kvcompress_b200.compressor.svd import sketch_width
@@ -65,6 +67,14 @@ def _regenerate(meta_case):
         got = hashlib.sha256(x.contiguous().view(torch.int16).numpy().tobytes()).hexdigest()
         assert got == meta_case[tag]["input_sha256"], f"regenerated {tag} input differs from the fixture's"
     return k, v
+
+
+def _cuda_svd_fn(cap):
+    """The oracle's randomised SVD (svd.py:221-316) on the device's sketches."""
+    def svd_fn(a, rank, mode):
+        _, k = _oj.sketch_width(a.shape[0], a.shape[1], rank, 10, cap)
+        return _oj.randomised_svd(a, rank, cuda_omega(a.shape[1], k), 2)
+    return svd_fn
 
 
 def _check_against_reference(comp, kp, vp, meta_case):
@@ -172,8 +182,25 @@ def test_qcap_sketch_width_513(large):
         e_got = rel(got.reshape(-1, d)[rows], x_np.reshape(-1, d)[rows])
         e_ref = rel(ref_rows, x_np.reshape(-1, d)[rows])
         assert abs(e_got / e_ref - 1) < 0.02, (tag, e_got, e_ref)
-        assert abs(pay.metadata["tail_token_mass"] - mc[tag]["metadata"]["tail_token_mass"]) < 2e-2
-        assert abs(pay.metadata["tail_feature_mass"] - mc[tag]["metadata"]["tail_feature_mass"]) < 1e-3
+        # the reference drew its sketches from the CPU generator: on these flat
+        # spectra another draw moves the tails by up to ~1 %
+        for key in ("tail_token_mass", "tail_feature_mass"):
+            ref_tail = mc[tag]["metadata"][key]
+            assert abs(pay.metadata[key] / ref_tail - 1) < 2e-2, (tag, key, pay.metadata[key], ref_tail)
+        # with this device's sketches the oracle's randomised SVDs give the
+        # same tails.  The token unfolding is built on the feature basis this
+        # device chose: a basis column of the other sign (LAPACK's choice in
+        # the reference) flips a column of the unfolding, which is a
+        # different sketch of it.
+        svd_fn = _cuda_svd_fn(oracle.flashjolt_cap(t, 4.0))
+        tails = {"tail_feature_mass": svd_fn(np.moveaxis(x_np, 2, 0).reshape(d, m * t), rd, "feature")[2]}
+        u_d = _oj.round_to(f32(pay.data["u_feature"]).reshape(d, rd), "bf16")
+        x_proj = _oj.matmul_round(x_np.reshape(m * t, d), u_d, "bf16").reshape(m, t, rd)
+        tails["tail_token_mass"] = svd_fn(np.moveaxis(x_proj, 1, 0).reshape(t, m * rd), rt, "token")[2]
+        for key, want in tails.items():
+            print(f"qcap/{tag} {key}: device {pay.metadata[key]:.8f} oracle {want:.8f}")
+        for key, want in tails.items():
+            assert abs(pay.metadata[key] - want) < 1e-5, (tag, key, pay.metadata[key], want)
     assert ops.device_error() == 0
 
 

@@ -112,7 +112,8 @@ def test_randomised_right(n, p, k, rank):
 
 
 @pytest.mark.parametrize("n,p,k,rank", [(4096, 1024, 513, 512), (4096, 1024, 513, 503), (3000, 300, 150, 150),
-                                        (5000, 700, 300, 290)])
+                                        (5000, 700, 300, 290), (3000, 300, 150, 134), (4096, 1024, 700, 696),
+                                        (4096, 1024, 700, 692)])
 def test_randomised_right_complement(n, p, k, rank):
     """Wide sketches without singular values (every compress call): the basis
     spans the top-rank Ritz subspace (columns not ordered) and the tail mass
