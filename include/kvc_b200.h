@@ -292,6 +292,9 @@ int kvc_decode_plan_run(const void* plan, size_t plan_bytes, int64_t t0, int64_t
  * tensor-core kernels (residual encode) and symmetric per-channel 8/4/2-bit
  * bf16 decodes run on the tcgen05 decoder; everything else on the SIMT
  * kernels.  Policy 1: SIMT kernels only (used to cross-check the two).
+ * Policy 2: as 0 with the residual encode's fp16 two-term modes (stats pass
+ * and, after it in one compress call, quantise pass with Pi in two fp16
+ * terms and R scaled by powers of two; d = 128, rank-1 row terms).
  * Process-wide; set it while no call is in flight.
  */
 int kvc_set_kernel_policy(int policy);

@@ -341,7 +341,7 @@ extern "C" int kvc_gram(int n_cells, const void* const* a, int64_t rows, int p, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int64_t stride = (int64_t)p * p + (int64_t)p * k + 1;
   int rc;
-  if (kernel_policy() == 0 && k > 0 && aligned && tc_gram_eligible(dtype, p, k) &&
+  if (kernel_policy() != 1 && k > 0 && aligned && tc_gram_eligible(dtype, p, k) &&
       ws_bytes >= tc_gram_workspace(n_cells, rows)) {
     if ((rc = tc_gram_launch(n_cells, a, rows, omega, k, out, workspace, ws_bytes, st))) return rc;
     gram_trace_kernel<<<(n_cells + 3) / 4, 128, 0, st>>>(out, n_cells, p, k, stride);

@@ -114,7 +114,7 @@ extern "C" int kvc_decompress_noalloc(int n_cells, const uint8_t* const* codes, 
   if (m <= 0 || t <= 0 || d <= 0 || rd < 0) return fail(KVC_ERR_SHAPE, "kvc_decompress_noalloc: bad shape");
   // only the tensor-core decode reads the workspace; the SIMT decode of the
   // other layouts ignores it, so its size is no limit there
-  if (kernel_policy() == 0 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj)) {
+  if (kernel_policy() != 1 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj)) {
     const size_t need = kvc_decompress_workspace_bytes(n_cells, m * t, d, rd);
     if (need > kScratchBytes)
       return fail(KVC_ERR_WORKSPACE, "kvc_decompress_noalloc: needs " + std::to_string(need) +

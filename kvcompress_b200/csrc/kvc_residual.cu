@@ -40,7 +40,9 @@ void tc_reuse_tucker_rows(bool allow);
 int tc_read_device_error(int* out);
 int tc_gram_read_device_error(int* out);
 
-static int g_policy = 0;  // 0: tensor cores when eligible, 1: SIMT kernels only
+// 0: tensor cores when eligible (bf16 operands), 1: SIMT kernels only,
+// 2: as 0 with the residual encode's fp16 two-term modes
+static int g_policy = 0;
 int kernel_policy() { return g_policy; }
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -491,7 +493,8 @@ extern "C" size_t kvc_decompress_workspace_bytes(int n_cells, int64_t rows, int 
 }
 
 extern "C" int kvc_set_kernel_policy(int policy) {
-  if (policy != 0 && policy != 1) return fail(KVC_ERR_ARG, "kvc_set_kernel_policy: 0 (auto) or 1 (SIMT)");
+  if (policy < 0 || policy > 2)
+    return fail(KVC_ERR_ARG, "kvc_set_kernel_policy: 0 (auto), 1 (SIMT) or 2 (fp16 two-term encode)");
   g_policy = policy;
   return KVC_OK;
 }
@@ -518,7 +521,7 @@ extern "C" int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, 
   if (rc) return rc;
   if (scale_mode == KVC_SCALE_GROUP) return fail(KVC_ERR_ARG, "kvc_residual_stats: group scales need no stats pass");
   cudaStream_t st0 = static_cast<cudaStream_t>(stream);
-  if (g_policy == 0 && tc_residual_eligible(dtype, d, rd, proj, scale_mode) && all_aligned(n_cells, x) &&
+  if (g_policy != 1 && tc_residual_eligible(dtype, d, rd, proj, scale_mode) && all_aligned(n_cells, x) &&
       workspace && ws_bytes >= tc_residual_workspace(n_cells, m * t, d, rd)) {
     return tc_residual_launch(0, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
                               scale_mode, stat_dtype, KVC_F32, scale_out, zp_out, nullptr, workspace, ws_bytes,
@@ -562,7 +565,7 @@ extern "C" int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, 
   if (scale_mode == KVC_SCALE_GROUP && (group_size <= 0 || d % group_size != 0))
     return fail(KVC_ERR_SHAPE, "kvc_residual_quant: d must be divisible by group_size");
   if (!dtype_ok(arith_dtype)) return fail(KVC_ERR_DTYPE, "kvc_residual_quant: bad arith dtype");
-  if (g_policy == 0 && scale_mode != KVC_SCALE_GROUP && tc_residual_eligible(dtype, d, rd, proj, scale_mode) &&
+  if (g_policy != 1 && scale_mode != KVC_SCALE_GROUP && tc_residual_eligible(dtype, d, rd, proj, scale_mode) &&
       all_aligned(n_cells, x) && all_aligned(n_cells, codes) && workspace &&
       ws_bytes >= tc_residual_workspace(n_cells, m * t, d, rd)) {
     return tc_residual_launch(1, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
@@ -610,7 +613,7 @@ extern "C" int kvc_decompress(int n_cells, const uint8_t* const* codes, const fl
     if (rt > 0 && (!core[c] || !u_token[c] || !u_feature[c]))
       return fail(KVC_ERR_ARG, "kvc_decompress: NULL factor");
   }
-  if (g_policy == 0 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj) &&
+  if (g_policy != 1 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj) &&
       all_aligned(n_cells, codes) && all_aligned(n_cells, out) && workspace &&
       ws_bytes >= tc_decompress_workspace(n_cells, m * t, d, rd)) {
     return tc_decompress_launch(n_cells, codes, scale, bits, core, u_token, u_feature, factor_dtype, m, t, d, rt,
@@ -695,7 +698,7 @@ extern "C" int kvc_decode_plan_init(void* plan, size_t plan_bytes, int n_cells, 
       return fail(KVC_ERR_ARG, "kvc_decode_plan_init: NULL factor");
   }
   (void)group_size;
-  if (!(g_policy == 0 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj) &&
+  if (!(g_policy != 1 && tc_decompress_eligible(out_dtype, d, rd, bits, symmetric, scale_mode, proj) &&
         all_aligned(n_cells, codes)))
     return fail(KVC_ERR_UNSUPPORTED,
                 "kvc_decode_plan_init: no tensor-core plan for this layout (decode with kvc_decompress)");

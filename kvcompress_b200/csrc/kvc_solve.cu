@@ -555,15 +555,13 @@ __global__ void __launch_bounds__(CH_NT) chol_kernel(double* Sb, int k, int nbma
       const bool keep = o > 0.0 && d > 1e-10 * o;
       const double rs = keep ? 1.0 / sqrt(d) : 0.0;
       const double inv_d = rs * rs;
-      const int ns = j > 0 ? w - (j - 1) : 0;
-      const int nu = (nb - 1 - j) * w;
-      for (int t = threadIdx.x; t < ns + nu; t += blockDim.x) {
-        if (t < ns) {
-          P[(j - 1) * w + (j - 1) + t] *= ri[j - 1];
-        } else {
-          const int u = t - ns, i = j + 1 + u / w, c = u % w;
-          if (c >= i) P[i * w + c] = fma(-P[j * w + i] * inv_d, P[j * w + c], P[i * w + c]);
-        }
+      // row j - 1 takes its scaling one step late; rows i > j the rank-1
+      // update by row j (columns c >= i)
+      if (j > 0)
+        for (int c = j - 1 + threadIdx.x; c < w; c += blockDim.x) P[(j - 1) * w + c] *= ri[j - 1];
+      for (int i = j + 1; i < nb; ++i) {
+        const double f = P[j * w + i] * inv_d;
+        for (int c = i + threadIdx.x; c < w; c += blockDim.x) P[i * w + c] = fma(-f, P[j * w + c], P[i * w + c]);
       }
       if (threadIdx.x == 0) ri[j] = rs;
       __syncthreads();
@@ -613,75 +611,159 @@ __global__ void __launch_bounds__(CH_NT) chol_kernel(double* Sb, int k, int nbma
 constexpr int TS_ROWS = 16;  // rows of W per CTA: 16 lanes of a warp per row
 constexpr int TS_NT = 256;
 
-// w <- w R^{-1} for the blockDim / 16 rows w of Wl (row stride ldw; row
-// threadIdx / 16, lane threadIdx % 16): R upper triangular (k x k, row
-// stride k, read through L1), rinv its inverse pivots.  Columns in blocks of
-// 32: the rank update by the finished columns, then the block's forward
-// substitution column by column, the 16 lanes of a row splitting each dot.
-__device__ inline void rows_solve_upper(double* Wl, int ldw, int k, const double* __restrict__ R,
-                                        const double* __restrict__ rinv) {
-  const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
-  double* wr = Wl + r * ldw;
-  for (int J0 = 0; J0 < k; J0 += 32) {
-    const int cb = min(32, k - J0);
-    if (J0 > 0) {
-      double a0 = 0.0, a1 = 0.0;
-      const int c0 = J0 + lane, c1 = J0 + lane + 16;
-      for (int i = 0; i < J0; ++i) {
-        const double wi = wr[i];
-        if (c0 < k) a0 = fma(wi, __ldg(R + (int64_t)i * k + c0), a0);
-        if (c1 < k) a1 = fma(wi, __ldg(R + (int64_t)i * k + c1), a1);
-      }
-      if (c0 < k) wr[c0] -= a0;
-      if (c1 < k) wr[c1] -= a1;
+// Staged blocks of R for the row solves: 32 x 32 doubles at row stride RS_LD
+// (padded: every read pattern below is conflict-free), a ring of NBUF of
+// them filled by 8-byte cp.async copies (zero outside the k x k matrix)
+// NBUF - 1 blocks ahead of their use, so the L2 latency of R overlaps the
+// arithmetic instead of sitting in every dependent step.
+constexpr int RS_LD = 33;
+constexpr int RS_BLOCK = 32 * RS_LD;  // doubles per staged block
+
+__device__ __forceinline__ void cp_async8(double* dst, const double* src, bool valid) {
+  const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst);
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(d), "l"(src), "r"(valid ? 8 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit8() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait8() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+
+// Block s of a row solve's sequence over the nbk x nbk blocks of R:
+// forward (w R^{-1}): column blocks jb = 0, 1, ..; in each, the update blocks
+// ib < jb then the diagonal; transposed (w R^{-T}): jb = nbk - 1 down to 0;
+// in each, the update blocks ib = nbk - 1 .. jb + 1 then the diagonal.
+// (rb, cb): the block's row and column block of R.
+struct SolveSeq {
+  int jb, ib;
+};
+template <bool TRANS>
+__device__ __forceinline__ void seq_first(SolveSeq& q, int nbk) {
+  if (TRANS) {
+    q.jb = nbk - 1;
+    q.ib = nbk - 1;
+  } else {
+    q.jb = 0;
+    q.ib = 0;
+  }
+}
+template <bool TRANS>
+__device__ __forceinline__ void seq_next(SolveSeq& q, int nbk) {
+  if (TRANS) {
+    if (q.ib > q.jb) --q.ib;
+    else {
+      --q.jb;
+      q.ib = nbk - 1;
     }
-    __syncwarp();
-    for (int c = 0; c < cb; ++c) {
-      const int col = J0 + c;
-      double part = 0.0;
-      if (lane < c) part = wr[J0 + lane] * __ldg(R + (int64_t)(J0 + lane) * k + col);
-      if (lane + 16 < c) part = fma(wr[J0 + lane + 16], __ldg(R + (int64_t)(J0 + lane + 16) * k + col), part);
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
-      if (lane == 0) wr[col] = (wr[col] - part) * rinv[col];
-      __syncwarp();
+  } else {
+    if (q.ib < q.jb) ++q.ib;
+    else {
+      ++q.jb;
+      q.ib = 0;
     }
   }
 }
 
-// w <- w R^{-T} for the blockDim / 16 rows of Wl (the same thread layout): y R^T = w,
-// y_j = (w_j - sum_{i > j} y_i R[j][i]) / R[j][j], columns in blocks of 32
-// from the last.
-__device__ inline void rows_solve_upper_t(double* Wl, int ldw, int k, const double* __restrict__ R,
-                                          const double* __restrict__ rinv) {
+template <bool TRANS>
+__device__ __forceinline__ void stage_block(double* buf, const double* __restrict__ R, int k, const SolveSeq& q) {
+  const int rb = TRANS ? q.jb : q.ib, cbk = TRANS ? q.ib : q.jb;
+  for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+    const int i = e >> 5, c = e & 31, r = rb * 32 + i, col = cbk * 32 + c;
+    const bool ok = r < k && col < k;
+    cp_async8(buf + i * RS_LD + c, ok ? R + (int64_t)r * k + col : R, ok);
+  }
+}
+
+// w <- w R^{-1} (TRANS: w <- w R^{-T}) for the blockDim / 16 rows w of Wl
+// (row stride ldw; row threadIdx / 16, lane threadIdx % 16; every thread of
+// the block calls it): R upper triangular (k x k, row stride k), rinv its
+// inverse pivots, Rs NBUF staged blocks.  Column blocks of 32: the rank
+// update by the finished columns (lane l owns columns l and l + 16 of the
+// block), then the block's substitution column by column, the 16 lanes of a
+// row splitting each dot product.
+//   forward:    y_c = (w_c - sum_{i < c} y_i R[i][c]) / R[c][c]
+//   transposed: y_j = (w_j - sum_{i > j} y_i R[j][i]) / R[j][j]
+template <bool TRANS, int NBUF>
+__device__ void rows_solve(double* Wl, int ldw, int k, const double* __restrict__ R,
+                           const double* __restrict__ rinv, double* Rs) {
   const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
   double* wr = Wl + r * ldw;
-  for (int J0 = ((k - 1) / 32) * 32; J0 >= 0; J0 -= 32) {
-    const int cb = min(32, k - J0), end = J0 + cb;
-    if (end < k) {
-      double a0 = 0.0, a1 = 0.0;
-      const int j0 = J0 + lane, j1 = J0 + lane + 16;
-      for (int i = end; i < k; ++i) {
-        const double yi = wr[i];
-        if (j0 < end) a0 = fma(yi, __ldg(R + (int64_t)j0 * k + i), a0);
-        if (j1 < end) a1 = fma(yi, __ldg(R + (int64_t)j1 * k + i), a1);
-      }
-      if (j0 < end) wr[j0] -= a0;
-      if (j1 < end) wr[j1] -= a1;
+  const int nbk = (k + 31) / 32;
+  const int total = nbk * (nbk + 1) / 2;
+  SolveSeq pre, cur;
+  seq_first<TRANS>(pre, nbk);
+  seq_first<TRANS>(cur, nbk);
+  __syncthreads();  // Rs is free (an earlier solve has consumed it)
+#pragma unroll 1
+  for (int n = 0; n < NBUF - 1; ++n) {
+    if (n < total) {
+      stage_block<TRANS>(Rs + n * RS_BLOCK, R, k, pre);
+      seq_next<TRANS>(pre, nbk);
     }
-    __syncwarp();
-    for (int c = cb - 1; c >= 0; --c) {
-      const int col = J0 + c;
-      double part = 0.0;
-      if (lane > c && lane < cb) part = wr[J0 + lane] * __ldg(R + (int64_t)col * k + J0 + lane);
-      if (lane + 16 > c && lane + 16 < cb)
-        part = fma(wr[J0 + lane + 16], __ldg(R + (int64_t)col * k + J0 + lane + 16), part);
-#pragma unroll
-      for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
-      if (lane == 0) wr[col] = (wr[col] - part) * rinv[col];
-      __syncwarp();
-    }
+    cp_async_commit8();
   }
+  double a0 = 0.0, a1 = 0.0;
+#pragma unroll 1
+  for (int n = 0; n < total; ++n) {
+    cp_async_wait8<NBUF - 2>();
+    __syncthreads();  // block n is in; every thread is done with block n - 1
+    if (n + NBUF - 1 < total) {
+      stage_block<TRANS>(Rs + ((n + NBUF - 1) % NBUF) * RS_BLOCK, R, k, pre);
+      seq_next<TRANS>(pre, nbk);
+    }
+    cp_async_commit8();
+    const double* B = Rs + (n % NBUF) * RS_BLOCK;
+    const int J0 = cur.jb * 32, cb = min(32, k - J0);
+    if (cur.ib != cur.jb) {
+      const int I0 = cur.ib * 32, ni = min(32, k - I0);
+      if (!TRANS) {
+        // forward update: rows I0 + i of R (all < k: ib < jb), columns J0 + lane (+16)
+#pragma unroll 8
+        for (int i = 0; i < 32; ++i) {
+          const double wi = wr[I0 + i];
+          a0 = fma(wi, B[i * RS_LD + lane], a0);
+          a1 = fma(wi, B[i * RS_LD + lane + 16], a1);
+        }
+      } else {
+        // transposed update: rows J0 + lane (+16) of R, columns I0 + i < k
+        for (int i = 0; i < ni; ++i) {
+          const double yi = wr[I0 + i];
+          a0 = fma(yi, B[lane * RS_LD + i], a0);
+          a1 = fma(yi, B[(lane + 16) * RS_LD + i], a1);
+        }
+      }
+    } else {
+      // the diagonal block: apply the update, then substitute column by column
+      if (lane < cb) wr[J0 + lane] -= a0;
+      if (lane + 16 < cb) wr[J0 + lane + 16] -= a1;
+      a0 = a1 = 0.0;
+      __syncwarp();
+      if (!TRANS) {
+        for (int c = 0; c < cb; ++c) {
+          double part = 0.0;
+          if (lane < c) part = wr[J0 + lane] * B[lane * RS_LD + c];
+          if (lane + 16 < c) part = fma(wr[J0 + lane + 16], B[(lane + 16) * RS_LD + c], part);
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
+          if (lane == 0) wr[J0 + c] = (wr[J0 + c] - part) * rinv[J0 + c];
+          __syncwarp();
+        }
+      } else {
+        for (int c = cb - 1; c >= 0; --c) {
+          double part = 0.0;
+          if (lane > c && lane < cb) part = wr[J0 + lane] * B[c * RS_LD + lane];
+          if (lane + 16 > c && lane + 16 < cb) part = fma(wr[J0 + lane + 16], B[c * RS_LD + lane + 16], part);
+#pragma unroll
+          for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
+          if (lane == 0) wr[J0 + c] = (wr[J0 + c] - part) * rinv[J0 + c];
+          __syncwarp();
+        }
+      }
+    }
+    seq_next<TRANS>(cur, nbk);
+  }
+  cp_async_wait8<0>();
+  __syncthreads();
 }
 
 // W <- W R^{-1} per cell (R upper triangular from chol_kernel, rinv its
@@ -690,9 +772,11 @@ __device__ inline void rows_solve_upper_t(double* Wl, int ldw, int k, const doub
 // of 32: first the rank update by the finished columns (R read through L1,
 // shared by every row), then the block's own forward substitution, column by
 // column, with the 16 lanes of a row splitting each dot product.
+constexpr int TS_NBUF = 8;  // staged blocks of R in flight per CTA
+
 __global__ void __launch_bounds__(TS_NT) trsm_kernel(double* Wb, int p, int k, int64_t sW, const double* Rb,
                                                      int64_t sR, const double* rinvb, int64_t sri) {
-  extern __shared__ double Wl[];  // TS_ROWS x k
+  extern __shared__ double Wl[];  // TS_ROWS x k, then TS_NBUF staged blocks of R
   const int cell = blockIdx.y;
   double* W = Wb + cell * sW;
   const double* R = Rb + cell * sR;
@@ -704,8 +788,7 @@ __global__ void __launch_bounds__(TS_NT) trsm_kernel(double* Wb, int p, int k, i
     Wl[e] = r < nr ? W[(int64_t)(row0 + r) * k + c] : 0.0;
   }
   __syncthreads();
-  rows_solve_upper(Wl, k, k, R, rinv);
-  __syncthreads();
+  rows_solve<false, TS_NBUF>(Wl, k, k, R, rinv, Wl + (size_t)TS_ROWS * k);
   for (int e = threadIdx.x; e < nr * k; e += blockDim.x) {
     const int rr = e / k, c = e % k;
     W[(int64_t)(row0 + rr) * k + c] = Wl[e];
@@ -787,9 +870,8 @@ __global__ void lr_store_kernel(SolveArgs a, LrLayout L) {
 // complement, inside the sketch space, of the s = k - rank trailing ones, and
 // s is at most the oversampling.  So only the trailing ones are found: block
 // inverse iteration on C + delta I (its Cholesky factor from chol_kernel;
-// nb = 32 vectors where they fit in shared memory, else 16; each step
-// W <- W R^{-1} R^{-T} and CholeskyQR2 of the rows), a Rayleigh-Ritz on the
-// nb x nb projection, then
+// nb = 16 vectors for s <= 4, else 32; each step W <- W R^{-1} R^{-T} and
+// CholeskyQR2 of the rows), a Rayleigh-Ritz on the nb x nb projection, then
 // Householder reflectors H_0 .. H_{s-1} of the s trailing vectors; the basis
 // is (W H_0 ... H_{s-1})[:, s:].  Its columns are an orthonormal basis of
 // the same Ritz subspace (not ordered by singular value); the tail mass is
@@ -800,6 +882,7 @@ constexpr int CP_MAX_S = 16;   // largest k - rank it handles
 constexpr int IV_GROUP = 16;   // vectors when 32 do not fit in shared memory
 constexpr int IV_MAX = 32;     // vectors of the block inverse iteration (16 threads each)
 constexpr int IV_ITERS = 20;   // steps: trailing Ritz values of flat spectra to ~1e-9 of |A|^2
+constexpr int CP_NBUF = 4;     // staged blocks of R in flight in the row solves
 
 // C += delta I (delta = 1e-13 of its largest diagonal entry, so the
 // Cholesky succeeds on a semi-definite C); misc[1] = trace(C), misc[2] = delta.
@@ -880,8 +963,9 @@ __device__ inline void cp_orth_rows(double* X, int ldx, int k, int nb, double* G
 // vector 16 threads) and Rayleigh-Ritz, then their Householder reflectors
 // (v_q in the S slot, rows of length k; tau_q in the lam slot) and the tail
 // mass.
-__global__ void __launch_bounds__(16 * IV_MAX) cp_bottom_kernel(SolveArgs a, LrLayout L, int s, int nb, int ldx) {
-  extern __shared__ double X[];  // nb rows of stride ldx
+__global__ void __launch_bounds__(16 * IV_MAX) cp_bottom_kernel(SolveArgs a, LrLayout L, int s, int nb, int ldx,
+                                                                 int iters) {
+  extern __shared__ double X[];  // nb rows of stride ldx, then CP_NBUF staged blocks of R
   __shared__ double G[IV_MAX * IV_MAX], T[IV_MAX * IV_MAX], Mb[IV_MAX * 32];
   __shared__ double Zs[CP_MAX_S * IV_MAX], vec[8 * IV_MAX], lam[IV_MAX], red[64];
   __shared__ double scr[3 * IV_MAX * CP_MAX_S];
@@ -897,9 +981,9 @@ __global__ void __launch_bounds__(16 * IV_MAX) cp_bottom_kernel(SolveArgs a, LrL
   __syncthreads();
   cp_orth_rows(X, ldx, k, nb, G);
   cp_orth_rows(X, ldx, k, nb, G);
-  for (int it = 0; it < IV_ITERS; ++it) {
-    rows_solve_upper(X, ldx, k, R, rinv);
-    rows_solve_upper_t(X, ldx, k, R, rinv);
+  for (int it = 0; it < iters; ++it) {
+    rows_solve<false, CP_NBUF>(X, ldx, k, R, rinv, X + (size_t)nb * ldx);
+    rows_solve<true, CP_NBUF>(X, ldx, k, R, rinv, X + (size_t)nb * ldx);
     __syncthreads();
     cp_orth_rows(X, ldx, k, nb, G);
     cp_orth_rows(X, ldx, k, nb, G);
@@ -1044,7 +1128,7 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
   double* ws = a.ws;
   const int nbmax = chol_panel_rows(k);
   const size_t chol_smem = sizeof(double) * (size_t)nbmax * k;
-  const size_t trsm_smem = sizeof(double) * (size_t)TS_ROWS * k;
+  const size_t trsm_smem = sizeof(double) * ((size_t)TS_ROWS * k + (size_t)TS_NBUF * RS_BLOCK);
   cudaError_t e = cudaFuncSetAttribute(chol_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)chol_smem);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(trsm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)trsm_smem);
@@ -1089,15 +1173,18 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
   if (rc) return rc;
   const int s = k - a.rank;
   const int ldx = k | 1;  // odd row stride: the rows' Gram reads are conflict-free
-  // 32 vectors when their rows fit next to the static arrays (k <= 680),
-  // else 16; IV_ITERS steps resolve s <= 16 trailing vectors with 32 and
-  // s <= 4 with 16; other sketches take the full eigensolver
-  const int nb = sizeof(double) * (size_t)IV_MAX * ldx <= 170 * 1024 ? IV_MAX : IV_GROUP;
-  const int cp_max_s = nb == IV_MAX ? CP_MAX_S : 4;
-  if (k >= CP_MIN_K && s <= cp_max_s && !a.sv2) {
+  // IV_ITERS steps on 16 vectors for s <= 4 trailing ones, on 32 for
+  // s <= 16 where their rows fit in shared memory next to the static arrays
+  // and the staged blocks of R (k <= 554); other sketches take the full
+  // eigensolver
+  const size_t rs_bytes = sizeof(double) * (size_t)CP_NBUF * RS_BLOCK;
+  const bool wide_fits = sizeof(double) * (size_t)IV_MAX * ldx + rs_bytes <= 176 * 1024;
+  const int nb = s <= 4 ? IV_GROUP : IV_MAX;
+  const int iters = IV_ITERS;
+  if (k >= CP_MIN_K && s <= CP_MAX_S && (s <= 4 || wide_fits) && !a.sv2) {
     // the complement of the s trailing Ritz vectors
     const int cp_smem = (int)(sizeof(double) * (size_t)TS_ROWS * k);
-    const int iv_smem = (int)(sizeof(double) * (size_t)nb * ldx);
+    const int iv_smem = (int)(sizeof(double) * (size_t)nb * ldx + rs_bytes);
     if ((e = cudaFuncSetAttribute(cp_complement_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cp_smem)) ==
         cudaSuccess)
       e = cudaFuncSetAttribute(cp_bottom_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, iv_smem);
@@ -1107,7 +1194,7 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
       if ((rc = check_launch("cp_shift_kernel"))) return rc;
       chol_kernel<<<n_cells, CH_NT, chol_smem, st>>>(ws + L.C, k, nbmax, cs, ws + L.rinv, cs);
       if ((rc = check_launch("chol_kernel"))) return rc;
-      cp_bottom_kernel<<<n_cells, 16 * nb, iv_smem, st>>>(a, L, s, nb, ldx);
+      cp_bottom_kernel<<<n_cells, 16 * nb, iv_smem, st>>>(a, L, s, nb, ldx, iters);
       if ((rc = check_launch("cp_bottom_kernel"))) return rc;
     } else {
       // the sketch space itself: tail = 1 - trace(C) / |A|^2

@@ -43,6 +43,7 @@
 #include "kvc_tma.cuh"
 
 namespace kvc {
+int kernel_policy();
 namespace {
 
 using namespace tc;
@@ -127,8 +128,9 @@ __device__ __forceinline__ void load_a_rows(uint32_t tmem_lane_base, uint32_t co
 // residual encode, stats pass: feature-major, one thread per output feature
 // ------------------------------------------------------------------------
 
-template <int D, int RDM, int NS>
+template <int D, int RDM, int NS, bool F16 = false>
 struct StatsLayout {
+  static constexpr int NTERM = F16 ? 2 : 3;                       // terms of Pi in TMEM
   static constexpr uint32_t B_BYTES = TILE_M * D * 2;             // R tile (MMA B operand)
   static constexpr uint32_t T_BYTES = TILE_M * RDM * 4;           // Tucker row term of a tile
   static constexpr uint32_t U_BYTES = RDM == 1 ? D : D * 8;  // per transform warp, its D/2 features of
@@ -137,8 +139,11 @@ struct StatsLayout {
   static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
   static constexpr uint32_t OFF_CORE = OFF_U + 8 * U_BYTES;  // per transform warp: core[h] of the cell
   static constexpr uint32_t OFF_RING = OFF_CORE + 8 * CORE_MAX * 4;  // tile ids drawn by the producer
-  static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
-  static constexpr uint32_t NBAR = 3 * NS + 4;                    // loaded, full, empty, acc full x2, acc empty x2
+  static constexpr uint32_t OFF_TE = OFF_RING + sched::RING * 4;          // fp16 mode: E of each tile (ring)
+  static constexpr uint32_t OFF_WM = OFF_TE + (F16 ? sched::RING * 4 : 0);  // fp16 mode: [2][8] warp maxima
+  static constexpr uint32_t OFF_BAR = OFF_WM + (F16 ? 64 : 0);
+  // loaded, full, empty, acc full x2, acc empty x2 (+ fp16 mode: tile max x2)
+  static constexpr uint32_t NBAR = 3 * NS + 4 + (F16 ? 2 : 0);
   static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
   static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;           // + alignment slack
 };
@@ -163,6 +168,8 @@ struct EncArgs {
   // per output feature n the epilogue's factor 2^-(E + G_n)
   uint32_t* rmax;
   const float* fscale;
+  // STATS (fp16 mode): G_n of the A rows Pi[n][.] * 2^G_n
+  const int32_t* gexp;
 };
 
 // Bits of the bf16 Tucker term of a tile's row ptid (rd = 1): from the
@@ -178,10 +185,11 @@ __device__ __forceinline__ uint32_t enc_row_term(const EncArgs& A, const uint8_t
   return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(v));
 }
 
-template <int D, bool SYM, int RDM, int NS>
+template <int D, bool SYM, int RDM, int NS, bool F16 = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_stats_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ EncArgs A) {
-  using L = StatsLayout<D, RDM, NS>;
+  static_assert(!F16 || RDM == 1, "the fp16 mode takes rank-1 row terms");
+  using L = StatsLayout<D, RDM, NS, F16>;
   static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align1024(smem_raw);
@@ -191,8 +199,10 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   uint64_t* empty = full + NS;
   uint64_t* accf = empty + NS;
   uint64_t* acce = accf + 2;
+  uint64_t* tbar = acce + 2;  // fp16 mode: the transform warps' maxima of a tile are in
   uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_TM);
   int32_t* ring = reinterpret_cast<int32_t*>(smem + L::OFF_RING);
+  int32_t* texp = reinterpret_cast<int32_t*>(smem + L::OFF_TE);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -204,6 +214,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     for (int i = 0; i < 2; ++i) {
       mbar_init(&accf[i], 1);     // tcgen05.commit
       mbar_init(&acce[i], 128);   // epilogue threads
+      if (F16) mbar_init(&tbar[i], 8);  // one arrive per transform warp
     }
     mbar_fence_init();
   }
@@ -216,7 +227,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tm_holder;
   // A operand: Pi, the same for every cell
-  if (warp < 4) load_a_rows<D / 2>(tmem + ((uint32_t)(warp * 32) << 16), 0, A.arows, 3, warp * 32 + lane, 128);
+  if (warp < 4) load_a_rows<D / 2>(tmem + ((uint32_t)(warp * 32) << 16), 0, A.arows, L::NTERM, warp * 32 + lane, 128);
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -256,6 +267,71 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int j = lane; j < (int)(A.rows / A.t_tok); j += 32) cs[j] = load_dt(A.core.p[cell], j, KVC_BF16);
         __syncwarp();
         cur_cell = cell;
+      }
+      if constexpr (F16) {
+        // fp16 mode: this thread's half row of R stays in registers until the
+        // tile's max |R| is known; then R * 2^E, E putting that max in
+        // [2^13, 2^14), goes to the B tile in fp16: exact for every bf16
+        // value above 2^-14 of the scaled range (smaller ones are below the
+        // fp32 resolution of the rotated values).  Rows past the end stay 0.
+        uint8_t* Bs = smem + st * L::B_BYTES;
+        const bool valid = row < A.rows;  // the launcher takes this mode with rt > 0 only
+        uint32_t r[HC * 4];
+        uint32_t mh = 0u;  // max of the bf16 magnitude bits (both halves)
+        if (valid) {
+          const uint32_t th = enc_row_term(A, smem + L::OFF_T + st * L::T_BYTES, cs, ptid, row - ptid);
+          const uint32_t t2 = th | (th << 16);
+          const uint4* u4 = reinterpret_cast<const uint4*>(ub);
+#pragma unroll
+          for (int c = 0; c < HC; ++c) {
+            const uint4 x = *reinterpret_cast<const uint4*>(Bs + sw128_off(ptid, (part * HC + c) * 8, TILE_M));
+            const uint4 u = u4[c];
+            r[4 * c] = bf16x2_sub(x.x, bf16x2_mul(t2, u.x));
+            r[4 * c + 1] = bf16x2_sub(x.y, bf16x2_mul(t2, u.y));
+            r[4 * c + 2] = bf16x2_sub(x.z, bf16x2_mul(t2, u.z));
+            r[4 * c + 3] = bf16x2_sub(x.w, bf16x2_mul(t2, u.w));
+            mh = __vmaxu2(mh, __vmaxu2(__vmaxu2(r[4 * c] & 0x7FFF7FFFu, r[4 * c + 1] & 0x7FFF7FFFu),
+                                       __vmaxu2(r[4 * c + 2] & 0x7FFF7FFFu, r[4 * c + 3] & 0x7FFF7FFFu)));
+          }
+        }
+        const uint32_t wm = __reduce_max_sync(0xffffffffu, max(mh & 0xFFFFu, mh >> 16));
+        uint32_t* wmax = reinterpret_cast<uint32_t*>(smem + L::OFF_WM) + (it & 1) * 8;
+        if (lane == 0) {
+          wmax[part * 4 + lgw] = wm;
+          if (A.rmax && wm) atomicMax(A.rmax + cell, wm << 16);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tbar[it & 1]);
+        if (!warp_wait(&tbar[it & 1], (uint32_t)((it >> 1) & 1), 0x132)) break;
+        uint32_t tmx = 0u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) tmx = max(tmx, wmax[i]);
+        // tmx: bf16 magnitude bits of the tile's max |R| (a subnormal max
+        // counts as 2^-126); E in [-114, 139]
+        const int E = tmx ? 13 - max((int)(tmx >> 7) - 127, -126) : 0;
+        if (warp == 0 && lane == 0) *reinterpret_cast<volatile int32_t*>(&texp[it % sched::RING]) = E;
+        if (valid) {
+          // 2^E as two bf16 factors (each product exact)
+          const int e1 = min(max(E, -100), 100), e2 = E - e1;
+          const uint32_t f1 = (uint32_t)(e1 + 127) << 7, f2 = (uint32_t)(e2 + 127) << 7;
+          const uint32_t p1 = f1 | (f1 << 16), p2 = f2 | (f2 << 16);
+#pragma unroll
+          for (int c = 0; c < HC; ++c) {
+            uint32_t h[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              uint32_t w = bf16x2_mul(r[4 * c + i], p1);
+              if (e2 != 0) w = bf16x2_mul(w, p2);
+              const __half2 h2 = __floats2half2_rn(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+              h[i] = *reinterpret_cast<const uint32_t*>(&h2);
+            }
+            *reinterpret_cast<uint4*>(Bs + sw128_off(ptid, (part * HC + c) * 8, TILE_M)) =
+                make_uint4(h[0], h[1], h[2], h[3]);
+          }
+        }
+        fence_async_smem();
+        mbar_arrive(&full[st]);
+        continue;
       }
       uint32_t rm = 0u;  // float bits of this thread's max |R| (monotonic for non-negative floats)
       if (A.rt > 0 && row < A.rows) {
@@ -343,7 +419,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   } else if (warp == MMA_WARP) {
     // ---------------- MMA issuer: D[feature][row] = sum_k Pi[feature][k] R[row][k] ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(128, TILE_M, true);
+      const uint32_t idesc = idesc_f16(128, TILE_M, !F16);
       int it = 0;
       bool ended = false;
       for (;; ++it) {
@@ -360,7 +436,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t b_base = sbase + st * L::B_BYTES;
         const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * TILE_M);
 #pragma unroll
-        for (int term = 0; term < 3; ++term) {
+        for (int term = 0; term < L::NTERM; ++term) {
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t kb = (uint32_t)((ks >> 2) * (TILE_M * 128) + (ks & 3) * 32);
@@ -383,6 +459,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int feat = lg * 32 + lane;
     const bool active = lg * 32 < D;  // warp-uniform (d = 64 uses lane groups 0-1)
     float run_max = 0.f, rmin = __int_as_float(0x7f800000), rmax = -__int_as_float(0x7f800000);
+    const int gn = F16 && active ? A.gexp[feat] : 0;  // fp16 mode: the accumulators hold R~ * 2^(E + G_n)
     auto flush_stats = [&](int cell) {
       if (!active) return;
       int32_t* mm = A.minmax + (int64_t)cell * 2 * D;
@@ -411,6 +488,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       tc_fence_after();
       const int64_t row0 = tile * TILE_M;
+      // fp16 mode: the tile's extremes in its scaled units, then exactly
+      // rescaled (2^-(E + G_n))
+      float t_abs = 0.f, t_min = __int_as_float(0x7f800000), t_max = -__int_as_float(0x7f800000);
+      float& a_max = F16 ? t_abs : run_max;
+      float& a_lo = F16 ? t_min : rmin;
+      float& a_hi = F16 ? t_max : rmax;
 #pragma unroll
       for (int cc = 0; cc < 4; ++cc) {
         float v[32];
@@ -419,15 +502,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (SYM) {
           // rows past the end hold R = 0 and cannot raise |max|
 #pragma unroll
-          for (int j = 0; j < 32; ++j) run_max = fmaxf(run_max, fabsf(v[j]));
+          for (int j = 0; j < 32; ++j) a_max = fmaxf(a_max, fabsf(v[j]));
         } else {
           const int64_t nvalid = A.rows - (row0 + cc * 32);
 #pragma unroll
           for (int j = 0; j < 32; ++j)
             if (j < nvalid) {
-              rmax = fmaxf(rmax, v[j]);
-              rmin = fminf(rmin, v[j]);
+              a_hi = fmaxf(a_hi, v[j]);
+              a_lo = fminf(a_lo, v[j]);
             }
+        }
+      }
+      if (F16 && active) {
+        const int sh = -(*reinterpret_cast<const volatile int32_t*>(&texp[it % sched::RING]) + gn);
+        if (SYM) {
+          run_max = fmaxf(run_max, ldexpf(t_abs, sh));
+        } else {
+          rmax = fmaxf(rmax, ldexpf(t_max, sh));  // ldexpf keeps +-inf (an empty tile)
+          rmin = fminf(rmin, ldexpf(t_min, sh));
         }
       }
       tc_fence_before();
@@ -529,6 +621,30 @@ __global__ void prep_rotation_kernel(const float* __restrict__ proj, int d, uint
     r1 -= __high2float(h);
     out[((size_t)term * 128 + m) * wpr + w] = *reinterpret_cast<const uint32_t*>(&h);
   }
+}
+
+// A rows of the fp16 stats pass: Pi[m][k] * 2^G_m in two fp16 terms (hi +
+// lo: 22 bits of each entry), G_m = 13 - ilogb(max_k |Pi[m][k]|), as 32-bit
+// pairs [term][m < 128][d / 2]; gexp[m] = G_m.  One block of d / 2 threads
+// per row m.
+__global__ void prep_rotation16_kernel(const float* __restrict__ proj, int d, uint32_t* out, int32_t* gexp) {
+  __shared__ float red[32];
+  const int m = blockIdx.x, w = threadIdx.x, wpr = d / 2;
+  const float r0 = m < d ? proj[m * d + 2 * w] : 0.f, r1 = m < d ? proj[m * d + 2 * w + 1] : 0.f;
+  float mx = fmaxf(fabsf(r0), fabsf(r1));
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((w & 31) == 0) red[w >> 5] = mx;
+  __syncthreads();
+  mx = 0.f;
+  for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) mx = fmaxf(mx, red[i]);
+  const int G = (mx > 0.f && isfinite(mx)) ? 13 - ilogbf(mx) : 0;
+  const float b0 = ldexpf(r0, G), b1 = ldexpf(r1, G);
+  const __half2 hi = __floats2half2_rn(b0, b1);
+  const __half2 lo = __floats2half2_rn(b0 - __low2float(hi), b1 - __high2float(hi));
+  out[(size_t)m * wpr + w] = *reinterpret_cast<const uint32_t*>(&hi);
+  out[((size_t)128 + m) * wpr + w] = *reinterpret_cast<const uint32_t*>(&lo);
+  if (w == 0) gexp[m] = G;
 }
 
 // B images of the quantise pass, per cell: B[n][k] = Pi[n][k] / s_n in three
@@ -1476,7 +1592,7 @@ size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd) {
   const int64_t rows_pad = ceil_div(rows, TILE_M) * TILE_M;
   return align256((size_t)3 * 128 * (d / 2) * 4) + align256((size_t)n_cells * 2 * d * sizeof(int32_t)) +
          align256((size_t)n_cells * rows_pad * rdm_enc(rd) * 4) + align256((size_t)n_cells * 3 * d * d * 2) +
-         align256((size_t)n_cells * 4) + align256((size_t)n_cells * (1 + d) * 4);
+         align256((size_t)n_cells * 4) + align256((size_t)n_cells * (1 + d) * 4) + align256((size_t)128 * 4);
 }
 
 // The Tucker row terms a stats launch left in its workspace, per host thread:
@@ -1560,13 +1676,24 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   uint32_t* rmax = reinterpret_cast<uint32_t*>(ws + off);  // stats: max |R| per cell
   off += align256((size_t)n_cells * 4);
   float* fscale = reinterpret_cast<float*>(ws + off);  // fp16 quantise: 2^E, 2^-(E + G_n) per cell
+  off += align256((size_t)n_cells * (1 + d) * 4);
+  int32_t* gexp = reinterpret_cast<int32_t*>(ws + off);  // fp16 stats: G_n per A row
+  a.gexp = gexp;
   a.arows = arows;
   a.minmax = mm;
   a.tmp = tmp;
   a.rmax = mode == 0 ? rmax : nullptr;
   // the stats pass takes Pi as TMEM rows, the quantise pass Pi / s of each
   // cell as shared-memory B images
-  if (mode == 0) {
+  // policy 2: the stats pass in two fp16 terms of Pi (rank-1 row terms,
+  // d = 128), a third fewer MMAs than three bf16 terms.  Not the default:
+  // inside the compress pipeline on B200 it measured slower than the bf16
+  // pass (the heavier transform outweighs the saved MMAs)
+  const bool f16s = kernel_policy() == 2 && mode == 0 && d == 128 && rdm == 1 && rt > 0;
+  if (f16s) {
+    prep_rotation16_kernel<<<128, d / 2, 0, st>>>(proj, d, arows, gexp);
+    if ((rc = check_launch("prep_rotation16_kernel"))) return rc;
+  } else if (mode == 0) {
     prep_rotation_kernel<<<(128 * (d / 2) + 255) / 256, 256, 0, st>>>(proj, d, arows);
     if ((rc = check_launch("prep_rotation_kernel"))) return rc;
   }
@@ -1577,7 +1704,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
                            tl_rows_key.n_cells == key.n_cells && tl_rows_key.rdm == key.rdm &&
                            tl_rows_key.rows == key.rows && tl_rows_key.core0 == key.core0 &&
                            tl_rows_key.ut0 == key.ut0;
-  const bool f16 = after_stats && d == 128 && rdm == 1 && rt > 0 && scale_mode == KVC_SCALE_CHANNEL;
+  const bool f16 = kernel_policy() == 2 && after_stats && d == 128 && rdm == 1 && rt > 0 && scale_mode == KVC_SCALE_CHANNEL;
   bool direct = rt == 1 && rd == 1 && t % TILE_M == 0 && m <= CORE_MAX;
   for (int c = 0; c < n_cells && direct; ++c) direct = (reinterpret_cast<uintptr_t>(u_token[c]) & 15u) == 0;
   a.rows_direct = direct ? 1 : 0;
@@ -1627,6 +1754,13 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
     if ((rc = set_smem(kern, sm))) return rc;           \
     kern<<<grid, NTHREADS, sm, st>>>(xmaps, a);         \
   } while (0)
+#define KVC_TC_STATS16(SYMV)                                 \
+  do {                                                       \
+    auto kern = tc_stats_kernel<128, SYMV, 1, 6, true>;      \
+    constexpr size_t sm = StatsLayout<128, 1, 6, true>::BYTES; \
+    if ((rc = set_smem(kern, sm))) return rc;                \
+    kern<<<grid, NTHREADS, sm, st>>>(xmaps, a);              \
+  } while (0)
 #define KVC_TC_QUANT(DD, SYMV, RR, NSV)                                          \
   do {                                                                           \
     auto kern = tc_quant_kernel<DD, SYMV, RR, NSV>;                              \
@@ -1648,7 +1782,10 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   } while (0)
   const bool sym = symmetric != 0;
   if (mode == 0) {
-    if (d == 128) {
+    if (f16s) {
+      if (sym) KVC_TC_STATS16(true);
+      else KVC_TC_STATS16(false);
+    } else if (d == 128) {
       if (sym) KVC_TC_ENC_R(KVC_TC_STATS, 128, true, 6);
       else KVC_TC_ENC_R(KVC_TC_STATS, 128, false, 6);
     } else {
@@ -1671,6 +1808,7 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
 #undef KVC_TC_ENC_R
 #undef KVC_TC_QUANT16
 #undef KVC_TC_QUANT
+#undef KVC_TC_STATS16
 #undef KVC_TC_STATS
   if ((rc = check_launch(mode == 0 ? "tc_stats_kernel" : "tc_quant_kernel"))) return rc;
   if (mode == 0) {

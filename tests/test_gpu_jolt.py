@@ -15,7 +15,7 @@ import numpy as np
 import pytest
 import torch
 
-from kvcompress_b200 import CompressedKVCache, build_compressor
+from kvcompress_b200 import CompressedKVCache, build_compressor, ops
 from kvcompress_b200.compressor.allocator import Allocation
 from kvcompress_b200.compressor.flashjolt import FlashJoLTCompressor, flashjolt_cap
 from kvcompress_b200.compressor.jolt import JoLTCompressor
@@ -241,12 +241,14 @@ def test_cache_roundtrip():
     assert len(cache.metadata().layers) == 6
 
 
+@pytest.mark.parametrize("policy", [0, 2])
 @pytest.mark.parametrize("layer,tokens", [(2, 2048), (9, 8192)])
-def test_compress_codes_exact_away_from_ties(layer, tokens):
-    """The codes of the whole compress (for bf16 rank-1 cells its quantise
-    pass runs in fp16 with power-of-two scalings) equal the rounding of the
-    exact rotated residual of the cell's own factors, except within 1e-3
-    quantisation steps of a rounding boundary."""
+def test_compress_codes_exact_away_from_ties(layer, tokens, policy):
+    """The codes of the whole compress (bf16 tensor-core operands, or with
+    kernel policy 2 the stats and quantise passes in two fp16 terms with
+    power-of-two scalings) equal the rounding of the exact rotated residual
+    of the cell's own factors, except within 1e-3 quantisation steps of a
+    rounding boundary."""
     import oracle
     import oracle.jolt
 
@@ -259,7 +261,11 @@ def test_compress_codes_exact_away_from_ties(layer, tokens):
     flips = []
     for x in (k, v):
         xc = x.reshape(8, tokens, 128).cuda()
-        fac = comp.compress_cell(xc, Allocation(1, 1, 8, 0, 0.0)).tucker
+        ops.set_kernel_policy(policy)
+        try:
+            fac = comp.compress_cell(xc, Allocation(1, 1, 8, 0, 0.0)).tucker
+        finally:
+            ops.set_kernel_policy(0)
         m, t, d = xc.shape
         rows = np.arange(m * t)
         recon = recon_rows(f32(fac.core), f32(fac.u_token), f32(fac.u_feature), "bf16", rows, t)
@@ -273,7 +279,7 @@ def test_compress_codes_exact_away_from_ties(layer, tokens):
         diff = got != q
         assert not (diff & ~ties).any(), int((diff & ~ties).sum())
         flips.append(float(diff.sum()) / max(1, int(ties.sum())))
-    print(f"layer {layer}, {tokens} tokens: near-tie flip rate {max(flips):.3f}")
+    print(f"layer {layer}, {tokens} tokens, policy {policy}: near-tie flip rate {max(flips):.3f}")
 
 
 def cached_projection_np(d):

@@ -279,6 +279,47 @@ def test_tensor_core_residual_matches_simt(d, bits, rank):
     print(f"near-tie flip rate d={d} bits={bits} rank={rank}: {max(flips):.3f}")
 
 
+@pytest.mark.parametrize("symmetric", [True, False])
+@pytest.mark.parametrize("mode", [KVC.SCALE_CHANNEL, KVC.SCALE_TENSOR])
+def test_tensor_core_stats_wide_range(symmetric, mode):
+    """Encode stats of rank-1 d = 128 cells on the tensor cores (policy 0:
+    three bf16 terms of Pi; policy 2: two fp16 terms, one power-of-two scale
+    of R per 128-row tile) against the SIMT pass, on cells of magnitude
+    2^-100, 1 and 2^60, the last with tiles stepping through 2^-20, 1, 2^20."""
+    from kvcompress_b200.compressor.jl import cached_projection
+
+    g = torch.Generator(device="cuda").manual_seed(7)
+    m, t, d = 2, 1024, 128
+    proj = cached_projection(d, d, seed=0, device="cuda").matrix
+    tile_step = 2.0 ** (20 * (torch.arange(t, device="cuda") // 128 % 3 - 1).float())
+    xs, cores, uts, uds = [], [], [], []
+    for e, stepped in ((-100, False), (0, False), (60, True)):
+        x = torch.randn(m, t, d, generator=g, device="cuda") * 2.0 ** e
+        if stepped:
+            x = x * tile_step[None, :, None]
+        xs.append(x.bfloat16())
+        cores.append((torch.randn(m, 1, 1, generator=g, device="cuda") * 2.0 ** e).bfloat16())
+        uts.append((torch.randn(t, 1, generator=g, device="cuda") / 30).bfloat16())
+        uds.append((torch.randn(d, 1, generator=g, device="cuda") / 11).bfloat16())
+    out = {}
+    try:
+        for pol in (0, 1, 2):
+            _policy(pol)
+            sc, zp = ops.residual_stats(xs, (cores, uts, uds), proj, bits=8, symmetric=symmetric, scale_mode=mode,
+                                        stat_dtype=torch.float32)
+            out[pol] = ([s.cpu().numpy() for s in sc], [z.cpu().numpy() for z in zp])
+    finally:
+        _policy(0)
+    assert ops.device_error() == 0
+    # 2e-6 (about 16 fp32 ulps): the two passes accumulate the 128 (x 3 terms)
+    # products of a rotated value in different orders
+    for pol in (0, 2):
+        for a, b in zip(out[pol][0], out[1][0]):
+            assert np.all(np.isfinite(a)) and np.all(a > 0) and rel(a, b) < 2e-6, pol
+        for a, b in zip(out[pol][1], out[1][1]):
+            assert np.abs(a.astype(np.int64) - b.astype(np.int64)).max() <= 1, pol
+
+
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("bits", [8, 4, 2])
 @pytest.mark.parametrize("rank", [(1, 1), (7, 4), (6, 12)])
