@@ -4,8 +4,8 @@
 // Rules the callers keep: the innermost box coordinate x times the element
 // size is a multiple of 16 bytes (x is 0 or a multiple of 64 bf16 elements
 // here); global bases are 16-byte aligned and row strides multiples of 16
-// bytes (checked when the map is encoded); loads never use cluster
-// multicast.  Rows outside the tensor read as zeros.
+// bytes (checked when the map is encoded); every load fills the issuing
+// CTA's own shared memory only.  Rows outside the tensor read as zeros.
 #pragma once
 
 #include <cuda.h>
