@@ -23,6 +23,9 @@ namespace kvc {
 
 bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale_mode);
 size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd);
+int simt_row_terms(const void* const* core, const void* const* ut, int n_cells, int dtype, int64_t m, int64_t t,
+                   int rt, int rd, int stride, float* tmp, cudaStream_t st);
+static size_t align256_(size_t x) { return (x + 255) & ~(size_t)255; }
 int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
                        const void* const* core, const void* const* u_token, const void* const* u_feature,
                        int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
@@ -73,6 +76,10 @@ struct ResArgs {
   CellPtrsMut scale, zp, codes;
   int code_bytes;
   int pi_in_smem;
+  // the Tucker row terms of every row, precomputed ([cell][row][rt_stride],
+  // rounded to the cell dtype), or NULL: each tile forms its own
+  const float* rowterm;
+  int rt_stride;
 };
 
 // Load a tile of rows into xs (fp32), subtract the Tucker reconstruction in
@@ -96,15 +103,20 @@ __device__ int residual_tile(const ResArgs& A, int cell, int64_t r0, float* xs, 
     for (int e = threadIdx.x; e < ROWS * rd; e += NT) {
       const int rr = e / rd, r = e % rd;
       float s = 0.f;
-      if (rr < nrow) {
-        const int64_t row = r0 + rr;
-        const int64_t h = row / A.t, t = row % A.t;
-        const T* cr = core + h * rt * rd + r;
-        const T* ur = ut + t * rt;
-        for (int a = 0; a < rt; ++a)
-          s = fmaf(Elt<T>::to_f32(cr[(int64_t)a * rd]), Elt<T>::to_f32(ur[a]), s);
+      if (A.rowterm) {
+        if (rr < nrow) s = A.rowterm[((int64_t)cell * A.rows + r0 + rr) * A.rt_stride + r];
+      } else {
+        if (rr < nrow) {
+          const int64_t row = r0 + rr;
+          const int64_t h = row / A.t, t = row % A.t;
+          const T* cr = core + h * rt * rd + r;
+          const T* ur = ut + t * rt;
+          for (int a = 0; a < rt; ++a)
+            s = fmaf(Elt<T>::to_f32(cr[(int64_t)a * rd]), Elt<T>::to_f32(ur[a]), s);
+        }
+        s = Elt<T>::round(s);
       }
-      tmp[e] = Elt<T>::round(s);
+      tmp[e] = s;
     }
     __syncthreads();
     for (int e = threadIdx.x; e < ROWS * d; e += NT) {
@@ -465,6 +477,13 @@ size_t res_smem(const ResArgs& a, bool quant) {
   return f * sizeof(float);
 }
 
+// Row terms precomputed once per call (simt_row_terms) from this rt on.
+constexpr int ROWTERM_RT = 8;
+int rowterm_stride(int rd) { return rd <= 1 ? 1 : (rd <= 4 ? 4 : (rd <= 16 ? 16 : rd)); }
+size_t rowterm_bytes(int n_cells, int64_t rows, int rd) {
+  return rd > 0 ? align256_(sizeof(float) * (size_t)n_cells * rows * rowterm_stride(rd)) : 0;
+}
+
 int blocks_per_cell(int64_t rows, int n_cells) {
   const int64_t tiles = ceil_div(rows, ROWS);
   const int64_t want = ceil_div(4LL * num_sms(), n_cells);
@@ -478,13 +497,14 @@ using namespace kvc;
 
 extern "C" size_t kvc_residual_stats_workspace_bytes(int n_cells, int64_t rows, int d, int rd) {
   if (n_cells <= 0 || rows <= 0 || d <= 0 || rd < 0) return 0;
-  return std::max((size_t)n_cells * blocks_per_cell(rows, n_cells) * 2 * d * sizeof(float),
+  return std::max(align256_((size_t)n_cells * blocks_per_cell(rows, n_cells) * 2 * d * sizeof(float)) +
+                      rowterm_bytes(n_cells, rows, rd),
                   tc_residual_workspace(n_cells, rows, d, rd));
 }
 
 extern "C" size_t kvc_residual_quant_workspace_bytes(int n_cells, int64_t rows, int d, int rd) {
   if (n_cells <= 0 || rows <= 0 || d <= 0 || rd < 0) return 0;
-  return tc_residual_workspace(n_cells, rows, d, rd);
+  return std::max(tc_residual_workspace(n_cells, rows, d, rd), rowterm_bytes(n_cells, rows, rd));
 }
 
 extern "C" size_t kvc_decompress_workspace_bytes(int n_cells, int64_t rows, int d, int rd) {
@@ -532,13 +552,20 @@ extern "C" int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, 
   if (!workspace || ws_bytes < need) return fail(KVC_ERR_WORKSPACE, "kvc_residual_stats: workspace too small");
   a.partial = static_cast<float*>(workspace);
   a.blocks_per_cell = bpc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rt >= ROWTERM_RT && ws_bytes >= align256_(need) + rowterm_bytes(n_cells, a.rows, rd)) {
+    float* rows_tmp = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + align256_(need));
+    if ((rc = simt_row_terms(core, u_token, n_cells, dtype, m, t, rt, rd, rowterm_stride(rd), rows_tmp, st)))
+      return rc;
+    a.rowterm = rows_tmp;
+    a.rt_stride = rowterm_stride(rd);
+  }
   CellPtrsMut sc, zz;
   for (int c = 0; c < n_cells; ++c) {
     if (!scale_out[c] || !zp_out[c]) return fail(KVC_ERR_ARG, "kvc_residual_stats: NULL output");
     sc.p[c] = scale_out[c];
     zz.p[c] = zp_out[c];
   }
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t smem = res_smem(a, false);
   dim3 grid(bpc, n_cells);
   KVC_DISPATCH_DTYPE(dtype, T, {
@@ -582,6 +609,13 @@ extern "C" int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, 
     a.codes.p[c] = codes[c];
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (rt >= ROWTERM_RT && workspace && ws_bytes >= rowterm_bytes(n_cells, a.rows, rd)) {
+    float* rows_tmp = static_cast<float*>(workspace);
+    if ((rc = simt_row_terms(core, u_token, n_cells, dtype, m, t, rt, rd, rowterm_stride(rd), rows_tmp, st)))
+      return rc;
+    a.rowterm = rows_tmp;
+    a.rt_stride = rowterm_stride(rd);
+  }
   const size_t smem = res_smem(a, true);
   dim3 grid(blocks_per_cell(a.rows, n_cells), n_cells);
   KVC_DISPATCH_DTYPE(dtype, T, {

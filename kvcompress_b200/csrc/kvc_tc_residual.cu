@@ -564,12 +564,86 @@ __global__ void tucker_rows_kernel(CellPtrs core, CellPtrs ut, int fdt, int roun
   }
 }
 
+// The same row terms as one GEMM per head (u_token rows times core[h]) for
+// larger rt: tiles of TR tokens x RDM columns, the rank axis in chunks of 32
+// staged in shared memory; each thread accumulates CW columns of one token
+// over a in order, the fmaf chain of tucker_rows_kernel, so both give the
+// same bits.
+template <int RDM>
+__global__ void __launch_bounds__(256) tucker_rows_tiled_kernel(CellPtrs core, CellPtrs ut, int fdt, int round_dt_,
+                                                                int64_t m, int64_t t0, int64_t tl, int rt, int rd,
+                                                                int64_t cell_stride, float* tmp) {
+  constexpr int CW = RDM >= 4 ? 4 : 1;  // columns per thread
+  constexpr int RG = RDM / CW;          // column groups
+  constexpr int TR = 256 / RG;          // tokens per tile
+  constexpr int KA = 32;                // rank chunk
+  __shared__ float us[TR][KA + 1];
+  __shared__ __align__(16) float cs[KA][RDM];
+  const int cell = blockIdx.y;
+  const int ti = threadIdx.x / RG, g = threadIdx.x % RG;
+  const int64_t per_head = (tl + TR - 1) / TR;
+  for (int64_t tile = blockIdx.x; tile < m * per_head; tile += gridDim.x) {
+    const int64_t h = tile / per_head, i0 = (tile - h * per_head) * TR;
+    float acc[CW];
+#pragma unroll
+    for (int q = 0; q < CW; ++q) acc[q] = 0.f;
+    for (int a0 = 0; a0 < rt; a0 += KA) {
+      const int ka = min(KA, rt - a0);
+      __syncthreads();  // the previous chunk is consumed
+      for (int e = threadIdx.x; e < TR * KA; e += blockDim.x) {
+        const int ii = e / KA, aa = e % KA;
+        us[ii][aa] = (aa < ka && i0 + ii < tl) ? load_dt(ut.p[cell], (t0 + i0 + ii) * rt + a0 + aa, fdt) : 0.f;
+      }
+      for (int e = threadIdx.x; e < KA * RDM; e += blockDim.x) {
+        const int aa = e / RDM, r = e % RDM;
+        cs[aa][r] = (aa < ka && r < rd) ? load_dt(core.p[cell], (h * rt + a0 + aa) * rd + r, fdt) : 0.f;
+      }
+      __syncthreads();
+      for (int aa = 0; aa < ka; ++aa) {
+        const float u = us[ti][aa];
+#pragma unroll
+        for (int q = 0; q < CW; ++q) acc[q] = fmaf(cs[aa][g * CW + q], u, acc[q]);
+      }
+    }
+    if (i0 + ti < tl) {
+      float* o = tmp + ((int64_t)cell * cell_stride + h * tl + i0 + ti) * RDM + g * CW;
+#pragma unroll
+      for (int q = 0; q < CW; ++q) o[q] = g * CW + q < rd ? round_dt(acc[q], round_dt_) : 0.f;
+    }
+  }
+}
+
 int rdm_enc(int rd) { return rd <= 1 ? 1 : 4; }
 int rdm_dec(int rd) { return rd <= 1 ? 1 : (rd <= 4 ? 4 : 16); }
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
 constexpr int kMaxCtas = 1024;  // grid cap of the persistent kernels
+constexpr int ROWTERM_TILED_RT = 8;  // rt from which the row terms take the tiled kernel
+
+// tmp[cell][row][rdm] (cell_stride rows per cell) = the Tucker row terms of
+// rows h * tl + i, tokens t0 + i (rdm 1, 4 or 16).
+int row_terms_launch(const CellPtrs& core, const CellPtrs& ut, int n_cells, int fdt, int round_dt_, int64_t m,
+                     int64_t t0, int64_t tl, int rt, int rd, int rdm, int64_t cell_stride, float* tmp,
+                     cudaStream_t st) {
+  if (rt >= ROWTERM_TILED_RT && (rdm == 1 || rdm == 4 || rdm == 16)) {
+    const int rg = rdm >= 4 ? rdm / 4 : 1, tr = 256 / rg;
+    const int64_t tiles = m * ((tl + tr - 1) / tr);
+    const dim3 grid((unsigned)std::max<int64_t>(1, std::min<int64_t>(tiles, 8 * num_sms())), n_cells);
+    if (rdm == 1)
+      tucker_rows_tiled_kernel<1><<<grid, 256, 0, st>>>(core, ut, fdt, round_dt_, m, t0, tl, rt, rd, cell_stride, tmp);
+    else if (rdm == 4)
+      tucker_rows_tiled_kernel<4><<<grid, 256, 0, st>>>(core, ut, fdt, round_dt_, m, t0, tl, rt, rd, cell_stride, tmp);
+    else
+      tucker_rows_tiled_kernel<16><<<grid, 256, 0, st>>>(core, ut, fdt, round_dt_, m, t0, tl, rt, rd, cell_stride,
+                                                         tmp);
+    return check_launch("tucker_rows_tiled_kernel");
+  }
+  const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(m * tl * rdm, 256), 1024));
+  tucker_rows_kernel<<<dim3(blocks, n_cells), 256, 0, st>>>(core, ut, fdt, round_dt_, m, t0, tl, rt, rd, rdm,
+                                                            cell_stride, tmp);
+  return check_launch("tucker_rows_kernel");
+}
 
 // min / max arrays to their identities (ordered ints of +inf / -inf).
 __global__ void minmax_init_kernel(int32_t* mm, int n_cells, int d, uint32_t* rmax) {
@@ -1581,6 +1655,18 @@ int set_smem(K kernel, size_t bytes) {
 
 }  // namespace
 
+// Row terms of the SIMT residual passes: tmp[cell][row][stride] (rows = m * t
+// per cell) rounded to the cell dtype, as the reference's einsum intermediate.
+int simt_row_terms(const void* const* core, const void* const* ut, int n_cells, int dtype, int64_t m, int64_t t,
+                   int rt, int rd, int stride, float* tmp, cudaStream_t st) {
+  CellPtrs cp, up;
+  for (int c = 0; c < n_cells; ++c) {
+    cp.p[c] = core[c];
+    up.p[c] = ut[c];
+  }
+  return row_terms_launch(cp, up, n_cells, dtype, dtype, m, 0, t, rt, rd, stride, m * t, tmp, st);
+}
+
 // ------------------------------- launchers --------------------------------
 
 bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale_mode) {
@@ -1737,10 +1823,9 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
       cp.p[c] = core[c];
       up.p[c] = u_token[c];
     }
-    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows * rdm, 256), 1024));
-    tucker_rows_kernel<<<dim3(blocks, n_cells), 256, 0, st>>>(cp, up, KVC_BF16, KVC_BF16, m, 0, t, rt, rd, rdm,
-                                                              a.tiles_per_cell * TILE_M, tmp);
-    if ((rc = check_launch("tucker_rows_kernel"))) return rc;
+    if ((rc = row_terms_launch(cp, up, n_cells, KVC_BF16, KVC_BF16, m, 0, t, rt, rd, rdm, a.tiles_per_cell * TILE_M,
+                               tmp, st)))
+      return rc;
   }
   const dim3 grid((unsigned)ceil_div(a.total_tiles, a.tiles_per_cta));
   if (mode == 0) {
@@ -1937,10 +2022,9 @@ int tc_decode_plan_run(const TcDecodePlan* p, int64_t t0, int64_t t1, void* cons
     }
   }
   if (rt > 0 && !direct) {
-    const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(m * tl * rdm, 256), 1024));
-    tucker_rows_kernel<<<dim3(blocks, n_cells), 256, 0, st>>>(p->core, p->ut, p->factor_dtype, KVC_F32, m, t0, tl, rt,
-                                                              rd, rdm, m * tl, p->tmp);
-    if ((rc = check_launch("tucker_rows_kernel"))) return rc;
+    if ((rc = row_terms_launch(p->core, p->ut, n_cells, p->factor_dtype, KVC_F32, m, t0, tl, rt, rd, rdm, m * tl,
+                               p->tmp, st)))
+      return rc;
   }
   const dim3 grid((unsigned)ceil_div(a.total_tiles, a.tiles_per_cta));
   const TmaMaps& cmaps = p->cmaps;
