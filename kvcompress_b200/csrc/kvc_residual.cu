@@ -592,7 +592,8 @@ extern "C" int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, 
   if (scale_mode == KVC_SCALE_GROUP && (group_size <= 0 || d % group_size != 0))
     return fail(KVC_ERR_SHAPE, "kvc_residual_quant: d must be divisible by group_size");
   if (!dtype_ok(arith_dtype)) return fail(KVC_ERR_DTYPE, "kvc_residual_quant: bad arith dtype");
-  if (g_policy != 1 && scale_mode != KVC_SCALE_GROUP && tc_residual_eligible(dtype, d, rd, proj, scale_mode) &&
+  if (g_policy != 1 && scale_mode != KVC_SCALE_GROUP && (bits == 2 || bits == 4 || bits == 8) &&
+      tc_residual_eligible(dtype, d, rd, proj, scale_mode) &&
       all_aligned(n_cells, x) && all_aligned(n_cells, codes) && workspace &&
       ws_bytes >= tc_residual_workspace(n_cells, m * t, d, rd)) {
     return tc_residual_launch(1, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,

@@ -815,11 +815,12 @@ struct QuantLayout {
   static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;
 };
 
-template <int D, bool SYM, int RDM, int NS, bool F16 = false>
+template <int D, bool SYM, int RDM, int NS, bool F16, int BITS>
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_quant_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ TmaMaps cmaps,
                     const __grid_constant__ EncArgs A, const uint8_t* bimg) {
   static_assert(!F16 || RDM == 1, "the fp16 mode takes rank-1 row terms");
+  static_assert(BITS == 2 || BITS == 4 || BITS == 8, "codes of 2, 4 or 8 bits");
   using L = QuantLayout<D, RDM, NS, F16>;
   static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   constexpr uint32_t ACOLS = D / 2;  // TMEM columns of one A buffer (bf16 pairs)
@@ -1085,13 +1086,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     // conflict-free) and leave by one TMA store of whole rows; 8-byte half
     // rows (d = 64, 2 bits) are stored directly.
     uint8_t* stg = smem + L::OFF_Q + e * L::Q_BYTES;
-    const int cbw = (D / 2) * A.bits / 8;
-    const bool tma_out = cbw >= 16;
+    constexpr int cbw = (D / 2) * BITS / 8;
+    constexpr bool tma_out = cbw >= 16;
     const int swz = tma_out ? ((lane * cbw) >> 7) & (cbw / 16 - 1) : 0;
     uint8_t* srow = stg + lane * cbw;
     int qmin, qmax;
-    qrange(A.bits, A.symmetric, qmin, qmax);
-    const int offset = A.symmetric ? (1 << (A.bits - 1)) : 0;
+    qrange(BITS, SYM ? 1 : 0, qmin, qmax);
+    constexpr int offset = SYM ? (1 << (BITS - 1)) : 0;
     const int ad = A.scale_mode == KVC_SCALE_TENSOR ? A.arith_dtype : KVC_F32;
     const bool fast = A.scale_mode != KVC_SCALE_TENSOR || A.arith_dtype == KVC_F32;
     const float magic = 12582912.0f + (float)offset;  // 1.5 * 2^23 + offset
@@ -1156,7 +1157,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           for (int j = 0; j < 32; ++j) code[j] = quantize_one(v[j], s_t, zp_t, qmin, qmax, ad) + offset;
         }
         // low byte of each code is (q + offset) & 0xFF
-        if (A.bits == 8) {
+        if constexpr (BITS == 8) {
           uint32_t w[8];
 #pragma unroll
           for (int q = 0; q < 8; ++q)
@@ -1165,7 +1166,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           const int j = cc * 2;  // 16-byte chunks of the staged half row
           *reinterpret_cast<uint4*>(srow + ((j ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
           *reinterpret_cast<uint4*>(srow + (((j + 1) ^ swz) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
-        } else if (A.bits == 4) {
+        } else if constexpr (BITS == 4) {
           uint32_t w[4];
 #pragma unroll
           for (int q = 0; q < 4; ++q) {
@@ -1189,7 +1190,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             w[q] = __byte_perm(__byte_perm(pb[0], pb[1], 0x0040), __byte_perm(pb[2], pb[3], 0x0040), 0x5410);
           }
-          if (tma_out) {
+          if constexpr (tma_out) {
             // 8 bytes per 32 features: chunk cc / 2, half cc % 2
             *reinterpret_cast<uint2*>(srow + (((cc >> 1) ^ swz) << 4) + (cc & 1) * 8) = make_uint2(w[0], w[1]);
           } else if (row < A.rows) {
@@ -1698,6 +1699,29 @@ static thread_local bool tl_rows_reuse = false;
 
 void tc_reuse_tucker_rows(bool allow) { tl_rows_reuse = allow; }
 
+// One quantise launch, the code width as a template argument (the epilogue's
+// packing and store path fixed at compile time).
+template <int D, bool SYM, int RDM, int NS, bool F16, int BITS>
+int launch_quant_bits(dim3 grid, cudaStream_t st, const TmaMaps& xmaps, const TmaMaps& cmaps, const EncArgs& a,
+                      const uint8_t* bimg) {
+  auto kern = tc_quant_kernel<D, SYM, RDM, NS, F16, BITS>;
+  constexpr size_t sm = QuantLayout<D, RDM, NS, F16>::BYTES;
+  int rc;
+  if ((rc = set_smem(kern, sm))) return rc;
+  kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, bimg);
+  return KVC_OK;
+}
+template <int D, bool SYM, int RDM, int NS, bool F16>
+int launch_quant(int bits, dim3 grid, cudaStream_t st, const TmaMaps& xmaps, const TmaMaps& cmaps, const EncArgs& a,
+                 const uint8_t* bimg) {
+  switch (bits) {
+    case 8: return launch_quant_bits<D, SYM, RDM, NS, F16, 8>(grid, st, xmaps, cmaps, a, bimg);
+    case 4: return launch_quant_bits<D, SYM, RDM, NS, F16, 4>(grid, st, xmaps, cmaps, a, bimg);
+    case 2: return launch_quant_bits<D, SYM, RDM, NS, F16, 2>(grid, st, xmaps, cmaps, a, bimg);
+    default: return fail(KVC_ERR_ARG, "tensor-core quantise: bits must be 2, 4 or 8");
+  }
+}
+
 int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
                        const void* const* core, const void* const* u_token, const void* const* u_feature,
                        int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
@@ -1846,19 +1870,13 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
     if ((rc = set_smem(kern, sm))) return rc;                \
     kern<<<grid, NTHREADS, sm, st>>>(xmaps, a);              \
   } while (0)
-#define KVC_TC_QUANT(DD, SYMV, RR, NSV)                                          \
-  do {                                                                           \
-    auto kern = tc_quant_kernel<DD, SYMV, RR, NSV>;                              \
-    constexpr size_t sm = QuantLayout<DD, RR, NSV>::BYTES;                       \
-    if ((rc = set_smem(kern, sm))) return rc;                                    \
-    kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, bimg);                     \
+#define KVC_TC_QUANT(DD, SYMV, RR, NSV)                                                          \
+  do {                                                                                           \
+    if ((rc = launch_quant<DD, SYMV, RR, NSV, false>(bits, grid, st, xmaps, cmaps, a, bimg))) return rc; \
   } while (0)
-#define KVC_TC_QUANT16(SYMV)                                                     \
-  do {                                                                           \
-    auto kern = tc_quant_kernel<128, SYMV, 1, 4, true>;                          \
-    constexpr size_t sm = QuantLayout<128, 1, 4, true>::BYTES;                   \
-    if ((rc = set_smem(kern, sm))) return rc;                                    \
-    kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, bimg);                     \
+#define KVC_TC_QUANT16(SYMV)                                                                     \
+  do {                                                                                           \
+    if ((rc = launch_quant<128, SYMV, 1, 4, true>(bits, grid, st, xmaps, cmaps, a, bimg))) return rc; \
   } while (0)
 #define KVC_TC_ENC_R(WHICH, DD, SYMV, NSV)     \
   do {                                         \
