@@ -317,19 +317,19 @@ def workload_config(w, n, alloc):
 
 # ----------------------------------------------------------------- GPU legs
 
-PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "tc_kernels_llama3-8b-8layers.md")
+PROFILE_SUMMARY = os.path.join(ROOT, "profiles", "tc_encode_llama3-8b-b8-t32768-1layer.md")
 
 
 def ncu_traffic(stage: str, cells: int, rows_per_cell: int):
     """DRAM bytes (read + write) of one launch of ``stage`` from the committed
-    ncu summary (a capture of 16 cells of 65,536 rows), scaled by the rows the
+    ncu summary (bytes per row of a captured launch), scaled by the rows the
     launch processes; None when the summary has no figure for the stage."""
     try:
         with open(PROFILE_SUMMARY) as f:
             for line in f:
                 parts = line.split()
-                if len(parts) == 3 and parts[0] == "traffic_per_cell_bytes" and parts[1] == stage:
-                    return float(parts[2]) * cells * rows_per_cell / 65536.0
+                if len(parts) == 3 and parts[0] == "traffic_per_row_bytes" and parts[1] == stage:
+                    return float(parts[2]) * cells * rows_per_cell
     except OSError:
         pass
     return None
