@@ -608,6 +608,129 @@ __global__ void __launch_bounds__(CH_NT) chol_kernel(double* Sb, int k, int nbma
   }
 }
 
+// Multi-CTA Cholesky for the wider sketches, left-looking by panels of CHP
+// rows, one launch per panel: CTA b of a panel takes the panel rows' columns
+// [j0 + 32 b, j0 + 32 b + 32).  It subtracts the earlier panels' rows of R
+// (staged 32 x 32 blocks, the next one loaded into registers while the
+// current one is used), eliminates the panel's diagonal block (every CTA,
+// redundantly: the pivots and multipliers of its columns) with the rank
+// dropping of chol_kernel, and writes its columns of the panel rows of R
+// into the upper triangle.  The original values come from the lower
+// triangle of S (the Gram is a full symmetric product and the upper
+// triangle only is overwritten) and from dg0, the original diagonal, so no
+// CTA reads what another CTA of the same launch writes.
+constexpr int CHP = 32;
+constexpr int CHP_MIN_K = 64;  // narrower sketches keep the single-CTA chol_kernel
+
+__global__ void chol_diag_copy_kernel(const double* Sb, int k, int64_t sS, double* dg0b, int64_t sD) {
+  const double* S = Sb + blockIdx.y * sS;
+  double* dg0 = dg0b + blockIdx.y * sD;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < k; i += gridDim.x * blockDim.x)
+    dg0[i] = S[(int64_t)i * k + i];
+}
+
+__global__ void __launch_bounds__(256, 1) chol_panel_kernel(double* Sb, int k, int64_t sS, double* rinvb, int64_t sR,
+                                                         const double* dg0b, int64_t sD, int j0) {
+  __shared__ double D[CHP][CHP + 1];   // the panel's diagonal block: D[r][q], q >= r
+  __shared__ double Sl[CHP][CHP + 1];  // the panel rows of this CTA's columns
+  __shared__ double A[CHP][CHP + 1];   // R[i0 + i][j0 + r] of the current chunk
+  __shared__ double B[CHP][CHP + 1];   // R[i0 + i][c0 + c] of the current chunk
+  __shared__ double rsv[CHP];
+  const int cell = blockIdx.y, blk = blockIdx.x;
+  double* S = Sb + cell * sS;
+  double* rinv = rinvb + cell * sR;
+  const double* dg0 = dg0b + cell * sD;
+  const int nb = min(CHP, k - j0);
+  const int c0 = j0 + blk * CHP, ncol = min(CHP, k - c0);
+  const bool diag = blk == 0;
+  const int tr = threadIdx.x >> 3, tq = (threadIdx.x & 7) * 4;  // 4 outputs a thread: row tr, columns tq..tq+3
+  double pd[4], ps[4];
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int qq = tq + q;
+    pd[q] = 0.0;
+    ps[q] = 0.0;
+    if (tr < nb && qq < nb && qq >= tr) pd[q] = qq == tr ? dg0[j0 + tr] : S[(int64_t)(j0 + qq) * k + j0 + tr];
+    if (!diag && tr < nb && qq < ncol) ps[q] = S[(int64_t)(c0 + qq) * k + j0 + tr];
+  }
+  // the earlier panels: P -= sum_{i < j0} R[i][j0 + r] R[i][column]
+  double na[4], nbv[4];
+  auto fetch = [&](int i0) {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = threadIdx.x + 256 * j, i = e >> 5, c = e & 31;
+      na[j] = c < nb ? S[(int64_t)(i0 + i) * k + j0 + c] : 0.0;
+      nbv[j] = (!diag && c < ncol) ? S[(int64_t)(i0 + i) * k + c0 + c] : 0.0;
+    }
+  };
+  if (j0 > 0) fetch(0);
+  for (int i0 = 0; i0 < j0; i0 += CHP) {  // j0 is a multiple of CHP: whole chunks of finished rows
+    __syncthreads();  // the previous chunk is consumed
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int e = threadIdx.x + 256 * j, i = e >> 5, c = e & 31;
+      A[i][c] = na[j];
+      B[i][c] = nbv[j];
+    }
+    __syncthreads();
+    if (i0 + CHP < j0) fetch(i0 + CHP);
+#pragma unroll 4
+    for (int i = 0; i < CHP; ++i) {
+      const double a = A[i][tr];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        pd[q] = fma(-a, A[i][tq + q], pd[q]);
+        ps[q] = fma(-a, B[i][tq + q], ps[q]);
+      }
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    D[tr][tq + q] = pd[q];
+    Sl[tr][tq + q] = ps[q];
+  }
+  __syncthreads();
+  // the panel: pivot r, row r - 1 scaled one step late, rows q > r updated
+  // with the unscaled row r times 1 / d
+  for (int r = 0; r < nb; ++r) {
+    if (threadIdx.x == 0) {
+      const double d = D[r][r], o = dg0[j0 + r];
+      rsv[r] = (o > 0.0 && d > 1e-10 * o) ? 1.0 / sqrt(d) : 0.0;
+    }
+    __syncthreads();
+    const double inv_d = rsv[r] * rsv[r];
+    if (r > 0) {
+      const double rs = rsv[r - 1];
+      for (int x = r - 1 + threadIdx.x; x < nb; x += blockDim.x) D[r - 1][x] *= rs;
+      if (!diag && (int)threadIdx.x < ncol) Sl[r - 1][threadIdx.x] *= rs;
+    }
+    for (int e = threadIdx.x; e < (nb - 1 - r) * CHP; e += blockDim.x) {
+      const int q = r + 1 + (e >> 5), x = e & 31;
+      const double f = D[r][q] * inv_d;
+      if (x >= q && x < nb) D[q][x] = fma(-f, D[r][x], D[q][x]);
+      if (!diag && x < ncol) Sl[q][x] = fma(-f, Sl[r][x], Sl[q][x]);
+    }
+    __syncthreads();
+  }
+  {
+    const double rs = rsv[nb - 1];
+    for (int x = nb - 1 + threadIdx.x; x < nb; x += blockDim.x) D[nb - 1][x] *= rs;
+    if (!diag && (int)threadIdx.x < ncol) Sl[nb - 1][threadIdx.x] *= rs;
+  }
+  __syncthreads();
+  // the panel rows of R: the diagonal CTA writes the block's upper triangle
+  // and the inverse pivots, the others their columns
+  for (int e = threadIdx.x; e < nb * CHP; e += blockDim.x) {
+    const int r = e >> 5, x = e & 31;
+    if (diag) {
+      if (x >= r && x < nb) S[(int64_t)(j0 + r) * k + j0 + x] = D[r][x];
+    } else if (x < ncol) {
+      S[(int64_t)(j0 + r) * k + c0 + x] = Sl[r][x];
+    }
+  }
+  if (diag && (int)threadIdx.x < nb) rinv[j0 + threadIdx.x] = rsv[threadIdx.x];
+}
+
 constexpr int TS_ROWS = 16;  // rows of W per CTA: 16 lanes of a warp per row
 constexpr int TS_NT = 256;
 
@@ -766,6 +889,61 @@ __device__ void rows_solve(double* Wl, int ldw, int k, const double* __restrict_
   __syncthreads();
 }
 
+// out = X M for the blockDim / 16 rows of X (row stride ldx; row threadIdx
+// / 16, lane threadIdx % 16 owns columns l and l + 16 of a block), M k x k
+// (row stride k) streamed through the Rs ring of staged blocks in the order
+// (column block jb, then row blocks ib); out: global, row stride k.
+template <int NBUF>
+__device__ void rows_times(const double* X, int ldx, int k, const double* __restrict__ M, double* out, double* Rs) {
+  const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
+  const double* xr = X + r * ldx;
+  const int nbk = (k + 31) / 32;
+  const int total = nbk * nbk;
+  auto stage = [&](int n, double* buf) {
+    const int jb = n / nbk, ib = n - jb * nbk;
+    for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+      const int i = e >> 5, c = e & 31, row = ib * 32 + i, col = jb * 32 + c;
+      const bool ok = row < k && col < k;
+      cp_async8(buf + i * RS_LD + c, ok ? M + (int64_t)row * k + col : M, ok);
+    }
+  };
+  __syncthreads();  // Rs is free
+#pragma unroll 1
+  for (int n = 0; n < NBUF - 1; ++n) {
+    if (n < total) stage(n, Rs + n * RS_BLOCK);
+    cp_async_commit8();
+  }
+  double a0 = 0.0, a1 = 0.0;
+#pragma unroll 1
+  for (int n = 0; n < total; ++n) {
+    cp_async_wait8<NBUF - 2>();
+    __syncthreads();
+    if (n + NBUF - 1 < total) stage(n + NBUF - 1, Rs + ((n + NBUF - 1) % NBUF) * RS_BLOCK);
+    cp_async_commit8();
+    const double* B = Rs + (n % NBUF) * RS_BLOCK;
+    const int jb = n / nbk, ib = n - jb * nbk, I0 = ib * 32, ni = min(32, k - I0);
+    for (int i = 0; i < ni; ++i) {
+      const double xi = xr[I0 + i];
+      a0 = fma(xi, B[i * RS_LD + lane], a0);
+      a1 = fma(xi, B[i * RS_LD + lane + 16], a1);
+    }
+    if (ib == nbk - 1) {
+      const int c = jb * 32 + lane;
+      if (c < k) out[(int64_t)r * k + c] = a0;
+      if (c + 16 < k) out[(int64_t)r * k + c + 16] = a1;
+      a0 = a1 = 0.0;
+    }
+  }
+  cp_async_wait8<0>();
+  __syncthreads();
+}
+
+__global__ void identity_kernel(double* Ab, int k, int64_t sA) {
+  double* A = Ab + blockIdx.y * sA;
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)k * k; e += (int64_t)gridDim.x * blockDim.x)
+    A[e] = (e / k == e % k) ? 1.0 : 0.0;
+}
+
 // W <- W R^{-1} per cell (R upper triangular from chol_kernel, rinv its
 // inverse pivots; a dropped column of R gives a zero column of W).  Each CTA
 // holds TS_ROWS rows of W in shared memory and sweeps the columns in blocks
@@ -869,9 +1047,10 @@ __global__ void lr_store_kernel(SolveArgs a, LrLayout L) {
 // compress call): the span of the `rank` leading Ritz vectors is the
 // complement, inside the sketch space, of the s = k - rank trailing ones, and
 // s is at most the oversampling.  So only the trailing ones are found: block
-// inverse iteration on C + delta I (its Cholesky factor from chol_kernel;
-// nb = 16 vectors for s <= 4, else 32; each step W <- W R^{-1} R^{-T} and
-// CholeskyQR2 of the rows), a Rayleigh-Ritz on the nb x nb projection, then
+// inverse iteration on C + delta I (nb = 16 vectors for s <= 4, else 32;
+// (C + delta I)^-1 = R^-1 R^-T formed once from its Cholesky factor, each
+// step W <- W (C + delta I)^-1 and CholeskyQR2 of the rows), a
+// Rayleigh-Ritz on the nb x nb projection, then
 // Householder reflectors H_0 .. H_{s-1} of the s trailing vectors; the basis
 // is (W H_0 ... H_{s-1})[:, s:].  Its columns are an orthonormal basis of
 // the same Ritz subspace (not ordered by singular value); the tail mass is
@@ -959,13 +1138,14 @@ __device__ inline void cp_orth_rows(double* X, int ldx, int k, int nb, double* G
 }
 
 // One CTA of 16 nb threads per cell: the s trailing Ritz vectors of C by
-// block inverse iteration on nb vectors (16 or 32; the row solves give each
-// vector 16 threads) and Rayleigh-Ritz, then their Householder reflectors
-// (v_q in the S slot, rows of length k; tau_q in the lam slot) and the tail
-// mass.
+// block inverse iteration on nb vectors (16 or 32; the products with the
+// inverse in the S slot give each vector 16 threads, through xn_off: nb x k
+// doubles of scratch) and Rayleigh-Ritz, then their Householder reflectors
+// (v_q in the S slot once the inverse is done with, rows of length k; tau_q
+// in the lam slot) and the tail mass.
 __global__ void __launch_bounds__(16 * IV_MAX) cp_bottom_kernel(SolveArgs a, LrLayout L, int s, int nb, int ldx,
-                                                                 int iters) {
-  extern __shared__ double X[];  // nb rows of stride ldx, then CP_NBUF staged blocks of R
+                                                                 int iters, int64_t xn_off) {
+  extern __shared__ double X[];  // nb rows of stride ldx, then CP_NBUF staged blocks
   __shared__ double G[IV_MAX * IV_MAX], T[IV_MAX * IV_MAX], Mb[IV_MAX * 32];
   __shared__ double Zs[CP_MAX_S * IV_MAX], vec[8 * IV_MAX], lam[IV_MAX], red[64];
   __shared__ double scr[3 * IV_MAX * CP_MAX_S];
@@ -973,7 +1153,8 @@ __global__ void __launch_bounds__(16 * IV_MAX) cp_bottom_kernel(SolveArgs a, LrL
   const int cell = blockIdx.x, k = a.k;
   double* ws = a.ws + cell * a.ws_cell;
   const double* R = ws + L.C;
-  const double* rinv = ws + L.rinv;
+  const double* Cinv = ws + L.S;  // (C + delta I)^-1 = R^-1 R^-T
+  double* Xn = ws + xn_off;       // nb x k of scratch (the free p x k slot)
   for (int e = threadIdx.x; e < nb * ldx; e += blockDim.x) {
     const int r = e / ldx, c = e % ldx;
     X[e] = c < k ? eig::start_entry(r, c) : 0.0;
@@ -982,8 +1163,11 @@ __global__ void __launch_bounds__(16 * IV_MAX) cp_bottom_kernel(SolveArgs a, LrL
   cp_orth_rows(X, ldx, k, nb, G);
   cp_orth_rows(X, ldx, k, nb, G);
   for (int it = 0; it < iters; ++it) {
-    rows_solve<false, CP_NBUF>(X, ldx, k, R, rinv, X + (size_t)nb * ldx);
-    rows_solve<true, CP_NBUF>(X, ldx, k, R, rinv, X + (size_t)nb * ldx);
+    rows_times<CP_NBUF>(X, ldx, k, Cinv, Xn, X + (size_t)nb * ldx);
+    for (int e = threadIdx.x; e < nb * k; e += blockDim.x) {
+      const int r = e / k, c = e - r * k;
+      X[r * ldx + c] = Xn[e];
+    }
     __syncthreads();
     cp_orth_rows(X, ldx, k, nb, G);
     cp_orth_rows(X, ldx, k, nb, G);
@@ -1121,6 +1305,26 @@ __global__ void __launch_bounds__(TS_NT) cp_complement_kernel(SolveArgs a, LrLay
   }
 }
 
+// S -> R (upper triangle, S = R^T R) and rinv for every cell: the panel
+// launches for k >= CHP_MIN_K (dg0: k doubles of scratch per cell), else
+// chol_kernel.
+int chol_launch(double* S, int k, int nbmax, size_t chol_smem, int64_t cs, double* rinv, double* dg0, int n_cells,
+                cudaStream_t st) {
+  if (k < CHP_MIN_K) {
+    chol_kernel<<<n_cells, CH_NT, chol_smem, st>>>(S, k, nbmax, cs, rinv, cs);
+    return check_launch("chol_kernel");
+  }
+  int rc;
+  chol_diag_copy_kernel<<<dim3(1, n_cells), 256, 0, st>>>(S, k, cs, dg0, cs);
+  if ((rc = check_launch("chol_diag_copy_kernel"))) return rc;
+  for (int j0 = 0; j0 < k; j0 += CHP) {
+    const dim3 grid((k - j0 + CHP - 1) / CHP, n_cells);
+    chol_panel_kernel<<<grid, 256, 0, st>>>(S, k, cs, rinv, cs, dg0, cs, j0);
+    if ((rc = check_launch("chol_panel_kernel"))) return rc;
+  }
+  return KVC_OK;
+}
+
 int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
   const int p = a.p, k = a.k;
   const LrLayout L = lr_layout(p, k);
@@ -1151,8 +1355,7 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
       rhs = ws + oth;
     }
     if ((r2 = gemm(ws + cur, cs, k, 1, rhs, cs, k, 0, ws + L.S, cs, k, k, k, p))) return r2;
-    chol_kernel<<<n_cells, CH_NT, chol_smem, st>>>(ws + L.S, k, nbmax, cs, ws + L.rinv, cs);
-    if ((r2 = check_launch("chol_kernel"))) return r2;
+    if ((r2 = chol_launch(ws + L.S, k, nbmax, chol_smem, cs, ws + L.rinv, ws + L.lam, n_cells, st))) return r2;
     const dim3 grid((p + TS_ROWS - 1) / TS_ROWS, n_cells);
     trsm_kernel<<<grid, TS_NT, trsm_smem, st>>>(ws + cur, p, k, cs, ws + L.S, cs, ws + L.rinv, cs);
     return check_launch("trsm_kernel");
@@ -1192,9 +1395,16 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
     if (s > 0) {
       cp_shift_kernel<<<n_cells, 256, 0, st>>>(ws, cs, L, k);
       if ((rc = check_launch("cp_shift_kernel"))) return rc;
-      chol_kernel<<<n_cells, CH_NT, chol_smem, st>>>(ws + L.C, k, nbmax, cs, ws + L.rinv, cs);
-      if ((rc = check_launch("chol_kernel"))) return rc;
-      cp_bottom_kernel<<<n_cells, 16 * nb, iv_smem, st>>>(a, L, s, nb, ldx, iters);
+      if ((rc = chol_launch(ws + L.C, k, nbmax, chol_smem, cs, ws + L.rinv, ws + L.lam, n_cells, st))) return rc;
+      // (C + delta I)^-1 = R^-1 R^-T: R^-1 as the rows of I R^-1 (one
+      // row-parallel triangular solve), then one product
+      identity_kernel<<<dim3(64, n_cells), 256, 0, st>>>(ws + L.Zt, k, cs);
+      if ((rc = check_launch("identity_kernel"))) return rc;
+      const dim3 tgrid((k + TS_ROWS - 1) / TS_ROWS, n_cells);
+      trsm_kernel<<<tgrid, TS_NT, trsm_smem, st>>>(ws + L.Zt, k, k, cs, ws + L.C, cs, ws + L.rinv, cs);
+      if ((rc = check_launch("trsm_kernel"))) return rc;
+      if ((rc = gemm(ws + L.Zt, cs, k, 0, ws + L.Zt, cs, k, 1, ws + L.S, cs, k, k, k, k))) return rc;
+      cp_bottom_kernel<<<n_cells, 16 * nb, iv_smem, st>>>(a, L, s, nb, ldx, iters, oth);
       if ((rc = check_launch("cp_bottom_kernel"))) return rc;
     } else {
       // the sketch space itself: tail = 1 - trace(C) / |A|^2
