@@ -889,55 +889,6 @@ __device__ void rows_solve(double* Wl, int ldw, int k, const double* __restrict_
   __syncthreads();
 }
 
-// out = X M for the blockDim / 16 rows of X (row stride ldx; row threadIdx
-// / 16, lane threadIdx % 16 owns columns l and l + 16 of a block), M k x k
-// (row stride k) streamed through the Rs ring of staged blocks in the order
-// (column block jb, then row blocks ib); out: global, row stride k.
-template <int NBUF>
-__device__ void rows_times(const double* X, int ldx, int k, const double* __restrict__ M, double* out, double* Rs) {
-  const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
-  const double* xr = X + r * ldx;
-  const int nbk = (k + 31) / 32;
-  const int total = nbk * nbk;
-  auto stage = [&](int n, double* buf) {
-    const int jb = n / nbk, ib = n - jb * nbk;
-    for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
-      const int i = e >> 5, c = e & 31, row = ib * 32 + i, col = jb * 32 + c;
-      const bool ok = row < k && col < k;
-      cp_async8(buf + i * RS_LD + c, ok ? M + (int64_t)row * k + col : M, ok);
-    }
-  };
-  __syncthreads();  // Rs is free
-#pragma unroll 1
-  for (int n = 0; n < NBUF - 1; ++n) {
-    if (n < total) stage(n, Rs + n * RS_BLOCK);
-    cp_async_commit8();
-  }
-  double a0 = 0.0, a1 = 0.0;
-#pragma unroll 1
-  for (int n = 0; n < total; ++n) {
-    cp_async_wait8<NBUF - 2>();
-    __syncthreads();
-    if (n + NBUF - 1 < total) stage(n + NBUF - 1, Rs + ((n + NBUF - 1) % NBUF) * RS_BLOCK);
-    cp_async_commit8();
-    const double* B = Rs + (n % NBUF) * RS_BLOCK;
-    const int jb = n / nbk, ib = n - jb * nbk, I0 = ib * 32, ni = min(32, k - I0);
-    for (int i = 0; i < ni; ++i) {
-      const double xi = xr[I0 + i];
-      a0 = fma(xi, B[i * RS_LD + lane], a0);
-      a1 = fma(xi, B[i * RS_LD + lane + 16], a1);
-    }
-    if (ib == nbk - 1) {
-      const int c = jb * 32 + lane;
-      if (c < k) out[(int64_t)r * k + c] = a0;
-      if (c + 16 < k) out[(int64_t)r * k + c + 16] = a1;
-      a0 = a1 = 0.0;
-    }
-  }
-  cp_async_wait8<0>();
-  __syncthreads();
-}
-
 __global__ void identity_kernel(double* Ab, int k, int64_t sA) {
   double* A = Ab + blockIdx.y * sA;
   for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < (int64_t)k * k; e += (int64_t)gridDim.x * blockDim.x)
@@ -1105,19 +1056,24 @@ __device__ inline void cp_orth_rows(double* X, int ldx, int k, int nb, double* G
     G[a * IV_MAX + b] = s0 + s1;
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    // G = L L^T in place (lower), rank dropping; L[j][j] stored inverted
+  if (threadIdx.x < 32) {
+    // G = L L^T in place (lower), rank dropping; L[j][j] stored inverted.
+    // Left-looking by columns; lane i > j forms L[i][j] (the sums in the
+    // order of the scalar recurrence)
+    const int lane = threadIdx.x;
     for (int j = 0; j < nb; ++j) {
       const double o = G[j * IV_MAX + j];
       double d = o;
       for (int q = 0; q < j; ++q) d -= G[j * IV_MAX + q] * G[j * IV_MAX + q];
       const double ri = (o > 0.0 && d > 1e-10 * o) ? 1.0 / sqrt(d) : 0.0;
-      G[j * IV_MAX + j] = ri;
-      for (int i2 = j + 1; i2 < nb; ++i2) {
-        double v = G[i2 * IV_MAX + j];
-        for (int q = 0; q < j; ++q) v -= G[i2 * IV_MAX + q] * G[j * IV_MAX + q];
-        G[i2 * IV_MAX + j] = v * ri;
+      if (lane > j && lane < nb) {
+        double v = G[lane * IV_MAX + j];
+        for (int q = 0; q < j; ++q) v -= G[lane * IV_MAX + q] * G[j * IV_MAX + q];
+        G[lane * IV_MAX + j] = v * ri;
       }
+      __syncwarp();
+      if (lane == 0) G[j * IV_MAX + j] = ri;
+      __syncwarp();
     }
   }
   __syncthreads();
@@ -1137,24 +1093,16 @@ __device__ inline void cp_orth_rows(double* X, int ldx, int k, int nb, double* G
   __syncthreads();
 }
 
-// One CTA of 16 nb threads per cell: the s trailing Ritz vectors of C by
-// block inverse iteration on nb vectors (16 or 32; the products with the
-// inverse in the S slot give each vector 16 threads, through xn_off: nb x k
-// doubles of scratch) and Rayleigh-Ritz, then their Householder reflectors
-// (v_q in the S slot once the inverse is done with, rows of length k; tau_q
-// in the lam slot) and the tail mass.
-__global__ void __launch_bounds__(16 * IV_MAX) cp_bottom_kernel(SolveArgs a, LrLayout L, int s, int nb, int ldx,
-                                                                 int iters, int64_t xn_off) {
-  extern __shared__ double X[];  // nb rows of stride ldx, then CP_NBUF staged blocks
-  __shared__ double G[IV_MAX * IV_MAX], T[IV_MAX * IV_MAX], Mb[IV_MAX * 32];
-  __shared__ double Zs[CP_MAX_S * IV_MAX], vec[8 * IV_MAX], lam[IV_MAX], red[64];
-  __shared__ double scr[3 * IV_MAX * CP_MAX_S];
-  __shared__ int cnt[16 * IV_MAX];
-  const int cell = blockIdx.x, k = a.k;
-  double* ws = a.ws + cell * a.ws_cell;
-  const double* R = ws + L.C;
-  const double* Cinv = ws + L.S;  // (C + delta I)^-1 = R^-1 R^-T
-  double* Xn = ws + xn_off;       // nb x k of scratch (the free p x k slot)
+// The block inverse iteration on nb vectors, in launches: cp_start_kernel
+// (the start block, orthonormalised), then per step iv_mult_kernel (X C^-1
+// over a grid of one CTA per 32 columns) and iv_orth_kernel (CholeskyQR2 of
+// the block), then cp_bottom_kernel.  The block lives in the workspace at
+// xoff (nb rows of length k), the product at xnoff.
+__global__ void __launch_bounds__(16 * IV_MAX) cp_start_kernel(SolveArgs a, int nb, int ldx, int64_t xoff) {
+  extern __shared__ double X[];  // nb rows of stride ldx
+  __shared__ double G[IV_MAX * IV_MAX];
+  const int k = a.k;
+  double* out = a.ws + blockIdx.x * a.ws_cell + xoff;
   for (int e = threadIdx.x; e < nb * ldx; e += blockDim.x) {
     const int r = e / ldx, c = e % ldx;
     X[e] = c < k ? eig::start_entry(r, c) : 0.0;
@@ -1162,16 +1110,116 @@ __global__ void __launch_bounds__(16 * IV_MAX) cp_bottom_kernel(SolveArgs a, LrL
   __syncthreads();
   cp_orth_rows(X, ldx, k, nb, G);
   cp_orth_rows(X, ldx, k, nb, G);
-  for (int it = 0; it < iters; ++it) {
-    rows_times<CP_NBUF>(X, ldx, k, Cinv, Xn, X + (size_t)nb * ldx);
-    for (int e = threadIdx.x; e < nb * k; e += blockDim.x) {
-      const int r = e / k, c = e - r * k;
-      X[r * ldx + c] = Xn[e];
-    }
-    __syncthreads();
-    cp_orth_rows(X, ldx, k, nb, G);
-    cp_orth_rows(X, ldx, k, nb, G);
+  for (int e = threadIdx.x; e < nb * k; e += blockDim.x) {
+    const int r = e / k, c = e - r * k;
+    out[e] = X[r * ldx + c];
   }
+}
+
+// Columns [32 jb, 32 jb + 32) of X (C + delta I)^-1 (the inverse in the S
+// slot), jb = blockIdx.x: the block's rows in shared memory, the inverse's
+// column block streamed through the ring of staged blocks; thread (row
+// threadIdx / 16, lane) owns columns lane and lane + 16.
+__global__ void __launch_bounds__(16 * IV_MAX) iv_mult_kernel(SolveArgs a, LrLayout L, int nb, int ldx, int64_t xoff,
+                                                              int64_t xnoff) {
+  extern __shared__ double X[];  // nb rows of stride ldx, then CP_NBUF staged blocks
+  const int cell = blockIdx.y, jb = blockIdx.x, k = a.k;
+  double* ws = a.ws + cell * a.ws_cell;
+  const double* Cinv = ws + L.S;
+  const double* xin = ws + xoff;
+  double* out = ws + xnoff;
+  double* Rs = X + (size_t)nb * ldx;
+  for (int e = threadIdx.x; e < nb * k; e += blockDim.x) {
+    const int r = e / k, c = e - r * k;
+    X[r * ldx + c] = xin[e];
+  }
+  const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
+  const double* xr = X + r * ldx;
+  const int nbk = (k + 31) / 32;
+  auto stage = [&](int ib, double* buf) {
+    for (int e = threadIdx.x; e < 1024; e += blockDim.x) {
+      const int i = e >> 5, c = e & 31, row = ib * 32 + i, col = jb * 32 + c;
+      const bool ok = row < k && col < k;
+      cp_async8(buf + i * RS_LD + c, ok ? Cinv + (int64_t)row * k + col : Cinv, ok);
+    }
+  };
+#pragma unroll 1
+  for (int n = 0; n < CP_NBUF - 1; ++n) {
+    if (n < nbk) stage(n, Rs + n * RS_BLOCK);
+    cp_async_commit8();
+  }
+  double a0 = 0.0, a1 = 0.0;
+#pragma unroll 1
+  for (int ib = 0; ib < nbk; ++ib) {
+    cp_async_wait8<CP_NBUF - 2>();
+    __syncthreads();  // block ib is in (and, the first time, the rows of X)
+    if (ib + CP_NBUF - 1 < nbk) stage(ib + CP_NBUF - 1, Rs + ((ib + CP_NBUF - 1) % CP_NBUF) * RS_BLOCK);
+    cp_async_commit8();
+    const double* B = Rs + (ib % CP_NBUF) * RS_BLOCK;
+    const int I0 = ib * 32;
+    if (k - I0 >= 32) {
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const double xi = xr[I0 + i];
+        a0 = fma(xi, B[i * RS_LD + lane], a0);
+        a1 = fma(xi, B[i * RS_LD + lane + 16], a1);
+      }
+    } else {
+      for (int i = 0; i < k - I0; ++i) {
+        const double xi = xr[I0 + i];
+        a0 = fma(xi, B[i * RS_LD + lane], a0);
+        a1 = fma(xi, B[i * RS_LD + lane + 16], a1);
+      }
+    }
+  }
+  cp_async_wait8<0>();
+  const int c = jb * 32 + lane;
+  if (c < k) out[(int64_t)r * k + c] = a0;
+  if (c + 16 < k) out[(int64_t)r * k + c + 16] = a1;
+}
+
+// CholeskyQR2 of the product block (xnoff) back into the block (xoff).
+__global__ void __launch_bounds__(16 * IV_MAX) iv_orth_kernel(SolveArgs a, int nb, int ldx, int64_t xnoff,
+                                                              int64_t xoff) {
+  extern __shared__ double X[];  // nb rows of stride ldx
+  __shared__ double G[IV_MAX * IV_MAX];
+  const int k = a.k;
+  double* ws = a.ws + blockIdx.x * a.ws_cell;
+  const double* xin = ws + xnoff;
+  double* out = ws + xoff;
+  for (int e = threadIdx.x; e < nb * ldx; e += blockDim.x) {
+    const int r = e / ldx, c = e % ldx;
+    X[e] = c < k ? xin[(int64_t)r * k + c] : 0.0;
+  }
+  __syncthreads();
+  cp_orth_rows(X, ldx, k, nb, G);
+  cp_orth_rows(X, ldx, k, nb, G);
+  for (int e = threadIdx.x; e < nb * k; e += blockDim.x) {
+    const int r = e / k, c = e - r * k;
+    out[e] = X[r * ldx + c];
+  }
+}
+
+// One CTA of 16 nb threads per cell, after the inverse iteration: the
+// Rayleigh-Ritz on the converged block (xoff), the s trailing Ritz vectors,
+// their Householder reflectors (v_q in the S slot, rows of length k; tau_q in
+// the lam slot) and the tail mass.
+__global__ void __launch_bounds__(16 * IV_MAX, 1) cp_bottom_kernel(SolveArgs a, LrLayout L, int s, int nb, int ldx,
+                                                                 int64_t xoff) {
+  extern __shared__ double X[];  // nb rows of stride ldx
+  __shared__ double G[IV_MAX * IV_MAX], T[IV_MAX * IV_MAX], Mb[IV_MAX * 32];
+  __shared__ double Zs[CP_MAX_S * IV_MAX], vec[8 * IV_MAX], lam[IV_MAX], red[64];
+  __shared__ double scr[3 * IV_MAX * CP_MAX_S];
+  __shared__ int cnt[16 * IV_MAX];
+  const int cell = blockIdx.x, k = a.k;
+  double* ws = a.ws + cell * a.ws_cell;
+  const double* R = ws + L.C;
+  const double* xin = ws + xoff;
+  for (int e = threadIdx.x; e < nb * ldx; e += blockDim.x) {
+    const int r = e / ldx, c = e % ldx;
+    X[e] = c < k ? xin[(int64_t)r * k + c] : 0.0;
+  }
+  __syncthreads();
   // T = (X R^T)(X R^T)^T - delta I = X C X^T, 32 columns of M = X R^T at a time
   for (int e = threadIdx.x; e < IV_MAX * IV_MAX; e += blockDim.x) T[e] = 0.0;
   __syncthreads();
@@ -1391,6 +1439,12 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
     if ((e = cudaFuncSetAttribute(cp_complement_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cp_smem)) ==
         cudaSuccess)
       e = cudaFuncSetAttribute(cp_bottom_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, iv_smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(cp_start_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, iv_smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(iv_mult_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, iv_smem);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(iv_orth_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, iv_smem);
     if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
     if (s > 0) {
       cp_shift_kernel<<<n_cells, 256, 0, st>>>(ws, cs, L, k);
@@ -1404,7 +1458,18 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
       trsm_kernel<<<tgrid, TS_NT, trsm_smem, st>>>(ws + L.Zt, k, k, cs, ws + L.C, cs, ws + L.rinv, cs);
       if ((rc = check_launch("trsm_kernel"))) return rc;
       if ((rc = gemm(ws + L.Zt, cs, k, 0, ws + L.Zt, cs, k, 1, ws + L.S, cs, k, k, k, k))) return rc;
-      cp_bottom_kernel<<<n_cells, 16 * nb, iv_smem, st>>>(a, L, s, nb, ldx, iters, oth);
+      const int64_t xoff = oth, xnoff = oth + (int64_t)nb * k;  // the free p x k slot (p >= k > 2 nb)
+      const int xs_smem = (int)(sizeof(double) * (size_t)nb * ldx);
+      cp_start_kernel<<<n_cells, 16 * nb, xs_smem, st>>>(a, nb, ldx, xoff);
+      if ((rc = check_launch("cp_start_kernel"))) return rc;
+      const dim3 mgrid((k + 31) / 32, n_cells);
+      for (int it = 0; it < iters; ++it) {
+        iv_mult_kernel<<<mgrid, 16 * nb, iv_smem, st>>>(a, L, nb, ldx, xoff, xnoff);
+        if ((rc = check_launch("iv_mult_kernel"))) return rc;
+        iv_orth_kernel<<<n_cells, 16 * nb, xs_smem, st>>>(a, nb, ldx, xnoff, xoff);
+        if ((rc = check_launch("iv_orth_kernel"))) return rc;
+      }
+      cp_bottom_kernel<<<n_cells, 16 * nb, xs_smem, st>>>(a, L, s, nb, ldx, xoff);
       if ((rc = check_launch("cp_bottom_kernel"))) return rc;
     } else {
       // the sketch space itself: tail = 1 - trace(C) / |A|^2
