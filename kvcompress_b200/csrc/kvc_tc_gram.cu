@@ -14,7 +14,8 @@
 // NY = 64 (SWIZZLE_128B) with four stages up to k = 32.
 //
 // Work: every cell is cut into segments of a fixed number of tiles that
-// depends on the row count only; CTAs take contiguous runs of segments, keep
+// depends on the row count only; CTAs take contiguous runs of segments in an
+// order that runs the cells fastest (every cell shares Omega), keep
 // one segment's sum in a TMEM accumulator (two buffers, so the flush of one
 // overlaps the next), flush it to a per-segment fp32 partial, and a second
 // kernel sums the segments of each cell in order in fp64.  The result of a
@@ -135,8 +136,14 @@ __global__ void __launch_bounds__(NTH, 1)
     if (lane == 0) {
       sched::Cursor cur((A.total_segs + gridDim.x - 1) / gridDim.x, A.total_segs);
       int j = 0;  // stage uses so far
+      const int64_t n_cells = A.total_segs / A.segs_per_cell;
       for (int si = 0;; ++si) {
-        const int64_t sg = sched::next_tile(cur);
+        // the schedule runs the cells fastest (g = segment * n_cells + cell),
+        // so a CTA takes one row range of every cell in turn and reads that
+        // range of Omega from L2 after the first cell; the id published is
+        // the segment's own (cell-major: its partial slot and its rows)
+        const int64_t g = sched::next_tile(cur);
+        const int64_t sg = g < 0 ? -1 : (g % n_cells) * A.segs_per_cell + g / n_cells;
         sched::ring_put(ring, si, (int32_t)sg);
         if (sg < 0) {  // the end, through the next stage with no bytes
           const int st = j % NS;
