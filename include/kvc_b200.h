@@ -274,7 +274,10 @@ int kvc_trace_stages(void* const* events, int n_events);
  *    factors in fp16 / bf16 over whole 128-token blocks starting at a
  *    multiple of 8 (the row terms are formed inside the decode), two
  *    otherwise; bit for bit the same rows as kvc_decompress over that range.  Runs of one plan
- *    share its workspace: issue them on one stream.
+ *    share its workspace: issue them on one stream.  While the stream is
+ *    being captured into a CUDA graph, a one-kernel run (head_dim 128) is
+ *    launched as a programmatic dependent of the previous launch, so
+ *    consecutive runs may overlap: give each captured run its own outputs.
  */
 size_t kvc_decode_plan_bytes(void);
 int kvc_decode_plan_init(void* plan, size_t plan_bytes, int n_cells, const uint8_t* const* codes,

@@ -1287,6 +1287,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   using L = DecLayout<D, CB, RDM, NS>;
   static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   static_assert(CB % 16 == 0, "code rows must be whole 16-byte chunks");
+  // a run launched as a programmatic dependent of this one may start at once:
+  // it reads nothing this one writes
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   constexpr bool FOLD = L::FOLD;
   // TMEM columns of one A buffer: D / 2 (+ 8 for the Tucker K-step, padded
   // so both buffers start on a 32-column boundary)
@@ -2046,13 +2049,42 @@ int tc_decode_plan_run(const TcDecodePlan* p, int64_t t0, int64_t t1, void* cons
   }
   const dim3 grid((unsigned)ceil_div(a.total_tiles, a.tiles_per_cta));
   const TmaMaps& cmaps = p->cmaps;
-#define KVC_TC_DEC3(DD, RR, BB)                                      \
-  do {                                                               \
-    constexpr int NSD = DecStages<DD, DD * BB / 8, RR>::value;       \
-    auto kern = tc_decode_kernel<DD, RR, BB, NSD>;                   \
-    using LL = DecLayout<DD, DD * BB / 8, RR, NSD>;                  \
-    if ((rc = set_smem(kern, LL::BYTES))) return rc;                 \
-    kern<<<grid, NTHREADS, LL::BYTES, st>>>(cmaps, omaps, a);        \
+  // Inside stream capture (DecodeStream.capture: every block decodes into its
+  // own outputs, with nothing else between the decodes), a run with rank-1
+  // factors (no row-term scratch shared between runs) is launched as a
+  // programmatic dependent of the run before it: consecutive runs are
+  // independent, so this run's CTAs start on the SMs the previous one's
+  // finishing CTAs free (its kernel lets dependents launch at once).  Only
+  // for layouts of more than half an SM's shared memory: one CTA per SM, so
+  // two runs never share an SM's tensor memory.
+  bool pdl = false;
+  if (direct) {
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    pdl = cudaStreamIsCapturing(st, &cap) == cudaSuccess && cap == cudaStreamCaptureStatusActive;
+  }
+#define KVC_TC_DEC3(DD, RR, BB)                                                        \
+  do {                                                                                 \
+    constexpr int NSD = DecStages<DD, DD * BB / 8, RR>::value;                         \
+    auto kern = tc_decode_kernel<DD, RR, BB, NSD>;                                     \
+    using LL = DecLayout<DD, DD * BB / 8, RR, NSD>;                                    \
+    if ((rc = set_smem(kern, LL::BYTES))) return rc;                                   \
+    if (pdl && LL::BYTES > 116 * 1024) {                                               \
+      cudaLaunchConfig_t cfg = {};                                                     \
+      cfg.gridDim = grid;                                                              \
+      cfg.blockDim = dim3(NTHREADS);                                                   \
+      cfg.dynamicSmemBytes = LL::BYTES;                                                \
+      cfg.stream = st;                                                                 \
+      cudaLaunchAttribute attr[1];                                                     \
+      attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;                 \
+      attr[0].val.programmaticStreamSerializationAllowed = 1;                          \
+      cfg.attrs = attr;                                                                \
+      cfg.numAttrs = 1;                                                                \
+      const cudaError_t le = cudaLaunchKernelEx(&cfg, kern, cmaps, omaps, a);          \
+      if (le != cudaSuccess)                                                           \
+        return fail(KVC_ERR_LAUNCH, std::string("tc_decode_kernel: ") + cudaGetErrorString(le)); \
+    } else {                                                                           \
+      kern<<<grid, NTHREADS, LL::BYTES, st>>>(cmaps, omaps, a);                        \
+    }                                                                                  \
   } while (0)
 #define KVC_TC_DEC(DD, RR)                      \
   do {                                          \
