@@ -298,6 +298,8 @@ int kvc_decode_plan_run(const void* plan, size_t plan_bytes, int64_t t0, int64_t
  * Policy 2: as 0 with the residual encode's fp16 two-term modes (stats pass
  * and, after it in one compress call, quantise pass with Pi in two fp16
  * terms and R scaled by powers of two; d = 128, rank-1 row terms).
+ * Policy 3: as 0 with the row-major tensor-core quantise pass everywhere
+ * (policy 0 takes the feature-major one for d = 128 and 8- or 4-bit codes).
  * Process-wide; set it while no call is in flight.
  */
 int kvc_set_kernel_policy(int policy);

@@ -44,7 +44,8 @@ int tc_read_device_error(int* out);
 int tc_gram_read_device_error(int* out);
 
 // 0: tensor cores when eligible (bf16 operands), 1: SIMT kernels only,
-// 2: as 0 with the residual encode's fp16 two-term modes
+// 2: as 0 with the residual encode's fp16 two-term modes, 3: as 0 with the
+// row-major tensor-core quantise pass for every layout
 static int g_policy = 0;
 int kernel_policy() { return g_policy; }
 
@@ -513,8 +514,9 @@ extern "C" size_t kvc_decompress_workspace_bytes(int n_cells, int64_t rows, int 
 }
 
 extern "C" int kvc_set_kernel_policy(int policy) {
-  if (policy < 0 || policy > 2)
-    return fail(KVC_ERR_ARG, "kvc_set_kernel_policy: 0 (auto), 1 (SIMT) or 2 (fp16 two-term encode)");
+  if (policy < 0 || policy > 3)
+    return fail(KVC_ERR_ARG,
+                "kvc_set_kernel_policy: 0 (auto), 1 (SIMT), 2 (fp16 two-term encode) or 3 (row-major quantise)");
   g_policy = policy;
   return KVC_OK;
 }

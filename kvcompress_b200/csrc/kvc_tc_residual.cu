@@ -1223,6 +1223,328 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 }
 
 // ------------------------------------------------------------------------
+// quantise pass, feature-major (d = 128, 8- and 4-bit codes): A = Pi / s of
+// the cell in three bf16 terms in TMEM (192 columns; the transform warps
+// reload them when the tile stream enters a new cell, after the MMAs of the
+// previous tile have completed), B = R in place in the TMA stage as in the
+// stats pass.  Shared memory then holds five x stages instead of the row-
+// major pass's three next to its 96 KB B image.  TMEM lane = output feature:
+// an epilogue thread quantises its feature's values of the tile's rows and
+// writes the code byte of each row (4-bit: even lanes, the byte of the
+// feature pair) into its warp's [128 rows][CBW] staging block, which the
+// warp stores by TMA (two staging buffers a warp).
+// ------------------------------------------------------------------------
+template <int RDM, int NS>
+struct QuantFmLayout {
+  static constexpr int D = 128;
+  static constexpr uint32_t B_BYTES = TILE_M * D * 2;         // x stage = R tile (MMA B operand)
+  static constexpr uint32_t T_BYTES = TILE_M * RDM * 4;       // Tucker row term of a tile
+  static constexpr uint32_t U_BYTES = RDM == 1 ? D : D * 8;   // per transform warp, as the stats pass
+  static constexpr uint32_t Q_BYTES = TILE_M * 32;            // per epilogue warp and buffer: 128 rows x 32 bytes
+  static constexpr uint32_t OFF_Q = NS * B_BYTES;
+  static constexpr uint32_t OFF_T = OFF_Q + 4 * 2 * Q_BYTES;
+  static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
+  static constexpr uint32_t OFF_CORE = OFF_U + 8 * U_BYTES;  // per transform warp: core[h] of the cell
+  static constexpr uint32_t OFF_RING = OFF_CORE + 8 * CORE_MAX * 4;
+  static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
+  static constexpr uint32_t NBAR = 3 * NS + 4;  // loaded, full, empty, acc full x2, acc empty x2
+  static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
+  static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;
+};
+
+// A rows of the feature-major quantise pass, per cell: Pi[n][k] / s_n
+// (s_0 for per-tensor scales) split in three bf16 terms, as 32-bit pairs
+// [cell][term][n < 128][d / 2] (k = 2w in the low half): the same values as
+// the row-major pass's B images.
+__global__ void prep_quant_arows_kernel(const float* __restrict__ proj, CellPtrs scale, int per_feature, int d,
+                                        uint32_t* out) {
+  const int cell = blockIdx.y;
+  const int e = blockIdx.x * blockDim.x + threadIdx.x;  // (n, w) over d x d/2
+  const int wpr = d / 2;
+  if (e >= d * wpr) return;
+  const int n = e / wpr, w = e % wpr;
+  const float s = static_cast<const float*>(scale.p[cell])[per_feature ? n : 0];
+  float r0 = __fdiv_rn(proj[n * d + 2 * w], s), r1 = __fdiv_rn(proj[n * d + 2 * w + 1], s);
+  uint32_t* base = out + (size_t)cell * 3 * 128 * wpr;
+  for (int term = 0; term < 3; ++term) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(r0, r1);
+    r0 -= __low2float(h);
+    r1 -= __high2float(h);
+    base[((size_t)term * 128 + n) * wpr + w] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+template <bool SYM, int RDM, int NS, int BITS>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    tc_quantfm_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ TmaMaps cmaps,
+                      const __grid_constant__ EncArgs A, const uint32_t* arows) {
+  constexpr int D = 128;
+  using L = QuantFmLayout<RDM, NS>;
+  static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
+  static_assert(BITS == 8 || BITS == 4, "feature-major codes of 8 or 4 bits");
+  constexpr int CBW = 32 * BITS / 8;  // code bytes of a warp's 32 features in a row
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* loaded = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* full = loaded + NS;
+  uint64_t* empty = full + NS;
+  uint64_t* accf = empty + NS;
+  uint64_t* acce = accf + 2;
+  uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_TM);
+  int32_t* ring = reinterpret_cast<int32_t*>(smem + L::OFF_RING);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&loaded[i], 1);  // TMA issue + transaction bytes
+      mbar_init(&full[i], 256);  // transform threads
+      mbar_init(&empty[i], 1);   // tcgen05.commit
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&accf[i], 1);    // tcgen05.commit
+      mbar_init(&acce[i], 128);  // epilogue threads
+    }
+    mbar_fence_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tm_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tm_holder;
+
+  if (warp < 4 || warp >= STATS_XF_WARP1) {
+    // ---------------- transform: R = x - recon, in place, one row per thread ----------------
+    constexpr int HF = D / 2, HC = HF / 8;
+    const int lgw = warp & 3, part = warp < 4 ? 0 : 1;
+    const int ptid = lgw * 32 + lane;
+    float* u32 = reinterpret_cast<float*>(smem + L::OFF_U + (part * 4 + lgw) * L::U_BYTES);       // [j][4]
+    uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + (part * 4 + lgw) * L::U_BYTES);  // [j]
+    float* cs = reinterpret_cast<float*>(smem + L::OFF_CORE) + (part * 4 + lgw) * CORE_MAX;     // [h]
+    int cur_cell = -1;
+    for (int it = 0;; ++it) {
+      const int st = it % NS;
+      if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x181)) break;
+      const int32_t g = sched::ring_get(ring, it);
+      if (g < 0) {  // no more tiles: pass the end on to the MMA thread
+        mbar_arrive(&full[st]);
+        break;
+      }
+      const int cell = (int)(g / A.tiles_per_cell);
+      const int64_t row = (g % A.tiles_per_cell) * TILE_M + ptid;
+      if (cell != cur_cell) {
+        if (warp < 4) {
+          // Pi / s of the new cell into TMEM, once the MMAs of the previous
+          // tile (the last ones to read the old terms) have completed
+          if (it > 0 && !warp_wait(&empty[(it - 1) % NS], (uint32_t)(((it - 1) / NS) & 1), 0x182)) break;
+          tc_fence_after();
+          load_a_rows<D / 2>(tmem + ((uint32_t)(warp * 32) << 16), 0, arows + (size_t)cell * 3 * 128 * (D / 2), 3,
+                             warp * 32 + lane, 128);
+          tc_fence_before();
+        }
+        if (A.rt > 0) {
+          __syncwarp();
+          const __nv_bfloat16* ud = static_cast<const __nv_bfloat16*>(A.ud.p[cell]);
+          if (RDM == 1) {
+            for (int j = lane; j < HF; j += 32) ub[j] = reinterpret_cast<const uint16_t*>(ud)[part * HF + j];
+          } else {
+            for (int i = lane; i < HF * 4; i += 32) {
+              const int j = i >> 2, r = i & 3;
+              u32[i] = r < A.rd ? __bfloat162float(ud[(part * HF + j) * A.rd + r]) : 0.f;
+            }
+          }
+          if (A.rows_direct)
+            for (int j = lane; j < (int)(A.rows / A.t_tok); j += 32) cs[j] = load_dt(A.core.p[cell], j, KVC_BF16);
+          __syncwarp();
+        }
+        cur_cell = cell;
+      }
+      if (A.rt > 0 && row < A.rows) {
+        uint8_t* Bs = smem + st * L::B_BYTES;
+        if (RDM == 1) {
+          const uint32_t th = enc_row_term(A, smem + L::OFF_T + st * L::T_BYTES, cs, ptid, row - ptid);
+          const uint32_t t2 = th | (th << 16);
+          const uint4* u4 = reinterpret_cast<const uint4*>(ub);
+#pragma unroll
+          for (int c = 0; c < HC; ++c) {
+            uint4* slot = reinterpret_cast<uint4*>(Bs + sw128_off(ptid, (part * HC + c) * 8, TILE_M));
+            uint4 x = *slot;
+            const uint4 u = u4[c];
+            x.x = bf16x2_sub(x.x, bf16x2_mul(t2, u.x));
+            x.y = bf16x2_sub(x.y, bf16x2_mul(t2, u.y));
+            x.z = bf16x2_sub(x.z, bf16x2_mul(t2, u.z));
+            x.w = bf16x2_sub(x.w, bf16x2_mul(t2, u.w));
+            *slot = x;
+          }
+        } else {
+          const float4 tv =
+              *reinterpret_cast<const float4*>(smem + L::OFF_T + st * L::T_BYTES + ptid * RDM * 4);
+          const float4* u4 = reinterpret_cast<const float4*>(u32);
+#pragma unroll 2
+          for (int c = 0; c < HC; ++c) {
+            uint4* slot = reinterpret_cast<uint4*>(Bs + sw128_off(ptid, (part * HC + c) * 8, TILE_M));
+            float xv[8];
+            unpack8_bf16(*slot, xv);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const float4 u = u4[c * 8 + e];
+              float rec = tv.x * u.x;
+              rec = fmaf(tv.y, u.y, rec);
+              rec = fmaf(tv.z, u.z, rec);
+              rec = fmaf(tv.w, u.w, rec);
+              xv[e] = Elt<__nv_bfloat16>::round(xv[e] - Elt<__nv_bfloat16>::round(rec));
+            }
+            *slot = pack8_bf16(xv);
+          }
+        }
+      }
+      fence_async_smem();
+      mbar_arrive(&full[st]);
+    }
+  } else if (warp == TMA_WARP) {
+    // ---------------- TMA producer: x tile (+ Tucker row term) ----------------
+    if (lane == 0) {
+      sched::Cursor cur(A.tiles_per_cta, A.total_tiles);
+      for (int it = 0;; ++it) {
+        const int64_t g = sched::next_tile(cur);
+        sched::ring_put(ring, it, (int32_t)g);
+        const int st = it % NS;
+        if (!mbar_wait(&empty[st], (uint32_t)((it / NS) & 1) ^ 1u, 0x183)) break;
+        if (g < 0) {
+          mbar_arrive(&loaded[st]);
+          break;
+        }
+        const int cell = (int)(g / A.tiles_per_cell);
+        const int y = (int)((g % A.tiles_per_cell) * TILE_M);
+        mbar_expect_tx(&loaded[st], L::B_BYTES + (A.rt > 0 ? (A.rows_direct ? TILE_M * 2u : L::T_BYTES) : 0u));
+        const uint32_t dst = sbase + st * L::B_BYTES;
+#pragma unroll
+        for (int h = 0; h < D / 64; ++h) tma_load_2d(dst + h * TILE_M * 128, &xmaps.m[cell], h * 64, y, &loaded[st]);
+        if (A.rt > 0 && A.rows_direct)
+          bulk_load(sbase + L::OFF_T + st * L::T_BYTES,
+                    static_cast<const uint8_t*>(A.ut.p[cell]) + ((uint32_t)y % (uint32_t)A.t_tok) * 2u, TILE_M * 2u,
+                    &loaded[st]);
+        else if (A.rt > 0)
+          bulk_load(sbase + L::OFF_T + st * L::T_BYTES,
+                    A.tmp + ((int64_t)cell * A.tiles_per_cell * TILE_M + y) * RDM, L::T_BYTES, &loaded[st]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    // ---------------- MMA issuer: D[feature][row] = sum_k (Pi / s)[feature][k] R[row][k] ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16(128, TILE_M, true);
+      int it = 0;
+      bool ended = false;
+      for (;; ++it) {
+        const int st = it % NS, ac = it & 1;
+        if (!mbar_wait(&full[st], (uint32_t)((it / NS) & 1), 0x284)) break;
+        const int32_t g = sched::ring_get(ring, it);
+        if (!mbar_wait(&acce[ac], (uint32_t)((it >> 1) & 1) ^ 1u, 0x285)) break;
+        if (g < 0) {
+          umma_commit(&accf[ac]);
+          ended = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t b_base = sbase + st * L::B_BYTES;
+        const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * TILE_M);
+#pragma unroll
+        for (int term = 0; term < 3; ++term) {
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint32_t kb = (uint32_t)((ks >> 2) * (TILE_M * 128) + (ks & 3) * 32);
+            umma_f16_ts(d_tmem, tmem + (uint32_t)(term * (D / 2) + ks * 8), desc_sw128(b_base + kb), idesc,
+                        (term | ks) ? 1u : 0u);
+          }
+        }
+        umma_commit(&empty[st]);
+        umma_commit(&accf[ac]);
+      }
+      if (ended) mbar_wait(&accf[it & 1], (uint32_t)(it >> 1) & 1u, 0x286);
+      else if (it > 0) mbar_wait(&accf[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, 0x286);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue: thread = output feature, codes of the tile's 128 rows ----------------
+    // (warps 6-9, one per TMEM lane group)
+    const int lg = warp & 3;
+    const int feat = lg * 32 + lane;
+    int qmin, qmax;
+    qrange(BITS, SYM ? 1 : 0, qmin, qmax);
+    constexpr int offset = SYM ? (1 << (BITS - 1)) : 0;
+    const float magic = 12582912.0f + (float)offset;  // 1.5 * 2^23 + offset
+    const int lo_bits = 0x4B400000 + offset + qmin, hi_bits = 0x4B400000 + offset + qmax;
+    const uint64_t M2 = f2_pack(magic, magic);
+    uint64_t z2 = 0;
+    int cur_cell = -1;
+    for (int it = 0;; ++it) {
+      const int ac = it & 1;
+      if (!warp_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x381)) break;
+      const int32_t g = sched::ring_get(ring, it);
+      if (g < 0) break;
+      const int cell = (int)(g / A.tiles_per_cell);
+      const int64_t row0 = (g % A.tiles_per_cell) * TILE_M;
+      if (!SYM && cell != cur_cell) {
+        const int32_t* zz = static_cast<const int32_t*>(A.zp.p[cell]);
+        const float zf = (float)zz[A.scale_mode == KVC_SCALE_CHANNEL ? feat : 0];
+        z2 = f2_pack(zf, zf);
+      }
+      cur_cell = cell;
+      uint8_t* stg = smem + L::OFF_Q + (lg * 2 + (it & 1)) * L::Q_BYTES;
+      // the store issued from this buffer two tiles ago has read it
+      if (lane == 0) bulk_wait_read<1>();
+      __syncwarp();
+      tc_fence_after();
+#pragma unroll
+      for (int cc = 0; cc < 4; ++cc) {
+        float v[32];
+        tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * TILE_M + cc * 32), v);
+        int code[32];
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          uint64_t t2 = f2_pack(v[j], v[j + 1]);
+          if (!SYM) t2 = f2_add(t2, z2);
+          float y0, y1;
+          f2_unpack(f2_add(t2, M2), y0, y1);
+          code[j] = min(max(__float_as_int(y0), lo_bits), hi_bits);
+          code[j + 1] = min(max(__float_as_int(y1), lo_bits), hi_bits);
+        }
+        uint8_t* rows8 = stg + cc * 32 * CBW;
+        if constexpr (BITS == 8) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) rows8[j * CBW + lane] = (uint8_t)code[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int nbr = __shfl_down_sync(0xffffffffu, code[j], 1);
+            if (!(lane & 1)) rows8[j * CBW + (lane >> 1)] = (uint8_t)((code[j] << 4) | (nbr & 0xF));
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acce[ac]);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        if (row0 < A.rows) tma_store_2d(&cmaps.m[cell], lg * CBW, (int)row0, smem_u32(stg));
+        bulk_commit();
+      }
+    }
+    if (lane == 0) bulk_wait<0>();  // shared memory outlives the stores
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------
 // decode, row-major: A = the codes as exact bf16 integers in TMEM (one row
 // per lane), B = diag(scale) Pi of the cell in shared memory (reloaded at a
 // cell change), thread = row in the epilogue, bf16 rows stored directly
@@ -1725,6 +2047,24 @@ int launch_quant(int bits, dim3 grid, cudaStream_t st, const TmaMaps& xmaps, con
   }
 }
 
+constexpr int QFM_NS = 5;  // x stages of the feature-major quantise pass
+template <bool SYM, int RDM>
+int launch_quantfm(int bits, dim3 grid, cudaStream_t st, const TmaMaps& xmaps, const TmaMaps& cmaps, const EncArgs& a,
+                   const uint32_t* arows) {
+  constexpr size_t sm = QuantFmLayout<RDM, QFM_NS>::BYTES;
+  int rc;
+  if (bits == 8) {
+    auto kern = tc_quantfm_kernel<SYM, RDM, QFM_NS, 8>;
+    if ((rc = set_smem(kern, sm))) return rc;
+    kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, arows);
+  } else {
+    auto kern = tc_quantfm_kernel<SYM, RDM, QFM_NS, 4>;
+    if ((rc = set_smem(kern, sm))) return rc;
+    kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, arows);
+  }
+  return KVC_OK;
+}
+
 int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
                        const void* const* core, const void* const* u_token, const void* const* u_feature,
                        int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
@@ -1830,10 +2170,31 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   }
   const bool rows_ready = direct || after_stats;
   tl_rows_key = RowsKey{nullptr, 0, 0, 0, nullptr, nullptr};
+  // the feature-major quantise pass (d = 128, 8- / 4-bit codes, the
+  // quantiser's fast path); policy 3 keeps the row-major one for comparison
+  const bool fm = mode == 1 && !f16 && kernel_policy() != 3 && d == 128 && (bits == 8 || bits == 4) &&
+                  (scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32);
+  TmaMaps fmaps;
+  if (fm) {
+    memset(&fmaps, 0, sizeof(fmaps));
+    const uint32_t fbw = (uint32_t)(32 * bits / 8);  // code bytes of 32 features
+    for (int c = 0; c < n_cells; ++c) {
+      const uint64_t cd[2] = {(uint64_t)cb, (uint64_t)rows};
+      const uint64_t cst[1] = {(uint64_t)cb};
+      const uint32_t cbx[2] = {fbw, (uint32_t)TILE_M};
+      if ((rc = encode_tma(&fmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, codes[c], cd, cst, cbx,
+                           CU_TENSOR_MAP_SWIZZLE_NONE)))
+        return rc;
+    }
+  }
   if (mode == 1) {
     CellPtrs sp;
     for (int c = 0; c < n_cells; ++c) sp.p[c] = scale[c];
-    if (f16) {
+    if (fm) {
+      prep_quant_arows_kernel<<<dim3((d * (d / 2) + 255) / 256, n_cells), 256, 0, st>>>(
+          proj, sp, scale_mode == KVC_SCALE_CHANNEL, d, reinterpret_cast<uint32_t*>(bimg));
+      if ((rc = check_launch("prep_quant_arows_kernel"))) return rc;
+    } else if (f16) {
       prep_quant_b16_kernel<<<dim3(d, n_cells), d, 0, st>>>(proj, sp, rmax, d, bimg, fscale);
       if ((rc = check_launch("prep_quant_b16_kernel"))) return rc;
       a.fscale = fscale;
@@ -1899,7 +2260,17 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
       else KVC_TC_ENC_R(KVC_TC_STATS, 64, false, 8);
     }
   } else {
-    if (f16) {
+    if (fm) {
+      const uint32_t* ar = reinterpret_cast<const uint32_t*>(bimg);
+      if (rdm == 1) {
+        if (sym) rc = launch_quantfm<true, 1>(bits, grid, st, xmaps, fmaps, a, ar);
+        else rc = launch_quantfm<false, 1>(bits, grid, st, xmaps, fmaps, a, ar);
+      } else {
+        if (sym) rc = launch_quantfm<true, 4>(bits, grid, st, xmaps, fmaps, a, ar);
+        else rc = launch_quantfm<false, 4>(bits, grid, st, xmaps, fmaps, a, ar);
+      }
+      if (rc) return rc;
+    } else if (f16) {
       // two fp16 terms of Pi / s (64 KB) leave room for a fourth x stage
       if (sym) KVC_TC_QUANT16(true);
       else KVC_TC_QUANT16(false);
