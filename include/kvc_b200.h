@@ -295,11 +295,14 @@ int kvc_decode_plan_run(const void* plan, size_t plan_bytes, int64_t t0, int64_t
  * tensor-core kernels (residual encode) and symmetric per-channel 8/4/2-bit
  * bf16 decodes run on the tcgen05 decoder; everything else on the SIMT
  * kernels.  Policy 1: SIMT kernels only (used to cross-check the two).
- * Policy 2: as 0 with the residual encode's fp16 two-term modes (stats pass
- * and, after it in one compress call, quantise pass with Pi in two fp16
- * terms and R scaled by powers of two; d = 128, rank-1 row terms).
- * Policy 3: as 0 with the row-major tensor-core quantise pass everywhere
- * (policy 0 takes the feature-major one for d = 128 and 8- or 4-bit codes).
+ * Under policy 0 the quantise pass runs feature-major for d = 128 with 8-
+ * or 4-bit codes (Pi / s in TMEM, the rows in shared memory), and inside a
+ * compress call (after the stats pass, rank-1 row terms, per-channel
+ * scales) in its fp16 two-term mode: Pi / s in two fp16 terms and R scaled
+ * by a power of two per cell.  Policy 2: the stats pass in fp16 too (R
+ * scaled by a power of two per 128-row tile).  Policy 3: bf16 operands with
+ * the row-major quantise pass; policy 4: bf16 operands with the
+ * feature-major one (both for comparison).
  * Process-wide; set it while no call is in flight.
  */
 int kvc_set_kernel_policy(int policy);

@@ -43,9 +43,10 @@ void tc_reuse_tucker_rows(bool allow);
 int tc_read_device_error(int* out);
 int tc_gram_read_device_error(int* out);
 
-// 0: tensor cores when eligible (bf16 operands), 1: SIMT kernels only,
-// 2: as 0 with the residual encode's fp16 two-term modes, 3: as 0 with the
-// row-major tensor-core quantise pass for every layout
+// 0: tensor cores when eligible (the quantise pass in its fp16 two-term
+// mode where it applies), 1: SIMT kernels only, 2: as 0 with the stats pass
+// in fp16 too, 3: bf16 operands with the row-major quantise pass, 4: bf16
+// operands with the feature-major quantise pass
 static int g_policy = 0;
 int kernel_policy() { return g_policy; }
 
@@ -514,9 +515,10 @@ extern "C" size_t kvc_decompress_workspace_bytes(int n_cells, int64_t rows, int 
 }
 
 extern "C" int kvc_set_kernel_policy(int policy) {
-  if (policy < 0 || policy > 3)
+  if (policy < 0 || policy > 4)
     return fail(KVC_ERR_ARG,
-                "kvc_set_kernel_policy: 0 (auto), 1 (SIMT), 2 (fp16 two-term encode) or 3 (row-major quantise)");
+                "kvc_set_kernel_policy: 0 (auto), 1 (SIMT), 2 (fp16 stats and quantise), 3 (bf16, row-major "
+                "quantise) or 4 (bf16, feature-major quantise)");
   g_policy = policy;
   return KVC_OK;
 }

@@ -749,8 +749,11 @@ __global__ void prep_quant_b_kernel(const float* __restrict__ proj, CellPtrs sca
 // powers of two and fp16 x fp16 products are exact in fp32, so the
 // epilogue's factor 2^-(E + G_n) gives R~ / s with an error below 2^-21 of
 // the largest term.  One block per (row n, cell), one thread per k.
+// rowfmt: the terms as TMEM A rows [cell][term][n < 128][d] (the
+// feature-major pass) instead of swizzled B images.
 __global__ void prep_quant_b16_kernel(const float* __restrict__ proj, CellPtrs scale,
-                                      const uint32_t* __restrict__ rmax, int d, uint8_t* out, float* fscale) {
+                                      const uint32_t* __restrict__ rmax, int d, uint8_t* out, float* fscale,
+                                      int rowfmt) {
   __shared__ float red[32];
   const int cell = blockIdx.y, n = blockIdx.x, k = threadIdx.x;
   const float v = k < d ? __fdiv_rn(proj[n * d + k], static_cast<const float*>(scale.p[cell])[n]) : 0.f;
@@ -769,8 +772,14 @@ __global__ void prep_quant_b16_kernel(const float* __restrict__ proj, CellPtrs s
     const __half hi = __float2half_rn(b);
     const __half lo = __float2half_rn(b - __half2float(hi));
     uint8_t* base = out + (size_t)cell * 3 * d * d * 2;
-    *reinterpret_cast<__half*>(base + sw128_off(n, k, d)) = hi;
-    *reinterpret_cast<__half*>(base + (size_t)d * d * 2 + sw128_off(n, k, d)) = lo;
+    if (rowfmt) {
+      __half* rows = reinterpret_cast<__half*>(base);
+      rows[(size_t)n * d + k] = hi;
+      rows[((size_t)128 + n) * d + k] = lo;
+    } else {
+      *reinterpret_cast<__half*>(base + sw128_off(n, k, d)) = hi;
+      *reinterpret_cast<__half*>(base + (size_t)d * d * 2 + sw128_off(n, k, d)) = lo;
+    }
   }
   if (k == 0) {
     fscale[(size_t)cell * (1 + d) + 1 + n] = ldexpf(1.f, -(E + G));
@@ -1274,11 +1283,17 @@ __global__ void prep_quant_arows_kernel(const float* __restrict__ proj, CellPtrs
   }
 }
 
-template <bool SYM, int RDM, int NS, int BITS>
+// F16 (kernel policy 2, after the stats pass): A = (Pi / s) 2^G_n in two
+// fp16 terms, R enters as fp16 scaled by 2^E of the cell, and the epilogue
+// takes the exact factor 2^-(E + G_n) of its feature (the row-major pass's
+// fp16 mode, prep_quant_b16_kernel).
+template <bool SYM, int RDM, int NS, int BITS, bool F16 = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_quantfm_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ TmaMaps cmaps,
                       const __grid_constant__ EncArgs A, const uint32_t* arows) {
   constexpr int D = 128;
+  constexpr int NTERM = F16 ? 2 : 3;
+  static_assert(!F16 || RDM == 1, "the fp16 mode takes rank-1 row terms");
   using L = QuantFmLayout<RDM, NS>;
   static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   static_assert(BITS == 8 || BITS == 4, "feature-major codes of 8 or 4 bits");
@@ -1324,6 +1339,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + (part * 4 + lgw) * L::U_BYTES);  // [j]
     float* cs = reinterpret_cast<float*>(smem + L::OFF_CORE) + (part * 4 + lgw) * CORE_MAX;     // [h]
     int cur_cell = -1;
+    float es = 1.f;  // fp16 mode: 2^E of the cell
     for (int it = 0;; ++it) {
       const int st = it % NS;
       if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x181)) break;
@@ -1340,8 +1356,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           // tile (the last ones to read the old terms) have completed
           if (it > 0 && !warp_wait(&empty[(it - 1) % NS], (uint32_t)(((it - 1) / NS) & 1), 0x182)) break;
           tc_fence_after();
-          load_a_rows<D / 2>(tmem + ((uint32_t)(warp * 32) << 16), 0, arows + (size_t)cell * 3 * 128 * (D / 2), 3,
-                             warp * 32 + lane, 128);
+          load_a_rows<D / 2>(tmem + ((uint32_t)(warp * 32) << 16), 0, arows + (size_t)cell * 3 * 128 * (D / 2),
+                             NTERM, warp * 32 + lane, 128);
           tc_fence_before();
         }
         if (A.rt > 0) {
@@ -1359,6 +1375,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             for (int j = lane; j < (int)(A.rows / A.t_tok); j += 32) cs[j] = load_dt(A.core.p[cell], j, KVC_BF16);
           __syncwarp();
         }
+        if (F16) es = A.fscale[(size_t)cell * (1 + D)];
         cur_cell = cell;
       }
       if (A.rt > 0 && row < A.rows) {
@@ -1372,11 +1389,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             uint4* slot = reinterpret_cast<uint4*>(Bs + sw128_off(ptid, (part * HC + c) * 8, TILE_M));
             uint4 x = *slot;
             const uint4 u = u4[c];
-            x.x = bf16x2_sub(x.x, bf16x2_mul(t2, u.x));
-            x.y = bf16x2_sub(x.y, bf16x2_mul(t2, u.y));
-            x.z = bf16x2_sub(x.z, bf16x2_mul(t2, u.z));
-            x.w = bf16x2_sub(x.w, bf16x2_mul(t2, u.w));
-            *slot = x;
+            uint32_t w[4] = {bf16x2_sub(x.x, bf16x2_mul(t2, u.x)), bf16x2_sub(x.y, bf16x2_mul(t2, u.y)),
+                             bf16x2_sub(x.z, bf16x2_mul(t2, u.z)), bf16x2_sub(x.w, bf16x2_mul(t2, u.w))};
+            if constexpr (F16) {
+              // R * 2^E in fp16: exact for every bf16 value down to 2^-14 of
+              // the scaled range
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const __half2 h2 =
+                    __floats2half2_rn(__uint_as_float(w[i] << 16) * es, __uint_as_float(w[i] & 0xFFFF0000u) * es);
+                w[i] = *reinterpret_cast<const uint32_t*>(&h2);
+              }
+            }
+            *slot = make_uint4(w[0], w[1], w[2], w[3]);
           }
         } else {
           const float4 tv =
@@ -1435,7 +1460,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   } else if (warp == MMA_WARP) {
     // ---------------- MMA issuer: D[feature][row] = sum_k (Pi / s)[feature][k] R[row][k] ----------------
     if (lane == 0) {
-      const uint32_t idesc = idesc_f16(128, TILE_M, true);
+      const uint32_t idesc = idesc_f16(128, TILE_M, !F16);
       int it = 0;
       bool ended = false;
       for (;; ++it) {
@@ -1452,7 +1477,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t b_base = sbase + st * L::B_BYTES;
         const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * TILE_M);
 #pragma unroll
-        for (int term = 0; term < 3; ++term) {
+        for (int term = 0; term < NTERM; ++term) {
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t kb = (uint32_t)((ks >> 2) * (TILE_M * 128) + (ks & 3) * 32);
@@ -1478,7 +1503,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const float magic = 12582912.0f + (float)offset;  // 1.5 * 2^23 + offset
     const int lo_bits = 0x4B400000 + offset + qmin, hi_bits = 0x4B400000 + offset + qmax;
     const uint64_t M2 = f2_pack(magic, magic);
-    uint64_t z2 = 0;
+    uint64_t z2 = 0, c2 = 0;
     int cur_cell = -1;
     for (int it = 0;; ++it) {
       const int ac = it & 1;
@@ -1487,10 +1512,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       if (g < 0) break;
       const int cell = (int)(g / A.tiles_per_cell);
       const int64_t row0 = (g % A.tiles_per_cell) * TILE_M;
-      if (!SYM && cell != cur_cell) {
-        const int32_t* zz = static_cast<const int32_t*>(A.zp.p[cell]);
-        const float zf = (float)zz[A.scale_mode == KVC_SCALE_CHANNEL ? feat : 0];
-        z2 = f2_pack(zf, zf);
+      if (cell != cur_cell) {
+        if (!SYM) {
+          const int32_t* zz = static_cast<const int32_t*>(A.zp.p[cell]);
+          const float zf = (float)zz[A.scale_mode == KVC_SCALE_CHANNEL ? feat : 0];
+          z2 = f2_pack(zf, zf);
+        }
+        if (F16) {
+          const float cf = A.fscale[(size_t)cell * (1 + D) + 1 + feat];
+          c2 = f2_pack(cf, cf);
+        }
       }
       cur_cell = cell;
       uint8_t* stg = smem + L::OFF_Q + (lg * 2 + (it & 1)) * L::Q_BYTES;
@@ -1506,6 +1537,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
           uint64_t t2 = f2_pack(v[j], v[j + 1]);
+          if (F16) t2 = f2_mul(t2, c2);  // exact: powers of two
           if (!SYM) t2 = f2_add(t2, z2);
           float y0, y1;
           f2_unpack(f2_add(t2, M2), y0, y1);
@@ -2048,17 +2080,17 @@ int launch_quant(int bits, dim3 grid, cudaStream_t st, const TmaMaps& xmaps, con
 }
 
 constexpr int QFM_NS = 5;  // x stages of the feature-major quantise pass
-template <bool SYM, int RDM>
+template <bool SYM, int RDM, bool F16 = false>
 int launch_quantfm(int bits, dim3 grid, cudaStream_t st, const TmaMaps& xmaps, const TmaMaps& cmaps, const EncArgs& a,
                    const uint32_t* arows) {
   constexpr size_t sm = QuantFmLayout<RDM, QFM_NS>::BYTES;
   int rc;
   if (bits == 8) {
-    auto kern = tc_quantfm_kernel<SYM, RDM, QFM_NS, 8>;
+    auto kern = tc_quantfm_kernel<SYM, RDM, QFM_NS, 8, F16>;
     if ((rc = set_smem(kern, sm))) return rc;
     kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, arows);
   } else {
-    auto kern = tc_quantfm_kernel<SYM, RDM, QFM_NS, 4>;
+    auto kern = tc_quantfm_kernel<SYM, RDM, QFM_NS, 4, F16>;
     if ((rc = set_smem(kern, sm))) return rc;
     kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, arows);
   }
@@ -2157,7 +2189,14 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
                            tl_rows_key.n_cells == key.n_cells && tl_rows_key.rdm == key.rdm &&
                            tl_rows_key.rows == key.rows && tl_rows_key.core0 == key.core0 &&
                            tl_rows_key.ut0 == key.ut0;
-  const bool f16 = kernel_policy() == 2 && after_stats && d == 128 && rdm == 1 && rt > 0 && scale_mode == KVC_SCALE_CHANNEL;
+  // the quantise pass's fp16 mode (after a stats launch on these cells,
+  // which leaves max |R| per cell): by default with the feature-major pass
+  // (measured faster), with either pass under policy 2
+  const int pol = kernel_policy();
+  const bool fm = mode == 1 && pol != 3 && d == 128 && (bits == 8 || bits == 4) &&
+                  (scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32);
+  const bool f16_ok = after_stats && d == 128 && rdm == 1 && rt > 0 && scale_mode == KVC_SCALE_CHANNEL;
+  const bool f16 = f16_ok && ((pol == 0 && fm) || pol == 2);
   bool direct = rt == 1 && rd == 1 && t % TILE_M == 0 && m <= CORE_MAX;
   for (int c = 0; c < n_cells && direct; ++c) direct = (reinterpret_cast<uintptr_t>(u_token[c]) & 15u) == 0;
   a.rows_direct = direct ? 1 : 0;
@@ -2172,8 +2211,6 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   tl_rows_key = RowsKey{nullptr, 0, 0, 0, nullptr, nullptr};
   // the feature-major quantise pass (d = 128, 8- / 4-bit codes, the
   // quantiser's fast path); policy 3 keeps the row-major one for comparison
-  const bool fm = mode == 1 && !f16 && kernel_policy() != 3 && d == 128 && (bits == 8 || bits == 4) &&
-                  (scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32);
   TmaMaps fmaps;
   if (fm) {
     memset(&fmaps, 0, sizeof(fmaps));
@@ -2190,12 +2227,12 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   if (mode == 1) {
     CellPtrs sp;
     for (int c = 0; c < n_cells; ++c) sp.p[c] = scale[c];
-    if (fm) {
+    if (fm && !f16) {
       prep_quant_arows_kernel<<<dim3((d * (d / 2) + 255) / 256, n_cells), 256, 0, st>>>(
           proj, sp, scale_mode == KVC_SCALE_CHANNEL, d, reinterpret_cast<uint32_t*>(bimg));
       if ((rc = check_launch("prep_quant_arows_kernel"))) return rc;
     } else if (f16) {
-      prep_quant_b16_kernel<<<dim3(d, n_cells), d, 0, st>>>(proj, sp, rmax, d, bimg, fscale);
+      prep_quant_b16_kernel<<<dim3(d, n_cells), d, 0, st>>>(proj, sp, rmax, d, bimg, fscale, fm ? 1 : 0);
       if ((rc = check_launch("prep_quant_b16_kernel"))) return rc;
       a.fscale = fscale;
     } else {
@@ -2262,7 +2299,10 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   } else {
     if (fm) {
       const uint32_t* ar = reinterpret_cast<const uint32_t*>(bimg);
-      if (rdm == 1) {
+      if (f16) {
+        if (sym) rc = launch_quantfm<true, 1, true>(bits, grid, st, xmaps, fmaps, a, ar);
+        else rc = launch_quantfm<false, 1, true>(bits, grid, st, xmaps, fmaps, a, ar);
+      } else if (rdm == 1) {
         if (sym) rc = launch_quantfm<true, 1>(bits, grid, st, xmaps, fmaps, a, ar);
         else rc = launch_quantfm<false, 1>(bits, grid, st, xmaps, fmaps, a, ar);
       } else {

@@ -636,9 +636,10 @@ def decompress_noalloc(shape, out_dtype: torch.dtype, *, codes=None, scales=None
 
 
 def set_kernel_policy(policy: int) -> None:
-    """0: tensor-core kernels where eligible, bf16 operands (default); 1: SIMT
-    kernels only; 2: as 0 with the residual encode's fp16 two-term modes;
-    3: as 0 with the row-major tensor-core quantise pass everywhere."""
+    """0: tensor-core kernels where eligible (default); 1: SIMT kernels only;
+    2: as 0 with the stats pass in its fp16 mode too; 3: bf16 operands with
+    the row-major quantise pass; 4: bf16 operands with the feature-major
+    quantise pass."""
     check(lib().kvc_set_kernel_policy(int(policy)), "kvc_set_kernel_policy")
 
 

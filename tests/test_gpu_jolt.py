@@ -241,14 +241,14 @@ def test_cache_roundtrip():
     assert len(cache.metadata().layers) == 6
 
 
-@pytest.mark.parametrize("policy", [0, 2, 3])
+@pytest.mark.parametrize("policy", [0, 2, 3, 4])
 @pytest.mark.parametrize("layer,tokens", [(2, 2048), (9, 8192)])
 def test_compress_codes_exact_away_from_ties(layer, tokens, policy):
-    """The codes of the whole compress (policy 0: bf16 tensor-core operands,
-    the feature-major quantise pass; 2: the stats and quantise passes in two
-    fp16 terms with power-of-two scalings; 3: the row-major quantise pass)
-    equal the rounding of the exact rotated residual of the cell's own
-    factors, except within 1e-3 quantisation steps of a rounding boundary."""
+    """The codes of the whole compress (policy 0: the feature-major quantise
+    pass in its fp16 mode; 2: the stats pass in fp16 too; 3: bf16, the
+    row-major quantise pass; 4: bf16, the feature-major one) equal the
+    rounding of the exact rotated residual of the cell's own factors, except
+    within 1e-3 quantisation steps of a rounding boundary."""
     import oracle
     import oracle.jolt
 
