@@ -24,6 +24,7 @@ namespace kvc {
 // lets the next tensor-core quantise launch on this thread reuse the Tucker
 // row terms the stats launch before it left in the shared scratch
 void tc_reuse_tucker_rows(bool allow);
+void tc_stats_gram_bound(const double* gram, int64_t stride);
 
 namespace {
 
@@ -199,10 +200,13 @@ extern "C" int kvc_compress(int n_cells, const void* const* x, int64_t m, int64_
     cell_ptrs(zz, zp_out, n, (size_t)ns * 4);
     cell_ptrs(cd, codes_out, n, (size_t)m * t * ((d * bits + 7) / 8));
     if ((rc = mark(ST_STATS, 0, stream))) return rc;
-    if (scale_mode != KVC_SCALE_GROUP &&
-        (rc = kvc_residual_stats(n, xf, m, t, d, dtype, co, ut, ud, rt, rd, proj, bits, symmetric, scale_mode,
-                                 stat_dtype, sc, zz, scratch, scr, stream)))
-      return rc;
+    // the feature Gram (still intact) bounds |R| of each cell for the stats pass
+    tc_stats_gram_bound(gram_f, (int64_t)d * d + (int64_t)d * kf + 1);
+    if (scale_mode != KVC_SCALE_GROUP)
+      rc = kvc_residual_stats(n, xf, m, t, d, dtype, co, ut, ud, rt, rd, proj, bits, symmetric, scale_mode,
+                              stat_dtype, sc, zz, scratch, scr, stream);
+    tc_stats_gram_bound(nullptr, 0);
+    if (rc) return rc;
     if ((rc = mark(ST_STATS, 1, stream))) return rc;
     if ((rc = mark(ST_QUANT, 0, stream))) return rc;
     // the stats call just above left the Tucker row terms in the same scratch

@@ -170,6 +170,9 @@ struct EncArgs {
   const float* fscale;
   // STATS (fp16 mode): G_n of the A rows Pi[n][.] * 2^G_n
   const int32_t* gexp;
+  // STATS (fp16 mode): [cell] E, R's scale 2^E from a bound on |R| known
+  // before the pass (stats_bound_kernel), or NULL: per 128-row tile
+  const int32_t* sexp;
 };
 
 // Bits of the bf16 Tucker term of a tile's row ptid (rd = 1): from the
@@ -242,6 +245,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint16_t* ub = reinterpret_cast<uint16_t*>(smem + L::OFF_U + (part * 4 + lgw) * L::U_BYTES);  // [j]
     float* cs = reinterpret_cast<float*>(smem + L::OFF_CORE) + (part * 4 + lgw) * CORE_MAX;     // [h]
     int cur_cell = -1;
+    int ecell = 0;  // fp16 mode with a per-cell bound: E of the cell
     for (int it = 0;; ++it) {
       const int st = it % NS;
       if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x131)) break;
@@ -265,10 +269,49 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         if (A.rows_direct)
           for (int j = lane; j < (int)(A.rows / A.t_tok); j += 32) cs[j] = load_dt(A.core.p[cell], j, KVC_BF16);
+        if (F16 && A.sexp) ecell = A.sexp[cell];
         __syncwarp();
         cur_cell = cell;
       }
       if constexpr (F16) {
+        if (A.sexp) {
+          // R * 2^E with E of the cell (its bound puts |R| 2^E below 2^14):
+          // no agreement between the warps is needed
+          uint8_t* Bs = smem + st * L::B_BYTES;
+          uint32_t mh = 0u;  // max of the bf16 magnitude bits (both halves)
+          if (row < A.rows) {
+            const uint32_t th = enc_row_term(A, smem + L::OFF_T + st * L::T_BYTES, cs, ptid, row - ptid);
+            const uint32_t t2 = th | (th << 16);
+            const uint4* u4 = reinterpret_cast<const uint4*>(ub);
+            const int e1 = min(max(ecell, -100), 100), e2 = ecell - e1;
+            const uint32_t f1 = (uint32_t)(e1 + 127) << 7, f2 = (uint32_t)(e2 + 127) << 7;
+            const uint32_t p1 = f1 | (f1 << 16), p2 = f2 | (f2 << 16);
+#pragma unroll
+            for (int c = 0; c < HC; ++c) {
+              uint4* slot = reinterpret_cast<uint4*>(Bs + sw128_off(ptid, (part * HC + c) * 8, TILE_M));
+              const uint4 x = *slot;
+              const uint4 u = u4[c];
+              uint32_t w[4] = {bf16x2_sub(x.x, bf16x2_mul(t2, u.x)), bf16x2_sub(x.y, bf16x2_mul(t2, u.y)),
+                               bf16x2_sub(x.z, bf16x2_mul(t2, u.z)), bf16x2_sub(x.w, bf16x2_mul(t2, u.w))};
+              mh = __vmaxu2(mh, __vmaxu2(__vmaxu2(w[0] & 0x7FFF7FFFu, w[1] & 0x7FFF7FFFu),
+                                         __vmaxu2(w[2] & 0x7FFF7FFFu, w[3] & 0x7FFF7FFFu)));
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                uint32_t v = bf16x2_mul(w[i], p1);
+                if (e2 != 0) v = bf16x2_mul(v, p2);
+                const __half2 h2 = __floats2half2_rn(__uint_as_float(v << 16), __uint_as_float(v & 0xFFFF0000u));
+                w[i] = *reinterpret_cast<const uint32_t*>(&h2);
+              }
+              *slot = make_uint4(w[0], w[1], w[2], w[3]);
+            }
+          }
+          const uint32_t wm = __reduce_max_sync(0xffffffffu, max(mh & 0xFFFFu, mh >> 16));
+          if (lane == 0 && A.rmax && wm) atomicMax(A.rmax + cell, wm << 16);
+          if (warp == 0 && lane == 0) *reinterpret_cast<volatile int32_t*>(&texp[it % sched::RING]) = ecell;
+          fence_async_smem();
+          mbar_arrive(&full[st]);
+          continue;
+        }
         // fp16 mode: this thread's half row of R stays in registers until the
         // tile's max |R| is known; then R * 2^E, E putting that max in
         // [2^13, 2^14), goes to the B tile in fp16: exact for every bf16
@@ -694,6 +737,42 @@ __global__ void prep_rotation_kernel(const float* __restrict__ proj, int d, uint
     r0 -= __low2float(h);
     r1 -= __high2float(h);
     out[((size_t)term * 128 + m) * wpr + w] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+}
+
+// E of each cell for the fp16 stats pass, from bounds known before it:
+// |x| <= sqrt(max_j G_jj) (G the cell's feature Gram x^T x) and |recon| <=
+// rt max|core| max|u_token| max|u_feature|, with a 10% margin for the
+// roundings of the Gram and of the bf16 products; E = 13 - ilogb(bound), so
+// |R| 2^E < 2^14.  A loose bound costs nothing: fp16 keeps every value
+// exact down to 2^-14 of the scaled range.  One block per cell.
+__global__ void stats_bound_kernel(const double* __restrict__ gram, int64_t gstride, int d, CellPtrs core,
+                                   CellPtrs ut, CellPtrs ud, int64_t ncore, int64_t nut, int nud, int rt,
+                                   int32_t* sexp) {
+  __shared__ double red[4][32];
+  const int cell = blockIdx.x, lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const double* G = gram + cell * gstride;
+  double m[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int i = threadIdx.x; i < d; i += blockDim.x) m[0] = fmax(m[0], G[(int64_t)i * d + i]);
+  for (int64_t i = threadIdx.x; i < ncore; i += blockDim.x)
+    m[1] = fmax(m[1], fabs((double)load_dt(core.p[cell], i, KVC_BF16)));
+  for (int64_t i = threadIdx.x; i < nut; i += blockDim.x) m[2] = fmax(m[2], fabs((double)load_dt(ut.p[cell], i, KVC_BF16)));
+  for (int i = threadIdx.x; i < nud; i += blockDim.x) m[3] = fmax(m[3], fabs((double)load_dt(ud.p[cell], i, KVC_BF16)));
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m[q] = fmax(m[q], __shfl_xor_sync(0xffffffffu, m[q], o));
+    if (lane == 0) red[q][w] = m[q];
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    double r[4] = {0.0, 0.0, 0.0, 0.0};
+    for (int q = 0; q < 4; ++q)
+      for (int i = 0; i < (int)(blockDim.x + 31) / 32; ++i) r[q] = fmax(r[q], red[q][i]);
+    const double b = 1.1 * (sqrt(r[0]) + (double)rt * r[1] * r[2] * r[3]);
+    int E = 0;
+    if (b > 0.0 && isfinite(b)) E = 13 - ilogb(b);
+    sexp[cell] = min(max(E, -200), 200);
   }
 }
 
@@ -2036,7 +2115,8 @@ size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd) {
   const int64_t rows_pad = ceil_div(rows, TILE_M) * TILE_M;
   return align256((size_t)3 * 128 * (d / 2) * 4) + align256((size_t)n_cells * 2 * d * sizeof(int32_t)) +
          align256((size_t)n_cells * rows_pad * rdm_enc(rd) * 4) + align256((size_t)n_cells * 3 * d * d * 2) +
-         align256((size_t)n_cells * 4) + align256((size_t)n_cells * (1 + d) * 4) + align256((size_t)128 * 4);
+         align256((size_t)n_cells * 4) + align256((size_t)n_cells * (1 + d) * 4) + align256((size_t)128 * 4) +
+         align256((size_t)n_cells * 4);
 }
 
 // The Tucker row terms a stats launch left in its workspace, per host thread:
@@ -2055,6 +2135,16 @@ static thread_local RowsKey tl_rows_key = {nullptr, 0, 0, 0, nullptr, nullptr};
 static thread_local bool tl_rows_reuse = false;
 
 void tc_reuse_tucker_rows(bool allow) { tl_rows_reuse = allow; }
+
+// The feature Gram of the cells of the next stats launch on this host thread
+// (kvc_compress, whose Gram is still intact then): it bounds |R| per cell
+// for the fp16 stats pass.  NULL: none.
+static thread_local const double* tl_stats_gram = nullptr;
+static thread_local int64_t tl_stats_gram_stride = 0;
+void tc_stats_gram_bound(const double* gram, int64_t stride) {
+  tl_stats_gram = gram;
+  tl_stats_gram_stride = stride;
+}
 
 // One quantise launch, the code width as a template argument (the epilogue's
 // packing and store path fixed at compile time).
@@ -2163,6 +2253,8 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   float* fscale = reinterpret_cast<float*>(ws + off);  // fp16 quantise: 2^E, 2^-(E + G_n) per cell
   off += align256((size_t)n_cells * (1 + d) * 4);
   int32_t* gexp = reinterpret_cast<int32_t*>(ws + off);  // fp16 stats: G_n per A row
+  off += align256((size_t)128 * 4);
+  int32_t* sexp = reinterpret_cast<int32_t*>(ws + off);  // fp16 stats: E per cell (bounded |R|)
   a.gexp = gexp;
   a.arows = arows;
   a.minmax = mm;
@@ -2171,10 +2263,26 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   // the stats pass takes Pi as TMEM rows, the quantise pass Pi / s of each
   // cell as shared-memory B images
   // policy 2: the stats pass in two fp16 terms of Pi (rank-1 row terms,
-  // d = 128), a third fewer MMAs than three bf16 terms.  Not the default:
-  // inside the compress pipeline on B200 it measured slower than the bf16
-  // pass (the heavier transform outweighs the saved MMAs)
-  const bool f16s = kernel_policy() == 2 && mode == 0 && d == 128 && rdm == 1 && rt > 0;
+  // d = 128), a third fewer MMAs than three bf16 terms.  R's power of two
+  // is per cell where the feature Gram bounds |R| (inside kvc_compress),
+  // else per 128-row tile (agreed between the transform warps).  Not the
+  // default: in the compress pipeline on B200 both forms measured slower
+  // than the bf16 pass (the conversion makes the transform the critical
+  // path; the bf16 pass is held by its MMAs only a little longer)
+  const bool gram_bound = tl_stats_gram != nullptr && mode == 0 && rd == 1;
+  const bool f16s = mode == 0 && d == 128 && rdm == 1 && rt > 0 && kernel_policy() == 2;
+  if (f16s && gram_bound) {
+    CellPtrs cp, up, dp;
+    for (int c = 0; c < n_cells; ++c) {
+      cp.p[c] = core[c];
+      up.p[c] = u_token[c];
+      dp.p[c] = u_feature[c];
+    }
+    stats_bound_kernel<<<n_cells, 256, 0, st>>>(tl_stats_gram, tl_stats_gram_stride, d, cp, up, dp, m * rt, t * rt, d,
+                                                rt, sexp);
+    if ((rc = check_launch("stats_bound_kernel"))) return rc;
+    a.sexp = sexp;
+  }
   if (f16s) {
     prep_rotation16_kernel<<<128, d / 2, 0, st>>>(proj, d, arows, gexp);
     if ((rc = check_launch("prep_rotation16_kernel"))) return rc;

@@ -274,6 +274,11 @@ def test_compress_codes_exact_away_from_ties(layer, tokens, policy):
         ties = near_ties(x_rows, recon, "bf16", proj, scale)
         resid = oracle.jolt.dt_op(lambda a, b: a - b, "bf16", x_rows, recon)
         rot = np.asarray(resid, np.float64) @ proj.astype(np.float64).T
+        # the per-channel scales are max |R~| / 127 of the exact rotated residual
+        # (fp32 resolution: the stats pass's Pi is fp32-exact in three bf16
+        # terms, 22 bits in two fp16 terms)
+        exact_scale = np.abs(rot).max(axis=0) / 127.0
+        assert np.abs(scale / exact_scale - 1).max() < 2e-6, float(np.abs(scale / exact_scale - 1).max())
         q = np.clip(np.rint(rot / scale.astype(np.float64)), -128, 127).astype(np.int32)
         got = oracle.unpack_codes(fac.packed.cpu().numpy(), 8, d)
         diff = got != q
