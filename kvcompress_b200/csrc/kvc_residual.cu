@@ -22,6 +22,7 @@
 namespace kvc {
 
 bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale_mode);
+bool tc_quant_fm_eligible(int d, int bits, int scale_mode, int arith_dtype);
 size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd);
 int simt_row_terms(const void* const* core, const void* const* ut, int n_cells, int dtype, int64_t m, int64_t t,
                    int rt, int rd, int stride, float* tmp, cudaStream_t st);
@@ -598,6 +599,7 @@ extern "C" int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, 
   if (!dtype_ok(arith_dtype)) return fail(KVC_ERR_DTYPE, "kvc_residual_quant: bad arith dtype");
   if (g_policy != 1 && scale_mode != KVC_SCALE_GROUP && (bits == 2 || bits == 4 || bits == 8) &&
       tc_residual_eligible(dtype, d, rd, proj, scale_mode) &&
+      (rd <= 4 || tc_quant_fm_eligible(d, bits, scale_mode, arith_dtype)) &&
       all_aligned(n_cells, x) && all_aligned(n_cells, codes) && workspace &&
       ws_bytes >= tc_residual_workspace(n_cells, m * t, d, rd)) {
     return tc_residual_launch(1, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,

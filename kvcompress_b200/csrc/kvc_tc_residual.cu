@@ -124,6 +124,40 @@ __device__ __forceinline__ void load_a_rows(uint32_t tmem_lane_base, uint32_t co
   tmem_wait_st();
 }
 
+// A row's RDM Tucker row terms from shared memory into registers.
+template <int RDM>
+__device__ __forceinline__ void load_row_terms(const float* ts, float (&tv)[RDM]) {
+#pragma unroll
+  for (int g = 0; g < RDM / 4; ++g) {
+    const float4 t4 = reinterpret_cast<const float4*>(ts)[g];
+    tv[4 * g] = t4.x;
+    tv[4 * g + 1] = t4.y;
+    tv[4 * g + 2] = t4.z;
+    tv[4 * g + 3] = t4.w;
+  }
+}
+
+// The Tucker reconstruction of one element before its bf16 rounding:
+// sum_r t[r] u[r] in the order r = 0, 1, .. (the fp32 order of the SIMT
+// residual), u the feature's RDM entries of u_feature.
+template <int RDM>
+__device__ __forceinline__ float recon_dot(const float (&tv)[RDM], const float4* u) {
+  float4 q = u[0];
+  float rec = tv[0] * q.x;
+  rec = fmaf(tv[1], q.y, rec);
+  rec = fmaf(tv[2], q.z, rec);
+  rec = fmaf(tv[3], q.w, rec);
+#pragma unroll
+  for (int g = 1; g < RDM / 4; ++g) {
+    q = u[g];
+    rec = fmaf(tv[4 * g], q.x, rec);
+    rec = fmaf(tv[4 * g + 1], q.y, rec);
+    rec = fmaf(tv[4 * g + 2], q.z, rec);
+    rec = fmaf(tv[4 * g + 3], q.w, rec);
+  }
+  return rec;
+}
+
 // ------------------------------------------------------------------------
 // residual encode, stats pass: feature-major, one thread per output feature
 // ------------------------------------------------------------------------
@@ -133,7 +167,7 @@ struct StatsLayout {
   static constexpr int NTERM = F16 ? 2 : 3;                       // terms of Pi in TMEM
   static constexpr uint32_t B_BYTES = TILE_M * D * 2;             // R tile (MMA B operand)
   static constexpr uint32_t T_BYTES = TILE_M * RDM * 4;           // Tucker row term of a tile
-  static constexpr uint32_t U_BYTES = RDM == 1 ? D : D * 8;  // per transform warp, its D/2 features of
+  static constexpr uint32_t U_BYTES = RDM == 1 ? D : D * RDM * 2;  // per transform warp, its D/2 features of
                                                               // u_feature: bf16 [j] or fp32 [j][4]
   static constexpr uint32_t OFF_T = NS * B_BYTES;
   static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
@@ -262,8 +296,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if (RDM == 1) {
           for (int j = lane; j < HF; j += 32) ub[j] = reinterpret_cast<const uint16_t*>(ud)[part * HF + j];
         } else {
-          for (int i = lane; i < HF * 4; i += 32) {
-            const int j = i >> 2, r = i & 3;
+          for (int i = lane; i < HF * RDM; i += 32) {
+            const int j = i / RDM, r = i % RDM;
             u32[i] = r < A.rd ? __bfloat162float(ud[(part * HF + j) * A.rd + r]) : 0.f;
           }
         }
@@ -402,7 +436,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           rm = max(mh & 0xFFFFu, mh >> 16) << 16;
         } else {
-          const float4 tv = *reinterpret_cast<const float4*>(ts);
+          float tv[RDM];
+          load_row_terms<RDM>(ts, tv);
           const float4* u4 = reinterpret_cast<const float4*>(u32);
 #pragma unroll 2
           for (int c = 0; c < HC; ++c) {
@@ -411,11 +446,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             unpack8_bf16(*slot, xv);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float4 u = u4[c * 8 + e];
-              float rec = tv.x * u.x;
-              rec = fmaf(tv.y, u.y, rec);
-              rec = fmaf(tv.z, u.z, rec);
-              rec = fmaf(tv.w, u.w, rec);
+              const float rec = recon_dot<RDM>(tv, u4 + (c * 8 + e) * (RDM / 4));
               xv[e] = Elt<__nv_bfloat16>::round(xv[e] - Elt<__nv_bfloat16>::round(rec));
               rm = max(rm, __float_as_uint(fabsf(xv[e])));
             }
@@ -656,7 +687,7 @@ __global__ void __launch_bounds__(256) tucker_rows_tiled_kernel(CellPtrs core, C
   }
 }
 
-int rdm_enc(int rd) { return rd <= 1 ? 1 : 4; }
+int rdm_enc(int rd) { return rd <= 1 ? 1 : (rd <= 4 ? 4 : 16); }
 int rdm_dec(int rd) { return rd <= 1 ? 1 : (rd <= 4 ? 4 : 16); }
 
 size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
@@ -1327,7 +1358,7 @@ struct QuantFmLayout {
   static constexpr int D = 128;
   static constexpr uint32_t B_BYTES = TILE_M * D * 2;         // x stage = R tile (MMA B operand)
   static constexpr uint32_t T_BYTES = TILE_M * RDM * 4;       // Tucker row term of a tile
-  static constexpr uint32_t U_BYTES = RDM == 1 ? D : D * 8;   // per transform warp, as the stats pass
+  static constexpr uint32_t U_BYTES = RDM == 1 ? D : D * RDM * 2;  // per transform warp, as the stats pass
   static constexpr uint32_t Q_BYTES = TILE_M * 32;            // per epilogue warp and buffer: 128 rows x 32 bytes
   static constexpr uint32_t OFF_Q = NS * B_BYTES;
   static constexpr uint32_t OFF_T = OFF_Q + 4 * 2 * Q_BYTES;
@@ -1445,8 +1476,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           if (RDM == 1) {
             for (int j = lane; j < HF; j += 32) ub[j] = reinterpret_cast<const uint16_t*>(ud)[part * HF + j];
           } else {
-            for (int i = lane; i < HF * 4; i += 32) {
-              const int j = i >> 2, r = i & 3;
+            for (int i = lane; i < HF * RDM; i += 32) {
+              const int j = i / RDM, r = i % RDM;
               u32[i] = r < A.rd ? __bfloat162float(ud[(part * HF + j) * A.rd + r]) : 0.f;
             }
           }
@@ -1483,8 +1514,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             *slot = make_uint4(w[0], w[1], w[2], w[3]);
           }
         } else {
-          const float4 tv =
-              *reinterpret_cast<const float4*>(smem + L::OFF_T + st * L::T_BYTES + ptid * RDM * 4);
+          float tv[RDM];
+          load_row_terms<RDM>(reinterpret_cast<const float*>(smem + L::OFF_T + st * L::T_BYTES) + ptid * RDM, tv);
           const float4* u4 = reinterpret_cast<const float4*>(u32);
 #pragma unroll 2
           for (int c = 0; c < HC; ++c) {
@@ -1493,11 +1524,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             unpack8_bf16(*slot, xv);
 #pragma unroll
             for (int e = 0; e < 8; ++e) {
-              const float4 u = u4[c * 8 + e];
-              float rec = tv.x * u.x;
-              rec = fmaf(tv.y, u.y, rec);
-              rec = fmaf(tv.z, u.z, rec);
-              rec = fmaf(tv.w, u.w, rec);
+              const float rec = recon_dot<RDM>(tv, u4 + (c * 8 + e) * (RDM / 4));
               xv[e] = Elt<__nv_bfloat16>::round(xv[e] - Elt<__nv_bfloat16>::round(rec));
             }
             *slot = pack8_bf16(xv);
@@ -2106,9 +2133,16 @@ int simt_row_terms(const void* const* core, const void* const* ut, int n_cells, 
 
 // ------------------------------- launchers --------------------------------
 
+// rd up to 4 for d = 64 and 128, up to 16 for d = 128 (the quantise pass
+// then needs its feature-major form: tc_quant_fm_eligible).
 bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale_mode) {
-  return dtype == KVC_BF16 && (d == 64 || d == 128) && rd <= 4 && proj != nullptr &&
+  return dtype == KVC_BF16 && (d == 64 || d == 128) && (rd <= 4 || (rd <= 16 && d == 128)) && proj != nullptr &&
          (scale_mode == KVC_SCALE_CHANNEL || scale_mode == KVC_SCALE_TENSOR);
+}
+
+bool tc_quant_fm_eligible(int d, int bits, int scale_mode, int arith_dtype) {
+  return kernel_policy() != 3 && d == 128 && (bits == 8 || bits == 4) &&
+         (scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32);
 }
 
 size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd) {
@@ -2173,14 +2207,16 @@ constexpr int QFM_NS = 5;  // x stages of the feature-major quantise pass
 template <bool SYM, int RDM, bool F16 = false>
 int launch_quantfm(int bits, dim3 grid, cudaStream_t st, const TmaMaps& xmaps, const TmaMaps& cmaps, const EncArgs& a,
                    const uint32_t* arows) {
-  constexpr size_t sm = QuantFmLayout<RDM, QFM_NS>::BYTES;
+  // 16 row terms a row: fewer stages for the larger row-term and u_feature tables
+  constexpr int NSQ = RDM == 16 ? 3 : QFM_NS;
+  constexpr size_t sm = QuantFmLayout<RDM, NSQ>::BYTES;
   int rc;
   if (bits == 8) {
-    auto kern = tc_quantfm_kernel<SYM, RDM, QFM_NS, 8, F16>;
+    auto kern = tc_quantfm_kernel<SYM, RDM, NSQ, 8, F16>;
     if ((rc = set_smem(kern, sm))) return rc;
     kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, arows);
   } else {
-    auto kern = tc_quantfm_kernel<SYM, RDM, QFM_NS, 4, F16>;
+    auto kern = tc_quantfm_kernel<SYM, RDM, NSQ, 4, F16>;
     if ((rc = set_smem(kern, sm))) return rc;
     kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, arows);
   }
@@ -2301,8 +2337,9 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   // which leaves max |R| per cell): by default with the feature-major pass
   // (measured faster), with either pass under policy 2
   const int pol = kernel_policy();
-  const bool fm = mode == 1 && pol != 3 && d == 128 && (bits == 8 || bits == 4) &&
-                  (scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32);
+  const bool fm = mode == 1 && tc_quant_fm_eligible(d, bits, scale_mode, arith_dtype);
+  if (mode == 1 && rdm == 16 && !fm)
+    return fail(KVC_ERR_UNSUPPORTED, "tensor-core quantise: rd > 4 needs d = 128 and 8- or 4-bit codes");
   const bool f16_ok = after_stats && d == 128 && rdm == 1 && rt > 0 && scale_mode == KVC_SCALE_CHANNEL;
   const bool f16 = f16_ok && ((pol == 0 && fm) || pol == 2);
   bool direct = rt == 1 && rd == 1 && t % TILE_M == 0 && m <= CORE_MAX;
@@ -2397,6 +2434,9 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
     if (f16s) {
       if (sym) KVC_TC_STATS16(true);
       else KVC_TC_STATS16(false);
+    } else if (d == 128 && rdm == 16) {
+      if (sym) KVC_TC_STATS(128, true, 16, 4);
+      else KVC_TC_STATS(128, false, 16, 4);
     } else if (d == 128) {
       if (sym) KVC_TC_ENC_R(KVC_TC_STATS, 128, true, 6);
       else KVC_TC_ENC_R(KVC_TC_STATS, 128, false, 6);
@@ -2413,6 +2453,9 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
       } else if (rdm == 1) {
         if (sym) rc = launch_quantfm<true, 1>(bits, grid, st, xmaps, fmaps, a, ar);
         else rc = launch_quantfm<false, 1>(bits, grid, st, xmaps, fmaps, a, ar);
+      } else if (rdm == 16) {
+        if (sym) rc = launch_quantfm<true, 16>(bits, grid, st, xmaps, fmaps, a, ar);
+        else rc = launch_quantfm<false, 16>(bits, grid, st, xmaps, fmaps, a, ar);
       } else {
         if (sym) rc = launch_quantfm<true, 4>(bits, grid, st, xmaps, fmaps, a, ar);
         else rc = launch_quantfm<false, 4>(bits, grid, st, xmaps, fmaps, a, ar);

@@ -237,7 +237,7 @@ def _exact_codes(x, recon, proj, scale, bits, d):
 
 @pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("bits", [8, 4, 2])
-@pytest.mark.parametrize("rank", [(1, 1), (5, 3), (12, 6)])
+@pytest.mark.parametrize("rank", [(1, 1), (5, 3), (12, 6), (20, 16)])
 def test_tensor_core_residual_matches_simt(d, bits, rank):
     """tcgen05 encode vs the SIMT encode of the same bf16 cells (two cells, ragged rows)."""
     from kvcompress_b200.compressor.jl import cached_projection
