@@ -458,10 +458,13 @@ struct Gemm {
 };
 
 constexpr int GT = 64;    // output tile GT x GT
-constexpr int GKD = 16;   // depth per stage
+constexpr int GKD = 32;   // depth per stage
 constexpr int GNT = 256;  // 16 x 16 threads, 4 x 4 outputs each (strided by 16: conflict-free reads)
+constexpr int GPT = GT * GKD / GNT;  // elements of each operand a thread stages per stage
 
-// C = op(A) op(B) per cell (row-major; op = transpose when tA / tB).
+// C = op(A) op(B) per cell (row-major; op = transpose when tA / tB).  The
+// next stage's operand elements are loaded into registers while the current
+// stage is multiplied, so the loads' latency overlaps the arithmetic.
 __global__ void __launch_bounds__(GNT) f64_gemm_kernel(Gemm g) {
   __shared__ double As[GKD][GT + 1];
   __shared__ double Bs[GKD][GT + 1];
@@ -476,23 +479,30 @@ __global__ void __launch_bounds__(GNT) f64_gemm_kernel(Gemm g) {
   for (int r = 0; r < 4; ++r)
 #pragma unroll
     for (int c = 0; c < 4; ++c) acc[r][c] = 0.0;
-  for (int l0 = 0; l0 < g.K; l0 += GKD) {
-    for (int e = threadIdx.x; e < GT * GKD; e += GNT) {
-      // consecutive threads read consecutive addresses
-      const int ii = g.tA ? e % GT : e / GKD, ll = g.tA ? e / GT : e % GKD;
-      const int i = i0 + ii, l = l0 + ll;
-      double v = 0.0;
-      if (i < g.M && l < g.K) v = g.tA ? A[(int64_t)l * g.lda + i] : A[(int64_t)i * g.lda + l];
-      As[ll][ii] = v;
+  double pa[GPT], pb[GPT];
+  // consecutive threads read consecutive addresses
+  auto fetch = [&](int l0) {
+#pragma unroll
+    for (int q = 0; q < GPT; ++q) {
+      const int e = threadIdx.x + q * GNT;
+      const int ii = g.tA ? e % GT : e / GKD, la = g.tA ? e / GT : e % GKD;
+      const int i = i0 + ii, l = l0 + la;
+      pa[q] = (i < g.M && l < g.K) ? (g.tA ? A[(int64_t)l * g.lda + i] : A[(int64_t)i * g.lda + l]) : 0.0;
+      const int jj = g.tB ? e / GKD : e % GT, lb = g.tB ? e % GKD : e / GT;
+      const int j = j0 + jj, m = l0 + lb;
+      pb[q] = (j < g.N && m < g.K) ? (g.tB ? B[(int64_t)j * g.ldb + m] : B[(int64_t)m * g.ldb + j]) : 0.0;
     }
-    for (int e = threadIdx.x; e < GT * GKD; e += GNT) {
-      const int jj = g.tB ? e / GKD : e % GT, ll = g.tB ? e % GKD : e / GT;
-      const int j = j0 + jj, l = l0 + ll;
-      double v = 0.0;
-      if (j < g.N && l < g.K) v = g.tB ? B[(int64_t)j * g.ldb + l] : B[(int64_t)l * g.ldb + j];
-      Bs[ll][jj] = v;
+  };
+  fetch(0);
+  for (int l0 = 0; l0 < g.K; l0 += GKD) {
+#pragma unroll
+    for (int q = 0; q < GPT; ++q) {
+      const int e = threadIdx.x + q * GNT;
+      As[g.tA ? e / GT : e % GKD][g.tA ? e % GT : e / GKD] = pa[q];
+      Bs[g.tB ? e % GKD : e / GT][g.tB ? e / GKD : e % GT] = pb[q];
     }
     __syncthreads();
+    if (l0 + GKD < g.K) fetch(l0 + GKD);
 #pragma unroll
     for (int ll = 0; ll < GKD; ++ll) {
       double a[4], b[4];
@@ -947,21 +957,26 @@ LrLayout lr_layout(int p, int k) {
 
 // W = the starting sketch (LEFT: Y0 = A Omega from the Gram buffer; RIGHT:
 // Omega), misc[0] = |A|_F^2.
+// (grid: blocks x cells; block 0 of a cell also writes misc[0])
 __global__ void lr_init_kernel(SolveArgs a, LrLayout L) {
-  const int cell = blockIdx.x, p = a.p, k = a.k;
+  const int cell = blockIdx.y, p = a.p, k = a.k;
   const double* gram = a.gram + cell * a.gram_stride;
   double* ws = a.ws + cell * a.ws_cell;
+  const int64_t n = (int64_t)p * k, step = (int64_t)gridDim.x * blockDim.x;
   if (a.side == KVC_SIDE_LEFT) {
     const double* y0 = gram + (int64_t)p * p;
-    for (int64_t i = threadIdx.x; i < (int64_t)p * k; i += blockDim.x) ws[L.W + i] = y0[i];
-    if (threadIdx.x == 0) ws[L.misc] = gram[(int64_t)p * p + (int64_t)p * k];
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += step) ws[L.W + i] = y0[i];
+    if (blockIdx.x == 0 && threadIdx.x == 0) ws[L.misc] = gram[(int64_t)p * p + (int64_t)p * k];
   } else {
-    for (int64_t i = threadIdx.x; i < (int64_t)p * k; i += blockDim.x) ws[L.W + i] = (double)a.omega[i];
-    __shared__ double red[64];
-    double part = 0.0;
-    for (int i = threadIdx.x; i < p; i += blockDim.x) part += gram[(int64_t)i * p + i];
-    const double t = eig::block_sum(part, red);
-    if (threadIdx.x == 0) ws[L.misc] = t;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n; i += step)
+      ws[L.W + i] = (double)a.omega[i];
+    if (blockIdx.x == 0) {
+      __shared__ double red[64];
+      double part = 0.0;
+      for (int i = threadIdx.x; i < p; i += blockDim.x) part += gram[(int64_t)i * p + i];
+      const double t = eig::block_sum(part, red);
+      if (threadIdx.x == 0) ws[L.misc] = t;
+    }
   }
 }
 
@@ -1386,7 +1401,7 @@ int lr_solve(const SolveArgs& a, int n_cells, cudaStream_t st) {
     e = cudaFuncSetAttribute(trsm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)trsm_smem);
   if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
   int rc;
-  lr_init_kernel<<<n_cells, 256, 0, st>>>(a, L);
+  lr_init_kernel<<<dim3((unsigned)std::min<int64_t>(ceil_div((int64_t)p * k, 256 * 4), 128), n_cells), 256, 0, st>>>(a, L);
   if ((rc = check_launch("lr_init_kernel"))) return rc;
   int64_t cur = L.W, oth = L.Z;  // the current basis and the other p x k slot
   auto gemm = [&](const double* A, int64_t sA, int lda, int tA, const double* B, int64_t sB, int ldb, int tB,
