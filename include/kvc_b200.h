@@ -290,17 +290,20 @@ int kvc_decode_plan_run(const void* plan, size_t plan_bytes, int64_t t0, int64_t
                         void* stream);
 
 /*
- * Kernel selection.  Policy 0 (default): bf16 cells with d in {64, 128},
- * rd <= 16, a JL rotation and channel / tensor scales run on the tcgen05
- * tensor-core kernels (residual encode) and symmetric per-channel 8/4/2-bit
- * bf16 decodes run on the tcgen05 decoder; everything else on the SIMT
- * kernels.  Policy 1: SIMT kernels only (used to cross-check the two).
+ * Kernel selection.  Policy 0 (default): the residual encode of bf16 cells
+ * with a JL rotation and channel / tensor scales runs on the tcgen05
+ * tensor-core kernels for d = 64 with rd <= 4 and d = 128 with rd <= 16
+ * (rd > 4: the quantise pass needs 8- or 4-bit codes), and symmetric
+ * per-channel 8/4/2-bit bf16 decodes with rd <= 16 run on the tcgen05
+ * decoder; everything else on the SIMT kernels.  Policy 1: SIMT kernels
+ * only (used to cross-check the two).
  * Under policy 0 the quantise pass runs feature-major for d = 128 with 8-
  * or 4-bit codes (Pi / s in TMEM, the rows in shared memory), and inside a
  * compress call (after the stats pass, rank-1 row terms, per-channel
  * scales) in its fp16 two-term mode: Pi / s in two fp16 terms and R scaled
  * by a power of two per cell.  Policy 2: the stats pass in fp16 too (R
- * scaled by a power of two per 128-row tile).  Policy 3: bf16 operands with
+ * scaled by a power of two per cell from a bound on |R| inside a compress
+ * call, per 128-row tile otherwise).  Policy 3: bf16 operands with
  * the row-major quantise pass; policy 4: bf16 operands with the
  * feature-major one (both for comparison).
  * Process-wide; set it while no call is in flight.
