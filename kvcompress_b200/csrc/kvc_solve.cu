@@ -646,6 +646,7 @@ __global__ void __launch_bounds__(256, 1) chol_panel_kernel(double* Sb, int k, i
   __shared__ double A[CHP][CHP + 1];   // R[i0 + i][j0 + r] of the current chunk
   __shared__ double B[CHP][CHP + 1];   // R[i0 + i][c0 + c] of the current chunk
   __shared__ double rsv[CHP];
+  __shared__ double dgs[CHP];  // the panel's original diagonal (read once, not per pivot)
   const int cell = blockIdx.y, blk = blockIdx.x;
   double* S = Sb + cell * sS;
   double* rinv = rinvb + cell * sR;
@@ -654,6 +655,7 @@ __global__ void __launch_bounds__(256, 1) chol_panel_kernel(double* Sb, int k, i
   const int c0 = j0 + blk * CHP, ncol = min(CHP, k - c0);
   const bool diag = blk == 0;
   const int tr = threadIdx.x >> 3, tq = (threadIdx.x & 7) * 4;  // 4 outputs a thread: row tr, columns tq..tq+3
+  if ((int)threadIdx.x < nb) dgs[threadIdx.x] = dg0[j0 + threadIdx.x];
   double pd[4], ps[4];
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
@@ -704,7 +706,7 @@ __global__ void __launch_bounds__(256, 1) chol_panel_kernel(double* Sb, int k, i
   // with the unscaled row r times 1 / d
   for (int r = 0; r < nb; ++r) {
     if (threadIdx.x == 0) {
-      const double d = D[r][r], o = dg0[j0 + r];
+      const double d = D[r][r], o = dgs[r];
       rsv[r] = (o > 0.0 && d > 1e-10 * o) ? 1.0 / sqrt(d) : 0.0;
     }
     __syncthreads();
@@ -867,6 +869,9 @@ __device__ void rows_solve(double* Wl, int ldw, int k, const double* __restrict_
       }
     } else {
       // the diagonal block: apply the update, then substitute column by column
+      // (the block's inverse pivots in registers, lane l holding columns l
+      // and l + 16: one load instead of one dependent load a column)
+      const double ri0 = lane < cb ? rinv[J0 + lane] : 0.0, ri1 = lane + 16 < cb ? rinv[J0 + lane + 16] : 0.0;
       if (lane < cb) wr[J0 + lane] -= a0;
       if (lane + 16 < cb) wr[J0 + lane + 16] -= a1;
       a0 = a1 = 0.0;
@@ -878,7 +883,8 @@ __device__ void rows_solve(double* Wl, int ldw, int k, const double* __restrict_
           if (lane + 16 < c) part = fma(wr[J0 + lane + 16], B[(lane + 16) * RS_LD + c], part);
 #pragma unroll
           for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
-          if (lane == 0) wr[J0 + c] = (wr[J0 + c] - part) * rinv[J0 + c];
+          const double ric = __shfl_sync(0xffffffffu, c < 16 ? ri0 : ri1, c & 15, 16);
+          if (lane == 0) wr[J0 + c] = (wr[J0 + c] - part) * ric;
           __syncwarp();
         }
       } else {
@@ -888,7 +894,8 @@ __device__ void rows_solve(double* Wl, int ldw, int k, const double* __restrict_
           if (lane + 16 > c && lane + 16 < cb) part = fma(wr[J0 + lane + 16], B[c * RS_LD + lane + 16], part);
 #pragma unroll
           for (int o = 8; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o, 16);
-          if (lane == 0) wr[J0 + c] = (wr[J0 + c] - part) * rinv[J0 + c];
+          const double ric = __shfl_sync(0xffffffffu, c < 16 ? ri0 : ri1, c & 15, 16);
+          if (lane == 0) wr[J0 + c] = (wr[J0 + c] - part) * ric;
           __syncwarp();
         }
       }
@@ -911,6 +918,26 @@ __global__ void identity_kernel(double* Ab, int k, int64_t sA) {
 // of 32: first the rank update by the finished columns (R read through L1,
 // shared by every row), then the block's own forward substitution, column by
 // column, with the 16 lanes of a row splitting each dot product.
+// X[r][c] (nb rows of stride ldx; zero past k and in rows r >= nr) <-
+// src[r][c] (rows of length k, written by an earlier launch): eight loads in
+// flight a thread before their stores.
+__device__ inline void load_rows(double* X, int ldx, const double* __restrict__ src, int nb, int nr, int k) {
+  const int n = nb * ldx;
+  for (int e0 = threadIdx.x; e0 < n; e0 += 8 * blockDim.x) {
+    double v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int e = e0 + q * (int)blockDim.x, r = e / ldx, c = e - r * ldx;
+      v[q] = (e < n && c < k && r < nr) ? __ldg(src + (int64_t)r * k + c) : 0.0;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int e = e0 + q * (int)blockDim.x;
+      if (e < n) X[e] = v[q];
+    }
+  }
+}
+
 constexpr int TS_NBUF = 8;  // staged blocks of R in flight per CTA
 
 __global__ void __launch_bounds__(TS_NT) trsm_kernel(double* Wb, int p, int k, int64_t sW, const double* Rb,
@@ -922,10 +949,7 @@ __global__ void __launch_bounds__(TS_NT) trsm_kernel(double* Wb, int p, int k, i
   const double* rinv = rinvb + cell * sri;
   const int row0 = blockIdx.x * TS_ROWS;
   const int nr = min(TS_ROWS, p - row0);
-  for (int e = threadIdx.x; e < TS_ROWS * k; e += blockDim.x) {
-    const int r = e / k, c = e % k;
-    Wl[e] = r < nr ? W[(int64_t)(row0 + r) * k + c] : 0.0;
-  }
+  load_rows(Wl, k, W + (int64_t)row0 * k, TS_ROWS, nr, k);
   __syncthreads();
   rows_solve<false, TS_NBUF>(Wl, k, k, R, rinv, Wl + (size_t)TS_ROWS * k);
   for (int e = threadIdx.x; e < nr * k; e += blockDim.x) {
@@ -1144,10 +1168,7 @@ __global__ void __launch_bounds__(16 * IV_MAX) iv_mult_kernel(SolveArgs a, LrLay
   const double* xin = ws + xoff;
   double* out = ws + xnoff;
   double* Rs = X + (size_t)nb * ldx;
-  for (int e = threadIdx.x; e < nb * k; e += blockDim.x) {
-    const int r = e / k, c = e - r * k;
-    X[r * ldx + c] = xin[e];
-  }
+  load_rows(X, ldx, xin, nb, nb, k);
   const int r = threadIdx.x >> 4, lane = threadIdx.x & 15;
   const double* xr = X + r * ldx;
   const int nbk = (k + 31) / 32;
@@ -1202,10 +1223,7 @@ __global__ void __launch_bounds__(16 * IV_MAX) iv_orth_kernel(SolveArgs a, int n
   double* ws = a.ws + blockIdx.x * a.ws_cell;
   const double* xin = ws + xnoff;
   double* out = ws + xoff;
-  for (int e = threadIdx.x; e < nb * ldx; e += blockDim.x) {
-    const int r = e / ldx, c = e % ldx;
-    X[e] = c < k ? xin[(int64_t)r * k + c] : 0.0;
-  }
+  load_rows(X, ldx, xin, nb, nb, k);
   __syncthreads();
   cp_orth_rows(X, ldx, k, nb, G);
   cp_orth_rows(X, ldx, k, nb, G);
@@ -1230,10 +1248,7 @@ __global__ void __launch_bounds__(16 * IV_MAX, 1) cp_bottom_kernel(SolveArgs a, 
   double* ws = a.ws + cell * a.ws_cell;
   const double* R = ws + L.C;
   const double* xin = ws + xoff;
-  for (int e = threadIdx.x; e < nb * ldx; e += blockDim.x) {
-    const int r = e / ldx, c = e % ldx;
-    X[e] = c < k ? xin[(int64_t)r * k + c] : 0.0;
-  }
+  load_rows(X, ldx, xin, nb, nb, k);
   __syncthreads();
   // T = (X R^T)(X R^T)^T - delta I = X C X^T, 32 columns of M = X R^T at a time
   for (int e = threadIdx.x; e < IV_MAX * IV_MAX; e += blockDim.x) T[e] = 0.0;
