@@ -45,6 +45,7 @@ DEFAULT_WORKLOAD = "llama3-8b-kv-b8-t32768-bf16"
 SINGLE_GPU_WORKLOAD = "llama3-8b-kv-b1-t8192-bf16"
 STREAM_WORKLOAD = "qwen2-7b-kv-b4-t131072-bf16"
 QCAP_WORKLOAD = "llama3-8b-kv-b8-t4096-bf16-qcap"
+FP32_WORKLOAD = "tinyllama-1.1b-kv-t2048-fp32"
 BREAKDOWN_STEPS = 3  # traced steps for the per-stage times, before the timed region
 FALLBACK_HBM_GBS = 6650.0
 REFERENCE_DIR = os.path.join(ROOT, "baseline", "_ref")
@@ -68,6 +69,8 @@ def parse_args():
     ap.add_argument("--stream-block", type=int, default=256, help="tokens per block of the decode-stream line (0: no such line)")
     ap.add_argument("--qcap-workload", default=QCAP_WORKLOAD,
                     help="the q-capped sketch config measured at N = 1 ('' to skip)")
+    ap.add_argument("--fp32-workload", default=FP32_WORKLOAD,
+                    help="the fp32, head-dim 64 config measured at N = 1 ('' to skip)")
     ap.add_argument("--stream-workload", default=STREAM_WORKLOAD,
                     help="the decode-stream config measured at N = 1, with the int4 / fp8 baselines ('' to skip)")
     ap.add_argument("--layers", type=int, default=0,
@@ -195,9 +198,18 @@ def reference_cpu(w, *, steps: int = 1, budget_s: float | None = None, batch: in
     build = _import_reference()
     if build is None:
         return None
+    threads0 = torch.get_num_threads()
+    torch.set_num_threads(os.cpu_count() or 1)
+    try:
+        return _reference_cpu_run(build, w, steps=steps, budget_s=budget_s, batch=batch)
+    finally:
+        # the GPU lines measured after this one run with the process's own setting
+        torch.set_num_threads(threads0)
+
+
+def _reference_cpu_run(build, w, *, steps, budget_s, batch):
     from kvcompress_b200.synthetic import make_kv_layer
 
-    torch.set_num_threads(os.cpu_count() or 1)
     full_m = w.cell_shape[0]
     if batch is not None and batch < w.batch:
         w = dataclasses.replace(w, batch=int(batch))
@@ -522,6 +534,10 @@ def run_ours(args, w):
         pairs = None
         torch.cuda.empty_cache()
         line["qcap_config"] = single_gpu(WORKLOADS[args.qcap_workload], args, dev, peak, cpu=False)
+    if world == 1 and args.fp32_workload:
+        pairs = None
+        torch.cuda.empty_cache()
+        line["fp32_config"] = single_gpu(WORKLOADS[args.fp32_workload], args, dev, peak, cpu=False)
     if world == 1 and args.stream_workload and args.stream_block > 0:
         pairs = None
         torch.cuda.empty_cache()

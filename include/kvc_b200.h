@@ -198,8 +198,9 @@ int kvc_decompress(int n_cells, const uint8_t* const* codes, const float* const*
  * same kernels as kvc_decompress, with scratch in a fixed array of
  * KVC_NOALLOC_SCRATCH_BYTES per device inside this library, and allocates
  * nothing.
- *  - Limit: decodes that take the tensor-core decoder (bf16 output, d of 64
- *    or 128, a JL rotation, symmetric per-channel scales) and whose
+ *  - Limit: decodes that take the tensor-core decoder (bf16 output at d of
+ *    64 or 128, or fp32 output at d = 64; a JL rotation, symmetric
+ *    per-channel scales) and whose
  *    kvc_decompress_workspace_bytes(n_cells, m*t, d, rd) exceeds
  *    KVC_NOALLOC_SCRATCH_BYTES fail with KVC_ERR_WORKSPACE (K and V of one
  *    Llama-3-8B layer at 8k tokens need about 0.7 MB).  Other layouts are
@@ -270,10 +271,10 @@ int kvc_trace_stages(void* const* events, int n_events);
  *    tensor-core decode have plans; others return KVC_ERR_UNSUPPORTED
  *    (decode them with kvc_decompress).
  *  - kvc_decode_plan_run: decodes tokens [t0, t1) of every cell into out[c]
- *    ((m, t1 - t0, d) bf16, 16-byte aligned): one kernel launch for rank-1
- *    factors in fp16 / bf16 over whole 128-token blocks starting at a
- *    multiple of 8 (the row terms are formed inside the decode), two
- *    otherwise; bit for bit the same rows as kvc_decompress over that range.  Runs of one plan
+ *    ((m, t1 - t0, d) of the plan's out_dtype, 16-byte aligned): for bf16
+ *    output one kernel launch for rank-1 factors in fp16 / bf16 over whole
+ *    128-token blocks starting at a multiple of 8 (the row terms are formed
+ *    inside the decode), two otherwise; bit for bit the same rows as kvc_decompress over that range.  Runs of one plan
  *    share its workspace: issue them on one stream.  While the stream is
  *    being captured into a CUDA graph, a one-kernel run (head_dim 128) is
  *    launched as a programmatic dependent of the previous launch, so
@@ -293,9 +294,12 @@ int kvc_decode_plan_run(const void* plan, size_t plan_bytes, int64_t t0, int64_t
  * Kernel selection.  Policy 0 (default): the residual encode of bf16 cells
  * with a JL rotation and channel / tensor scales runs on the tcgen05
  * tensor-core kernels for d = 64 with rd <= 4 and d = 128 with rd <= 16
- * (rd > 4: the quantise pass needs 8- or 4-bit codes), and symmetric
- * per-channel 8/4/2-bit bf16 decodes with rd <= 16 run on the tcgen05
- * decoder; everything else on the SIMT kernels.  Policy 1: SIMT kernels
+ * (rd > 4: the quantise pass needs 8- or 4-bit codes), that of fp32 cells
+ * for d = 64 with rd <= 4 (the residual and Pi each in three bf16 terms,
+ * the six products of order up to two: fp32 accuracy), and symmetric
+ * per-channel 8/4/2-bit decodes with rd <= 16 run on the tcgen05 decoder
+ * for bf16 output at d = 64 / 128 and fp32 output at d = 64 (diag(scale) Pi
+ * in three bf16 terms); everything else on the SIMT kernels.  Policy 1: SIMT kernels
  * only (used to cross-check the two).
  * Under policy 0 the quantise pass runs feature-major for d = 128 with 8-
  * or 4-bit codes (Pi / s in TMEM, the rows in shared memory), and inside a

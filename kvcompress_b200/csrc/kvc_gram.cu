@@ -271,7 +271,9 @@ ChunkPlan plan_chunks(int n_cells, int64_t rows, int p, int q) {
     return pl;
   }
   pl.tiles = (int)(ceil_div(p, TB) * ceil_div(q, TB));
-  int64_t cr = std::max<int64_t>(2048, ceil_div(rows, 128));
+  // narrow outputs (a feature Gram of d = 64 and its sketch: two tiles) get
+  // shorter chunks, so a few cells still fill the GPU with blocks
+  int64_t cr = std::max<int64_t>(pl.tiles <= 4 ? 512 : 2048, ceil_div(rows, 128));
   cr = ceil_div(cr, RB) * RB;
   pl.chunk_rows = cr;
   pl.chunks = (int)std::max<int64_t>(1, ceil_div(rows, cr));

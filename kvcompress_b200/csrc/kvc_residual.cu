@@ -27,7 +27,7 @@ size_t tc_residual_workspace(int n_cells, int64_t rows, int d, int rd);
 int simt_row_terms(const void* const* core, const void* const* ut, int n_cells, int dtype, int64_t m, int64_t t,
                    int rt, int rd, int stride, float* tmp, cudaStream_t st);
 static size_t align256_(size_t x) { return (x + 255) & ~(size_t)255; }
-int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
+int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d, int dtype,
                        const void* const* core, const void* const* u_token, const void* const* u_feature,
                        int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
                        int stat_dtype, int arith_dtype, float* const* scale, int32_t* const* zp,
@@ -38,8 +38,8 @@ size_t tc_decompress_workspace(int n_cells, int64_t rows, int d, int rd);
 int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* const* scale, int bits,
                          const void* const* core, const void* const* u_token, const void* const* u_feature,
                          int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd, const float* proj,
-                         int64_t t0, int64_t t1, void* const* out, void* workspace, size_t ws_bytes,
-                         cudaStream_t st);
+                         int64_t t0, int64_t t1, int out_dtype, void* const* out, void* workspace,
+                         size_t ws_bytes, cudaStream_t st);
 void tc_reuse_tucker_rows(bool allow);
 int tc_read_device_error(int* out);
 int tc_gram_read_device_error(int* out);
@@ -548,7 +548,7 @@ extern "C" int kvc_residual_stats(int n_cells, const void* const* x, int64_t m, 
   cudaStream_t st0 = static_cast<cudaStream_t>(stream);
   if (g_policy != 1 && tc_residual_eligible(dtype, d, rd, proj, scale_mode) && all_aligned(n_cells, x) &&
       workspace && ws_bytes >= tc_residual_workspace(n_cells, m * t, d, rd)) {
-    return tc_residual_launch(0, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
+    return tc_residual_launch(0, n_cells, x, m, t, d, dtype, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
                               scale_mode, stat_dtype, KVC_F32, scale_out, zp_out, nullptr, workspace, ws_bytes,
                               st0);
   }
@@ -602,7 +602,7 @@ extern "C" int kvc_residual_quant(int n_cells, const void* const* x, int64_t m, 
       (rd <= 4 || tc_quant_fm_eligible(d, bits, scale_mode, arith_dtype)) &&
       all_aligned(n_cells, x) && all_aligned(n_cells, codes) && workspace &&
       ws_bytes >= tc_residual_workspace(n_cells, m * t, d, rd)) {
-    return tc_residual_launch(1, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
+    return tc_residual_launch(1, n_cells, x, m, t, d, dtype, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
                               scale_mode, stat_dtype, arith_dtype, scale, zp, codes, workspace, ws_bytes,
                               static_cast<cudaStream_t>(stream));
   }
@@ -658,7 +658,8 @@ extern "C" int kvc_decompress(int n_cells, const uint8_t* const* codes, const fl
       all_aligned(n_cells, codes) && all_aligned(n_cells, out) && workspace &&
       ws_bytes >= tc_decompress_workspace(n_cells, m * t, d, rd)) {
     return tc_decompress_launch(n_cells, codes, scale, bits, core, u_token, u_feature, factor_dtype, m, t, d, rt,
-                                rd, proj, t0, t1, out, workspace, ws_bytes, static_cast<cudaStream_t>(stream));
+                                rd, proj, t0, t1, out_dtype, out, workspace, ws_bytes,
+                                static_cast<cudaStream_t>(stream));
   }
   DecArgs a;
   memset(&a, 0, sizeof(a));
@@ -745,7 +746,8 @@ extern "C" int kvc_decode_plan_init(void* plan, size_t plan_bytes, int n_cells, 
                 "kvc_decode_plan_init: no tensor-core plan for this layout (decode with kvc_decompress)");
   TcDecodePlan local;
   const int rc = tc_decode_plan_init(&local, n_cells, codes, scale, bits, core, u_token, u_feature, factor_dtype, m,
-                                     t, d, rt, rd, proj, workspace, ws_bytes, static_cast<cudaStream_t>(stream));
+                                     t, d, rt, rd, proj, out_dtype, workspace, ws_bytes,
+                                     static_cast<cudaStream_t>(stream));
   if (rc) return rc;
   memcpy(static_cast<uint8_t*>(plan) + kPlanHeader, &local, sizeof(local));
   memcpy(plan, &kPlanMagic, sizeof(kPlanMagic));

@@ -1,5 +1,6 @@
 // Tensor-core (tcgen05 / TMEM, TMA-fed) kernels for the residual encode and
-// the fused decode, bf16 caches with head_dim 64 or 128.
+// the fused decode, bf16 caches with head_dim 64 or 128 and fp32 caches with
+// head_dim 64 (tc_enc32_kernel; the decode's fp32 output mode).
 //
 // All three are persistent, warp-specialised kernels (448 threads, one CTA
 // per SM) over 128-row tiles of a cell:
@@ -1342,6 +1343,452 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 }
 
 // ------------------------------------------------------------------------
+// fp32 cells with head_dim 64, both encode passes, row-major: A = R in three
+// bf16 terms in TMEM (R0 = bf16(R), R1 = bf16(R - R0), R2 = bf16(R - R0 -
+// R1): their sum is R to 2^-27 of |R|), B = Pi (stats) or Pi / s (quantise)
+// in three bf16 terms in shared memory.  The six products R_i P_j with
+// i + j <= 2 accumulate in fp32 (each of the three left out is below 2^-26
+// of the leading one), so the accumulator holds the rotated residual
+// (x - recon) Pi^T to fp32 accuracy (kvcompress/compressor/residual.py:
+// 201-239).  A 64-float row is 256 bytes, so an x tile is the 32 KB of a
+// bf16 row of 128: two 128-byte SWIZZLE_128B boxes of 32 floats.
+//   stats:    each epilogue thread keeps its 32 features' extremes over the
+//             rows it sees in registers; at a cell change the warp merges
+//             them (a reduce-scatter over the lanes, lane = feature) into the
+//             cell's ordered-int min / max;
+//   quantise: the epilogue of tc_quant_kernel (codes of the magic-constant
+//             rounding, staged and stored by TMA from 16-byte half rows).
+// ------------------------------------------------------------------------
+template <int RDM, int NS>
+struct Enc32Layout {
+  static constexpr int D = 64;
+  static constexpr uint32_t B_TERM = D * D * 2;
+  static constexpr uint32_t B_BYTES = 3 * B_TERM;    // Pi or Pi / s of the cell in three bf16 terms
+  static constexpr uint32_t X_BYTES = TILE_M * D * 4;  // fp32 x tile (TMA, two SWIZZLE_128B boxes)
+  static constexpr uint32_t T_BYTES = TILE_M * RDM * 4;  // Tucker row terms of a tile
+  static constexpr uint32_t U_BYTES = D * RDM * 4;       // per transform warp: u_feature fp32 [j][RDM]
+  static constexpr uint32_t S_BYTES = (D / 2) * 4;       // per epilogue warp: zp of its D/2 features
+  static constexpr uint32_t Q_BYTES = 32 * (D / 2);      // per epilogue warp: codes of 32 rows x D/2 (8-bit)
+  static constexpr uint32_t OFF_X = B_BYTES;             // 1024-aligned
+  static constexpr uint32_t OFF_Q = OFF_X + NS * X_BYTES;  // 1024-aligned (swizzled staging)
+  static constexpr uint32_t OFF_T = OFF_Q + 8 * Q_BYTES;
+  static constexpr uint32_t OFF_U = OFF_T + NS * T_BYTES;
+  static constexpr uint32_t OFF_S = OFF_U + 4 * U_BYTES;
+  static constexpr uint32_t OFF_RING = OFF_S + 8 * S_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_RING + sched::RING * 4;
+  static constexpr uint32_t NBAR = 2 * NS + 2 * 2 + 4 + 2;  // loaded, empty, A full/free x2, acc x2 x2, B free/ready
+  static constexpr uint32_t OFF_TM = OFF_BAR + NBAR * 8;
+  static constexpr uint32_t BYTES = OFF_TM + 16 + 1024;
+};
+
+// The lanes' v[0..31] reduced over the warp by min or max, lane l ending
+// with the result for index l (five exchange steps, 31 shuffles).
+template <bool MAX>
+__device__ __forceinline__ float lane_reduce_scatter32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int s = 16; s >= 1; s >>= 1) {
+    const bool up = (lane & s) != 0;
+#pragma unroll
+    for (int i = 0; i < s; ++i) {
+      const float send = up ? v[i] : v[i + s];
+      const float keep = up ? v[i + s] : v[i];
+      const float got = __shfl_xor_sync(0xffffffffu, send, s);
+      v[i] = MAX ? fmaxf(keep, got) : fminf(keep, got);
+    }
+  }
+  return v[0];
+}
+
+template <bool STATS, bool SYM, int RDM, int NS, int BITS>
+__global__ void __launch_bounds__(NTHREADS, 1)
+    tc_enc32_kernel(const __grid_constant__ TmaMaps xmaps, const __grid_constant__ TmaMaps cmaps,
+                    const __grid_constant__ EncArgs A, const uint8_t* bimg) {
+  static_assert(BITS == 2 || BITS == 4 || BITS == 8, "codes of 2, 4 or 8 bits");
+  static_assert(RDM == 1 || RDM == 4, "up to four feature-rank terms a row");
+  constexpr int D = 64;
+  using L = Enc32Layout<RDM, NS>;
+  static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
+  constexpr uint32_t TCOLS = D / 2;      // TMEM columns of one bf16 term of a row
+  constexpr uint32_t ACOLS = 3 * TCOLS;  // one A buffer: the three terms
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align1024(smem_raw);
+  const uint32_t sbase = smem_u32(smem);
+  uint64_t* loaded = reinterpret_cast<uint64_t*>(smem + L::OFF_BAR);
+  uint64_t* empty = loaded + NS;
+  uint64_t* afull = empty + NS;
+  uint64_t* afree = afull + 2;
+  uint64_t* accf = afree + 2;
+  uint64_t* acce = accf + 2;
+  uint64_t* bfree = acce + 2;
+  uint64_t* bready = bfree + 1;
+  uint32_t* tm_holder = reinterpret_cast<uint32_t*>(smem + L::OFF_TM);
+  int32_t* ring = reinterpret_cast<int32_t*>(smem + L::OFF_RING);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NS; ++i) {
+      mbar_init(&loaded[i], 1);
+      mbar_init(&empty[i], 128);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&afull[i], 128);
+      mbar_init(&afree[i], 1);
+      mbar_init(&accf[i], 1);
+      mbar_init(&acce[i], NEPI);
+    }
+    mbar_init(bfree, 1);
+    mbar_init(bready, 1);
+    mbar_fence_init();
+  }
+  if (warp == MMA_WARP) {
+    tmem_alloc(tm_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tm_holder;
+
+  if (warp < 4) {
+    // ---------------- transform: R = x - recon of one row, three bf16 terms into a TMEM A buffer ----------------
+    const int ptid = threadIdx.x;
+    float* us = reinterpret_cast<float*>(smem + L::OFF_U + warp * L::U_BYTES);  // [j][RDM]
+    int cur_cell = -1;
+    for (int it = 0;; ++it) {
+      const int st = it % NS, b = it & 1;
+      if (!warp_wait(&loaded[st], (uint32_t)((it / NS) & 1), 0x1A1)) break;
+      const int32_t tile = sched::ring_get(ring, it);
+      if (tile < 0) {  // no more tiles: pass the end on to the MMA thread
+        if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x1A2)) break;
+        mbar_arrive(&afull[b]);
+        break;
+      }
+      const int cell = (int)(tile / A.tiles_per_cell);
+      const int64_t row = (tile % A.tiles_per_cell) * TILE_M + ptid;
+      if (A.rt > 0 && cell != cur_cell) {
+        __syncwarp();
+        const float* ud = static_cast<const float*>(A.ud.p[cell]);
+        for (int i = lane; i < D * RDM; i += 32) {
+          const int j = i / RDM, r = i % RDM;
+          us[i] = r < A.rd ? ud[j * A.rd + r] : 0.f;
+        }
+        __syncwarp();
+        cur_cell = cell;
+      }
+      const uint8_t* Xs = smem + L::OFF_X + st * L::X_BYTES;
+      const bool sub = A.rt > 0 && row < A.rows;
+      // the row and its row terms in registers, then the stage goes back
+      float xv[D];
+#pragma unroll
+      for (int c = 0; c < D / 4; ++c) {
+        // floats 4c .. 4c + 3 are the 16 bytes of bf16 columns 8c .. 8c + 7
+        const uint4 raw = *reinterpret_cast<const uint4*>(Xs + sw128_off(ptid, c * 8, TILE_M));
+        xv[4 * c] = __uint_as_float(raw.x);
+        xv[4 * c + 1] = __uint_as_float(raw.y);
+        xv[4 * c + 2] = __uint_as_float(raw.z);
+        xv[4 * c + 3] = __uint_as_float(raw.w);
+      }
+      float tv[RDM];
+      if (sub) {
+        const float* ts = reinterpret_cast<const float*>(smem + L::OFF_T + st * L::T_BYTES) + ptid * RDM;
+        if constexpr (RDM == 1) tv[0] = ts[0];
+        else load_row_terms<RDM>(ts, tv);
+      }
+      mbar_arrive(&empty[st]);  // the x stage is no longer needed
+      if (sub) {
+        // recon in the fp32 order of the SIMT residual, then R = x - recon
+#pragma unroll
+        for (int j = 0; j < D; ++j) {
+          float rec;
+          if constexpr (RDM == 1) rec = tv[0] * us[j];
+          else rec = recon_dot<RDM>(tv, reinterpret_cast<const float4*>(us + j * RDM));
+          xv[j] = xv[j] - rec;
+        }
+      }
+      // the MMAs of tile it - 2 read this A buffer last
+      if (it >= 2 && !warp_wait(&afree[b], (uint32_t)(((it - 2) >> 1) & 1), 0x1A2)) break;
+      tc_fence_after();
+      const uint32_t tm_row = tmem + ((uint32_t)(warp * 32) << 16) + b * ACOLS;
+#pragma unroll
+      for (int term = 0; term < 3; ++term) {
+        uint32_t w[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const __nv_bfloat162 h = __floats2bfloat162_rn(xv[2 * i], xv[2 * i + 1]);
+          w[i] = *reinterpret_cast<const uint32_t*>(&h);
+          if (term < 2) {  // what the term leaves, exact in fp32
+            xv[2 * i] -= __low2float(h);
+            xv[2 * i + 1] -= __high2float(h);
+          }
+        }
+        tmem_st32(tm_row + term * TCOLS, w);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(&afull[b]);
+    }
+  } else if (warp == TMA_WARP) {
+    if (lane == 0) {
+      sched::Cursor cur(A.tiles_per_cta, A.total_tiles);
+      for (int it = 0;; ++it) {
+        const int64_t tile = sched::next_tile(cur);
+        sched::ring_put(ring, it, (int32_t)tile);
+        const int st = it % NS;
+        if (!mbar_wait(&empty[st], (uint32_t)((it / NS) & 1) ^ 1u, 0x1A3)) break;
+        if (tile < 0) {  // the end: a plain arrive completes the stage with no bytes
+          mbar_arrive(&loaded[st]);
+          break;
+        }
+        const int cell = (int)(tile / A.tiles_per_cell);
+        const int y = (int)((tile % A.tiles_per_cell) * TILE_M);
+        mbar_expect_tx(&loaded[st], L::X_BYTES + (A.rt > 0 ? L::T_BYTES : 0u));
+        const uint32_t dst = sbase + L::OFF_X + st * L::X_BYTES;
+        tma_load_2d(dst, &xmaps.m[cell], 0, y, &loaded[st]);
+        tma_load_2d(dst + TILE_M * 128, &xmaps.m[cell], 32, y, &loaded[st]);
+        if (A.rt > 0)
+          bulk_load(sbase + L::OFF_T + st * L::T_BYTES,
+                    A.tmp + ((int64_t)cell * A.tiles_per_cell * TILE_M + y) * RDM, L::T_BYTES, &loaded[st]);
+      }
+    }
+    __syncwarp();
+  } else if (warp == MMA_WARP) {
+    // D[row][feature] = sum_k R[row][k] B[feature][k], the six term pairs
+    // smallest first
+    if (lane == 0) {
+      constexpr int PA[6] = {1, 0, 2, 1, 0, 0}, PB[6] = {1, 2, 0, 0, 1, 0};
+      const uint32_t idesc = idesc_f16(TILE_M, D, true);
+      int it = 0, cur_cell = -1, nb = 0;
+      bool ended = false;
+      for (;; ++it) {
+        const int b = it & 1, ac = it & 1;
+        if (!mbar_wait(&afull[b], (uint32_t)((it >> 1) & 1), 0x2A1)) break;
+        const int32_t tile = sched::ring_get(ring, it);
+        if (!mbar_wait(&acce[ac], (uint32_t)((it >> 1) & 1) ^ 1u, 0x2A2)) break;
+        if (tile < 0) {  // the end: the epilogue learns it from the same accumulator barrier
+          umma_commit(&accf[ac]);
+          ended = true;
+          break;
+        }
+        const int cell = (int)(tile / A.tiles_per_cell);
+        // stats: one image of Pi for every cell; quantise: Pi / s per cell
+        if (STATS ? cur_cell < 0 : cell != cur_cell) {
+          if (cur_cell >= 0) {
+            umma_commit(bfree);
+            if (!mbar_wait(bfree, (uint32_t)((nb - 1) & 1), 0x2A4)) break;
+          }
+          mbar_expect_tx(bready, L::B_BYTES);
+          bulk_load(sbase, bimg + (STATS ? (size_t)0 : (size_t)cell * L::B_BYTES), L::B_BYTES, bready);
+          if (!mbar_wait(bready, (uint32_t)(nb & 1), 0x2A5)) break;
+          ++nb;
+        }
+        cur_cell = cell;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * D);
+#pragma unroll
+        for (int p = 0; p < 6; ++p) {
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks)
+            umma_f16_ts(d_tmem, tmem + b * ACOLS + PA[p] * TCOLS + (uint32_t)(ks * 8),
+                        desc_sw128(sbase + PB[p] * L::B_TERM + (uint32_t)(ks * 32)), idesc, (p | ks) ? 1u : 0u);
+        }
+        umma_commit(&afree[b]);
+        umma_commit(&accf[ac]);
+      }
+      // do not leave while MMAs that write TMEM are still in flight
+      if (ended) mbar_wait(&accf[it & 1], (uint32_t)(it >> 1) & 1u, 0x2A3);
+      else if (it > 0) mbar_wait(&accf[(it - 1) & 1], (uint32_t)((it - 1) >> 1) & 1u, 0x2A3);
+    }
+    __syncwarp();
+  } else if (STATS) {
+    // ---------------- stats epilogue: thread = row, 32 features per warp ----------------
+    const int e = warp - EPI_WARP0;
+    const int lg = warp & 3;
+    const int half = e >> 2;
+    const int rloc = lg * 32 + lane;
+    float lo[32], hi[32];  // SYM: hi = max |v|
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      lo[j] = __int_as_float(0x7f800000);
+      hi[j] = SYM ? 0.f : -__int_as_float(0x7f800000);
+    }
+    auto flush = [&](int cell) {
+      int32_t* mm = A.minmax + (int64_t)cell * 2 * D;
+      const int f = half * 32 + lane;
+      const float mx = lane_reduce_scatter32<true>(hi, lane);
+      if (SYM) {
+        atomicMin(&mm[f], ordered_bits(-mx));
+        atomicMax(&mm[D + f], ordered_bits(mx));
+      } else {
+        const float mn = lane_reduce_scatter32<false>(lo, lane);
+        atomicMin(&mm[f], ordered_bits(mn));
+        atomicMax(&mm[D + f], ordered_bits(mx));
+      }
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        lo[j] = __int_as_float(0x7f800000);
+        hi[j] = SYM ? 0.f : -__int_as_float(0x7f800000);
+      }
+    };
+    int cur_cell = -1;
+    for (int it = 0;; ++it) {
+      const int ac = it & 1;
+      if (!warp_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x3A1)) break;
+      const int32_t tile = sched::ring_get(ring, it);
+      if (tile < 0) break;
+      const int cell = (int)(tile / A.tiles_per_cell);
+      const int64_t row = (tile % A.tiles_per_cell) * TILE_M + rloc;
+      if (cell != cur_cell) {
+        if (cur_cell >= 0) flush(cur_cell);
+        cur_cell = cell;
+      }
+      tc_fence_after();
+      float v[32];
+      tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * D + half * 32), v);
+      tc_fence_before();
+      mbar_arrive(&acce[ac]);
+      if (row < A.rows) {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (SYM) {
+            hi[j] = fmaxf(hi[j], fabsf(v[j]));
+          } else {
+            lo[j] = fminf(lo[j], v[j]);
+            hi[j] = fmaxf(hi[j], v[j]);
+          }
+        }
+      }
+    }
+    if (cur_cell >= 0) flush(cur_cell);
+    __syncwarp();
+  } else {
+    // ---------------- quantise epilogue: thread = row, 32 features per warp ----------------
+    const int e = warp - EPI_WARP0;
+    const int lg = warp & 3;
+    const int half = e >> 2;
+    const int rloc = lg * 32 + lane;
+    float* zpf = reinterpret_cast<float*>(smem + L::OFF_S + e * L::S_BYTES);  // [feature]: zp
+    uint8_t* stg = smem + L::OFF_Q + e * L::Q_BYTES;
+    constexpr int cbw = (D / 2) * BITS / 8;  // code bytes of a half row: 32, 16 or 8
+    constexpr bool tma_out = cbw >= 16;
+    const int swz = tma_out ? ((lane * cbw) >> 7) & (cbw / 16 - 1) : 0;
+    uint8_t* srow = stg + lane * cbw;
+    int qmin, qmax;
+    qrange(BITS, SYM ? 1 : 0, qmin, qmax);
+    constexpr int offset = SYM ? (1 << (BITS - 1)) : 0;
+    const int ad = A.scale_mode == KVC_SCALE_TENSOR ? A.arith_dtype : KVC_F32;
+    const bool fast = A.scale_mode != KVC_SCALE_TENSOR || A.arith_dtype == KVC_F32;
+    const float magic = 12582912.0f + (float)offset;  // 1.5 * 2^23 + offset
+    const int lo_bits = 0x4B400000 + offset + qmin, hi_bits = 0x4B400000 + offset + qmax;
+    float s_t = 1.f;
+    int32_t zp_t = 0;
+    int cur_cell = -1;
+    for (int it = 0;; ++it) {
+      const int ac = it & 1;
+      if (!warp_wait(&accf[ac], (uint32_t)((it >> 1) & 1), 0x3A2)) break;
+      const int32_t tile = sched::ring_get(ring, it);
+      if (tile < 0) break;
+      const int cell = (int)(tile / A.tiles_per_cell);
+      const int64_t row = (tile % A.tiles_per_cell) * TILE_M + rloc;
+      if (cell != cur_cell) {
+        const int32_t* zz = static_cast<const int32_t*>(A.zp.p[cell]);
+        if (!SYM) {
+          __syncwarp();
+          for (int jl = lane; jl < D / 2; jl += 32)
+            zpf[jl] = (float)zz[A.scale_mode == KVC_SCALE_CHANNEL ? half * (D / 2) + jl : 0];
+          __syncwarp();
+        }
+        s_t = static_cast<const float*>(A.scale.p[cell])[0];
+        zp_t = zz[0];
+        cur_cell = cell;
+      }
+      tc_fence_after();
+      if (tma_out) {
+        // the previous tile's store has read the staging rows
+        if (lane == 0) bulk_wait_read<0>();
+        __syncwarp();
+      }
+      float v[32];
+      tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * D + half * 32), v);
+      tc_fence_before();
+      mbar_arrive(&acce[ac]);
+      int code[32];
+      if (fast) {
+        // v holds R~ / s: add zp, round half to even with the magic constant
+        // and clamp on the float bits
+        const uint64_t M2 = f2_pack(magic, magic);
+        const uint64_t* z2 = reinterpret_cast<const uint64_t*>(zpf);
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+          uint64_t t2 = f2_pack(v[j], v[j + 1]);
+          if (!SYM) t2 = f2_add(t2, z2[j / 2]);
+          float y0, y1;
+          f2_unpack(f2_add(t2, M2), y0, y1);
+          code[j] = min(max(__float_as_int(y0), lo_bits), hi_bits);
+          code[j + 1] = min(max(__float_as_int(y1), lo_bits), hi_bits);
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) code[j] = quantize_one(v[j], s_t, zp_t, qmin, qmax, ad) + offset;
+      }
+      // low byte of each code is (q + offset) & 0xFF
+      if constexpr (BITS == 8) {
+        uint32_t w[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          w[q] = __byte_perm(__byte_perm(code[4 * q], code[4 * q + 1], 0x0040),
+                             __byte_perm(code[4 * q + 2], code[4 * q + 3], 0x0040), 0x5410);
+        *reinterpret_cast<uint4*>(srow + ((0 ^ swz) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        *reinterpret_cast<uint4*>(srow + ((1 ^ swz) << 4)) = make_uint4(w[4], w[5], w[6], w[7]);
+      } else if constexpr (BITS == 4) {
+        uint32_t w[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          uint32_t pb[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            pb[i] = ((uint32_t)code[8 * q + 2 * i] << 4) | ((uint32_t)code[8 * q + 2 * i + 1] & 0xFu);
+          w[q] = __byte_perm(__byte_perm(pb[0], pb[1], 0x0040), __byte_perm(pb[2], pb[3], 0x0040), 0x5410);
+        }
+        *reinterpret_cast<uint4*>(srow) = make_uint4(w[0], w[1], w[2], w[3]);
+      } else {
+        uint32_t w[2];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          uint32_t pb[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int k = 16 * q + 4 * i;
+            pb[i] = ((uint32_t)code[k] << 6) | (((uint32_t)code[k + 1] & 3u) << 4) |
+                    (((uint32_t)code[k + 2] & 3u) << 2) | ((uint32_t)code[k + 3] & 3u);
+          }
+          w[q] = __byte_perm(__byte_perm(pb[0], pb[1], 0x0040), __byte_perm(pb[2], pb[3], 0x0040), 0x5410);
+        }
+        if (row < A.rows) {
+          uint8_t* dst = static_cast<uint8_t*>(A.codes.p[cell]) + row * A.code_bytes + half * 8;
+          *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+        }
+      }
+      if (tma_out) {
+        fence_async_smem();
+        __syncwarp();
+        const int64_t row0 = (tile % A.tiles_per_cell) * TILE_M + lg * 32;
+        if (lane == 0) {
+          if (row0 < A.rows) tma_store_2d(&cmaps.m[cell], half * cbw, (int)row0, smem_u32(stg));
+          bulk_commit();
+        }
+      }
+    }
+    if (lane == 0) bulk_wait<0>();  // shared memory outlives the stores
+    __syncwarp();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == MMA_WARP) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// ------------------------------------------------------------------------
 // quantise pass, feature-major (d = 128, 8- and 4-bit codes): A = Pi / s of
 // the cell in three bf16 terms in TMEM (192 columns; the transform warps
 // reload them when the tile stream enters a new cell, after the MMAs of the
@@ -1690,15 +2137,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 // rd = 1: the Tucker term t_row * u_feature is one more K-step of the MMA
 // (A: t split hi + mid + lo, B: u split hi + lo, every pairing once), so the
 // epilogue only rounds; rd > 1 adds it in the epilogue.
-template <int D, int CB, int RDM, int NS>
+// fp32 output (O32, d = 64): diag(scale) Pi in three bf16 terms and the
+// Tucker term added in fp32 by the epilogue for every rd (the reference adds
+// the fp32 reconstruction to the fp32 residual, jolt.py:424-463).
+template <int D, int CB, int RDM, int NS, bool O32 = false>
 struct DecLayout {
-  static constexpr bool FOLD = RDM == 1;
+  static constexpr bool FOLD = RDM == 1 && !O32;
+  static constexpr int NTB = O32 ? 3 : 2;                  // terms of diag(scale) Pi
   static constexpr uint32_t B_TERM = D * D * 2;
   static constexpr uint32_t B_TUCKER = FOLD ? D * 128 : 0;  // the extra K block (SW128, 16 of 64 used)
-  static constexpr uint32_t B_BYTES = 2 * B_TERM + B_TUCKER;  // diag(scale) Pi in two terms (+ u_feature)
+  static constexpr uint32_t B_BYTES = NTB * B_TERM + B_TUCKER;  // diag(scale) Pi (+ u_feature)
   static constexpr uint32_t C_BYTES = TILE_M * CB;    // codes as loaded (dense rows)
   static constexpr uint32_t U_BYTES = FOLD ? 0 : (D / 2) * RDM * 4;  // per epilogue warp: u_feature of its features
-  static constexpr uint32_t O_BYTES = 32 * D;              // per epilogue warp: 32 rows x D/2 bf16
+  static constexpr uint32_t ROW_BYTES = O32 ? 2 * D : D;   // one row's D/2 outputs
+  static constexpr uint32_t O_BYTES = 32 * ROW_BYTES;      // per epilogue warp: 32 rows x D/2 outputs
   // rd = 1: the tile's Tucker terms, bulk-copied from the 16-byte boundary at
   // or below the first row (up to 3 floats early), 132 floats
   static constexpr uint32_t T_BYTES = FOLD ? (TILE_M + 4) * 4 : 0;
@@ -1714,13 +2166,13 @@ struct DecLayout {
 };
 
 // Deepest codes ring (at most 8 stages) whose layout fits the 227 KB.
-template <int D, int CB, int RDM, int NS = 8>
+template <int D, int CB, int RDM, bool O32 = false, int NS = 8>
 struct DecStages {
   static constexpr int value =
-      DecLayout<D, CB, RDM, NS>::BYTES <= 227 * 1024 ? NS : DecStages<D, CB, RDM, NS - 1>::value;
+      DecLayout<D, CB, RDM, NS, O32>::BYTES <= 227 * 1024 ? NS : DecStages<D, CB, RDM, O32, NS - 1>::value;
 };
-template <int D, int CB, int RDM>
-struct DecStages<D, CB, RDM, 2> {
+template <int D, int CB, int RDM, bool O32>
+struct DecStages<D, CB, RDM, O32, 2> {
   static constexpr int value = 2;
 };
 
@@ -1739,12 +2191,12 @@ struct DecArgsTc {
   const float* tmp;     // [cell][m * tl][rdm] fp32 Tucker row term (+ 132 floats of slack at the end)
 };
 
-template <int D, int RDM, int BITS, int NS>
+template <int D, int RDM, int BITS, int NS, bool O32 = false>
 __global__ void __launch_bounds__(NTHREADS, 1)
     tc_decode_kernel(const __grid_constant__ TmaMaps cmaps, const __grid_constant__ TmaMaps omaps,
                      const __grid_constant__ DecArgsTc A) {
   constexpr int CB = D * BITS / 8;  // code bytes per row
-  using L = DecLayout<D, CB, RDM, NS>;
+  using L = DecLayout<D, CB, RDM, NS, O32>;
   static_assert(L::BYTES <= 227 * 1024, "shared-memory layout above the 227 KB per block");
   static_assert(CB % 16 == 0, "code rows must be whole 16-byte chunks");
   // a run launched as a programmatic dependent of this one may start at once:
@@ -1935,8 +2387,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           }
           mbar_expect_tx(bready, L::B_BYTES);
           const uint8_t* src = A.bimg + (size_t)cell * L::B_BYTES;
-          bulk_load(sbase, src, L::B_TERM, bready);
-          bulk_load(sbase + L::B_TERM, src + L::B_TERM, L::B_TERM, bready);
+#pragma unroll
+          for (int term = 0; term < L::NTB; ++term)
+            bulk_load(sbase + term * L::B_TERM, src + term * L::B_TERM, L::B_TERM, bready);
           if (FOLD) bulk_load(sbase + 2 * L::B_TERM, src + 2 * L::B_TERM, L::B_TUCKER, bready);
           if (!mbar_wait(bready, (uint32_t)(nb & 1), 0x295)) break;
           ++nb;
@@ -1944,13 +2397,15 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem + TM_ACC + (uint32_t)(ac * D);
+        // the smaller terms first
 #pragma unroll
-        for (int term = 0; term < 2; ++term) {
+        for (int tt = 0; tt < L::NTB; ++tt) {
+          const int term = L::NTB - 1 - tt;
 #pragma unroll
           for (int ks = 0; ks < D / 16; ++ks) {
             const uint32_t kb = (uint32_t)((ks >> 2) * (D * 128) + (ks & 3) * 32);
             umma_f16_ts(d_tmem, tmem + b * ACOLS + (uint32_t)(ks * 8), desc_sw128(sbase + term * L::B_TERM + kb),
-                        idesc, (term | ks) ? 1u : 0u);
+                        idesc, (tt | ks) ? 1u : 0u);
           }
         }
         if (FOLD)  // + t_row * u_feature: K positions 0-5 of the extra block
@@ -1970,12 +2425,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int rloc = lg * 32 + lane;
     constexpr int NCH = D / 64;
     float* us = reinterpret_cast<float*>(smem + L::OFF_U + e * L::U_BYTES);  // [feature][RDM]
-    // the warp's 32 rows x D/2 outputs (D bytes a row) are staged with the
-    // swizzle of that width (16-byte chunk j of row r at j ^ ((r * D / 128)
-    // mod (D / 16)), conflict-free) and leave by one TMA store
+    // the warp's 32 rows x D/2 outputs (ROW_BYTES a row) are staged with the
+    // swizzle of that width (16-byte chunk j of row r at j ^ ((r * ROW_BYTES /
+    // 128) mod (ROW_BYTES / 16)), conflict-free) and leave by one TMA store
+    constexpr int RB = (int)L::ROW_BYTES;
     uint8_t* stg = smem + L::OFF_O + e * L::O_BYTES;
-    const int swz = ((lane * D) >> 7) & (D / 16 - 1);
-    uint8_t* srow = stg + lane * D;
+    const int swz = ((lane * RB) >> 7) & (RB / 16 - 1);
+    uint8_t* srow = stg + lane * RB;
     int cur_cell = -1;
     for (int it = 0;; ++it) {
       const int ac = it & 1;
@@ -2013,6 +2469,37 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         float v[32];
         tmem_ld32(tmem + TM_ACC + ((uint32_t)(lg * 32) << 16) + (uint32_t)(ac * D + c * 32), v);
         uint32_t o[16];
+        if constexpr (O32) {
+          float oo[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (A.rt > 0) {
+              const int f = cc * 32 + j;
+              float rec = 0.f;
+              if (RDM == 1) {
+                rec = tv[0] * us[f];
+              } else {
+                const float4* u4 = reinterpret_cast<const float4*>(us + f * RDM);
+#pragma unroll
+                for (int r4 = 0; r4 < RDM / 4; ++r4) {
+                  const float4 u = u4[r4];
+                  rec = fmaf(tv[4 * r4], u.x, rec);
+                  rec = fmaf(tv[4 * r4 + 1], u.y, rec);
+                  rec = fmaf(tv[4 * r4 + 2], u.z, rec);
+                  rec = fmaf(tv[4 * r4 + 3], u.w, rec);
+                }
+              }
+              oo[j] = __fadd_rn(rec, v[j]);
+            } else {
+              oo[j] = v[j];
+            }
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(srow + (((cc * 8 + q) ^ swz) << 4)) =
+                make_float4(oo[4 * q], oo[4 * q + 1], oo[4 * q + 2], oo[4 * q + 3]);
+          continue;
+        }
         if (FOLD) {
           // the accumulator already holds residual + Tucker term
 #pragma unroll
@@ -2079,21 +2566,21 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 }
 
 // B images of the decode, per cell: B[n][k] = scale[k] * Pi[k][n] in two
-// bf16 terms, swizzled K-major [cell][term] (D[row][n] = sum_k q[row][k] B[n][k]),
+// bf16 terms (three for fp32 output), swizzled K-major [cell][term] (D[row][n] = sum_k q[row][k] B[n][k]),
 // then (rd = 1) the Tucker block B[n][k] for k < 64: u_feature[n] split
 // hi + lo at k = 0-2 and 3-5 (the A side holds t_row split hi + mid + lo
 // twice), zero elsewhere; zero throughout when there is no Tucker term.
 __global__ void prep_decode_kernel(const float* __restrict__ proj, CellPtrs scale, CellPtrs ufeat, int fdt,
-                                   int tucker_block, int d, uint8_t* out) {
+                                   int tucker_block, int nterm, int d, uint8_t* out) {
   const int cell = blockIdx.y;
   const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  const size_t per_cell = (size_t)2 * d * d * 2 + (tucker_block ? (size_t)d * 128 : 0);
+  const size_t per_cell = (size_t)nterm * d * d * 2 + (tucker_block ? (size_t)d * 128 : 0);
   uint8_t* base = out + (size_t)cell * per_cell;
   if (e < d * d) {
     const int n = e / d, k = e % d;
     const float sk = static_cast<const float*>(scale.p[cell])[k];
     float rest = __fmul_rn(sk, proj[(int64_t)k * d + n]);
-    for (int term = 0; term < 2; ++term) {
+    for (int term = 0; term < nterm; ++term) {
       const __nv_bfloat16 v = __float2bfloat16_rn(rest);
       rest -= __bfloat162float(v);
       *reinterpret_cast<__nv_bfloat16*>(base + (size_t)term * d * d * 2 + sw128_off(n, k, d)) = v;
@@ -2133,11 +2620,13 @@ int simt_row_terms(const void* const* core, const void* const* ut, int n_cells, 
 
 // ------------------------------- launchers --------------------------------
 
-// rd up to 4 for d = 64 and 128, up to 16 for d = 128 (the quantise pass
-// then needs its feature-major form: tc_quant_fm_eligible).
+// bf16 cells: rd up to 4 for d = 64 and 128, up to 16 for d = 128 (the
+// quantise pass then needs its feature-major form: tc_quant_fm_eligible);
+// fp32 cells: d = 64, rd up to 4 (tc_enc32_kernel).
 bool tc_residual_eligible(int dtype, int d, int rd, const float* proj, int scale_mode) {
-  return dtype == KVC_BF16 && (d == 64 || d == 128) && (rd <= 4 || (rd <= 16 && d == 128)) && proj != nullptr &&
-         (scale_mode == KVC_SCALE_CHANNEL || scale_mode == KVC_SCALE_TENSOR);
+  const bool shape = dtype == KVC_BF16 ? (d == 64 || d == 128) && (rd <= 4 || (rd <= 16 && d == 128))
+                                       : dtype == KVC_F32 && d == 64 && rd <= 4;
+  return shape && proj != nullptr && (scale_mode == KVC_SCALE_CHANNEL || scale_mode == KVC_SCALE_TENSOR);
 }
 
 bool tc_quant_fm_eligible(int d, int bits, int scale_mode, int arith_dtype) {
@@ -2223,7 +2712,143 @@ int launch_quantfm(int bits, dim3 grid, cudaStream_t st, const TmaMaps& xmaps, c
   return KVC_OK;
 }
 
-int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
+template <bool STATS, bool SYM, int RDM>
+int launch_enc32(int bits, dim3 grid, cudaStream_t st, const TmaMaps& xmaps, const TmaMaps& cmaps, const EncArgs& a,
+                 const uint8_t* bimg) {
+  constexpr int NS = 5;
+  constexpr size_t sm = Enc32Layout<RDM, NS>::BYTES;
+  int rc;
+#define KVC_ENC32(BB)                                                  \
+  do {                                                                 \
+    auto kern = tc_enc32_kernel<STATS, SYM, RDM, NS, BB>;              \
+    if ((rc = set_smem(kern, sm))) return rc;                          \
+    kern<<<grid, NTHREADS, sm, st>>>(xmaps, cmaps, a, bimg);           \
+  } while (0)
+  if constexpr (STATS) {
+    KVC_ENC32(8);  // the code width does not enter the stats pass
+  } else {
+    if (bits == 8) KVC_ENC32(8);
+    else if (bits == 4) KVC_ENC32(4);
+    else if (bits == 2) KVC_ENC32(2);
+    else return fail(KVC_ERR_ARG, "tensor-core quantise: bits must be 2, 4 or 8");
+  }
+#undef KVC_ENC32
+  return check_launch(STATS ? "tc_enc32_kernel (stats)" : "tc_enc32_kernel (quantise)");
+}
+
+// Both encode passes of fp32 cells with head_dim 64 (tc_enc32_kernel); the
+// workspace is carved as for the bf16 passes.
+static int tc_residual_f32_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d,
+                           const void* const* core, const void* const* u_token, const void* const* u_feature,
+                           int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
+                           int stat_dtype, int arith_dtype, float* const* scale, int32_t* const* zp,
+                           uint8_t* const* codes, void* workspace, cudaStream_t st) {
+  const int64_t rows = m * t;
+  const int rdm = rdm_enc(rd);
+  TmaMaps xmaps, cmaps;
+  EncArgs a;
+  memset(&a, 0, sizeof(a));
+  memset(&cmaps, 0, sizeof(cmaps));
+  const int cbw = (d / 2) * bits / 8;
+  const int cb = (d * bits + 7) / 8;
+  int rc;
+  for (int c = 0; c < n_cells; ++c) {
+    // rows of 64 floats: two boxes of 32 floats (128 bytes) x 128 rows
+    const uint64_t dims[2] = {(uint64_t)d, (uint64_t)rows};
+    const uint64_t strides[1] = {(uint64_t)d * 4};
+    const uint32_t box[2] = {32u, (uint32_t)TILE_M};
+    if ((rc = encode_tma(&xmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, x[c], dims, strides, box,
+                         CU_TENSOR_MAP_SWIZZLE_128B)))
+      return rc;
+    if (mode == 1 && cbw >= 16) {
+      const uint64_t cd[2] = {(uint64_t)cb, (uint64_t)rows};
+      const uint64_t cs[1] = {(uint64_t)cb};
+      const uint32_t cbx[2] = {(uint32_t)cbw, 32u};
+      const CUtensorMapSwizzle sw = cbw == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_NONE;
+      if ((rc = encode_tma(&cmaps.m[c], CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, codes[c], cd, cs, cbx, sw))) return rc;
+    }
+    if (rt > 0) a.ud.p[c] = u_feature[c];
+    if (scale) a.scale.p[c] = scale[c];
+    if (zp) a.zp.p[c] = zp[c];
+    if (codes) a.codes.p[c] = codes[c];
+  }
+  a.rows = rows;
+  a.rt = rt;
+  a.rd = rd;
+  a.bits = bits;
+  a.symmetric = symmetric;
+  a.scale_mode = scale_mode;
+  a.arith_dtype = arith_dtype;
+  a.code_bytes = cb;
+  a.tiles_per_cell = ceil_div(rows, TILE_M);
+  a.total_tiles = a.tiles_per_cell * n_cells;
+  const int64_t ctas = std::min<int64_t>(std::min<int64_t>(a.total_tiles, num_sms()), kMaxCtas);
+  a.tiles_per_cta = ceil_div(a.total_tiles, ctas);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  size_t off = align256((size_t)3 * 128 * (d / 2) * 4);
+  int32_t* mm = reinterpret_cast<int32_t*>(ws + off);
+  off += align256((size_t)n_cells * 2 * d * sizeof(int32_t));
+  float* tmp = reinterpret_cast<float*>(ws + off);
+  off += align256((size_t)n_cells * a.tiles_per_cell * TILE_M * rdm * 4);
+  uint8_t* bimg = ws + off;  // n_cells x 3 x d x d bf16
+  a.minmax = mm;
+  a.tmp = tmp;
+  const RowsKey key = {workspace, n_cells, rdm, rows, rt > 0 ? core[0] : nullptr, rt > 0 ? u_token[0] : nullptr};
+  const bool after_stats = mode == 1 && tl_rows_reuse && tl_rows_key.ws == key.ws &&
+                           tl_rows_key.n_cells == key.n_cells && tl_rows_key.rdm == key.rdm &&
+                           tl_rows_key.rows == key.rows && tl_rows_key.core0 == key.core0 &&
+                           tl_rows_key.ut0 == key.ut0;
+  tl_rows_key = RowsKey{nullptr, 0, 0, 0, nullptr, nullptr};
+  CellPtrs sp;
+  for (int c = 0; c < n_cells; ++c) sp.p[c] = scale ? scale[c] : nullptr;
+  if (mode == 0) {
+    // Pi in three terms, one image for every cell
+    prep_quant_b_kernel<<<dim3((d * d + 255) / 256, 1), 256, 0, st>>>(proj, sp, 0, 0, d, bimg);
+    if ((rc = check_launch("prep_quant_b_kernel"))) return rc;
+  } else {
+    const int fold = scale_mode != KVC_SCALE_TENSOR || arith_dtype == KVC_F32;
+    prep_quant_b_kernel<<<dim3((d * d + 255) / 256, n_cells), 256, 0, st>>>(
+        proj, sp, scale_mode == KVC_SCALE_CHANNEL, fold, d, bimg);
+    if ((rc = check_launch("prep_quant_b_kernel"))) return rc;
+  }
+  if (rt > 0 && !after_stats) {
+    CellPtrs cp, up;
+    for (int c = 0; c < n_cells; ++c) {
+      cp.p[c] = core[c];
+      up.p[c] = u_token[c];
+    }
+    if ((rc = row_terms_launch(cp, up, n_cells, KVC_F32, KVC_F32, m, 0, t, rt, rd, rdm, a.tiles_per_cell * TILE_M,
+                               tmp, st)))
+      return rc;
+  }
+  const dim3 grid((unsigned)ceil_div(a.total_tiles, a.tiles_per_cta));
+  const bool sym = symmetric != 0;
+  if (mode == 0) {
+    minmax_init_kernel<<<(n_cells * 2 * d + 255) / 256, 256, 0, st>>>(mm, n_cells, d, nullptr);
+    if ((rc = check_launch("minmax_init_kernel"))) return rc;
+    if (sym) rc = rdm == 1 ? launch_enc32<true, true, 1>(bits, grid, st, xmaps, cmaps, a, bimg)
+                           : launch_enc32<true, true, 4>(bits, grid, st, xmaps, cmaps, a, bimg);
+    else rc = rdm == 1 ? launch_enc32<true, false, 1>(bits, grid, st, xmaps, cmaps, a, bimg)
+                       : launch_enc32<true, false, 4>(bits, grid, st, xmaps, cmaps, a, bimg);
+    if (rc) return rc;
+    CellPtrsMut sc, zz;
+    for (int c = 0; c < n_cells; ++c) {
+      sc.p[c] = scale[c];
+      zz.p[c] = zp[c];
+    }
+    minmax_finalize_kernel<<<n_cells, 128, 0, st>>>(mm, n_cells, d, bits, symmetric, scale_mode, stat_dtype, sc, zz);
+    if ((rc = check_launch("minmax_finalize_kernel"))) return rc;
+    tl_rows_key = key;  // the row terms stay in the workspace for a following quantise launch
+    return KVC_OK;
+  }
+  if (sym) rc = rdm == 1 ? launch_enc32<false, true, 1>(bits, grid, st, xmaps, cmaps, a, bimg)
+                         : launch_enc32<false, true, 4>(bits, grid, st, xmaps, cmaps, a, bimg);
+  else rc = rdm == 1 ? launch_enc32<false, false, 1>(bits, grid, st, xmaps, cmaps, a, bimg)
+                     : launch_enc32<false, false, 4>(bits, grid, st, xmaps, cmaps, a, bimg);
+  return rc;
+}
+
+int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, int64_t t, int d, int dtype,
                        const void* const* core, const void* const* u_token, const void* const* u_feature,
                        int rt, int rd, const float* proj, int bits, int symmetric, int scale_mode,
                        int stat_dtype, int arith_dtype, float* const* scale, int32_t* const* zp,
@@ -2234,6 +2859,12 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
   const int rdm = rdm_enc(rd);
   if (ceil_div(rows, TILE_M) * TILE_M * rdm >= (1LL << 31))
     return fail(KVC_ERR_SHAPE, "tensor-core residual: too many rows per cell");
+  if (dtype == KVC_F32) {
+    if (d != 64 || rdm > 4) return fail(KVC_ERR_UNSUPPORTED, "tensor-core residual: fp32 cells need d = 64, rd <= 4");
+    return tc_residual_f32_launch(mode, n_cells, x, m, t, d, core, u_token, u_feature, rt, rd, proj, bits, symmetric,
+                                  scale_mode, stat_dtype, arith_dtype, scale, zp, codes, workspace, st);
+  }
+  if (dtype != KVC_BF16) return fail(KVC_ERR_DTYPE, "tensor-core residual: bf16 or fp32 cells");
   TmaMaps xmaps, cmaps;  // copied into the launch parameters
   EncArgs a;
   memset(&a, 0, sizeof(a));
@@ -2494,13 +3125,21 @@ int tc_residual_launch(int mode, int n_cells, const void* const* x, int64_t m, i
 
 bool tc_decompress_eligible(int out_dtype, int d, int rd, int bits, int symmetric, int scale_mode,
                             const float* proj) {
-  return out_dtype == KVC_BF16 && (d == 64 || d == 128) && rd <= RD_MAX && bits > 0 && d * bits / 8 >= 16 &&
-         symmetric && scale_mode == KVC_SCALE_CHANNEL && proj != nullptr;
+  const bool out_ok = out_dtype == KVC_BF16 ? (d == 64 || d == 128) : out_dtype == KVC_F32 && d == 64;
+  return out_ok && rd <= RD_MAX && bits > 0 && d * bits / 8 >= 16 && symmetric && scale_mode == KVC_SCALE_CHANNEL &&
+         proj != nullptr;
+}
+
+// Bytes of one cell's decode B image: bf16 output two terms (+ the Tucker
+// block at rd = 1), fp32 output three terms.
+size_t dec_bimg_cell_bytes(int d, int rd, bool o32) {
+  return o32 ? (size_t)6 * d * d : (size_t)4 * d * d + (rdm_dec(rd) == 1 ? (size_t)128 * d : 0);
 }
 
 size_t tc_decompress_workspace(int n_cells, int64_t rows, int d, int rd) {
-  const size_t bimg = (size_t)n_cells * ((size_t)4 * d * d + (rdm_dec(rd) == 1 ? (size_t)128 * d : 0));
-  return align256(bimg) + align256((size_t)n_cells * rows * rdm_dec(rd) * 4 + 132 * 4);
+  // d = 64 may decode to fp32 (three terms)
+  const size_t cellb = std::max(dec_bimg_cell_bytes(d, rd, false), d == 64 ? dec_bimg_cell_bytes(d, rd, true) : 0);
+  return align256((size_t)n_cells * cellb) + align256((size_t)n_cells * rows * rdm_dec(rd) * 4 + 132 * 4);
 }
 
 // A decode plan holds what does not depend on the token range: the codes'
@@ -2510,7 +3149,9 @@ size_t tc_decompress_workspace(int n_cells, int64_t rows, int d, int rd) {
 int tc_decode_plan_init(TcDecodePlan* p, int n_cells, const uint8_t* const* codes, const float* const* scale,
                         int bits, const void* const* core, const void* const* u_token,
                         const void* const* u_feature, int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd,
-                        const float* proj, void* workspace, size_t ws_bytes, cudaStream_t st) {
+                        const float* proj, int out_dtype, void* workspace, size_t ws_bytes, cudaStream_t st) {
+  if (out_dtype != KVC_BF16 && !(out_dtype == KVC_F32 && d == 64))
+    return fail(KVC_ERR_UNSUPPORTED, "tensor-core decompress: bf16 output, or fp32 output at d = 64");
   if (!workspace || ws_bytes < tc_decompress_workspace(n_cells, m * t, d, rd))
     return fail(KVC_ERR_WORKSPACE, "tensor-core decompress: workspace too small");
   if (t >= (1LL << 31) || m * t * rdm_dec(rd) >= (1LL << 31) || ceil_div(t, TILE_M) * m >= (1LL << 31))
@@ -2522,6 +3163,7 @@ int tc_decode_plan_init(TcDecodePlan* p, int n_cells, const uint8_t* const* code
   p->rt = rt;
   p->rd = rd;
   p->factor_dtype = factor_dtype;
+  p->out_dtype = out_dtype;
   p->m = m;
   p->t = t;
   const int cb = d * bits / 8;
@@ -2547,12 +3189,12 @@ int tc_decode_plan_init(TcDecodePlan* p, int n_cells, const uint8_t* const* code
       p->ud.p[c] = u_feature[c];
     }
   }
-  const int tucker_block = rdm_dec(rd) == 1;
+  const bool o32 = out_dtype == KVC_F32;
+  const int tucker_block = rdm_dec(rd) == 1 && !o32;
   p->bimg = static_cast<uint8_t*>(workspace);
-  p->tmp = reinterpret_cast<float*>(
-      p->bimg + align256((size_t)n_cells * ((size_t)4 * d * d + (tucker_block ? (size_t)128 * d : 0))));
-  prep_decode_kernel<<<dim3((d * d + d * 64 + 255) / 256, n_cells), 256, 0, st>>>(proj, sc, uf, factor_dtype,
-                                                                                tucker_block, d, p->bimg);
+  p->tmp = reinterpret_cast<float*>(p->bimg + align256((size_t)n_cells * dec_bimg_cell_bytes(d, rd, o32)));
+  prep_decode_kernel<<<dim3((d * d + d * 64 + 255) / 256, n_cells), 256, 0, st>>>(
+      proj, sc, uf, factor_dtype, tucker_block, o32 ? 3 : 2, d, p->bimg);
   return check_launch("prep_decode_kernel");
 }
 
@@ -2569,13 +3211,16 @@ int tc_decode_plan_run(const TcDecodePlan* p, int64_t t0, int64_t t1, void* cons
   for (int c = 0; c < n_cells; ++c) {
     if (!out[c] || (reinterpret_cast<uintptr_t>(out[c]) & 15u))
       return fail(KVC_ERR_ALIGN, "tensor-core decompress: output not 16-byte aligned");
-    // output (m, tl, d) bf16: boxes of d/2 features x 32 tokens, swizzled by
-    // their d-byte rows
+    // output (m, tl, d): boxes of d/2 features x 32 tokens, swizzled by their
+    // rows (bf16: d bytes; fp32 at d = 64: 128 bytes)
+    const bool o32 = p->out_dtype == KVC_F32;
+    const int esz = o32 ? 4 : 2;
     const uint64_t od[3] = {(uint64_t)d, (uint64_t)tl, (uint64_t)m};
-    const uint64_t os[2] = {(uint64_t)d * 2, (uint64_t)d * 2 * tl};
+    const uint64_t os[2] = {(uint64_t)d * esz, (uint64_t)d * esz * tl};
     const uint32_t ob[3] = {(uint32_t)(d / 2), 32u, 1u};
-    if ((rc = encode_tma(&omaps.m[c], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, out[c], od, os, ob,
-                         d == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
+    if ((rc = encode_tma(&omaps.m[c], o32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                         out[c], od, os, ob,
+                         (d == 128 || o32) ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B)))
       return rc;
     a.out.p[c] = out[c];
     if (rt > 0) a.ud.p[c] = p->ud.p[c];
@@ -2593,8 +3238,9 @@ int tc_decode_plan_run(const TcDecodePlan* p, int64_t t0, int64_t t1, void* cons
   a.factor_dtype = p->factor_dtype;
   a.bimg = p->bimg;
   a.tmp = p->tmp;
+  // (fp32 output adds the row terms in its epilogue, from the row-term kernel)
   bool direct = rt == 1 && rd == 1 && (p->factor_dtype == KVC_F16 || p->factor_dtype == KVC_BF16) &&
-                tl % TILE_M == 0 && t0 % 8 == 0;
+                tl % TILE_M == 0 && t0 % 8 == 0 && p->out_dtype != KVC_F32;
   for (int c = 0; c < n_cells && direct; ++c)
     direct = (reinterpret_cast<uintptr_t>(p->ut.p[c]) & 15u) == 0;
   a.rows_direct = direct ? 1 : 0;
@@ -2654,7 +3300,26 @@ int tc_decode_plan_run(const TcDecodePlan* p, int64_t t0, int64_t t1, void* cons
     else if (bits == 4) KVC_TC_DEC3(DD, RR, 4); \
     else KVC_TC_DEC3(DD, RR, 2);                \
   } while (0)
-  if (d == 128) {
+#define KVC_TC_DEC32_3(RR, BB)                                                 \
+  do {                                                                         \
+    constexpr int NSD = DecStages<64, 64 * BB / 8, RR, true>::value;           \
+    auto kern = tc_decode_kernel<64, RR, BB, NSD, true>;                       \
+    using LL = DecLayout<64, 64 * BB / 8, RR, NSD, true>;                      \
+    if ((rc = set_smem(kern, LL::BYTES))) return rc;                           \
+    kern<<<grid, NTHREADS, LL::BYTES, st>>>(cmaps, omaps, a);                  \
+  } while (0)
+#define KVC_TC_DEC32(RR)                         \
+  do {                                           \
+    if (bits == 8) KVC_TC_DEC32_3(RR, 8);        \
+    else if (bits == 4) KVC_TC_DEC32_3(RR, 4);   \
+    else KVC_TC_DEC32_3(RR, 2);                  \
+  } while (0)
+  if (p->out_dtype == KVC_F32) {
+    // d = 64 (checked when the plan was made)
+    if (rdm == 1) KVC_TC_DEC32(1);
+    else if (rdm == 4) KVC_TC_DEC32(4);
+    else KVC_TC_DEC32(16);
+  } else if (d == 128) {
     if (rdm == 1) KVC_TC_DEC(128, 1);
     else if (rdm == 4) KVC_TC_DEC(128, 4);
     else KVC_TC_DEC(128, 16);
@@ -2664,6 +3329,8 @@ int tc_decode_plan_run(const TcDecodePlan* p, int64_t t0, int64_t t1, void* cons
     else if (rdm == 4) KVC_TC_DEC(64, 4);
     else KVC_TC_DEC(64, 16);
   }
+#undef KVC_TC_DEC32
+#undef KVC_TC_DEC32_3
 #undef KVC_TC_DEC3
 #undef KVC_TC_DEC
   return check_launch("tc_decode_kernel");
@@ -2672,11 +3339,11 @@ int tc_decode_plan_run(const TcDecodePlan* p, int64_t t0, int64_t t1, void* cons
 int tc_decompress_launch(int n_cells, const uint8_t* const* codes, const float* const* scale, int bits,
                          const void* const* core, const void* const* u_token, const void* const* u_feature,
                          int factor_dtype, int64_t m, int64_t t, int d, int rt, int rd, const float* proj,
-                         int64_t t0, int64_t t1, void* const* out, void* workspace, size_t ws_bytes,
+                         int64_t t0, int64_t t1, int out_dtype, void* const* out, void* workspace, size_t ws_bytes,
                          cudaStream_t st) {
   TcDecodePlan plan;
   int rc = tc_decode_plan_init(&plan, n_cells, codes, scale, bits, core, u_token, u_feature, factor_dtype, m, t, d,
-                               rt, rd, proj, workspace, ws_bytes, st);
+                               rt, rd, proj, out_dtype, workspace, ws_bytes, st);
   if (rc) return rc;
   return tc_decode_plan_run(&plan, t0, t1, out, st);
 }

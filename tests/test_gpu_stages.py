@@ -279,6 +279,61 @@ def test_tensor_core_residual_matches_simt(d, bits, rank):
     print(f"near-tie flip rate d={d} bits={bits} rank={rank}: {max(flips):.3f}")
 
 
+@pytest.mark.parametrize("bits", [8, 4, 2])
+@pytest.mark.parametrize("rank", [(1, 1), (5, 3), (7, 4)])
+@pytest.mark.parametrize("symmetric", [True, False])
+def test_tensor_core_residual_f32_matches_simt(bits, rank, symmetric):
+    """tcgen05 encode of fp32 cells with head_dim 64 (R and Pi each in three
+    bf16 terms) vs the SIMT fp32 encode of the same cells (two cells, ragged
+    rows): scales to 2e-6, zero points within one step, and on each path
+    every code more than 1e-3 quantisation steps from a rounding boundary of
+    the float64 rotated residual (with that path's scale and zero point)
+    equal to the exact code."""
+    import oracle.jolt
+    from kvcompress_b200.compressor.jl import cached_projection
+
+    g = torch.Generator(device="cuda").manual_seed(100 + bits + 10 * rank[1] + int(symmetric))
+    m, t, d = 3, 333, 64
+    xs = [torch.randn(m, t, d, generator=g, device="cuda") * 3 + 0.5 for _ in range(2)]
+    rt, rd = rank
+    fac = ([torch.randn(m, rt, rd, generator=g, device="cuda") for _ in xs],
+           [torch.randn(t, rt, generator=g, device="cuda") / 10 for _ in xs],
+           [torch.randn(d, rd, generator=g, device="cuda") / 5 for _ in xs])
+    proj = cached_projection(d, d, seed=0, device="cuda").matrix
+    out = {}
+    try:
+        for pol in (0, 1):
+            _policy(pol)
+            sc, zp = ops.residual_stats(xs, fac, proj, bits=bits, symmetric=symmetric, scale_mode=KVC.SCALE_CHANNEL,
+                                        stat_dtype=torch.float32)
+            codes, _, _ = ops.residual_quant(xs, fac, proj, sc, zp, bits=bits, symmetric=symmetric,
+                                             scale_mode=KVC.SCALE_CHANNEL, group_size=None,
+                                             stat_dtype=torch.float32, arith_dtype=torch.float32)
+            out[pol] = ([s_.cpu().numpy() for s_ in sc], [z.cpu().numpy() for z in zp],
+                        [c.cpu().numpy() for c in codes])
+    finally:
+        _policy(0)
+    assert ops.device_error() == 0
+    for a, b in zip(out[0][0], out[1][0]):
+        assert rel(a, b) < 2e-6
+    for a, b in zip(out[0][1], out[1][1]):
+        assert np.abs(a.astype(np.int64) - b.astype(np.int64)).max() <= 1
+    qmin, qmax = (-(1 << (bits - 1)), (1 << (bits - 1)) - 1) if symmetric else (0, (1 << bits) - 1)
+    rows = np.arange(m * t)
+    flips = []
+    for i, x in enumerate(xs):
+        cf = [f32(f[i]) for f in fac]
+        recon = recon_rows(cf[0], cf[1], cf[2], "f32", rows, t)
+        resid = oracle.jolt.dt_op(lambda a, b: a - b, "f32", f32(x).reshape(m * t, d), recon)
+        rot = np.asarray(resid, np.float64) @ proj.cpu().numpy().astype(np.float64).T
+        for pol in (0, 1):
+            v = rot / out[pol][0][i].astype(np.float64) + out[pol][1][i].astype(np.float64)
+            ties = np.abs(v - np.floor(v) - 0.5) < 1e-3
+            exact = oracle.pack_codes(np.clip(np.rint(v), qmin, qmax).astype(np.int32), bits, symmetric)
+            flips.append(assert_codes_match(out[pol][2][i], exact, bits, d, ties))
+    print(f"fp32 near-tie flip rate bits={bits} rank={rank} symmetric={symmetric}: {max(flips):.3f}")
+
+
 @pytest.mark.parametrize("symmetric", [True, False])
 @pytest.mark.parametrize("mode", [KVC.SCALE_CHANNEL, KVC.SCALE_TENSOR])
 def test_tensor_core_stats_wide_range(symmetric, mode):
@@ -352,6 +407,46 @@ def test_tensor_core_decompress_matches_simt(d, bits, rank):
     assert ops.device_error() == 0
     for a, b in zip(res[0][0], res[1][0]):
         assert rel(a, b) < 2e-3
+    for full, part in zip(res[0][0], res[0][1]):
+        np.testing.assert_array_equal(full[:, 37:299], part)
+
+
+@pytest.mark.parametrize("bits", [8, 4, 2])
+@pytest.mark.parametrize("rank", [(1, 1), (7, 4), (6, 12)])
+def test_tensor_core_decompress_f32_matches_simt(bits, rank):
+    """fp32 output at head_dim 64 (diag(scale) Pi in three bf16 terms, the
+    fp32 Tucker term added by the epilogue) vs the SIMT fp32 decode: 1e-6
+    relative, and a token range equal to the same rows of the whole decode."""
+    from kvcompress_b200.compressor.jl import cached_projection
+
+    d = 64
+    g = torch.Generator(device="cuda").manual_seed(11 * bits + rank[1])
+    m, t = 2, 300
+    rt, rd = rank
+    cb = d * bits // 8
+    codes = [torch.randint(0, 256, (m * t, cb), generator=g, device="cuda", dtype=torch.int32).to(torch.uint8)
+             for _ in range(3)]
+    scales = [torch.rand(d, generator=g, device="cuda") * 0.1 + 0.01 for _ in range(3)]
+    zps = [torch.zeros(d, dtype=torch.int32, device="cuda") for _ in range(3)]
+    fac = ([torch.randn(m, rt, rd, generator=g, device="cuda") for _ in range(3)],
+           [torch.randn(t, rt, generator=g, device="cuda") / 10 for _ in range(3)],
+           [torch.randn(d, rd, generator=g, device="cuda") / 5 for _ in range(3)])
+    proj = cached_projection(d, d, seed=0, device="cuda").matrix
+    res = {}
+    try:
+        for pol in (0, 1):
+            _policy(pol)
+            outs = ops.decompress((m, t, d), torch.float32, codes=codes, scales=scales, zps=zps, bits=bits,
+                                  factors=fac, proj=proj, n_cells=3, device="cuda")
+            part = ops.decompress((m, t, d), torch.float32, codes=codes, scales=scales, zps=zps, bits=bits,
+                                  factors=fac, proj=proj, n_cells=3, device="cuda", t0=37, t1=299)
+            res[pol] = ([f32(o) for o in outs], [f32(o) for o in part])
+    finally:
+        _policy(0)
+    assert ops.device_error() == 0
+    for a, b in zip(res[0][0], res[1][0]):
+        assert rel(a, b) < 1e-6
+        assert np.abs(a - b).max() <= 1e-6 * np.abs(b).max()
     for full, part in zip(res[0][0], res[0][1]):
         np.testing.assert_array_equal(full[:, 37:299], part)
 
