@@ -26,6 +26,7 @@ workload per step.
 from __future__ import annotations
 
 import argparse
+import gc
 import dataclasses
 import json
 import os
@@ -373,6 +374,9 @@ def measure(comp, pairs, w, *, steps: int, warmup: int, world: int, dev, peak: f
         ev[2].record()
         return ev, payloads, outs
 
+    # garbage from the lines measured before (payload dicts, traces, the CPU
+    # legs' objects) is collected here, not inside this line's timed steps
+    gc.collect()
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
@@ -525,11 +529,7 @@ def run_ours(args, w):
         line["e2e"] = e2e(comp, pairs, w, dev, world, steps=min(args.steps, 3), chunk=args.e2e_chunk,
                           host_layers=args.e2e_host_layers)
     del payloads
-    if world == 1 and args.single_gpu_workload and args.single_gpu_workload != w.name:
-        pairs = None
-        torch.cuda.empty_cache()
-        line["single_gpu_config"] = single_gpu(WORKLOADS[args.single_gpu_workload], args, dev, peak,
-                                               cpu=not args.no_cpu_baseline)
+    # the GPU-only lines first, then the single-B200 config with its CPU legs
     if world == 1 and args.qcap_workload:
         pairs = None
         torch.cuda.empty_cache()
@@ -538,6 +538,11 @@ def run_ours(args, w):
         pairs = None
         torch.cuda.empty_cache()
         line["fp32_config"] = single_gpu(WORKLOADS[args.fp32_workload], args, dev, peak, cpu=False)
+    if world == 1 and args.single_gpu_workload and args.single_gpu_workload != w.name:
+        pairs = None
+        torch.cuda.empty_cache()
+        line["single_gpu_config"] = single_gpu(WORKLOADS[args.single_gpu_workload], args, dev, peak,
+                                               cpu=not args.no_cpu_baseline)
     if world == 1 and args.stream_workload and args.stream_block > 0:
         pairs = None
         torch.cuda.empty_cache()
