@@ -26,19 +26,20 @@ constexpr int TB = 64;   // output tile edge
 constexpr int RB = 32;   // rows staged per iteration
 constexpr int NT = 256;  // threads per block (16 x 16, 4x4 outputs each)
 
-// One operand's RB x TB stage (rows r0.., columns c0.. of a row-major matrix
+// One operand's RB x W stage (rows r0.., columns c0.. of a row-major matrix
 // with ld columns, the columns past ncols zero) held in registers until it
 // is stored to shared memory, so the next stage's loads are in flight while
 // the current one is multiplied.  16-bit operands whose row length is a
-// multiple of 8 on 16-byte boundaries take one 16-byte load per thread.
-template <typename T>
+// multiple of 8 on 16-byte boundaries take one 16-byte load per thread
+// (W = 64 only).
+template <typename T, int W = TB>
 struct StageRegs {
   uint4 v;
-  float s[RB * TB / NT];
+  float s[RB * W / NT];
 
   __device__ __forceinline__ void load(const T* __restrict__ base, int64_t r0, int64_t r_end, int c0, int ncols,
                                        int ld, bool vec, const float* __restrict__ extra, int q1) {
-    if constexpr (sizeof(T) == 2) {
+    if constexpr (sizeof(T) == 2 && W == TB) {
       if (vec) {
         const int rr = threadIdx.x >> 3, col = c0 + ((threadIdx.x & 7) << 3);
         const int64_t r = r0 + rr;
@@ -48,9 +49,9 @@ struct StageRegs {
       }
     }
 #pragma unroll
-    for (int u = 0; u < RB * TB / NT; ++u) {
+    for (int u = 0; u < RB * W / NT; ++u) {
       const int e = threadIdx.x + u * NT;
-      const int rr = e / TB, cc = e % TB;
+      const int rr = e / W, cc = e % W;
       const int64_t r = r0 + rr;
       const int c = c0 + cc;
       float val = 0.f;
@@ -62,8 +63,8 @@ struct StageRegs {
     }
   }
 
-  __device__ __forceinline__ void store(float (*sm)[TB], bool vec) {
-    if constexpr (sizeof(T) == 2) {
+  __device__ __forceinline__ void store(float (*sm)[W], bool vec) {
+    if constexpr (sizeof(T) == 2 && W == TB) {
       if (vec) {
         const int rr = threadIdx.x >> 3, cb = (threadIdx.x & 7) << 3;
         const T* e = reinterpret_cast<const T*>(&v);
@@ -73,39 +74,42 @@ struct StageRegs {
       }
     }
 #pragma unroll
-    for (int u = 0; u < RB * TB / NT; ++u) {
+    for (int u = 0; u < RB * W / NT; ++u) {
       const int e = threadIdx.x + u * NT;
-      sm[e / TB][e % TB] = s[u];
+      sm[e / W][e % W] = s[u];
     }
   }
 };
 
-template <typename TA, typename TB1>
+// CW output columns a thread (tiles of 64 x 16 CW): 4, or 5 for outputs
+// of 65 to 80 columns (a d = 64 Gram with its sketch in one tile).
+template <typename TA, typename TB1, int CW>
 __global__ void __launch_bounds__(NT)
 atb_partial_kernel(CellPtrs A, CellPtrs B1, const float* __restrict__ B2, int64_t rows, int p,
                    int q1, int q2, int chunks, int64_t chunk_rows, float* __restrict__ partial, int vec_a,
                    int vec_b) {
+  constexpr int TJ = 16 * CW;
   const int cell = blockIdx.z;
   const int chunk = blockIdx.x;
   const int q = q1 + q2;
-  const int tiles_j = (q + TB - 1) / TB;
+  const int tiles_j = (q + TJ - 1) / TJ;
   const int ti = blockIdx.y / tiles_j, tj = blockIdx.y % tiles_j;
-  const int i0 = ti * TB, j0 = tj * TB;
+  const int i0 = ti * TB, j0 = tj * TJ;
   const TA* __restrict__ a = static_cast<const TA*>(A.p[cell]);
   const TB1* __restrict__ b1 = static_cast<const TB1*>(B1.p[cell]);
-  __shared__ float sA[RB][TB];
-  __shared__ __align__(16) float sB[RB][TB];
+  __shared__ __align__(16) float sA[RB][TB];
+  __shared__ __align__(16) float sB[RB][TJ];
   const int tx = threadIdx.x % 16, ty = threadIdx.x / 16;
-  float acc[4][4];
+  float acc[4][CW];
 #pragma unroll
   for (int u = 0; u < 4; ++u)
 #pragma unroll
-    for (int v = 0; v < 4; ++v) acc[u][v] = 0.f;
+    for (int v = 0; v < CW; ++v) acc[u][v] = 0.f;
 
   const int64_t r_begin = (int64_t)chunk * chunk_rows;
   const int64_t r_end = r_begin + chunk_rows < rows ? r_begin + chunk_rows : rows;
   StageRegs<TA> ra;
-  StageRegs<TB1> rb;
+  StageRegs<TB1, TJ> rb;
   ra.load(a, r_begin, r_end, i0, p, p, vec_a, nullptr, p);
   rb.load(b1, r_begin, r_end, j0, q, q1, vec_b, B2, q1);
   for (int64_t r0 = r_begin; r0 < r_end; r0 += RB) {
@@ -118,17 +122,24 @@ atb_partial_kernel(CellPtrs A, CellPtrs B1, const float* __restrict__ B2, int64_
     }
 #pragma unroll 4
     for (int rr = 0; rr < RB; ++rr) {
-      float av[4];
+      const float4 a4 = *reinterpret_cast<const float4*>(&sA[rr][ty * 4]);
+      const float av[4] = {a4.x, a4.y, a4.z, a4.w};
+      float bv[CW];
+      if constexpr (CW == 4) {
+        const float4 b4 = *reinterpret_cast<const float4*>(&sB[rr][tx * 4]);
+        bv[0] = b4.x;
+        bv[1] = b4.y;
+        bv[2] = b4.z;
+        bv[3] = b4.w;
+      } else {
+        // column stride 5: the 16 columns groups of a half warp hit distinct banks
 #pragma unroll
-      for (int u = 0; u < 4; ++u) av[u] = sA[rr][ty * 4 + u];
-      const float4 bv = *reinterpret_cast<const float4*>(&sB[rr][tx * 4]);
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        acc[u][0] = fmaf(av[u], bv.x, acc[u][0]);
-        acc[u][1] = fmaf(av[u], bv.y, acc[u][1]);
-        acc[u][2] = fmaf(av[u], bv.z, acc[u][2]);
-        acc[u][3] = fmaf(av[u], bv.w, acc[u][3]);
+        for (int v = 0; v < CW; ++v) bv[v] = sB[rr][tx * CW + v];
       }
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+#pragma unroll
+        for (int v = 0; v < CW; ++v) acc[u][v] = fmaf(av[u], bv[v], acc[u][v]);
     }
     __syncthreads();
   }
@@ -136,19 +147,24 @@ atb_partial_kernel(CellPtrs A, CellPtrs B1, const float* __restrict__ B2, int64_
 #pragma unroll
   for (int u = 0; u < 4; ++u)
 #pragma unroll
-    for (int v = 0; v < 4; ++v) {
-      const int i = i0 + ty * 4 + u, j = j0 + tx * 4 + v;
+    for (int v = 0; v < CW; ++v) {
+      const int i = i0 + ty * 4 + u, j = j0 + tx * CW + v;
       if (i < p && j < q) out[(int64_t)i * q + j] = acc[u][v];
     }
 }
 
-// Skinny variant (p + q <= SK_MAXPQ): one block loads a chunk of SK_ROWS
-// rows of A and [B1 | B2] into shared memory with independent loads, then
-// each thread sums one or more outputs over the chunk.  Used for the token
-// Gram (p = m * rd) and the Tucker core (p = rt), whose operands are a few
-// columns wide: the tiled kernel above would serialise its loads there.
+// Skinny variant (p + q <= SK_MAXPQ, or p <= SK_MAXP_WIDE with p + q <=
+// SK_MAXPQ_WIDE): one block loads a chunk of SK_ROWS rows of A and [B1 | B2]
+// into shared memory with independent loads, then each thread sums one or
+// more outputs over the chunk.  Used for the token Gram (p = m * rd) and the
+// Tucker core (p = rt), whose operands are a few columns wide: the tiled
+// kernel above would serialise its loads there, or (one row of A) compute a
+// 64 x 64 tile for one row of outputs.
 constexpr int SK_ROWS = 256;
 constexpr int SK_MAXPQ = 48;
+// a few rows of A (the Tucker core's u_token^T, rt <= 8) against up to 120
+// columns: the tiled kernel would compute a 64 x 64 tile for each of them
+constexpr int SK_MAXP_WIDE = 8, SK_MAXPQ_WIDE = 128;
 
 template <typename TA, typename TB1>
 __global__ void __launch_bounds__(NT)
@@ -250,6 +266,10 @@ __global__ void core_reduce_kernel(const float* __restrict__ partial, int n_cell
   }
 }
 
+// Output columns a thread of atb_partial_kernel takes: 5 when the columns
+// fit one 80-wide tile but not a 64-wide one.
+int cols_per_thread(int q) { return q > TB && q <= 80 ? 5 : 4; }
+
 struct ChunkPlan {
   int chunks;
   int64_t chunk_rows;
@@ -263,14 +283,14 @@ struct ChunkPlan {
 ChunkPlan plan_chunks(int n_cells, int64_t rows, int p, int q) {
   (void)n_cells;
   ChunkPlan pl;
-  pl.skinny = p + q <= SK_MAXPQ;
+  pl.skinny = p + q <= SK_MAXPQ || (p <= SK_MAXP_WIDE && p + q <= SK_MAXPQ_WIDE);
   if (pl.skinny) {
     pl.tiles = 1;
     pl.chunk_rows = SK_ROWS;
     pl.chunks = (int)std::max<int64_t>(1, ceil_div(rows, SK_ROWS));
     return pl;
   }
-  pl.tiles = (int)(ceil_div(p, TB) * ceil_div(q, TB));
+  pl.tiles = (int)(ceil_div(p, TB) * ceil_div(q, 16 * cols_per_thread(q)));
   // narrow outputs (a feature Gram of d = 64 and its sketch: two tiles) get
   // shorter chunks, so a few cells still fill the GPU with blocks
   int64_t cr = std::max<int64_t>(pl.tiles <= 4 ? 512 : 2048, ceil_div(rows, 128));
@@ -297,7 +317,12 @@ template <typename TA, typename TB1>
 int launch_partial(int n_cells, const CellPtrs& a, const CellPtrs& b1, const float* b2, int64_t rows,
                    int p, int q1, int q2, const ChunkPlan& pl, float* partial, cudaStream_t st) {
   if (pl.skinny) {
-    const size_t smem = (size_t)SK_ROWS * (p + q1 + q2) * sizeof(float);
+    const size_t smem = (size_t)SK_ROWS * (p + q1 + q2) * sizeof(float);  // at most 128 KB
+    if (smem > 48 * 1024) {
+      const cudaError_t e = cudaFuncSetAttribute(atb_skinny_kernel<TA, TB1>,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      if (e != cudaSuccess) return fail(KVC_ERR_LAUNCH, std::string("atb_skinny_kernel: ") + cudaGetErrorString(e));
+    }
     atb_skinny_kernel<TA, TB1><<<dim3(pl.chunks, n_cells), NT, smem, st>>>(a, b1, b2, rows, p, q1, q2, pl.chunks,
                                                                            partial);
     return check_launch("atb_skinny_kernel");
@@ -305,8 +330,12 @@ int launch_partial(int n_cells, const CellPtrs& a, const CellPtrs& b1, const flo
   dim3 grid(pl.chunks, pl.tiles, n_cells);
   const int vec_a = rows_vectorizable<TA>(a, n_cells, p);
   const int vec_b = q2 == 0 && rows_vectorizable<TB1>(b1, n_cells, q1);
-  atb_partial_kernel<TA, TB1><<<grid, NT, 0, st>>>(a, b1, b2, rows, p, q1, q2, pl.chunks,
-                                                   pl.chunk_rows, partial, vec_a, vec_b);
+  if (cols_per_thread(q1 + q2) == 5)
+    atb_partial_kernel<TA, TB1, 5><<<grid, NT, 0, st>>>(a, b1, b2, rows, p, q1, q2, pl.chunks, pl.chunk_rows, partial,
+                                                        vec_a, 0);
+  else
+    atb_partial_kernel<TA, TB1, 4><<<grid, NT, 0, st>>>(a, b1, b2, rows, p, q1, q2, pl.chunks, pl.chunk_rows, partial,
+                                                        vec_a, vec_b);
   return check_launch("atb_partial_kernel");
 }
 

@@ -302,11 +302,15 @@ struct GPlan {
 };
 
 // The segment length depends on the row count only (about 16 segments per
-// cell, 4..32 tiles each), never on how many cells share the launch.
+// cell, 4..128 tiles each), never on how many cells share the launch.  Each
+// segment costs a flush of its 128 x (128 + NY) fp32 sums and their read in
+// the reduce: at 128 tiles that is 2.5% of the segment's x bytes (10% at
+// 32), while 128 segments a cell still split a launch of many cells evenly
+// over the SMs.
 GPlan gplan(int n_cells, int64_t rows) {
   GPlan p;
   p.tiles_per_cell = ceil_div(rows, TILE);
-  p.seg_tiles = std::min<int64_t>(p.tiles_per_cell, std::min<int64_t>(32, std::max<int64_t>(4, ceil_div(p.tiles_per_cell, 16))));
+  p.seg_tiles = std::min<int64_t>(p.tiles_per_cell, std::min<int64_t>(128, std::max<int64_t>(4, ceil_div(p.tiles_per_cell, 16))));
   p.segs_per_cell = ceil_div(p.tiles_per_cell, p.seg_tiles);
   p.total_segs = p.segs_per_cell * n_cells;
   p.ctas = (int)std::min<int64_t>(std::min<int64_t>(p.total_segs, num_sms()), 1024);

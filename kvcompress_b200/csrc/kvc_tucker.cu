@@ -343,12 +343,14 @@ __global__ void __launch_bounds__(PJ_THREADS, 1)
 
 // out (rows x N) = round_T(A (rows x K) * M (K x N)) for K <= 64, N <= 16:
 // one thread per row, M in shared memory as float, fp32 accumulation in k
-// order (the same arithmetic as rowmat_kernel).
-constexpr int SKK = 64, SKN = 16;
-template <typename T>
+// order (the same arithmetic as rowmat_kernel).  SKN: the column count
+// rounded up to 1, 2, 4, 8 or 16, so a rank-1 basis costs one FMA and one
+// shared-memory read per element, not sixteen predicated ones.
+constexpr int SKK = 64, SKN_MAX = 16;
+template <typename T, int SKN>
 __global__ void __launch_bounds__(256) rowmat_skinny_kernel(CellPtrs A, const double* __restrict__ mat, int64_t rows,
                                                             int K, int N, CellPtrsMut out) {
-  __shared__ float sM[SKK * SKN];
+  __shared__ float sM[SKK * SKN_MAX];
   const int cell = blockIdx.y;
   const double* m = mat + (int64_t)cell * K * N;
   for (int i = threadIdx.x; i < K * N; i += blockDim.x) sM[i] = (float)m[i];
@@ -510,10 +512,17 @@ extern "C" int kvc_apply_basis(int n_cells, const void* const* a, int64_t rows, 
     o.p[c] = out[c];
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (p <= SKK && r <= SKN) {
+  if (p <= SKK && r <= SKN_MAX) {
     const int blocks = (int)std::max<int64_t>(1, std::min<int64_t>(ceil_div(rows, 256), ceil_div(16LL * num_sms(), n_cells)));
-    KVC_DISPATCH_DTYPE(dtype, T,
-                       rowmat_skinny_kernel<T><<<dim3(blocks, n_cells), 256, 0, st>>>(aa, mat, rows, p, r, o));
+    const dim3 grid(blocks, n_cells);
+#define KVC_ROWMAT_SKINNY(NN) \
+  KVC_DISPATCH_DTYPE(dtype, T, rowmat_skinny_kernel<T, NN><<<grid, 256, 0, st>>>(aa, mat, rows, p, r, o))
+    if (r <= 1) KVC_ROWMAT_SKINNY(1);
+    else if (r <= 2) KVC_ROWMAT_SKINNY(2);
+    else if (r <= 4) KVC_ROWMAT_SKINNY(4);
+    else if (r <= 8) KVC_ROWMAT_SKINNY(8);
+    else KVC_ROWMAT_SKINNY(16);
+#undef KVC_ROWMAT_SKINNY
     return check_launch("rowmat_skinny_kernel");
   }
   dim3 grid((unsigned)ceil_div(rows, TM), (unsigned)ceil_div(r, TN), n_cells);
